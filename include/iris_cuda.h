@@ -1,0 +1,258 @@
+/*
+ * iris_cuda.h — C ABI of the B200 (sm_100a) backend for iris.c.
+ *
+ * libiris_cuda.so replaces the reference's compute backends (make generic /
+ * make blas / make mps) for the DiT denoising step: the Flux.2 Klein
+ * transformer forward, the Z-Image S3-DiT forward and the Euler samplers that
+ * drive them.  Plain C: host or device pointers, sizes, status codes; no C++
+ * or framework types cross this boundary.
+ *
+ * Three layers, each citing the reference interface it replaces:
+ *   1. runtime            iris_metal_init / iris_metal_available / iris_gpu_sync
+ *                         (iris_metal.h:23-33, :309)
+ *   2. model + sampler    iris_transformer_* (iris_transformer_flux.c:3939, :4579,
+ *                         :5300), zi_transformer_* (iris_transformer_zimage.c:1696,
+ *                         :2164), iris_sample_* (iris_sample.c:171-1188)
+ *   3. tensor/op surface  the iris_gpu_* device-resident API of iris_metal.h
+ *                         (:155-600), same names and signatures, so the
+ *                         reference's bf16 block code can link against it.
+ *
+ * Conventions (same as the reference): latents are NCHW f32 [C, h, w] with
+ * h, w in patches (image pixels / 16 for Flux); text embeddings are f32
+ * [txt_seq, text_dim]; functions returning float* hand back malloc'd host
+ * memory the caller frees; NULL / non-zero status means failure.  Status
+ * codes are the IRIS_CUDA_* values below; iris_cuda_last_error() describes
+ * the last failure.  All calls are synchronous with respect to the host
+ * unless the name ends in _dev / _async, and are single-threaded like the
+ * reference's (iris_kernels.h:100-106).
+ */
+#ifndef IRIS_CUDA_H
+#define IRIS_CUDA_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ status */
+#define IRIS_CUDA_OK 0
+#define IRIS_CUDA_ERR_ARG -1         /* bad argument / unsupported shape            */
+#define IRIS_CUDA_ERR_OOM -2         /* device or host allocation failed            */
+#define IRIS_CUDA_ERR_CUDA -3        /* CUDA runtime/driver error                   */
+#define IRIS_CUDA_ERR_IO -4          /* model file missing or malformed             */
+#define IRIS_CUDA_ERR_TIMEOUT -5     /* a kernel's bounded wait expired (see below) */
+#define IRIS_CUDA_ERR_NODEV -6       /* no usable sm_100 device                     */
+#define IRIS_CUDA_ERR_INJECTED -7    /* failure injected through IRIS_CUDA_FAULT    */
+
+/* ------------------------------------------------------------------ 1. runtime */
+/* Select and initialise a device (idempotent).  Replaces iris_metal_init
+ * (iris_metal.h:23). */
+int iris_cuda_init(int device);
+/* 1 when an sm_100 device is usable.  Replaces iris_metal_available (iris_metal.h:28). */
+int iris_cuda_available(void);
+/* Release library state (streams, caches).  Replaces iris_metal_cleanup (iris_metal.h:33). */
+void iris_cuda_cleanup(void);
+/* Human-readable description of the last failure on this thread. */
+const char *iris_cuda_last_error(void);
+/* Non-zero code recorded by a kernel whose bounded wait expired (0 = none);
+ * clear != 0 resets it.  No reference counterpart (the reference has no
+ * device-side waits). */
+int iris_cuda_device_status(int clear);
+/* Wait for all queued work.  Replaces iris_gpu_sync (iris_metal.h:309). */
+int iris_cuda_synchronize(void);
+/* The cudaStream_t (as void*) all library work is queued on. */
+void *iris_cuda_stream(void);
+/* Number of kernels this library has enqueued since load (graph replays
+ * count every kernel node).  Used by benchmarks to report launch counts. */
+uint64_t iris_cuda_kernel_launches(void);
+
+/* ------------------------------------------------------------------ 2a. Flux.2 Klein */
+typedef struct iris_cuda_flux iris_cuda_flux_t;
+
+typedef struct {
+    int hidden;          /* heads * head_dim (3072 for Klein 4B)          */
+    int heads;           /* 24                                            */
+    int head_dim;        /* must be 128                                   */
+    int mlp;             /* hidden * mlp_ratio (9216)                     */
+    int n_double;        /* 5                                             */
+    int n_single;        /* 20                                            */
+    int text_dim;        /* joint_attention_dim (7680)                    */
+    int channels;        /* in_channels (128)                             */
+    float rope_theta;    /* 2000                                          */
+} iris_cuda_flux_config_t;
+
+/* Multi-reference conditioning input.  Same fields as iris_ref_t
+ * (iris_sample.c:282-286). */
+typedef struct {
+    const float *latent; /* NCHW [C, h, w]                                */
+    int h, w;
+    int t_offset;        /* RoPE T coordinate (10, 20, ...)               */
+} iris_cuda_ref_t;
+
+/* Load a model directory (transformer/config.json + safetensors shards),
+ * uploading every weight once to HBM as bf16.  Replaces
+ * iris_transformer_load_safetensors (iris_transformer_flux.c:5300). */
+iris_cuda_flux_t *iris_cuda_flux_load(const char *model_dir);
+/* Random-init model of the given shape: every tensor N(0, std) from a
+ * counter-based RNG keyed by (seed, tensor name), generated on the device
+ * (no reference counterpart; benchmark and test fixture).  norm_unit != 0
+ * draws the QK-norm scales as 1 + N(0, 0.1) instead. */
+iris_cuda_flux_t *iris_cuda_flux_random(const iris_cuda_flux_config_t *cfg, uint64_t seed,
+                                        float std, int norm_unit);
+/* Replaces iris_transformer_free (iris_transformer_flux.c:4973). */
+void iris_cuda_flux_free(iris_cuda_flux_t *tf);
+int iris_cuda_flux_get_config(const iris_cuda_flux_t *tf, iris_cuda_flux_config_t *out);
+/* Copy one weight, in the reference's (safetensors) layout, as bf16 bits.
+ * numel must match the tensor's element count. */
+int iris_cuda_flux_read_weight(iris_cuda_flux_t *tf, const char *name, uint16_t *out,
+                               size_t numel);
+/* Bytes of HBM held by the model's weights. */
+size_t iris_cuda_flux_weight_bytes(const iris_cuda_flux_t *tf);
+
+/* One denoising step: velocity v(z, t, ctx), host buffers in and out.
+ * Replaces iris_transformer_forward (iris_transformer_flux.c:3939); returns
+ * malloc'd NCHW [C, h, w] or NULL. */
+float *iris_cuda_transformer_forward(iris_cuda_flux_t *tf, const float *img_latent, int img_h,
+                                     int img_w, const float *txt_emb, int txt_seq,
+                                     float timestep);
+/* Replaces iris_transformer_forward_with_multi_refs (iris_transformer_flux.c:4579). */
+float *iris_cuda_transformer_forward_with_multi_refs(iris_cuda_flux_t *tf,
+                                                     const float *img_latent, int img_h,
+                                                     int img_w, const iris_cuda_ref_t *refs,
+                                                     int num_refs, const float *txt_emb,
+                                                     int txt_seq, float timestep);
+/* Device-resident forward: every pointer (latent, ref latents, txt_emb, out)
+ * is device memory; work is queued on iris_cuda_stream() and this call does
+ * not synchronise.  out = [C, img_h, img_w]. */
+int iris_cuda_flux_forward_dev(iris_cuda_flux_t *tf, const float *d_latent, int img_h,
+                               int img_w, const iris_cuda_ref_t *d_refs, int num_refs,
+                               const float *d_txt_emb, int txt_seq, float timestep,
+                               float *d_out);
+
+/* Run ONE block on a caller-supplied hidden state (per-block parity hook).
+ * hidden: host f32 [txt_seq + img_h*img_w, hidden] in [TXT, IMG] row order,
+ * updated in place; modulations are computed from `timestep`.  kind 0 runs
+ * double block idx (replaces double_block_forward, iris_transformer_flux.c:2366,
+ * with hidden split into its txt/img streams), kind 1 single block idx
+ * (single_block_forward, :3761). */
+int iris_cuda_flux_run_block(iris_cuda_flux_t *tf, int kind, int idx, float *hidden, int txt_seq,
+                             int img_h, int img_w, float timestep);
+
+/* ------------------------------------------------------------------ 2b. samplers */
+/* Replaces iris_official_schedule (iris_sample.c:171). malloc'd [steps+1]. */
+float *iris_cuda_official_schedule(int num_steps, int image_seq_len);
+/* Replaces iris_linear_schedule (iris_sample.c:61). */
+float *iris_cuda_linear_schedule(int num_steps);
+/* Replaces iris_zimage_schedule (iris_sample.c:216) (IRIS_ZIMAGE_SHIFT honoured). */
+float *iris_cuda_zimage_schedule(int num_steps, int image_seq_len);
+/* Replaces iris_init_noise (iris_sample.c:1146): same xoshiro256** stream,
+ * bit-identical values. malloc'd [batch, C, h, w]. */
+float *iris_cuda_init_noise(int batch, int channels, int h, int w, int64_t seed);
+
+/* Euler rectified-flow loop, host buffers.  Replaces iris_sample_euler
+ * (iris_sample.c:313): returns malloc'd final latent.  batch must be 1. */
+float *iris_cuda_sample_euler(iris_cuda_flux_t *tf, const float *z, int batch, int channels,
+                              int h, int w, const float *text_emb, int text_seq,
+                              const float *schedule, int num_steps,
+                              void (*progress_callback)(int step, int total));
+/* Replaces iris_sample_euler_cfg (iris_sample.c:717). */
+float *iris_cuda_sample_euler_cfg(iris_cuda_flux_t *tf, const float *z, int batch,
+                                  int channels, int h, int w, const float *text_emb_cond,
+                                  int text_seq_cond, const float *text_emb_uncond,
+                                  int text_seq_uncond, float guidance_scale,
+                                  const float *schedule, int num_steps,
+                                  void (*progress_callback)(int step, int total));
+/* Replaces iris_sample_euler_with_multi_refs (iris_sample.c:630). */
+float *iris_cuda_sample_euler_with_multi_refs(iris_cuda_flux_t *tf, const float *z, int batch,
+                                              int channels, int h, int w,
+                                              const iris_cuda_ref_t *refs, int num_refs,
+                                              const float *text_emb, int text_seq,
+                                              const float *schedule, int num_steps,
+                                              void (*progress_callback)(int step, int total));
+/* Device-resident sampler: d_z [C,h,w] is updated in place, d_txt (and
+ * d_txt_uncond when guidance is used; NULL otherwise) are device buffers,
+ * schedule is a host array.  Queued on iris_cuda_stream(); the call returns
+ * after the denoising loop has been queued and its scratch released. */
+int iris_cuda_sample_euler_dev(iris_cuda_flux_t *tf, float *d_z, int h, int w,
+                               const float *d_txt, int txt_seq, const float *d_txt_uncond,
+                               int txt_seq_uncond, float guidance, const float *schedule,
+                               int num_steps);
+
+/* ------------------------------------------------------------------ 3. iris_gpu_* surface
+ * Device-resident tensors and ops with the names and signatures of
+ * iris_metal.h.  Tensors are f32 or bf16 device buffers; "host" weight
+ * pointers (const uint16_t *W_bf16) are uploaded once and cached by
+ * address, exactly like the Metal backend's weight cache (iris_metal.m:1001). */
+typedef struct iris_gpu_tensor *iris_gpu_tensor_t;
+
+iris_gpu_tensor_t iris_gpu_tensor_create(const float *data, size_t num_elements);   /* :172 */
+iris_gpu_tensor_t iris_gpu_tensor_alloc(size_t num_elements);                       /* :177 */
+iris_gpu_tensor_t iris_gpu_tensor_alloc_persistent(size_t num_elements);            /* :184 */
+void iris_gpu_tensor_set_persistent(iris_gpu_tensor_t tensor, int persistent);      /* :189 */
+void iris_gpu_tensor_read(iris_gpu_tensor_t tensor, float *out);                    /* :195 */
+void iris_gpu_tensor_write(iris_gpu_tensor_t tensor, const float *data);            /* :201 */
+void iris_gpu_tensor_free(iris_gpu_tensor_t tensor);                                /* :213 */
+size_t iris_gpu_tensor_size(iris_gpu_tensor_t tensor);                              /* :218 */
+int iris_gpu_tensor_is_f16(iris_gpu_tensor_t tensor);                               /* :223 */
+iris_gpu_tensor_t iris_gpu_tensor_alloc_f16(size_t num_elements);                   /* :276 */
+iris_gpu_tensor_t iris_gpu_tensor_create_bf16(const float *data, size_t num_elements); /* :283 */
+iris_gpu_tensor_t iris_gpu_tensor_f32_to_bf16(iris_gpu_tensor_t f32_tensor);        /* :571 */
+iris_gpu_tensor_t iris_gpu_tensor_bf16_to_f32(iris_gpu_tensor_t bf16_tensor);       /* :574 */
+int iris_gpu_convert_f32_to_bf16_into(iris_gpu_tensor_t bf16_out, iris_gpu_tensor_t f32_in); /* :577 */
+int iris_gpu_convert_bf16_to_f32_into(iris_gpu_tensor_t f32_out, iris_gpu_tensor_t bf16_in); /* :580 */
+void iris_gpu_sync(void);                                                           /* :309 */
+void iris_gpu_batch_begin(void);                                                    /* :315 */
+void iris_gpu_batch_end(void);                                                      /* :320 */
+
+/* y = x W^T with a bf16 weight; x and result bf16.  :583 / :589 */
+iris_gpu_tensor_t iris_gpu_linear_bf16_native(iris_gpu_tensor_t x, const uint16_t *W_bf16,
+                                              int seq_len, int in_dim, int out_dim);
+int iris_gpu_linear_bf16_native_into(iris_gpu_tensor_t out, iris_gpu_tensor_t x,
+                                     const uint16_t *W_bf16, int seq_len, int in_dim,
+                                     int out_dim);
+/* (1 + scale) * LayerNorm(x) + shift, bf16.  :433 */
+void iris_gpu_adaln_norm_bf16(iris_gpu_tensor_t out, iris_gpu_tensor_t x,
+                              iris_gpu_tensor_t shift_bf16, iris_gpu_tensor_t scale_bf16,
+                              int seq, int hidden, float eps);
+/* per-head RMSNorm of Q and K in place.  :438 */
+void iris_gpu_qk_rms_norm_bf16(iris_gpu_tensor_t q, iris_gpu_tensor_t k,
+                               iris_gpu_tensor_t q_weight_bf16, iris_gpu_tensor_t k_weight_bf16,
+                               int seq, int heads, int head_dim, float eps);
+/* text rows [0, img_offset) with txt tables, image rows with img tables.  :466 */
+void iris_gpu_rope_unified_bf16(iris_gpu_tensor_t q, iris_gpu_tensor_t k, const float *txt_cos,
+                                const float *txt_sin, const float *img_cos,
+                                const float *img_sin, const float *img_cos_k,
+                                const float *img_sin_k, int seq, int img_offset, int heads,
+                                int head_dim, int axis_dim);
+/* one table for all rows.  :473 */
+void iris_gpu_rope_2d_bf16(iris_gpu_tensor_t x, const float *cos_freq, const float *sin_freq,
+                           int seq, int heads, int head_dim, int axis_dim);
+/* softmax(Q K^T scale) V, bf16.  :423 (no sequence-length limit here) */
+int iris_gpu_attention_fused_bf16(iris_gpu_tensor_t out, iris_gpu_tensor_t Q,
+                                  iris_gpu_tensor_t K, iris_gpu_tensor_t V, int seq_q,
+                                  int seq_k, int num_heads, int head_dim, float scale);
+void iris_gpu_silu_mul_bf16(iris_gpu_tensor_t gate, iris_gpu_tensor_t up, int n);   /* :457 */
+void iris_gpu_gated_add_bf16(iris_gpu_tensor_t out, iris_gpu_tensor_t gate_bf16,
+                             iris_gpu_tensor_t proj, int seq, int hidden);          /* :460 */
+void iris_gpu_concat_seq_bf16(iris_gpu_tensor_t out, iris_gpu_tensor_t a,
+                              iris_gpu_tensor_t b, int seq_a, int seq_b, int hidden); /* :501 */
+void iris_gpu_slice_seq_bf16(iris_gpu_tensor_t out, iris_gpu_tensor_t in, int seq_out,
+                             int hidden, int start);                               /* :506 */
+void iris_gpu_split_qkv_mlp_bf16(iris_gpu_tensor_t fused, iris_gpu_tensor_t q,
+                                 iris_gpu_tensor_t k, iris_gpu_tensor_t v,
+                                 iris_gpu_tensor_t gate, iris_gpu_tensor_t up, int seq,
+                                 int hidden, int mlp_hidden);                      /* :511 */
+void iris_gpu_concat_attn_mlp_bf16(iris_gpu_tensor_t attn, iris_gpu_tensor_t mlp,
+                                   iris_gpu_tensor_t out, int seq, int hidden,
+                                   int mlp_hidden);                                /* :517 */
+/* capability probes of the Metal backend, answered for CUDA:  :28, :703, :743 */
+int iris_metal_available(void);
+int iris_metal_shaders_available(void);
+int iris_bf16_pipeline_available(void);
+
+#ifdef __cplusplus
+}
+#endif
+#endif /* IRIS_CUDA_H */

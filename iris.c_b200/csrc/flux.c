@@ -1,0 +1,852 @@
+/*
+ * Flux.2 Klein transformer on B200: weights resident in HBM as bf16, one
+ * denoising step = one CUDA graph of fused kernels.
+ *
+ * Reference: iris_transformer_flux.c — loader :5300-5497, forward :3939-4326,
+ * double block :2366-2614, single block :3761-3928, multi-reference forward
+ * :4579-4840.
+ *
+ * Data layout in HBM
+ *   hidden   f32  [S, H]   S = S_txt + S_img(+refs), rows in [TXT, IMG] order
+ *                          for the whole step (the reference concatenates the
+ *                          same way before the single blocks, :4110-4114, and
+ *                          orders joint-attention K/V [TXT, IMG], :1899-1905)
+ *   xmod     bf16 [S, H]   adaLN output = GEMM A operand
+ *   q, k, v  bf16 [S, H]   written by the QKV GEMM epilogue after QK-RMSNorm+RoPE
+ *   attn     bf16 [S, H]   double-block attention output
+ *   mlp      bf16 [S, F]   SiLU(gate)*up (double blocks)
+ *   cat      bf16 [S, H+F] single block [attention | SiLU(gate)*up]
+ *   rope     f32  [S, 64]  cos / sin per (token, rotation pair)
+ * Weights (bf16, [out, in] row-major = K-major GEMM B operands)
+ *   double   w_qkv[s] [3H, H] = to_q; to_k; to_v stacked, per stream s
+ *            w_in[s]  [2F, H] = ff.linear_in with gate/up interleaved in
+ *                              blocks of 128 rows (SwiGLU epilogue layout)
+ *   single   w_fused  [3H+2F, H] = Q,K,V rows then interleaved gate/up
+ *   w_mod    [17H, H] = double img 6H | double txt 6H | single 3H | final 2H
+ *                      (all modulation linears in one GEMV per step)
+ */
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#include "iris_internal.h"
+
+#define MAXREFS 8
+
+typedef struct {
+    uint16_t *w_qkv[2], *w_out[2], *w_in[2], *w_down[2]; /* [0] txt, [1] img */
+    float *qn[2], *kn[2];
+    CUtensorMap tm_qkv[2], tm_out[2], tm_in[2], tm_down[2];
+} flux_dbl_t;
+
+typedef struct {
+    uint16_t *w_fused, *w_out;
+    float *qn, *kn;
+    CUtensorMap tm_fused, tm_out;
+} flux_sgl_t;
+
+typedef struct {
+    int valid;
+    int s_txt, img_h, img_w, n_img, n_img_total, S;
+    int num_refs, ref_h[MAXREFS], ref_w[MAXREFS], ref_t[MAXREFS];
+    float *hidden, *lat_in, *out, *txt_f32, *rope_cos, *rope_sin;
+    uint16_t *xmod, *q, *k, *v, *attn, *mlp, *cat, *tok_img, *tok_txt;
+    CUtensorMap tm_xmod, tm_attn, tm_mlp, tm_cat, tm_tok_img, tm_tok_txt;
+    cudaGraph_t graph;
+    cudaGraphExec_t gexec;
+    int graph_ok;
+    uint64_t graph_kernels;
+} flux_plan_t;
+
+struct iris_cuda_flux {
+    iris_cuda_flux_config_t cfg;
+    int H, F, C, T, NH;
+    uint16_t *w_x, *w_ctx, *w_t1, *w_t2, *w_mod, *w_proj;
+    CUtensorMap tm_x, tm_ctx, tm_proj;
+    flux_dbl_t *dbl;
+    flux_sgl_t *sgl;
+    size_t weight_bytes;
+    float *t_dev, *sincos, *temb_h, *temb, *mods;
+    flux_plan_t plan;
+    /* weight source for iris_cuda_flux_read_weight */
+    int random;
+    uint64_t seed;
+    float std;
+    int norm_unit;
+    char model_dir[1024];
+};
+
+/* ------------------------------------------------------------------ weight sources */
+typedef struct {
+    int random;
+    st_model_t st;
+    uint64_t seed;
+    float std;
+    int norm_unit;
+    uint16_t *host_stage;
+    size_t host_stage_n;
+} wsrc_t;
+
+static int is_norm_name(const char *name) {
+    return strstr(name, "norm_q") || strstr(name, "norm_k") || strstr(name, "norm_added_q") ||
+           strstr(name, "norm_added_k");
+}
+
+/* Write the reference-layout tensor `name` ([numel] bf16) to device memory d_dst. */
+static int wsrc_get(wsrc_t *ws, const char *name, size_t numel, uint16_t *d_dst) {
+    if (ws->random) {
+        int unit = ws->norm_unit && is_norm_name(name);
+        cudaError_t e = iris_launch_randn_bf16(d_dst, (long)numel, ws->seed, iris_crc32(name),
+                                               unit ? 1.0f : 0.0f, unit ? 0.1f : ws->std,
+                                               g_rt.stream);
+        iris_count_launch(1);
+        return iris_cuda_check(e, name);
+    }
+    const st_tensor_t *t = st_find(&ws->st, name);
+    if (!t) return iris_fail(IRIS_CUDA_ERR_IO, "tensor %s not found", name);
+    if (ws->host_stage_n < numel) {
+        if (ws->host_stage) cudaFreeHost(ws->host_stage);
+        ws->host_stage = NULL;
+        ws->host_stage_n = 0;
+        if (cudaMallocHost((void **)&ws->host_stage, numel * 2) != cudaSuccess)
+            return iris_fail(IRIS_CUDA_ERR_OOM, "pinned staging for %s", name);
+        ws->host_stage_n = numel;
+    }
+    /* the staging buffer is reused: finish the previous upload first */
+    cudaStreamSynchronize(g_rt.stream);
+    if (st_read_bf16(&ws->st, t, ws->host_stage, numel) != 0)
+        return iris_fail(IRIS_CUDA_ERR_IO, "tensor %s: bad shape or dtype", name);
+    return iris_cuda_check(cudaMemcpyAsync(d_dst, ws->host_stage, numel * 2,
+                                           cudaMemcpyHostToDevice, g_rt.stream), name);
+}
+
+/* f32 copy of a (small) tensor, through a bf16 device temp */
+static int wsrc_get_f32(wsrc_t *ws, const char *name, size_t numel, float *d_dst, uint16_t *tmp) {
+    int rc = wsrc_get(ws, name, numel, tmp);
+    if (rc) return rc;
+    iris_count_launch(1);
+    return iris_cuda_check(iris_launch_bf16_to_f32(tmp, d_dst, (long)numel, g_rt.stream), name);
+}
+
+/* ------------------------------------------------------------------ load */
+static uint16_t *walloc(iris_cuda_flux_t *tf, size_t numel) {
+    uint16_t *p = (uint16_t *)iris_dmalloc(numel * 2);
+    if (p) tf->weight_bytes += numel * 2;
+    return p;
+}
+
+static int mk_tmap(CUtensorMap *m, const void *p, int rows, int cols, int ld, int box) {
+    int r = iris_make_tmap_bf16(m, p, (uint64_t)rows, (uint64_t)cols, (uint64_t)ld, (uint32_t)box);
+    return r ? iris_fail(IRIS_CUDA_ERR_CUDA, "tensor map encode failed (%d)", r) : 0;
+}
+
+static int check_cfg(const iris_cuda_flux_config_t *c) {
+    if (c->head_dim != 128) return iris_fail(IRIS_CUDA_ERR_ARG, "head_dim must be 128");
+    if (c->hidden != c->heads * 128) return iris_fail(IRIS_CUDA_ERR_ARG, "hidden != heads*128");
+    if (c->hidden % 256) return iris_fail(IRIS_CUDA_ERR_ARG, "hidden must be a multiple of 256");
+    if (c->mlp % 128) return iris_fail(IRIS_CUDA_ERR_ARG, "mlp must be a multiple of 128");
+    if (c->text_dim % 64 || c->channels % 128)
+        return iris_fail(IRIS_CUDA_ERR_ARG, "text_dim %% 64 and channels %% 128 required");
+    if (c->hidden > 8192) return iris_fail(IRIS_CUDA_ERR_ARG, "hidden > 8192 unsupported");
+    return 0;
+}
+
+static int load_weights(iris_cuda_flux_t *tf, wsrc_t *ws) {
+    int H = tf->H, F = tf->F, C = tf->C, T = tf->T;
+    int rc = 0;
+    char nm[256];
+    size_t tmp_n = (size_t)(3 * H + 2 * F) * H;
+    uint16_t *tmp = (uint16_t *)iris_dmalloc(tmp_n * 2);
+    if (!tmp) return IRIS_CUDA_ERR_OOM;
+
+#define CHK(x) do { if ((rc = (x)) != 0) goto done; } while (0)
+#define ALLOC(p, n) do { if (!((p) = walloc(tf, (n)))) { rc = IRIS_CUDA_ERR_OOM; goto done; } } while (0)
+    ALLOC(tf->w_x, (size_t)H * C);
+    ALLOC(tf->w_ctx, (size_t)H * T);
+    ALLOC(tf->w_t1, (size_t)H * 256);
+    ALLOC(tf->w_t2, (size_t)H * H);
+    ALLOC(tf->w_mod, (size_t)17 * H * H);
+    ALLOC(tf->w_proj, (size_t)C * H);
+    CHK(wsrc_get(ws, "x_embedder.weight", (size_t)H * C, tf->w_x));
+    CHK(wsrc_get(ws, "context_embedder.weight", (size_t)H * T, tf->w_ctx));
+    CHK(wsrc_get(ws, "time_guidance_embed.timestep_embedder.linear_1.weight", (size_t)H * 256, tf->w_t1));
+    CHK(wsrc_get(ws, "time_guidance_embed.timestep_embedder.linear_2.weight", (size_t)H * H, tf->w_t2));
+    CHK(wsrc_get(ws, "double_stream_modulation_img.linear.weight", (size_t)6 * H * H, tf->w_mod));
+    CHK(wsrc_get(ws, "double_stream_modulation_txt.linear.weight", (size_t)6 * H * H,
+                 tf->w_mod + (size_t)6 * H * H));
+    CHK(wsrc_get(ws, "single_stream_modulation.linear.weight", (size_t)3 * H * H,
+                 tf->w_mod + (size_t)12 * H * H));
+    CHK(wsrc_get(ws, "norm_out.linear.weight", (size_t)2 * H * H, tf->w_mod + (size_t)15 * H * H));
+    CHK(wsrc_get(ws, "proj_out.weight", (size_t)C * H, tf->w_proj));
+    CHK(mk_tmap(&tf->tm_x, tf->w_x, H, C, C, 256));
+    CHK(mk_tmap(&tf->tm_ctx, tf->w_ctx, H, T, T, 256));
+    CHK(mk_tmap(&tf->tm_proj, tf->w_proj, C, H, H, 128));
+
+    tf->dbl = (flux_dbl_t *)calloc((size_t)tf->cfg.n_double, sizeof(flux_dbl_t));
+    tf->sgl = (flux_sgl_t *)calloc((size_t)tf->cfg.n_single, sizeof(flux_sgl_t));
+    if (!tf->dbl || !tf->sgl) { rc = iris_fail(IRIS_CUDA_ERR_OOM, "block tables"); goto done; }
+
+    static const char *qkv_name[2][3] = {{"attn.add_q_proj", "attn.add_k_proj", "attn.add_v_proj"},
+                                         {"attn.to_q", "attn.to_k", "attn.to_v"}};
+    static const char *out_name[2] = {"attn.to_add_out", "attn.to_out.0"};
+    static const char *ff_name[2] = {"ff_context", "ff"};
+    static const char *qn_name[2] = {"attn.norm_added_q", "attn.norm_q"};
+    static const char *kn_name[2] = {"attn.norm_added_k", "attn.norm_k"};
+    for (int i = 0; i < tf->cfg.n_double; i++) {
+        flux_dbl_t *b = &tf->dbl[i];
+        for (int s = 0; s < 2; s++) {
+            ALLOC(b->w_qkv[s], (size_t)3 * H * H);
+            ALLOC(b->w_out[s], (size_t)H * H);
+            ALLOC(b->w_in[s], (size_t)2 * F * H);
+            ALLOC(b->w_down[s], (size_t)H * F);
+            b->qn[s] = (float *)iris_dmalloc(128 * 4);
+            b->kn[s] = (float *)iris_dmalloc(128 * 4);
+            if (!b->qn[s] || !b->kn[s]) { rc = IRIS_CUDA_ERR_OOM; goto done; }
+            for (int j = 0; j < 3; j++) {
+                snprintf(nm, sizeof(nm), "transformer_blocks.%d.%s.weight", i, qkv_name[s][j]);
+                CHK(wsrc_get(ws, nm, (size_t)H * H, b->w_qkv[s] + (size_t)j * H * H));
+            }
+            snprintf(nm, sizeof(nm), "transformer_blocks.%d.%s.weight", i, out_name[s]);
+            CHK(wsrc_get(ws, nm, (size_t)H * H, b->w_out[s]));
+            snprintf(nm, sizeof(nm), "transformer_blocks.%d.%s.linear_in.weight", i, ff_name[s]);
+            CHK(wsrc_get(ws, nm, (size_t)2 * F * H, tmp));
+            iris_count_launch(1);
+            CHK(iris_cuda_check(iris_launch_interleave_gate_up(b->w_in[s], tmp, F, H, g_rt.stream), nm));
+            snprintf(nm, sizeof(nm), "transformer_blocks.%d.%s.linear_out.weight", i, ff_name[s]);
+            CHK(wsrc_get(ws, nm, (size_t)H * F, b->w_down[s]));
+            snprintf(nm, sizeof(nm), "transformer_blocks.%d.%s.weight", i, qn_name[s]);
+            CHK(wsrc_get_f32(ws, nm, 128, b->qn[s], tmp + (size_t)2 * F * H));
+            snprintf(nm, sizeof(nm), "transformer_blocks.%d.%s.weight", i, kn_name[s]);
+            CHK(wsrc_get_f32(ws, nm, 128, b->kn[s], tmp + (size_t)2 * F * H + 128));
+            CHK(mk_tmap(&b->tm_qkv[s], b->w_qkv[s], 3 * H, H, H, 256));
+            CHK(mk_tmap(&b->tm_out[s], b->w_out[s], H, H, H, 256));
+            CHK(mk_tmap(&b->tm_in[s], b->w_in[s], 2 * F, H, H, 256));
+            CHK(mk_tmap(&b->tm_down[s], b->w_down[s], H, F, F, 256));
+        }
+    }
+    for (int i = 0; i < tf->cfg.n_single; i++) {
+        flux_sgl_t *b = &tf->sgl[i];
+        ALLOC(b->w_fused, (size_t)(3 * H + 2 * F) * H);
+        ALLOC(b->w_out, (size_t)H * (H + F));
+        b->qn = (float *)iris_dmalloc(128 * 4);
+        b->kn = (float *)iris_dmalloc(128 * 4);
+        if (!b->qn || !b->kn) { rc = IRIS_CUDA_ERR_OOM; goto done; }
+        snprintf(nm, sizeof(nm), "single_transformer_blocks.%d.attn.to_qkv_mlp_proj.weight", i);
+        CHK(wsrc_get(ws, nm, (size_t)(3 * H + 2 * F) * H, tmp));
+        CHK(iris_cuda_check(cudaMemcpyAsync(b->w_fused, tmp, (size_t)3 * H * H * 2,
+                                            cudaMemcpyDeviceToDevice, g_rt.stream), nm));
+        iris_count_launch(1);
+        CHK(iris_cuda_check(iris_launch_interleave_gate_up(b->w_fused + (size_t)3 * H * H,
+                                                           tmp + (size_t)3 * H * H, F, H,
+                                                           g_rt.stream), nm));
+        snprintf(nm, sizeof(nm), "single_transformer_blocks.%d.attn.to_out.weight", i);
+        CHK(wsrc_get(ws, nm, (size_t)H * (H + F), b->w_out));
+        /* norm weights go through a temp slot that the next fused weight does not overwrite
+           before the conversion kernel ran: same stream, so ordering is guaranteed */
+        snprintf(nm, sizeof(nm), "single_transformer_blocks.%d.attn.norm_q.weight", i);
+        CHK(wsrc_get_f32(ws, nm, 128, b->qn, tmp));
+        snprintf(nm, sizeof(nm), "single_transformer_blocks.%d.attn.norm_k.weight", i);
+        CHK(wsrc_get_f32(ws, nm, 128, b->kn, tmp + 128));
+        CHK(mk_tmap(&b->tm_fused, b->w_fused, 3 * H + 2 * F, H, H, 256));
+        CHK(mk_tmap(&b->tm_out, b->w_out, H, H + F, H + F, 256));
+    }
+    tf->t_dev = (float *)iris_dmalloc(4 * 4);
+    tf->sincos = (float *)iris_dmalloc(256 * 4);
+    tf->temb_h = (float *)iris_dmalloc((size_t)H * 4);
+    tf->temb = (float *)iris_dmalloc((size_t)H * 4);
+    tf->mods = (float *)iris_dmalloc((size_t)17 * H * 4);
+    if (!tf->t_dev || !tf->sincos || !tf->temb_h || !tf->temb || !tf->mods) {
+        rc = IRIS_CUDA_ERR_OOM;
+        goto done;
+    }
+    rc = iris_cuda_check(cudaStreamSynchronize(g_rt.stream), "weight upload");
+#undef CHK
+#undef ALLOC
+done:
+    cudaStreamSynchronize(g_rt.stream);
+    iris_dfree(tmp);
+    return rc;
+}
+
+static void plan_free(flux_plan_t *P);
+
+void iris_cuda_flux_free(iris_cuda_flux_t *tf) {
+    if (!tf) return;
+    cudaStreamSynchronize(g_rt.stream);
+    plan_free(&tf->plan);
+    iris_dfree(tf->w_x); iris_dfree(tf->w_ctx); iris_dfree(tf->w_t1); iris_dfree(tf->w_t2);
+    iris_dfree(tf->w_mod); iris_dfree(tf->w_proj);
+    if (tf->dbl) {
+        for (int i = 0; i < tf->cfg.n_double; i++)
+            for (int s = 0; s < 2; s++) {
+                iris_dfree(tf->dbl[i].w_qkv[s]); iris_dfree(tf->dbl[i].w_out[s]);
+                iris_dfree(tf->dbl[i].w_in[s]); iris_dfree(tf->dbl[i].w_down[s]);
+                iris_dfree(tf->dbl[i].qn[s]); iris_dfree(tf->dbl[i].kn[s]);
+            }
+        free(tf->dbl);
+    }
+    if (tf->sgl) {
+        for (int i = 0; i < tf->cfg.n_single; i++) {
+            iris_dfree(tf->sgl[i].w_fused); iris_dfree(tf->sgl[i].w_out);
+            iris_dfree(tf->sgl[i].qn); iris_dfree(tf->sgl[i].kn);
+        }
+        free(tf->sgl);
+    }
+    iris_dfree(tf->t_dev); iris_dfree(tf->sincos); iris_dfree(tf->temb_h);
+    iris_dfree(tf->temb); iris_dfree(tf->mods);
+    free(tf);
+}
+
+static iris_cuda_flux_t *flux_new(const iris_cuda_flux_config_t *cfg) {
+    if (check_cfg(cfg)) return NULL;
+    iris_cuda_flux_t *tf = (iris_cuda_flux_t *)calloc(1, sizeof(*tf));
+    if (!tf) { iris_fail(IRIS_CUDA_ERR_OOM, "model struct"); return NULL; }
+    tf->cfg = *cfg;
+    tf->H = cfg->hidden;
+    tf->F = cfg->mlp;
+    tf->C = cfg->channels;
+    tf->T = cfg->text_dim;
+    tf->NH = cfg->heads;
+    return tf;
+}
+
+/* Parse transformer/config.json with the keys and defaults of the reference's
+ * parse_transformer_config (iris_transformer_flux.c:395-455, defaults :5309-5320). */
+static int parse_config(const char *model_dir, iris_cuda_flux_config_t *c) {
+    c->hidden = 3072; c->heads = 24; c->head_dim = 128; c->mlp = 9216;
+    c->n_double = 5; c->n_single = 20; c->text_dim = 7680; c->channels = 128;
+    c->rope_theta = 2000.0f;
+    char path[1200];
+    snprintf(path, sizeof(path), "%s/transformer/config.json", model_dir);
+    FILE *f = fopen(path, "rb");
+    if (!f) return 0;
+    char buf[8192];
+    size_t n = fread(buf, 1, sizeof(buf) - 1, f);
+    fclose(f);
+    buf[n] = 0;
+    double v, heads = 0, hd = 0;
+    if (json_get_number(buf, "num_attention_heads", &v) == 0) heads = v;
+    if (json_get_number(buf, "attention_head_dim", &v) == 0) hd = v;
+    if (heads <= 0 || hd <= 0) return 0;
+    c->heads = (int)heads;
+    c->head_dim = (int)hd;
+    c->hidden = c->heads * c->head_dim;
+    double ratio = 3.0;
+    if (json_get_number(buf, "mlp_ratio", &v) == 0 && v > 0) ratio = v;
+    c->mlp = (int)(c->hidden * (float)ratio);
+    if (json_get_number(buf, "num_layers", &v) == 0 && v > 0) c->n_double = (int)v;
+    if (json_get_number(buf, "num_single_layers", &v) == 0 && v > 0) c->n_single = (int)v;
+    if (json_get_number(buf, "joint_attention_dim", &v) == 0 && v > 0) c->text_dim = (int)v;
+    if (json_get_number(buf, "in_channels", &v) == 0 && v > 0) c->channels = (int)v;
+    if (json_get_number(buf, "rope_theta", &v) == 0 && v > 0) c->rope_theta = (float)v;
+    return 0;
+}
+
+iris_cuda_flux_t *iris_cuda_flux_load(const char *model_dir) {
+    if (iris_rt_ensure() != IRIS_CUDA_OK) return NULL;
+    iris_cuda_flux_config_t cfg;
+    parse_config(model_dir, &cfg);
+    iris_cuda_flux_t *tf = flux_new(&cfg);
+    if (!tf) return NULL;
+    snprintf(tf->model_dir, sizeof(tf->model_dir), "%s", model_dir);
+    wsrc_t ws;
+    memset(&ws, 0, sizeof(ws));
+    char tdir[1200];
+    snprintf(tdir, sizeof(tdir), "%s/transformer", model_dir);
+    if (st_open_dir(&ws.st, tdir) != 0) {
+        iris_fail(IRIS_CUDA_ERR_IO, "cannot open safetensors in %s", tdir);
+        free(tf);
+        return NULL;
+    }
+    int rc = load_weights(tf, &ws);
+    st_close(&ws.st);
+    if (ws.host_stage) cudaFreeHost(ws.host_stage);
+    if (rc) { iris_cuda_flux_free(tf); return NULL; }
+    return tf;
+}
+
+iris_cuda_flux_t *iris_cuda_flux_random(const iris_cuda_flux_config_t *cfg, uint64_t seed,
+                                        float std, int norm_unit) {
+    if (iris_rt_ensure() != IRIS_CUDA_OK) return NULL;
+    iris_cuda_flux_t *tf = flux_new(cfg);
+    if (!tf) return NULL;
+    tf->random = 1;
+    tf->seed = seed;
+    tf->std = std;
+    tf->norm_unit = norm_unit;
+    wsrc_t ws;
+    memset(&ws, 0, sizeof(ws));
+    ws.random = 1;
+    ws.seed = seed;
+    ws.std = std;
+    ws.norm_unit = norm_unit;
+    if (load_weights(tf, &ws)) { iris_cuda_flux_free(tf); return NULL; }
+    return tf;
+}
+
+int iris_cuda_flux_get_config(const iris_cuda_flux_t *tf, iris_cuda_flux_config_t *out) {
+    if (!tf || !out) return iris_fail(IRIS_CUDA_ERR_ARG, "null argument");
+    *out = tf->cfg;
+    return 0;
+}
+
+size_t iris_cuda_flux_weight_bytes(const iris_cuda_flux_t *tf) { return tf ? tf->weight_bytes : 0; }
+
+int iris_cuda_flux_read_weight(iris_cuda_flux_t *tf, const char *name, uint16_t *out, size_t numel) {
+    if (!tf || !name || !out) return iris_fail(IRIS_CUDA_ERR_ARG, "null argument");
+    if (tf->random) {
+        uint16_t *d = (uint16_t *)iris_dmalloc(numel * 2);
+        if (!d) return IRIS_CUDA_ERR_OOM;
+        wsrc_t ws;
+        memset(&ws, 0, sizeof(ws));
+        ws.random = 1; ws.seed = tf->seed; ws.std = tf->std; ws.norm_unit = tf->norm_unit;
+        int rc = wsrc_get(&ws, name, numel, d);
+        if (!rc) rc = iris_cuda_check(cudaMemcpyAsync(out, d, numel * 2, cudaMemcpyDeviceToHost,
+                                                      g_rt.stream), "read weight");
+        cudaStreamSynchronize(g_rt.stream);
+        iris_dfree(d);
+        return rc;
+    }
+    st_model_t st;
+    char tdir[1200];
+    snprintf(tdir, sizeof(tdir), "%s/transformer", tf->model_dir);
+    if (st_open_dir(&st, tdir) != 0) return iris_fail(IRIS_CUDA_ERR_IO, "cannot reopen %s", tdir);
+    const st_tensor_t *t = st_find(&st, name);
+    int rc = t ? st_read_bf16(&st, t, out, numel) : -1;
+    st_close(&st);
+    return rc ? iris_fail(IRIS_CUDA_ERR_IO, "tensor %s unreadable", name) : 0;
+}
+
+/* ------------------------------------------------------------------ plan */
+static void plan_free(flux_plan_t *P) {
+    if (P->graph_ok) {
+        cudaGraphExecDestroy(P->gexec);
+        cudaGraphDestroy(P->graph);
+    }
+    iris_dfree(P->hidden); iris_dfree(P->lat_in); iris_dfree(P->out); iris_dfree(P->txt_f32);
+    iris_dfree(P->rope_cos); iris_dfree(P->rope_sin); iris_dfree(P->xmod); iris_dfree(P->q);
+    iris_dfree(P->k); iris_dfree(P->v); iris_dfree(P->attn); iris_dfree(P->mlp);
+    iris_dfree(P->cat); iris_dfree(P->tok_img); iris_dfree(P->tok_txt);
+    memset(P, 0, sizeof(*P));
+}
+
+/* RoPE per token and rotation pair, computed exactly like the reference's
+ * tables: base_freq[d] = 1/theta^(2d/32), angle = pos * base_freq[d] for the
+ * T, H, W, L axes (compute_rope_2d :897, compute_rope_2d_with_t_offset :961,
+ * compute_rope_text :1055).  Text rows: (0, 0, 0, i); image rows: (T, y, x, 0). */
+static void fill_rope(const iris_cuda_flux_t *tf, const flux_plan_t *P, float *cs, float *sn) {
+    float base[16];
+    for (int d = 0; d < 16; d++) base[d] = 1.0f / powf(tf->cfg.rope_theta, (float)(2 * d) / 32.0f);
+    int row = 0;
+    for (int i = 0; i < P->s_txt; i++, row++) {
+        float *c = cs + (size_t)row * 64, *s = sn + (size_t)row * 64;
+        for (int p = 0; p < 48; p++) { c[p] = 1.0f; s[p] = 0.0f; }
+        for (int d = 0; d < 16; d++) {
+            float a = (float)i * base[d];
+            c[48 + d] = cosf(a);
+            s[48 + d] = sinf(a);
+        }
+    }
+    for (int r = -1; r < P->num_refs; r++) {
+        int h = r < 0 ? P->img_h : P->ref_h[r], w = r < 0 ? P->img_w : P->ref_w[r];
+        int t = r < 0 ? 0 : P->ref_t[r];
+        for (int y = 0; y < h; y++)
+            for (int x = 0; x < w; x++, row++) {
+                float *c = cs + (size_t)row * 64, *s = sn + (size_t)row * 64;
+                for (int d = 0; d < 16; d++) {
+                    float at = (float)t * base[d], ay = (float)y * base[d], ax = (float)x * base[d];
+                    c[d] = t ? cosf(at) : 1.0f;
+                    s[d] = t ? sinf(at) : 0.0f;
+                    c[16 + d] = cosf(ay);
+                    s[16 + d] = sinf(ay);
+                    c[32 + d] = cosf(ax);
+                    s[32 + d] = sinf(ax);
+                    c[48 + d] = 1.0f;
+                    s[48 + d] = 0.0f;
+                }
+            }
+    }
+}
+
+static int plan_ensure(iris_cuda_flux_t *tf, int s_txt, int img_h, int img_w,
+                       const iris_cuda_ref_t *refs, int num_refs) {
+    flux_plan_t *P = &tf->plan;
+    if (num_refs < 0 || num_refs > MAXREFS) return iris_fail(IRIS_CUDA_ERR_ARG, "num_refs");
+    if (s_txt <= 0 || img_h <= 0 || img_w <= 0) return iris_fail(IRIS_CUDA_ERR_ARG, "empty input");
+    int same = P->valid && P->s_txt == s_txt && P->img_h == img_h && P->img_w == img_w &&
+               P->num_refs == num_refs;
+    for (int r = 0; same && r < num_refs; r++)
+        same = P->ref_h[r] == refs[r].h && P->ref_w[r] == refs[r].w && P->ref_t[r] == refs[r].t_offset;
+    if (same) return 0;
+    cudaStreamSynchronize(g_rt.stream);
+    plan_free(P);
+    int H = tf->H, F = tf->F, C = tf->C, T = tf->T;
+    P->s_txt = s_txt; P->img_h = img_h; P->img_w = img_w; P->num_refs = num_refs;
+    P->n_img = img_h * img_w;
+    P->n_img_total = P->n_img;
+    for (int r = 0; r < num_refs; r++) {
+        if (refs[r].h <= 0 || refs[r].w <= 0) return iris_fail(IRIS_CUDA_ERR_ARG, "empty ref");
+        P->ref_h[r] = refs[r].h; P->ref_w[r] = refs[r].w; P->ref_t[r] = refs[r].t_offset;
+        P->n_img_total += refs[r].h * refs[r].w;
+    }
+    int S = P->S = s_txt + P->n_img_total;
+    size_t sH = (size_t)S * H;
+#define PA(p, bytes) do { if (!((p) = iris_dmalloc(bytes))) goto oom; } while (0)
+    PA(P->hidden, sH * 4);
+    PA(P->lat_in, (size_t)C * P->n_img_total * 4);
+    PA(P->out, (size_t)C * P->n_img * 4);
+    PA(P->txt_f32, (size_t)s_txt * T * 4);
+    PA(P->rope_cos, (size_t)S * 64 * 4);
+    PA(P->rope_sin, (size_t)S * 64 * 4);
+    PA(P->xmod, sH * 2);
+    PA(P->q, sH * 2);
+    PA(P->k, sH * 2);
+    PA(P->v, sH * 2);
+    PA(P->attn, sH * 2);
+    PA(P->mlp, (size_t)S * F * 2);
+    PA(P->cat, (size_t)S * (H + F) * 2);
+    PA(P->tok_img, (size_t)P->n_img_total * C * 2);
+    PA(P->tok_txt, (size_t)s_txt * T * 2);
+#undef PA
+    if (mk_tmap(&P->tm_xmod, P->xmod, S, H, H, 128) || mk_tmap(&P->tm_attn, P->attn, S, H, H, 128) ||
+        mk_tmap(&P->tm_mlp, P->mlp, S, F, F, 128) ||
+        mk_tmap(&P->tm_cat, P->cat, S, H + F, H + F, 128) ||
+        mk_tmap(&P->tm_tok_img, P->tok_img, P->n_img_total, C, C, 128) ||
+        mk_tmap(&P->tm_tok_txt, P->tok_txt, s_txt, T, T, 128)) {
+        plan_free(P);
+        return IRIS_CUDA_ERR_CUDA;
+    }
+    {
+        float *cs = (float *)malloc((size_t)S * 64 * 4), *sn = (float *)malloc((size_t)S * 64 * 4);
+        if (!cs || !sn) { free(cs); free(sn); goto oom; }
+        fill_rope(tf, P, cs, sn);
+        int rc = iris_cuda_check(cudaMemcpy(P->rope_cos, cs, (size_t)S * 64 * 4, cudaMemcpyHostToDevice), "rope") ||
+                 iris_cuda_check(cudaMemcpy(P->rope_sin, sn, (size_t)S * 64 * 4, cudaMemcpyHostToDevice), "rope");
+        free(cs);
+        free(sn);
+        if (rc) { plan_free(P); return IRIS_CUDA_ERR_CUDA; }
+    }
+    P->valid = 1;
+    return 0;
+oom:
+    plan_free(P);
+    return iris_fail(IRIS_CUDA_ERR_OOM, "activation buffers for S=%d", S);
+}
+
+/* ------------------------------------------------------------------ forward */
+static void gp_init(IrisGemmParams *p, const CUtensorMap *ta, int N, int K, int mode) {
+    memset(p, 0, sizeof(*p));
+    p->tmap_a = *ta;
+    p->N = N;
+    p->K = K;
+    p->mode = mode;
+    p->bn = 256;
+    p->eps = 1e-6f;
+    p->status = g_rt.d_status;
+}
+
+static void gp_group(IrisGemmParams *p, int g, const CUtensorMap *tb, int row0, int rows) {
+    p->tmap_b[g] = *tb;
+    p->row0[g] = row0;
+    p->rows[g] = rows;
+    if (g + 1 > p->ngroups) p->ngroups = g + 1;
+}
+
+typedef struct {
+    int rc;
+    uint64_t kernels;
+} enq_t;
+
+static void enq(enq_t *E, cudaError_t e, const char *what) {
+    E->kernels++;
+    if (!E->rc && e != cudaSuccess) E->rc = iris_cuda_check(e, what);
+}
+
+static void enq_gemm(enq_t *E, const IrisGemmParams *p, const char *what) {
+    enq(E, iris_launch_gemm(p, g_rt.num_sms, g_rt.stream), what);
+}
+
+/* timestep embedding and every modulation vector of the step */
+static void enq_mods(iris_cuda_flux_t *tf, enq_t *E) {
+    cudaStream_t st = g_rt.stream;
+    const int H = tf->H;
+    enq(E, iris_launch_timestep_sincos(tf->t_dev, 1000.0f, tf->sincos, 256, st), "sincos");
+    enq(E, iris_launch_gemv(tf->w_t1, tf->sincos, NULL, tf->temb_h, H, 256, 0, 1, st), "t_fc1");
+    enq(E, iris_launch_gemv(tf->w_t2, tf->temb_h, NULL, tf->temb, H, H, 0, 0, st), "t_fc2");
+    enq(E, iris_launch_gemv(tf->w_mod, tf->temb, NULL, tf->mods, 17 * H, H, 1, 0, st), "mods");
+}
+
+/* input projections: hidden = [txt_in(ctx); img_in(latent tokens)] */
+static void enq_embed(iris_cuda_flux_t *tf, enq_t *E) {
+    flux_plan_t *P = &tf->plan;
+    cudaStream_t st = g_rt.stream;
+    const int H = tf->H, C = tf->C, T = tf->T, St = P->s_txt, Si = P->n_img_total;
+    IrisGemmParams gp;
+    size_t off = 0;
+    int row = 0;
+    for (int r = -1; r < P->num_refs; r++) {
+        int n = r < 0 ? P->n_img : P->ref_h[r] * P->ref_w[r];
+        enq(E, iris_launch_nchw_to_tokens(P->lat_in + off, C, n, P->tok_img + (size_t)row * C, C, st),
+            "nchw_to_tokens");
+        off += (size_t)C * n;
+        row += n;
+    }
+    enq(E, iris_launch_f32_to_bf16(P->txt_f32, P->tok_txt, (long)St * T, st), "txt_bf16");
+    gp_init(&gp, &P->tm_tok_txt, H, T, IRIS_EPI_F32);
+    gp_group(&gp, 0, &tf->tm_ctx, 0, St);
+    gp.out = P->hidden;
+    gp.ldo = H;
+    enq_gemm(E, &gp, "txt_in");
+    gp_init(&gp, &P->tm_tok_img, H, C, IRIS_EPI_F32);
+    gp_group(&gp, 0, &tf->tm_x, 0, Si);
+    gp.out = P->hidden + (size_t)St * H;
+    gp.ldo = H;
+    enq_gemm(E, &gp, "img_in");
+}
+
+/* double-stream block i: group 0 = text rows [0, St), group 1 = image rows */
+static void enq_double(iris_cuda_flux_t *tf, int i, enq_t *E) {
+    flux_plan_t *P = &tf->plan;
+    cudaStream_t st = g_rt.stream;
+    const int H = tf->H, F = tf->F, NH = tf->NH, St = P->s_txt, Si = P->n_img_total, S = P->S;
+    const float *mi = tf->mods, *mt = tf->mods + (size_t)6 * H;
+    flux_dbl_t *b = &tf->dbl[i];
+    IrisGemmParams gp;
+    enq(E, iris_launch_adaln(P->hidden, H, P->xmod, H, S, H, mt, mt + H, mi, mi + H, St, 1e-6f, st),
+        "adaln1");
+    gp_init(&gp, &P->tm_xmod, 3 * H, H, IRIS_EPI_QKV);
+    gp_group(&gp, 0, &b->tm_qkv[0], 0, St);
+    gp_group(&gp, 1, &b->tm_qkv[1], St, Si);
+    gp.qnorm[0] = b->qn[0]; gp.knorm[0] = b->kn[0];
+    gp.qnorm[1] = b->qn[1]; gp.knorm[1] = b->kn[1];
+    gp.rope_cos = P->rope_cos; gp.rope_sin = P->rope_sin;
+    gp.q = P->q; gp.k = P->k; gp.v = P->v; gp.ldqkv = H; gp.H = H;
+    enq_gemm(E, &gp, "dbl_qkv");
+    enq(E, iris_launch_attention(P->q, H, P->k, P->v, H, P->attn, H, S, S, NH,
+                                 1.0f / sqrtf(128.0f), NULL, st), "dbl_attn");
+    gp_init(&gp, &P->tm_attn, H, H, IRIS_EPI_RESID_GATE);
+    gp_group(&gp, 0, &b->tm_out[0], 0, St);
+    gp_group(&gp, 1, &b->tm_out[1], St, Si);
+    gp.out = P->hidden; gp.ldo = H;
+    gp.gate[0] = mt + 2 * H; gp.gate[1] = mi + 2 * H;
+    enq_gemm(E, &gp, "dbl_out");
+    enq(E, iris_launch_adaln(P->hidden, H, P->xmod, H, S, H, mt + 3 * H, mt + 4 * H, mi + 3 * H,
+                             mi + 4 * H, St, 1e-6f, st), "adaln2");
+    gp_init(&gp, &P->tm_xmod, 2 * F, H, IRIS_EPI_SWIGLU);
+    gp_group(&gp, 0, &b->tm_in[0], 0, St);
+    gp_group(&gp, 1, &b->tm_in[1], St, Si);
+    gp.mlp_out = P->mlp; gp.ld_mlp = F; gp.mlp_col0 = 0; gp.swiglu_base = 0;
+    enq_gemm(E, &gp, "dbl_mlp_in");
+    gp_init(&gp, &P->tm_mlp, H, F, IRIS_EPI_RESID_GATE);
+    gp_group(&gp, 0, &b->tm_down[0], 0, St);
+    gp_group(&gp, 1, &b->tm_down[1], St, Si);
+    gp.out = P->hidden; gp.ldo = H;
+    gp.gate[0] = mt + 5 * H; gp.gate[1] = mi + 5 * H;
+    enq_gemm(E, &gp, "dbl_mlp_out");
+}
+
+/* single-stream block i over the whole [TXT, IMG] sequence */
+static void enq_single(iris_cuda_flux_t *tf, int i, enq_t *E) {
+    flux_plan_t *P = &tf->plan;
+    cudaStream_t st = g_rt.stream;
+    const int H = tf->H, F = tf->F, NH = tf->NH, S = P->S;
+    const float *ms = tf->mods + (size_t)12 * H;
+    flux_sgl_t *b = &tf->sgl[i];
+    IrisGemmParams gp;
+    enq(E, iris_launch_adaln(P->hidden, H, P->xmod, H, S, H, ms, ms + H, NULL, NULL, S, 1e-6f, st),
+        "adaln_s");
+    gp_init(&gp, &P->tm_xmod, 3 * H + 2 * F, H, IRIS_EPI_SINGLE);
+    gp_group(&gp, 0, &b->tm_fused, 0, S);
+    gp.qnorm[0] = b->qn; gp.knorm[0] = b->kn;
+    gp.rope_cos = P->rope_cos; gp.rope_sin = P->rope_sin;
+    gp.q = P->q; gp.k = P->k; gp.v = P->v; gp.ldqkv = H; gp.H = H;
+    gp.mlp_out = P->cat; gp.ld_mlp = H + F; gp.mlp_col0 = H; gp.swiglu_base = 3 * H;
+    enq_gemm(E, &gp, "sgl_fused");
+    enq(E, iris_launch_attention(P->q, H, P->k, P->v, H, P->cat, H + F, S, S, NH,
+                                 1.0f / sqrtf(128.0f), NULL, st), "sgl_attn");
+    gp_init(&gp, &P->tm_cat, H, H + F, IRIS_EPI_RESID_GATE);
+    gp_group(&gp, 0, &b->tm_out, 0, S);
+    gp.out = P->hidden; gp.ldo = H;
+    gp.gate[0] = ms + 2 * H;
+    enq_gemm(E, &gp, "sgl_out");
+}
+
+/* final layer on the target image rows only (scale first, then shift: :4277-4281) */
+static void enq_final(iris_cuda_flux_t *tf, enq_t *E) {
+    flux_plan_t *P = &tf->plan;
+    const int H = tf->H, C = tf->C, St = P->s_txt;
+    const float *mf = tf->mods + (size_t)15 * H;
+    IrisGemmParams gp;
+    enq(E, iris_launch_adaln(P->hidden + (size_t)St * H, H, P->xmod, H, P->n_img, H, mf + H, mf,
+                             NULL, NULL, P->n_img, 1e-6f, g_rt.stream), "adaln_final");
+    gp_init(&gp, &P->tm_xmod, C, H, IRIS_EPI_F32_NCHW);
+    gp.bn = 128;
+    gp_group(&gp, 0, &tf->tm_proj, 0, P->n_img);
+    gp.out = P->out;
+    gp.nchw_rows = P->n_img;
+    enq_gemm(E, &gp, "proj_out");
+}
+
+/* Queue one forward over the current plan: reads P->lat_in, P->txt_f32 and
+ * tf->t_dev, writes P->out. */
+static int enqueue_forward(iris_cuda_flux_t *tf, enq_t *E) {
+    enq_mods(tf, E);
+    enq_embed(tf, E);
+    for (int i = 0; i < tf->cfg.n_double; i++) enq_double(tf, i, E);
+    for (int i = 0; i < tf->cfg.n_single; i++) enq_single(tf, i, E);
+    enq_final(tf, E);
+    return E->rc;
+}
+
+/* Test hook for per-block parity: run ONE block on a caller-supplied hidden
+ * state.  hidden [txt_seq + img_h*img_w, H] f32 host buffer in [TXT, IMG]
+ * order, updated in place; the modulation vectors come from timestep t.
+ * kind 0 = double block (the reference's double_block_forward, :2366),
+ * kind 1 = single block (single_block_forward, :3761). */
+int iris_cuda_flux_run_block(iris_cuda_flux_t *tf, int kind, int idx, float *hidden, int txt_seq,
+                             int img_h, int img_w, float t) {
+    if (!tf || !hidden) return iris_fail(IRIS_CUDA_ERR_ARG, "null argument");
+    if ((kind == 0 && (idx < 0 || idx >= tf->cfg.n_double)) ||
+        (kind == 1 && (idx < 0 || idx >= tf->cfg.n_single)) || kind < 0 || kind > 1)
+        return iris_fail(IRIS_CUDA_ERR_ARG, "block index");
+    int rc = plan_ensure(tf, txt_seq, img_h, img_w, NULL, 0);
+    if (rc) return rc;
+    flux_plan_t *P = &tf->plan;
+    size_t bytes = (size_t)P->S * tf->H * 4;
+    rc = iris_cuda_check(cudaMemcpyAsync(P->hidden, hidden, bytes, cudaMemcpyHostToDevice, g_rt.stream), "h2d");
+    if (!rc) rc = iris_cuda_check(cudaMemcpyAsync(tf->t_dev, &t, 4, cudaMemcpyHostToDevice, g_rt.stream), "t");
+    if (rc) return rc;
+    enq_t E = {0, 0};
+    enq_mods(tf, &E);
+    if (kind == 0) enq_double(tf, idx, &E);
+    else enq_single(tf, idx, &E);
+    iris_count_launch(E.kernels);
+    if (E.rc) return E.rc;
+    rc = iris_cuda_check(cudaMemcpyAsync(hidden, P->hidden, bytes, cudaMemcpyDeviceToHost, g_rt.stream), "d2h");
+    if (!rc) rc = iris_cuda_synchronize();
+    return rc;
+}
+
+/* Run the forward of the current plan (captured once into a CUDA graph). */
+static int run_forward(iris_cuda_flux_t *tf) {
+    flux_plan_t *P = &tf->plan;
+    if (iris_fault("launch"))
+        return iris_fail(IRIS_CUDA_ERR_INJECTED, "injected launch failure");
+    if (!P->graph_ok) {
+        static int no_graph = -1;
+        if (no_graph < 0) no_graph = getenv("IRIS_CUDA_NO_GRAPH") ? 1 : 0;
+        enq_t E = {0, 0};
+        if (no_graph) {
+            int rc = enqueue_forward(tf, &E);
+            iris_count_launch(E.kernels);
+            return rc;
+        }
+        cudaError_t e = cudaStreamBeginCapture(g_rt.stream, cudaStreamCaptureModeThreadLocal);
+        if (e != cudaSuccess) return iris_cuda_check(e, "begin capture");
+        int rc = enqueue_forward(tf, &E);
+        cudaGraph_t g = NULL;
+        e = cudaStreamEndCapture(g_rt.stream, &g);
+        if (rc) { if (g) cudaGraphDestroy(g); return rc; }
+        if (e != cudaSuccess) return iris_cuda_check(e, "end capture");
+        e = cudaGraphInstantiate(&P->gexec, g, 0);
+        if (e != cudaSuccess) { cudaGraphDestroy(g); return iris_cuda_check(e, "graph instantiate"); }
+        P->graph = g;
+        P->graph_ok = 1;
+        P->graph_kernels = E.kernels;
+    }
+    iris_count_launch(P->graph_kernels);
+    return iris_cuda_check(cudaGraphLaunch(P->gexec, g_rt.stream), "graph launch");
+}
+
+/* shared by the public forward entry points and the samplers */
+int iris_flux_plan_and_inputs(iris_cuda_flux_t *tf, const float *d_latent, int img_h, int img_w,
+                              const iris_cuda_ref_t *d_refs, int num_refs, const float *d_txt,
+                              int txt_seq, enum cudaMemcpyKind kind) {
+    int rc = plan_ensure(tf, txt_seq, img_h, img_w, d_refs, num_refs);
+    if (rc) return rc;
+    flux_plan_t *P = &tf->plan;
+    cudaStream_t st = g_rt.stream;
+    size_t nC = (size_t)tf->C;
+    if (d_latent && d_latent != P->lat_in)
+        if ((rc = iris_cuda_check(cudaMemcpyAsync(P->lat_in, d_latent, nC * P->n_img * 4, kind, st),
+                                  "latent copy")))
+            return rc;
+    size_t off = nC * P->n_img;
+    for (int r = 0; r < num_refs; r++) {
+        size_t n = nC * d_refs[r].h * d_refs[r].w;
+        if ((rc = iris_cuda_check(cudaMemcpyAsync(P->lat_in + off, d_refs[r].latent, n * 4, kind, st),
+                                  "ref copy")))
+            return rc;
+        off += n;
+    }
+    if (d_txt && d_txt != P->txt_f32)
+        if ((rc = iris_cuda_check(cudaMemcpyAsync(P->txt_f32, d_txt, (size_t)txt_seq * tf->T * 4,
+                                                  kind, st), "txt copy")))
+            return rc;
+    return 0;
+}
+
+float *iris_flux_plan_latent(iris_cuda_flux_t *tf) { return tf->plan.lat_in; }
+float *iris_flux_plan_out(iris_cuda_flux_t *tf) { return tf->plan.out; }
+float *iris_flux_plan_txt(iris_cuda_flux_t *tf) { return tf->plan.txt_f32; }
+float *iris_flux_t_dev(iris_cuda_flux_t *tf) { return tf->t_dev; }
+int iris_flux_channels(iris_cuda_flux_t *tf) { return tf->C; }
+int iris_flux_text_dim(iris_cuda_flux_t *tf) { return tf->T; }
+
+/* set t on the device (async, from a device or pinned source) and run */
+int iris_flux_run(iris_cuda_flux_t *tf, const float *t_src, enum cudaMemcpyKind kind) {
+    int rc = iris_cuda_check(cudaMemcpyAsync(tf->t_dev, t_src, 4, kind, g_rt.stream), "t copy");
+    if (rc) return rc;
+    return run_forward(tf);
+}
+
+int iris_cuda_flux_forward_dev(iris_cuda_flux_t *tf, const float *d_latent, int img_h, int img_w,
+                               const iris_cuda_ref_t *d_refs, int num_refs, const float *d_txt,
+                               int txt_seq, float timestep, float *d_out) {
+    if (!tf || !d_latent || !d_txt || !d_out) return iris_fail(IRIS_CUDA_ERR_ARG, "null argument");
+    int rc = iris_flux_plan_and_inputs(tf, d_latent, img_h, img_w, d_refs, num_refs, d_txt, txt_seq,
+                                       cudaMemcpyDeviceToDevice);
+    if (rc) return rc;
+    /* timestep through a small device scratch slot, ordered on the stream */
+    rc = iris_cuda_check(cudaMemcpyAsync(tf->t_dev + 1, &timestep, 4, cudaMemcpyHostToDevice,
+                                         g_rt.stream), "t upload");
+    if (rc) return rc;
+    if ((rc = iris_flux_run(tf, tf->t_dev + 1, cudaMemcpyDeviceToDevice))) return rc;
+    return iris_cuda_check(cudaMemcpyAsync(d_out, tf->plan.out,
+                                           (size_t)tf->C * img_h * img_w * 4,
+                                           cudaMemcpyDeviceToDevice, g_rt.stream), "out copy");
+}
+
+static float *forward_host(iris_cuda_flux_t *tf, const float *latent, int h, int w,
+                           const iris_cuda_ref_t *refs, int num_refs, const float *txt, int txt_seq,
+                           float t) {
+    if (!tf || !latent || !txt) { iris_fail(IRIS_CUDA_ERR_ARG, "null argument"); return NULL; }
+    if (iris_fault("h2d")) { iris_fail(IRIS_CUDA_ERR_INJECTED, "injected H2D failure"); return NULL; }
+    int rc = iris_flux_plan_and_inputs(tf, latent, h, w, refs, num_refs, txt, txt_seq,
+                                       cudaMemcpyHostToDevice);
+    if (!rc) rc = iris_cuda_check(cudaMemcpyAsync(tf->t_dev + 1, &t, 4, cudaMemcpyHostToDevice,
+                                                  g_rt.stream), "t upload");
+    if (!rc) rc = iris_flux_run(tf, tf->t_dev + 1, cudaMemcpyDeviceToDevice);
+    size_t n = (size_t)tf->C * h * w;
+    float *out = rc ? NULL : (float *)malloc(n * 4);
+    if (!rc && !out) rc = iris_fail(IRIS_CUDA_ERR_OOM, "output");
+    if (!rc) rc = iris_cuda_check(cudaMemcpyAsync(out, tf->plan.out, n * 4, cudaMemcpyDeviceToHost,
+                                                  g_rt.stream), "out copy");
+    if (!rc) rc = iris_cuda_synchronize();
+    if (rc) { free(out); return NULL; }
+    return out;
+}
+
+float *iris_cuda_transformer_forward(iris_cuda_flux_t *tf, const float *img_latent, int img_h,
+                                     int img_w, const float *txt_emb, int txt_seq, float timestep) {
+    return forward_host(tf, img_latent, img_h, img_w, NULL, 0, txt_emb, txt_seq, timestep);
+}
+
+float *iris_cuda_transformer_forward_with_multi_refs(iris_cuda_flux_t *tf, const float *img_latent,
+                                                     int img_h, int img_w,
+                                                     const iris_cuda_ref_t *refs, int num_refs,
+                                                     const float *txt_emb, int txt_seq,
+                                                     float timestep) {
+    return forward_host(tf, img_latent, img_h, img_w, refs, num_refs, txt_emb, txt_seq, timestep);
+}

@@ -1,0 +1,404 @@
+// Persistent tcgen05 GEMM for the DiT linears, with the block epilogues fused.
+//
+//   C[M, N] = A[M, K] * W[N, K]^T     (bf16 operands, f32 accumulation in TMEM)
+//
+// Replaces the reference's per-linear sgemm calls (iris_linear_nobias /
+// iris_linear_nobias_bf16, iris_kernels.c:220-336; LINEAR_BF16_OR_F32,
+// iris_transformer_flux.c:121) together with the elementwise passes that
+// follow them: QK-RMSNorm + RoPE (:1464, :1026), SiLU-gate * up (:2299),
+// gate * proj + residual (:136) and the split/concat copies of the single
+// block (:3833-3840, :3896-3902).
+//
+// CTA layout (192 threads, one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: A tile 128x64 and W tile bn x 64 per stage
+//   warp 1      TMEM owner + MMA issuer (one thread): 4 x UMMA 128xbnx16 per stage
+//   warps 2..5  epilogue: TMEM -> registers -> fused math -> global
+// Two TMEM accumulators (2 x 256 columns) let the epilogue of tile i overlap
+// the main loop of tile i+1.  Tiles are ordered M-fastest so the CTAs that
+// run concurrently share one weight column band in L2.
+#include "iris_kernels.h"
+#include "ptx.cuh"
+
+#include <cuda_bf16.h>
+
+namespace {
+
+constexpr int BM = 128;
+constexpr int BK = 64;
+constexpr int STAGES = 4;
+constexpr int A_BYTES = BM * BK * 2;        // 16 KB
+constexpr int B_BYTES_MAX = 256 * BK * 2;   // 32 KB
+constexpr int STAGE_BYTES = A_BYTES + B_BYTES_MAX;
+constexpr int NUM_THREADS = 192;
+constexpr int TMEM_COLS = 512;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*barriers*/ + 1024 /*align slack*/;
+
+struct Bars {
+  uint64_t full[STAGES];
+  uint64_t empty[STAGES];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__device__ __forceinline__ void tile_coords(const IrisGemmParams& p, int t, int mt0, int mtot,
+                                            int& g, int& m_local, int& n0) {
+  int nt = t / mtot;
+  int mt = t - nt * mtot;
+  g = (mt < mt0) ? 0 : 1;
+  m_local = g ? mt - mt0 : mt;
+  n0 = nt * p.bn;
+}
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+
+// Store 32 f32 values (cols j0..j0+31 of a chunk) as bf16 to dst (16B aligned).
+__device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float* v) {
+  uint4* d = reinterpret_cast<uint4*>(dst);
+#pragma unroll
+  for (int i = 0; i < 4; i++) {
+    uint4 u;
+    u.x = pack_bf16(v[8 * i + 0], v[8 * i + 1]);
+    u.y = pack_bf16(v[8 * i + 2], v[8 * i + 3]);
+    u.z = pack_bf16(v[8 * i + 4], v[8 * i + 5]);
+    u.w = pack_bf16(v[8 * i + 6], v[8 * i + 7]);
+    d[i] = u;
+  }
+}
+
+// Epilogue for one 128-column chunk that belongs to the Q/K/V region.
+// TMEM loads are warp-collective and always executed by all 32 lanes; only
+// the global-memory traffic is predicated on `valid`.
+__device__ __forceinline__ void epi_qkv_chunk(const IrisGemmParams& p, uint32_t taddr, int g,
+                                              int row, bool valid, int col0) {
+  int which = col0 / p.H;
+  int cin = col0 - which * p.H;
+  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(which == 0 ? p.q : which == 1 ? p.k : p.v);
+  dst += (size_t)row * p.ldqkv + cin;
+  float r = 1.0f;
+  const float* nw = nullptr;
+  if (which < 2) {
+    // pass 1: sum of squares over the 128-wide head (TMEM is re-read in pass 2
+    // rather than keeping 128 values live in registers)
+    nw = (which == 0) ? p.qnorm[g] : p.knorm[g];
+    float ss = 0.f;
+#pragma unroll 1
+    for (int j = 0; j < 4; j++) {
+      float v[32];
+      iris::tmem_ld32(taddr + 32 * j, v);
+#pragma unroll
+      for (int e = 0; e < 32; e++) ss += v[e] * v[e];
+    }
+    r = rsqrtf(ss * (1.0f / 128.0f) + p.eps);
+  }
+#pragma unroll 1
+  for (int j = 0; j < 4; j++) {
+    float v[32];
+    iris::tmem_ld32(taddr + 32 * j, v);
+    if (!valid) continue;
+    if (which < 2) {
+      const float4* w4 = reinterpret_cast<const float4*>(nw + 32 * j);
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        float4 w = __ldg(w4 + e);
+        v[4 * e + 0] = v[4 * e + 0] * r * w.x;
+        v[4 * e + 1] = v[4 * e + 1] * r * w.y;
+        v[4 * e + 2] = v[4 * e + 2] * r * w.z;
+        v[4 * e + 3] = v[4 * e + 3] * r * w.w;
+      }
+      if (p.rope_cos) {
+        const float4* cp = reinterpret_cast<const float4*>(p.rope_cos + (size_t)row * 64 + 16 * j);
+        const float4* sp = reinterpret_cast<const float4*>(p.rope_sin + (size_t)row * 64 + 16 * j);
+#pragma unroll
+        for (int q4 = 0; q4 < 4; q4++) {
+          float4 c = __ldg(cp + q4), s = __ldg(sp + q4);
+          float cc[4] = {c.x, c.y, c.z, c.w}, sn[4] = {s.x, s.y, s.z, s.w};
+#pragma unroll
+          for (int e = 0; e < 4; e++) {
+            int jj = 2 * (4 * q4 + e);
+            float x0 = v[jj], x1 = v[jj + 1];
+            v[jj] = x0 * cc[e] - x1 * sn[e];
+            v[jj + 1] = x1 * cc[e] + x0 * sn[e];
+          }
+        }
+      }
+    }
+    store_bf16x32(dst + 32 * j, v);
+  }
+}
+
+// Epilogue for a 256-column tile laid out as [gate 128 | up 128].
+__device__ __forceinline__ void epi_swiglu_tile(const IrisGemmParams& p, uint32_t taddr, int row,
+                                                bool valid, int n0) {
+  int f0 = (n0 - p.swiglu_base) >> 1;
+  __nv_bfloat16* dst =
+      reinterpret_cast<__nv_bfloat16*>(p.mlp_out) + (size_t)row * p.ld_mlp + p.mlp_col0 + f0;
+#pragma unroll 1
+  for (int j = 0; j < 4; j++) {
+    float gv[32], uv[32];
+    iris::tmem_ld32(taddr + 32 * j, gv);
+    iris::tmem_ld32(taddr + 128 + 32 * j, uv);
+#pragma unroll
+    for (int e = 0; e < 32; e++) gv[e] = silu_f(gv[e]) * uv[e];
+    if (valid) store_bf16x32(dst + 32 * j, gv);
+  }
+}
+
+__device__ __forceinline__ void epi_plain_chunk(const IrisGemmParams& p, uint32_t taddr, int g,
+                                                int row, int row_local, bool valid, int col0) {
+#pragma unroll 1
+  for (int j = 0; j < 4; j++) {
+    float v[32];
+    iris::tmem_ld32(taddr + 32 * j, v);
+    if (!valid) continue;
+    int c = col0 + 32 * j;
+    if (p.bias) {
+#pragma unroll
+      for (int e = 0; e < 32; e++) v[e] += __ldg(p.bias + c + e);
+    }
+    if (p.mode == IRIS_EPI_BF16) {
+      store_bf16x32(reinterpret_cast<__nv_bfloat16*>(p.out) + (size_t)row * p.ldo + c, v);
+    } else if (p.mode == IRIS_EPI_F32) {
+      float4* d = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (size_t)row * p.ldo + c);
+#pragma unroll
+      for (int e = 0; e < 8; e++) d[e] = make_float4(v[4 * e], v[4 * e + 1], v[4 * e + 2], v[4 * e + 3]);
+    } else if (p.mode == IRIS_EPI_F32_NCHW) {
+      float* d = reinterpret_cast<float*>(p.out) + row_local;
+#pragma unroll
+      for (int e = 0; e < 32; e++) d[(size_t)(c + e) * p.nchw_rows] = v[e];
+    } else {  // IRIS_EPI_RESID_GATE
+      float4* d = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (size_t)row * p.ldo + c);
+      const float4* gp = reinterpret_cast<const float4*>(p.gate[g] + c);
+#pragma unroll
+      for (int e = 0; e < 8; e++) {
+        float4 h = d[e], gg = __ldg(gp + e);
+        h.x += gg.x * v[4 * e];
+        h.y += gg.y * v[4 * e + 1];
+        h.z += gg.z * v[4 * e + 2];
+        h.w += gg.w * v[4 * e + 3];
+        d[e] = h;
+      }
+    }
+  }
+}
+
+__global__ void __launch_bounds__(NUM_THREADS, 1)
+gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars* bars = reinterpret_cast<Bars*>(smem + STAGES * STAGE_BYTES);
+  volatile int* abort_flag = &bars->abort;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+
+  const int mt0 = (p.rows[0] + BM - 1) / BM;
+  const int mt1 = p.ngroups > 1 ? (p.rows[1] + BM - 1) / BM : 0;
+  const int mtot = mt0 + mt1;
+  const int ntiles_n = (p.N + p.bn - 1) / p.bn;
+  const int total = mtot * ntiles_n;
+  const int num_kb = (p.K + BK - 1) / BK;
+  const uint32_t b_bytes = (uint32_t)p.bn * BK * 2;
+  const uint32_t idesc = iris::umma_idesc_bf16_f32(BM, p.bn);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; s++) {
+      iris::mbar_init(&bars->full[s], 1);
+      iris::mbar_init(&bars->empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      iris::mbar_init(&bars->tfull[b], 1);
+      iris::mbar_init(&bars->tempty[b], 128);
+    }
+    iris::mbar_init(&bars->drain, 1);
+    bars->abort = 0;
+    iris::fence_mbar_init();
+    iris::tma_prefetch_desc(&p.tmap_a);
+    iris::tma_prefetch_desc(&p.tmap_b[0]);
+    if (p.ngroups > 1) iris::tma_prefetch_desc(&p.tmap_b[1]);
+  }
+  if (warp == 1) iris::tmem_alloc(&bars->tmem_base, TMEM_COLS);
+  iris::tc_fence_before();
+  __syncthreads();
+  iris::tc_fence_after();
+  const uint32_t tmem_base = bars->tmem_base;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------ TMA producer
+    int stage = 0;
+    uint32_t phase = 0;
+    long issued = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+      int g, ml, n0;
+      tile_coords(p, t, mt0, mtot, g, ml, n0);
+      int arow = p.row0[g] + ml * BM;
+      for (int kb = 0; kb < num_kb; kb++) {
+        if (!iris::mbar_wait(&bars->empty[stage], phase ^ 1, abort_flag, p.status, IRIS_DEV_ERR_GEMM_PRODUCER)) {
+          ok = false;
+          break;
+        }
+        uint8_t* sa = smem + stage * STAGE_BYTES;
+        uint8_t* sb = sa + A_BYTES;
+        iris::mbar_arrive_expect_tx(&bars->full[stage], A_BYTES + b_bytes);
+        iris::tma_load_2d(sa, &p.tmap_a, &bars->full[stage], kb * BK, arow);
+        iris::tma_load_2d(sb, &p.tmap_b[g], &bars->full[stage], kb * BK, n0);
+        issued++;
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+    }
+    if (!ok) {
+      // Drain: wait (bounded) for the copies this thread issued last, so no
+      // TMA write lands in shared memory after the CTA exits.
+      long n = issued < STAGES ? issued : STAGES;
+      int s = stage;
+      uint32_t ph = phase;
+      for (long i = 0; i < n; i++) {
+        if (--s < 0) { s = STAGES - 1; ph ^= 1; }
+        volatile int no_abort = 0;
+        iris::mbar_wait(&bars->full[s], ph, &no_abort, p.status, IRIS_DEV_ERR_GEMM_DRAIN);
+      }
+    }
+  } else if (warp == 1 && lane == 0) {
+    // ------------------------------------------------ MMA issuer
+    int stage = 0;
+    uint32_t phase = 0;
+    int it = 0;
+    bool ok = true;
+    for (int t = blockIdx.x; t < total && ok; t += gridDim.x, it++) {
+      int buf = it & 1;
+      uint32_t use = (uint32_t)(it >> 1);
+      if (!iris::mbar_wait(&bars->tempty[buf], (use & 1) ^ 1, abort_flag, p.status, IRIS_DEV_ERR_GEMM_MMA)) {
+        ok = false;
+        break;
+      }
+      iris::tc_fence_after();
+      uint32_t d_tmem = tmem_base + buf * 256;
+      for (int kb = 0; kb < num_kb; kb++) {
+        if (!iris::mbar_wait(&bars->full[stage], phase, abort_flag, p.status, IRIS_DEV_ERR_GEMM_MMA)) {
+          ok = false;
+          break;
+        }
+        iris::tc_fence_after();
+        uint32_t sa = iris::smem_u32(smem + stage * STAGE_BYTES);
+        uint32_t sb = sa + A_BYTES;
+        uint64_t adesc = iris::umma_desc_k_sw128(sa);
+        uint64_t bdesc = iris::umma_desc_k_sw128(sb);
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; kk++) {
+          // +32 bytes along K inside the 128B swizzle atom = +2 in the >>4 address field
+          iris::umma_bf16(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0);
+        }
+        iris::umma_commit(&bars->empty[stage]);
+        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+      }
+      if (ok) iris::umma_commit(&bars->tfull[buf]);
+    }
+    if (!ok) {
+      iris::umma_commit(&bars->drain);
+      volatile int no_abort = 0;
+      iris::mbar_wait(&bars->drain, 0, &no_abort, p.status, IRIS_DEV_ERR_GEMM_DRAIN);
+    }
+  } else if (warp >= 2) {
+    // ------------------------------------------------ epilogue
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    int it = 0;
+    for (int t = blockIdx.x; t < total; t += gridDim.x, it++) {
+      int buf = it & 1;
+      uint32_t use = (uint32_t)(it >> 1);
+      if (!iris::mbar_wait(&bars->tfull[buf], use & 1, abort_flag, p.status, IRIS_DEV_ERR_GEMM_EPILOGUE)) break;
+      iris::tc_fence_after();
+      int g, ml, n0;
+      tile_coords(p, t, mt0, mtot, g, ml, n0);
+      int row_local = ml * BM + quarter * 32 + lane;
+      bool valid = row_local < p.rows[g];
+      int row = p.row0[g] + row_local;
+      uint32_t taddr = tmem_base + buf * 256 + ((uint32_t)(quarter * 32) << 16);
+
+      bool swiglu_tile = (p.mode == IRIS_EPI_SWIGLU) ||
+                         (p.mode == IRIS_EPI_SINGLE && n0 >= p.swiglu_base);
+      if (swiglu_tile) {
+        epi_swiglu_tile(p, taddr, row, valid, n0);
+      } else {
+        for (int c = 0; c < p.bn / 128; c++) {
+          int col0 = n0 + c * 128;
+          if (col0 >= p.N) break;
+          if (p.mode == IRIS_EPI_QKV || p.mode == IRIS_EPI_SINGLE)
+            epi_qkv_chunk(p, taddr + c * 128, g, row, valid, col0);
+          else
+            epi_plain_chunk(p, taddr + c * 128, g, row, row_local, valid, col0);
+        }
+      }
+      iris::tc_fence_before();
+      iris::mbar_arrive(&bars->tempty[buf]);
+    }
+  }
+
+  __syncthreads();
+  if (warp == 1) {
+    iris::tc_fence_after();
+    iris::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+}  // namespace
+
+extern "C" int iris_make_tmap_bf16(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t cols,
+                                   uint64_t ld, uint32_t box_rows) {
+  typedef CUresult (*EncodeFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*,
+                               const cuuint64_t*, const cuuint64_t*, const cuuint32_t*,
+                               const cuuint32_t*, CUtensorMapInterleave, CUtensorMapSwizzle,
+                               CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+  static EncodeFn fn = nullptr;
+  if (!fn) {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f, cudaEnableDefault, &q) != cudaSuccess ||
+        q != cudaDriverEntryPointSuccess || !f)
+      return -1;
+    fn = reinterpret_cast<EncodeFn>(f);
+  }
+  if ((reinterpret_cast<uintptr_t>(ptr) & 15) || ((ld * 2) & 15) || box_rows == 0 || box_rows > 256)
+    return -2;
+  cuuint64_t dims[2] = {cols, rows};
+  cuuint64_t strides[1] = {ld * 2};
+  cuuint32_t box[2] = {64, box_rows};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : -3;
+}
+
+static bool g_gemm_attr = false;
+
+extern "C" cudaError_t iris_gemm_init(void) {
+  if (g_gemm_attr) return cudaSuccess;
+  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                       SMEM_BYTES);
+  if (e == cudaSuccess) g_gemm_attr = true;
+  return e;
+}
+
+extern "C" cudaError_t iris_launch_gemm(const IrisGemmParams* p, int num_sms, cudaStream_t stream) {
+  if (!g_gemm_attr) {
+    cudaError_t e = iris_gemm_init();
+    if (e != cudaSuccess) return e;
+  }
+  if (p->bn != 128 && p->bn != 256) return cudaErrorInvalidValue;
+  if (p->K % BK != 0 || p->N % 128 != 0) return cudaErrorInvalidValue;
+  int mt = (p->rows[0] + BM - 1) / BM + (p->ngroups > 1 ? (p->rows[1] + BM - 1) / BM : 0);
+  long total = (long)mt * ((p->N + p->bn - 1) / p->bn);
+  if (total <= 0) return cudaSuccess;
+  int grid = (int)(total < num_sms ? total : num_sms);
+  gemm_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(*p);
+  return cudaGetLastError();
+}
+

@@ -1,0 +1,91 @@
+/*
+ * Shared internals of the iris CUDA backend host code (C11).
+ */
+#ifndef IRIS_INTERNAL_H
+#define IRIS_INTERNAL_H
+
+#include <cuda_runtime_api.h>
+#include <stddef.h>
+#include <stdint.h>
+
+#include "iris_cuda.h"
+#include "iris_kernels.h"
+
+typedef struct {
+    int initialized;
+    int device;
+    int num_sms;
+    int cc_major, cc_minor;
+    cudaStream_t stream;
+    int *d_status;          /* device status word (bounded-wait failures) */
+    uint64_t launches;      /* kernels enqueued (graph replays add their node count) */
+} iris_rt_t;
+
+extern iris_rt_t g_rt;
+
+/* error reporting: sets the thread's last-error string and returns code */
+int iris_fail(int code, const char *fmt, ...);
+/* map a cudaError_t to a status, recording the message; 0 if success */
+int iris_cuda_check(cudaError_t e, const char *what);
+
+/* host-side fault injection (IRIS_CUDA_FAULT=alloc@N|launch@N|h2d@N):
+ * returns 1 when the N-th call of that kind should fail. */
+int iris_fault(const char *kind);
+
+/* device allocation through the library (counts, fault injection) */
+void *iris_dmalloc(size_t bytes);
+void iris_dfree(void *p);
+
+/* note `n` kernel launches (for iris_cuda_kernel_launches) */
+static inline void iris_count_launch(uint64_t n) { g_rt.launches += n; }
+
+/* ensure the runtime is up; returns status */
+int iris_rt_ensure(void);
+
+/* ---------------- safetensors (own reader) ---------------- */
+typedef enum { ST_F32 = 0, ST_F16 = 1, ST_BF16 = 2, ST_OTHER = 3 } st_dtype_t;
+
+typedef struct {
+    char name[256];
+    st_dtype_t dtype;
+    int ndim;
+    int64_t shape[8];
+    size_t offset, nbytes;
+    int file;
+} st_tensor_t;
+
+typedef struct {
+    int nfiles;
+    void *maps[16];
+    size_t sizes[16];
+    size_t data_start[16];
+    int ntensors;
+    st_tensor_t *tensors;
+} st_model_t;
+
+int st_open_dir(st_model_t *m, const char *transformer_dir);
+void st_close(st_model_t *m);
+const st_tensor_t *st_find(const st_model_t *m, const char *name);
+/* convert a tensor to bf16 bits into out (numel elements); returns 0 on success */
+int st_read_bf16(const st_model_t *m, const st_tensor_t *t, uint16_t *out, size_t numel);
+int st_read_f32(const st_model_t *m, const st_tensor_t *t, float *out, size_t numel);
+
+/* simple "key": number extraction from a small JSON text */
+int json_get_number(const char *json, const char *key, double *out);
+
+/* 32-bit CRC (IEEE) of a string; keys the per-tensor RNG streams */
+uint32_t iris_crc32(const char *s);
+
+/* host bf16 helpers */
+static inline uint16_t f32_to_bf16_bits(float f) {
+    union { float f; uint32_t u; } v = {f};
+    uint32_t u = v.u;
+    u += 0x7FFFu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+static inline float bf16_bits_to_f32(uint16_t b) {
+    union { uint32_t u; float f; } v = {(uint32_t)b << 16};
+    return v.f;
+}
+
+#endif

@@ -1,0 +1,130 @@
+/*
+ * Internal C interface between the C host code of the iris CUDA backend and
+ * its sm_100a kernels (.cu files).  Plain C: pointers, sizes and CUtensorMap
+ * descriptors, no C++ types.  Every launcher enqueues work on `stream` and
+ * returns a cudaError_t value (0 = success).
+ */
+#ifndef IRIS_KERNELS_CUDA_H
+#define IRIS_KERNELS_CUDA_H
+
+#include <cuda.h>
+#include <cuda_runtime_api.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* ------------------------------------------------------------------ GEMM
+ * C[M, N] = A[M, K] * B[N, K]^T with bf16 operands (both K-major, row-major
+ * in memory) and f32 accumulation in TMEM, followed by one of the fused
+ * epilogues below.  Rows of A are split into up to two groups (the text and
+ * image streams of a double block), each with its own weight matrix B and
+ * epilogue vectors; groups share N and K. */
+enum {
+    IRIS_EPI_BF16 = 0,        /* out bf16 [row, ldo] (+ bias[col])                         */
+    IRIS_EPI_F32 = 1,         /* out f32  [row, ldo] (+ bias[col])                         */
+    IRIS_EPI_F32_NCHW = 2,    /* out f32 [col, nchw_rows] (channel-major, + bias)          */
+    IRIS_EPI_RESID_GATE = 3,  /* f32 out[row, col] += gate[g][col] * acc                   */
+    IRIS_EPI_QKV = 4,         /* cols [0,H) Q, [H,2H) K, [2H,3H) V; per-head RMSNorm on Q/K
+                                 then pair RoPE from rope_cos/sin[row][64]; bf16 stores     */
+    IRIS_EPI_SWIGLU = 5,      /* 256-col tiles hold [gate 128 | up 128] of 128 features:
+                                 mlp_out[row, mlp_col0 + f] = SiLU(gate) * up (bf16)       */
+    IRIS_EPI_SINGLE = 6,      /* cols < 3H as IRIS_EPI_QKV, cols >= 3H as IRIS_EPI_SWIGLU   */
+};
+
+typedef struct {
+    CUtensorMap tmap_a;       /* A: box {64, 128} rows, 128B swizzle                  */
+    CUtensorMap tmap_b[2];    /* B per group: box {64, bn} rows, 128B swizzle          */
+    int ngroups;
+    int row0[2];              /* first row of each group in A and row-indexed outputs  */
+    int rows[2];              /* rows per group                                        */
+    int N, K;
+    int bn;                   /* 128 or 256 */
+    int mode;
+    void *out;                /* BF16/F32/NCHW/RESID destination                       */
+    int ldo;                  /* elements */
+    int nchw_rows;            /* IRIS_EPI_F32_NCHW: channel stride                      */
+    const float *bias;        /* optional [N]                                          */
+    const float *gate[2];     /* RESID: per group [N]                                  */
+    const float *qnorm[2];    /* QKV: per group [128]                                  */
+    const float *knorm[2];
+    const float *rope_cos;    /* QKV: [rows_total, 64] by absolute row (NULL = no RoPE) */
+    const float *rope_sin;
+    void *q, *k, *v;          /* QKV destinations (bf16) with row stride ldqkv         */
+    int ldqkv;
+    int H;                    /* width of Q, K and V blocks (heads * 128)              */
+    float eps;
+    void *mlp_out;            /* SWIGLU destination (bf16)                             */
+    int ld_mlp;
+    int mlp_col0;
+    int swiglu_base;          /* first column of the gate/up region in N              */
+    int *status;              /* device status word for bounded-wait failures         */
+} IrisGemmParams;
+
+/* Encodes a 2-D bf16 tensor map over a row-major [rows, cols] matrix with
+ * row stride ld (elements) and box {64, box_rows}, 128-byte swizzle. */
+int iris_make_tmap_bf16(CUtensorMap *m, const void *ptr, uint64_t rows, uint64_t cols,
+                        uint64_t ld, uint32_t box_rows);
+
+cudaError_t iris_launch_gemm(const IrisGemmParams *p, int num_sms, cudaStream_t stream);
+
+/* one-time kernel attribute setup (dynamic shared memory limits); called at
+ * library init so that nothing but launches happens during graph capture */
+cudaError_t iris_gemm_init(void);
+cudaError_t iris_attention_init(void);
+
+/* ------------------------------------------------------------------ attention
+ * O = softmax(Q K^T * scale) V for every head, bf16 in/out, f32 softmax.
+ * Q [sq, ldq], K/V [sk, ldk] with head h at columns h*128 .. h*128+127.
+ * key_mask (optional, [sk], 1 = valid) sets masked scores to -1e9 exactly as
+ * the Z-Image reference does. */
+cudaError_t iris_launch_attention(const void *q, int ldq, const void *k, const void *v, int ldk,
+                                  void *o, int ldo, int sq, int sk, int heads, float scale,
+                                  const uint8_t *key_mask, cudaStream_t stream);
+
+/* ------------------------------------------------------------------ row kernels */
+/* out_bf16[r] = (1 + scale_g) * LayerNorm(x[r]) + shift_g, g = (r >= split) */
+cudaError_t iris_launch_adaln(const float *x, int ldx, void *out, int ldout, int rows, int cols,
+                              const float *shift0, const float *scale0, const float *shift1,
+                              const float *scale1, int split, float eps, cudaStream_t stream);
+/* y[n] = act_out(sum_k W[n,k] * act_in(x[k]) + b[n]); W bf16 [N, K]; act 0 none, 1 SiLU */
+cudaError_t iris_launch_gemv(const void *w, const float *x, const float *bias, float *y, int n,
+                             int k, int act_in, int act_out, cudaStream_t stream);
+/* out[i] = [cos(t*1000*f_i), sin(...)] with f_i = exp(-ln(1e4) i/half), t read from *t_dev */
+cudaError_t iris_launch_timestep_sincos(const float *t_dev, float t_scale, float *out, int dim,
+                                        cudaStream_t stream);
+/* NCHW f32 [C, n] -> row-major bf16 [n, C] at row stride ldo */
+cudaError_t iris_launch_nchw_to_tokens(const float *x, int c, int n, void *out, int ldo,
+                                       cudaStream_t stream);
+cudaError_t iris_launch_f32_to_bf16(const float *x, void *out, long n, cudaStream_t stream);
+cudaError_t iris_launch_bf16_to_f32(const void *x, float *out, long n, cudaStream_t stream);
+/* z += dt * v ; or with CFG: z += dt * (vu + g (vc - vu)) */
+cudaError_t iris_launch_euler(float *z, const float *v, const float *v_uncond, float guidance,
+                              float dt, long n, cudaStream_t stream);
+/* seeded N(0, std) bf16 fill (counter-based hash RNG; used for random-init models) */
+cudaError_t iris_launch_randn_bf16(void *out, long n, uint64_t seed, uint64_t stream_id,
+                                   float mean, float std, cudaStream_t stream);
+cudaError_t iris_launch_randn_f32(float *out, long n, uint64_t seed, uint64_t stream_id,
+                                  float mean, float std, cudaStream_t stream);
+
+/* op-level helpers (iris_gpu_* surface) */
+cudaError_t iris_launch_head_rmsnorm_rope(void *x, int ld, int rows, int heads, const float *w,
+                                          float eps, const float *rope_cos,
+                                          const float *rope_sin, cudaStream_t stream);
+cudaError_t iris_launch_silu_mul_bf16(void *gate, const void *up, long n, cudaStream_t stream);
+cudaError_t iris_launch_gated_add_bf16(void *out, const void *gate, const void *proj, int rows,
+                                       int cols, cudaStream_t stream);
+cudaError_t iris_launch_rmsnorm(const float *x, int ldx, const float *w, float *out_f32,
+                                void *out_bf16, int ldout, int rows, int cols, float eps,
+                                const float *mul, cudaStream_t stream);
+/* [gate; up] (2F rows) -> 256-row blocks of [gate 128 | up 128] (GEMM SwiGLU layout) */
+cudaError_t iris_launch_interleave_gate_up(void *dst, const void *src, int F, int cols,
+                                           cudaStream_t stream);
+cudaError_t iris_launch_copy_rows_bf16(void *dst, int ldd, const void *src, int lds, int rows,
+                                       int cols, cudaStream_t stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif

@@ -1,0 +1,267 @@
+"""ctypes binding of libiris_cuda.so (the C ABI declared in include/iris_cuda.h).
+
+Used by the tests, bench.py and __graft_entry__.py.  It loads the in-tree
+library built by ``make -C iris.c_b200 cuda`` and fails loudly when it is
+missing: there is no CPU or framework fallback behind these calls.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+LIB_PATH = os.path.join(HERE, "libiris_cuda.so")
+
+OK = 0
+ERR_ARG, ERR_OOM, ERR_CUDA, ERR_IO, ERR_TIMEOUT, ERR_NODEV, ERR_INJECTED = -1, -2, -3, -4, -5, -6, -7
+
+_fp = C.POINTER(C.c_float)
+_u16p = C.POINTER(C.c_uint16)
+
+
+class FluxConfig(C.Structure):
+    _fields_ = [("hidden", C.c_int), ("heads", C.c_int), ("head_dim", C.c_int), ("mlp", C.c_int),
+                ("n_double", C.c_int), ("n_single", C.c_int), ("text_dim", C.c_int),
+                ("channels", C.c_int), ("rope_theta", C.c_float)]
+
+    @classmethod
+    def from_hf(cls, cfg: dict) -> "FluxConfig":
+        h = cfg["num_attention_heads"] * cfg["attention_head_dim"]
+        return cls(hidden=h, heads=cfg["num_attention_heads"], head_dim=cfg["attention_head_dim"],
+                   mlp=int(h * cfg.get("mlp_ratio", 3.0)), n_double=cfg["num_layers"],
+                   n_single=cfg["num_single_layers"], text_dim=cfg["joint_attention_dim"],
+                   channels=cfg["in_channels"], rope_theta=float(cfg.get("rope_theta", 2000.0)))
+
+
+class Ref(C.Structure):
+    _fields_ = [("latent", _fp), ("h", C.c_int), ("w", C.c_int), ("t_offset", C.c_int)]
+
+
+PROGRESS_CB = C.CFUNCTYPE(None, C.c_int, C.c_int)
+
+# name -> (restype, argtypes) for every exported entry point of include/iris_cuda.h
+SIGNATURES = {
+    "iris_cuda_init": (C.c_int, [C.c_int]),
+    "iris_cuda_available": (C.c_int, []),
+    "iris_cuda_cleanup": (None, []),
+    "iris_cuda_last_error": (C.c_char_p, []),
+    "iris_cuda_device_status": (C.c_int, [C.c_int]),
+    "iris_cuda_synchronize": (C.c_int, []),
+    "iris_cuda_stream": (C.c_void_p, []),
+    "iris_cuda_kernel_launches": (C.c_uint64, []),
+    "iris_cuda_flux_load": (C.c_void_p, [C.c_char_p]),
+    "iris_cuda_flux_random": (C.c_void_p, [C.POINTER(FluxConfig), C.c_uint64, C.c_float, C.c_int]),
+    "iris_cuda_flux_free": (None, [C.c_void_p]),
+    "iris_cuda_flux_get_config": (C.c_int, [C.c_void_p, C.POINTER(FluxConfig)]),
+    "iris_cuda_flux_read_weight": (C.c_int, [C.c_void_p, C.c_char_p, _u16p, C.c_size_t]),
+    "iris_cuda_flux_weight_bytes": (C.c_size_t, [C.c_void_p]),
+    "iris_cuda_transformer_forward": (C.c_void_p, [C.c_void_p, _fp, C.c_int, C.c_int, _fp, C.c_int,
+                                                   C.c_float]),
+    "iris_cuda_transformer_forward_with_multi_refs": (C.c_void_p, [C.c_void_p, _fp, C.c_int, C.c_int,
+                                                                   C.POINTER(Ref), C.c_int, _fp,
+                                                                   C.c_int, C.c_float]),
+    "iris_cuda_flux_forward_dev": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int,
+                                             C.POINTER(Ref), C.c_int, C.c_void_p, C.c_int,
+                                             C.c_float, C.c_void_p]),
+    "iris_cuda_flux_run_block": (C.c_int, [C.c_void_p, C.c_int, C.c_int, _fp, C.c_int, C.c_int,
+                                           C.c_int, C.c_float]),
+    "iris_cuda_official_schedule": (C.c_void_p, [C.c_int, C.c_int]),
+    "iris_cuda_linear_schedule": (C.c_void_p, [C.c_int]),
+    "iris_cuda_zimage_schedule": (C.c_void_p, [C.c_int, C.c_int]),
+    "iris_cuda_init_noise": (C.c_void_p, [C.c_int, C.c_int, C.c_int, C.c_int, C.c_int64]),
+    "iris_cuda_sample_euler": (C.c_void_p, [C.c_void_p, _fp, C.c_int, C.c_int, C.c_int, C.c_int,
+                                            _fp, C.c_int, _fp, C.c_int, PROGRESS_CB]),
+    "iris_cuda_sample_euler_cfg": (C.c_void_p, [C.c_void_p, _fp, C.c_int, C.c_int, C.c_int, C.c_int,
+                                                _fp, C.c_int, _fp, C.c_int, C.c_float, _fp, C.c_int,
+                                                PROGRESS_CB]),
+    "iris_cuda_sample_euler_with_multi_refs": (C.c_void_p, [C.c_void_p, _fp, C.c_int, C.c_int,
+                                                            C.c_int, C.c_int, C.POINTER(Ref), C.c_int,
+                                                            _fp, C.c_int, _fp, C.c_int, PROGRESS_CB]),
+    "iris_cuda_sample_euler_dev": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p,
+                                             C.c_int, C.c_void_p, C.c_int, C.c_float, _fp, C.c_int]),
+    # iris_gpu_* surface (iris_metal.h names)
+    "iris_gpu_tensor_create": (C.c_void_p, [_fp, C.c_size_t]),
+    "iris_gpu_tensor_alloc": (C.c_void_p, [C.c_size_t]),
+    "iris_gpu_tensor_alloc_persistent": (C.c_void_p, [C.c_size_t]),
+    "iris_gpu_tensor_set_persistent": (None, [C.c_void_p, C.c_int]),
+    "iris_gpu_tensor_read": (None, [C.c_void_p, _fp]),
+    "iris_gpu_tensor_write": (None, [C.c_void_p, _fp]),
+    "iris_gpu_tensor_free": (None, [C.c_void_p]),
+    "iris_gpu_tensor_size": (C.c_size_t, [C.c_void_p]),
+    "iris_gpu_tensor_is_f16": (C.c_int, [C.c_void_p]),
+    "iris_gpu_tensor_alloc_f16": (C.c_void_p, [C.c_size_t]),
+    "iris_gpu_tensor_create_bf16": (C.c_void_p, [_fp, C.c_size_t]),
+    "iris_gpu_tensor_f32_to_bf16": (C.c_void_p, [C.c_void_p]),
+    "iris_gpu_tensor_bf16_to_f32": (C.c_void_p, [C.c_void_p]),
+    "iris_gpu_convert_f32_to_bf16_into": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "iris_gpu_convert_bf16_to_f32_into": (C.c_int, [C.c_void_p, C.c_void_p]),
+    "iris_gpu_sync": (None, []),
+    "iris_gpu_batch_begin": (None, []),
+    "iris_gpu_batch_end": (None, []),
+    "iris_gpu_linear_bf16_native": (C.c_void_p, [C.c_void_p, _u16p, C.c_int, C.c_int, C.c_int]),
+    "iris_gpu_linear_bf16_native_into": (C.c_int, [C.c_void_p, C.c_void_p, _u16p, C.c_int, C.c_int,
+                                                   C.c_int]),
+    "iris_gpu_adaln_norm_bf16": (None, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                        C.c_int, C.c_float]),
+    "iris_gpu_qk_rms_norm_bf16": (None, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
+                                         C.c_int, C.c_int, C.c_float]),
+    "iris_gpu_rope_unified_bf16": (None, [C.c_void_p, C.c_void_p, _fp, _fp, _fp, _fp, _fp, _fp,
+                                          C.c_int, C.c_int, C.c_int, C.c_int, C.c_int]),
+    "iris_gpu_rope_2d_bf16": (None, [C.c_void_p, _fp, _fp, C.c_int, C.c_int, C.c_int, C.c_int]),
+    "iris_gpu_attention_fused_bf16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                                C.c_int, C.c_int, C.c_int, C.c_int, C.c_float]),
+    "iris_gpu_silu_mul_bf16": (None, [C.c_void_p, C.c_void_p, C.c_int]),
+    "iris_gpu_gated_add_bf16": (None, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int]),
+    "iris_gpu_concat_seq_bf16": (None, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
+                                        C.c_int]),
+    "iris_gpu_slice_seq_bf16": (None, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int]),
+    "iris_gpu_split_qkv_mlp_bf16": (None, [C.c_void_p] * 6 + [C.c_int] * 3),
+    "iris_gpu_concat_attn_mlp_bf16": (None, [C.c_void_p] * 3 + [C.c_int] * 3),
+    "iris_metal_available": (C.c_int, []),
+    "iris_metal_shaders_available": (C.c_int, []),
+    "iris_bf16_pipeline_available": (C.c_int, []),
+}
+
+_libc = C.CDLL(None)
+_libc.free.argtypes = [C.c_void_p]
+_libc.free.restype = None
+
+
+class IrisCudaError(RuntimeError):
+    pass
+
+
+def load(path: str = LIB_PATH) -> C.CDLL:
+    if not os.path.exists(path):
+        raise IrisCudaError(f"{path} not built: run `make -C iris.c_b200 cuda` (no fallback path exists)")
+    lib = C.CDLL(path)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    return lib
+
+
+_LIB = None
+
+
+def lib() -> C.CDLL:
+    global _LIB
+    if _LIB is None:
+        _LIB = load()
+    return _LIB
+
+
+def last_error() -> str:
+    return (lib().iris_cuda_last_error() or b"").decode()
+
+
+def _f(a: np.ndarray):
+    assert a.dtype == np.float32 and a.flags["C_CONTIGUOUS"]
+    return a.ctypes.data_as(_fp)
+
+
+def _take_floats(ptr, n, shape=None) -> np.ndarray:
+    if not ptr:
+        raise IrisCudaError(last_error() or "call failed")
+    arr = np.ctypeslib.as_array(C.cast(ptr, _fp), shape=(n,)).copy()
+    _libc.free(ptr)
+    return arr.reshape(shape) if shape is not None else arr
+
+
+class Flux:
+    """Resident Flux.2 Klein transformer (libiris_cuda)."""
+
+    def __init__(self, handle):
+        if not handle:
+            raise IrisCudaError(last_error() or "model creation failed")
+        self.h = handle
+        cfg = FluxConfig()
+        lib().iris_cuda_flux_get_config(self.h, C.byref(cfg))
+        self.cfg = cfg
+
+    @classmethod
+    def load(cls, model_dir: str) -> "Flux":
+        return cls(lib().iris_cuda_flux_load(model_dir.encode()))
+
+    @classmethod
+    def random(cls, cfg: FluxConfig, seed: int, std: float = 0.02, norm_unit: bool = False) -> "Flux":
+        return cls(lib().iris_cuda_flux_random(C.byref(cfg), seed, std, int(norm_unit)))
+
+    def close(self):
+        if self.h:
+            lib().iris_cuda_flux_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def weight_bytes(self) -> int:
+        return lib().iris_cuda_flux_weight_bytes(self.h)
+
+    def read_weight(self, name: str, shape) -> np.ndarray:
+        out = np.zeros(int(np.prod(shape)), np.uint16)
+        rc = lib().iris_cuda_flux_read_weight(self.h, name.encode(), out.ctypes.data_as(_u16p), out.size)
+        if rc:
+            raise IrisCudaError(last_error())
+        return out.reshape(shape)
+
+    def run_block(self, kind: int, idx: int, hidden: np.ndarray, txt_seq: int, img_h: int, img_w: int,
+                  t: float) -> np.ndarray:
+        hid = np.ascontiguousarray(hidden, np.float32).copy()
+        rc = lib().iris_cuda_flux_run_block(self.h, kind, idx, _f(hid), txt_seq, img_h, img_w, t)
+        if rc:
+            raise IrisCudaError(last_error())
+        return hid
+
+    def forward(self, latent: np.ndarray, txt: np.ndarray, t: float, refs=()) -> np.ndarray:
+        lat = np.ascontiguousarray(latent, np.float32)
+        tx = np.ascontiguousarray(txt, np.float32)
+        c, h, w = lat.shape
+        if refs:
+            keep = [np.ascontiguousarray(r, np.float32) for r in refs]
+            arr = (Ref * len(keep))(*[Ref(_f(r), r.shape[1], r.shape[2], 10 * (i + 1))
+                                      for i, r in enumerate(keep)])
+            p = lib().iris_cuda_transformer_forward_with_multi_refs(self.h, _f(lat), h, w, arr, len(keep),
+                                                                    _f(tx), tx.shape[0], t)
+        else:
+            p = lib().iris_cuda_transformer_forward(self.h, _f(lat), h, w, _f(tx), tx.shape[0], t)
+        return _take_floats(p, c * h * w, (c, h, w))
+
+    def sample_euler(self, z, txt, schedule, refs=(), txt_uncond=None, guidance=1.0):
+        zz = np.ascontiguousarray(z, np.float32)
+        tx = np.ascontiguousarray(txt, np.float32)
+        sc = np.ascontiguousarray(schedule, np.float32)
+        c, h, w = zz.shape
+        cb = PROGRESS_CB(0)
+        if txt_uncond is not None:
+            tu = np.ascontiguousarray(txt_uncond, np.float32)
+            p = lib().iris_cuda_sample_euler_cfg(self.h, _f(zz), 1, c, h, w, _f(tx), tx.shape[0], _f(tu),
+                                                 tu.shape[0], guidance, _f(sc), len(sc) - 1, cb)
+        elif refs:
+            keep = [np.ascontiguousarray(r, np.float32) for r in refs]
+            arr = (Ref * len(keep))(*[Ref(_f(r), r.shape[1], r.shape[2], 10 * (i + 1))
+                                      for i, r in enumerate(keep)])
+            p = lib().iris_cuda_sample_euler_with_multi_refs(self.h, _f(zz), 1, c, h, w, arr, len(keep),
+                                                             _f(tx), tx.shape[0], _f(sc), len(sc) - 1, cb)
+        else:
+            p = lib().iris_cuda_sample_euler(self.h, _f(zz), 1, c, h, w, _f(tx), tx.shape[0], _f(sc),
+                                             len(sc) - 1, cb)
+        return _take_floats(p, c * h * w, (c, h, w))
+
+
+def official_schedule(steps: int, seq: int) -> np.ndarray:
+    return _take_floats(lib().iris_cuda_official_schedule(steps, seq), steps + 1)
+
+
+def zimage_schedule(steps: int, seq: int) -> np.ndarray:
+    return _take_floats(lib().iris_cuda_zimage_schedule(steps, seq), steps + 1)
+
+
+def init_noise(c: int, h: int, w: int, seed: int) -> np.ndarray:
+    return _take_floats(lib().iris_cuda_init_noise(1, c, h, w, seed), c * h * w, (c, h, w))

@@ -1,0 +1,224 @@
+"""Seeded random-init model directories — TEST INFRASTRUCTURE ONLY.
+
+Writes HF-style model directories (``transformer/config.json`` plus a bf16
+``diffusion_pytorch_model.safetensors``) whose tensor names and shapes are the
+ones the reference loaders read:
+
+* Flux.2 Klein: ``iris_transformer_load_safetensors``
+  (iris_transformer_flux.c:5300-5497; config keys parsed at :395-455).
+* Z-Image S3-DiT: ``zi_transformer_load_safetensors``
+  (iris_transformer_zimage.c:2164-2427).
+
+Every tensor is drawn from its own generator seeded by (seed, crc32(name)),
+so any subset of tensors can be regenerated bit-identically without
+generating the rest.  Values are N(0, std) rounded to bf16 (round to nearest
+even), so the f32 reference oracle and the bf16 CUDA path see identical
+weights.
+"""
+from __future__ import annotations
+
+import json
+import os
+import struct
+import zlib
+
+import numpy as np
+
+# ---------------------------------------------------------------------------
+# bf16 helpers
+# ---------------------------------------------------------------------------
+
+
+def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
+    """Round-to-nearest-even f32 -> bf16, returned as uint16 bit patterns."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
+    u = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
+    return u.astype(np.uint16)
+
+
+def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
+    return (np.ascontiguousarray(b, dtype=np.uint16).astype(np.uint32) << 16).view(np.float32)
+
+
+def round_bf16(x: np.ndarray) -> np.ndarray:
+    return bf16_bits_to_f32(f32_to_bf16_bits(x))
+
+
+# ---------------------------------------------------------------------------
+# Flux.2 Klein
+# ---------------------------------------------------------------------------
+
+KLEIN_4B = dict(num_attention_heads=24, attention_head_dim=128, num_layers=5,
+                num_single_layers=20, joint_attention_dim=7680, in_channels=128,
+                mlp_ratio=3.0, rope_theta=2000.0)
+KLEIN_9B = dict(num_attention_heads=32, attention_head_dim=128, num_layers=8,
+                num_single_layers=24, joint_attention_dim=12288, in_channels=128,
+                mlp_ratio=3.0, rope_theta=2000.0)
+
+
+def flux_dims(cfg: dict) -> dict:
+    h = cfg["num_attention_heads"] * cfg["attention_head_dim"]
+    return dict(hidden=h, heads=cfg["num_attention_heads"], head_dim=cfg["attention_head_dim"],
+                mlp=int(h * cfg.get("mlp_ratio", 3.0)), n_double=cfg["num_layers"],
+                n_single=cfg["num_single_layers"], text_dim=cfg["joint_attention_dim"],
+                channels=cfg["in_channels"], theta=float(cfg.get("rope_theta", 2000.0)))
+
+
+def flux_tensor_specs(cfg: dict) -> list[tuple[str, tuple, str]]:
+    """(name, shape, kind) for every tensor the Flux loader reads.
+
+    kind is "linear" for projection matrices and "norm" for the per-head
+    QK-RMSNorm scale vectors (iris_transformer_flux.c:5374-5497)."""
+    d = flux_dims(cfg)
+    H, F, D, C, T = d["hidden"], d["mlp"], d["head_dim"], d["channels"], d["text_dim"]
+    s = [("x_embedder.weight", (H, C), "linear"),
+         ("context_embedder.weight", (H, T), "linear"),
+         ("time_guidance_embed.timestep_embedder.linear_1.weight", (H, 256), "linear"),
+         ("time_guidance_embed.timestep_embedder.linear_2.weight", (H, H), "linear"),
+         ("double_stream_modulation_img.linear.weight", (6 * H, H), "linear"),
+         ("double_stream_modulation_txt.linear.weight", (6 * H, H), "linear"),
+         ("single_stream_modulation.linear.weight", (3 * H, H), "linear")]
+    for i in range(d["n_double"]):
+        p = f"transformer_blocks.{i}."
+        s += [(p + "attn.norm_q.weight", (D,), "norm"), (p + "attn.norm_k.weight", (D,), "norm"),
+              (p + "attn.to_q.weight", (H, H), "linear"), (p + "attn.to_k.weight", (H, H), "linear"),
+              (p + "attn.to_v.weight", (H, H), "linear"),
+              (p + "attn.to_out.0.weight", (H, H), "linear"),
+              (p + "ff.linear_in.weight", (2 * F, H), "linear"),
+              (p + "ff.linear_out.weight", (H, F), "linear"),
+              (p + "attn.norm_added_q.weight", (D,), "norm"),
+              (p + "attn.norm_added_k.weight", (D,), "norm"),
+              (p + "attn.add_q_proj.weight", (H, H), "linear"),
+              (p + "attn.add_k_proj.weight", (H, H), "linear"),
+              (p + "attn.add_v_proj.weight", (H, H), "linear"),
+              (p + "attn.to_add_out.weight", (H, H), "linear"),
+              (p + "ff_context.linear_in.weight", (2 * F, H), "linear"),
+              (p + "ff_context.linear_out.weight", (H, F), "linear")]
+    for i in range(d["n_single"]):
+        p = f"single_transformer_blocks.{i}."
+        s += [(p + "attn.norm_q.weight", (D,), "norm"), (p + "attn.norm_k.weight", (D,), "norm"),
+              (p + "attn.to_qkv_mlp_proj.weight", (3 * H + 2 * F, H), "linear"),
+              (p + "attn.to_out.weight", (H, H + F), "linear")]
+    s += [("norm_out.linear.weight", (2 * H, H), "linear"),
+          ("proj_out.weight", (C, H), "linear")]
+    return s
+
+
+def gen_tensor(seed: int, name: str, shape: tuple, kind: str, std: float = 0.02,
+               norm_mode: str = "random") -> np.ndarray:
+    """bf16 bit pattern (uint16) of one seeded tensor.
+
+    norm_mode "random": N(0, std) like every other tensor.
+    norm_mode "unit":   1 + N(0, 0.1) so QK-RMSNorm keeps O(1) logits and the
+                        softmax is actually exercised."""
+    rng = np.random.default_rng([seed, zlib.crc32(name.encode())])
+    if kind == "norm" and norm_mode == "unit":
+        x = 1.0 + 0.1 * rng.standard_normal(shape, dtype=np.float32)
+    else:
+        x = std * rng.standard_normal(shape, dtype=np.float32)
+    return f32_to_bf16_bits(x)
+
+
+def write_safetensors(path: str, tensors: dict[str, np.ndarray]) -> None:
+    """Write uint16 (bf16) / float32 arrays in the safetensors container format."""
+    header = {}
+    off = 0
+    for name, arr in tensors.items():
+        dt = "BF16" if arr.dtype == np.uint16 else "F32"
+        n = arr.nbytes
+        header[name] = {"dtype": dt, "shape": list(arr.shape), "data_offsets": [off, off + n]}
+        off += n
+    hj = json.dumps(header).encode()
+    hj += b" " * ((8 - len(hj) % 8) % 8)
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(hj)))
+        f.write(hj)
+        for arr in tensors.values():
+            f.write(np.ascontiguousarray(arr).tobytes())
+
+
+def make_flux_model(model_dir: str, cfg: dict, seed: int, std: float = 0.02,
+                    norm_mode: str = "random") -> dict[str, np.ndarray]:
+    """Create a random Flux model directory; returns {name: f32 values}."""
+    os.makedirs(os.path.join(model_dir, "transformer"), exist_ok=True)
+    full = dict(_class_name="Flux2Transformer2DModel", **cfg)
+    with open(os.path.join(model_dir, "transformer", "config.json"), "w") as f:
+        json.dump(full, f, indent=1)
+    with open(os.path.join(model_dir, "model_index.json"), "w") as f:
+        json.dump({"_class_name": "Flux2KleinPipeline"}, f)
+    bits = {n: gen_tensor(seed, n, shp, kind, std, norm_mode)
+            for n, shp, kind in flux_tensor_specs(cfg)}
+    write_safetensors(os.path.join(model_dir, "transformer",
+                                   "diffusion_pytorch_model.safetensors"), bits)
+    return {n: bf16_bits_to_f32(b) for n, b in bits.items()}
+
+
+def flux_weights(cfg: dict, seed: int, std: float = 0.02, norm_mode: str = "random"):
+    """Regenerate the f32 (bf16-valued) weights of make_flux_model without disk I/O."""
+    return {n: bf16_bits_to_f32(gen_tensor(seed, n, shp, kind, std, norm_mode))
+            for n, shp, kind in flux_tensor_specs(cfg)}
+
+
+def flux_weights_bits(cfg: dict, seed: int, std: float = 0.02, norm_mode: str = "random"):
+    return {n: gen_tensor(seed, n, shp, kind, std, norm_mode)
+            for n, shp, kind in flux_tensor_specs(cfg)}
+
+
+# ---------------------------------------------------------------------------
+# Z-Image S3-DiT
+# ---------------------------------------------------------------------------
+
+ZIMAGE_6B = dict(dim=3840, n_heads=30, n_layers=30, n_refiner=2, cap_feat_dim=2560,
+                 in_channels=16, patch_size=2, rope_theta=256.0, axes_dims=[32, 48, 48],
+                 ffn_dim=10240, adaln_dim=256, t_mid=1024)
+
+
+def zimage_tensor_specs(cfg: dict) -> list[tuple[str, tuple, str]]:
+    """(name, shape, kind) for the tensors zi_transformer_load_safetensors reads
+    (iris_transformer_zimage.c:2024-2383).  Biases are kind "bias"."""
+    D, F, A = cfg["dim"], cfg["ffn_dim"], cfg["adaln_dim"]
+    hd = D // cfg["n_heads"]
+    ps, ic, cap = cfg["patch_size"], cfg["in_channels"], cfg["cap_feat_dim"]
+    pf = ps * ps * ic
+    s = [("t_embedder.mlp.0.weight", (cfg["t_mid"], 256), "linear"),
+         ("t_embedder.mlp.0.bias", (cfg["t_mid"],), "bias"),
+         ("t_embedder.mlp.2.weight", (A, cfg["t_mid"]), "linear"),
+         ("t_embedder.mlp.2.bias", (A,), "bias"),
+         ("cap_embedder.0.weight", (cap,), "norm"),
+         ("cap_embedder.1.weight", (D, cap), "linear"),
+         ("cap_embedder.1.bias", (D,), "bias"),
+         (f"all_x_embedder.{ps}-1.weight", (D, pf), "linear"),
+         (f"all_x_embedder.{ps}-1.bias", (D,), "bias"),
+         ("x_pad_token", (1, D), "linear"),
+         ("cap_pad_token", (1, D), "linear"),
+         (f"all_final_layer.{ps}-1.adaLN_modulation.1.weight", (D, A), "linear"),
+         (f"all_final_layer.{ps}-1.adaLN_modulation.1.bias", (D,), "bias"),
+         (f"all_final_layer.{ps}-1.linear.weight", (pf, D), "linear"),
+         (f"all_final_layer.{ps}-1.linear.bias", (pf,), "bias")]
+
+    def block(p, modulated):
+        b = [(p + "attention.to_q.weight", (D, D), "linear"),
+             (p + "attention.to_k.weight", (D, D), "linear"),
+             (p + "attention.to_v.weight", (D, D), "linear"),
+             (p + "attention.to_out.0.weight", (D, D), "linear"),
+             (p + "attention.norm_q.weight", (hd,), "norm"),
+             (p + "attention.norm_k.weight", (hd,), "norm"),
+             (p + "attention_norm1.weight", (D,), "norm"),
+             (p + "attention_norm2.weight", (D,), "norm"),
+             (p + "ffn_norm1.weight", (D,), "norm"),
+             (p + "ffn_norm2.weight", (D,), "norm"),
+             (p + "feed_forward.w1.weight", (F, D), "linear"),
+             (p + "feed_forward.w2.weight", (D, F), "linear"),
+             (p + "feed_forward.w3.weight", (F, D), "linear")]
+        if modulated:
+            b += [(p + "adaLN_modulation.0.weight", (4 * D, A), "linear"),
+                  (p + "adaLN_modulation.0.bias", (4 * D,), "bias")]
+        return b
+
+    for i in range(cfg["n_refiner"]):
+        s += block(f"noise_refiner.{i}.", True)
+    for i in range(cfg["n_refiner"]):
+        s += block(f"context_refiner.{i}.", False)
+    for i in range(cfg["n_layers"]):
+        s += block(f"layers.{i}.", True)
+    return s

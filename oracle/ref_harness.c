@@ -1,0 +1,248 @@
+/*
+ * ORACLE HARNESS — test infrastructure only, never part of the product path.
+ *
+ * White-box driver for the reference's own CPU implementation of the Flux.2
+ * DiT forward (iris.c, built from the unmodified sources under the reference
+ * tree by oracle/Makefile).  It #includes the reference's
+ * iris_transformer_flux.c so that the file-static block functions can be
+ * driven one block at a time, the same technique the reference uses for its
+ * VAE unit test (debug/test_vae.c:58).
+ *
+ * Every entry point is a thin call into reference code:
+ *   ref_flux_load            -> iris_transformer_load_safetensors  (iris_transformer_flux.c:5300)
+ *   ref_flux_forward         -> iris_transformer_forward           (iris_transformer_flux.c:3939)
+ *   ref_flux_forward_refs    -> iris_transformer_forward_with_multi_refs (:4579)
+ *   ref_flux_temb            -> get_timestep_embedding + time_embed_forward (:1349, :1366)
+ *   ref_flux_double_block    -> double_block_forward                (:2366)
+ *   ref_flux_single_block    -> single_block_forward                (:3761)
+ *   ref_flux_rope_img/_txt   -> compute_rope_2d / compute_rope_text (:897, :1055)
+ *   ref_sample_euler(_cfg)   -> iris_sample_euler / _cfg            (iris_sample.c:313, :717)
+ *   ref_init_noise           -> iris_init_noise                     (iris_sample.c:1146)
+ *   ref_official_schedule    -> iris_official_schedule              (iris_sample.c:171)
+ *   ref_zimage_schedule      -> iris_zimage_schedule                (iris_sample.c:216)
+ *   ref_zi_load/forward      -> zi_transformer_load_safetensors / zi_transformer_forward
+ *                                                                    (iris_transformer_zimage.c:2164, :1696)
+ *
+ * Build: see oracle/Makefile.  Outputs go to oracle/_ref/ only.
+ */
+#include "iris_transformer_flux.c"
+
+extern float *iris_official_schedule(int num_steps, int image_seq_len);
+extern float *iris_zimage_schedule(int num_steps, int image_seq_len);
+extern float *iris_init_noise(int batch, int channels, int h, int w, int64_t seed);
+extern float *iris_sample_euler(void *transformer, void *text_encoder,
+                                float *z, int batch, int channels, int h, int w,
+                                const float *text_emb, int text_seq,
+                                const float *schedule, int num_steps,
+                                void (*progress_callback)(int step, int total));
+extern float *iris_sample_euler_cfg(void *transformer, void *text_encoder,
+                                    float *z, int batch, int channels, int h, int w,
+                                    const float *text_emb_cond, int text_seq_cond,
+                                    const float *text_emb_uncond, int text_seq_uncond,
+                                    float guidance_scale,
+                                    const float *schedule, int num_steps,
+                                    void (*progress_callback)(int step, int total));
+extern float *iris_sample_euler_zimage(void *transformer,
+                                       float *z, int batch, int channels, int h, int w,
+                                       int patch_size,
+                                       const float *cap_feats, int cap_seq,
+                                       const float *schedule, int num_steps,
+                                       void (*progress_callback)(int step, int total));
+typedef struct zi_transformer zi_transformer_t;
+extern zi_transformer_t *zi_transformer_load_safetensors(const char *model_dir,
+                                                         int dim, int n_heads,
+                                                         int n_layers, int n_refiner,
+                                                         int cap_feat_dim, int in_channels,
+                                                         int patch_size, float rope_theta,
+                                                         const int *axes_dims);
+extern void zi_transformer_free(zi_transformer_t *tf);
+extern float *zi_transformer_forward(zi_transformer_t *tf, const float *latent,
+                                     int latent_h, int latent_w, float timestep,
+                                     const float *cap_feats, int cap_seq_len);
+
+void ref_set_threads(int n) {
+#ifdef USE_OPENBLAS
+    openblas_set_num_threads(n);
+#else
+    (void)n;
+#endif
+}
+
+void *ref_flux_load(const char *model_dir) {
+    return iris_transformer_load_safetensors(model_dir);
+}
+
+void ref_flux_free(void *tf) { iris_transformer_free((iris_transformer_t *)tf); }
+
+/* cfg[0..9] = hidden, heads, head_dim, mlp, n_double, n_single, text_dim,
+ * latent_channels, rope_theta, axis_dim */
+void ref_flux_config(void *p, float *cfg) {
+    iris_transformer_t *tf = (iris_transformer_t *)p;
+    cfg[0] = tf->hidden_size; cfg[1] = tf->num_heads; cfg[2] = tf->head_dim;
+    cfg[3] = tf->mlp_hidden; cfg[4] = tf->num_double_layers; cfg[5] = tf->num_single_layers;
+    cfg[6] = tf->text_dim; cfg[7] = tf->latent_channels; cfg[8] = tf->rope_theta;
+    cfg[9] = tf->axis_dim;
+}
+
+int ref_flux_forward(void *p, const float *latent, int h, int w,
+                     const float *txt, int txt_seq, float t, float *out) {
+    iris_transformer_t *tf = (iris_transformer_t *)p;
+    float *v = iris_transformer_forward(tf, latent, h, w, txt, txt_seq, t);
+    if (!v) return -1;
+    memcpy(out, v, (size_t)tf->latent_channels * h * w * sizeof(float));
+    free(v);
+    return 0;
+}
+
+/* refs_latent: num_refs latents [C, rh, rw] back to back; t offsets 10*(i+1). */
+int ref_flux_forward_refs(void *p, const float *latent, int h, int w,
+                          const float *refs_latent, int num_refs, int rh, int rw,
+                          const float *txt, int txt_seq, float t, float *out) {
+    iris_transformer_t *tf = (iris_transformer_t *)p;
+    iris_ref_t refs[8];
+    if (num_refs > 8) return -2;
+    for (int i = 0; i < num_refs; i++) {
+        refs[i].latent = refs_latent + (size_t)i * tf->latent_channels * rh * rw;
+        refs[i].h = rh; refs[i].w = rw; refs[i].t_offset = 10 * (i + 1);
+    }
+    float *v = iris_transformer_forward_with_multi_refs(tf, latent, h, w, refs, num_refs,
+                                                        txt, txt_seq, t);
+    if (!v) return -1;
+    memcpy(out, v, (size_t)tf->latent_channels * h * w * sizeof(float));
+    free(v);
+    return 0;
+}
+
+void ref_flux_temb(void *p, float t, float *t_emb) {
+    iris_transformer_t *tf = (iris_transformer_t *)p;
+    float sincos[256];
+    get_timestep_embedding(sincos, t * 1000.0f, tf->time_embed.sincos_dim, 10000.0f);
+    time_embed_forward(t_emb, sincos, &tf->time_embed, tf->hidden_size, tf->t_emb_silu);
+}
+
+/* Modulation vectors exactly as the forward computes them (:4059-4069, :3787-3797, :4277-4281). */
+void ref_flux_mods(void *p, const float *t_emb, float *dbl_img, float *dbl_txt,
+                   float *single, float *final_mod) {
+    iris_transformer_t *tf = (iris_transformer_t *)p;
+    int h = tf->hidden_size;
+    float *s = malloc((size_t)h * sizeof(float));
+    for (int j = 0; j < h; j++) s[j] = t_emb[j] / (1.0f + expf(-t_emb[j]));
+    iris_linear_nobias(dbl_img, s, tf->adaln_double_img_weight, 1, h, 6 * h);
+    iris_linear_nobias(dbl_txt, s, tf->adaln_double_txt_weight, 1, h, 6 * h);
+    iris_linear_nobias(single, s, tf->adaln_single_weight, 1, h, 3 * h);
+    iris_linear_nobias(final_mod, s, tf->final_norm_weight, 1, h, 2 * h);
+    free(s);
+}
+
+void ref_flux_rope_img(void *p, int ph, int pw, float *cos_out, float *sin_out) {
+    iris_transformer_t *tf = (iris_transformer_t *)p;
+    compute_rope_2d(cos_out, sin_out, ph, pw, tf->axis_dim, tf->rope_theta);
+}
+
+void ref_flux_rope_txt(void *p, int txt_seq, float *cos_out, float *sin_out) {
+    iris_transformer_t *tf = (iris_transformer_t *)p;
+    compute_rope_text(cos_out, sin_out, txt_seq, tf->axis_dim, tf->rope_theta);
+}
+
+int ref_flux_double_block(void *p, int idx, float *img_hidden, float *txt_hidden,
+                          const float *img_mod, const float *txt_mod,
+                          int ph, int pw, int txt_seq) {
+    iris_transformer_t *tf = (iris_transformer_t *)p;
+    int img_seq = ph * pw;
+    if (ensure_work_buffers(tf, img_seq + txt_seq) < 0) return -1;
+    if (ensure_attn_scores(tf, img_seq, txt_seq) < 0) return -1;
+    float *ic, *is, *tc, *ts;
+    get_cached_img_rope(tf, ph, pw, &ic, &is);
+    get_cached_txt_rope(tf, txt_seq, &tc, &ts);
+    double_block_forward(img_hidden, txt_hidden, &tf->double_blocks[idx], img_mod, txt_mod,
+                         ic, is, tc, ts, img_seq, txt_seq, idx, tf);
+    return 0;
+}
+
+/* hidden: [txt_seq + ph*pw, H] in [TXT, IMG] order. */
+int ref_flux_single_block(void *p, int idx, float *hidden, const float *t_emb,
+                          int ph, int pw, int txt_seq) {
+    iris_transformer_t *tf = (iris_transformer_t *)p;
+    int img_seq = ph * pw;
+    if (ensure_work_buffers(tf, img_seq + txt_seq) < 0) return -1;
+    if (ensure_attn_scores(tf, img_seq, txt_seq) < 0) return -1;
+    float *ic, *is, *tc, *ts;
+    get_cached_img_rope(tf, ph, pw, &ic, &is);
+    get_cached_txt_rope(tf, txt_seq, &tc, &ts);
+    tf->sref_krope_cos = NULL;
+    tf->sref_krope_sin = NULL;
+    single_block_forward(hidden, &tf->single_blocks[idx], t_emb, tf->adaln_single_weight,
+                         ic, is, tc, ts, img_seq + txt_seq, txt_seq, idx, tf);
+    return 0;
+}
+
+int ref_init_noise(int c, int h, int w, int64_t seed, float *out) {
+    float *z = iris_init_noise(1, c, h, w, seed);
+    if (!z) return -1;
+    memcpy(out, z, (size_t)c * h * w * sizeof(float));
+    free(z);
+    return 0;
+}
+
+int ref_official_schedule(int steps, int image_seq_len, float *out) {
+    float *s = iris_official_schedule(steps, image_seq_len);
+    if (!s) return -1;
+    memcpy(out, s, (size_t)(steps + 1) * sizeof(float));
+    free(s);
+    return 0;
+}
+
+int ref_zimage_schedule(int steps, int image_seq_len, float *out) {
+    float *s = iris_zimage_schedule(steps, image_seq_len);
+    if (!s) return -1;
+    memcpy(out, s, (size_t)(steps + 1) * sizeof(float));
+    free(s);
+    return 0;
+}
+
+int ref_sample_euler(void *tf, float *z, int c, int h, int w, const float *txt, int txt_seq,
+                     const float *schedule, int steps, float *out) {
+    float *r = iris_sample_euler(tf, NULL, z, 1, c, h, w, txt, txt_seq, schedule, steps, NULL);
+    if (!r) return -1;
+    memcpy(out, r, (size_t)c * h * w * sizeof(float));
+    free(r);
+    return 0;
+}
+
+int ref_sample_euler_cfg(void *tf, float *z, int c, int h, int w,
+                         const float *txt_c, int seq_c, const float *txt_u, int seq_u,
+                         float g, const float *schedule, int steps, float *out) {
+    float *r = iris_sample_euler_cfg(tf, NULL, z, 1, c, h, w, txt_c, seq_c, txt_u, seq_u, g,
+                                     schedule, steps, NULL);
+    if (!r) return -1;
+    memcpy(out, r, (size_t)c * h * w * sizeof(float));
+    free(r);
+    return 0;
+}
+
+/* cfg: dim, n_heads, n_layers, n_refiner, cap_feat_dim, in_channels, patch_size,
+ * axes_dims[3]; rope_theta separately (iris.c:309-322 passes these from config.json). */
+void *ref_zi_load(const char *model_dir, const int *cfg, float rope_theta) {
+    return zi_transformer_load_safetensors(model_dir, cfg[0], cfg[1], cfg[2], cfg[3], cfg[4],
+                                           cfg[5], cfg[6], rope_theta, cfg + 7);
+}
+void ref_zi_free(void *tf) { zi_transformer_free((zi_transformer_t *)tf); }
+
+int ref_zi_forward(void *tf, const float *latent, int lh, int lw, float t,
+                   const float *cap, int cap_seq, int in_ch, float *out) {
+    float *v = zi_transformer_forward((zi_transformer_t *)tf, latent, lh, lw, t, cap, cap_seq);
+    if (!v) return -1;
+    memcpy(out, v, (size_t)in_ch * lh * lw * sizeof(float));
+    free(v);
+    return 0;
+}
+
+int ref_sample_euler_zimage(void *tf, float *z, int c, int h, int w, int ps,
+                            const float *cap, int cap_seq, const float *schedule, int steps,
+                            float *out) {
+    float *r = iris_sample_euler_zimage(tf, z, 1, c, h, w, ps, cap, cap_seq, schedule, steps, NULL);
+    if (!r) return -1;
+    memcpy(out, r, (size_t)c * h * w * sizeof(float));
+    free(r);
+    return 0;
+}

@@ -1,0 +1,175 @@
+"""ctypes loader for the reference compiled from its own sources — TEST INFRASTRUCTURE ONLY.
+
+oracle/Makefile builds oracle/_ref/libiris_ref_{generic,blas}.so from the
+unmodified reference C files plus oracle/ref_harness.c.  This module binds
+the harness entry points (see ref_harness.c for the reference function each
+one calls).  Used to generate golden fixtures, to pin the numpy oracle and as
+bench.py's reference (CPU) arm.
+"""
+from __future__ import annotations
+
+import ctypes as C
+import os
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+REF_DIR = os.path.join(HERE, "_ref")
+
+_fp = C.POINTER(C.c_float)
+
+
+def _f(a):
+    return a.ctypes.data_as(_fp)
+
+
+class RefLib:
+    def __init__(self, variant: str = "blas"):
+        path = os.path.join(REF_DIR, f"libiris_ref_{variant}.so")
+        if not os.path.exists(path):
+            raise FileNotFoundError(f"{path} missing: run `make -C oracle` where the reference tree exists")
+        self.lib = L = C.CDLL(path)
+        L.ref_flux_load.restype = C.c_void_p
+        L.ref_flux_load.argtypes = [C.c_char_p]
+        L.ref_flux_free.argtypes = [C.c_void_p]
+        L.ref_flux_config.argtypes = [C.c_void_p, _fp]
+        L.ref_flux_forward.argtypes = [C.c_void_p, _fp, C.c_int, C.c_int, _fp, C.c_int, C.c_float, _fp]
+        L.ref_flux_forward_refs.argtypes = [C.c_void_p, _fp, C.c_int, C.c_int, _fp, C.c_int,
+                                            C.c_int, C.c_int, _fp, C.c_int, C.c_float, _fp]
+        L.ref_flux_temb.argtypes = [C.c_void_p, C.c_float, _fp]
+        L.ref_flux_mods.argtypes = [C.c_void_p, _fp, _fp, _fp, _fp, _fp]
+        L.ref_flux_rope_img.argtypes = [C.c_void_p, C.c_int, C.c_int, _fp, _fp]
+        L.ref_flux_rope_txt.argtypes = [C.c_void_p, C.c_int, _fp, _fp]
+        L.ref_flux_double_block.argtypes = [C.c_void_p, C.c_int, _fp, _fp, _fp, _fp,
+                                            C.c_int, C.c_int, C.c_int]
+        L.ref_flux_single_block.argtypes = [C.c_void_p, C.c_int, _fp, _fp, C.c_int, C.c_int, C.c_int]
+        L.ref_init_noise.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int64, _fp]
+        L.ref_official_schedule.argtypes = [C.c_int, C.c_int, _fp]
+        L.ref_zimage_schedule.argtypes = [C.c_int, C.c_int, _fp]
+        L.ref_sample_euler.argtypes = [C.c_void_p, _fp, C.c_int, C.c_int, C.c_int, _fp, C.c_int,
+                                       _fp, C.c_int, _fp]
+        L.ref_sample_euler_cfg.argtypes = [C.c_void_p, _fp, C.c_int, C.c_int, C.c_int, _fp, C.c_int,
+                                           _fp, C.c_int, C.c_float, _fp, C.c_int, _fp]
+        L.ref_zi_load.restype = C.c_void_p
+        L.ref_zi_load.argtypes = [C.c_char_p, C.POINTER(C.c_int), C.c_float]
+        L.ref_zi_free.argtypes = [C.c_void_p]
+        L.ref_zi_forward.argtypes = [C.c_void_p, _fp, C.c_int, C.c_int, C.c_float, _fp, C.c_int,
+                                     C.c_int, _fp]
+        L.ref_sample_euler_zimage.argtypes = [C.c_void_p, _fp, C.c_int, C.c_int, C.c_int, C.c_int,
+                                              _fp, C.c_int, _fp, C.c_int, _fp]
+        L.ref_set_threads.argtypes = [C.c_int]
+
+    def set_threads(self, n: int):
+        self.lib.ref_set_threads(n)
+
+
+class RefFlux:
+    """A reference Flux transformer loaded from a model directory."""
+
+    def __init__(self, ref: RefLib, model_dir: str):
+        self.ref = ref
+        self.h = ref.lib.ref_flux_load(model_dir.encode())
+        if not self.h:
+            raise RuntimeError(f"reference failed to load {model_dir}")
+        cfg = np.zeros(10, np.float32)
+        ref.lib.ref_flux_config(self.h, _f(cfg))
+        (self.hidden, self.heads, self.head_dim, self.mlp, self.n_double, self.n_single,
+         self.text_dim, self.channels) = (int(x) for x in cfg[:8])
+        self.theta = float(cfg[8])
+
+    def close(self):
+        if self.h:
+            self.ref.lib.ref_flux_free(self.h)
+            self.h = None
+
+    def forward(self, latent, txt, t):
+        c, h, w = latent.shape
+        lat = np.ascontiguousarray(latent, np.float32)
+        tx = np.ascontiguousarray(txt, np.float32)
+        out = np.zeros_like(lat)
+        rc = self.ref.lib.ref_flux_forward(self.h, _f(lat), h, w, _f(tx), tx.shape[0], t, _f(out))
+        assert rc == 0
+        return out
+
+    def forward_refs(self, latent, refs, txt, t):
+        c, h, w = latent.shape
+        lat = np.ascontiguousarray(latent, np.float32)
+        rl = np.ascontiguousarray(np.stack(refs), np.float32)
+        tx = np.ascontiguousarray(txt, np.float32)
+        out = np.zeros_like(lat)
+        rc = self.ref.lib.ref_flux_forward_refs(self.h, _f(lat), h, w, _f(rl), len(refs),
+                                                refs[0].shape[1], refs[0].shape[2],
+                                                _f(tx), tx.shape[0], t, _f(out))
+        assert rc == 0
+        return out
+
+    def temb(self, t):
+        out = np.zeros(self.hidden, np.float32)
+        self.ref.lib.ref_flux_temb(self.h, t, _f(out))
+        return out
+
+    def mods(self, t_emb):
+        H = self.hidden
+        a, b, c, d = (np.zeros(n * H, np.float32) for n in (6, 6, 3, 2))
+        self.ref.lib.ref_flux_mods(self.h, _f(np.ascontiguousarray(t_emb, np.float32)),
+                                   _f(a), _f(b), _f(c), _f(d))
+        return dict(dbl_img=a, dbl_txt=b, single=c, final=d)
+
+    def double_block(self, i, img, txt, mod_img, mod_txt, ph, pw):
+        img = np.ascontiguousarray(img, np.float32).copy()
+        txt = np.ascontiguousarray(txt, np.float32).copy()
+        rc = self.ref.lib.ref_flux_double_block(self.h, i, _f(img), _f(txt),
+                                                _f(np.ascontiguousarray(mod_img, np.float32)),
+                                                _f(np.ascontiguousarray(mod_txt, np.float32)),
+                                                ph, pw, txt.shape[0])
+        assert rc == 0
+        return img, txt
+
+    def single_block(self, i, hidden, t_emb, ph, pw, txt_seq):
+        hid = np.ascontiguousarray(hidden, np.float32).copy()
+        rc = self.ref.lib.ref_flux_single_block(self.h, i, _f(hid),
+                                                _f(np.ascontiguousarray(t_emb, np.float32)),
+                                                ph, pw, txt_seq)
+        assert rc == 0
+        return hid
+
+    def sample_euler(self, z, txt, schedule):
+        c, h, w = z.shape
+        zz = np.ascontiguousarray(z, np.float32).copy()
+        tx = np.ascontiguousarray(txt, np.float32)
+        sc = np.ascontiguousarray(schedule, np.float32)
+        out = np.zeros_like(zz)
+        rc = self.ref.lib.ref_sample_euler(self.h, _f(zz), c, h, w, _f(tx), tx.shape[0], _f(sc),
+                                           len(sc) - 1, _f(out))
+        assert rc == 0
+        return out
+
+    def sample_euler_cfg(self, z, txt_c, txt_u, g, schedule):
+        c, h, w = z.shape
+        zz = np.ascontiguousarray(z, np.float32).copy()
+        tc = np.ascontiguousarray(txt_c, np.float32)
+        tu = np.ascontiguousarray(txt_u, np.float32)
+        sc = np.ascontiguousarray(schedule, np.float32)
+        out = np.zeros_like(zz)
+        rc = self.ref.lib.ref_sample_euler_cfg(self.h, _f(zz), c, h, w, _f(tc), tc.shape[0],
+                                               _f(tu), tu.shape[0], g, _f(sc), len(sc) - 1, _f(out))
+        assert rc == 0
+        return out
+
+
+def ref_init_noise(ref: RefLib, c, h, w, seed):
+    out = np.zeros((c, h, w), np.float32)
+    assert ref.lib.ref_init_noise(c, h, w, seed, _f(out)) == 0
+    return out
+
+
+def ref_official_schedule(ref: RefLib, steps, seq):
+    out = np.zeros(steps + 1, np.float32)
+    assert ref.lib.ref_official_schedule(steps, seq, _f(out)) == 0
+    return out
+
+
+def ref_zimage_schedule(ref: RefLib, steps, seq):
+    out = np.zeros(steps + 1, np.float32)
+    assert ref.lib.ref_zimage_schedule(steps, seq, _f(out)) == 0
+    return out
