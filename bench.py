@@ -1,0 +1,422 @@
+#!/usr/bin/env python
+"""Benchmark: Flux.2 Klein-4B 512x512, 4-step Euler denoising on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+One bench step = one image = 4 denoising steps (transformer forward + Euler
+update each) of Klein-4B at 512x512: 1024 image tokens + 512 text tokens,
+random-init bf16 weights N(0, 0.02), seeded N(0,1) latents and context.
+
+* value     denoise steps/s of the whole job (all ranks), device-timed with
+            CUDA events on the library stream, inputs resident in HBM
+            (iris_cuda_sample_euler_dev).
+* e2e       the same metric through the public host API
+            (iris_cuda_sample_euler): every image copies its latent and text
+            context from pinned host memory and reads the final latent back.
+* roofline  the tcgen05 GEMM (the dominant kernel): algorithmic FLOPs of its
+            launches in one forward / their CUDA-event time
+            (iris_cuda_flux_profile), against MEASURED_PEAKS.json.
+* cpu_baseline  the reference's own `make blas` build (oracle/_ref) on the
+            host cores: one double + one single block at the same shapes,
+            extrapolated to a full step (5 double + 20 single blocks).
+
+Multi-GPU (torchrun, one process per GPU): independent seeds per rank
+("replicas", no data-path collective); a barrier brackets the timed region
+and the reported time is the max over ranks.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import tempfile
+import time
+
+import numpy as np
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+for p in (ROOT, os.path.join(ROOT, "iris.c_b200")):
+    if p not in sys.path:
+        sys.path.insert(0, p)
+
+K4B = dict(num_attention_heads=24, attention_head_dim=128, num_layers=5, num_single_layers=20,
+           joint_attention_dim=7680, in_channels=128, mlp_ratio=3.0, rope_theta=2000.0)
+IMG_H = IMG_W = 32          # 512 px / 16
+TXT = 512
+STEPS_PER_IMAGE = 4
+WEIGHT_SEED = 20261201
+METRIC = "denoise steps/s (Klein-4B 512x512, 4-step Euler)"
+UNIT = "steps/s"
+PEAKS_FALLBACK = dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=1400.0)
+
+
+def parse_args(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=30, help="timed images (4 denoising steps each)")
+    ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    return ap.parse_args(argv)
+
+
+# ----------------------------------------------------------------------------- distributed plumbing
+def dist_env():
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    return rank, world, local
+
+
+def dist_init(world, backend="nccl", device=None):
+    if world <= 1:
+        return None
+    import datetime
+
+    import torch.distributed as dist
+    kw = {}
+    if device is not None and backend == "nccl":
+        kw["device_id"] = device
+    dist.init_process_group(backend, timeout=datetime.timedelta(seconds=300), **kw)
+    return dist
+
+
+def reduce_max(value: float, world: int, device=None) -> float:
+    """Max of a per-rank float over all ranks (the timing rule)."""
+    if world <= 1:
+        return value
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def image_seed(rank: int, i: int) -> int:
+    """Each rank denoises its own seeds (seed-parallel replicas)."""
+    return 1000 + 100003 * rank + i
+
+
+# ----------------------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clock / throttle-reason samples every 200 ms during the timed region."""
+
+    QUERY = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+             "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+             "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_id: str):
+        self.gpu_id = gpu_id
+        self.proc = None
+        self.lines = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.QUERY}", "--format=csv,noheader,nounits", "-lms", "200",
+                 "-i", self.gpu_id], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx.append(float(f[2]))
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(n)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": max(mx) if mx else None,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def gpu_smi_id(local: int) -> str:
+    try:
+        import torch
+        u = str(torch.cuda.get_device_properties(local).uuid)
+        return u if u.startswith("GPU-") else "GPU-" + u
+    except Exception:
+        return str(local)
+
+
+def load_peaks():
+    path = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(path):
+        with open(path) as f:
+            p = json.load(f)
+        return dict(hbm_gbs=p["hbm_gbs"], bf16_tflops=p["bf16_tflops"],
+                    bf16_tflops_sustained=p.get("bf16_tflops_sustained", p["bf16_tflops"])), "measured"
+    return PEAKS_FALLBACK, "fallback"
+
+
+# ----------------------------------------------------------------------------- CPU reference arm
+class RefSample:
+    """The reference's own BLAS build timed on one double + one single block of
+    Klein-4B at the 512x512 shapes; a full denoising step is extrapolated as
+    5 double + 20 single blocks (embedders and final layer are < 1% of it)."""
+
+    def __init__(self):
+        from oracle import model_gen as mg
+        from oracle.ref_lib import RefFlux, RefLib
+        self.tmp = tempfile.TemporaryDirectory()
+        cfg = dict(K4B, num_layers=1, num_single_layers=1)
+        mg.make_flux_model(self.tmp.name, cfg, WEIGHT_SEED, 0.02, "random")
+        self.ref = RefLib("blas")
+        self.cores = len(os.sched_getaffinity(0))
+        self.ref.set_threads(self.cores)
+        self.rf = RefFlux(self.ref, self.tmp.name)
+        r = np.random.default_rng(7)
+        H = self.rf.hidden
+        self.img = r.standard_normal((IMG_H * IMG_W, H)).astype(np.float32)
+        self.txt = r.standard_normal((TXT, H)).astype(np.float32)
+        self.t_emb = self.rf.temb(1.0)
+        self.mods = self.rf.mods(self.t_emb)
+
+    def step_seconds(self):
+        t0 = time.perf_counter()
+        self.rf.double_block(0, self.img, self.txt, self.mods["dbl_img"], self.mods["dbl_txt"], IMG_H, IMG_W)
+        t1 = time.perf_counter()
+        self.rf.single_block(0, np.concatenate([self.txt, self.img]), self.t_emb, IMG_H, IMG_W, TXT)
+        t2 = time.perf_counter()
+        return 5 * (t1 - t0) + 20 * (t2 - t1), t2 - t0
+
+    def close(self):
+        self.rf.close()
+        self.tmp.cleanup()
+
+    SAMPLE = ("reference make-blas build (oracle/_ref, OpenBLAS 0.3.15): 1 double + 1 single Klein-4B block "
+              "at 1024 img + 512 txt tokens per sample, extrapolated to 5 double + 20 single blocks per step")
+
+
+def run_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    rs = RefSample()
+    for _ in range(args.warmup):
+        rs.step_seconds()
+    est, wall = [], 0.0
+    for _ in range(args.steps):
+        s, w = rs.step_seconds()
+        est.append(s)
+        wall += w
+    rs.close()
+    step_s = statistics.mean(est)
+    value = 1.0 / step_s
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1000.0 * STEPS_PER_IMAGE,
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": bench_config(world),
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": rs.cores, "kind": "reference",
+                         "sample": RefSample.SAMPLE, "measured_wall_s": wall},
+        "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def bench_config(world):
+    return {"workload": "Flux.2 Klein-4B distilled, 512x512 (32x32 latent patches = 1024 image tokens) + "
+                        "512 text tokens, 4-step Euler, guidance 1.0, batch 1 per GPU",
+            "model": "klein-4b (random-init bf16 N(0,0.02))", "image_tokens": IMG_H * IMG_W,
+            "text_tokens": TXT, "denoise_steps_per_image": STEPS_PER_IMAGE, "global_batch": world,
+            "parallelism": f"seed-replicas x{world}",
+            "l2": "no flush needed: every forward streams all 7.7 GB of weights (> 126 MB L2)"}
+
+
+# ----------------------------------------------------------------------------- our arm
+def run_ours(args):
+    import ctypes as C
+
+    import torch
+
+    import iris_cuda
+
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dist = dist_init(world, "nccl", torch.device("cuda", local))
+    lib = iris_cuda.lib()
+    if lib.iris_cuda_init(local) != 0:
+        raise iris_cuda.IrisCudaError(iris_cuda.last_error())
+    model = iris_cuda.Flux.random(iris_cuda.FluxConfig.from_hf(K4B), seed=WEIGHT_SEED, std=0.02)
+    stream = torch.cuda.ExternalStream(lib.iris_cuda_stream(), device=torch.device("cuda", local))
+
+    rng = np.random.default_rng(500 + rank)
+    txt = rng.standard_normal((TXT, K4B["joint_attention_dim"])).astype(np.float32)
+    sched = np.ascontiguousarray(iris_cuda.official_schedule(STEPS_PER_IMAGE, IMG_H * IMG_W), np.float32)
+    sched_p = sched.ctypes.data_as(C.POINTER(C.c_float))
+    n_img = args.warmup + args.steps
+    noises = [iris_cuda.init_noise(128, IMG_H, IMG_W, image_seed(rank, i)) for i in range(n_img)]
+
+    # ---- device-resident arm
+    dev = torch.device("cuda", local)
+    txt_d = torch.from_numpy(txt).to(dev)
+    z0_d = torch.from_numpy(np.stack(noises)).to(dev)
+    z_d = torch.empty_like(z0_d[0])
+    torch.cuda.synchronize()
+
+    def image_dev(i):
+        with torch.cuda.stream(stream):
+            z_d.copy_(z0_d[i])
+        rc = lib.iris_cuda_sample_euler_dev(model.h, z_d.data_ptr(), IMG_H, IMG_W, txt_d.data_ptr(), TXT,
+                                            None, 0, 1.0, sched_p, STEPS_PER_IMAGE)
+        if rc:
+            raise iris_cuda.IrisCudaError(iris_cuda.last_error())
+
+    for i in range(args.warmup):
+        image_dev(i)
+    stream.synchronize()
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    l0 = lib.iris_cuda_kernel_launches()
+    with ClockSampler(gpu_smi_id(local)) as clocks:
+        ev0.record(stream)
+        for i in range(args.warmup, n_img):
+            image_dev(i)
+        ev1.record(stream)
+        ev1.synchronize()
+    launches = lib.iris_cuda_kernel_launches() - l0
+    torch.cuda.synchronize()
+    ms = ev0.elapsed_time(ev1)
+    if dist:
+        dist.barrier()
+    ms_max = reduce_max(ms, world, dev)
+    value = world * args.steps * STEPS_PER_IMAGE / (ms_max / 1000.0)
+    if lib.iris_cuda_device_status(0):
+        raise iris_cuda.IrisCudaError("device wait expired during the timed region")
+
+    # ---- end-to-end arm: public host API, pinned inputs, result read back
+    txt_h = torch.from_numpy(txt).pin_memory()
+    z_h = [torch.from_numpy(n).pin_memory() for n in noises]
+    cb = iris_cuda.PROGRESS_CB(0)
+    _free = C.CDLL(None).free
+    _free.argtypes = [C.c_void_p]
+
+    def image_e2e(i):
+        p = lib.iris_cuda_sample_euler(model.h, C.cast(z_h[i].data_ptr(), C.POINTER(C.c_float)), 1, 128,
+                                       IMG_H, IMG_W, C.cast(txt_h.data_ptr(), C.POINTER(C.c_float)), TXT,
+                                       sched_p, STEPS_PER_IMAGE, cb)
+        if not p:
+            raise iris_cuda.IrisCudaError(iris_cuda.last_error())
+        _free(p)
+
+    for i in range(args.warmup):
+        image_e2e(i)
+    if dist:
+        dist.barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
+    e0.record(stream)
+    for i in range(args.warmup, n_img):
+        image_e2e(i)
+    e1.record(stream)
+    e1.synchronize()
+    e2e_wall = time.perf_counter() - w0
+    e2e_ms = reduce_max(e0.elapsed_time(e1), world, dev)
+    e2e_value = world * args.steps * STEPS_PER_IMAGE / (e2e_ms / 1000.0)
+    h2d = 4 * (128 * IMG_H * IMG_W + TXT * K4B["joint_attention_dim"] + STEPS_PER_IMAGE + 1)
+    d2h = 4 * 128 * IMG_H * IMG_W
+
+    # ---- roofline of the dominant kernel (tcgen05 GEMM), live CUDA-event profile
+    peaks, peak_src = load_peaks()
+    prof = None
+    for _ in range(3):
+        p = model.profile(0.5)
+        if prof is None:
+            prof = [dict(e) for e in p]
+        else:
+            for a, b in zip(prof, p):
+                a["ms"] += b["ms"]
+    for e in prof:
+        e["ms"] /= 3.0
+    gemm = [e for e in prof if e["flops"] > 0 and "attn" not in e["name"] and e["name"] != "mods"]
+    attn = [e for e in prof if "attn" in e["name"]]
+    g_fl, g_ms = sum(e["flops"] for e in gemm), sum(e["ms"] for e in gemm)
+    a_fl, a_ms = sum(e["flops"] for e in attn), sum(e["ms"] for e in attn)
+    step_ms = sum(e["ms"] for e in prof)
+    achieved = g_fl / (g_ms / 1000.0) / 1e12
+    traffic = None
+    tpath = os.path.join(ROOT, "profiles", "gemm_traffic.json")
+    if os.path.exists(tpath):
+        with open(tpath) as f:
+            traffic = json.load(f).get("dram_bytes_per_launch")
+    roofline = {"kernel": "gemm_tc_kernel (tcgen05, all linears of a step)", "bound": "tensor",
+                "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                "frac": achieved / peaks["bf16_tflops"], "peak_source": peak_src,
+                "frac_of_sustained": achieved / peaks["bf16_tflops_sustained"], "traffic": traffic,
+                "gemm_launches_per_forward": len(gemm), "gemm_tflop_per_forward": g_fl / 1e12,
+                "attention_tflops": a_fl / (a_ms / 1000.0) / 1e12 if a_ms else None,
+                "forward_ms_unfused_launches": step_ms,
+                "share": {"gemm": g_ms / step_ms, "attention": a_ms / step_ms,
+                          "other": 1 - (g_ms + a_ms) / step_ms}}
+
+    # ---- CPU baseline (rank 0, N=1 only)
+    cpu = None
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        try:
+            rs = RefSample()
+            rs.step_seconds()
+            est = [rs.step_seconds()[0] for _ in range(2)]
+            cpu = {"value": 1.0 / statistics.mean(est), "unit": UNIT, "cores": rs.cores,
+                   "kind": "reference", "sample": RefSample.SAMPLE}
+            rs.close()
+        except Exception as ex:  # the reference build is optional on a box without it
+            cpu = {"value": None, "unit": UNIT, "cores": None, "kind": "reference",
+                   "sample": f"unavailable: {type(ex).__name__}: {ex}"}
+
+    line = {
+        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+        "images_per_s": value / STEPS_PER_IMAGE,
+        "config": bench_config(world),
+        "clocks": clocks.summary(),
+        "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+                "wall_s": e2e_wall},
+        "gpu_launches": int(launches),
+        "roofline": roofline,
+        "cpu_baseline": cpu,
+    }
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    model.close()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
+def main(argv=None):
+    args = parse_args(argv)
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_ours(args)
+
+
+if __name__ == "__main__":
+    sys.exit(main())

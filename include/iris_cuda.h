@@ -140,6 +140,21 @@ int iris_cuda_flux_forward_dev(iris_cuda_flux_t *tf, const float *d_latent, int 
 int iris_cuda_flux_run_block(iris_cuda_flux_t *tf, int kind, int idx, float *hidden, int txt_seq,
                              int img_h, int img_w, float timestep);
 
+/* One kernel of a profiled forward (iris_cuda_flux_profile). */
+typedef struct {
+    char name[32];
+    double flops;        /* algorithmic FLOPs of the launch (0 if not FLOP-bound) */
+    double bytes;        /* algorithmic HBM bytes (operands once + outputs once)  */
+    float ms;            /* CUDA-event time of the launch                          */
+} iris_cuda_kernel_time_t;
+
+/* Time every kernel of one forward over the most recent input shape (no
+ * graph; an event after each launch).  Returns the number of entries or a
+ * negative status.  No reference counterpart (the reference's BLAS profile
+ * counters, iris_transformer_flux.c:40-76, play the same role on the CPU). */
+int iris_cuda_flux_profile(iris_cuda_flux_t *tf, float timestep, iris_cuda_kernel_time_t *out,
+                           int max_entries);
+
 /* ------------------------------------------------------------------ 2b. samplers */
 /* Replaces iris_official_schedule (iris_sample.c:171). malloc'd [steps+1]. */
 float *iris_cuda_official_schedule(int num_steps, int image_seq_len);

@@ -556,15 +556,39 @@ static void gp_group(IrisGemmParams *p, int g, const CUtensorMap *tb, int row0, 
 typedef struct {
     int rc;
     uint64_t kernels;
+    /* live profiling (iris_cuda_flux_profile): an event after every launch */
+    iris_cuda_kernel_time_t *prof;
+    cudaEvent_t *ev;
+    int nprof, maxprof;
 } enq_t;
 
-static void enq(enq_t *E, cudaError_t e, const char *what) {
+static void enq_x(enq_t *E, cudaError_t e, const char *what, double flops, double bytes) {
     E->kernels++;
     if (!E->rc && e != cudaSuccess) E->rc = iris_cuda_check(e, what);
+    if (E->prof && E->nprof < E->maxprof) {
+        iris_cuda_kernel_time_t *k = &E->prof[E->nprof];
+        snprintf(k->name, sizeof(k->name), "%s", what);
+        k->flops = flops;
+        k->bytes = bytes;
+        cudaEventRecord(E->ev[E->nprof + 1], g_rt.stream);
+        E->nprof++;
+    }
 }
 
+static void enq(enq_t *E, cudaError_t e, const char *what) { enq_x(E, e, what, 0.0, 0.0); }
+
 static void enq_gemm(enq_t *E, const IrisGemmParams *p, const char *what) {
-    enq(E, iris_launch_gemm(p, g_rt.num_sms, g_rt.stream), what);
+    double rows = (double)p->rows[0] + (p->ngroups > 1 ? (double)p->rows[1] : 0.0);
+    double out_bytes = (p->mode == IRIS_EPI_RESID_GATE) ? 8.0 /* f32 read + write */
+                       : (p->mode == IRIS_EPI_F32 || p->mode == IRIS_EPI_F32_NCHW) ? 4.0
+                       : (p->mode == IRIS_EPI_SWIGLU) ? 1.0 /* N/2 bf16 outputs */
+                       : 2.0;
+    if (p->mode == IRIS_EPI_SINGLE) {
+        /* 3H bf16 Q/K/V columns + (N-3H)/2 bf16 SwiGLU outputs */
+        out_bytes = (3.0 * p->H * 2.0 + (p->N - 3.0 * p->H)) / p->N;
+    }
+    double bytes = rows * p->K * 2.0 + (double)p->ngroups * p->N * p->K * 2.0 + rows * p->N * out_bytes;
+    enq_x(E, iris_launch_gemm(p, g_rt.num_sms, g_rt.stream), what, 2.0 * rows * p->N * p->K, bytes);
 }
 
 /* timestep embedding and every modulation vector of the step */
@@ -574,7 +598,8 @@ static void enq_mods(iris_cuda_flux_t *tf, enq_t *E) {
     enq(E, iris_launch_timestep_sincos(tf->t_dev, 1000.0f, tf->sincos, 256, st), "sincos");
     enq(E, iris_launch_gemv(tf->w_t1, tf->sincos, NULL, tf->temb_h, H, 256, 0, 1, st), "t_fc1");
     enq(E, iris_launch_gemv(tf->w_t2, tf->temb_h, NULL, tf->temb, H, H, 0, 0, st), "t_fc2");
-    enq(E, iris_launch_gemv(tf->w_mod, tf->temb, NULL, tf->mods, 17 * H, H, 1, 0, st), "mods");
+    enq_x(E, iris_launch_gemv(tf->w_mod, tf->temb, NULL, tf->mods, 17 * H, H, 1, 0, st), "mods",
+          2.0 * 17 * H * (double)H, 2.0 * 17 * H * (double)H);
 }
 
 /* input projections: hidden = [txt_in(ctx); img_in(latent tokens)] */
@@ -613,8 +638,8 @@ static void enq_double(iris_cuda_flux_t *tf, int i, enq_t *E) {
     const float *mi = tf->mods, *mt = tf->mods + (size_t)6 * H;
     flux_dbl_t *b = &tf->dbl[i];
     IrisGemmParams gp;
-    enq(E, iris_launch_adaln(P->hidden, H, P->xmod, H, S, H, mt, mt + H, mi, mi + H, St, 1e-6f, st),
-        "adaln1");
+    enq_x(E, iris_launch_adaln(P->hidden, H, P->xmod, H, S, H, mt, mt + H, mi, mi + H, St, 1e-6f, st),
+          "adaln1", 0.0, 6.0 * S * (double)H);
     gp_init(&gp, &P->tm_xmod, 3 * H, H, IRIS_EPI_QKV);
     gp_group(&gp, 0, &b->tm_qkv[0], 0, St);
     gp_group(&gp, 1, &b->tm_qkv[1], St, Si);
@@ -623,16 +648,17 @@ static void enq_double(iris_cuda_flux_t *tf, int i, enq_t *E) {
     gp.rope_cos = P->rope_cos; gp.rope_sin = P->rope_sin;
     gp.q = P->q; gp.k = P->k; gp.v = P->v; gp.ldqkv = H; gp.H = H;
     enq_gemm(E, &gp, "dbl_qkv");
-    enq(E, iris_launch_attention(P->q, H, P->k, P->v, H, P->attn, H, S, S, NH,
-                                 1.0f / sqrtf(128.0f), NULL, st), "dbl_attn");
+    enq_x(E, iris_launch_attention(P->q, H, P->k, P->v, H, P->attn, H, S, S, NH,
+                                   1.0f / sqrtf(128.0f), NULL, st), "dbl_attn",
+          4.0 * S * S * (double)H, 8.0 * S * (double)H);
     gp_init(&gp, &P->tm_attn, H, H, IRIS_EPI_RESID_GATE);
     gp_group(&gp, 0, &b->tm_out[0], 0, St);
     gp_group(&gp, 1, &b->tm_out[1], St, Si);
     gp.out = P->hidden; gp.ldo = H;
     gp.gate[0] = mt + 2 * H; gp.gate[1] = mi + 2 * H;
     enq_gemm(E, &gp, "dbl_out");
-    enq(E, iris_launch_adaln(P->hidden, H, P->xmod, H, S, H, mt + 3 * H, mt + 4 * H, mi + 3 * H,
-                             mi + 4 * H, St, 1e-6f, st), "adaln2");
+    enq_x(E, iris_launch_adaln(P->hidden, H, P->xmod, H, S, H, mt + 3 * H, mt + 4 * H, mi + 3 * H,
+                               mi + 4 * H, St, 1e-6f, st), "adaln2", 0.0, 6.0 * S * (double)H);
     gp_init(&gp, &P->tm_xmod, 2 * F, H, IRIS_EPI_SWIGLU);
     gp_group(&gp, 0, &b->tm_in[0], 0, St);
     gp_group(&gp, 1, &b->tm_in[1], St, Si);
@@ -654,8 +680,8 @@ static void enq_single(iris_cuda_flux_t *tf, int i, enq_t *E) {
     const float *ms = tf->mods + (size_t)12 * H;
     flux_sgl_t *b = &tf->sgl[i];
     IrisGemmParams gp;
-    enq(E, iris_launch_adaln(P->hidden, H, P->xmod, H, S, H, ms, ms + H, NULL, NULL, S, 1e-6f, st),
-        "adaln_s");
+    enq_x(E, iris_launch_adaln(P->hidden, H, P->xmod, H, S, H, ms, ms + H, NULL, NULL, S, 1e-6f, st),
+          "adaln_s", 0.0, 6.0 * S * (double)H);
     gp_init(&gp, &P->tm_xmod, 3 * H + 2 * F, H, IRIS_EPI_SINGLE);
     gp_group(&gp, 0, &b->tm_fused, 0, S);
     gp.qnorm[0] = b->qn; gp.knorm[0] = b->kn;
@@ -663,8 +689,9 @@ static void enq_single(iris_cuda_flux_t *tf, int i, enq_t *E) {
     gp.q = P->q; gp.k = P->k; gp.v = P->v; gp.ldqkv = H; gp.H = H;
     gp.mlp_out = P->cat; gp.ld_mlp = H + F; gp.mlp_col0 = H; gp.swiglu_base = 3 * H;
     enq_gemm(E, &gp, "sgl_fused");
-    enq(E, iris_launch_attention(P->q, H, P->k, P->v, H, P->cat, H + F, S, S, NH,
-                                 1.0f / sqrtf(128.0f), NULL, st), "sgl_attn");
+    enq_x(E, iris_launch_attention(P->q, H, P->k, P->v, H, P->cat, H + F, S, S, NH,
+                                   1.0f / sqrtf(128.0f), NULL, st), "sgl_attn",
+          4.0 * S * S * (double)H, 8.0 * S * (double)H);
     gp_init(&gp, &P->tm_cat, H, H + F, IRIS_EPI_RESID_GATE);
     gp_group(&gp, 0, &b->tm_out, 0, S);
     gp.out = P->hidden; gp.ldo = H;
@@ -717,7 +744,7 @@ int iris_cuda_flux_run_block(iris_cuda_flux_t *tf, int kind, int idx, float *hid
     rc = iris_cuda_check(cudaMemcpyAsync(P->hidden, hidden, bytes, cudaMemcpyHostToDevice, g_rt.stream), "h2d");
     if (!rc) rc = iris_cuda_check(cudaMemcpyAsync(tf->t_dev, &t, 4, cudaMemcpyHostToDevice, g_rt.stream), "t");
     if (rc) return rc;
-    enq_t E = {0, 0};
+    enq_t E = {0};
     enq_mods(tf, &E);
     if (kind == 0) enq_double(tf, idx, &E);
     else enq_single(tf, idx, &E);
@@ -728,6 +755,38 @@ int iris_cuda_flux_run_block(iris_cuda_flux_t *tf, int kind, int idx, float *hid
     return rc;
 }
 
+/* Live per-kernel timing of one forward over the current plan: the kernels
+ * are launched one by one (no graph) with a CUDA event after each, so entry i
+ * covers kernel i plus the launch gap before it.  Returns the number of
+ * entries written or a negative status. */
+int iris_cuda_flux_profile(iris_cuda_flux_t *tf, float timestep, iris_cuda_kernel_time_t *out,
+                           int max_entries) {
+    if (!tf || !out || max_entries <= 0) return iris_fail(IRIS_CUDA_ERR_ARG, "null argument");
+    if (!tf->plan.valid) return iris_fail(IRIS_CUDA_ERR_ARG, "run a forward first (no plan)");
+    cudaEvent_t *ev = (cudaEvent_t *)calloc((size_t)max_entries + 1, sizeof(cudaEvent_t));
+    if (!ev) return iris_fail(IRIS_CUDA_ERR_OOM, "events");
+    int rc = 0, n = 0;
+    for (int i = 0; i <= max_entries && !rc; i++) rc = iris_cuda_check(cudaEventCreate(&ev[i]), "event");
+    if (!rc) rc = iris_cuda_check(cudaMemcpyAsync(tf->t_dev, &timestep, 4, cudaMemcpyHostToDevice,
+                                                  g_rt.stream), "t");
+    if (!rc) {
+        enq_t E = {0};
+        E.prof = out;
+        E.ev = ev;
+        E.maxprof = max_entries;
+        cudaEventRecord(ev[0], g_rt.stream);
+        rc = enqueue_forward(tf, &E);
+        iris_count_launch(E.kernels);
+        if (!rc) rc = iris_cuda_synchronize();
+        for (int i = 0; !rc && i < E.nprof; i++) cudaEventElapsedTime(&out[i].ms, ev[i], ev[i + 1]);
+        n = E.nprof;
+    }
+    for (int i = 0; i <= max_entries; i++)
+        if (ev[i]) cudaEventDestroy(ev[i]);
+    free(ev);
+    return rc ? rc : n;
+}
+
 /* Run the forward of the current plan (captured once into a CUDA graph). */
 static int run_forward(iris_cuda_flux_t *tf) {
     flux_plan_t *P = &tf->plan;
@@ -736,7 +795,7 @@ static int run_forward(iris_cuda_flux_t *tf) {
     if (!P->graph_ok) {
         static int no_graph = -1;
         if (no_graph < 0) no_graph = getenv("IRIS_CUDA_NO_GRAPH") ? 1 : 0;
-        enq_t E = {0, 0};
+        enq_t E = {0};
         if (no_graph) {
             int rc = enqueue_forward(tf, &E);
             iris_count_launch(E.kernels);

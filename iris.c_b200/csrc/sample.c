@@ -150,64 +150,74 @@ float *iris_cuda_init_noise(int batch, int c, int h, int w, int64_t seed) {
 }
 
 /* ------------------------------------------------------------------ samplers */
-typedef struct {
-    float *sched;  /* device copy of the schedule */
-    float *vu;     /* uncond velocity (CFG) */
-} sampler_ws_t;
+/* Device scratch of the samplers (schedule copy, uncond velocity, the two
+ * CFG contexts), kept across calls and grown on demand so back-to-back
+ * images queue without allocations or host synchronisation. */
+static struct {
+    float *sched, *vu, *txt_c, *txt_u;
+    size_t sched_n, vu_n, txt_n;
+} g_sws;
+
+static int ws_grow(float **p, size_t *cap, size_t n) {
+    if (*cap >= n) return 0;
+    cudaStreamSynchronize(g_rt.stream); /* the old buffer may still be in use */
+    iris_dfree(*p);
+    *p = (float *)iris_dmalloc(n * 4);
+    *cap = *p ? n : 0;
+    return *p ? 0 : IRIS_CUDA_ERR_OOM;
+}
 
 /* Core loop.  The latent lives in the plan's latent buffer (the forward reads
- * it in place); z <- z + dt v after every forward. */
+ * it in place); z <- z + dt v after every forward.  Queued on the library
+ * stream; does not synchronise. */
 static int euler_core(iris_cuda_flux_t *tf, int h, int w, const float *txt_c, const float *txt_u,
                       int txt_seq, float guidance, const float *schedule, int steps,
                       enum cudaMemcpyKind txt_kind, void (*progress)(int, int)) {
     cudaStream_t st = g_rt.stream;
     float *z = iris_flux_plan_latent(tf), *v = iris_flux_plan_out(tf);
     size_t n = (size_t)iris_flux_channels(tf) * h * w;
-    size_t txt_bytes = (size_t)txt_seq * iris_flux_text_dim(tf) * 4;
+    size_t txt_n = (size_t)txt_seq * iris_flux_text_dim(tf);
     int rc;
-    float *d_sched = (float *)iris_dmalloc((size_t)(steps + 1) * 4);
-    if (!d_sched) return IRIS_CUDA_ERR_OOM;
-    float *vu = NULL, *txt_cd = NULL, *txt_ud = NULL;
+    if ((rc = ws_grow(&g_sws.sched, &g_sws.sched_n, IRIS_CUDA_MAX_STEPS + 1))) return rc;
     if (txt_u) {
-        vu = (float *)iris_dmalloc(n * 4);
-        txt_cd = (float *)iris_dmalloc(txt_bytes);
-        txt_ud = (float *)iris_dmalloc(txt_bytes);
-        if (!vu || !txt_cd || !txt_ud) { rc = IRIS_CUDA_ERR_OOM; goto out; }
-        if ((rc = iris_cuda_check(cudaMemcpyAsync(txt_cd, txt_c, txt_bytes, txt_kind, st), "txt")) ||
-            (rc = iris_cuda_check(cudaMemcpyAsync(txt_ud, txt_u, txt_bytes, txt_kind, st), "txt")))
-            goto out;
+        if ((rc = ws_grow(&g_sws.vu, &g_sws.vu_n, n))) return rc;
+        if (g_sws.txt_n < txt_n) {
+            size_t c1 = g_sws.txt_n, c2 = g_sws.txt_n;
+            if ((rc = ws_grow(&g_sws.txt_c, &c1, txt_n)) || (rc = ws_grow(&g_sws.txt_u, &c2, txt_n)))
+                return rc;
+            g_sws.txt_n = txt_n;
+        }
+        if ((rc = iris_cuda_check(cudaMemcpyAsync(g_sws.txt_c, txt_c, txt_n * 4, txt_kind, st), "txt")) ||
+            (rc = iris_cuda_check(cudaMemcpyAsync(g_sws.txt_u, txt_u, txt_n * 4, txt_kind, st), "txt")))
+            return rc;
     }
-    if ((rc = iris_cuda_check(cudaMemcpyAsync(d_sched, schedule, (size_t)(steps + 1) * 4,
+    /* the host schedule is staged through pageable memory: the copy completes
+       before cudaMemcpyAsync returns, so the caller's array may be freed */
+    if ((rc = iris_cuda_check(cudaMemcpyAsync(g_sws.sched, schedule, (size_t)(steps + 1) * 4,
                                               cudaMemcpyHostToDevice, st), "schedule")))
-        goto out;
+        return rc;
     for (int s = 0; s < steps; s++) {
         float dt = schedule[s + 1] - schedule[s];
         if (txt_u) {
-            if ((rc = iris_cuda_check(cudaMemcpyAsync(iris_flux_plan_txt(tf), txt_ud, txt_bytes,
+            if ((rc = iris_cuda_check(cudaMemcpyAsync(iris_flux_plan_txt(tf), g_sws.txt_u, txt_n * 4,
                                                       cudaMemcpyDeviceToDevice, st), "txt_u")))
-                goto out;
-            if ((rc = iris_flux_run(tf, d_sched + s, cudaMemcpyDeviceToDevice))) goto out;
-            if ((rc = iris_cuda_check(cudaMemcpyAsync(vu, v, n * 4, cudaMemcpyDeviceToDevice, st),
+                return rc;
+            if ((rc = iris_flux_run(tf, g_sws.sched + s, cudaMemcpyDeviceToDevice))) return rc;
+            if ((rc = iris_cuda_check(cudaMemcpyAsync(g_sws.vu, v, n * 4, cudaMemcpyDeviceToDevice, st),
                                       "v_u")))
-                goto out;
-            if ((rc = iris_cuda_check(cudaMemcpyAsync(iris_flux_plan_txt(tf), txt_cd, txt_bytes,
+                return rc;
+            if ((rc = iris_cuda_check(cudaMemcpyAsync(iris_flux_plan_txt(tf), g_sws.txt_c, txt_n * 4,
                                                       cudaMemcpyDeviceToDevice, st), "txt_c")))
-                goto out;
+                return rc;
         }
-        if ((rc = iris_flux_run(tf, d_sched + s, cudaMemcpyDeviceToDevice))) goto out;
+        if ((rc = iris_flux_run(tf, g_sws.sched + s, cudaMemcpyDeviceToDevice))) return rc;
         iris_count_launch(1);
-        if ((rc = iris_cuda_check(iris_launch_euler(z, v, vu, guidance, dt, (long)n, st), "euler")))
-            goto out;
+        if ((rc = iris_cuda_check(iris_launch_euler(z, v, txt_u ? g_sws.vu : NULL, guidance, dt, (long)n, st),
+                                  "euler")))
+            return rc;
         if (progress) progress(s + 1, steps);
     }
-out:
-    /* the device temporaries are freed only after the queued work used them */
-    cudaStreamSynchronize(st);
-    iris_dfree(d_sched);
-    iris_dfree(vu);
-    iris_dfree(txt_cd);
-    iris_dfree(txt_ud);
-    return rc;
+    return 0;
 }
 
 static float *sample_host(iris_cuda_flux_t *tf, const float *z, int batch, int c, int h, int w,

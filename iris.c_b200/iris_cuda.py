@@ -35,6 +35,10 @@ class FluxConfig(C.Structure):
                    channels=cfg["in_channels"], rope_theta=float(cfg.get("rope_theta", 2000.0)))
 
 
+class KernelTime(C.Structure):
+    _fields_ = [("name", C.c_char * 32), ("flops", C.c_double), ("bytes", C.c_double), ("ms", C.c_float)]
+
+
 class Ref(C.Structure):
     _fields_ = [("latent", _fp), ("h", C.c_int), ("w", C.c_int), ("t_offset", C.c_int)]
 
@@ -67,6 +71,7 @@ SIGNATURES = {
                                              C.c_float, C.c_void_p]),
     "iris_cuda_flux_run_block": (C.c_int, [C.c_void_p, C.c_int, C.c_int, _fp, C.c_int, C.c_int,
                                            C.c_int, C.c_float]),
+    "iris_cuda_flux_profile": (C.c_int, [C.c_void_p, C.c_float, C.POINTER(KernelTime), C.c_int]),
     "iris_cuda_official_schedule": (C.c_void_p, [C.c_int, C.c_int]),
     "iris_cuda_linear_schedule": (C.c_void_p, [C.c_int]),
     "iris_cuda_zimage_schedule": (C.c_void_p, [C.c_int, C.c_int]),
@@ -232,6 +237,15 @@ class Flux:
         else:
             p = lib().iris_cuda_transformer_forward(self.h, _f(lat), h, w, _f(tx), tx.shape[0], t)
         return _take_floats(p, c * h * w, (c, h, w))
+
+    def profile(self, t: float, max_entries: int = 512):
+        """Per-kernel CUDA-event times of one forward over the last input shape."""
+        buf = (KernelTime * max_entries)()
+        n = lib().iris_cuda_flux_profile(self.h, t, buf, max_entries)
+        if n < 0:
+            raise IrisCudaError(last_error())
+        return [dict(name=buf[i].name.decode(), flops=buf[i].flops, bytes=buf[i].bytes, ms=buf[i].ms)
+                for i in range(n)]
 
     def sample_euler(self, z, txt, schedule, refs=(), txt_uncond=None, guidance=1.0):
         zz = np.ascontiguousarray(z, np.float32)
