@@ -231,6 +231,21 @@ int iris_gpu_linear_bf16_native_into(iris_gpu_tensor_t out, iris_gpu_tensor_t x,
 void iris_gpu_adaln_norm_bf16(iris_gpu_tensor_t out, iris_gpu_tensor_t x,
                               iris_gpu_tensor_t shift_bf16, iris_gpu_tensor_t scale_bf16,
                               int seq, int hidden, float eps);
+/* Same result as iris_gpu_adaln_norm_bf16, for callers that cannot allocate
+ * device memory (a host application whose pool allocator owns all device
+ * memory, code running while a stream capture is open, or latency-critical
+ * loops that cannot take cudaMalloc/cudaFree's implicit synchronisation).  No
+ * counterpart in the reference.  Takes raw bf16 device pointers the caller
+ * owns (x, out [seq, hidden]; shift, scale [hidden]) and a cudaStream_t
+ * (void *, 0 = default stream); queues work without synchronising and calls
+ * no allocating routine.  Its scratch is one fixed array inside the library
+ * (about 16.8 MB per GPU, held until exit): seq * hidden <= 4194304 and
+ * hidden <= 8192, larger calls return IRIS_CUDA_ERR_ARG.  All calls share that
+ * array, so calls whose GPU work overlaps race; the first call on a device
+ * looks up the array's address and should come before any stream capture. */
+int iris_gpu_adaln_norm_bf16_noalloc(void *out, const void *x, const void *shift,
+                                     const void *scale, int seq, int hidden, float eps,
+                                     void *stream);
 /* per-head RMSNorm of Q and K in place.  :438 */
 void iris_gpu_qk_rms_norm_bf16(iris_gpu_tensor_t q, iris_gpu_tensor_t k,
                                iris_gpu_tensor_t q_weight_bf16, iris_gpu_tensor_t k_weight_bf16,

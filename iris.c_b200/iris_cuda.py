@@ -110,6 +110,8 @@ SIGNATURES = {
                                                    C.c_int]),
     "iris_gpu_adaln_norm_bf16": (None, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                         C.c_int, C.c_float]),
+    "iris_gpu_adaln_norm_bf16_noalloc": (C.c_int, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p,
+                                                   C.c_int, C.c_int, C.c_float, C.c_void_p]),
     "iris_gpu_qk_rms_norm_bf16": (None, [C.c_void_p, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int,
                                          C.c_int, C.c_int, C.c_float]),
     "iris_gpu_rope_unified_bf16": (None, [C.c_void_p, C.c_void_p, _fp, _fp, _fp, _fp, _fp, _fp,
