@@ -60,6 +60,10 @@ def parse_args(argv=None):
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--blocks", type=int, nargs=2, metavar=("DOUBLE", "SINGLE"), default=None,
+                    help="profiling case: a Klein-4B-shaped model truncated to DOUBLE + SINGLE blocks "
+                         "(same kernels and shapes, less memory); not a benchmark number")
+    ap.add_argument("--profile-out", default=None, help="write the per-kernel CUDA-event profile (JSON)")
     return ap.parse_args(argv)
 
 
@@ -260,7 +264,10 @@ def run_ours(args):
     lib = iris_cuda.lib()
     if lib.iris_cuda_init(local) != 0:
         raise iris_cuda.IrisCudaError(iris_cuda.last_error())
-    model = iris_cuda.Flux.random(iris_cuda.FluxConfig.from_hf(K4B), seed=WEIGHT_SEED, std=0.02)
+    mcfg = dict(K4B)
+    if args.blocks:
+        mcfg.update(num_layers=args.blocks[0], num_single_layers=args.blocks[1])
+    model = iris_cuda.Flux.random(iris_cuda.FluxConfig.from_hf(mcfg), seed=WEIGHT_SEED, std=0.02)
     stream = torch.cuda.ExternalStream(lib.iris_cuda_stream(), device=torch.device("cuda", local))
 
     rng = np.random.default_rng(500 + rank)
@@ -354,6 +361,9 @@ def run_ours(args):
                 a["ms"] += b["ms"]
     for e in prof:
         e["ms"] /= 3.0
+    if args.profile_out and rank == 0:
+        with open(args.profile_out, "w") as f:
+            json.dump(prof, f, indent=0)
     gemm = [e for e in prof if e["flops"] > 0 and "attn" not in e["name"] and e["name"] != "mods"]
     attn = [e for e in prof if "attn" in e["name"]]
     g_fl, g_ms = sum(e["flops"] for e in gemm), sum(e["ms"] for e in gemm)
@@ -377,7 +387,7 @@ def run_ours(args):
 
     # ---- CPU baseline (rank 0, N=1 only)
     cpu = None
-    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+    if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.blocks:
         try:
             rs = RefSample()
             rs.step_seconds()
@@ -394,7 +404,7 @@ def run_ours(args):
         "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "images_per_s": value / STEPS_PER_IMAGE,
-        "config": bench_config(world),
+        "config": dict(bench_config(world), **({"truncated_blocks": args.blocks} if args.blocks else {})),
         "clocks": clocks.summary(),
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "wall_s": e2e_wall},
