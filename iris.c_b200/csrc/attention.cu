@@ -261,7 +261,7 @@ extern "C" cudaError_t iris_attention_init(void) {
   return e;
 }
 
-extern "C" cudaError_t iris_launch_attention(const void* q, int ldq, const void* k, const void* v,
+extern "C" cudaError_t iris_launch_attention_mma(const void* q, int ldq, const void* k, const void* v,
                                              int ldk, void* o, int ldo, int sq, int sk, int heads,
                                              float scale, const uint8_t* key_mask,
                                              cudaStream_t stream) {

@@ -82,6 +82,15 @@ cudaError_t iris_attention_init(void);
 cudaError_t iris_launch_attention(const void *q, int ldq, const void *k, const void *v, int ldk,
                                   void *o, int ldo, int sq, int sk, int heads, float scale,
                                   const uint8_t *key_mask, cudaStream_t stream);
+/* the two implementations behind it: tcgen05/TMEM (default) and mma.sync */
+cudaError_t iris_launch_attention_tc(const void *q, int ldq, const void *k, const void *v, int ldk,
+                                     void *o, int ldo, int sq, int sk, int heads, float scale,
+                                     const uint8_t *key_mask, cudaStream_t stream);
+cudaError_t iris_launch_attention_mma(const void *q, int ldq, const void *k, const void *v, int ldk,
+                                      void *o, int ldo, int sq, int sk, int heads, float scale,
+                                      const uint8_t *key_mask, cudaStream_t stream);
+cudaError_t iris_attention_tc_init(void);
+void iris_attention_set_status(int *status);
 
 /* ------------------------------------------------------------------ row kernels */
 /* out_bf16[r] = (1 + scale_g) * LayerNorm(x[r]) + shift_g, g = (r >= split) */

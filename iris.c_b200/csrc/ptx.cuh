@@ -126,6 +126,22 @@ __device__ __forceinline__ uint64_t umma_desc_k_sw128(uint32_t smem_addr) {
   return d;
 }
 
+// Shared-memory descriptor for an MN-major operand (MN contiguous in memory)
+// written by TMA with 128-byte swizzle: each 128 B row holds 64 consecutive
+// MN elements of one K index; 8 K rows form a 1024 B atom.
+//   leading byte offset = distance between successive 64-element MN chunks
+//   stride byte offset  = distance between successive groups of 8 K rows
+__device__ __forceinline__ uint64_t umma_desc_mn_sw128(uint32_t smem_addr, uint32_t lbo_bytes,
+                                                       uint32_t sbo_bytes) {
+  uint64_t d = 0;
+  d |= (uint64_t)((smem_addr >> 4) & 0x3FFF);
+  d |= (uint64_t)((lbo_bytes >> 4) & 0x3FFF) << 16;
+  d |= (uint64_t)((sbo_bytes >> 4) & 0x3FFF) << 32;
+  d |= (uint64_t)1 << 46;
+  d |= (uint64_t)2 << 61;
+  return d;
+}
+
 // Instruction descriptor for kind::f16 with bf16 A/B, f32 accumulate,
 // both operands K-major, tile M x N.
 __host__ __device__ constexpr uint32_t umma_idesc_bf16_f32(int M, int N) {
@@ -134,6 +150,11 @@ __host__ __device__ constexpr uint32_t umma_idesc_bf16_f32(int M, int N) {
          | (1u << 10)                   // B format: bf16
          | ((uint32_t)(N >> 3) << 17)   // N / 8
          | ((uint32_t)(M >> 4) << 24);  // M / 16
+}
+
+// Same with B MN-major (bit 16): B is stored N-contiguous (e.g. V as [keys, d]).
+__host__ __device__ constexpr uint32_t umma_idesc_bf16_f32_bmn(int M, int N) {
+  return umma_idesc_bf16_f32(M, N) | (1u << 16);
 }
 
 // D[tmem] (+)= A[smem] * B[smem]^T, issued by one thread.
@@ -197,6 +218,34 @@ __device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
       : "memory");
 #pragma unroll
   for (int i = 0; i < 32; i++) v[i] = __uint_as_float(r[i]);
+}
+
+// Registers -> 32 consecutive 32-bit TMEM columns of this thread's lane; the
+// store is complete (wait::st) when the block returns.
+__device__ __forceinline__ void tmem_st32(uint32_t taddr, const float* v) {
+  asm volatile(
+      "tcgen05.st.sync.aligned.32x32b.x32.b32 [%0], "
+      "{%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16,"
+      "%17,%18,%19,%20,%21,%22,%23,%24,%25,%26,%27,%28,%29,%30,%31,%32};\n\t"
+      "tcgen05.wait::st.sync.aligned;" ::"r"(taddr),
+      "r"(__float_as_uint(v[0])), "r"(__float_as_uint(v[1])), "r"(__float_as_uint(v[2])),
+      "r"(__float_as_uint(v[3])), "r"(__float_as_uint(v[4])), "r"(__float_as_uint(v[5])),
+      "r"(__float_as_uint(v[6])), "r"(__float_as_uint(v[7])), "r"(__float_as_uint(v[8])),
+      "r"(__float_as_uint(v[9])), "r"(__float_as_uint(v[10])), "r"(__float_as_uint(v[11])),
+      "r"(__float_as_uint(v[12])), "r"(__float_as_uint(v[13])), "r"(__float_as_uint(v[14])),
+      "r"(__float_as_uint(v[15])), "r"(__float_as_uint(v[16])), "r"(__float_as_uint(v[17])),
+      "r"(__float_as_uint(v[18])), "r"(__float_as_uint(v[19])), "r"(__float_as_uint(v[20])),
+      "r"(__float_as_uint(v[21])), "r"(__float_as_uint(v[22])), "r"(__float_as_uint(v[23])),
+      "r"(__float_as_uint(v[24])), "r"(__float_as_uint(v[25])), "r"(__float_as_uint(v[26])),
+      "r"(__float_as_uint(v[27])), "r"(__float_as_uint(v[28])), "r"(__float_as_uint(v[29])),
+      "r"(__float_as_uint(v[30])), "r"(__float_as_uint(v[31]))
+      : "memory");
+}
+
+// Make this thread's generic-proxy shared-memory writes visible to the async
+// proxy (TMA, tcgen05.mma) before signalling the consumer.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
 }
 
 __device__ __forceinline__ uint32_t lane_id() { return threadIdx.x & 31; }

@@ -99,6 +99,8 @@ int iris_cuda_init(int device) {
     cudaMemset(g_rt.d_status, 0, sizeof(int));
     if ((e = iris_gemm_init()) != cudaSuccess) return iris_cuda_check(e, "gemm init");
     if ((e = iris_attention_init()) != cudaSuccess) return iris_cuda_check(e, "attention init");
+    if ((e = iris_attention_tc_init()) != cudaSuccess) return iris_cuda_check(e, "attention init");
+    iris_attention_set_status(g_rt.d_status);
     g_rt.initialized = 1;
     return IRIS_CUDA_OK;
 }
