@@ -222,3 +222,31 @@ def zimage_tensor_specs(cfg: dict) -> list[tuple[str, tuple, str]]:
     for i in range(cfg["n_layers"]):
         s += block(f"layers.{i}.", True)
     return s
+
+
+def make_zimage_model(model_dir: str, cfg: dict, seed: int, std: float = 0.02,
+                      norm_mode: str = "random") -> dict[str, np.ndarray]:
+    """Random Z-Image model directory (config keys as read by the reference's
+    model autodetection, iris.c:300-330); returns {name: f32 values}."""
+    os.makedirs(os.path.join(model_dir, "transformer"), exist_ok=True)
+    conf = {k: cfg[k] for k in ("dim", "n_layers", "cap_feat_dim", "in_channels", "patch_size",
+                                "rope_theta", "axes_dims")}
+    conf.update(_class_name="ZImageTransformer2DModel", n_refiner_layers=cfg["n_refiner"],
+                n_heads=cfg["dim"] // 128)
+    with open(os.path.join(model_dir, "transformer", "config.json"), "w") as f:
+        json.dump(conf, f, indent=1)
+    with open(os.path.join(model_dir, "model_index.json"), "w") as f:
+        json.dump({"_class_name": "ZImagePipeline"}, f)
+    bits = {n: gen_tensor(seed, n, shp, kind, std, norm_mode) for n, shp, kind in zimage_tensor_specs(cfg)}
+    write_safetensors(os.path.join(model_dir, "transformer", "diffusion_pytorch_model.safetensors"), bits)
+    return {n: bf16_bits_to_f32(b) for n, b in bits.items()}
+
+
+def zimage_weights(cfg: dict, seed: int, std: float = 0.02, norm_mode: str = "random"):
+    return {n: bf16_bits_to_f32(gen_tensor(seed, n, shp, kind, std, norm_mode))
+            for n, shp, kind in zimage_tensor_specs(cfg)}
+
+
+def zimage_ffn_dim(dim: int) -> int:
+    """ffn width used by the reference when no weight says otherwise: 8*dim/3 rounded up to 256."""
+    return (8 * dim // 3 + 255) // 256 * 256

@@ -173,3 +173,41 @@ def ref_zimage_schedule(ref: RefLib, steps, seq):
     out = np.zeros(steps + 1, np.float32)
     assert ref.lib.ref_zimage_schedule(steps, seq, _f(out)) == 0
     return out
+
+
+class RefZImage:
+    """A reference Z-Image transformer loaded from a model directory."""
+
+    def __init__(self, ref: RefLib, model_dir: str, cfg: dict):
+        self.ref = ref
+        self.cfg = cfg
+        arr = (C.c_int * 10)(cfg["dim"], cfg["dim"] // 128, cfg["n_layers"], cfg["n_refiner"],
+                             cfg["cap_feat_dim"], cfg["in_channels"], cfg["patch_size"], *cfg["axes_dims"])
+        self.h = ref.lib.ref_zi_load(model_dir.encode(), arr, float(cfg["rope_theta"]))
+        if not self.h:
+            raise RuntimeError(f"reference failed to load {model_dir}")
+
+    def close(self):
+        if self.h:
+            self.ref.lib.ref_zi_free(self.h)
+            self.h = None
+
+    def forward(self, latent, cap, t):
+        c, h, w = latent.shape
+        lat = np.ascontiguousarray(latent, np.float32)
+        cp = np.ascontiguousarray(cap, np.float32)
+        out = np.zeros_like(lat)
+        rc = self.ref.lib.ref_zi_forward(self.h, _f(lat), h, w, t, _f(cp), cp.shape[0], c, _f(out))
+        assert rc == 0
+        return out
+
+    def sample_euler(self, z, cap, schedule):
+        c, h, w = z.shape
+        zz = np.ascontiguousarray(z, np.float32).copy()
+        cp = np.ascontiguousarray(cap, np.float32)
+        sc = np.ascontiguousarray(schedule, np.float32)
+        out = np.zeros_like(zz)
+        rc = self.ref.lib.ref_sample_euler_zimage(self.h, _f(zz), c, h, w, self.cfg["patch_size"], _f(cp),
+                                                  cp.shape[0], _f(sc), len(sc) - 1, _f(out))
+        assert rc == 0
+        return out

@@ -49,3 +49,24 @@ def ref_inputs(channels, txt_shape):
     refs = [rr.standard_normal((channels, 2, 3)).astype(np.float32) for _ in range(2)]
     ctx_u = rr.standard_normal(txt_shape).astype(np.float32)
     return refs, ctx_u
+
+
+ZIMAGE_CASES = {
+    # tiny: dim 256 (2 heads), 1 refiner each, 1 main layer; 30 image tokens (pad 2), 7 caption tokens (pad 25)
+    "zimage_tiny": dict(cfg=dict(dim=256, n_heads=2, n_layers=1, n_refiner=1, cap_feat_dim=64, in_channels=16,
+                                 patch_size=2, rope_theta=256.0, axes_dims=[32, 48, 48], ffn_dim=768,
+                                 adaln_dim=256, t_mid=256),
+                        seed=3, std=0.05, norm_mode="unit", latent=(16, 10, 12), cap=7),
+    # small: dim 512, 2 refiners each, 2 main layers; 64 image tokens (no pad), 40 caption tokens (pad 24)
+    "zimage_small": dict(cfg=dict(dim=512, n_heads=4, n_layers=2, n_refiner=2, cap_feat_dim=128, in_channels=16,
+                                  patch_size=2, rope_theta=256.0, axes_dims=[32, 48, 48], ffn_dim=1536,
+                                  adaln_dim=256, t_mid=512),
+                         seed=9, std=0.04, norm_mode="unit", latent=(16, 16, 16), cap=40),
+}
+
+
+def zimage_inputs(spec):
+    r = np.random.default_rng(spec["seed"] + 100)
+    lat = r.standard_normal(spec["latent"]).astype(np.float32)
+    cap = r.standard_normal((spec["cap"], spec["cfg"]["cap_feat_dim"])).astype(np.float32)
+    return lat, cap

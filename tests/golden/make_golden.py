@@ -25,12 +25,13 @@ sys.path.insert(0, ROOT)
 sys.path.insert(0, os.path.dirname(os.path.abspath(__file__)))
 
 from oracle import model_gen as mg  # noqa: E402
-from oracle.ref_lib import (RefFlux, RefLib, ref_init_noise, ref_official_schedule,  # noqa: E402
-                            ref_zimage_schedule)
+from oracle.ref_lib import (RefFlux, RefLib, RefZImage, ref_init_noise,  # noqa: E402
+                            ref_official_schedule, ref_zimage_schedule)
 
 OUT = os.path.dirname(os.path.abspath(__file__))
 
-from cases import FLUX_CASES, block_inputs, ref_inputs, rng_inputs  # noqa: E402
+from cases import (FLUX_CASES, ZIMAGE_CASES, block_inputs, ref_inputs, rng_inputs,  # noqa: E402
+                   zimage_inputs)
 
 
 def flux_case(ref: RefLib, name: str, spec: dict) -> dict:
@@ -74,6 +75,32 @@ def flux_case(ref: RefLib, name: str, spec: dict) -> dict:
     return out
 
 
+def zimage_case(name: str, spec: dict) -> dict:
+    """Z-Image outputs from the alias-safe reference build (oracle/alias_safe_matmul.c:
+    the reference's code with its in-place attention output GEMM made alias-safe),
+    plus the unmodified builds' velocities, which disagree with each other."""
+    out = {}
+    lat, cap = zimage_inputs(spec)
+    with tempfile.TemporaryDirectory() as d:
+        mg.make_zimage_model(d, spec["cfg"], spec["seed"], spec["std"], spec["norm_mode"])
+        for variant, tag in (("generic_as", ""), ("generic", "_unfixed_generic"), ("blas", "_unfixed_blas")):
+            ref = RefLib(variant)
+            rz = RefZImage(ref, d, spec["cfg"])
+            for t in ((0.3, 0.9) if not tag else (0.3,)):
+                out[f"v_t{t}{tag}"] = rz.forward(lat, cap, t)
+            if not tag:
+                n_img = (spec["latent"][1] // 2) * (spec["latent"][2] // 2)
+                sched = ref_zimage_schedule(ref, 3, n_img)
+                z0 = ref_init_noise(ref, *spec["latent"], 42)
+                out["sched3"], out["z0"] = sched, z0
+                out["z3"] = rz.sample_euler(z0, cap, sched)
+            rz.close()
+    meta = dict(cfg=spec["cfg"], seed=spec["seed"], std=spec["std"], norm_mode=spec["norm_mode"],
+                latent=list(spec["latent"]), cap=spec["cap"], variant="generic_as")
+    out["meta"] = np.frombuffer(json.dumps(meta).encode(), dtype=np.uint8)
+    return out
+
+
 def sampler_case(ref: RefLib) -> dict:
     out = {}
     for steps, seq in ((4, 1024), (4, 256), (50, 4096), (28, 4608), (4, 12544)):
@@ -93,6 +120,10 @@ def main():
     ref = RefLib("generic")
     for name, spec in FLUX_CASES.items():
         data = flux_case(ref, name, spec)
+        np.savez_compressed(os.path.join(OUT, f"{name}.npz"), **data)
+        print("wrote", name, {k: v.shape for k, v in data.items() if k != "meta"})
+    for name, spec in ZIMAGE_CASES.items():
+        data = zimage_case(name, spec)
         np.savez_compressed(os.path.join(OUT, f"{name}.npz"), **data)
         print("wrote", name, {k: v.shape for k, v in data.items() if k != "meta"})
     np.savez_compressed(os.path.join(OUT, "sampler.npz"), **sampler_case(ref))
