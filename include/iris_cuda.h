@@ -195,6 +195,51 @@ int iris_cuda_sample_euler_dev(iris_cuda_flux_t *tf, float *d_z, int h, int w,
                                int txt_seq_uncond, float guidance, const float *schedule,
                                int num_steps);
 
+/* ------------------------------------------------------------------ 2c. Z-Image S3-DiT */
+typedef struct iris_cuda_zimage iris_cuda_zimage_t;
+
+typedef struct {
+    int dim;             /* 3840 */
+    int heads;           /* dim / 128 */
+    int n_layers;        /* 30 main layers */
+    int n_refiner;       /* 2 noise + 2 context refiners */
+    int cap_feat_dim;    /* 2560 */
+    int in_channels;     /* 16 */
+    int patch_size;      /* 2 */
+    int ffn_dim;         /* 10240 */
+    int adaln_dim;       /* min(dim, 256) */
+    int t_mid;           /* timestep MLP width, 1024 */
+    float rope_theta;    /* 256 */
+    int axes_dims[3];    /* 32, 48, 48 */
+} iris_cuda_zimage_config_t;
+
+/* Replaces zi_transformer_load_safetensors (iris_transformer_zimage.c:2164)
+ * with the config keys of the reference's model autodetection (iris.c:300-330). */
+iris_cuda_zimage_t *iris_cuda_zimage_load(const char *model_dir);
+/* Random-init Z-Image model (seeded device RNG); no reference counterpart. */
+iris_cuda_zimage_t *iris_cuda_zimage_random(const iris_cuda_zimage_config_t *cfg, uint64_t seed,
+                                            float std, int norm_unit);
+/* Replaces zi_transformer_free (iris_transformer_zimage.c:2429). */
+void iris_cuda_zimage_free(iris_cuda_zimage_t *z);
+int iris_cuda_zimage_get_config(const iris_cuda_zimage_t *z, iris_cuda_zimage_config_t *out);
+size_t iris_cuda_zimage_weight_bytes(const iris_cuda_zimage_t *z);
+/* Replaces zi_transformer_forward (iris_transformer_zimage.c:1696): latent
+ * [in_channels, latent_h, latent_w] (pre-patch), caption features
+ * [cap_seq, cap_feat_dim]; returns malloc'd model output of the latent's shape. */
+float *iris_cuda_zi_transformer_forward(iris_cuda_zimage_t *z, const float *latent, int latent_h,
+                                        int latent_w, float timestep, const float *cap_feats,
+                                        int cap_seq);
+/* Replaces iris_sample_euler_zimage (iris_sample.c:412): t = 1 - sigma,
+ * z += (sigma_next - sigma) * (-v).  Returns the malloc'd final latent. */
+float *iris_cuda_sample_euler_zimage(iris_cuda_zimage_t *z, const float *zin, int batch,
+                                     int channels, int h, int w, int patch_size,
+                                     const float *cap_feats, int cap_seq, const float *schedule,
+                                     int num_steps, void (*progress_callback)(int step, int total));
+/* Device-resident Z-Image sampler (d_z updated in place, d_cap device). */
+int iris_cuda_sample_euler_zimage_dev(iris_cuda_zimage_t *z, float *d_z, int h, int w,
+                                      const float *d_cap, int cap_seq, const float *schedule,
+                                      int num_steps);
+
 /* ------------------------------------------------------------------ 3. iris_gpu_* surface
  * Device-resident tensors and ops with the names and signatures of
  * iris_metal.h.  Tensors are f32 or bf16 device buffers; "host" weight

@@ -77,68 +77,11 @@ struct iris_cuda_flux {
     char model_dir[1024];
 };
 
-/* ------------------------------------------------------------------ weight sources */
-typedef struct {
-    int random;
-    st_model_t st;
-    uint64_t seed;
-    float std;
-    int norm_unit;
-    uint16_t *host_stage;
-    size_t host_stage_n;
-} wsrc_t;
-
-static int is_norm_name(const char *name) {
-    return strstr(name, "norm_q") || strstr(name, "norm_k") || strstr(name, "norm_added_q") ||
-           strstr(name, "norm_added_k");
-}
-
-/* Write the reference-layout tensor `name` ([numel] bf16) to device memory d_dst. */
-static int wsrc_get(wsrc_t *ws, const char *name, size_t numel, uint16_t *d_dst) {
-    if (ws->random) {
-        int unit = ws->norm_unit && is_norm_name(name);
-        cudaError_t e = iris_launch_randn_bf16(d_dst, (long)numel, ws->seed, iris_crc32(name),
-                                               unit ? 1.0f : 0.0f, unit ? 0.1f : ws->std,
-                                               g_rt.stream);
-        iris_count_launch(1);
-        return iris_cuda_check(e, name);
-    }
-    const st_tensor_t *t = st_find(&ws->st, name);
-    if (!t) return iris_fail(IRIS_CUDA_ERR_IO, "tensor %s not found", name);
-    if (ws->host_stage_n < numel) {
-        if (ws->host_stage) cudaFreeHost(ws->host_stage);
-        ws->host_stage = NULL;
-        ws->host_stage_n = 0;
-        if (cudaMallocHost((void **)&ws->host_stage, numel * 2) != cudaSuccess)
-            return iris_fail(IRIS_CUDA_ERR_OOM, "pinned staging for %s", name);
-        ws->host_stage_n = numel;
-    }
-    /* the staging buffer is reused: finish the previous upload first */
-    cudaStreamSynchronize(g_rt.stream);
-    if (st_read_bf16(&ws->st, t, ws->host_stage, numel) != 0)
-        return iris_fail(IRIS_CUDA_ERR_IO, "tensor %s: bad shape or dtype", name);
-    return iris_cuda_check(cudaMemcpyAsync(d_dst, ws->host_stage, numel * 2,
-                                           cudaMemcpyHostToDevice, g_rt.stream), name);
-}
-
-/* f32 copy of a (small) tensor, through a bf16 device temp */
-static int wsrc_get_f32(wsrc_t *ws, const char *name, size_t numel, float *d_dst, uint16_t *tmp) {
-    int rc = wsrc_get(ws, name, numel, tmp);
-    if (rc) return rc;
-    iris_count_launch(1);
-    return iris_cuda_check(iris_launch_bf16_to_f32(tmp, d_dst, (long)numel, g_rt.stream), name);
-}
-
 /* ------------------------------------------------------------------ load */
 static uint16_t *walloc(iris_cuda_flux_t *tf, size_t numel) {
     uint16_t *p = (uint16_t *)iris_dmalloc(numel * 2);
     if (p) tf->weight_bytes += numel * 2;
     return p;
-}
-
-static int mk_tmap(CUtensorMap *m, const void *p, int rows, int cols, int ld, int box) {
-    int r = iris_make_tmap_bf16(m, p, (uint64_t)rows, (uint64_t)cols, (uint64_t)ld, (uint32_t)box);
-    return r ? iris_fail(IRIS_CUDA_ERR_CUDA, "tensor map encode failed (%d)", r) : 0;
 }
 
 static int check_cfg(const iris_cuda_flux_config_t *c) {
@@ -152,7 +95,7 @@ static int check_cfg(const iris_cuda_flux_config_t *c) {
     return 0;
 }
 
-static int load_weights(iris_cuda_flux_t *tf, wsrc_t *ws) {
+static int load_weights(iris_cuda_flux_t *tf, iris_wsrc_t *ws) {
     int H = tf->H, F = tf->F, C = tf->C, T = tf->T;
     int rc = 0;
     char nm[256];
@@ -168,20 +111,20 @@ static int load_weights(iris_cuda_flux_t *tf, wsrc_t *ws) {
     ALLOC(tf->w_t2, (size_t)H * H);
     ALLOC(tf->w_mod, (size_t)17 * H * H);
     ALLOC(tf->w_proj, (size_t)C * H);
-    CHK(wsrc_get(ws, "x_embedder.weight", (size_t)H * C, tf->w_x));
-    CHK(wsrc_get(ws, "context_embedder.weight", (size_t)H * T, tf->w_ctx));
-    CHK(wsrc_get(ws, "time_guidance_embed.timestep_embedder.linear_1.weight", (size_t)H * 256, tf->w_t1));
-    CHK(wsrc_get(ws, "time_guidance_embed.timestep_embedder.linear_2.weight", (size_t)H * H, tf->w_t2));
-    CHK(wsrc_get(ws, "double_stream_modulation_img.linear.weight", (size_t)6 * H * H, tf->w_mod));
-    CHK(wsrc_get(ws, "double_stream_modulation_txt.linear.weight", (size_t)6 * H * H,
+    CHK(iris_wsrc_get(ws, "x_embedder.weight", (size_t)H * C, tf->w_x));
+    CHK(iris_wsrc_get(ws, "context_embedder.weight", (size_t)H * T, tf->w_ctx));
+    CHK(iris_wsrc_get(ws, "time_guidance_embed.timestep_embedder.linear_1.weight", (size_t)H * 256, tf->w_t1));
+    CHK(iris_wsrc_get(ws, "time_guidance_embed.timestep_embedder.linear_2.weight", (size_t)H * H, tf->w_t2));
+    CHK(iris_wsrc_get(ws, "double_stream_modulation_img.linear.weight", (size_t)6 * H * H, tf->w_mod));
+    CHK(iris_wsrc_get(ws, "double_stream_modulation_txt.linear.weight", (size_t)6 * H * H,
                  tf->w_mod + (size_t)6 * H * H));
-    CHK(wsrc_get(ws, "single_stream_modulation.linear.weight", (size_t)3 * H * H,
+    CHK(iris_wsrc_get(ws, "single_stream_modulation.linear.weight", (size_t)3 * H * H,
                  tf->w_mod + (size_t)12 * H * H));
-    CHK(wsrc_get(ws, "norm_out.linear.weight", (size_t)2 * H * H, tf->w_mod + (size_t)15 * H * H));
-    CHK(wsrc_get(ws, "proj_out.weight", (size_t)C * H, tf->w_proj));
-    CHK(mk_tmap(&tf->tm_x, tf->w_x, H, C, C, 256));
-    CHK(mk_tmap(&tf->tm_ctx, tf->w_ctx, H, T, T, 256));
-    CHK(mk_tmap(&tf->tm_proj, tf->w_proj, C, H, H, 128));
+    CHK(iris_wsrc_get(ws, "norm_out.linear.weight", (size_t)2 * H * H, tf->w_mod + (size_t)15 * H * H));
+    CHK(iris_wsrc_get(ws, "proj_out.weight", (size_t)C * H, tf->w_proj));
+    CHK(iris_mk_tmap(&tf->tm_x, tf->w_x, H, C, C, 256));
+    CHK(iris_mk_tmap(&tf->tm_ctx, tf->w_ctx, H, T, T, 256));
+    CHK(iris_mk_tmap(&tf->tm_proj, tf->w_proj, C, H, H, 128));
 
     tf->dbl = (flux_dbl_t *)calloc((size_t)tf->cfg.n_double, sizeof(flux_dbl_t));
     tf->sgl = (flux_sgl_t *)calloc((size_t)tf->cfg.n_single, sizeof(flux_sgl_t));
@@ -205,24 +148,24 @@ static int load_weights(iris_cuda_flux_t *tf, wsrc_t *ws) {
             if (!b->qn[s] || !b->kn[s]) { rc = IRIS_CUDA_ERR_OOM; goto done; }
             for (int j = 0; j < 3; j++) {
                 snprintf(nm, sizeof(nm), "transformer_blocks.%d.%s.weight", i, qkv_name[s][j]);
-                CHK(wsrc_get(ws, nm, (size_t)H * H, b->w_qkv[s] + (size_t)j * H * H));
+                CHK(iris_wsrc_get(ws, nm, (size_t)H * H, b->w_qkv[s] + (size_t)j * H * H));
             }
             snprintf(nm, sizeof(nm), "transformer_blocks.%d.%s.weight", i, out_name[s]);
-            CHK(wsrc_get(ws, nm, (size_t)H * H, b->w_out[s]));
+            CHK(iris_wsrc_get(ws, nm, (size_t)H * H, b->w_out[s]));
             snprintf(nm, sizeof(nm), "transformer_blocks.%d.%s.linear_in.weight", i, ff_name[s]);
-            CHK(wsrc_get(ws, nm, (size_t)2 * F * H, tmp));
+            CHK(iris_wsrc_get(ws, nm, (size_t)2 * F * H, tmp));
             iris_count_launch(1);
             CHK(iris_cuda_check(iris_launch_interleave_gate_up(b->w_in[s], tmp, F, H, g_rt.stream), nm));
             snprintf(nm, sizeof(nm), "transformer_blocks.%d.%s.linear_out.weight", i, ff_name[s]);
-            CHK(wsrc_get(ws, nm, (size_t)H * F, b->w_down[s]));
+            CHK(iris_wsrc_get(ws, nm, (size_t)H * F, b->w_down[s]));
             snprintf(nm, sizeof(nm), "transformer_blocks.%d.%s.weight", i, qn_name[s]);
-            CHK(wsrc_get_f32(ws, nm, 128, b->qn[s], tmp + (size_t)2 * F * H));
+            CHK(iris_wsrc_get_f32(ws, nm, 128, b->qn[s], tmp + (size_t)2 * F * H));
             snprintf(nm, sizeof(nm), "transformer_blocks.%d.%s.weight", i, kn_name[s]);
-            CHK(wsrc_get_f32(ws, nm, 128, b->kn[s], tmp + (size_t)2 * F * H + 128));
-            CHK(mk_tmap(&b->tm_qkv[s], b->w_qkv[s], 3 * H, H, H, 256));
-            CHK(mk_tmap(&b->tm_out[s], b->w_out[s], H, H, H, 256));
-            CHK(mk_tmap(&b->tm_in[s], b->w_in[s], 2 * F, H, H, 256));
-            CHK(mk_tmap(&b->tm_down[s], b->w_down[s], H, F, F, 256));
+            CHK(iris_wsrc_get_f32(ws, nm, 128, b->kn[s], tmp + (size_t)2 * F * H + 128));
+            CHK(iris_mk_tmap(&b->tm_qkv[s], b->w_qkv[s], 3 * H, H, H, 256));
+            CHK(iris_mk_tmap(&b->tm_out[s], b->w_out[s], H, H, H, 256));
+            CHK(iris_mk_tmap(&b->tm_in[s], b->w_in[s], 2 * F, H, H, 256));
+            CHK(iris_mk_tmap(&b->tm_down[s], b->w_down[s], H, F, F, 256));
         }
     }
     for (int i = 0; i < tf->cfg.n_single; i++) {
@@ -233,7 +176,7 @@ static int load_weights(iris_cuda_flux_t *tf, wsrc_t *ws) {
         b->kn = (float *)iris_dmalloc(128 * 4);
         if (!b->qn || !b->kn) { rc = IRIS_CUDA_ERR_OOM; goto done; }
         snprintf(nm, sizeof(nm), "single_transformer_blocks.%d.attn.to_qkv_mlp_proj.weight", i);
-        CHK(wsrc_get(ws, nm, (size_t)(3 * H + 2 * F) * H, tmp));
+        CHK(iris_wsrc_get(ws, nm, (size_t)(3 * H + 2 * F) * H, tmp));
         CHK(iris_cuda_check(cudaMemcpyAsync(b->w_fused, tmp, (size_t)3 * H * H * 2,
                                             cudaMemcpyDeviceToDevice, g_rt.stream), nm));
         iris_count_launch(1);
@@ -241,15 +184,15 @@ static int load_weights(iris_cuda_flux_t *tf, wsrc_t *ws) {
                                                            tmp + (size_t)3 * H * H, F, H,
                                                            g_rt.stream), nm));
         snprintf(nm, sizeof(nm), "single_transformer_blocks.%d.attn.to_out.weight", i);
-        CHK(wsrc_get(ws, nm, (size_t)H * (H + F), b->w_out));
+        CHK(iris_wsrc_get(ws, nm, (size_t)H * (H + F), b->w_out));
         /* norm weights go through a temp slot that the next fused weight does not overwrite
            before the conversion kernel ran: same stream, so ordering is guaranteed */
         snprintf(nm, sizeof(nm), "single_transformer_blocks.%d.attn.norm_q.weight", i);
-        CHK(wsrc_get_f32(ws, nm, 128, b->qn, tmp));
+        CHK(iris_wsrc_get_f32(ws, nm, 128, b->qn, tmp));
         snprintf(nm, sizeof(nm), "single_transformer_blocks.%d.attn.norm_k.weight", i);
-        CHK(wsrc_get_f32(ws, nm, 128, b->kn, tmp + 128));
-        CHK(mk_tmap(&b->tm_fused, b->w_fused, 3 * H + 2 * F, H, H, 256));
-        CHK(mk_tmap(&b->tm_out, b->w_out, H, H + F, H + F, 256));
+        CHK(iris_wsrc_get_f32(ws, nm, 128, b->kn, tmp + 128));
+        CHK(iris_mk_tmap(&b->tm_fused, b->w_fused, 3 * H + 2 * F, H, H, 256));
+        CHK(iris_mk_tmap(&b->tm_out, b->w_out, H, H + F, H + F, 256));
     }
     tf->t_dev = (float *)iris_dmalloc(4 * 4);
     tf->sincos = (float *)iris_dmalloc(256 * 4);
@@ -350,7 +293,7 @@ iris_cuda_flux_t *iris_cuda_flux_load(const char *model_dir) {
     iris_cuda_flux_t *tf = flux_new(&cfg);
     if (!tf) return NULL;
     snprintf(tf->model_dir, sizeof(tf->model_dir), "%s", model_dir);
-    wsrc_t ws;
+    iris_wsrc_t ws;
     memset(&ws, 0, sizeof(ws));
     char tdir[1200];
     snprintf(tdir, sizeof(tdir), "%s/transformer", model_dir);
@@ -375,7 +318,7 @@ iris_cuda_flux_t *iris_cuda_flux_random(const iris_cuda_flux_config_t *cfg, uint
     tf->seed = seed;
     tf->std = std;
     tf->norm_unit = norm_unit;
-    wsrc_t ws;
+    iris_wsrc_t ws;
     memset(&ws, 0, sizeof(ws));
     ws.random = 1;
     ws.seed = seed;
@@ -398,10 +341,10 @@ int iris_cuda_flux_read_weight(iris_cuda_flux_t *tf, const char *name, uint16_t 
     if (tf->random) {
         uint16_t *d = (uint16_t *)iris_dmalloc(numel * 2);
         if (!d) return IRIS_CUDA_ERR_OOM;
-        wsrc_t ws;
+        iris_wsrc_t ws;
         memset(&ws, 0, sizeof(ws));
         ws.random = 1; ws.seed = tf->seed; ws.std = tf->std; ws.norm_unit = tf->norm_unit;
-        int rc = wsrc_get(&ws, name, numel, d);
+        int rc = iris_wsrc_get(&ws, name, numel, d);
         if (!rc) rc = iris_cuda_check(cudaMemcpyAsync(out, d, numel * 2, cudaMemcpyDeviceToHost,
                                                       g_rt.stream), "read weight");
         cudaStreamSynchronize(g_rt.stream);
@@ -509,11 +452,11 @@ static int plan_ensure(iris_cuda_flux_t *tf, int s_txt, int img_h, int img_w,
     PA(P->tok_img, (size_t)P->n_img_total * C * 2);
     PA(P->tok_txt, (size_t)s_txt * T * 2);
 #undef PA
-    if (mk_tmap(&P->tm_xmod, P->xmod, S, H, H, 128) || mk_tmap(&P->tm_attn, P->attn, S, H, H, 128) ||
-        mk_tmap(&P->tm_mlp, P->mlp, S, F, F, 128) ||
-        mk_tmap(&P->tm_cat, P->cat, S, H + F, H + F, 128) ||
-        mk_tmap(&P->tm_tok_img, P->tok_img, P->n_img_total, C, C, 128) ||
-        mk_tmap(&P->tm_tok_txt, P->tok_txt, s_txt, T, T, 128)) {
+    if (iris_mk_tmap(&P->tm_xmod, P->xmod, S, H, H, 128) || iris_mk_tmap(&P->tm_attn, P->attn, S, H, H, 128) ||
+        iris_mk_tmap(&P->tm_mlp, P->mlp, S, F, F, 128) ||
+        iris_mk_tmap(&P->tm_cat, P->cat, S, H + F, H + F, 128) ||
+        iris_mk_tmap(&P->tm_tok_img, P->tok_img, P->n_img_total, C, C, 128) ||
+        iris_mk_tmap(&P->tm_tok_txt, P->tok_txt, s_txt, T, T, 128)) {
         plan_free(P);
         return IRIS_CUDA_ERR_CUDA;
     }

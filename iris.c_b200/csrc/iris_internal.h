@@ -70,6 +70,24 @@ const st_tensor_t *st_find(const st_model_t *m, const char *name);
 int st_read_bf16(const st_model_t *m, const st_tensor_t *t, uint16_t *out, size_t numel);
 int st_read_f32(const st_model_t *m, const st_tensor_t *t, float *out, size_t numel);
 
+/* ---------------- weight sources (weights.c) ---------------- */
+typedef struct {
+    int random;           /* 1: seeded device RNG, 0: safetensors file       */
+    st_model_t st;
+    uint64_t seed;
+    float std;
+    int norm_unit;        /* norm-scale tensors drawn as 1 + N(0, 0.1)       */
+    uint16_t *host_stage;
+    size_t host_stage_n;
+} iris_wsrc_t;
+
+/* Write the reference-layout tensor `name` ([numel] bf16) to device memory. */
+int iris_wsrc_get(iris_wsrc_t *ws, const char *name, size_t numel, uint16_t *d_dst);
+/* f32 copy of a small tensor through a bf16 device temp. */
+int iris_wsrc_get_f32(iris_wsrc_t *ws, const char *name, size_t numel, float *d_dst, uint16_t *tmp);
+/* bf16 tensor map over a row-major [rows, cols] matrix (row stride ld), box {64, box} */
+int iris_mk_tmap(CUtensorMap *m, const void *p, int rows, int cols, int ld, int box);
+
 /* simple "key": number extraction from a small JSON text */
 int json_get_number(const char *json, const char *key, double *out);
 

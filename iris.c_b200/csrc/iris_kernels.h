@@ -127,6 +127,17 @@ cudaError_t iris_launch_gated_add_bf16(void *out, const void *gate, const void *
 cudaError_t iris_launch_rmsnorm(const float *x, int ldx, const float *w, float *out_f32,
                                 void *out_bf16, int ldout, int rows, int cols, float eps,
                                 const float *mul, cudaStream_t stream);
+/* Z-Image row kernels */
+cudaError_t iris_launch_resid_rmsnorm_gate(float *x, int ldx, const float *y, int ldy, const float *w,
+                                           const float *gate, int rows, int cols, float eps,
+                                           cudaStream_t stream);
+cudaError_t iris_launch_zi_mod_transform(float *m, int dim, long n, cudaStream_t stream);
+cudaError_t iris_launch_patchify(const float *lat, int c, int H, int W, int ps, void *out, int ldo,
+                                 cudaStream_t stream);
+cudaError_t iris_launch_unpatchify(const float *tok, int ldt, int c, int H, int W, int ps, float *lat,
+                                   cudaStream_t stream);
+cudaError_t iris_launch_fill_rows_f32(float *dst, int ld, const float *vec, int n, int cols,
+                                      cudaStream_t stream);
 /* [gate; up] (2F rows) -> 256-row blocks of [gate 128 | up 128] (GEMM SwiGLU layout) */
 cudaError_t iris_launch_interleave_gate_up(void *dst, const void *src, int F, int cols,
                                            cudaStream_t stream);

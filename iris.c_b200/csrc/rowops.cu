@@ -310,6 +310,69 @@ __global__ void interleave_gate_up_kernel(uint4* dst, const uint4* src, int F, i
     dst[(size_t)r * cols8 + c] = src[(size_t)sr * cols8 + c];
 }
 
+// ------------------------------------------------------------------ Z-Image
+// x[r] += gate * RMSNorm(y[r]) * w   (gate NULL = 1): the post-norm gated
+// residual of zi_block_forward (iris_transformer_zimage.c:831-835, :845-849).
+__global__ void __launch_bounds__(256)
+resid_rmsnorm_gate_kernel(float* __restrict__ x, int ldx, const float* __restrict__ y, int ldy,
+                          const float* __restrict__ w, const float* __restrict__ gate, int cols,
+                          float eps) {
+  __shared__ float red[8];
+  const int row = blockIdx.x;
+  const float* yr = y + (size_t)row * ldy;
+  float* xr = x + (size_t)row * ldx;
+  float s = 0.f;
+  for (int c = threadIdx.x; c < cols; c += 256) s += yr[c] * yr[c];
+  const float r = 1.0f / sqrtf(block_sum(s, red) / (float)cols + eps);
+  for (int c = threadIdx.x; c < cols; c += 256) {
+    float v = yr[c] * r * w[c];
+    xr[c] += gate ? gate[c] * v : v;
+  }
+}
+
+// per block of 4*dim modulation values: [1+scale_msa | tanh(gate_msa) | 1+scale_mlp | tanh(gate_mlp)]
+// (zi_block_forward :812-818)
+__global__ void zi_mod_transform_kernel(float* m, int dim, long n) {
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  long stride = (long)gridDim.x * blockDim.x;
+  for (; i < n; i += stride) {
+    int part = (int)((i / dim) & 3);
+    m[i] = (part & 1) ? tanhf(m[i]) : 1.0f + m[i];
+  }
+}
+
+// latent [C, H, W] f32 -> tokens [H/ps * W/ps, ps*ps*C] bf16 in (ph, pw, c) order (zi_patchify :1634)
+__global__ void patchify_kernel(const float* __restrict__ lat, int c, int H, int W, int ps,
+                                __nv_bfloat16* __restrict__ out, int ldo) {
+  const int wt = W / ps;
+  const int pf = ps * ps * c;
+  const int tok = blockIdx.x;
+  const int ty = tok / wt, tx = tok - ty * wt;
+  for (int j = threadIdx.x; j < pf; j += blockDim.x) {
+    int ch = j % c, pp = j / c, pw = pp % ps, ph = pp / ps;
+    out[(size_t)tok * ldo + j] = __float2bfloat16_rn(lat[((size_t)ch * H + ty * ps + ph) * W + tx * ps + pw]);
+  }
+}
+
+// tokens f32 [n, ldt] (first ps*ps*C columns) -> latent [C, H, W] (zi_unpatchify :1663)
+__global__ void unpatchify_kernel(const float* __restrict__ tok, int ldt, int c, int H, int W, int ps,
+                                  float* __restrict__ lat) {
+  const int wt = W / ps;
+  const int pf = ps * ps * c;
+  const int t = blockIdx.x;
+  const int ty = t / wt, tx = t - ty * wt;
+  for (int j = threadIdx.x; j < pf; j += blockDim.x) {
+    int ch = j % c, pp = j / c, pw = pp % ps, ph = pp / ps;
+    lat[((size_t)ch * H + ty * ps + ph) * W + tx * ps + pw] = tok[(size_t)t * ldt + j];
+  }
+}
+
+// rows [0, n) of dst (row stride ld) = vec [cols]
+__global__ void fill_rows_f32_kernel(float* dst, int ld, const float* __restrict__ vec, int n, int cols) {
+  for (int r = blockIdx.x; r < n; r += gridDim.x)
+    for (int c = threadIdx.x; c < cols; c += blockDim.x) dst[(size_t)r * ld + c] = vec[c];
+}
+
 inline int grid_for(long n, int threads) {
   long b = (n + threads - 1) / threads;
   if (b > 148 * 16) b = 148 * 16;
@@ -432,6 +495,43 @@ cudaError_t iris_launch_rmsnorm(const float* x, int ldx, const float* w, float* 
   if (rows <= 0) return cudaSuccess;
   rmsnorm_kernel<<<rows, 256, 0, stream>>>(x, ldx, w, out_f32, static_cast<__nv_bfloat16*>(out_bf16),
                                            ldout, cols, eps, mul);
+  return cudaGetLastError();
+}
+
+cudaError_t iris_launch_resid_rmsnorm_gate(float* x, int ldx, const float* y, int ldy, const float* w,
+                                           const float* gate, int rows, int cols, float eps,
+                                           cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  resid_rmsnorm_gate_kernel<<<rows, 256, 0, stream>>>(x, ldx, y, ldy, w, gate, cols, eps);
+  return cudaGetLastError();
+}
+
+cudaError_t iris_launch_zi_mod_transform(float* m, int dim, long n, cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  zi_mod_transform_kernel<<<grid_for(n, 256), 256, 0, stream>>>(m, dim, n);
+  return cudaGetLastError();
+}
+
+cudaError_t iris_launch_patchify(const float* lat, int c, int H, int W, int ps, void* out, int ldo,
+                                 cudaStream_t stream) {
+  int n = (H / ps) * (W / ps);
+  if (n <= 0) return cudaSuccess;
+  patchify_kernel<<<n, 128, 0, stream>>>(lat, c, H, W, ps, static_cast<__nv_bfloat16*>(out), ldo);
+  return cudaGetLastError();
+}
+
+cudaError_t iris_launch_unpatchify(const float* tok, int ldt, int c, int H, int W, int ps, float* lat,
+                                   cudaStream_t stream) {
+  int n = (H / ps) * (W / ps);
+  if (n <= 0) return cudaSuccess;
+  unpatchify_kernel<<<n, 128, 0, stream>>>(tok, ldt, c, H, W, ps, lat);
+  return cudaGetLastError();
+}
+
+cudaError_t iris_launch_fill_rows_f32(float* dst, int ld, const float* vec, int n, int cols,
+                                      cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  fill_rows_f32_kernel<<<n < 1024 ? n : 1024, 256, 0, stream>>>(dst, ld, vec, n, cols);
   return cudaGetLastError();
 }
 

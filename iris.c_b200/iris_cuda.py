@@ -39,6 +39,20 @@ class KernelTime(C.Structure):
     _fields_ = [("name", C.c_char * 32), ("flops", C.c_double), ("bytes", C.c_double), ("ms", C.c_float)]
 
 
+class ZImageConfig(C.Structure):
+    _fields_ = [("dim", C.c_int), ("heads", C.c_int), ("n_layers", C.c_int), ("n_refiner", C.c_int),
+                ("cap_feat_dim", C.c_int), ("in_channels", C.c_int), ("patch_size", C.c_int),
+                ("ffn_dim", C.c_int), ("adaln_dim", C.c_int), ("t_mid", C.c_int), ("rope_theta", C.c_float),
+                ("axes_dims", C.c_int * 3)]
+
+    @classmethod
+    def from_dict(cls, c: dict) -> "ZImageConfig":
+        return cls(dim=c["dim"], heads=c["dim"] // 128, n_layers=c["n_layers"], n_refiner=c["n_refiner"],
+                   cap_feat_dim=c["cap_feat_dim"], in_channels=c["in_channels"], patch_size=c["patch_size"],
+                   ffn_dim=c["ffn_dim"], adaln_dim=min(c["dim"], 256), t_mid=c["t_mid"],
+                   rope_theta=float(c["rope_theta"]), axes_dims=(C.c_int * 3)(*c["axes_dims"]))
+
+
 class Ref(C.Structure):
     _fields_ = [("latent", _fp), ("h", C.c_int), ("w", C.c_int), ("t_offset", C.c_int)]
 
@@ -86,6 +100,17 @@ SIGNATURES = {
                                                             _fp, C.c_int, _fp, C.c_int, PROGRESS_CB]),
     "iris_cuda_sample_euler_dev": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p,
                                              C.c_int, C.c_void_p, C.c_int, C.c_float, _fp, C.c_int]),
+    "iris_cuda_zimage_load": (C.c_void_p, [C.c_char_p]),
+    "iris_cuda_zimage_random": (C.c_void_p, [C.POINTER(ZImageConfig), C.c_uint64, C.c_float, C.c_int]),
+    "iris_cuda_zimage_free": (None, [C.c_void_p]),
+    "iris_cuda_zimage_get_config": (C.c_int, [C.c_void_p, C.POINTER(ZImageConfig)]),
+    "iris_cuda_zimage_weight_bytes": (C.c_size_t, [C.c_void_p]),
+    "iris_cuda_zi_transformer_forward": (C.c_void_p, [C.c_void_p, _fp, C.c_int, C.c_int, C.c_float, _fp,
+                                                      C.c_int]),
+    "iris_cuda_sample_euler_zimage": (C.c_void_p, [C.c_void_p, _fp, C.c_int, C.c_int, C.c_int, C.c_int,
+                                                   C.c_int, _fp, C.c_int, _fp, C.c_int, PROGRESS_CB]),
+    "iris_cuda_sample_euler_zimage_dev": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p,
+                                                    C.c_int, _fp, C.c_int]),
     # iris_gpu_* surface (iris_metal.h names)
     "iris_gpu_tensor_create": (C.c_void_p, [_fp, C.c_size_t]),
     "iris_gpu_tensor_alloc": (C.c_void_p, [C.c_size_t]),
@@ -281,3 +306,50 @@ def zimage_schedule(steps: int, seq: int) -> np.ndarray:
 
 def init_noise(c: int, h: int, w: int, seed: int) -> np.ndarray:
     return _take_floats(lib().iris_cuda_init_noise(1, c, h, w, seed), c * h * w, (c, h, w))
+
+
+class ZImage:
+    """Resident Z-Image S3-DiT transformer (libiris_cuda)."""
+
+    def __init__(self, handle):
+        if not handle:
+            raise IrisCudaError(last_error() or "model creation failed")
+        self.h = handle
+        cfg = ZImageConfig()
+        lib().iris_cuda_zimage_get_config(self.h, C.byref(cfg))
+        self.cfg = cfg
+
+    @classmethod
+    def load(cls, model_dir: str) -> "ZImage":
+        return cls(lib().iris_cuda_zimage_load(model_dir.encode()))
+
+    @classmethod
+    def random(cls, cfg: ZImageConfig, seed: int, std: float = 0.02, norm_unit: bool = False) -> "ZImage":
+        return cls(lib().iris_cuda_zimage_random(C.byref(cfg), seed, std, int(norm_unit)))
+
+    def close(self):
+        if self.h:
+            lib().iris_cuda_zimage_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def forward(self, latent: np.ndarray, cap: np.ndarray, t: float) -> np.ndarray:
+        lat = np.ascontiguousarray(latent, np.float32)
+        cp = np.ascontiguousarray(cap, np.float32)
+        c, h, w = lat.shape
+        p = lib().iris_cuda_zi_transformer_forward(self.h, _f(lat), h, w, t, _f(cp), cp.shape[0])
+        return _take_floats(p, c * h * w, (c, h, w))
+
+    def sample_euler(self, z: np.ndarray, cap: np.ndarray, schedule) -> np.ndarray:
+        zz = np.ascontiguousarray(z, np.float32)
+        cp = np.ascontiguousarray(cap, np.float32)
+        sc = np.ascontiguousarray(schedule, np.float32)
+        c, h, w = zz.shape
+        p = lib().iris_cuda_sample_euler_zimage(self.h, _f(zz), 1, c, h, w, self.cfg.patch_size, _f(cp),
+                                                cp.shape[0], _f(sc), len(sc) - 1, PROGRESS_CB(0))
+        return _take_floats(p, c * h * w, (c, h, w))
