@@ -64,6 +64,10 @@ def parse_args(argv=None):
                     help="profiling case: a Klein-4B-shaped model truncated to DOUBLE + SINGLE blocks "
                          "(same kernels and shapes, less memory); not a benchmark number")
     ap.add_argument("--profile-out", default=None, help="write the per-kernel CUDA-event profile (JSON)")
+    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "c5b"],
+                    help="c2 (default) is the benchmark; the others measure the remaining SURVEY configs "
+                         "on one GPU (c1 K4B 64x64 single forward, c3 K4B 1024x1024 CFG 4.0, c4 K9B "
+                         "1792x1792, c5 Z-Image 1024x1024, c5b K4B + 2 references)")
     return ap.parse_args(argv)
 
 
@@ -426,10 +430,141 @@ def run_ours(args):
     return 0
 
 
+K9B = dict(K4B, num_attention_heads=32, num_layers=8, num_single_layers=24, joint_attention_dim=12288)
+ZIMAGE_6B = dict(dim=3840, n_layers=30, n_refiner=2, cap_feat_dim=2560, in_channels=16, patch_size=2,
+                 rope_theta=256.0, axes_dims=[32, 48, 48], ffn_dim=10240, t_mid=1024)
+
+
+def zimage_step_flops(cfg, n_img_tokens, n_cap):
+    """Algorithmic FLOPs of one Z-Image forward (linears + attention), padded rows included."""
+    D, F = cfg["dim"], cfg["ffn_dim"]
+    ni = -(-n_img_tokens // 32) * 32
+    nc = -(-n_cap // 32) * 32
+
+    def blk(s):
+        return 2.0 * s * (4 * D * D + 3 * D * F) + 4.0 * s * s * D
+    return (cfg["n_refiner"] * (blk(ni) + blk(nc)) + cfg["n_layers"] * blk(ni + nc)
+            + 2.0 * ni * D * 64 + 2.0 * nc * D * cfg["cap_feat_dim"] + 2.0 * n_img_tokens * D * 64)
+
+
+def run_config(args):
+    """One-GPU measurement of the non-headline configs (device-timed, inputs resident)."""
+    import ctypes as C
+
+    import torch
+
+    import iris_cuda
+    lib = iris_cuda.lib()
+    assert lib.iris_cuda_init(0) == 0, iris_cuda.last_error()
+    dev = torch.device("cuda", 0)
+    stream = torch.cuda.ExternalStream(lib.iris_cuda_stream(), device=dev)
+    rng = np.random.default_rng(7)
+    peaks, peak_src = load_peaks()
+    fp = C.POINTER(C.c_float)
+    out = {"impl": "ours", "config_name": args.config, "steps": args.steps, "warmup": args.warmup}
+
+    def timed(fn, n):
+        torch.cuda.synchronize()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        l0 = lib.iris_cuda_kernel_launches()
+        e0.record(stream)
+        for i in range(n):
+            fn(i)
+        e1.record(stream)
+        e1.synchronize()
+        return e0.elapsed_time(e1), lib.iris_cuda_kernel_launches() - l0
+
+    if args.config in ("c1", "c3", "c4", "c5b"):
+        mcfg = K9B if args.config == "c4" else K4B
+        model = iris_cuda.Flux.random(iris_cuda.FluxConfig.from_hf(mcfg), seed=WEIGHT_SEED, std=0.02)
+        lat_hw = {"c1": 4, "c3": 64, "c4": 112, "c5b": 32}[args.config]
+        ntxt = 64 if args.config == "c1" else 512
+        txt = rng.standard_normal((ntxt, mcfg["joint_attention_dim"])).astype(np.float32)
+        z0 = iris_cuda.init_noise(128, lat_hw, lat_hw, 42)
+        txt_d = torch.from_numpy(txt).to(dev)
+        z_d = torch.from_numpy(z0).to(dev)
+        refs = [iris_cuda.init_noise(128, 32, 32, 100 + r) for r in range(2)] if args.config == "c5b" else ()
+        model.forward(z0, txt, 1.0, refs=refs)  # plan + graph
+        prof = model.profile(1.0)
+        fwd_flops = sum(e["flops"] for e in prof if e["name"] != "mods")
+        if args.config == "c1":
+            o_d = torch.empty_like(z_d)
+            rc_fn = lambda i: lib.iris_cuda_flux_forward_dev(model.h, z_d.data_ptr(), lat_hw, lat_hw, None, 0,
+                                                              txt_d.data_ptr(), ntxt, 1.0, o_d.data_ptr())
+            for i in range(args.warmup):
+                rc_fn(i)
+            ms, launches = timed(rc_fn, args.steps)
+            per = ms / args.steps
+            wb = model.weight_bytes()
+            out.update(metric="transformer forwards/s (Klein-4B 64x64, 16 img + 64 txt tokens, t=1.0)",
+                       value=1000.0 / per, unit="forwards/s", ms_per_step=per, gpu_launches=int(launches),
+                       roofline={"bound": "hbm", "achieved": wb / (per / 1000.0) / 1e9, "peak": peaks["hbm_gbs"],
+                                 "unit": "GB/s", "frac": wb / (per / 1000.0) / 1e9 / peaks["hbm_gbs"],
+                                 "algorithmic_bytes": wb, "peak_source": peak_src})
+        else:
+            n_steps = {"c3": 50, "c4": 4, "c5b": 4}[args.config]
+            sched = np.ascontiguousarray(iris_cuda.official_schedule(n_steps, lat_hw * lat_hw), np.float32)
+            k = min(args.steps, n_steps)
+            if args.config == "c3":
+                txt_u = torch.from_numpy(rng.standard_normal(txt.shape).astype(np.float32)).to(dev)
+                run = lambda i: lib.iris_cuda_sample_euler_dev(model.h, z_d.data_ptr(), lat_hw, lat_hw,
+                                                                txt_d.data_ptr(), ntxt, txt_u.data_ptr(), ntxt,
+                                                                4.0, sched.ctypes.data_as(fp), k)
+                fwd_per_step = 2
+            elif args.config == "c5b":
+                run = lambda i: model.sample_euler(z0, txt, sched[:k + 1], refs=refs)
+                fwd_per_step = 1
+            else:
+                run = lambda i: lib.iris_cuda_sample_euler_dev(model.h, z_d.data_ptr(), lat_hw, lat_hw,
+                                                                txt_d.data_ptr(), ntxt, None, 0, 1.0,
+                                                                sched.ctypes.data_as(fp), k)
+                fwd_per_step = 1
+            run(0)
+            ms, launches = timed(run, 1)
+            per = ms / k
+            tflops = fwd_per_step * fwd_flops / (per / 1000.0) / 1e12
+            out.update(metric=f"denoise steps/s ({args.config})", value=1000.0 / per, unit="steps/s",
+                       ms_per_step=per, timed_steps=k, gpu_launches=int(launches),
+                       tflop_per_step=fwd_per_step * fwd_flops / 1e12,
+                       roofline={"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops"],
+                                 "unit": "TFLOP/s", "frac": tflops / peaks["bf16_tflops"], "peak_source": peak_src},
+                       note="c5b timed through the host API (refs re-uploaded per call)" if args.config == "c5b"
+                       else None)
+        model.close()
+    else:  # c5 Z-Image 1024x1024
+        zc = dict(ZIMAGE_6B)
+        model = iris_cuda.ZImage.random(iris_cuda.ZImageConfig.from_dict(zc), seed=WEIGHT_SEED, std=0.02)
+        cap = rng.standard_normal((256, zc["cap_feat_dim"])).astype(np.float32)
+        z0 = rng.standard_normal((16, 128, 128)).astype(np.float32)
+        cap_d = torch.from_numpy(cap).to(dev)
+        z_d = torch.from_numpy(z0).to(dev)
+        n_steps = 8
+        sched = np.ascontiguousarray(iris_cuda.zimage_schedule(n_steps, 4096), np.float32)
+        k = min(args.steps, n_steps)
+        run = lambda i: lib.iris_cuda_sample_euler_zimage_dev(model.h, z_d.data_ptr(), 128, 128, cap_d.data_ptr(),
+                                                               256, sched.ctypes.data_as(fp), k)
+        run(0)
+        ms, launches = timed(run, 1)
+        per = ms / k
+        fl = zimage_step_flops(zc, 4096, 256)
+        tflops = fl / (per / 1000.0) / 1e12
+        out.update(metric="denoise steps/s (Z-Image 6B 1024x1024, 4096 img + 256 caption tokens)",
+                   value=1000.0 / per, unit="steps/s", ms_per_step=per, timed_steps=k, gpu_launches=int(launches),
+                   tflop_per_step=fl / 1e12, weight_gb=model.weight_bytes() / 1e9 if hasattr(model, "weight_bytes")
+                   else None,
+                   roofline={"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                             "frac": tflops / peaks["bf16_tflops"], "peak_source": peak_src})
+        model.close()
+    print(json.dumps(out), flush=True)
+    return 0
+
+
 def main(argv=None):
     args = parse_args(argv)
     if args.impl == "reference":
         return run_reference(args)
+    if args.config != "c2":
+        return run_config(args)
     return run_ours(args)
 
 
