@@ -92,6 +92,16 @@ def dist_init(world, backend="nccl", device=None):
     return dist
 
 
+def reduce_sum(value: float, world: int, device=None) -> float:
+    if world <= 1:
+        return value
+    import torch
+    import torch.distributed as dist
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
 def reduce_max(value: float, world: int, device=None) -> float:
     """Max of a per-rank float over all ranks (the timing rule)."""
     if world <= 1:
@@ -448,23 +458,47 @@ def zimage_step_flops(cfg, n_img_tokens, n_cap):
 
 
 def run_config(args):
-    """One-GPU measurement of the non-headline configs (device-timed, inputs resident)."""
+    """Measurement of the non-headline configs (device-timed, inputs resident).
+
+    At N > 1 GPUs: c3 splits the CFG branches over rank pairs (N/2 images at a
+    time, weak scaling), c4 runs one image tensor-parallel over all N ranks
+    (strong scaling); the other configs run N seed replicas."""
     import ctypes as C
 
     import torch
 
     import iris_cuda
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = dist_init(world, "nccl", dev)
     lib = iris_cuda.lib()
-    assert lib.iris_cuda_init(0) == 0, iris_cuda.last_error()
-    dev = torch.device("cuda", 0)
+    assert lib.iris_cuda_init(local) == 0, iris_cuda.last_error()
     stream = torch.cuda.ExternalStream(lib.iris_cuda_stream(), device=dev)
     rng = np.random.default_rng(7)
     peaks, peak_src = load_peaks()
     fp = C.POINTER(C.c_float)
-    out = {"impl": "ours", "config_name": args.config, "steps": args.steps, "warmup": args.warmup}
+    out = {"impl": "ours", "config_name": args.config, "steps": args.steps, "warmup": args.warmup,
+           "n_gpus": world}
+    mode = "replicas"
+    if world > 1 and args.config in ("c3", "c4"):
+        def exchange(obj):
+            lst = [None] * world
+            dist.all_gather_object(lst, obj)
+            return lst
+        mode = "cfg_pair" if args.config == "c3" else "tp"
+        if mode == "cfg_pair" and world % 2:
+            raise SystemExit("c3 at N > 1 needs an even number of GPUs (CFG pairs)")
+        iris_cuda.comm_init_group(exchange, rank, world, 2 if mode == "cfg_pair" else world)
+    units = {"replicas": world, "cfg_pair": world // 2, "tp": 1}[mode]
+    out["parallelism"] = {"replicas": f"seed-replicas x{world}", "cfg_pair": f"cfg-pairs x{world // 2}",
+                          "tp": f"tp{world}"}[mode]
+    out["scaling"] = "strong" if mode == "tp" else "weak"
 
     def timed(fn, n):
         torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
         l0 = lib.iris_cuda_kernel_launches()
         e0.record(stream)
@@ -472,21 +506,32 @@ def run_config(args):
             fn(i)
         e1.record(stream)
         e1.synchronize()
-        return e0.elapsed_time(e1), lib.iris_cuda_kernel_launches() - l0
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        return reduce_max(e0.elapsed_time(e1), world, dev), lib.iris_cuda_kernel_launches() - l0
 
     if args.config in ("c1", "c3", "c4", "c5b"):
         mcfg = K9B if args.config == "c4" else K4B
-        model = iris_cuda.Flux.random(iris_cuda.FluxConfig.from_hf(mcfg), seed=WEIGHT_SEED, std=0.02)
+        if mode == "tp":
+            model = iris_cuda.Flux.random(iris_cuda.FluxConfig.from_hf(mcfg), seed=WEIGHT_SEED, std=0.02,
+                                          tp_rank=rank, tp_size=world)
+        else:
+            model = iris_cuda.Flux.random(iris_cuda.FluxConfig.from_hf(mcfg), seed=WEIGHT_SEED, std=0.02)
         lat_hw = {"c1": 4, "c3": 64, "c4": 112, "c5b": 32}[args.config]
         ntxt = 64 if args.config == "c1" else 512
         txt = rng.standard_normal((ntxt, mcfg["joint_attention_dim"])).astype(np.float32)
-        z0 = iris_cuda.init_noise(128, lat_hw, lat_hw, 42)
+        z0 = iris_cuda.init_noise(128, lat_hw, lat_hw, 42 + (rank // 2 if mode == "cfg_pair" else
+                                                            0 if mode == "tp" else rank))
         txt_d = torch.from_numpy(txt).to(dev)
         z_d = torch.from_numpy(z0).to(dev)
         refs = [iris_cuda.init_noise(128, 32, 32, 100 + r) for r in range(2)] if args.config == "c5b" else ()
         model.forward(z0, txt, 1.0, refs=refs)  # plan + graph
         prof = model.profile(1.0)
+        # a shard's profile counts its own heads / MLP columns: scale to the whole model
         fwd_flops = sum(e["flops"] for e in prof if e["name"] != "mods")
+        if mode == "tp":
+            fwd_flops = reduce_sum(fwd_flops, world, dev)
         if args.config == "c1":
             o_d = torch.empty_like(z_d)
             rc_fn = lambda i: lib.iris_cuda_flux_forward_dev(model.h, z_d.data_ptr(), lat_hw, lat_hw, None, 0,
@@ -497,7 +542,7 @@ def run_config(args):
             per = ms / args.steps
             wb = model.weight_bytes()
             out.update(metric="transformer forwards/s (Klein-4B 64x64, 16 img + 64 txt tokens, t=1.0)",
-                       value=1000.0 / per, unit="forwards/s", ms_per_step=per, gpu_launches=int(launches),
+                       value=units * 1000.0 / per, unit="forwards/s", ms_per_step=per, gpu_launches=int(launches),
                        roofline={"bound": "hbm", "achieved": wb / (per / 1000.0) / 1e9, "peak": peaks["hbm_gbs"],
                                  "unit": "GB/s", "frac": wb / (per / 1000.0) / 1e9 / peaks["hbm_gbs"],
                                  "algorithmic_bytes": wb, "peak_source": peak_src})
@@ -505,7 +550,13 @@ def run_config(args):
             n_steps = {"c3": 50, "c4": 4, "c5b": 4}[args.config]
             sched = np.ascontiguousarray(iris_cuda.official_schedule(n_steps, lat_hw * lat_hw), np.float32)
             k = min(args.steps, n_steps)
-            if args.config == "c3":
+            if args.config == "c3" and mode == "cfg_pair":
+                txt_u = torch.from_numpy(rng.standard_normal(txt.shape).astype(np.float32)).to(dev)
+                run = lambda i: lib.iris_cuda_sample_euler_cfg_pair_dev(model.h, z_d.data_ptr(), lat_hw, lat_hw,
+                                                                         txt_d.data_ptr(), txt_u.data_ptr(), ntxt,
+                                                                         4.0, sched.ctypes.data_as(fp), k)
+                fwd_per_step = 2
+            elif args.config == "c3":
                 txt_u = torch.from_numpy(rng.standard_normal(txt.shape).astype(np.float32)).to(dev)
                 run = lambda i: lib.iris_cuda_sample_euler_dev(model.h, z_d.data_ptr(), lat_hw, lat_hw,
                                                                 txt_d.data_ptr(), ntxt, txt_u.data_ptr(), ntxt,
@@ -522,12 +573,13 @@ def run_config(args):
             run(0)
             ms, launches = timed(run, 1)
             per = ms / k
-            tflops = fwd_per_step * fwd_flops / (per / 1000.0) / 1e12
-            out.update(metric=f"denoise steps/s ({args.config})", value=1000.0 / per, unit="steps/s",
+            tflops = units * fwd_per_step * fwd_flops / (per / 1000.0) / 1e12
+            out.update(metric=f"denoise steps/s ({args.config})", value=units * 1000.0 / per, unit="steps/s",
                        ms_per_step=per, timed_steps=k, gpu_launches=int(launches),
                        tflop_per_step=fwd_per_step * fwd_flops / 1e12,
-                       roofline={"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops"],
-                                 "unit": "TFLOP/s", "frac": tflops / peaks["bf16_tflops"], "peak_source": peak_src},
+                       roofline={"bound": "tensor", "achieved": tflops, "peak": world * peaks["bf16_tflops"],
+                                 "unit": "TFLOP/s", "frac": tflops / (world * peaks["bf16_tflops"]),
+                                 "peak_source": peak_src},
                        note="c5b timed through the host API (refs re-uploaded per call)" if args.config == "c5b"
                        else None)
         model.close()
@@ -547,15 +599,21 @@ def run_config(args):
         ms, launches = timed(run, 1)
         per = ms / k
         fl = zimage_step_flops(zc, 4096, 256)
-        tflops = fl / (per / 1000.0) / 1e12
+        tflops = units * fl / (per / 1000.0) / 1e12
         out.update(metric="denoise steps/s (Z-Image 6B 1024x1024, 4096 img + 256 caption tokens)",
-                   value=1000.0 / per, unit="steps/s", ms_per_step=per, timed_steps=k, gpu_launches=int(launches),
+                   value=units * 1000.0 / per, unit="steps/s", ms_per_step=per, timed_steps=k, gpu_launches=int(launches),
                    tflop_per_step=fl / 1e12, weight_gb=model.weight_bytes() / 1e9 if hasattr(model, "weight_bytes")
                    else None,
-                   roofline={"bound": "tensor", "achieved": tflops, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
-                             "frac": tflops / peaks["bf16_tflops"], "peak_source": peak_src})
+                   roofline={"bound": "tensor", "achieved": tflops, "peak": world * peaks["bf16_tflops"],
+                             "unit": "TFLOP/s", "frac": tflops / (world * peaks["bf16_tflops"]),
+                             "peak_source": peak_src})
         model.close()
-    print(json.dumps(out), flush=True)
+    if rank == 0:
+        print(json.dumps(out), flush=True)
+    iris_cuda.comm_destroy()
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
     return 0
 
 

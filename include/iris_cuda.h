@@ -101,6 +101,18 @@ iris_cuda_flux_t *iris_cuda_flux_load(const char *model_dir);
  * draws the QK-norm scales as 1 + N(0, 0.1) instead. */
 iris_cuda_flux_t *iris_cuda_flux_random(const iris_cuda_flux_config_t *cfg, uint64_t seed,
                                         float std, int norm_unit);
+/* Tensor-parallel shard tp_rank of tp_size (no reference counterpart; the
+ * reference runs on one device).  The shard holds heads
+ * [r*heads/tp, (r+1)*heads/tp) and MLP columns [r*mlp/tp, (r+1)*mlp/tp) of
+ * every block (heads % (2*tp) == 0 and mlp % (128*tp) == 0 required); the
+ * embedders, modulation and final layer are replicated.  Its forwards and
+ * samplers need a communicator of size tp_size in which this process has rank
+ * tp_rank (iris_cuda_comm_init); they all-reduce the hidden state after every
+ * attention/MLP output projection and return the full result on every rank.
+ * tp_size 1 is the same as iris_cuda_flux_load / iris_cuda_flux_random. */
+iris_cuda_flux_t *iris_cuda_flux_load_tp(const char *model_dir, int tp_rank, int tp_size);
+iris_cuda_flux_t *iris_cuda_flux_random_tp(const iris_cuda_flux_config_t *cfg, uint64_t seed,
+                                           float std, int norm_unit, int tp_rank, int tp_size);
 /* Replaces iris_transformer_free (iris_transformer_flux.c:4973). */
 void iris_cuda_flux_free(iris_cuda_flux_t *tf);
 int iris_cuda_flux_get_config(const iris_cuda_flux_t *tf, iris_cuda_flux_config_t *out);
@@ -194,6 +206,39 @@ int iris_cuda_sample_euler_dev(iris_cuda_flux_t *tf, float *d_z, int h, int w,
                                const float *d_txt, int txt_seq, const float *d_txt_uncond,
                                int txt_seq_uncond, float guidance, const float *schedule,
                                int num_steps);
+
+/* ------------------------------------------------------------------ 2b2. multi-GPU
+ * One NCCL communicator per process (no reference counterpart: the reference
+ * is single-device).  NCCL is loaded at first use (dlopen "libnccl.so.2").
+ * Every host wait that depends on peers is bounded (env IRIS_COMM_TIMEOUT_MS,
+ * default 60000): a peer that never joins or dies yields
+ * IRIS_CUDA_ERR_TIMEOUT and the communicator is aborted. */
+#define IRIS_CUDA_COMM_ID_BYTES 128
+/* Fill id_out (>= IRIS_CUDA_COMM_ID_BYTES) with a new unique id; one rank
+ * creates it and hands it to the others. */
+int iris_cuda_comm_unique_id(void *id_out, size_t id_bytes);
+/* Join the communicator `id` as rank `rank` of `world` (collective). */
+int iris_cuda_comm_init(const void *id, int world, int rank);
+void iris_cuda_comm_destroy(void);
+int iris_cuda_comm_world(void); /* 1 without a communicator */
+int iris_cuda_comm_rank(void);
+
+/* Classifier-free guidance with the two branches on a 2-rank communicator:
+ * rank 0 runs the unconditional forward, rank 1 the conditional one; after
+ * every step the pair all-gathers the velocities and both apply the guided
+ * Euler update, so both return the same latent as iris_cuda_sample_euler_cfg
+ * on one GPU.  Both ranks pass both contexts.  Arguments as
+ * iris_cuda_sample_euler_cfg / iris_cuda_sample_euler_dev. */
+float *iris_cuda_sample_euler_cfg_pair(iris_cuda_flux_t *tf, const float *z, int batch,
+                                       int channels, int h, int w, const float *text_emb_cond,
+                                       int text_seq_cond, const float *text_emb_uncond,
+                                       int text_seq_uncond, float guidance_scale,
+                                       const float *schedule, int num_steps,
+                                       void (*progress_callback)(int step, int total));
+int iris_cuda_sample_euler_cfg_pair_dev(iris_cuda_flux_t *tf, float *d_z, int h, int w,
+                                        const float *d_txt_cond, const float *d_txt_uncond,
+                                        int txt_seq, float guidance, const float *schedule,
+                                        int num_steps);
 
 /* ------------------------------------------------------------------ 2c. Z-Image S3-DiT */
 typedef struct iris_cuda_zimage iris_cuda_zimage_t;

@@ -14,10 +14,14 @@
 //                 O  += P_{j-1} V_{j-1} -> TMEM columns [256, 384)         (f32)
 //               S_{j+1} is computed while the softmax warps work on S_j.
 //   warps 2..5  softmax: thread = query row (TMEM lane), so row max and row
-//               sum need no shuffles; P_j (bf16) goes to a 128B-swizzled
-//               shared tile that is the A operand of the P.V MMA; the running
-//               max correction of O is applied in TMEM (tcgen05.ld / st) when
-//               a row's max grows.  Epilogue: O / l -> bf16 -> global.
+//               sum need no shuffles; P_j (bf16) goes to one of two
+//               128B-swizzled shared tiles (A operand of the P.V MMA), so the
+//               softmax of tile j overlaps P_{j-1} V_{j-1} and S_{j+1}.
+//               Lazy rescaling: a row keeps its reference max until a tile's
+//               max exceeds it by more than 2^8, so the O correction in TMEM
+//               (tcgen05.ld / st, after P_{j-1} V_{j-1} is done) is rare; O
+//               and l always share the same reference, so the result is
+//               exact.  Epilogue: O / l -> bf16 -> global.
 // V is consumed as an MN-major B operand straight from its [keys, d] layout.
 // Every wait is bounded (see ptx.cuh).
 #include "iris_kernels.h"
@@ -39,9 +43,10 @@ constexpr int TILE = 2 * BOX;       // 128 x 128 bf16 tile
 constexpr int OFF_Q = 0;
 constexpr int OFF_K = TILE;          // 2 stages
 constexpr int OFF_V = 3 * TILE;      // 2 stages
-constexpr int OFF_P = 5 * TILE;
-constexpr int OFF_BAR = 6 * TILE;
-constexpr int SMEM_BYTES = 6 * TILE + 256 + 1024;
+constexpr int OFF_P = 5 * TILE;      // 2 buffers
+constexpr int OFF_BAR = 7 * TILE;
+constexpr int SMEM_BYTES = 7 * TILE + 256 + 1024;
+constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P values stay <= 256
 constexpr int NUM_THREADS = 192;
 constexpr int TMEM_COLS = 512;
 constexpr float LOG2E = 1.4426950408889634f;
@@ -57,7 +62,7 @@ struct AttnBars {
   uint64_t v_full[2], v_empty[2];
   uint64_t s_full[2];
   uint64_t p_full;
-  uint64_t pv_done;
+  uint64_t pv_done[2];  // P_j V_j done, by P buffer j & 1
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -102,7 +107,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
       iris::mbar_init(&bars->s_full[s], 1);
     }
     iris::mbar_init(&bars->p_full, 128);
-    iris::mbar_init(&bars->pv_done, 1);
+    iris::mbar_init(&bars->pv_done[0], 1);
+    iris::mbar_init(&bars->pv_done[1], 1);
     iris::mbar_init(&bars->drain, 1);
     bars->abort = 0;
     iris::fence_mbar_init();
@@ -192,17 +198,18 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
         }
         iris::tc_fence_after();
         const uint32_t vb = iris::smem_u32(smem + OFF_V + s * TILE);
+        const uint32_t pb = pa + (uint32_t)(s * TILE);
 #pragma unroll
         for (int kk = 0; kk < BKV / 16; kk++) {
           // A: P rows, 16 keys = 32 bytes inside a 64-key swizzle box
-          uint64_t adesc = iris::umma_desc_k_sw128(pa + (uint32_t)((kk >> 2) * BOX + (kk & 3) * 32));
+          uint64_t adesc = iris::umma_desc_k_sw128(pb + (uint32_t)((kk >> 2) * BOX + (kk & 3) * 32));
           // B: V [keys, d] MN-major; 16 keys = 2 atoms of 8 rows (2048 B);
           // the two 64-wide d chunks are BOX apart, 8-key groups 1024 B apart
           uint64_t bdesc = iris::umma_desc_mn_sw128(vb + (uint32_t)(kk * 2048), BOX, 1024);
           iris::umma_bf16(tmem + 256, adesc, bdesc, idesc_o, (jj > 0 || kk > 0));
         }
         iris::umma_commit(&bars->v_empty[s]);
-        iris::umma_commit(&bars->pv_done);
+        iris::umma_commit(&bars->pv_done[s]);
       }
     }
     if (!ok) {
@@ -215,11 +222,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // query row within the tile = TMEM lane
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    uint8_t* prow = smem + OFF_P + r * 128;
-    float m = -INFINITY, l = 0.f;
+    float m = -INFINITY, l = 0.f;  // reference max (scaled, log2 units) and row sum
     bool ok = true;
-    for (int j = 0; j < n; j++) {
-      int b = j & 1;
+    for (int j = 0; j < n && ok; j++) {
+      const int b = j & 1;
       if (!iris::mbar_wait(&bars->s_full[b], (uint32_t)((j >> 1) & 1), abort_flag, p.status,
                            IRIS_DEV_ERR_ATTN_SOFTMAX)) {
         ok = false;
@@ -227,16 +233,16 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
       }
       iris::tc_fence_after();
       float s[BKV];
-#pragma unroll
-      for (int c = 0; c < 4; c++) iris::tmem_ld32(tmem + b * 128 + lane_off + 32 * c, s + 32 * c);
+      iris::tmem_ld64(tmem + b * 128 + lane_off, s);
+      iris::tmem_ld64(tmem + b * 128 + lane_off + 64, s + 64);
       const int kbase = j * BKV;
-      float tmax = -INFINITY;
+      // full tiles stay raw (scale folded into the exponent's FMA); ragged or
+      // masked tiles are scaled here so that padding can be set in log2 units
+      float sc = p.scale_log2, tmax = -INFINITY;
       if (kbase + BKV <= p.sk && !p.kmask) {
 #pragma unroll
-        for (int i = 0; i < BKV; i++) {
-          s[i] *= p.scale_log2;
-          tmax = fmaxf(tmax, s[i]);
-        }
+        for (int i = 0; i < BKV; i++) tmax = fmaxf(tmax, s[i]);
+        tmax *= sc;
       } else {
 #pragma unroll
         for (int i = 0; i < BKV; i++) {
@@ -247,20 +253,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
           s[i] = v;
           tmax = fmaxf(tmax, v);
         }
+        sc = 1.0f;
       }
-      const float m_new = fmaxf(m, tmax);
-      // P_{j-1} must be consumed and O final for tile j-1 before P and O change
-      if (j > 0) {
-        if (!iris::mbar_wait(&bars->pv_done, (uint32_t)((j - 1) & 1), abort_flag, p.status,
+      const bool grow = tmax > m + RESCALE_THRESHOLD;
+      const float m_new = grow ? tmax : m;
+      const float alpha = (grow && m != -INFINITY) ? iris::ex2_approx(m - m_new) : (grow ? 0.f : 1.f);
+      // O holds P_0..P_{j-1} V: correct it once P_{j-1} V_{j-1} is in (warp-uniform:
+      // tcgen05.ld / st are collective)
+      if (j > 0 && __any_sync(0xffffffffu, grow)) {
+        if (!iris::mbar_wait(&bars->pv_done[(j - 1) & 1], (uint32_t)(((j - 1) >> 1) & 1), abort_flag, p.status,
                              IRIS_DEV_ERR_ATTN_SOFTMAX)) {
           ok = false;
           break;
         }
         iris::tc_fence_after();
-      }
-      const float alpha = (m == -INFINITY) ? 0.f : exp2f(m - m_new);
-      // rescale this row of O in TMEM (warp-uniform: tcgen05.ld/st are collective)
-      if (j > 0 && __any_sync(0xffffffffu, alpha != 1.0f)) {
 #pragma unroll 1
         for (int c = 0; c < 4; c++) {
           float o[32];
@@ -271,14 +277,21 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
         }
       }
       m = m_new;
-      const float msub = (m == -INFINITY) ? 0.f : m;
+      const float nm = (m == -INFINITY) ? 0.f : -m;
+      // P buffer b was last read by P_{j-2} V_{j-2}
+      if (j >= 2 && !iris::mbar_wait(&bars->pv_done[b], (uint32_t)(((j - 2) >> 1) & 1), abort_flag, p.status,
+                                     IRIS_DEV_ERR_ATTN_SOFTMAX)) {
+        ok = false;
+        break;
+      }
+      uint8_t* prow = smem + OFF_P + b * TILE + r * 128;
       float rs = 0.f;
 #pragma unroll
       for (int c16 = 0; c16 < 16; c16++) {  // 8 keys = one 16-byte chunk
         float e[8];
 #pragma unroll
         for (int t = 0; t < 8; t++) {
-          e[t] = exp2f(s[c16 * 8 + t] - msub);
+          e[t] = iris::ex2_approx(fmaf(s[c16 * 8 + t], sc, nm));
           rs += e[t];
         }
         uint4 w;
@@ -294,8 +307,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
       iris::tc_fence_before();
       iris::mbar_arrive(&bars->p_full);
     }
+    // the last commit covers every earlier MMA of this CTA
     if (ok && n > 0 &&
-        iris::mbar_wait(&bars->pv_done, (uint32_t)((n - 1) & 1), abort_flag, p.status, IRIS_DEV_ERR_ATTN_SOFTMAX)) {
+        iris::mbar_wait(&bars->pv_done[(n - 1) & 1], (uint32_t)(((n - 1) >> 1) & 1), abort_flag, p.status,
+                        IRIS_DEV_ERR_ATTN_SOFTMAX)) {
       iris::tc_fence_after();
       const float inv = l > 0.f ? 1.0f / l : 0.f;
       const int row = q0 + r;

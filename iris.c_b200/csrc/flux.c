@@ -62,6 +62,8 @@ typedef struct {
 struct iris_cuda_flux {
     iris_cuda_flux_config_t cfg;
     int H, F, C, T, NH;
+    /* tensor parallelism: this rank's shard of heads / MLP columns */
+    int tp, tp_rank, NHl, Hl, Fl;
     uint16_t *w_x, *w_ctx, *w_t1, *w_t2, *w_mod, *w_proj;
     CUtensorMap tm_x, tm_ctx, tm_proj;
     flux_dbl_t *dbl;
@@ -95,13 +97,39 @@ static int check_cfg(const iris_cuda_flux_config_t *c) {
     return 0;
 }
 
+/* Row block [r0, r0+n) of a row-major [*, cols] device matrix -> dst (contiguous). */
+static int copy_rows(uint16_t *dst, const uint16_t *src, size_t r0, size_t n, size_t cols) {
+    return iris_cuda_check(cudaMemcpyAsync(dst, src + r0 * cols, n * cols * 2, cudaMemcpyDeviceToDevice,
+                                           g_rt.stream), "weight rows");
+}
+
+/* Column block [c0, c0+w) of a row-major [rows, lds] device matrix -> dst
+ * columns [d0, d0+w) of a row-major [rows, ldd] matrix. */
+static int copy_cols(uint16_t *dst, size_t ldd, size_t d0, const uint16_t *src, size_t lds, size_t c0,
+                     size_t w, size_t rows) {
+    return iris_cuda_check(cudaMemcpy2DAsync(dst + d0, ldd * 2, src + c0, lds * 2, w * 2, rows,
+                                             cudaMemcpyDeviceToDevice, g_rt.stream), "weight cols");
+}
+
+/* GEMM N-tile width for an output of N columns (256 when it divides N). */
+static int bn_for(int N) { return N % 256 == 0 ? 256 : 128; }
+
+/* Load and pack every weight of this rank's tensor-parallel shard (the whole
+ * model when tp == 1).  Shard r of tp holds attention heads
+ * [r*NH/tp, (r+1)*NH/tp) and MLP columns [r*F/tp, (r+1)*F/tp): the Q/K/V and
+ * gate/up rows of those heads/columns, and the matching input columns of the
+ * output and down projections.  Embedders, modulation and the final layer are
+ * replicated. */
 static int load_weights(iris_cuda_flux_t *tf, iris_wsrc_t *ws) {
-    int H = tf->H, F = tf->F, C = tf->C, T = tf->T;
+    const int H = tf->H, F = tf->F, C = tf->C, T = tf->T, Hl = tf->Hl, Fl = tf->Fl;
+    const size_t h0 = (size_t)tf->tp_rank * Hl, f0 = (size_t)tf->tp_rank * Fl;
     int rc = 0;
     char nm[256];
-    size_t tmp_n = (size_t)(3 * H + 2 * F) * H;
-    uint16_t *tmp = (uint16_t *)iris_dmalloc(tmp_n * 2);
+    /* tmp: a full source tensor | gate/up staging of the shard | norm staging */
+    size_t full_n = (size_t)(3 * H + 2 * F) * H, stage_n = (size_t)2 * Fl * H;
+    uint16_t *tmp = (uint16_t *)iris_dmalloc((full_n + stage_n + 512) * 2);
     if (!tmp) return IRIS_CUDA_ERR_OOM;
+    uint16_t *stage = tmp + full_n, *ntmp = stage + stage_n;
 
 #define CHK(x) do { if ((rc = (x)) != 0) goto done; } while (0)
 #define ALLOC(p, n) do { if (!((p) = walloc(tf, (n)))) { rc = IRIS_CUDA_ERR_OOM; goto done; } } while (0)
@@ -139,60 +167,67 @@ static int load_weights(iris_cuda_flux_t *tf, iris_wsrc_t *ws) {
     for (int i = 0; i < tf->cfg.n_double; i++) {
         flux_dbl_t *b = &tf->dbl[i];
         for (int s = 0; s < 2; s++) {
-            ALLOC(b->w_qkv[s], (size_t)3 * H * H);
-            ALLOC(b->w_out[s], (size_t)H * H);
-            ALLOC(b->w_in[s], (size_t)2 * F * H);
-            ALLOC(b->w_down[s], (size_t)H * F);
+            ALLOC(b->w_qkv[s], (size_t)3 * Hl * H);
+            ALLOC(b->w_out[s], (size_t)H * Hl);
+            ALLOC(b->w_in[s], (size_t)2 * Fl * H);
+            ALLOC(b->w_down[s], (size_t)H * Fl);
             b->qn[s] = (float *)iris_dmalloc(128 * 4);
             b->kn[s] = (float *)iris_dmalloc(128 * 4);
             if (!b->qn[s] || !b->kn[s]) { rc = IRIS_CUDA_ERR_OOM; goto done; }
             for (int j = 0; j < 3; j++) {
                 snprintf(nm, sizeof(nm), "transformer_blocks.%d.%s.weight", i, qkv_name[s][j]);
-                CHK(iris_wsrc_get(ws, nm, (size_t)H * H, b->w_qkv[s] + (size_t)j * H * H));
+                CHK(iris_wsrc_get(ws, nm, (size_t)H * H, tmp));
+                CHK(copy_rows(b->w_qkv[s] + (size_t)j * Hl * H, tmp, h0, Hl, H));
             }
             snprintf(nm, sizeof(nm), "transformer_blocks.%d.%s.weight", i, out_name[s]);
-            CHK(iris_wsrc_get(ws, nm, (size_t)H * H, b->w_out[s]));
+            CHK(iris_wsrc_get(ws, nm, (size_t)H * H, tmp));
+            CHK(copy_cols(b->w_out[s], Hl, 0, tmp, H, h0, Hl, H));
             snprintf(nm, sizeof(nm), "transformer_blocks.%d.%s.linear_in.weight", i, ff_name[s]);
             CHK(iris_wsrc_get(ws, nm, (size_t)2 * F * H, tmp));
+            CHK(copy_rows(stage, tmp, f0, Fl, H));
+            CHK(copy_rows(stage + (size_t)Fl * H, tmp, F + f0, Fl, H));
             iris_count_launch(1);
-            CHK(iris_cuda_check(iris_launch_interleave_gate_up(b->w_in[s], tmp, F, H, g_rt.stream), nm));
+            CHK(iris_cuda_check(iris_launch_interleave_gate_up(b->w_in[s], stage, Fl, H, g_rt.stream), nm));
             snprintf(nm, sizeof(nm), "transformer_blocks.%d.%s.linear_out.weight", i, ff_name[s]);
-            CHK(iris_wsrc_get(ws, nm, (size_t)H * F, b->w_down[s]));
+            CHK(iris_wsrc_get(ws, nm, (size_t)H * F, tmp));
+            CHK(copy_cols(b->w_down[s], Fl, 0, tmp, F, f0, Fl, H));
             snprintf(nm, sizeof(nm), "transformer_blocks.%d.%s.weight", i, qn_name[s]);
-            CHK(iris_wsrc_get_f32(ws, nm, 128, b->qn[s], tmp + (size_t)2 * F * H));
+            CHK(iris_wsrc_get_f32(ws, nm, 128, b->qn[s], ntmp));
             snprintf(nm, sizeof(nm), "transformer_blocks.%d.%s.weight", i, kn_name[s]);
-            CHK(iris_wsrc_get_f32(ws, nm, 128, b->kn[s], tmp + (size_t)2 * F * H + 128));
-            CHK(iris_mk_tmap(&b->tm_qkv[s], b->w_qkv[s], 3 * H, H, H, 256));
-            CHK(iris_mk_tmap(&b->tm_out[s], b->w_out[s], H, H, H, 256));
-            CHK(iris_mk_tmap(&b->tm_in[s], b->w_in[s], 2 * F, H, H, 256));
-            CHK(iris_mk_tmap(&b->tm_down[s], b->w_down[s], H, F, F, 256));
+            CHK(iris_wsrc_get_f32(ws, nm, 128, b->kn[s], ntmp + 128));
+            CHK(iris_mk_tmap(&b->tm_qkv[s], b->w_qkv[s], 3 * Hl, H, H, bn_for(3 * Hl)));
+            CHK(iris_mk_tmap(&b->tm_out[s], b->w_out[s], H, Hl, Hl, bn_for(H)));
+            CHK(iris_mk_tmap(&b->tm_in[s], b->w_in[s], 2 * Fl, H, H, 256));
+            CHK(iris_mk_tmap(&b->tm_down[s], b->w_down[s], H, Fl, Fl, bn_for(H)));
         }
     }
     for (int i = 0; i < tf->cfg.n_single; i++) {
         flux_sgl_t *b = &tf->sgl[i];
-        ALLOC(b->w_fused, (size_t)(3 * H + 2 * F) * H);
-        ALLOC(b->w_out, (size_t)H * (H + F));
+        ALLOC(b->w_fused, (size_t)(3 * Hl + 2 * Fl) * H);
+        ALLOC(b->w_out, (size_t)H * (Hl + Fl));
         b->qn = (float *)iris_dmalloc(128 * 4);
         b->kn = (float *)iris_dmalloc(128 * 4);
         if (!b->qn || !b->kn) { rc = IRIS_CUDA_ERR_OOM; goto done; }
         snprintf(nm, sizeof(nm), "single_transformer_blocks.%d.attn.to_qkv_mlp_proj.weight", i);
-        CHK(iris_wsrc_get(ws, nm, (size_t)(3 * H + 2 * F) * H, tmp));
-        CHK(iris_cuda_check(cudaMemcpyAsync(b->w_fused, tmp, (size_t)3 * H * H * 2,
-                                            cudaMemcpyDeviceToDevice, g_rt.stream), nm));
+        CHK(iris_wsrc_get(ws, nm, full_n, tmp));
+        for (int j = 0; j < 3; j++)
+            CHK(copy_rows(b->w_fused + (size_t)j * Hl * H, tmp, (size_t)j * H + h0, Hl, H));
+        CHK(copy_rows(stage, tmp, (size_t)3 * H + f0, Fl, H));
+        CHK(copy_rows(stage + (size_t)Fl * H, tmp, (size_t)3 * H + F + f0, Fl, H));
         iris_count_launch(1);
-        CHK(iris_cuda_check(iris_launch_interleave_gate_up(b->w_fused + (size_t)3 * H * H,
-                                                           tmp + (size_t)3 * H * H, F, H,
+        CHK(iris_cuda_check(iris_launch_interleave_gate_up(b->w_fused + (size_t)3 * Hl * H, stage, Fl, H,
                                                            g_rt.stream), nm));
+        /* linear2 input is [attention H | MLP F]: keep this shard's columns of both */
         snprintf(nm, sizeof(nm), "single_transformer_blocks.%d.attn.to_out.weight", i);
-        CHK(iris_wsrc_get(ws, nm, (size_t)H * (H + F), b->w_out));
-        /* norm weights go through a temp slot that the next fused weight does not overwrite
-           before the conversion kernel ran: same stream, so ordering is guaranteed */
+        CHK(iris_wsrc_get(ws, nm, (size_t)H * (H + F), tmp));
+        CHK(copy_cols(b->w_out, Hl + Fl, 0, tmp, H + F, h0, Hl, H));
+        CHK(copy_cols(b->w_out, Hl + Fl, Hl, tmp, H + F, H + f0, Fl, H));
         snprintf(nm, sizeof(nm), "single_transformer_blocks.%d.attn.norm_q.weight", i);
-        CHK(iris_wsrc_get_f32(ws, nm, 128, b->qn, tmp));
+        CHK(iris_wsrc_get_f32(ws, nm, 128, b->qn, ntmp));
         snprintf(nm, sizeof(nm), "single_transformer_blocks.%d.attn.norm_k.weight", i);
-        CHK(iris_wsrc_get_f32(ws, nm, 128, b->kn, tmp + 128));
-        CHK(iris_mk_tmap(&b->tm_fused, b->w_fused, 3 * H + 2 * F, H, H, 256));
-        CHK(iris_mk_tmap(&b->tm_out, b->w_out, H, H + F, H + F, 256));
+        CHK(iris_wsrc_get_f32(ws, nm, 128, b->kn, ntmp + 128));
+        CHK(iris_mk_tmap(&b->tm_fused, b->w_fused, 3 * Hl + 2 * Fl, H, H, 256));
+        CHK(iris_mk_tmap(&b->tm_out, b->w_out, H, Hl + Fl, Hl + Fl, bn_for(H)));
     }
     tf->t_dev = (float *)iris_dmalloc(4 * 4);
     tf->sincos = (float *)iris_dmalloc(256 * 4);
@@ -216,7 +251,7 @@ static void plan_free(flux_plan_t *P);
 
 void iris_cuda_flux_free(iris_cuda_flux_t *tf) {
     if (!tf) return;
-    cudaStreamSynchronize(g_rt.stream);
+    iris_stream_drain();
     plan_free(&tf->plan);
     iris_dfree(tf->w_x); iris_dfree(tf->w_ctx); iris_dfree(tf->w_t1); iris_dfree(tf->w_t2);
     iris_dfree(tf->w_mod); iris_dfree(tf->w_proj);
@@ -241,8 +276,18 @@ void iris_cuda_flux_free(iris_cuda_flux_t *tf) {
     free(tf);
 }
 
-static iris_cuda_flux_t *flux_new(const iris_cuda_flux_config_t *cfg) {
+static iris_cuda_flux_t *flux_new(const iris_cuda_flux_config_t *cfg, int tp_rank, int tp) {
     if (check_cfg(cfg)) return NULL;
+    if (tp < 1 || tp_rank < 0 || tp_rank >= tp) {
+        iris_fail(IRIS_CUDA_ERR_ARG, "tensor-parallel rank %d of %d", tp_rank, tp);
+        return NULL;
+    }
+    /* each shard keeps whole heads in pairs (256-column GEMM tiles over Q|K|V
+       and an aligned gate/up region) and whole 128-column MLP blocks */
+    if (tp > 1 && (cfg->heads % (2 * tp) || cfg->mlp % (128 * tp))) {
+        iris_fail(IRIS_CUDA_ERR_ARG, "tp=%d needs heads %% (2*tp) == 0 and mlp %% (128*tp) == 0", tp);
+        return NULL;
+    }
     iris_cuda_flux_t *tf = (iris_cuda_flux_t *)calloc(1, sizeof(*tf));
     if (!tf) { iris_fail(IRIS_CUDA_ERR_OOM, "model struct"); return NULL; }
     tf->cfg = *cfg;
@@ -251,6 +296,11 @@ static iris_cuda_flux_t *flux_new(const iris_cuda_flux_config_t *cfg) {
     tf->C = cfg->channels;
     tf->T = cfg->text_dim;
     tf->NH = cfg->heads;
+    tf->tp = tp;
+    tf->tp_rank = tp_rank;
+    tf->NHl = cfg->heads / tp;
+    tf->Hl = tf->NHl * 128;
+    tf->Fl = cfg->mlp / tp;
     return tf;
 }
 
@@ -287,10 +337,14 @@ static int parse_config(const char *model_dir, iris_cuda_flux_config_t *c) {
 }
 
 iris_cuda_flux_t *iris_cuda_flux_load(const char *model_dir) {
+    return iris_cuda_flux_load_tp(model_dir, 0, 1);
+}
+
+iris_cuda_flux_t *iris_cuda_flux_load_tp(const char *model_dir, int tp_rank, int tp_size) {
     if (iris_rt_ensure() != IRIS_CUDA_OK) return NULL;
     iris_cuda_flux_config_t cfg;
     parse_config(model_dir, &cfg);
-    iris_cuda_flux_t *tf = flux_new(&cfg);
+    iris_cuda_flux_t *tf = flux_new(&cfg, tp_rank, tp_size);
     if (!tf) return NULL;
     snprintf(tf->model_dir, sizeof(tf->model_dir), "%s", model_dir);
     iris_wsrc_t ws;
@@ -311,8 +365,13 @@ iris_cuda_flux_t *iris_cuda_flux_load(const char *model_dir) {
 
 iris_cuda_flux_t *iris_cuda_flux_random(const iris_cuda_flux_config_t *cfg, uint64_t seed,
                                         float std, int norm_unit) {
+    return iris_cuda_flux_random_tp(cfg, seed, std, norm_unit, 0, 1);
+}
+
+iris_cuda_flux_t *iris_cuda_flux_random_tp(const iris_cuda_flux_config_t *cfg, uint64_t seed,
+                                           float std, int norm_unit, int tp_rank, int tp_size) {
     if (iris_rt_ensure() != IRIS_CUDA_OK) return NULL;
-    iris_cuda_flux_t *tf = flux_new(cfg);
+    iris_cuda_flux_t *tf = flux_new(cfg, tp_rank, tp_size);
     if (!tf) return NULL;
     tf->random = 1;
     tf->seed = seed;
@@ -347,7 +406,7 @@ int iris_cuda_flux_read_weight(iris_cuda_flux_t *tf, const char *name, uint16_t 
         int rc = iris_wsrc_get(&ws, name, numel, d);
         if (!rc) rc = iris_cuda_check(cudaMemcpyAsync(out, d, numel * 2, cudaMemcpyDeviceToHost,
                                                       g_rt.stream), "read weight");
-        cudaStreamSynchronize(g_rt.stream);
+        iris_stream_drain();
         iris_dfree(d);
         return rc;
     }
@@ -422,9 +481,9 @@ static int plan_ensure(iris_cuda_flux_t *tf, int s_txt, int img_h, int img_w,
     for (int r = 0; same && r < num_refs; r++)
         same = P->ref_h[r] == refs[r].h && P->ref_w[r] == refs[r].w && P->ref_t[r] == refs[r].t_offset;
     if (same) return 0;
-    cudaStreamSynchronize(g_rt.stream);
+    iris_stream_drain();
     plan_free(P);
-    int H = tf->H, F = tf->F, C = tf->C, T = tf->T;
+    int H = tf->H, C = tf->C, T = tf->T, Hl = tf->Hl, Fl = tf->Fl;
     P->s_txt = s_txt; P->img_h = img_h; P->img_w = img_w; P->num_refs = num_refs;
     P->n_img = img_h * img_w;
     P->n_img_total = P->n_img;
@@ -434,7 +493,7 @@ static int plan_ensure(iris_cuda_flux_t *tf, int s_txt, int img_h, int img_w,
         P->n_img_total += refs[r].h * refs[r].w;
     }
     int S = P->S = s_txt + P->n_img_total;
-    size_t sH = (size_t)S * H;
+    size_t sH = (size_t)S * H, sHl = (size_t)S * Hl;
 #define PA(p, bytes) do { if (!((p) = iris_dmalloc(bytes))) goto oom; } while (0)
     PA(P->hidden, sH * 4);
     PA(P->lat_in, (size_t)C * P->n_img_total * 4);
@@ -443,18 +502,19 @@ static int plan_ensure(iris_cuda_flux_t *tf, int s_txt, int img_h, int img_w,
     PA(P->rope_cos, (size_t)S * 64 * 4);
     PA(P->rope_sin, (size_t)S * 64 * 4);
     PA(P->xmod, sH * 2);
-    PA(P->q, sH * 2);
-    PA(P->k, sH * 2);
-    PA(P->v, sH * 2);
-    PA(P->attn, sH * 2);
-    PA(P->mlp, (size_t)S * F * 2);
-    PA(P->cat, (size_t)S * (H + F) * 2);
+    PA(P->q, sHl * 2);
+    PA(P->k, sHl * 2);
+    PA(P->v, sHl * 2);
+    PA(P->attn, sHl * 2);
+    PA(P->mlp, (size_t)S * Fl * 2);
+    PA(P->cat, (size_t)S * (Hl + Fl) * 2);
     PA(P->tok_img, (size_t)P->n_img_total * C * 2);
     PA(P->tok_txt, (size_t)s_txt * T * 2);
 #undef PA
-    if (iris_mk_tmap(&P->tm_xmod, P->xmod, S, H, H, 128) || iris_mk_tmap(&P->tm_attn, P->attn, S, H, H, 128) ||
-        iris_mk_tmap(&P->tm_mlp, P->mlp, S, F, F, 128) ||
-        iris_mk_tmap(&P->tm_cat, P->cat, S, H + F, H + F, 128) ||
+    if (iris_mk_tmap(&P->tm_xmod, P->xmod, S, H, H, 128) ||
+        iris_mk_tmap(&P->tm_attn, P->attn, S, Hl, Hl, 128) ||
+        iris_mk_tmap(&P->tm_mlp, P->mlp, S, Fl, Fl, 128) ||
+        iris_mk_tmap(&P->tm_cat, P->cat, S, Hl + Fl, Hl + Fl, 128) ||
         iris_mk_tmap(&P->tm_tok_img, P->tok_img, P->n_img_total, C, C, 128) ||
         iris_mk_tmap(&P->tm_tok_txt, P->tok_txt, s_txt, T, T, 128)) {
         plan_free(P);
@@ -534,6 +594,19 @@ static void enq_gemm(enq_t *E, const IrisGemmParams *p, const char *what) {
     enq_x(E, iris_launch_gemm(p, g_rt.num_sms, g_rt.stream), what, 2.0 * rows * p->N * p->K, bytes);
 }
 
+/* Tensor parallelism: the output projections of a shard write gate * partial
+ * (rank 0 adds it to the residual stream, the other ranks store it alone), so
+ * one in-place sum all-reduce of the f32 hidden state completes the residual
+ * update on every rank. */
+static void tp_resid(const iris_cuda_flux_t *tf, IrisGemmParams *gp) {
+    gp->resid_store = tf->tp > 1 && tf->tp_rank != 0;
+}
+
+static void enq_allreduce(iris_cuda_flux_t *tf, enq_t *E) {
+    if (tf->tp <= 1 || E->rc) return;
+    E->rc = iris_comm_allreduce_sum(tf->plan.hidden, (size_t)tf->plan.S * tf->H, 0);
+}
+
 /* timestep embedding and every modulation vector of the step */
 static void enq_mods(iris_cuda_flux_t *tf, enq_t *E) {
     cudaStream_t st = g_rt.stream;
@@ -577,69 +650,77 @@ static void enq_embed(iris_cuda_flux_t *tf, enq_t *E) {
 static void enq_double(iris_cuda_flux_t *tf, int i, enq_t *E) {
     flux_plan_t *P = &tf->plan;
     cudaStream_t st = g_rt.stream;
-    const int H = tf->H, F = tf->F, NH = tf->NH, St = P->s_txt, Si = P->n_img_total, S = P->S;
+    const int H = tf->H, Hl = tf->Hl, Fl = tf->Fl, NHl = tf->NHl, St = P->s_txt, Si = P->n_img_total,
+              S = P->S;
     const float *mi = tf->mods, *mt = tf->mods + (size_t)6 * H;
     flux_dbl_t *b = &tf->dbl[i];
     IrisGemmParams gp;
     enq_x(E, iris_launch_adaln(P->hidden, H, P->xmod, H, S, H, mt, mt + H, mi, mi + H, St, 1e-6f, st),
           "adaln1", 0.0, 6.0 * S * (double)H);
-    gp_init(&gp, &P->tm_xmod, 3 * H, H, IRIS_EPI_QKV);
+    gp_init(&gp, &P->tm_xmod, 3 * Hl, H, IRIS_EPI_QKV);
+    gp.bn = bn_for(3 * Hl);
     gp_group(&gp, 0, &b->tm_qkv[0], 0, St);
     gp_group(&gp, 1, &b->tm_qkv[1], St, Si);
     gp.qnorm[0] = b->qn[0]; gp.knorm[0] = b->kn[0];
     gp.qnorm[1] = b->qn[1]; gp.knorm[1] = b->kn[1];
     gp.rope_cos = P->rope_cos; gp.rope_sin = P->rope_sin;
-    gp.q = P->q; gp.k = P->k; gp.v = P->v; gp.ldqkv = H; gp.H = H;
+    gp.q = P->q; gp.k = P->k; gp.v = P->v; gp.ldqkv = Hl; gp.H = Hl;
     enq_gemm(E, &gp, "dbl_qkv");
-    enq_x(E, iris_launch_attention(P->q, H, P->k, P->v, H, P->attn, H, S, S, NH,
+    enq_x(E, iris_launch_attention(P->q, Hl, P->k, P->v, Hl, P->attn, Hl, S, S, NHl,
                                    1.0f / sqrtf(128.0f), NULL, st), "dbl_attn",
-          4.0 * S * S * (double)H, 8.0 * S * (double)H);
-    gp_init(&gp, &P->tm_attn, H, H, IRIS_EPI_RESID_GATE);
+          4.0 * S * S * (double)Hl, 8.0 * S * (double)Hl);
+    gp_init(&gp, &P->tm_attn, H, Hl, IRIS_EPI_RESID_GATE);
     gp_group(&gp, 0, &b->tm_out[0], 0, St);
     gp_group(&gp, 1, &b->tm_out[1], St, Si);
     gp.out = P->hidden; gp.ldo = H;
     gp.gate[0] = mt + 2 * H; gp.gate[1] = mi + 2 * H;
+    tp_resid(tf, &gp);
     enq_gemm(E, &gp, "dbl_out");
+    enq_allreduce(tf, E);
     enq_x(E, iris_launch_adaln(P->hidden, H, P->xmod, H, S, H, mt + 3 * H, mt + 4 * H, mi + 3 * H,
                                mi + 4 * H, St, 1e-6f, st), "adaln2", 0.0, 6.0 * S * (double)H);
-    gp_init(&gp, &P->tm_xmod, 2 * F, H, IRIS_EPI_SWIGLU);
+    gp_init(&gp, &P->tm_xmod, 2 * Fl, H, IRIS_EPI_SWIGLU);
     gp_group(&gp, 0, &b->tm_in[0], 0, St);
     gp_group(&gp, 1, &b->tm_in[1], St, Si);
-    gp.mlp_out = P->mlp; gp.ld_mlp = F; gp.mlp_col0 = 0; gp.swiglu_base = 0;
+    gp.mlp_out = P->mlp; gp.ld_mlp = Fl; gp.mlp_col0 = 0; gp.swiglu_base = 0;
     enq_gemm(E, &gp, "dbl_mlp_in");
-    gp_init(&gp, &P->tm_mlp, H, F, IRIS_EPI_RESID_GATE);
+    gp_init(&gp, &P->tm_mlp, H, Fl, IRIS_EPI_RESID_GATE);
     gp_group(&gp, 0, &b->tm_down[0], 0, St);
     gp_group(&gp, 1, &b->tm_down[1], St, Si);
     gp.out = P->hidden; gp.ldo = H;
     gp.gate[0] = mt + 5 * H; gp.gate[1] = mi + 5 * H;
+    tp_resid(tf, &gp);
     enq_gemm(E, &gp, "dbl_mlp_out");
+    enq_allreduce(tf, E);
 }
 
 /* single-stream block i over the whole [TXT, IMG] sequence */
 static void enq_single(iris_cuda_flux_t *tf, int i, enq_t *E) {
     flux_plan_t *P = &tf->plan;
     cudaStream_t st = g_rt.stream;
-    const int H = tf->H, F = tf->F, NH = tf->NH, S = P->S;
+    const int H = tf->H, Hl = tf->Hl, Fl = tf->Fl, NHl = tf->NHl, S = P->S;
     const float *ms = tf->mods + (size_t)12 * H;
     flux_sgl_t *b = &tf->sgl[i];
     IrisGemmParams gp;
     enq_x(E, iris_launch_adaln(P->hidden, H, P->xmod, H, S, H, ms, ms + H, NULL, NULL, S, 1e-6f, st),
           "adaln_s", 0.0, 6.0 * S * (double)H);
-    gp_init(&gp, &P->tm_xmod, 3 * H + 2 * F, H, IRIS_EPI_SINGLE);
+    gp_init(&gp, &P->tm_xmod, 3 * Hl + 2 * Fl, H, IRIS_EPI_SINGLE);
     gp_group(&gp, 0, &b->tm_fused, 0, S);
     gp.qnorm[0] = b->qn; gp.knorm[0] = b->kn;
     gp.rope_cos = P->rope_cos; gp.rope_sin = P->rope_sin;
-    gp.q = P->q; gp.k = P->k; gp.v = P->v; gp.ldqkv = H; gp.H = H;
-    gp.mlp_out = P->cat; gp.ld_mlp = H + F; gp.mlp_col0 = H; gp.swiglu_base = 3 * H;
+    gp.q = P->q; gp.k = P->k; gp.v = P->v; gp.ldqkv = Hl; gp.H = Hl;
+    gp.mlp_out = P->cat; gp.ld_mlp = Hl + Fl; gp.mlp_col0 = Hl; gp.swiglu_base = 3 * Hl;
     enq_gemm(E, &gp, "sgl_fused");
-    enq_x(E, iris_launch_attention(P->q, H, P->k, P->v, H, P->cat, H + F, S, S, NH,
+    enq_x(E, iris_launch_attention(P->q, Hl, P->k, P->v, Hl, P->cat, Hl + Fl, S, S, NHl,
                                    1.0f / sqrtf(128.0f), NULL, st), "sgl_attn",
-          4.0 * S * S * (double)H, 8.0 * S * (double)H);
-    gp_init(&gp, &P->tm_cat, H, H + F, IRIS_EPI_RESID_GATE);
+          4.0 * S * S * (double)Hl, 8.0 * S * (double)Hl);
+    gp_init(&gp, &P->tm_cat, H, Hl + Fl, IRIS_EPI_RESID_GATE);
     gp_group(&gp, 0, &b->tm_out, 0, S);
     gp.out = P->hidden; gp.ldo = H;
     gp.gate[0] = ms + 2 * H;
+    tp_resid(tf, &gp);
     enq_gemm(E, &gp, "sgl_out");
+    enq_allreduce(tf, E);
 }
 
 /* final layer on the target image rows only (scale first, then shift: :4277-4281) */
@@ -730,16 +811,21 @@ int iris_cuda_flux_profile(iris_cuda_flux_t *tf, float timestep, iris_cuda_kerne
     return rc ? rc : n;
 }
 
-/* Run the forward of the current plan (captured once into a CUDA graph). */
+/* Run the forward of the current plan (captured once into a CUDA graph; a
+ * tensor-parallel shard launches eagerly, its all-reduces between the blocks'
+ * kernels). */
 static int run_forward(iris_cuda_flux_t *tf) {
     flux_plan_t *P = &tf->plan;
     if (iris_fault("launch"))
         return iris_fail(IRIS_CUDA_ERR_INJECTED, "injected launch failure");
+    if (tf->tp > 1 && (iris_comm_world() != tf->tp || iris_comm_rank() != tf->tp_rank))
+        return iris_fail(IRIS_CUDA_ERR_ARG, "shard %d of %d needs a communicator of that rank and size",
+                         tf->tp_rank, tf->tp);
     if (!P->graph_ok) {
         static int no_graph = -1;
         if (no_graph < 0) no_graph = getenv("IRIS_CUDA_NO_GRAPH") ? 1 : 0;
         enq_t E = {0};
-        if (no_graph) {
+        if (no_graph || tf->tp > 1) {
             int rc = enqueue_forward(tf, &E);
             iris_count_launch(E.kernels);
             return rc;
@@ -795,6 +881,7 @@ float *iris_flux_plan_txt(iris_cuda_flux_t *tf) { return tf->plan.txt_f32; }
 float *iris_flux_t_dev(iris_cuda_flux_t *tf) { return tf->t_dev; }
 int iris_flux_channels(iris_cuda_flux_t *tf) { return tf->C; }
 int iris_flux_text_dim(iris_cuda_flux_t *tf) { return tf->T; }
+int iris_flux_tp(iris_cuda_flux_t *tf) { return tf->tp; }
 
 /* set t on the device (async, from a device or pinned source) and run */
 int iris_flux_run(iris_cuda_flux_t *tf, const float *t_src, enum cudaMemcpyKind kind) {

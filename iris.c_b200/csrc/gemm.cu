@@ -178,7 +178,7 @@ __device__ __forceinline__ void epi_plain_chunk(const IrisGemmParams& p, uint32_
       const float4* gp = reinterpret_cast<const float4*>(p.gate[g] + c);
 #pragma unroll
       for (int e = 0; e < 8; e++) {
-        float4 h = d[e], gg = __ldg(gp + e);
+        float4 h = p.resid_store ? make_float4(0.f, 0.f, 0.f, 0.f) : d[e], gg = __ldg(gp + e);
         h.x += gg.x * v[4 * e];
         h.y += gg.y * v[4 * e + 1];
         h.z += gg.z * v[4 * e + 2];

@@ -42,6 +42,19 @@ static inline void iris_count_launch(uint64_t n) { g_rt.launches += n; }
 /* ensure the runtime is up; returns status */
 int iris_rt_ensure(void);
 
+/* ---------------- NCCL communicator (comm.c) ---------------- */
+int iris_comm_world(void);  /* 1 without a communicator */
+int iris_comm_rank(void);
+int iris_comm_active(void);
+/* in-place sum all-reduce of n f32 (bf16 = 0) or bf16 elements on the library stream */
+int iris_comm_allreduce_sum(void *buf, size_t n, int bf16);
+/* all-gather of n f32 per rank into recv [world * n] on the library stream */
+int iris_comm_allgather_f32(const float *send, float *recv, size_t n);
+/* bounded stream synchronisation while collectives may be queued */
+int iris_comm_sync_stream(void);
+/* wait for the library stream (bounded when a communicator exists) */
+int iris_stream_drain(void);
+
 /* ---------------- safetensors (own reader) ---------------- */
 typedef enum { ST_F32 = 0, ST_F16 = 1, ST_BF16 = 2, ST_OTHER = 3 } st_dtype_t;
 

@@ -47,6 +47,7 @@ typedef struct {
     int nchw_rows;            /* IRIS_EPI_F32_NCHW: channel stride                      */
     const float *bias;        /* optional [N]                                          */
     const float *gate[2];     /* RESID: per group [N]                                  */
+    int resid_store;          /* RESID: out = gate*acc instead of out += gate*acc      */
     const float *qnorm[2];    /* QKV: per group [128]                                  */
     const float *knorm[2];
     const float *rope_cos;    /* QKV: [rows_total, 64] by absolute row (NULL = no RoPE) */

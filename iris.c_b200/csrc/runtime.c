@@ -123,9 +123,14 @@ int iris_cuda_device_status(int clear) {
     return v;
 }
 
+int iris_stream_drain(void) {
+    return iris_comm_active() ? iris_comm_sync_stream()
+                              : iris_cuda_check(cudaStreamSynchronize(g_rt.stream), "cudaStreamSynchronize");
+}
+
 int iris_cuda_synchronize(void) {
     if (!g_rt.initialized) return IRIS_CUDA_OK;
-    int rc = iris_cuda_check(cudaStreamSynchronize(g_rt.stream), "cudaStreamSynchronize");
+    int rc = iris_stream_drain();
     if (rc) return rc;
     int st = iris_cuda_device_status(0);
     if (st) return iris_fail(IRIS_CUDA_ERR_TIMEOUT, "device wait expired (code 0x%x)", st);

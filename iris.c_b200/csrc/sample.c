@@ -24,6 +24,7 @@ float *iris_flux_plan_txt(iris_cuda_flux_t *tf);
 int iris_flux_run(iris_cuda_flux_t *tf, const float *t_src, enum cudaMemcpyKind kind);
 int iris_flux_channels(iris_cuda_flux_t *tf);
 int iris_flux_text_dim(iris_cuda_flux_t *tf);
+int iris_flux_tp(iris_cuda_flux_t *tf);
 
 #define IRIS_CUDA_MAX_STEPS 1000
 
@@ -154,13 +155,13 @@ float *iris_cuda_init_noise(int batch, int c, int h, int w, int64_t seed) {
  * CFG contexts), kept across calls and grown on demand so back-to-back
  * images queue without allocations or host synchronisation. */
 static struct {
-    float *sched, *vu, *txt_c, *txt_u;
-    size_t sched_n, vu_n, txt_n;
+    float *sched, *vu, *txt_c, *txt_u, *vpair;
+    size_t sched_n, vu_n, txt_n, vpair_n;
 } g_sws;
 
 static int ws_grow(float **p, size_t *cap, size_t n) {
     if (*cap >= n) return 0;
-    cudaStreamSynchronize(g_rt.stream); /* the old buffer may still be in use */
+    iris_stream_drain(); /* the old buffer may still be in use */
     iris_dfree(*p);
     *p = (float *)iris_dmalloc(n * 4);
     *cap = *p ? n : 0;
@@ -290,4 +291,85 @@ int iris_cuda_sample_euler_dev(iris_cuda_flux_t *tf, float *d_z, int h, int w, c
     return iris_cuda_check(cudaMemcpyAsync(d_z, iris_flux_plan_latent(tf),
                                            (size_t)iris_flux_channels(tf) * h * w * 4,
                                            cudaMemcpyDeviceToDevice, g_rt.stream), "z copy");
+}
+
+/* ------------------------------------------------------------ CFG over a GPU pair
+ * The two branches of classifier-free guidance run on the two ranks of the
+ * process's communicator (rank 0 unconditional, rank 1 conditional).  After
+ * every forward the pair all-gathers its velocities [v_uncond | v_cond] and
+ * both ranks apply the same guided Euler update, so both hold the identical
+ * latent, bit-equal to the one-GPU CFG sampler (iris_sample_euler_cfg,
+ * iris_sample.c:717: v = v_uncond + g (v_cond - v_uncond)). */
+static int euler_pair_core(iris_cuda_flux_t *tf, int h, int w, float guidance, const float *schedule,
+                           int steps, void (*progress)(int, int)) {
+    cudaStream_t st = g_rt.stream;
+    float *z = iris_flux_plan_latent(tf), *v = iris_flux_plan_out(tf);
+    size_t n = (size_t)iris_flux_channels(tf) * h * w;
+    int rc;
+    if ((rc = ws_grow(&g_sws.sched, &g_sws.sched_n, IRIS_CUDA_MAX_STEPS + 1)) ||
+        (rc = ws_grow(&g_sws.vpair, &g_sws.vpair_n, 2 * n)))
+        return rc;
+    if ((rc = iris_cuda_check(cudaMemcpyAsync(g_sws.sched, schedule, (size_t)(steps + 1) * 4,
+                                              cudaMemcpyHostToDevice, st), "schedule")))
+        return rc;
+    for (int s = 0; s < steps; s++) {
+        if ((rc = iris_flux_run(tf, g_sws.sched + s, cudaMemcpyDeviceToDevice))) return rc;
+        if ((rc = iris_comm_allgather_f32(v, g_sws.vpair, n))) return rc;
+        iris_count_launch(1);
+        if ((rc = iris_cuda_check(iris_launch_euler(z, g_sws.vpair + n, g_sws.vpair, guidance,
+                                                    schedule[s + 1] - schedule[s], (long)n, st), "euler")))
+            return rc;
+        if (progress) progress(s + 1, steps);
+    }
+    return 0;
+}
+
+static int pair_check(iris_cuda_flux_t *tf, const void *c, const void *u, int seq_c, int seq_u,
+                      const float *schedule, int steps) {
+    if (!tf || !c || !u || !schedule) return iris_fail(IRIS_CUDA_ERR_ARG, "null argument");
+    if (steps <= 0 || steps > IRIS_CUDA_MAX_STEPS) return iris_fail(IRIS_CUDA_ERR_ARG, "num_steps");
+    if (seq_c != seq_u) return iris_fail(IRIS_CUDA_ERR_ARG, "cond/uncond text lengths must match");
+    if (iris_comm_world() != 2) return iris_fail(IRIS_CUDA_ERR_ARG, "CFG pair needs a 2-rank communicator");
+    if (iris_flux_tp(tf) != 1) return iris_fail(IRIS_CUDA_ERR_ARG, "CFG pair needs an unsharded model");
+    return 0;
+}
+
+int iris_cuda_sample_euler_cfg_pair_dev(iris_cuda_flux_t *tf, float *d_z, int h, int w,
+                                        const float *d_txt_cond, const float *d_txt_uncond,
+                                        int txt_seq, float guidance, const float *schedule,
+                                        int num_steps) {
+    int rc = pair_check(tf, d_txt_cond, d_txt_uncond, txt_seq, txt_seq, schedule, num_steps);
+    if (rc) return rc;
+    if (!d_z) return iris_fail(IRIS_CUDA_ERR_ARG, "null latent");
+    const float *txt = iris_comm_rank() == 0 ? d_txt_uncond : d_txt_cond;
+    if ((rc = iris_flux_plan_and_inputs(tf, d_z, h, w, NULL, 0, txt, txt_seq, cudaMemcpyDeviceToDevice)) ||
+        (rc = euler_pair_core(tf, h, w, guidance, schedule, num_steps, NULL)))
+        return rc;
+    return iris_cuda_check(cudaMemcpyAsync(d_z, iris_flux_plan_latent(tf),
+                                           (size_t)iris_flux_channels(tf) * h * w * 4,
+                                           cudaMemcpyDeviceToDevice, g_rt.stream), "z copy");
+}
+
+float *iris_cuda_sample_euler_cfg_pair(iris_cuda_flux_t *tf, const float *z, int batch, int channels,
+                                       int h, int w, const float *text_emb_cond, int text_seq_cond,
+                                       const float *text_emb_uncond, int text_seq_uncond,
+                                       float guidance_scale, const float *schedule, int num_steps,
+                                       void (*progress_callback)(int, int)) {
+    if (pair_check(tf, text_emb_cond, text_emb_uncond, text_seq_cond, text_seq_uncond, schedule, num_steps))
+        return NULL;
+    if (!z || batch != 1 || channels != iris_flux_channels(tf)) {
+        iris_fail(IRIS_CUDA_ERR_ARG, "latent must be [1, %d, h, w]", iris_flux_channels(tf));
+        return NULL;
+    }
+    const float *txt = iris_comm_rank() == 0 ? text_emb_uncond : text_emb_cond;
+    int rc = iris_flux_plan_and_inputs(tf, z, h, w, NULL, 0, txt, text_seq_cond, cudaMemcpyHostToDevice);
+    if (!rc) rc = euler_pair_core(tf, h, w, guidance_scale, schedule, num_steps, progress_callback);
+    size_t n = (size_t)channels * h * w;
+    float *out = rc ? NULL : (float *)malloc(n * 4);
+    if (!rc && !out) rc = iris_fail(IRIS_CUDA_ERR_OOM, "output");
+    if (!rc) rc = iris_cuda_check(cudaMemcpyAsync(out, iris_flux_plan_latent(tf), n * 4,
+                                                  cudaMemcpyDeviceToHost, g_rt.stream), "z copy");
+    if (!rc) rc = iris_cuda_synchronize();
+    if (rc) { free(out); return NULL; }
+    return out;
 }

@@ -71,6 +71,9 @@ SIGNATURES = {
     "iris_cuda_kernel_launches": (C.c_uint64, []),
     "iris_cuda_flux_load": (C.c_void_p, [C.c_char_p]),
     "iris_cuda_flux_random": (C.c_void_p, [C.POINTER(FluxConfig), C.c_uint64, C.c_float, C.c_int]),
+    "iris_cuda_flux_load_tp": (C.c_void_p, [C.c_char_p, C.c_int, C.c_int]),
+    "iris_cuda_flux_random_tp": (C.c_void_p, [C.POINTER(FluxConfig), C.c_uint64, C.c_float, C.c_int,
+                                              C.c_int, C.c_int]),
     "iris_cuda_flux_free": (None, [C.c_void_p]),
     "iris_cuda_flux_get_config": (C.c_int, [C.c_void_p, C.POINTER(FluxConfig)]),
     "iris_cuda_flux_read_weight": (C.c_int, [C.c_void_p, C.c_char_p, _u16p, C.c_size_t]),
@@ -100,6 +103,17 @@ SIGNATURES = {
                                                             _fp, C.c_int, _fp, C.c_int, PROGRESS_CB]),
     "iris_cuda_sample_euler_dev": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p,
                                              C.c_int, C.c_void_p, C.c_int, C.c_float, _fp, C.c_int]),
+    "iris_cuda_comm_unique_id": (C.c_int, [C.c_void_p, C.c_size_t]),
+    "iris_cuda_comm_init": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
+    "iris_cuda_comm_destroy": (None, []),
+    "iris_cuda_comm_world": (C.c_int, []),
+    "iris_cuda_comm_rank": (C.c_int, []),
+    "iris_cuda_sample_euler_cfg_pair": (C.c_void_p, [C.c_void_p, _fp, C.c_int, C.c_int, C.c_int, C.c_int,
+                                                     _fp, C.c_int, _fp, C.c_int, C.c_float, _fp, C.c_int,
+                                                     PROGRESS_CB]),
+    "iris_cuda_sample_euler_cfg_pair_dev": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int,
+                                                      C.c_void_p, C.c_void_p, C.c_int, C.c_float, _fp,
+                                                      C.c_int]),
     "iris_cuda_zimage_load": (C.c_void_p, [C.c_char_p]),
     "iris_cuda_zimage_random": (C.c_void_p, [C.POINTER(ZImageConfig), C.c_uint64, C.c_float, C.c_int]),
     "iris_cuda_zimage_free": (None, [C.c_void_p]),
@@ -215,12 +229,17 @@ class Flux:
         self.cfg = cfg
 
     @classmethod
-    def load(cls, model_dir: str) -> "Flux":
-        return cls(lib().iris_cuda_flux_load(model_dir.encode()))
+    def load(cls, model_dir: str, tp_rank: int = 0, tp_size: int = 1) -> "Flux":
+        if tp_size == 1:
+            return cls(lib().iris_cuda_flux_load(model_dir.encode()))
+        return cls(lib().iris_cuda_flux_load_tp(model_dir.encode(), tp_rank, tp_size))
 
     @classmethod
-    def random(cls, cfg: FluxConfig, seed: int, std: float = 0.02, norm_unit: bool = False) -> "Flux":
-        return cls(lib().iris_cuda_flux_random(C.byref(cfg), seed, std, int(norm_unit)))
+    def random(cls, cfg: FluxConfig, seed: int, std: float = 0.02, norm_unit: bool = False,
+               tp_rank: int = 0, tp_size: int = 1) -> "Flux":
+        if tp_size == 1:
+            return cls(lib().iris_cuda_flux_random(C.byref(cfg), seed, std, int(norm_unit)))
+        return cls(lib().iris_cuda_flux_random_tp(C.byref(cfg), seed, std, int(norm_unit), tp_rank, tp_size))
 
     def close(self):
         if self.h:
@@ -274,13 +293,19 @@ class Flux:
         return [dict(name=buf[i].name.decode(), flops=buf[i].flops, bytes=buf[i].bytes, ms=buf[i].ms)
                 for i in range(n)]
 
-    def sample_euler(self, z, txt, schedule, refs=(), txt_uncond=None, guidance=1.0):
+    def sample_euler(self, z, txt, schedule, refs=(), txt_uncond=None, guidance=1.0, cfg_pair=False):
+        """Euler sampler; cfg_pair=True splits the CFG branches over the
+        process's 2-rank communicator (comm_init)."""
         zz = np.ascontiguousarray(z, np.float32)
         tx = np.ascontiguousarray(txt, np.float32)
         sc = np.ascontiguousarray(schedule, np.float32)
         c, h, w = zz.shape
         cb = PROGRESS_CB(0)
-        if txt_uncond is not None:
+        if cfg_pair:
+            tu = np.ascontiguousarray(txt_uncond, np.float32)
+            p = lib().iris_cuda_sample_euler_cfg_pair(self.h, _f(zz), 1, c, h, w, _f(tx), tx.shape[0], _f(tu),
+                                                      tu.shape[0], guidance, _f(sc), len(sc) - 1, cb)
+        elif txt_uncond is not None:
             tu = np.ascontiguousarray(txt_uncond, np.float32)
             p = lib().iris_cuda_sample_euler_cfg(self.h, _f(zz), 1, c, h, w, _f(tx), tx.shape[0], _f(tu),
                                                  tu.shape[0], guidance, _f(sc), len(sc) - 1, cb)
@@ -294,6 +319,45 @@ class Flux:
             p = lib().iris_cuda_sample_euler(self.h, _f(zz), 1, c, h, w, _f(tx), tx.shape[0], _f(sc),
                                              len(sc) - 1, cb)
         return _take_floats(p, c * h * w, (c, h, w))
+
+
+def comm_unique_id() -> bytes:
+    """A new NCCL unique id (IRIS_CUDA_COMM_ID_BYTES bytes) for comm_init."""
+    buf = C.create_string_buffer(128)
+    if lib().iris_cuda_comm_unique_id(buf, 128):
+        raise IrisCudaError(last_error())
+    return buf.raw
+
+
+def comm_init(uid: bytes, world: int, rank: int) -> None:
+    buf = C.create_string_buffer(bytes(uid), 128)
+    if lib().iris_cuda_comm_init(buf, world, rank):
+        raise IrisCudaError(last_error())
+
+
+def comm_destroy() -> None:
+    lib().iris_cuda_comm_destroy()
+
+
+def comm_groups(world: int, group_size: int):
+    """Rank groups of `group_size` consecutive ranks ((0,1), (2,3), ... for CFG
+    pairs); every rank is in exactly one."""
+    if group_size < 1 or world % group_size:
+        raise ValueError(f"world {world} is not a multiple of group size {group_size}")
+    return [tuple(range(g, g + group_size)) for g in range(0, world, group_size)]
+
+
+def comm_init_group(exchange, rank: int, world: int, group_size: int) -> tuple:
+    """Create this rank's NCCL communicator over its group of `group_size`
+    consecutive ranks.  `exchange(obj)` must return the list of every rank's
+    obj (e.g. torch.distributed.all_gather_object); the first rank of each
+    group creates the id.  Returns (group, rank in group)."""
+    groups = comm_groups(world, group_size)
+    group = next(g for g in groups if rank in g)
+    mine = comm_unique_id() if rank == group[0] else None
+    ids = exchange(mine)
+    comm_init(ids[group[0]], len(group), group.index(rank))
+    return group, group.index(rank)
 
 
 def official_schedule(steps: int, seq: int) -> np.ndarray:
