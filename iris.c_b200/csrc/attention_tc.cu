@@ -7,22 +7,27 @@
 // iris_kernels.c:943-1048; the masked zi_attention,
 // iris_transformer_zimage.c:689-762).
 //
-// One CTA = 128 query rows of one head; keys stream in tiles of 128.
-//   warp 0      TMA producer: Q once, then K_j and V_j into two-stage rings
-//   warp 1      TMEM owner + single-thread MMA issuer:
-//                 S_j = Q K_j^T       -> TMEM columns [128 (j&1), +128)  (f32)
-//                 O  += P_{j-1} V_{j-1} -> TMEM columns [256, 384)         (f32)
-//               S_{j+1} is computed while the softmax warps work on S_j.
-//   warps 2..5  softmax: thread = query row (TMEM lane), so row max and row
-//               sum need no shuffles; P_j (bf16) goes to one of two
-//               128B-swizzled shared tiles (A operand of the P.V MMA), so the
-//               softmax of tile j overlaps P_{j-1} V_{j-1} and S_{j+1}.
-//               Lazy rescaling: a row keeps its reference max until a tile's
-//               max exceeds it by more than 2^8, so the O correction in TMEM
-//               (tcgen05.ld / st, after P_{j-1} V_{j-1} is done) is rare; O
-//               and l always share the same reference, so the result is
-//               exact.  Epilogue: O / l -> bf16 -> global.
-// V is consumed as an MN-major B operand straight from its [keys, d] layout.
+// One CTA = two 128-row query tiles (Q0, Q1) of one head; both read the same
+// K/V tiles of 128 keys, which stream through two-stage TMA rings.
+//   warp 0      TMA producer
+//   warp 1      TMEM owner + single-thread MMA issuer.  TMEM columns:
+//                 [0,128) S0 / P0   [128,256) S1 / P1   [256,384) O0   [384,512) O1
+//               Per key tile j, in issue order (the tensor pipe runs them in
+//               order, so an MMA never overtakes the one before it):
+//                 O0 += P0_j V_j,  S0_{j+1} = Q0 K_{j+1}^T,
+//                 O1 += P1_j V_j,  S1_{j+1} = Q1 K_{j+1}^T
+//               so the softmax of one query tile overlaps the MMAs of the other.
+//   warps 2..5  softmax of Q0, warps 6..9 softmax of Q1: thread = query row
+//               (TMEM lane), so row max and row sum need no shuffles.  S_j is
+//               read from TMEM, P_j = 2^(S_j - m) goes back as bf16 over the
+//               first 64 columns of the same S buffer and is the TMEM A
+//               operand of P_j V_j (V is an MN-major B operand straight from
+//               its [keys, d] layout).  Lazy rescaling: a row keeps its
+//               reference max m until a tile's max exceeds it by more than
+//               2^8; only then is O (already final for tiles < j, since the
+//               commit that signals S_j covers P_{j-1} V_{j-1}) scaled in TMEM.
+//               O and l always share the same m, so the result is exact.
+//               Epilogue: O / l -> bf16 -> global.
 // Every wait is bounded (see ptx.cuh).
 #include "iris_kernels.h"
 #include "ptx.cuh"
@@ -35,21 +40,25 @@
 
 namespace {
 
-constexpr int BQ = 128;
+constexpr int BQ = 128;             // rows per query tile; a CTA holds two
 constexpr int BKV = 128;
 constexpr int HD = 128;
 constexpr int BOX = 128 * 64 * 2;   // one 64-column swizzle box of a 128-row tile: 16 KB
 constexpr int TILE = 2 * BOX;       // 128 x 128 bf16 tile
-constexpr int OFF_Q = 0;
-constexpr int OFF_K = TILE;          // 2 stages
-constexpr int OFF_V = 3 * TILE;      // 2 stages
-constexpr int OFF_P = 5 * TILE;      // 2 buffers
-constexpr int OFF_BAR = 7 * TILE;
-constexpr int SMEM_BYTES = 7 * TILE + 256 + 1024;
-constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P values stay <= 256
-constexpr int NUM_THREADS = 192;
+constexpr int OFF_Q = 0;            // 2 query tiles
+constexpr int OFF_K = 2 * TILE;     // 2 stages
+constexpr int OFF_V = 4 * TILE;     // 2 stages
+constexpr int OFF_BAR = 6 * TILE;
+constexpr int SMEM_BYTES = 6 * TILE + 256 + 1024;
+constexpr int NUM_THREADS = 320;
 constexpr int TMEM_COLS = 512;
 constexpr float LOG2E = 1.4426950408889634f;
+constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P values stay <= 256
+// Of every 8 exponentials, this many are evaluated on the FMA pipe (exp2_fma)
+// instead of the SFU.
+#ifndef IRIS_ATTN_EMU_PER8
+#define IRIS_ATTN_EMU_PER8 0
+#endif
 
 #define IRIS_DEV_ERR_ATTN_PRODUCER 0x201
 #define IRIS_DEV_ERR_ATTN_MMA 0x202
@@ -60,9 +69,9 @@ struct AttnBars {
   uint64_t q_full;
   uint64_t k_full[2], k_empty[2];
   uint64_t v_full[2], v_empty[2];
-  uint64_t s_full[2];
-  uint64_t p_full;
-  uint64_t pv_done[2];  // P_j V_j done, by P buffer j & 1
+  uint64_t s_full[2];  // per query tile: S_j written (and every earlier MMA done)
+  uint64_t p_full[2];  // per query tile: P_j in TMEM (128 arrivals)
+  uint64_t o_done;
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
@@ -80,6 +89,21 @@ struct AttnParams {
 
 int* g_attn_status = nullptr;
 
+// 2^x for x <= 8 on the FMA/ALU pipes: x = n + f with n = rint(x) (1.5*2^23
+// rounding constant, so n also sits in the low mantissa bits of t) and
+// f in [-1/2, 1/2]; 2^f by a cubic fitted to minimise the relative error on
+// that interval (max 7.5e-5, far below bf16's 2^-9 rounding of P); 2^n is
+// added to the exponent field.  x is clamped to -125 so the result stays
+// normal (2^-125 instead of 0 for padding and masked keys: irrelevant next
+// to a row sum >= 1; padding keys also have V rows of zeros).
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fmaxf(x, -125.0f);
+  const float t = x + 12582912.0f;
+  const float f = x - (t - 12582912.0f);
+  float p = fmaf(fmaf(fmaf(0.05517145f, f, 0.24261114f), f, 0.69326103f), f, 0.99992806f);
+  return __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
@@ -93,7 +117,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int head = blockIdx.y;
-  const int q0 = blockIdx.x * BQ;
+  const int q0 = blockIdx.x * (2 * BQ);
+  const bool has1 = q0 + BQ < p.sq;  // second query tile holds rows
   const int col0 = head * HD;
   const int n = (p.sk + BKV - 1) / BKV;
 
@@ -105,10 +130,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
       iris::mbar_init(&bars->v_full[s], 1);
       iris::mbar_init(&bars->v_empty[s], 1);
       iris::mbar_init(&bars->s_full[s], 1);
+      iris::mbar_init(&bars->p_full[s], 128);
     }
-    iris::mbar_init(&bars->p_full, 128);
-    iris::mbar_init(&bars->pv_done[0], 1);
-    iris::mbar_init(&bars->pv_done[1], 1);
+    iris::mbar_init(&bars->o_done, 1);
     iris::mbar_init(&bars->drain, 1);
     bars->abort = 0;
     iris::fence_mbar_init();
@@ -124,9 +148,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer
-    iris::mbar_arrive_expect_tx(&bars->q_full, TILE);
-    iris::tma_load_2d(smem + OFF_Q, &p.tq, &bars->q_full, col0, q0);
-    iris::tma_load_2d(smem + OFF_Q + BOX, &p.tq, &bars->q_full, col0 + 64, q0);
+    iris::mbar_arrive_expect_tx(&bars->q_full, (has1 ? 2 : 1) * TILE);
+    for (int t = 0; t < (has1 ? 2 : 1); t++) {
+      iris::tma_load_2d(smem + OFF_Q + t * TILE, &p.tq, &bars->q_full, col0, q0 + t * BQ);
+      iris::tma_load_2d(smem + OFF_Q + t * TILE + BOX, &p.tq, &bars->q_full, col0 + 64, q0 + t * BQ);
+    }
     int issued = 0;  // K/V tiles issued (each arms k_full and v_full of its stage)
     bool ok = true;
     for (int j = 0; j < n && ok; j++) {
@@ -147,7 +173,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
         break;
       }
       iris::mbar_arrive_expect_tx(&bars->v_full[s], TILE);
-      iris::tma_load_2d(smem + OFF_V + s * TILE, &p.tv, &bars->v_full[s], 0 + col0, j * BKV);
+      iris::tma_load_2d(smem + OFF_V + s * TILE, &p.tv, &bars->v_full[s], col0, j * BKV);
       iris::tma_load_2d(smem + OFF_V + s * TILE + BOX, &p.tv, &bars->v_full[s], col0 + 64, j * BKV);
       issued = j + 1;
     }
@@ -165,160 +191,181 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
     // ------------------------------------------------------------ MMA issuer
     const uint32_t idesc_s = iris::umma_idesc_bf16_f32(BQ, BKV);
     const uint32_t idesc_o = iris::umma_idesc_bf16_f32_bmn(BQ, HD);
-    const uint32_t qa = iris::smem_u32(smem + OFF_Q);
-    const uint32_t pa = iris::smem_u32(smem + OFF_P);
-    bool ok = iris::mbar_wait(&bars->q_full, 0, abort_flag, p.status, IRIS_DEV_ERR_ATTN_MMA);
-    iris::tc_fence_after();
-    for (int j = 0; j <= n && ok; j++) {
-      if (j < n) {
-        int s = j & 1;
-        uint32_t u = (uint32_t)(j >> 1);
-        if (!iris::mbar_wait(&bars->k_full[s], u & 1, abort_flag, p.status, IRIS_DEV_ERR_ATTN_MMA)) {
-          ok = false;
-          break;
-        }
-        iris::tc_fence_after();
-        const uint32_t kb = iris::smem_u32(smem + OFF_K + s * TILE);
+    const int nq = has1 ? 2 : 1;
+    auto qk = [&](int t, int j) {  // S_t = Q_t K_j^T
+      const uint32_t qa = iris::smem_u32(smem + OFF_Q + t * TILE);
+      const uint32_t kb = iris::smem_u32(smem + OFF_K + (j & 1) * TILE);
 #pragma unroll
-        for (int kk = 0; kk < HD / 16; kk++) {
-          uint32_t off = (uint32_t)((kk >> 2) * BOX + (kk & 3) * 32);
-          iris::umma_bf16(tmem + s * 128, iris::umma_desc_k_sw128(qa + off),
-                          iris::umma_desc_k_sw128(kb + off), idesc_s, kk > 0);
-        }
-        iris::umma_commit(&bars->k_empty[s]);
-        iris::umma_commit(&bars->s_full[s]);
+      for (int kk = 0; kk < HD / 16; kk++) {
+        uint32_t off = (uint32_t)((kk >> 2) * BOX + (kk & 3) * 32);
+        iris::umma_bf16(tmem + t * 128, iris::umma_desc_k_sw128(qa + off), iris::umma_desc_k_sw128(kb + off),
+                        idesc_s, kk > 0);
       }
-      if (j > 0) {
-        int jj = j - 1, s = jj & 1;
-        uint32_t u = (uint32_t)(jj >> 1);
-        if (!iris::mbar_wait(&bars->p_full, (uint32_t)(jj & 1), abort_flag, p.status, IRIS_DEV_ERR_ATTN_MMA) ||
-            !iris::mbar_wait(&bars->v_full[s], u & 1, abort_flag, p.status, IRIS_DEV_ERR_ATTN_MMA)) {
-          ok = false;
-          break;
-        }
-        iris::tc_fence_after();
-        const uint32_t vb = iris::smem_u32(smem + OFF_V + s * TILE);
-        const uint32_t pb = pa + (uint32_t)(s * TILE);
+    };
+    auto pv = [&](int t, int j) {  // O_t += P_t V_j, P_t from TMEM
+      const uint32_t vb = iris::smem_u32(smem + OFF_V + (j & 1) * TILE);
 #pragma unroll
-        for (int kk = 0; kk < BKV / 16; kk++) {
-          // A: P rows, 16 keys = 32 bytes inside a 64-key swizzle box
-          uint64_t adesc = iris::umma_desc_k_sw128(pb + (uint32_t)((kk >> 2) * BOX + (kk & 3) * 32));
-          // B: V [keys, d] MN-major; 16 keys = 2 atoms of 8 rows (2048 B);
-          // the two 64-wide d chunks are BOX apart, 8-key groups 1024 B apart
-          uint64_t bdesc = iris::umma_desc_mn_sw128(vb + (uint32_t)(kk * 2048), BOX, 1024);
-          iris::umma_bf16(tmem + 256, adesc, bdesc, idesc_o, (jj > 0 || kk > 0));
-        }
-        iris::umma_commit(&bars->v_empty[s]);
-        iris::umma_commit(&bars->pv_done[s]);
+      for (int kk = 0; kk < BKV / 16; kk++) {
+        // B: V [keys, d] MN-major; 16 keys = 2 atoms of 8 rows (2048 B);
+        // the two 64-wide d chunks are BOX apart, 8-key groups 1024 B apart
+        uint64_t bdesc = iris::umma_desc_mn_sw128(vb + (uint32_t)(kk * 2048), BOX, 1024);
+        iris::umma_bf16_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, bdesc, idesc_o, (j > 0 || kk > 0));
       }
+    };
+    bool ok = iris::mbar_wait(&bars->q_full, 0, abort_flag, p.status, IRIS_DEV_ERR_ATTN_MMA) &&
+              iris::mbar_wait(&bars->k_full[0], 0, abort_flag, p.status, IRIS_DEV_ERR_ATTN_MMA);
+    if (ok) {
+      iris::tc_fence_after();
+      for (int t = 0; t < nq; t++) {
+        qk(t, 0);
+        iris::umma_commit(&bars->s_full[t]);
+      }
+      iris::umma_commit(&bars->k_empty[0]);
     }
-    if (!ok) {
+    for (int j = 0; j < n && ok; j++) {
+      const int s = j & 1;
+      const bool more = j + 1 < n;
+      if (!iris::mbar_wait(&bars->v_full[s], (uint32_t)((j >> 1) & 1), abort_flag, p.status, IRIS_DEV_ERR_ATTN_MMA) ||
+          (more && !iris::mbar_wait(&bars->k_full[(j + 1) & 1], (uint32_t)(((j + 1) >> 1) & 1), abort_flag, p.status,
+                                    IRIS_DEV_ERR_ATTN_MMA))) {
+        ok = false;
+        break;
+      }
+      for (int t = 0; t < nq; t++) {
+        if (!iris::mbar_wait(&bars->p_full[t], (uint32_t)(j & 1), abort_flag, p.status, IRIS_DEV_ERR_ATTN_MMA)) {
+          ok = false;
+          break;
+        }
+        iris::tc_fence_after();
+        pv(t, j);
+        if (more) {
+          qk(t, j + 1);
+          iris::umma_commit(&bars->s_full[t]);
+        }
+      }
+      if (!ok) break;
+      iris::umma_commit(&bars->v_empty[s]);
+      if (more) iris::umma_commit(&bars->k_empty[(j + 1) & 1]);
+    }
+    if (ok) {
+      iris::umma_commit(&bars->o_done);
+    } else {
       iris::umma_commit(&bars->drain);
       volatile int no_abort = 0;
       iris::mbar_wait(&bars->drain, 0, &no_abort, p.status, IRIS_DEV_ERR_ATTN_DRAIN);
     }
-  } else if (warp >= 2) {
+  } else if (warp >= 2 && (warp < 6 || has1)) {
     // ------------------------------------------------------------ softmax + epilogue
+    const int t = warp >= 6 ? 1 : 0;  // query tile
     const int quarter = warp & 3;
     const int r = quarter * 32 + lane;  // query row within the tile = TMEM lane
     const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+    const uint32_t s_addr = tmem + lane_off + t * 128;
+    const uint32_t o_addr = tmem + lane_off + 256 + t * 128;
     float m = -INFINITY, l = 0.f;  // reference max (scaled, log2 units) and row sum
     bool ok = true;
-    for (int j = 0; j < n && ok; j++) {
-      const int b = j & 1;
-      if (!iris::mbar_wait(&bars->s_full[b], (uint32_t)((j >> 1) & 1), abort_flag, p.status,
-                           IRIS_DEV_ERR_ATTN_SOFTMAX)) {
-        ok = false;
-        break;
-      }
-      iris::tc_fence_after();
-      float s[BKV];
-      iris::tmem_ld64(tmem + b * 128 + lane_off, s);
-      iris::tmem_ld64(tmem + b * 128 + lane_off + 64, s + 64);
-      const int kbase = j * BKV;
-      // full tiles stay raw (scale folded into the exponent's FMA); ragged or
-      // masked tiles are scaled here so that padding can be set in log2 units
-      float sc = p.scale_log2, tmax = -INFINITY;
-      if (kbase + BKV <= p.sk && !p.kmask) {
+    // S row -> scaled logits (log2 units): padding keys -inf, masked keys
+    // -1e9 (in natural-log units, as the reference's masked softmax)
+    auto logit = [&](float sv, int key, bool full) -> float {
+      if (full) return sv * p.scale_log2;
+      if (key >= p.sk) return -INFINITY;
+      if (p.kmask && !p.kmask[key]) return -1e9f * LOG2E;
+      return sv * p.scale_log2;
+    };
+    // exponentials of 64 keys (half h of the tile) against reference max -nm
+    // -> 32 packed bf16 words; returns the largest exponent argument
+    auto half_exps = [&](int h, int kbase, bool full, float nm, uint32_t* pw, float* rsum) -> float {
+      float sv[64];
+      iris::tmem_ld64(s_addr + 64 * h, sv);
+      float xm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll
-        for (int i = 0; i < BKV; i++) tmax = fmaxf(tmax, s[i]);
-        tmax *= sc;
-      } else {
-#pragma unroll
-        for (int i = 0; i < BKV; i++) {
-          int key = kbase + i;
-          float v = s[i] * p.scale_log2;
-          if (key >= p.sk) v = -INFINITY;
-          else if (p.kmask && !p.kmask[key]) v = -1e9f * LOG2E;
-          s[i] = v;
-          tmax = fmaxf(tmax, v);
-        }
-        sc = 1.0f;
-      }
-      const bool grow = tmax > m + RESCALE_THRESHOLD;
-      const float m_new = grow ? tmax : m;
-      const float alpha = (grow && m != -INFINITY) ? iris::ex2_approx(m - m_new) : (grow ? 0.f : 1.f);
-      // O holds P_0..P_{j-1} V: correct it once P_{j-1} V_{j-1} is in (warp-uniform:
-      // tcgen05.ld / st are collective)
-      if (j > 0 && __any_sync(0xffffffffu, grow)) {
-        if (!iris::mbar_wait(&bars->pv_done[(j - 1) & 1], (uint32_t)(((j - 1) >> 1) & 1), abort_flag, p.status,
-                             IRIS_DEV_ERR_ATTN_SOFTMAX)) {
-          ok = false;
-          break;
-        }
-        iris::tc_fence_after();
-#pragma unroll 1
-        for (int c = 0; c < 4; c++) {
-          float o[32];
-          iris::tmem_ld32(tmem + 256 + lane_off + 32 * c, o);
-#pragma unroll
-          for (int e = 0; e < 32; e++) o[e] *= alpha;
-          iris::tmem_st32(tmem + 256 + lane_off + 32 * c, o);
-        }
-      }
-      m = m_new;
-      const float nm = (m == -INFINITY) ? 0.f : -m;
-      // P buffer b was last read by P_{j-2} V_{j-2}
-      if (j >= 2 && !iris::mbar_wait(&bars->pv_done[b], (uint32_t)(((j - 2) >> 1) & 1), abort_flag, p.status,
-                                     IRIS_DEV_ERR_ATTN_SOFTMAX)) {
-        ok = false;
-        break;
-      }
-      uint8_t* prow = smem + OFF_P + b * TILE + r * 128;
-      float rs = 0.f;
-#pragma unroll
-      for (int c16 = 0; c16 < 16; c16++) {  // 8 keys = one 16-byte chunk
+      for (int c = 0; c < 8; c++) {
         float e[8];
 #pragma unroll
-        for (int t = 0; t < 8; t++) {
-          e[t] = iris::ex2_approx(fmaf(s[c16 * 8 + t], sc, nm));
-          rs += e[t];
+        for (int u = 0; u < 8; u++) {
+          const int i = c * 8 + u;
+          const float x = full ? fmaf(sv[i], p.scale_log2, nm) : logit(sv[i], kbase + 64 * h + i, false) + nm;
+          xm[u & 3] = fmaxf(xm[u & 3], x);
+          e[u] = (u < IRIS_ATTN_EMU_PER8) ? exp2_fma(x) : iris::ex2_approx(x);
+          rsum[u] += e[u];
         }
-        uint4 w;
-        w.x = pack_bf16(e[0], e[1]);
-        w.y = pack_bf16(e[2], e[3]);
-        w.z = pack_bf16(e[4], e[5]);
-        w.w = pack_bf16(e[6], e[7]);
-        int box = c16 >> 3, ch = c16 & 7;
-        *reinterpret_cast<uint4*>(prow + box * BOX + ((ch ^ (r & 7)) << 4)) = w;
+#pragma unroll
+        for (int u = 0; u < 4; u++) pw[c * 4 + u] = pack_bf16(e[2 * u], e[2 * u + 1]);
       }
+      return fmaxf(fmaxf(xm[0], xm[1]), fmaxf(xm[2], xm[3]));
+    };
+    for (int j = 0; j < n; j++) {
+      if (!iris::mbar_wait(&bars->s_full[t], (uint32_t)(j & 1), abort_flag, p.status, IRIS_DEV_ERR_ATTN_SOFTMAX)) {
+        ok = false;
+        break;
+      }
+      iris::tc_fence_after();
+      const int kbase = j * BKV;
+      const bool full = kbase + BKV <= p.sk && !p.kmask;
+      uint32_t pw[BKV / 2];
+      float rsum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+      float alpha = 1.f;
+      // fast path: P against the current reference max; it stands unless a
+      // logit exceeds it by more than the threshold (m = -inf: first tile)
+      bool redo = true;
+      if (m != -INFINITY) {
+        const float nm = -m;
+        const float x0 = half_exps(0, kbase, full, nm, pw, rsum);
+        const float x1 = half_exps(1, kbase, full, nm, pw + 32, rsum);
+        redo = __any_sync(0xffffffffu, fmaxf(x0, x1) > RESCALE_THRESHOLD);
+      }
+      if (redo) {
+        // slow path (warp-uniform): row max of the tile, new reference, O
+        // correction, P again
+        float tm[8];
+#pragma unroll
+        for (int i = 0; i < 8; i++) tm[i] = -INFINITY;
+#pragma unroll
+        for (int h = 0; h < 2; h++) {
+          float sv[64];
+          iris::tmem_ld64(s_addr + 64 * h, sv);
+#pragma unroll
+          for (int i = 0; i < 64; i++) tm[i & 7] = fmaxf(tm[i & 7], logit(sv[i], kbase + 64 * h + i, full));
+        }
+        const float tmax = fmaxf(fmaxf(fmaxf(tm[0], tm[1]), fmaxf(tm[2], tm[3])),
+                                 fmaxf(fmaxf(tm[4], tm[5]), fmaxf(tm[6], tm[7])));
+        const bool grow = tmax > m + RESCALE_THRESHOLD;
+        const float m_new = grow ? tmax : m;
+        alpha = (grow && m != -INFINITY) ? iris::ex2_approx(m - m_new) : (grow ? 0.f : 1.f);
+        // O = P_0..P_{j-1} V is final here (the commit behind s_full covers
+        // P_{j-1} V_{j-1})
+        if (j > 0) {
+#pragma unroll 1
+          for (int c = 0; c < 4; c++) {
+            float o[32];
+            iris::tmem_ld32(o_addr + 32 * c, o);
+#pragma unroll
+            for (int e = 0; e < 32; e++) o[e] *= alpha;
+            iris::tmem_st32(o_addr + 32 * c, o);
+          }
+        }
+        m = m_new;
+        const float nm = (m == -INFINITY) ? 0.f : -m;
+#pragma unroll
+        for (int i = 0; i < 8; i++) rsum[i] = 0.f;
+        half_exps(0, kbase, full, nm, pw, rsum);
+        half_exps(1, kbase, full, nm, pw + 32, rsum);
+      }
+      iris::tmem_st64(s_addr, pw);  // P_j over the first 64 columns of S_j
+      const float rs = ((rsum[0] + rsum[1]) + (rsum[2] + rsum[3])) + ((rsum[4] + rsum[5]) + (rsum[6] + rsum[7]));
       l = l * alpha + rs;
-      iris::fence_proxy_async_smem();
       iris::tc_fence_before();
-      iris::mbar_arrive(&bars->p_full);
+      iris::mbar_arrive(&bars->p_full[t]);
     }
-    // the last commit covers every earlier MMA of this CTA
-    if (ok && n > 0 &&
-        iris::mbar_wait(&bars->pv_done[(n - 1) & 1], (uint32_t)(((n - 1) >> 1) & 1), abort_flag, p.status,
-                        IRIS_DEV_ERR_ATTN_SOFTMAX)) {
+    if (ok && n > 0 && iris::mbar_wait(&bars->o_done, 0, abort_flag, p.status, IRIS_DEV_ERR_ATTN_SOFTMAX)) {
       iris::tc_fence_after();
       const float inv = l > 0.f ? 1.0f / l : 0.f;
-      const int row = q0 + r;
+      const int row = q0 + t * BQ + r;
       __nv_bfloat16* dst = p.o + (size_t)row * p.ldo + col0;
 #pragma unroll 1
       for (int c = 0; c < 4; c++) {
         float o[32];
-        iris::tmem_ld32(tmem + 256 + lane_off + 32 * c, o);
+        iris::tmem_ld32(o_addr + 32 * c, o);
         if (row < p.sq) {
           uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * c);
 #pragma unroll
@@ -377,7 +424,7 @@ extern "C" cudaError_t iris_launch_attention_tc(const void* q, int ldq, const vo
   p.scale_log2 = scale * LOG2E;
   p.kmask = key_mask;
   p.status = g_attn_status;
-  dim3 grid((sq + BQ - 1) / BQ, heads);
+  dim3 grid((sq + 2 * BQ - 1) / (2 * BQ), heads);
   attn_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(p);
   return cudaGetLastError();
 }

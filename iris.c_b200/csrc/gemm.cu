@@ -20,6 +20,8 @@
 #include "ptx.cuh"
 
 #include <cuda_bf16.h>
+#include <stdlib.h>
+#include <string.h>
 
 namespace {
 
@@ -189,6 +191,24 @@ __device__ __forceinline__ void epi_plain_chunk(const IrisGemmParams& p, uint32_
   }
 }
 
+// Epilogue of one accumulator tile for this thread's row (all modes).
+__device__ __forceinline__ void epi_tile(const IrisGemmParams& p, uint32_t taddr, int g, int row, int row_local,
+                                         bool valid, int n0) {
+  bool swiglu_tile = (p.mode == IRIS_EPI_SWIGLU) || (p.mode == IRIS_EPI_SINGLE && n0 >= p.swiglu_base);
+  if (swiglu_tile) {
+    epi_swiglu_tile(p, taddr, row, valid, n0);
+  } else {
+    for (int c = 0; c < p.bn / 128; c++) {
+      int col0 = n0 + c * 128;
+      if (col0 >= p.N) break;
+      if (p.mode == IRIS_EPI_QKV || p.mode == IRIS_EPI_SINGLE)
+        epi_qkv_chunk(p, taddr + c * 128, g, row, valid, col0);
+      else
+        epi_plain_chunk(p, taddr + c * 128, g, row, row_local, valid, col0);
+    }
+  }
+}
+
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -249,7 +269,8 @@ gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
         uint8_t* sb = sa + A_BYTES;
         iris::mbar_arrive_expect_tx(&bars->full[stage], A_BYTES + b_bytes);
         iris::tma_load_2d(sa, &p.tmap_a, &bars->full[stage], kb * BK, arow);
-        iris::tma_load_2d(sb, &p.tmap_b[g], &bars->full[stage], kb * BK, n0);
+        for (int h = 0; h < p.bn / 128; h++)  // weight tensor maps have 128-row boxes
+          iris::tma_load_2d(sb + h * (128 * BK * 2), &p.tmap_b[g], &bars->full[stage], kb * BK, n0 + 128 * h);
         issued++;
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
       }
@@ -321,21 +342,7 @@ gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
       bool valid = row_local < p.rows[g];
       int row = p.row0[g] + row_local;
       uint32_t taddr = tmem_base + buf * 256 + ((uint32_t)(quarter * 32) << 16);
-
-      bool swiglu_tile = (p.mode == IRIS_EPI_SWIGLU) ||
-                         (p.mode == IRIS_EPI_SINGLE && n0 >= p.swiglu_base);
-      if (swiglu_tile) {
-        epi_swiglu_tile(p, taddr, row, valid, n0);
-      } else {
-        for (int c = 0; c < p.bn / 128; c++) {
-          int col0 = n0 + c * 128;
-          if (col0 >= p.N) break;
-          if (p.mode == IRIS_EPI_QKV || p.mode == IRIS_EPI_SINGLE)
-            epi_qkv_chunk(p, taddr + c * 128, g, row, valid, col0);
-          else
-            epi_plain_chunk(p, taddr + c * 128, g, row, row_local, valid, col0);
-        }
-      }
+      epi_tile(p, taddr, g, row, row_local, valid, n0);
       iris::tc_fence_before();
       iris::mbar_arrive(&bars->tempty[buf]);
     }
@@ -345,6 +352,175 @@ gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
   if (warp == 1) {
     iris::tc_fence_after();
     iris::tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+
+// ---------------------------------------------------------------------------
+// CTA-pair variant (cluster of 2, cta_group::2): one MMA of M = 256, N = 256
+// per K step, issued by the even CTA over both CTAs' shared memory.  Each CTA
+// loads its own 128 rows of A and its own 128-row half of the weight tile, so
+// per CTA and K step the tensor cores read 8 KB of shared memory instead of
+// 12 KB and the weights cross L2 once per 256 rows instead of per 128.  Each
+// CTA's TMEM holds the accumulator of its own 128 rows; both epilogues run as
+// in the single-CTA kernel.
+constexpr int BM2 = 256;
+constexpr int STAGES2 = 6;
+constexpr int STAGE2_BYTES = A_BYTES + 128 * BK * 2;  // 32 KB
+constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + 1024;
+
+struct Bars2 {
+  uint64_t full[STAGES2];   // even CTA: both CTAs' tiles of the stage landed (2 arrivals + bytes)
+  uint64_t empty[STAGES2];  // each CTA: the pair MMA released the stage
+  uint64_t tfull[2];        // each CTA: accumulator ready
+  uint64_t tempty[2];       // even CTA: both epilogues drained the accumulator (8 warp arrivals)
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+gemm_tc2_kernel(const __grid_constant__ IrisGemmParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  Bars2* bars = reinterpret_cast<Bars2*>(smem + STAGES2 * STAGE2_BYTES);
+  volatile int* abort_flag = &bars->abort;
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const uint32_t rank = iris::cluster_ctarank();
+  const int pair = blockIdx.x >> 1, npairs = gridDim.x >> 1;
+
+  const int mt0 = (p.rows[0] + BM2 - 1) / BM2;
+  const int mt1 = p.ngroups > 1 ? (p.rows[1] + BM2 - 1) / BM2 : 0;
+  const int mtot = mt0 + mt1;
+  const int ntiles_n = (p.N + p.bn - 1) / p.bn;
+  const int total = mtot * ntiles_n;
+  const int num_kb = (p.K + BK - 1) / BK;
+  const uint32_t idesc = iris::umma_idesc_bf16_f32(BM2, 256);
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES2; s++) {
+      iris::mbar_init(&bars->full[s], 2);
+      iris::mbar_init(&bars->empty[s], 1);
+    }
+    for (int b = 0; b < 2; b++) {
+      iris::mbar_init(&bars->tfull[b], 1);
+      iris::mbar_init(&bars->tempty[b], 8);
+    }
+    iris::mbar_init(&bars->drain, 1);
+    bars->abort = 0;
+    iris::fence_mbar_init();
+    iris::tma_prefetch_desc(&p.tmap_a);
+    iris::tma_prefetch_desc(&p.tmap_b[0]);
+    if (p.ngroups > 1) iris::tma_prefetch_desc(&p.tmap_b[1]);
+  }
+  if (warp == 1) iris::tmem_alloc_pair(&bars->tmem_base, TMEM_COLS);
+  iris::tc_fence_before();
+  __syncthreads();
+  iris::cluster_sync();  // both CTAs' barriers are initialised before any remote arrive
+  iris::tc_fence_after();
+  const uint32_t tmem_base = bars->tmem_base;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------ TMA producer (both CTAs)
+    int stage = 0;
+    uint32_t phase = 0;
+    bool ok = true, issued_any = false;
+    for (int t = pair; t < total && ok; t += npairs) {
+      int g, ml, n0;
+      tile_coords(p, t, mt0, mtot, g, ml, n0);
+      const int arow = p.row0[g] + ml * BM2 + 128 * (int)rank;
+      const int brow = n0 + 128 * (int)rank;
+      for (int kb = 0; kb < num_kb; kb++) {
+        if (!iris::mbar_wait(&bars->empty[stage], phase ^ 1, abort_flag, p.status, IRIS_DEV_ERR_GEMM_PRODUCER)) {
+          ok = false;
+          break;
+        }
+        uint8_t* sa = smem + stage * STAGE2_BYTES;
+        uint8_t* sb = sa + A_BYTES;
+        const uint32_t full_c = iris::mapa_shared(&bars->full[stage], 0);
+        iris::mbar_arrive_expect_tx_cluster(full_c, STAGE2_BYTES);
+        iris::tma_load_2d_pair(sa, &p.tmap_a, full_c, kb * BK, arow);
+        iris::tma_load_2d_pair(sb, &p.tmap_b[g], full_c, kb * BK, brow);
+        issued_any = true;
+        if (++stage == STAGES2) { stage = 0; phase ^= 1; }
+      }
+    }
+    if (!ok && issued_any) {
+      // the stage barriers live in the even CTA: give copies still in flight
+      // (microseconds) time to land before this CTA can exit
+      const uint64_t t0 = iris::globaltimer();
+      while (iris::globaltimer() - t0 < 50000ull) {
+      }
+    }
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    // ------------------------------------------------ MMA issuer (even CTA)
+    int stage = 0;
+    uint32_t phase = 0;
+    int it = 0;
+    bool ok = true;
+    for (int t = pair; t < total && ok; t += npairs, it++) {
+      int buf = it & 1;
+      uint32_t use = (uint32_t)(it >> 1);
+      if (!iris::mbar_wait(&bars->tempty[buf], (use & 1) ^ 1, abort_flag, p.status, IRIS_DEV_ERR_GEMM_MMA)) {
+        ok = false;
+        break;
+      }
+      iris::tc_fence_after();
+      uint32_t d_tmem = tmem_base + buf * 256;
+      for (int kb = 0; kb < num_kb; kb++) {
+        if (!iris::mbar_wait(&bars->full[stage], phase, abort_flag, p.status, IRIS_DEV_ERR_GEMM_MMA)) {
+          ok = false;
+          break;
+        }
+        iris::tc_fence_after();
+        uint32_t sa = iris::smem_u32(smem + stage * STAGE2_BYTES);
+        uint32_t sb = sa + A_BYTES;
+        uint64_t adesc = iris::umma_desc_k_sw128(sa);
+        uint64_t bdesc = iris::umma_desc_k_sw128(sb);
+#pragma unroll
+        for (int kk = 0; kk < BK / 16; kk++)
+          iris::umma_bf16_pair(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0);
+        iris::umma_commit_pair(&bars->empty[stage]);
+        if (++stage == STAGES2) { stage = 0; phase ^= 1; }
+      }
+      if (ok) iris::umma_commit_pair(&bars->tfull[buf]);
+    }
+    if (!ok) {
+      iris::umma_commit_pair(&bars->drain);
+      volatile int no_abort = 0;
+      iris::mbar_wait(&bars->drain, 0, &no_abort, p.status, IRIS_DEV_ERR_GEMM_DRAIN);
+    }
+  } else if (warp >= 2) {
+    // ------------------------------------------------ epilogue (both CTAs)
+    const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    const uint32_t tempty_c0 = iris::mapa_shared(&bars->tempty[0], 0);
+    const uint32_t tempty_c1 = iris::mapa_shared(&bars->tempty[1], 0);
+    int it = 0;
+    for (int t = pair; t < total; t += npairs, it++) {
+      int buf = it & 1;
+      uint32_t use = (uint32_t)(it >> 1);
+      if (!iris::mbar_wait(&bars->tfull[buf], use & 1, abort_flag, p.status, IRIS_DEV_ERR_GEMM_EPILOGUE)) break;
+      iris::tc_fence_after();
+      int g, ml, n0;
+      tile_coords(p, t, mt0, mtot, g, ml, n0);
+      int row_local = ml * BM2 + 128 * (int)rank + quarter * 32 + lane;
+      bool valid = row_local < p.rows[g];
+      int row = p.row0[g] + row_local;
+      uint32_t taddr = tmem_base + buf * 256 + ((uint32_t)(quarter * 32) << 16);
+      epi_tile(p, taddr, g, row, row_local, valid, n0);
+      iris::tc_fence_before();
+      __syncwarp();
+      if (lane == 0) iris::mbar_arrive_cluster(buf ? tempty_c1 : tempty_c0);
+    }
+  }
+
+  __syncthreads();
+  iris::cluster_sync();  // no CTA leaves while the pair MMA may still read its shared memory
+  if (warp == 1) {
+    iris::tc_fence_after();
+    iris::tmem_dealloc_pair(tmem_base, TMEM_COLS);
   }
 }
 
@@ -369,7 +545,9 @@ extern "C" int iris_make_tmap_bf16(CUtensorMap* m, const void* ptr, uint64_t row
     return -2;
   cuuint64_t dims[2] = {cols, rows};
   cuuint64_t strides[1] = {ld * 2};
-  cuuint32_t box[2] = {64, box_rows};
+  // 128-row boxes at most: a 256-row weight tile is loaded as two boxes (the
+  // swizzled layout of two stacked 128-row boxes equals one 256-row box)
+  cuuint32_t box[2] = {64, box_rows > 128 ? 128u : box_rows};
   cuuint32_t estr[2] = {1, 1};
   CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void*>(ptr), dims, strides,
                   box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
@@ -378,11 +556,32 @@ extern "C" int iris_make_tmap_bf16(CUtensorMap* m, const void* ptr, uint64_t row
 }
 
 static bool g_gemm_attr = false;
+static int g_max_pairs = 0;  // CTA pairs that can be resident at once
 
 extern "C" cudaError_t iris_gemm_init(void) {
   if (g_gemm_attr) return cudaSuccess;
   cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        SMEM_BYTES);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gemm_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
+  if (e == cudaSuccess) {
+    // clusters are placed within GPCs: ask how many pairs fit at once rather
+    // than assuming SMs / 2 (a persistent grid larger than that would run its
+    // last pairs after the others)
+    int dev = 0, sms = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaLaunchConfig_t cfg;
+    memset(&cfg, 0, sizeof(cfg));
+    cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
+    cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+    cfg.dynamicSmemBytes = SMEM2_BYTES;
+    int n = 0;
+    e = cudaOccupancyMaxActiveClusters(&n, gemm_tc2_kernel, &cfg);
+    g_max_pairs = (e == cudaSuccess && n > 0) ? n : 0;
+    e = cudaSuccess;
+    cudaGetLastError();
+  }
   if (e == cudaSuccess) g_gemm_attr = true;
   return e;
 }
@@ -394,6 +593,20 @@ extern "C" cudaError_t iris_launch_gemm(const IrisGemmParams* p, int num_sms, cu
   }
   if (p->bn != 128 && p->bn != 256) return cudaErrorInvalidValue;
   if (p->K % BK != 0 || p->N % 128 != 0) return cudaErrorInvalidValue;
+  static int mode = -1;  // IRIS_GEMM=1cta keeps every launch on the single-CTA kernel
+  if (mode < 0) {
+    const char* e = getenv("IRIS_GEMM");
+    mode = (e && strcmp(e, "1cta") == 0) ? 1 : 0;
+  }
+  const int rows = p->rows[0] + (p->ngroups > 1 ? p->rows[1] : 0);
+  if (mode == 0 && p->bn == 256 && rows >= 512 && g_max_pairs > 0) {
+    int mt = (p->rows[0] + BM2 - 1) / BM2 + (p->ngroups > 1 ? (p->rows[1] + BM2 - 1) / BM2 : 0);
+    long total = (long)mt * ((p->N + 255) / 256);
+    long cap = g_max_pairs < num_sms / 2 ? g_max_pairs : num_sms / 2;
+    long pairs = total < cap ? total : cap;
+    gemm_tc2_kernel<<<(int)(2 * pairs), NUM_THREADS, SMEM2_BYTES, stream>>>(*p);
+    return cudaGetLastError();
+  }
   int mt = (p->rows[0] + BM - 1) / BM + (p->ngroups > 1 ? (p->rows[1] + BM - 1) / BM : 0);
   long total = (long)mt * ((p->N + p->bn - 1) / p->bn);
   if (total <= 0) return cudaSuccess;

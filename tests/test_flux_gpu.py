@@ -132,3 +132,20 @@ def test_random_init_model_matches_oracle(iris):
     v = m.forward(lat, ctx, 0.5)
     assert rel_l2(v, fo.forward(w, cfg, lat, ctx, 0.5)) < TOL
     m.close()
+
+
+def test_long_sequence_matches_oracle(iris):
+    """677 rows (77 text + 600 image): every linear with N % 256 == 0 runs on
+    the CTA-pair GEMM with its fused epilogue (QKV norm/RoPE, SwiGLU, gated
+    residual, single-block split), with ragged row groups."""
+    cfg = dict(num_attention_heads=2, attention_head_dim=128, num_layers=1, num_single_layers=1,
+               joint_attention_dim=64, in_channels=128, mlp_ratio=3.0, rope_theta=2000.0)
+    m = iris.Flux.random(iris.FluxConfig.from_hf(cfg), seed=12, std=0.04, norm_unit=True)
+    w = {n: mg.bf16_bits_to_f32(m.read_weight(n, shp)) for n, shp, _ in mg.flux_tensor_specs(cfg)}
+    rng = np.random.default_rng(3)
+    lat = rng.standard_normal((128, 20, 30)).astype(np.float32)
+    ctx = rng.standard_normal((77, 64)).astype(np.float32)
+    v = m.forward(lat, ctx, 0.6)
+    assert rel_l2(v, fo.forward(w, cfg, lat, ctx, 0.6)) < TOL
+    m.close()
+

@@ -19,6 +19,10 @@ SHAPES = [
     (1, 64, 128), (7, 128, 128), (128, 64, 256), (128, 128, 256), (129, 192, 384),
     (300, 256, 512), (512, 3072, 3072), (1024, 3072, 9216), (1536, 12288, 3072),
     (80, 7680, 3072), (16, 128, 3072), (1024, 3072, 128),
+    # >= 512 rows with N % 256 == 0 run on the CTA-pair kernel (M tiles of
+    # 256 rows); ragged row counts leave the odd CTA of the last pair partly
+    # or wholly past the end
+    (600, 512, 768), (777, 192, 512), (2000, 1024, 2304), (640, 3072, 256),
 ]
 
 

@@ -70,3 +70,19 @@ def test_zimage_random_init_runs(iris):
                   rng.standard_normal((33, 64)).astype(np.float32), 0.5)
     assert v.shape == (16, 12, 8) and np.isfinite(v).all() and np.abs(v).max() > 0
     m.close()
+
+
+def test_zimage_long_sequence_matches_oracle(iris, tmp_path):
+    """576 image + 64 caption rows: the CTA-pair GEMM under every Z-Image
+    linear with N % 256 == 0."""
+    cfg = dict(dim=256, n_heads=2, n_layers=1, n_refiner=1, cap_feat_dim=64, in_channels=16, patch_size=2,
+               rope_theta=256.0, axes_dims=[32, 48, 48], ffn_dim=768, adaln_dim=256, t_mid=256)
+    w = mg.make_zimage_model(str(tmp_path), cfg, 8, 0.04, "unit")
+    m = iris.ZImage.load(str(tmp_path))
+    rng = np.random.default_rng(5)
+    lat = rng.standard_normal((16, 48, 48)).astype(np.float32)
+    cap = rng.standard_normal((60, 64)).astype(np.float32)
+    v = m.forward(lat, cap, 0.4)
+    assert rel_l2(v, zo.forward(w, cfg, lat, cap, 0.4)) < TOL
+    m.close()
+
