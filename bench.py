@@ -92,6 +92,24 @@ def dist_init(world, backend="nccl", device=None):
     return dist
 
 
+def by_name(prof):
+    """Per launch name of one forward: launches, ms, and TFLOP/s or GB/s."""
+    out = {}
+    for e in prof:
+        d = out.setdefault(e["name"], {"launches": 0, "ms": 0.0, "flops": 0.0, "bytes": 0.0})
+        d["launches"] += 1
+        d["ms"] += e["ms"]
+        d["flops"] += e["flops"]
+        d["bytes"] += e["bytes"]
+    for d in out.values():
+        sec = d["ms"] / 1000.0
+        d["tflops"] = d["flops"] / sec / 1e12 if d["flops"] and sec else None
+        d["gbs"] = d["bytes"] / sec / 1e9 if d["bytes"] and sec else None
+        d["ms"] = round(d["ms"], 4)
+        del d["flops"], d["bytes"]
+    return out
+
+
 def reduce_sum(value: float, world: int, device=None) -> float:
     if world <= 1:
         return value
@@ -402,7 +420,8 @@ def run_ours(args):
                 "attention_tflops": a_fl / (a_ms / 1000.0) / 1e12 if a_ms else None,
                 "forward_ms_unfused_launches": step_ms,
                 "share": {"gemm": g_ms / step_ms, "attention": a_ms / step_ms,
-                          "other": 1 - (g_ms + a_ms) / step_ms}}
+                          "other": 1 - (g_ms + a_ms) / step_ms},
+                "by_launch_name": by_name(prof)}
 
     # ---- CPU baseline (rank 0, N=1 only)
     cpu = None

@@ -46,14 +46,20 @@ constexpr int HD = 128;
 constexpr int BOX = 128 * 64 * 2;   // one 64-column swizzle box of a 128-row tile: 16 KB
 constexpr int TILE = 2 * BOX;       // 128 x 128 bf16 tile
 constexpr int OFF_Q = 0;            // 2 query tiles
-constexpr int OFF_K = 2 * TILE;     // 2 stages
-constexpr int OFF_V = 4 * TILE;     // 2 stages
-constexpr int OFF_BAR = 6 * TILE;
-constexpr int SMEM_BYTES = 6 * TILE + 256 + 1024;
+constexpr int KST = 2;              // K ring stages
+constexpr int VST = 3;              // V ring stages (V_j is released half a key tile after K_j)
+constexpr int OFF_K = 2 * TILE;
+constexpr int OFF_V = OFF_K + KST * TILE;
+constexpr int OFF_BAR = OFF_V + VST * TILE;
+constexpr int SMEM_BYTES = OFF_BAR + 256 + 1024;
 constexpr int NUM_THREADS = 320;
 constexpr int TMEM_COLS = 512;
 constexpr float LOG2E = 1.4426950408889634f;
-constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P values stay <= 256
+constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: a new reference max moves P by >= 2^8
+// A tile whose row sum against the current reference stays <= 2^16 has every
+// P <= 2^16, which bf16 P and the f32 O / l accumulators take as they are;
+// only larger sums send the row's warp to the exact max / rescale path.
+constexpr float FAST_SUM_LIMIT = 65536.0f;
 // Of every 8 exponentials, this many are evaluated on the FMA pipe (exp2_fma)
 // instead of the SFU.
 #ifndef IRIS_ATTN_EMU_PER8
@@ -67,8 +73,8 @@ constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: P values stay <= 256
 
 struct AttnBars {
   uint64_t q_full;
-  uint64_t k_full[2], k_empty[2];
-  uint64_t v_full[2], v_empty[2];
+  uint64_t k_full[KST], k_empty[KST];
+  uint64_t v_full[VST], v_empty[VST];
   uint64_t s_full[2];  // per query tile: S_j written (and every earlier MMA done)
   uint64_t p_full[2];  // per query tile: P_j in TMEM (128 arrivals)
   uint64_t o_done;
@@ -109,6 +115,38 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// Two keys of a full tile in one go, on Blackwell's paired f32 ops:
+//   x = s * scale + nm (fma.f32x2), e = 2^x (SFU), row-sum accumulator += e
+//   (add.f32x2), P pair -> bf16x2: 5 instructions for 2 keys.  The softmax
+//   is bound by instruction issue, not by one pipe, so every one counts.
+__device__ __forceinline__ uint32_t exp_pair(float s0, float s1, uint64_t sc2, uint64_t nm2, uint64_t& acc) {
+  uint32_t pw;
+  asm("{\n\t.reg .b64 sv, xv, ev;\n\t.reg .f32 x0, x1, e0, e1;\n\t"
+      "mov.b64 sv, {%2, %3};\n\t"
+      "fma.rn.f32x2 xv, sv, %4, %5;\n\t"
+      "mov.b64 {x0, x1}, xv;\n\t"
+      "ex2.approx.ftz.f32 e0, x0;\n\t"
+      "ex2.approx.ftz.f32 e1, x1;\n\t"
+      "mov.b64 ev, {e0, e1};\n\t"
+      "add.rn.f32x2 %1, %1, ev;\n\t"
+      "cvt.rn.bf16x2.f32 %0, e1, e0;\n\t}"
+      : "=r"(pw), "+l"(acc)
+      : "f"(s0), "f"(s1), "l"(sc2), "l"(nm2));
+  return pw;
+}
+
+__device__ __forceinline__ uint64_t f32x2(float a, float b) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(a), "f"(b));
+  return r;
+}
+
+__device__ __forceinline__ float sum_f32x2(uint64_t v) {
+  float a, b;
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(a), "=f"(b) : "l"(v));
+  return a + b;
+}
+
 __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -124,11 +162,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
 
   if (threadIdx.x == 0) {
     iris::mbar_init(&bars->q_full, 1);
-    for (int s = 0; s < 2; s++) {
+    for (int s = 0; s < KST; s++) {
       iris::mbar_init(&bars->k_full[s], 1);
       iris::mbar_init(&bars->k_empty[s], 1);
+    }
+    for (int s = 0; s < VST; s++) {
       iris::mbar_init(&bars->v_full[s], 1);
       iris::mbar_init(&bars->v_empty[s], 1);
+    }
+    for (int s = 0; s < 2; s++) {
       iris::mbar_init(&bars->s_full[s], 1);
       iris::mbar_init(&bars->p_full[s], 128);
     }
@@ -153,39 +195,50 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
       iris::tma_load_2d(smem + OFF_Q + t * TILE, &p.tq, &bars->q_full, col0, q0 + t * BQ);
       iris::tma_load_2d(smem + OFF_Q + t * TILE + BOX, &p.tq, &bars->q_full, col0 + 64, q0 + t * BQ);
     }
-    int issued = 0;  // K/V tiles issued (each arms k_full and v_full of its stage)
+    // Loads in the order their stages are released: K_{j+KST} once Q1 K_j^T
+    // is done, V_{j+VST} once P1_j V_j is done (the tensor pipe finishes
+    // P1_{j-1} V_{j-1} before Q1 K_j^T before P1_j V_j), so no wait of this
+    // single thread holds back a load whose stage is already free.
+    int nk = 0, nv = 0;  // tiles issued
     bool ok = true;
-    for (int j = 0; j < n && ok; j++) {
-      int s = j & 1;
-      uint32_t u = (uint32_t)(j >> 1);
-      if (!iris::mbar_wait(&bars->k_empty[s], (u & 1) ^ 1, abort_flag, p.status, IRIS_DEV_ERR_ATTN_PRODUCER)) {
-        ok = false;
-        break;
-      }
+    auto load_k = [&]() -> bool {
+      const int s = nk % KST;
+      const uint32_t u = (uint32_t)(nk / KST);
+      if (!iris::mbar_wait(&bars->k_empty[s], (u & 1) ^ 1, abort_flag, p.status, IRIS_DEV_ERR_ATTN_PRODUCER))
+        return false;
       iris::mbar_arrive_expect_tx(&bars->k_full[s], TILE);
-      iris::tma_load_2d(smem + OFF_K + s * TILE, &p.tk, &bars->k_full[s], col0, j * BKV);
-      iris::tma_load_2d(smem + OFF_K + s * TILE + BOX, &p.tk, &bars->k_full[s], col0 + 64, j * BKV);
-      if (!iris::mbar_wait(&bars->v_empty[s], (u & 1) ^ 1, abort_flag, p.status, IRIS_DEV_ERR_ATTN_PRODUCER)) {
-        ok = false;
-        // K_j was issued without its V_j: drain it below through k_full
-        volatile int no_abort = 0;
-        iris::mbar_wait(&bars->k_full[s], u & 1, &no_abort, p.status, IRIS_DEV_ERR_ATTN_DRAIN);
-        break;
-      }
+      iris::tma_load_2d(smem + OFF_K + s * TILE, &p.tk, &bars->k_full[s], col0, nk * BKV);
+      iris::tma_load_2d(smem + OFF_K + s * TILE + BOX, &p.tk, &bars->k_full[s], col0 + 64, nk * BKV);
+      nk++;
+      return true;
+    };
+    auto load_v = [&]() -> bool {
+      const int s = nv % VST;
+      const uint32_t u = (uint32_t)(nv / VST);
+      if (!iris::mbar_wait(&bars->v_empty[s], (u & 1) ^ 1, abort_flag, p.status, IRIS_DEV_ERR_ATTN_PRODUCER))
+        return false;
       iris::mbar_arrive_expect_tx(&bars->v_full[s], TILE);
-      iris::tma_load_2d(smem + OFF_V + s * TILE, &p.tv, &bars->v_full[s], col0, j * BKV);
-      iris::tma_load_2d(smem + OFF_V + s * TILE + BOX, &p.tv, &bars->v_full[s], col0 + 64, j * BKV);
-      issued = j + 1;
+      iris::tma_load_2d(smem + OFF_V + s * TILE, &p.tv, &bars->v_full[s], col0, nv * BKV);
+      iris::tma_load_2d(smem + OFF_V + s * TILE + BOX, &p.tv, &bars->v_full[s], col0 + 64, nv * BKV);
+      nv++;
+      return true;
+    };
+    while (ok && nk < (n < KST ? n : KST)) ok = load_k();
+    while (ok && nv < (n < VST ? n : VST)) ok = load_v();
+    while (ok && (nk < n || nv < n)) {
+      if (nk < n) ok = load_k();
+      if (ok && nv < n) ok = load_v();
     }
     if (!ok) {
       // wait (bounded) for the copies still in flight before the CTA exits
       volatile int no_abort = 0;
       iris::mbar_wait(&bars->q_full, 0, &no_abort, p.status, IRIS_DEV_ERR_ATTN_DRAIN);
-      for (int j = issued - 2 < 0 ? 0 : issued - 2; j < issued; j++) {
-        uint32_t u = (uint32_t)(j >> 1);
-        iris::mbar_wait(&bars->k_full[j & 1], u & 1, &no_abort, p.status, IRIS_DEV_ERR_ATTN_DRAIN);
-        iris::mbar_wait(&bars->v_full[j & 1], u & 1, &no_abort, p.status, IRIS_DEV_ERR_ATTN_DRAIN);
-      }
+      for (int j = nk - KST < 0 ? 0 : nk - KST; j < nk; j++)
+        iris::mbar_wait(&bars->k_full[j % KST], (uint32_t)((j / KST) & 1), &no_abort, p.status,
+                        IRIS_DEV_ERR_ATTN_DRAIN);
+      for (int j = nv - VST < 0 ? 0 : nv - VST; j < nv; j++)
+        iris::mbar_wait(&bars->v_full[j % VST], (uint32_t)((j / VST) & 1), &no_abort, p.status,
+                        IRIS_DEV_ERR_ATTN_DRAIN);
     }
   } else if (warp == 1 && lane == 0) {
     // ------------------------------------------------------------ MMA issuer
@@ -194,7 +247,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
     const int nq = has1 ? 2 : 1;
     auto qk = [&](int t, int j) {  // S_t = Q_t K_j^T
       const uint32_t qa = iris::smem_u32(smem + OFF_Q + t * TILE);
-      const uint32_t kb = iris::smem_u32(smem + OFF_K + (j & 1) * TILE);
+      const uint32_t kb = iris::smem_u32(smem + OFF_K + (j % KST) * TILE);
 #pragma unroll
       for (int kk = 0; kk < HD / 16; kk++) {
         uint32_t off = (uint32_t)((kk >> 2) * BOX + (kk & 3) * 32);
@@ -203,7 +256,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
       }
     };
     auto pv = [&](int t, int j) {  // O_t += P_t V_j, P_t from TMEM
-      const uint32_t vb = iris::smem_u32(smem + OFF_V + (j & 1) * TILE);
+      const uint32_t vb = iris::smem_u32(smem + OFF_V + (j % VST) * TILE);
 #pragma unroll
       for (int kk = 0; kk < BKV / 16; kk++) {
         // B: V [keys, d] MN-major; 16 keys = 2 atoms of 8 rows (2048 B);
@@ -223,11 +276,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
       iris::umma_commit(&bars->k_empty[0]);
     }
     for (int j = 0; j < n && ok; j++) {
-      const int s = j & 1;
       const bool more = j + 1 < n;
-      if (!iris::mbar_wait(&bars->v_full[s], (uint32_t)((j >> 1) & 1), abort_flag, p.status, IRIS_DEV_ERR_ATTN_MMA) ||
-          (more && !iris::mbar_wait(&bars->k_full[(j + 1) & 1], (uint32_t)(((j + 1) >> 1) & 1), abort_flag, p.status,
-                                    IRIS_DEV_ERR_ATTN_MMA))) {
+      if (!iris::mbar_wait(&bars->v_full[j % VST], (uint32_t)((j / VST) & 1), abort_flag, p.status,
+                           IRIS_DEV_ERR_ATTN_MMA)) {
         ok = false;
         break;
       }
@@ -239,13 +290,20 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
         iris::tc_fence_after();
         pv(t, j);
         if (more) {
+          // K_{j+1} is first needed here, after P0_j V_j went in
+          if (t == 0 && !iris::mbar_wait(&bars->k_full[(j + 1) % KST], (uint32_t)(((j + 1) / KST) & 1), abort_flag,
+                                         p.status, IRIS_DEV_ERR_ATTN_MMA)) {
+            ok = false;
+            break;
+          }
+          iris::tc_fence_after();
           qk(t, j + 1);
           iris::umma_commit(&bars->s_full[t]);
         }
       }
       if (!ok) break;
-      iris::umma_commit(&bars->v_empty[s]);
-      if (more) iris::umma_commit(&bars->k_empty[(j + 1) & 1]);
+      iris::umma_commit(&bars->v_empty[j % VST]);
+      if (more) iris::umma_commit(&bars->k_empty[(j + 1) % KST]);
     }
     if (ok) {
       iris::umma_commit(&bars->o_done);
@@ -278,6 +336,15 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
       float sv[64];
       iris::tmem_ld64(s_addr + 64 * h, sv);
       float xm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (full && IRIS_ATTN_EMU_PER8 == 0) {
+        const uint64_t sc2 = f32x2(p.scale_log2, p.scale_log2), nm2 = f32x2(nm, nm);
+        uint64_t acc[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int i = 0; i < 32; i++) pw[i] = exp_pair(sv[2 * i], sv[2 * i + 1], sc2, nm2, acc[i & 3]);
+#pragma unroll
+        for (int i = 0; i < 4; i++) rsum[i] += sum_f32x2(acc[i]);
+        return -INFINITY;  // the caller checks the row sum instead
+      }
 #pragma unroll
       for (int c = 0; c < 8; c++) {
         float e[8];
@@ -312,7 +379,9 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
         const float nm = -m;
         const float x0 = half_exps(0, kbase, full, nm, pw, rsum);
         const float x1 = half_exps(1, kbase, full, nm, pw + 32, rsum);
-        redo = __any_sync(0xffffffffu, fmaxf(x0, x1) > RESCALE_THRESHOLD);
+        const float rs = ((rsum[0] + rsum[1]) + (rsum[2] + rsum[3])) + ((rsum[4] + rsum[5]) + (rsum[6] + rsum[7]));
+        // (a NaN sum also redoes: !(rs <= limit))
+        redo = __any_sync(0xffffffffu, fmaxf(x0, x1) > RESCALE_THRESHOLD || !(rs <= FAST_SUM_LIMIT));
       }
       if (redo) {
         // slow path (warp-uniform): row max of the tile, new reference, O

@@ -33,7 +33,12 @@ constexpr int B_BYTES_MAX = 256 * BK * 2;   // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES_MAX;
 constexpr int NUM_THREADS = 192;
 constexpr int TMEM_COLS = 512;
-constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*barriers*/ + 1024 /*align slack*/;
+// f32 epilogue staging: 32 rows x (32 + 4) floats per epilogue warp, so that
+// 16-byte shared accesses run in conflict-free 8-lane phases
+constexpr int EPI_LD = 36;
+constexpr int EPI_WARP_BYTES = 32 * EPI_LD * 4;
+constexpr int EPI_BYTES = 4 * EPI_WARP_BYTES;
+constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*barriers*/ + EPI_BYTES + 1024 /*align slack*/;
 
 struct Bars {
   uint64_t full[STAGES];
@@ -153,14 +158,61 @@ __device__ __forceinline__ void epi_swiglu_tile(const IrisGemmParams& p, uint32_
   }
 }
 
+// f32 outputs (plain store or gated residual update) of a 32-row x 32-column
+// block: lane i holds row row_first + i in v.  The block is transposed through
+// this warp's shared staging tile so that every global access covers 4 rows x
+// 128 contiguous bytes (one thread per row would touch 32 rows per access).
+__device__ __forceinline__ void epi_f32_block(const IrisGemmParams& p, int g, float* stage, const float* v,
+                                              int lane, int row_first, int rows_valid, int c) {
+  float4* st = reinterpret_cast<float4*>(stage + lane * EPI_LD);
+#pragma unroll
+  for (int q = 0; q < 8; q++) st[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  __syncwarp();
+  const int rr = lane >> 3, c4 = (lane & 7) * 4;
+  const bool resid = p.mode == IRIS_EPI_RESID_GATE;
+  float* base = reinterpret_cast<float*>(p.out) + (size_t)(row_first + rr) * p.ldo + c + c4;
+  const size_t step = (size_t)4 * p.ldo;  // 4 rows per pass
+  // all residual loads in flight before the first store
+  float4 h[8];
+#pragma unroll
+  for (int it = 0; it < 8; it++) {
+    h[it] = make_float4(0.f, 0.f, 0.f, 0.f);
+    if (resid && !p.resid_store && it * 4 + rr < rows_valid)
+      h[it] = __ldcg(reinterpret_cast<const float4*>(base + it * step));
+  }
+  const float4 gg = resid ? __ldg(reinterpret_cast<const float4*>(p.gate[g] + c + c4)) : make_float4(1.f, 1.f, 1.f, 1.f);
+#pragma unroll
+  for (int it = 0; it < 8; it++) {
+    const int r = it * 4 + rr;
+    const float4 a = *reinterpret_cast<const float4*>(stage + r * EPI_LD + c4);
+    float4 o = h[it];
+    o.x += gg.x * a.x;
+    o.y += gg.y * a.y;
+    o.z += gg.z * a.z;
+    o.w += gg.w * a.w;
+    if (r < rows_valid) *reinterpret_cast<float4*>(base + it * step) = o;
+  }
+  __syncwarp();  // the stage is rewritten by the next block
+}
+
 __device__ __forceinline__ void epi_plain_chunk(const IrisGemmParams& p, uint32_t taddr, int g,
-                                                int row, int row_local, bool valid, int col0) {
+                                                int row, int row_local, bool valid, int col0, float* stage,
+                                                int lane, int rows_valid) {
 #pragma unroll 1
   for (int j = 0; j < 4; j++) {
     float v[32];
     iris::tmem_ld32(taddr + 32 * j, v);
-    if (!valid) continue;
     int c = col0 + 32 * j;
+    if (p.mode == IRIS_EPI_RESID_GATE || p.mode == IRIS_EPI_F32) {
+      if (p.bias) {
+#pragma unroll
+        for (int e = 0; e < 32; e++) v[e] += __ldg(p.bias + c + e);
+      }
+      // warp-collective: every lane takes part, rows_valid masks the stores
+      epi_f32_block(p, g, stage, v, lane, row - lane, rows_valid, c);
+      continue;
+    }
+    if (!valid) continue;
     if (p.bias) {
 #pragma unroll
       for (int e = 0; e < 32; e++) v[e] += __ldg(p.bias + c + e);
@@ -191,9 +243,10 @@ __device__ __forceinline__ void epi_plain_chunk(const IrisGemmParams& p, uint32_
   }
 }
 
-// Epilogue of one accumulator tile for this thread's row (all modes).
+// Epilogue of one accumulator tile for this thread's row (all modes); the
+// warp's 32 rows start at row - lane, rows_valid of them are real.
 __device__ __forceinline__ void epi_tile(const IrisGemmParams& p, uint32_t taddr, int g, int row, int row_local,
-                                         bool valid, int n0) {
+                                         bool valid, int n0, float* stage, int lane, int rows_valid) {
   bool swiglu_tile = (p.mode == IRIS_EPI_SWIGLU) || (p.mode == IRIS_EPI_SINGLE && n0 >= p.swiglu_base);
   if (swiglu_tile) {
     epi_swiglu_tile(p, taddr, row, valid, n0);
@@ -204,7 +257,7 @@ __device__ __forceinline__ void epi_tile(const IrisGemmParams& p, uint32_t taddr
       if (p.mode == IRIS_EPI_QKV || p.mode == IRIS_EPI_SINGLE)
         epi_qkv_chunk(p, taddr + c * 128, g, row, valid, col0);
       else
-        epi_plain_chunk(p, taddr + c * 128, g, row, row_local, valid, col0);
+        epi_plain_chunk(p, taddr + c * 128, g, row, row_local, valid, col0, stage, lane, rows_valid);
     }
   }
 }
@@ -330,6 +383,7 @@ gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
   } else if (warp >= 2) {
     // ------------------------------------------------ epilogue
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    float* stage = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES + 1024 + (warp - 2) * EPI_WARP_BYTES);
     int it = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x, it++) {
       int buf = it & 1;
@@ -342,7 +396,8 @@ gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
       bool valid = row_local < p.rows[g];
       int row = p.row0[g] + row_local;
       uint32_t taddr = tmem_base + buf * 256 + ((uint32_t)(quarter * 32) << 16);
-      epi_tile(p, taddr, g, row, row_local, valid, n0);
+      const int rows_valid = min(32, max(0, p.rows[g] - (row_local - lane)));
+      epi_tile(p, taddr, g, row, row_local, valid, n0, stage, lane, rows_valid);
       iris::tc_fence_before();
       iris::mbar_arrive(&bars->tempty[buf]);
     }
@@ -367,7 +422,7 @@ gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
 constexpr int BM2 = 256;
 constexpr int STAGES2 = 6;
 constexpr int STAGE2_BYTES = A_BYTES + 128 * BK * 2;  // 32 KB
-constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + 1024;
+constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + EPI_BYTES + 1024;
 
 struct Bars2 {
   uint64_t full[STAGES2];   // even CTA: both CTAs' tiles of the stage landed (2 arrivals + bytes)
@@ -495,6 +550,7 @@ gemm_tc2_kernel(const __grid_constant__ IrisGemmParams p) {
   } else if (warp >= 2) {
     // ------------------------------------------------ epilogue (both CTAs)
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
+    float* stage = reinterpret_cast<float*>(smem + STAGES2 * STAGE2_BYTES + 1024 + (warp - 2) * EPI_WARP_BYTES);
     const uint32_t tempty_c0 = iris::mapa_shared(&bars->tempty[0], 0);
     const uint32_t tempty_c1 = iris::mapa_shared(&bars->tempty[1], 0);
     int it = 0;
@@ -509,7 +565,8 @@ gemm_tc2_kernel(const __grid_constant__ IrisGemmParams p) {
       bool valid = row_local < p.rows[g];
       int row = p.row0[g] + row_local;
       uint32_t taddr = tmem_base + buf * 256 + ((uint32_t)(quarter * 32) << 16);
-      epi_tile(p, taddr, g, row, row_local, valid, n0);
+      const int rows_valid = min(32, max(0, p.rows[g] - (row_local - lane)));
+      epi_tile(p, taddr, g, row, row_local, valid, n0, stage, lane, rows_valid);
       iris::tc_fence_before();
       __syncwarp();
       if (lane == 0) iris::mbar_arrive_cluster(buf ? tempty_c1 : tempty_c0);

@@ -97,6 +97,55 @@ adaln_kernel(const float* __restrict__ x, int ldx, __nv_bfloat16* __restrict__ o
   }
 }
 
+// Warp-per-row variant for rows of NV*128 floats (H = 3072 / 4096): the whole
+// row sits in registers (NV float4 per lane), both reductions are warp
+// shuffles (no shared memory or block barriers), and every load of the row is
+// issued before the first reduction, so each warp keeps NV*512 bytes in
+// flight.  Same two-pass mean / variance as the block kernel above.
+template <int NV>
+__global__ void __launch_bounds__(256)
+adaln_warp_kernel(const float* __restrict__ x, int ldx, __nv_bfloat16* __restrict__ out, int ldout, int rows,
+                  const float* __restrict__ shift0, const float* __restrict__ scale0,
+                  const float* __restrict__ shift1, const float* __restrict__ scale1, int split, float eps) {
+  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= rows) return;
+  constexpr int cols = NV * 128;
+  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * ldx);
+  float4 v[NV];
+#pragma unroll
+  for (int i = 0; i < NV; i++) v[i] = xr[lane + 32 * i];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; i++) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
+#pragma unroll
+  for (int o = 16; o; o >>= 1) s += __shfl_xor_sync(0xffffffffu, s, o);
+  const float mean = s / (float)cols;
+  float q = 0.f;
+#pragma unroll
+  for (int i = 0; i < NV; i++) {
+    float a = v[i].x - mean, b = v[i].y - mean, c = v[i].z - mean, d = v[i].w - mean;
+    q += (a * a + b * b) + (c * c + d * d);
+  }
+#pragma unroll
+  for (int o = 16; o; o >>= 1) q += __shfl_xor_sync(0xffffffffu, q, o);
+  const float rstd = 1.0f / sqrtf(q / (float)cols + eps);
+  const bool g1 = row >= split;
+  const float4* sh = reinterpret_cast<const float4*>(g1 ? shift1 : shift0);
+  const float4* sc = reinterpret_cast<const float4*>(g1 ? scale1 : scale0);
+  uint2* o = reinterpret_cast<uint2*>(out + (size_t)row * ldout);
+#pragma unroll
+  for (int i = 0; i < NV; i++) {
+    const int c = lane + 32 * i;
+    float4 a = __ldg(sh + c), b = __ldg(sc + c);
+    float y0 = (1.0f + b.x) * ((v[i].x - mean) * rstd) + a.x;
+    float y1 = (1.0f + b.y) * ((v[i].y - mean) * rstd) + a.y;
+    float y2 = (1.0f + b.z) * ((v[i].z - mean) * rstd) + a.z;
+    float y3 = (1.0f + b.w) * ((v[i].w - mean) * rstd) + a.w;
+    o[c] = make_uint2(pack2(y0, y1), pack2(y2, y3));
+  }
+}
+
 // ------------------------------------------------------------------ GEMV
 // One warp per output row; x (after the optional SiLU) is staged in shared
 // memory; W rows are read with 16-byte loads.
@@ -390,6 +439,18 @@ cudaError_t iris_launch_adaln(const float* x, int ldx, void* out, int ldout, int
   if (rows <= 0) return cudaSuccess;
   if ((cols & 3) || cols > 256 * 4 * ADALN_MAXV || (ldx & 3) || (ldout & 3))
     return cudaErrorInvalidValue;
+  if (cols == 3072 || cols == 4096) {
+    const float* sh1 = shift1 ? shift1 : shift0;
+    const float* sc1 = scale1 ? scale1 : scale0;
+    __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out);
+    if (cols == 3072)
+      adaln_warp_kernel<24><<<(rows + 7) / 8, 256, 0, stream>>>(x, ldx, o, ldout, rows, shift0, scale0, sh1, sc1,
+                                                                split, eps);
+    else
+      adaln_warp_kernel<32><<<(rows + 7) / 8, 256, 0, stream>>>(x, ldx, o, ldout, rows, shift0, scale0, sh1, sc1,
+                                                                split, eps);
+    return cudaGetLastError();
+  }
   adaln_kernel<<<rows, 256, 0, stream>>>(x, ldx, static_cast<__nv_bfloat16*>(out), ldout, cols,
                                          shift0, scale0, shift1 ? shift1 : shift0,
                                          scale1 ? scale1 : scale0, split, eps);

@@ -33,7 +33,7 @@ def test_attention(iris, sq, sk, heads, scale_std):
     assert rel_l2(O.read((sq, heads * 128)), ref) < 1e-2
 
 
-@pytest.mark.parametrize("seq,hidden", [(24, 256), (1536, 3072), (97, 512)])
+@pytest.mark.parametrize("seq,hidden", [(24, 256), (1536, 3072), (97, 512), (13, 4096), (9, 3072)])
 def test_adaln(iris, seq, hidden):
     rng = np.random.default_rng(seq)
     x = bf16_round(rng.standard_normal((seq, hidden)) * 3 + 0.5)
