@@ -409,7 +409,7 @@ def run_ours(args):
     if os.path.exists(tpath):
         with open(tpath) as f:
             traffic = json.load(f).get("dram_bytes_per_launch")
-    roofline = {"kernel": "gemm_tc_kernel, single-block fused QKV+MLP launch (M=1536, N=27648, K=3072)",
+    roofline = {"kernel": "gemm_tc2_kernel (CTA pair), single-block fused QKV+MLP launch (M=1536, N=27648, K=3072)",
                 "bound": "tensor", "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
                 "frac": achieved / peaks["bf16_tflops"], "peak_source": peak_src,
                 "frac_of_sustained": achieved / peaks["bf16_tflops_sustained"], "traffic": traffic,

@@ -147,6 +147,158 @@ __device__ __forceinline__ float sum_f32x2(uint64_t v) {
   return a + b;
 }
 
+// Softmax and epilogue of one 128-row query tile t (warps of one warpgroup):
+// per key tile, S_t from TMEM -> P_t (bf16) back into TMEM, running row sum and
+// lazy reference max; at the end O_t / l -> bf16 rows [row0, row0 + 128).
+// kPair: the P-ready barrier lives in the even CTA of a pair (one arrival per
+// warp through its cluster address), otherwise in this CTA (128 arrivals).
+template <bool kPair>
+__device__ __forceinline__ void softmax_role(const AttnParams& p, uint32_t tmem, int t, int warp, int lane,
+                                             uint64_t* s_full, uint64_t* p_full, uint32_t p_full_cluster,
+                                             uint64_t* o_done, volatile int* abort_flag, int row0, int col0,
+                                             int n) {
+  const int quarter = warp & 3;
+  const int r = quarter * 32 + lane;  // query row within the tile = TMEM lane
+  const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
+  const uint32_t s_addr = tmem + lane_off + t * 128;
+  const uint32_t o_addr = tmem + lane_off + 256 + t * 128;
+  float m = -INFINITY, l = 0.f;  // reference max (scaled, log2 units) and row sum
+  bool ok = true;
+  // S row -> scaled logits (log2 units): padding keys -inf, masked keys
+  // -1e9 (in natural-log units, as the reference's masked softmax)
+  auto logit = [&](float sv, int key, bool full) -> float {
+    if (full) return sv * p.scale_log2;
+    if (key >= p.sk) return -INFINITY;
+    if (p.kmask && !p.kmask[key]) return -1e9f * LOG2E;
+    return sv * p.scale_log2;
+  };
+  // exponentials of 64 keys (half h of the tile) against reference max -nm
+  // -> 32 packed bf16 words; returns the largest exponent argument
+  auto half_exps = [&](int h, int kbase, bool full, float nm, uint32_t* pw, float* rsum) -> float {
+    float sv[64];
+    iris::tmem_ld64(s_addr + 64 * h, sv);
+    float xm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+    if (full && IRIS_ATTN_EMU_PER8 == 0) {
+      const uint64_t sc2 = f32x2(p.scale_log2, p.scale_log2), nm2 = f32x2(nm, nm);
+      uint64_t acc[4] = {0, 0, 0, 0};
+#pragma unroll
+      for (int i = 0; i < 32; i++) pw[i] = exp_pair(sv[2 * i], sv[2 * i + 1], sc2, nm2, acc[i & 3]);
+#pragma unroll
+      for (int i = 0; i < 4; i++) rsum[i] += sum_f32x2(acc[i]);
+      return -INFINITY;  // the caller checks the row sum instead
+    }
+#pragma unroll
+    for (int c = 0; c < 8; c++) {
+      float e[8];
+#pragma unroll
+      for (int u = 0; u < 8; u++) {
+        const int i = c * 8 + u;
+        const float x = full ? fmaf(sv[i], p.scale_log2, nm) : logit(sv[i], kbase + 64 * h + i, false) + nm;
+        xm[u & 3] = fmaxf(xm[u & 3], x);
+        e[u] = (u < IRIS_ATTN_EMU_PER8) ? exp2_fma(x) : iris::ex2_approx(x);
+        rsum[u] += e[u];
+      }
+#pragma unroll
+      for (int u = 0; u < 4; u++) pw[c * 4 + u] = pack_bf16(e[2 * u], e[2 * u + 1]);
+    }
+    return fmaxf(fmaxf(xm[0], xm[1]), fmaxf(xm[2], xm[3]));
+  };
+  for (int j = 0; j < n; j++) {
+    if (!iris::mbar_wait(s_full, (uint32_t)(j & 1), abort_flag, p.status, IRIS_DEV_ERR_ATTN_SOFTMAX)) {
+      ok = false;
+      break;
+    }
+    iris::tc_fence_after();
+    const int kbase = j * BKV;
+    const bool full = kbase + BKV <= p.sk && !p.kmask;
+    uint32_t pw[BKV / 2];
+    float rsum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    float alpha = 1.f;
+    // fast path: P against the current reference max; it stands unless a
+    // logit exceeds it by more than the threshold (m = -inf: first tile)
+    bool redo = true;
+    if (m != -INFINITY) {
+      const float nm = -m;
+      const float x0 = half_exps(0, kbase, full, nm, pw, rsum);
+      const float x1 = half_exps(1, kbase, full, nm, pw + 32, rsum);
+      const float rs = ((rsum[0] + rsum[1]) + (rsum[2] + rsum[3])) + ((rsum[4] + rsum[5]) + (rsum[6] + rsum[7]));
+      // (a NaN sum also redoes: !(rs <= limit))
+      redo = __any_sync(0xffffffffu, fmaxf(x0, x1) > RESCALE_THRESHOLD || !(rs <= FAST_SUM_LIMIT));
+    }
+    if (redo) {
+      // slow path (warp-uniform): row max of the tile, new reference, O
+      // correction, P again
+      float tm[8];
+#pragma unroll
+      for (int i = 0; i < 8; i++) tm[i] = -INFINITY;
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        float sv[64];
+        iris::tmem_ld64(s_addr + 64 * h, sv);
+#pragma unroll
+        for (int i = 0; i < 64; i++) tm[i & 7] = fmaxf(tm[i & 7], logit(sv[i], kbase + 64 * h + i, full));
+      }
+      const float tmax = fmaxf(fmaxf(fmaxf(tm[0], tm[1]), fmaxf(tm[2], tm[3])),
+                               fmaxf(fmaxf(tm[4], tm[5]), fmaxf(tm[6], tm[7])));
+      const bool grow = tmax > m + RESCALE_THRESHOLD;
+      const float m_new = grow ? tmax : m;
+      alpha = (grow && m != -INFINITY) ? iris::ex2_approx(m - m_new) : (grow ? 0.f : 1.f);
+      // O = P_0..P_{j-1} V is final here (the commit behind s_full covers
+      // P_{j-1} V_{j-1})
+      if (j > 0) {
+#pragma unroll 1
+        for (int c = 0; c < 4; c++) {
+          float o[32];
+          iris::tmem_ld32(o_addr + 32 * c, o);
+#pragma unroll
+          for (int e = 0; e < 32; e++) o[e] *= alpha;
+          iris::tmem_st32(o_addr + 32 * c, o);
+        }
+      }
+      m = m_new;
+      const float nm = (m == -INFINITY) ? 0.f : -m;
+#pragma unroll
+      for (int i = 0; i < 8; i++) rsum[i] = 0.f;
+      half_exps(0, kbase, full, nm, pw, rsum);
+      half_exps(1, kbase, full, nm, pw + 32, rsum);
+    }
+    iris::tmem_st64(s_addr, pw);  // P_j over the first 64 columns of S_j
+    const float rs = ((rsum[0] + rsum[1]) + (rsum[2] + rsum[3])) + ((rsum[4] + rsum[5]) + (rsum[6] + rsum[7]));
+    l = l * alpha + rs;
+    iris::tc_fence_before();
+    if (kPair) {
+      // the even CTA's MMA thread waits for both CTAs' P: one arrival per warp
+      __syncwarp();
+      if (lane == 0) iris::mbar_arrive_cluster(p_full_cluster);
+    } else {
+      iris::mbar_arrive(p_full);
+    }
+  }
+  if (ok && n > 0 && iris::mbar_wait(o_done, 0, abort_flag, p.status, IRIS_DEV_ERR_ATTN_SOFTMAX)) {
+    iris::tc_fence_after();
+    const float inv = l > 0.f ? 1.0f / l : 0.f;
+    const int row = row0 + r;
+    __nv_bfloat16* dst = p.o + (size_t)row * p.ldo + col0;
+#pragma unroll 1
+    for (int c = 0; c < 4; c++) {
+      float o[32];
+      iris::tmem_ld32(o_addr + 32 * c, o);
+      if (row < p.sq) {
+        uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * c);
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          uint4 w;
+          w.x = pack_bf16(o[8 * q + 0] * inv, o[8 * q + 1] * inv);
+          w.y = pack_bf16(o[8 * q + 2] * inv, o[8 * q + 3] * inv);
+          w.z = pack_bf16(o[8 * q + 4] * inv, o[8 * q + 5] * inv);
+          w.w = pack_bf16(o[8 * q + 6] * inv, o[8 * q + 7] * inv);
+          d4[q] = w;
+        }
+      }
+    }
+  }
+}
+
 __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -315,146 +467,218 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
   } else if (warp >= 2 && (warp < 6 || has1)) {
     // ------------------------------------------------------------ softmax + epilogue
     const int t = warp >= 6 ? 1 : 0;  // query tile
-    const int quarter = warp & 3;
-    const int r = quarter * 32 + lane;  // query row within the tile = TMEM lane
-    const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
-    const uint32_t s_addr = tmem + lane_off + t * 128;
-    const uint32_t o_addr = tmem + lane_off + 256 + t * 128;
-    float m = -INFINITY, l = 0.f;  // reference max (scaled, log2 units) and row sum
-    bool ok = true;
-    // S row -> scaled logits (log2 units): padding keys -inf, masked keys
-    // -1e9 (in natural-log units, as the reference's masked softmax)
-    auto logit = [&](float sv, int key, bool full) -> float {
-      if (full) return sv * p.scale_log2;
-      if (key >= p.sk) return -INFINITY;
-      if (p.kmask && !p.kmask[key]) return -1e9f * LOG2E;
-      return sv * p.scale_log2;
-    };
-    // exponentials of 64 keys (half h of the tile) against reference max -nm
-    // -> 32 packed bf16 words; returns the largest exponent argument
-    auto half_exps = [&](int h, int kbase, bool full, float nm, uint32_t* pw, float* rsum) -> float {
-      float sv[64];
-      iris::tmem_ld64(s_addr + 64 * h, sv);
-      float xm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-      if (full && IRIS_ATTN_EMU_PER8 == 0) {
-        const uint64_t sc2 = f32x2(p.scale_log2, p.scale_log2), nm2 = f32x2(nm, nm);
-        uint64_t acc[4] = {0, 0, 0, 0};
-#pragma unroll
-        for (int i = 0; i < 32; i++) pw[i] = exp_pair(sv[2 * i], sv[2 * i + 1], sc2, nm2, acc[i & 3]);
-#pragma unroll
-        for (int i = 0; i < 4; i++) rsum[i] += sum_f32x2(acc[i]);
-        return -INFINITY;  // the caller checks the row sum instead
-      }
-#pragma unroll
-      for (int c = 0; c < 8; c++) {
-        float e[8];
-#pragma unroll
-        for (int u = 0; u < 8; u++) {
-          const int i = c * 8 + u;
-          const float x = full ? fmaf(sv[i], p.scale_log2, nm) : logit(sv[i], kbase + 64 * h + i, false) + nm;
-          xm[u & 3] = fmaxf(xm[u & 3], x);
-          e[u] = (u < IRIS_ATTN_EMU_PER8) ? exp2_fma(x) : iris::ex2_approx(x);
-          rsum[u] += e[u];
-        }
-#pragma unroll
-        for (int u = 0; u < 4; u++) pw[c * 4 + u] = pack_bf16(e[2 * u], e[2 * u + 1]);
-      }
-      return fmaxf(fmaxf(xm[0], xm[1]), fmaxf(xm[2], xm[3]));
-    };
-    for (int j = 0; j < n; j++) {
-      if (!iris::mbar_wait(&bars->s_full[t], (uint32_t)(j & 1), abort_flag, p.status, IRIS_DEV_ERR_ATTN_SOFTMAX)) {
-        ok = false;
-        break;
-      }
-      iris::tc_fence_after();
-      const int kbase = j * BKV;
-      const bool full = kbase + BKV <= p.sk && !p.kmask;
-      uint32_t pw[BKV / 2];
-      float rsum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-      float alpha = 1.f;
-      // fast path: P against the current reference max; it stands unless a
-      // logit exceeds it by more than the threshold (m = -inf: first tile)
-      bool redo = true;
-      if (m != -INFINITY) {
-        const float nm = -m;
-        const float x0 = half_exps(0, kbase, full, nm, pw, rsum);
-        const float x1 = half_exps(1, kbase, full, nm, pw + 32, rsum);
-        const float rs = ((rsum[0] + rsum[1]) + (rsum[2] + rsum[3])) + ((rsum[4] + rsum[5]) + (rsum[6] + rsum[7]));
-        // (a NaN sum also redoes: !(rs <= limit))
-        redo = __any_sync(0xffffffffu, fmaxf(x0, x1) > RESCALE_THRESHOLD || !(rs <= FAST_SUM_LIMIT));
-      }
-      if (redo) {
-        // slow path (warp-uniform): row max of the tile, new reference, O
-        // correction, P again
-        float tm[8];
-#pragma unroll
-        for (int i = 0; i < 8; i++) tm[i] = -INFINITY;
-#pragma unroll
-        for (int h = 0; h < 2; h++) {
-          float sv[64];
-          iris::tmem_ld64(s_addr + 64 * h, sv);
-#pragma unroll
-          for (int i = 0; i < 64; i++) tm[i & 7] = fmaxf(tm[i & 7], logit(sv[i], kbase + 64 * h + i, full));
-        }
-        const float tmax = fmaxf(fmaxf(fmaxf(tm[0], tm[1]), fmaxf(tm[2], tm[3])),
-                                 fmaxf(fmaxf(tm[4], tm[5]), fmaxf(tm[6], tm[7])));
-        const bool grow = tmax > m + RESCALE_THRESHOLD;
-        const float m_new = grow ? tmax : m;
-        alpha = (grow && m != -INFINITY) ? iris::ex2_approx(m - m_new) : (grow ? 0.f : 1.f);
-        // O = P_0..P_{j-1} V is final here (the commit behind s_full covers
-        // P_{j-1} V_{j-1})
-        if (j > 0) {
-#pragma unroll 1
-          for (int c = 0; c < 4; c++) {
-            float o[32];
-            iris::tmem_ld32(o_addr + 32 * c, o);
-#pragma unroll
-            for (int e = 0; e < 32; e++) o[e] *= alpha;
-            iris::tmem_st32(o_addr + 32 * c, o);
-          }
-        }
-        m = m_new;
-        const float nm = (m == -INFINITY) ? 0.f : -m;
-#pragma unroll
-        for (int i = 0; i < 8; i++) rsum[i] = 0.f;
-        half_exps(0, kbase, full, nm, pw, rsum);
-        half_exps(1, kbase, full, nm, pw + 32, rsum);
-      }
-      iris::tmem_st64(s_addr, pw);  // P_j over the first 64 columns of S_j
-      const float rs = ((rsum[0] + rsum[1]) + (rsum[2] + rsum[3])) + ((rsum[4] + rsum[5]) + (rsum[6] + rsum[7]));
-      l = l * alpha + rs;
-      iris::tc_fence_before();
-      iris::mbar_arrive(&bars->p_full[t]);
-    }
-    if (ok && n > 0 && iris::mbar_wait(&bars->o_done, 0, abort_flag, p.status, IRIS_DEV_ERR_ATTN_SOFTMAX)) {
-      iris::tc_fence_after();
-      const float inv = l > 0.f ? 1.0f / l : 0.f;
-      const int row = q0 + t * BQ + r;
-      __nv_bfloat16* dst = p.o + (size_t)row * p.ldo + col0;
-#pragma unroll 1
-      for (int c = 0; c < 4; c++) {
-        float o[32];
-        iris::tmem_ld32(o_addr + 32 * c, o);
-        if (row < p.sq) {
-          uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * c);
-#pragma unroll
-          for (int q = 0; q < 4; q++) {
-            uint4 w;
-            w.x = pack_bf16(o[8 * q + 0] * inv, o[8 * q + 1] * inv);
-            w.y = pack_bf16(o[8 * q + 2] * inv, o[8 * q + 3] * inv);
-            w.z = pack_bf16(o[8 * q + 4] * inv, o[8 * q + 5] * inv);
-            w.w = pack_bf16(o[8 * q + 6] * inv, o[8 * q + 7] * inv);
-            d4[q] = w;
-          }
-        }
-      }
-    }
+    softmax_role<false>(p, tmem, t, warp, lane, &bars->s_full[t], &bars->p_full[t], 0u, &bars->o_done, abort_flag,
+                        q0 + t * BQ, col0, n);
   }
 
   __syncthreads();
   if (warp == 1) {
     iris::tc_fence_after();
     iris::tmem_dealloc(tmem, TMEM_COLS);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// CTA-pair variant (cluster of 2, cta_group::2).  The pair holds four query
+// tiles (two per CTA); every MMA is M = 256 over the pair: S_t = Q_t K_j^T
+// takes query tile t of both CTAs and a key tile whose 128 keys are split
+// 64 / 64 between the CTAs' shared memory; O_t += P_t V_j takes both CTAs'
+// P_t from their TMEM and V_j's 128 head dimensions split 64 / 64.  Per CTA
+// and K step the tensor cores read 6 KB (S) or 2 KB (O) of shared memory
+// instead of 8 KB / 4 KB, which is what bounded the single-CTA kernel, and
+// every K/V byte crosses L2 once per 256 query rows.  The even CTA's thread 32
+// issues all MMAs; softmax and epilogue run in both CTAs as above.
+constexpr int HALF = TILE / 2;  // 16 KB: a 64-key K half (two 64x64 boxes) or a 128-key x 64-dim V half
+constexpr int PK_ST = 4;
+constexpr int PV_ST = 4;
+constexpr int P_OFF_K = 2 * TILE;
+constexpr int P_OFF_V = P_OFF_K + PK_ST * HALF;
+constexpr int P_OFF_BAR = P_OFF_V + PV_ST * HALF;
+constexpr int P_SMEM_BYTES = P_OFF_BAR + 512 + 1024;
+
+struct PairBars {
+  uint64_t q_full;                           // even CTA: both CTAs' query tiles (2 arrivals + bytes)
+  uint64_t k_full[PK_ST], k_empty[PK_ST];    // full: even CTA (2 arrivals + bytes); empty: each CTA
+  uint64_t v_full[PV_ST], v_empty[PV_ST];
+  uint64_t s_full[2];                        // each CTA
+  uint64_t p_full[2];                        // even CTA: 8 warp arrivals (4 per CTA)
+  uint64_t o_done;                           // each CTA
+  uint64_t drain;
+  uint32_t tmem_base;
+  int abort;
+};
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+attn_pair_kernel(const __grid_constant__ AttnParams p) {
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  PairBars* bars = reinterpret_cast<PairBars*>(smem + P_OFF_BAR);
+  volatile int* abort_flag = &bars->abort;
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int head = blockIdx.y;
+  const uint32_t rank = iris::cluster_ctarank();
+  const int q0 = (blockIdx.x >> 1) * (4 * BQ) + (int)rank * (2 * BQ);  // this CTA's two query tiles
+  const int col0 = head * HD;
+  const int n = (p.sk + BKV - 1) / BKV;
+
+  if (threadIdx.x == 0) {
+    iris::mbar_init(&bars->q_full, 2);
+    for (int s = 0; s < PK_ST; s++) {
+      iris::mbar_init(&bars->k_full[s], 2);
+      iris::mbar_init(&bars->k_empty[s], 1);
+    }
+    for (int s = 0; s < PV_ST; s++) {
+      iris::mbar_init(&bars->v_full[s], 2);
+      iris::mbar_init(&bars->v_empty[s], 1);
+    }
+    for (int t = 0; t < 2; t++) {
+      iris::mbar_init(&bars->s_full[t], 1);
+      iris::mbar_init(&bars->p_full[t], 8);
+    }
+    iris::mbar_init(&bars->o_done, 1);
+    iris::mbar_init(&bars->drain, 1);
+    bars->abort = 0;
+    iris::fence_mbar_init();
+    iris::tma_prefetch_desc(&p.tq);
+    iris::tma_prefetch_desc(&p.tk);
+    iris::tma_prefetch_desc(&p.tv);
+  }
+  if (warp == 1) iris::tmem_alloc_pair(&bars->tmem_base, TMEM_COLS);
+  iris::tc_fence_before();
+  __syncthreads();
+  iris::cluster_sync();  // both CTAs' barriers exist before any remote arrive
+  iris::tc_fence_after();
+  const uint32_t tmem = bars->tmem_base;
+
+  if (warp == 0 && lane == 0) {
+    // ------------------------------------------------------------ producer (both CTAs)
+    const uint32_t qf = iris::mapa_shared(&bars->q_full, 0);
+    iris::mbar_arrive_expect_tx_cluster(qf, 2 * TILE);
+    for (int t = 0; t < 2; t++) {
+      iris::tma_load_2d_pair(smem + t * TILE, &p.tq, qf, col0, q0 + t * BQ);
+      iris::tma_load_2d_pair(smem + t * TILE + BOX, &p.tq, qf, col0 + 64, q0 + t * BQ);
+    }
+    int nk = 0, nv = 0;
+    bool ok = true;
+    auto load_k = [&]() -> bool {  // this CTA's 64 keys of key tile nk, both head-dim halves
+      const int s = nk % PK_ST;
+      const uint32_t u = (uint32_t)(nk / PK_ST);
+      if (!iris::mbar_wait(&bars->k_empty[s], (u & 1) ^ 1, abort_flag, p.status, IRIS_DEV_ERR_ATTN_PRODUCER))
+        return false;
+      const uint32_t kf = iris::mapa_shared(&bars->k_full[s], 0);
+      iris::mbar_arrive_expect_tx_cluster(kf, HALF);
+      const int krow = nk * BKV + 64 * (int)rank;
+      iris::tma_load_2d_pair(smem + P_OFF_K + s * HALF, &p.tk, kf, col0, krow);
+      iris::tma_load_2d_pair(smem + P_OFF_K + s * HALF + HALF / 2, &p.tk, kf, col0 + 64, krow);
+      nk++;
+      return true;
+    };
+    auto load_v = [&]() -> bool {  // this CTA's 64 head dims of value tile nv, all 128 keys
+      const int s = nv % PV_ST;
+      const uint32_t u = (uint32_t)(nv / PV_ST);
+      if (!iris::mbar_wait(&bars->v_empty[s], (u & 1) ^ 1, abort_flag, p.status, IRIS_DEV_ERR_ATTN_PRODUCER))
+        return false;
+      const uint32_t vf = iris::mapa_shared(&bars->v_full[s], 0);
+      iris::mbar_arrive_expect_tx_cluster(vf, HALF);
+      iris::tma_load_2d_pair(smem + P_OFF_V + s * HALF, &p.tv, vf, col0 + 64 * (int)rank, nv * BKV);
+      nv++;
+      return true;
+    };
+    while (ok && nk < (n < PK_ST ? n : PK_ST)) ok = load_k();
+    while (ok && nv < (n < PV_ST ? n : PV_ST)) ok = load_v();
+    while (ok && (nk < n || nv < n)) {
+      if (nk < n) ok = load_k();
+      if (ok && nv < n) ok = load_v();
+    }
+    if (!ok) {
+      // the stage barriers live in the even CTA: give copies still in flight
+      // (microseconds) time to land before this CTA can exit
+      const uint64_t t0 = iris::globaltimer();
+      while (iris::globaltimer() - t0 < 50000ull) {
+      }
+    }
+  } else if (warp == 1 && lane == 0 && rank == 0) {
+    // ------------------------------------------------------------ MMA issuer (even CTA)
+    const uint32_t idesc_s = iris::umma_idesc_bf16_f32(2 * BQ, BKV);
+    const uint32_t idesc_o = iris::umma_idesc_bf16_f32_bmn(2 * BQ, HD);
+    auto qk = [&](int t, int j) {  // S_t = Q_t K_j^T over the pair
+      const uint32_t qa = iris::smem_u32(smem + t * TILE);
+      const uint32_t kb = iris::smem_u32(smem + P_OFF_K + (j % PK_ST) * HALF);
+#pragma unroll
+      for (int kk = 0; kk < HD / 16; kk++) {
+        const uint32_t in = (uint32_t)((kk & 3) * 32);
+        iris::umma_bf16_pair(tmem + t * 128, iris::umma_desc_k_sw128(qa + (kk >> 2) * BOX + in),
+                             iris::umma_desc_k_sw128(kb + (kk >> 2) * (HALF / 2) + in), idesc_s, kk > 0);
+      }
+    };
+    auto pv = [&](int t, int j) {  // O_t += P_t V_j over the pair, P_t from TMEM
+      const uint32_t vb = iris::smem_u32(smem + P_OFF_V + (j % PV_ST) * HALF);
+#pragma unroll
+      for (int kk = 0; kk < BKV / 16; kk++) {
+        // B: this CTA's 64 head dims of V [keys, d] MN-major; 16 keys = 2048 B
+        const uint64_t bdesc = iris::umma_desc_mn_sw128(vb + (uint32_t)(kk * 2048), BOX, 1024);
+        iris::umma_bf16_pair_ts(tmem + 256 + t * 128, tmem + t * 128 + kk * 8, bdesc, idesc_o, (j > 0 || kk > 0));
+      }
+    };
+    bool ok = iris::mbar_wait(&bars->q_full, 0, abort_flag, p.status, IRIS_DEV_ERR_ATTN_MMA) &&
+              iris::mbar_wait(&bars->k_full[0], 0, abort_flag, p.status, IRIS_DEV_ERR_ATTN_MMA);
+    if (ok) {
+      iris::tc_fence_after();
+      for (int t = 0; t < 2; t++) {
+        qk(t, 0);
+        iris::umma_commit_pair(&bars->s_full[t]);
+      }
+      iris::umma_commit_pair(&bars->k_empty[0]);
+    }
+    for (int j = 0; j < n && ok; j++) {
+      const bool more = j + 1 < n;
+      if (!iris::mbar_wait(&bars->v_full[j % PV_ST], (uint32_t)((j / PV_ST) & 1), abort_flag, p.status,
+                           IRIS_DEV_ERR_ATTN_MMA)) {
+        ok = false;
+        break;
+      }
+      for (int t = 0; t < 2; t++) {
+        if (!iris::mbar_wait(&bars->p_full[t], (uint32_t)(j & 1), abort_flag, p.status, IRIS_DEV_ERR_ATTN_MMA)) {
+          ok = false;
+          break;
+        }
+        iris::tc_fence_after();
+        pv(t, j);
+        if (more) {
+          if (t == 0 && !iris::mbar_wait(&bars->k_full[(j + 1) % PK_ST], (uint32_t)(((j + 1) / PK_ST) & 1),
+                                         abort_flag, p.status, IRIS_DEV_ERR_ATTN_MMA)) {
+            ok = false;
+            break;
+          }
+          iris::tc_fence_after();
+          qk(t, j + 1);
+          iris::umma_commit_pair(&bars->s_full[t]);
+        }
+      }
+      if (!ok) break;
+      iris::umma_commit_pair(&bars->v_empty[j % PV_ST]);
+      if (more) iris::umma_commit_pair(&bars->k_empty[(j + 1) % PK_ST]);
+    }
+    if (ok) {
+      iris::umma_commit_pair(&bars->o_done);
+    } else {
+      iris::umma_commit_pair(&bars->drain);
+      volatile int no_abort = 0;
+      iris::mbar_wait(&bars->drain, 0, &no_abort, p.status, IRIS_DEV_ERR_ATTN_DRAIN);
+    }
+  } else if (warp >= 2) {
+    // ------------------------------------------------------------ softmax + epilogue (both CTAs)
+    const int t = warp >= 6 ? 1 : 0;
+    softmax_role<true>(p, tmem, t, warp, lane, &bars->s_full[t], nullptr, iris::mapa_shared(&bars->p_full[t], 0),
+                       &bars->o_done, abort_flag, q0 + t * BQ, col0, n);
+  }
+
+  __syncthreads();
+  iris::cluster_sync();  // no CTA leaves while the pair MMA may still read its shared memory / TMEM
+  if (warp == 1) {
+    iris::tc_fence_after();
+    iris::tmem_dealloc_pair(tmem, TMEM_COLS);
   }
 }
 
@@ -467,6 +691,8 @@ extern "C" void iris_attention_set_status(int* status) { g_attn_status = status;
 extern "C" cudaError_t iris_attention_tc_init(void) {
   if (g_attn_tc_attr) return cudaSuccess;
   cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attn_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES);
   if (e == cudaSuccess) g_attn_tc_attr = true;
   return e;
 }
@@ -480,10 +706,16 @@ extern "C" cudaError_t iris_launch_attention_tc(const void* q, int ldq, const vo
     cudaError_t e = iris_attention_tc_init();
     if (e != cudaSuccess) return e;
   }
+  static int single = -1;  // IRIS_ATTN=1cta keeps the single-CTA kernel (A/B measurements)
+  if (single < 0) {
+    const char* e = getenv("IRIS_ATTN");
+    single = (e && strcmp(e, "1cta") == 0) ? 1 : 0;
+  }
   AttnParams p;
   memset(&p, 0, sizeof(p));
+  // the pair kernel loads 64-key halves of each key tile
   if (iris_make_tmap_bf16(&p.tq, q, (uint64_t)sq, (uint64_t)heads * HD, (uint64_t)ldq, BQ) ||
-      iris_make_tmap_bf16(&p.tk, k, (uint64_t)sk, (uint64_t)heads * HD, (uint64_t)ldk, BKV) ||
+      iris_make_tmap_bf16(&p.tk, k, (uint64_t)sk, (uint64_t)heads * HD, (uint64_t)ldk, single ? BKV : 64) ||
       iris_make_tmap_bf16(&p.tv, v, (uint64_t)sk, (uint64_t)heads * HD, (uint64_t)ldk, BKV))
     return cudaErrorInvalidValue;
   p.o = static_cast<__nv_bfloat16*>(o);
@@ -493,8 +725,13 @@ extern "C" cudaError_t iris_launch_attention_tc(const void* q, int ldq, const vo
   p.scale_log2 = scale * LOG2E;
   p.kmask = key_mask;
   p.status = g_attn_status;
-  dim3 grid((sq + 2 * BQ - 1) / (2 * BQ), heads);
-  attn_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(p);
+  if (single) {
+    dim3 grid((sq + 2 * BQ - 1) / (2 * BQ), heads);
+    attn_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(p);
+  } else {
+    dim3 grid(2 * ((sq + 4 * BQ - 1) / (4 * BQ)), heads);
+    attn_pair_kernel<<<grid, NUM_THREADS, P_SMEM_BYTES, stream>>>(p);
+  }
   return cudaGetLastError();
 }
 

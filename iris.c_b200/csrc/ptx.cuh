@@ -163,6 +163,17 @@ __device__ __forceinline__ void umma_bf16_pair(uint32_t tmem_d, uint64_t adesc, 
       : "memory");
 }
 
+// Pair MMA with A read from TMEM (each CTA's own 128 lanes at tmem_a).
+__device__ __forceinline__ void umma_bf16_pair_ts(uint32_t tmem_d, uint32_t tmem_a, uint64_t bdesc, uint32_t idesc,
+                                                  uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::2.kind::f16 [%0], [%1], %2, %3, p;\n\t}" ::"r"(tmem_d),
+      "r"(tmem_a), "l"(bdesc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Arrive on the mbarrier at this shared offset in both CTAs of the pair once
 // every earlier pair MMA of this thread is complete.
 __device__ __forceinline__ void umma_commit_pair(uint64_t* bar) {

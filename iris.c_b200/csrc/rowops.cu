@@ -101,14 +101,16 @@ adaln_kernel(const float* __restrict__ x, int ldx, __nv_bfloat16* __restrict__ o
 // row sits in registers (NV float4 per lane), both reductions are warp
 // shuffles (no shared memory or block barriers), and every load of the row is
 // issued before the first reduction, so each warp keeps NV*512 bytes in
-// flight.  Same two-pass mean / variance as the block kernel above.
+// flight.  One-warp blocks: the register budget allows ~11 such warps per SM,
+// so a 1536-row launch runs as a single wave.  Same two-pass mean / variance
+// as the block kernel above.
 template <int NV>
-__global__ void __launch_bounds__(256)
+__global__ void __launch_bounds__(32)
 adaln_warp_kernel(const float* __restrict__ x, int ldx, __nv_bfloat16* __restrict__ out, int ldout, int rows,
                   const float* __restrict__ shift0, const float* __restrict__ scale0,
                   const float* __restrict__ shift1, const float* __restrict__ scale1, int split, float eps) {
-  const int row = blockIdx.x * 8 + (threadIdx.x >> 5);
-  const int lane = threadIdx.x & 31;
+  const int row = blockIdx.x;
+  const int lane = threadIdx.x;
   if (row >= rows) return;
   constexpr int cols = NV * 128;
   const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * ldx);
@@ -444,11 +446,9 @@ cudaError_t iris_launch_adaln(const float* x, int ldx, void* out, int ldout, int
     const float* sc1 = scale1 ? scale1 : scale0;
     __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out);
     if (cols == 3072)
-      adaln_warp_kernel<24><<<(rows + 7) / 8, 256, 0, stream>>>(x, ldx, o, ldout, rows, shift0, scale0, sh1, sc1,
-                                                                split, eps);
+      adaln_warp_kernel<24><<<rows, 32, 0, stream>>>(x, ldx, o, ldout, rows, shift0, scale0, sh1, sc1, split, eps);
     else
-      adaln_warp_kernel<32><<<(rows + 7) / 8, 256, 0, stream>>>(x, ldx, o, ldout, rows, shift0, scale0, sh1, sc1,
-                                                                split, eps);
+      adaln_warp_kernel<32><<<rows, 32, 0, stream>>>(x, ldx, o, ldout, rows, shift0, scale0, sh1, sc1, split, eps);
     return cudaGetLastError();
   }
   adaln_kernel<<<rows, 256, 0, stream>>>(x, ldx, static_cast<__nv_bfloat16*>(out), ldout, cols,

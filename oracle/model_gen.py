@@ -250,3 +250,91 @@ def zimage_weights(cfg: dict, seed: int, std: float = 0.02, norm_mode: str = "ra
 def zimage_ffn_dim(dim: int) -> int:
     """ffn width used by the reference when no weight says otherwise: 8*dim/3 rounded up to 256."""
     return (8 * dim // 3 + 255) // 256 * 256
+
+
+# ------------------------------------------------------------------ Flux VAE
+def vae_tensor_specs(z: int = 32) -> list[tuple[str, tuple, str]]:
+    """Tensors of the Flux autoencoder as the reference's loader reads them
+    (iris_vae_load_safetensors_ex, iris_vae.c:1227-1385: base 128 channels,
+    multipliers 1/2/4/4, two resnets per encoder level and three per decoder
+    level, one attention in each mid block, batch-norm latent statistics)."""
+    mult = [1, 2, 4, 4]
+    s = []
+
+    def resblock(prefix, cin, cout):
+        s.extend([(f"{prefix}.norm1.weight", (cin,), "gn_w"), (f"{prefix}.norm1.bias", (cin,), "bias"),
+                  (f"{prefix}.conv1.weight", (cout, cin, 3, 3), "conv"), (f"{prefix}.conv1.bias", (cout,), "bias"),
+                  (f"{prefix}.norm2.weight", (cout,), "gn_w"), (f"{prefix}.norm2.bias", (cout,), "bias"),
+                  (f"{prefix}.conv2.weight", (cout, cout, 3, 3), "conv"), (f"{prefix}.conv2.bias", (cout,), "bias")])
+        if cin != cout:
+            s.extend([(f"{prefix}.conv_shortcut.weight", (cout, cin, 1, 1), "conv"),
+                      (f"{prefix}.conv_shortcut.bias", (cout,), "bias")])
+
+    def attn(prefix, c):
+        s.extend([(f"{prefix}.group_norm.weight", (c,), "gn_w"), (f"{prefix}.group_norm.bias", (c,), "bias")])
+        for n in ("to_q", "to_k", "to_v", "to_out.0"):
+            s.extend([(f"{prefix}.{n}.weight", (c, c), "conv"), (f"{prefix}.{n}.bias", (c,), "bias")])
+
+    s.extend([("encoder.conv_in.weight", (128, 3, 3, 3), "conv"), ("encoder.conv_in.bias", (128,), "bias")])
+    for level in range(4):
+        ch = 128 * mult[level]
+        prev = 128 if level == 0 else 128 * mult[level - 1]
+        for r in range(2):
+            resblock(f"encoder.down_blocks.{level}.resnets.{r}", prev if (r == 0 and level > 0) else ch, ch)
+    for i in range(3):
+        ch = 128 * mult[i]
+        s.extend([(f"encoder.down_blocks.{i}.downsamplers.0.conv.weight", (ch, ch, 3, 3), "conv"),
+                  (f"encoder.down_blocks.{i}.downsamplers.0.conv.bias", (ch,), "bias")])
+    resblock("encoder.mid_block.resnets.0", 512, 512)
+    attn("encoder.mid_block.attentions.0", 512)
+    resblock("encoder.mid_block.resnets.1", 512, 512)
+    s.extend([("encoder.conv_norm_out.weight", (512,), "gn_w"), ("encoder.conv_norm_out.bias", (512,), "bias"),
+              ("encoder.conv_out.weight", (2 * z, 512, 3, 3), "conv"), ("encoder.conv_out.bias", (2 * z,), "bias"),
+              ("quant_conv.weight", (2 * z, 2 * z, 1, 1), "conv"), ("quant_conv.bias", (2 * z,), "bias")])
+    s.extend([("decoder.conv_in.weight", (512, z, 3, 3), "conv"), ("decoder.conv_in.bias", (512,), "bias")])
+    resblock("decoder.mid_block.resnets.0", 512, 512)
+    attn("decoder.mid_block.attentions.0", 512)
+    resblock("decoder.mid_block.resnets.1", 512, 512)
+    for level in range(3, -1, -1):
+        ch = 128 * mult[level]
+        prev = 512 if level == 3 else 128 * mult[level + 1]
+        for r in range(3):
+            resblock(f"decoder.up_blocks.{3 - level}.resnets.{r}", prev if r == 0 else ch, ch)
+    for i in range(3):
+        ch = 128 * mult[3 - i]
+        s.extend([(f"decoder.up_blocks.{i}.upsamplers.0.conv.weight", (ch, ch, 3, 3), "conv"),
+                  (f"decoder.up_blocks.{i}.upsamplers.0.conv.bias", (ch,), "bias")])
+    s.extend([("decoder.conv_norm_out.weight", (128,), "gn_w"), ("decoder.conv_norm_out.bias", (128,), "bias"),
+              ("decoder.conv_out.weight", (3, 128, 3, 3), "conv"), ("decoder.conv_out.bias", (3,), "bias"),
+              ("bn.running_mean", (4 * z,), "bn_mean"), ("bn.running_var", (4 * z,), "bn_var"),
+              ("post_quant_conv.weight", (z, z, 1, 1), "conv"), ("post_quant_conv.bias", (z,), "bias")])
+    return s
+
+
+def make_vae_model(model_dir: str, seed: int, z: int = 32) -> str:
+    """Random Flux VAE (bf16 safetensors) under model_dir/vae/; returns the
+    weights file.  Convolutions ~ N(0, 1/fan_in) so activations keep O(1)
+    scale through the decoder; GroupNorm scales 1 + N(0, 0.1); batch-norm
+    latent statistics mean N(0, 0.5), variance 1 + |N(0, 0.2)|."""
+    os.makedirs(os.path.join(model_dir, "vae"), exist_ok=True)
+    with open(os.path.join(model_dir, "vae", "config.json"), "w") as f:
+        json.dump({"_class_name": "AutoencoderKLFlux2", "latent_channels": z}, f)
+    bits = {}
+    for name, shp, kind in vae_tensor_specs(z):
+        rng = np.random.default_rng([seed, zlib.crc32(name.encode())])
+        g = rng.standard_normal(shp, dtype=np.float32)
+        if kind == "conv":
+            x = g / np.float32(np.sqrt(np.prod(shp[1:])))
+        elif kind == "gn_w":
+            x = 1.0 + 0.1 * g
+        elif kind == "bn_mean":
+            x = 0.5 * g
+        elif kind == "bn_var":
+            x = 1.0 + np.abs(0.2 * g)
+        else:
+            x = 0.02 * g
+        bits[name] = f32_to_bf16_bits(x.astype(np.float32))
+    path = os.path.join(model_dir, "vae", "diffusion_pytorch_model.safetensors")
+    write_safetensors(path, bits)
+    return path
+

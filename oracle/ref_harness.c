@@ -22,6 +22,8 @@
  *   ref_zimage_schedule      -> iris_zimage_schedule                (iris_sample.c:216)
  *   ref_zi_load/forward      -> zi_transformer_load_safetensors / zi_transformer_forward
  *                                                                    (iris_transformer_zimage.c:2164, :1696)
+ *   ref_vae_decode           -> iris_vae_load_safetensors_ex + iris_vae_decode
+ *                                                                    (iris_vae.c:1227, :835)
  *
  * Build: see oracle/Makefile.  Outputs go to oracle/_ref/ only.
  */
@@ -246,3 +248,36 @@ int ref_sample_euler_zimage(void *tf, float *z, int c, int h, int w, int ps,
     free(r);
     return 0;
 }
+
+/* ------------------------------------------------------------------ VAE decode
+ * The reference's CPU decoder on a model file (Flux layout: batch-norm latent
+ * statistics, post-quant conv, z_channels latent channels before the 2x2
+ * patchify).  Writes the uint8 RGB image (height x width x 3) to out_rgb,
+ * which must hold 3 * (16 lh) * (16 lw) bytes. */
+typedef struct iris_vae iris_vae_t;
+extern iris_vae_t *iris_vae_load_safetensors_ex(safetensors_file_t *sf, int z_channels,
+                                                float scaling_factor, float shift_factor);
+extern void iris_vae_free(iris_vae_t *vae);
+extern iris_image *iris_vae_decode(iris_vae_t *vae, const float *latent, int batch,
+                                   int latent_h, int latent_w);
+
+int ref_vae_decode(const char *vae_file, int z_channels, const float *latent, int lh, int lw,
+                   uint8_t *out_rgb, int *out_w, int *out_h) {
+    safetensors_file_t *sf = safetensors_open(vae_file);
+    if (!sf) return -1;
+    iris_vae_t *vae = iris_vae_load_safetensors_ex(sf, z_channels, 0.0f, 0.0f);
+    if (!vae) { safetensors_close(sf); return -2; }
+    iris_image *img = iris_vae_decode(vae, latent, 1, lh, lw);
+    int rc = -3;
+    if (img) {
+        *out_w = img->width;
+        *out_h = img->height;
+        memcpy(out_rgb, img->data, (size_t)img->width * img->height * img->channels);
+        rc = img->channels;
+        iris_image_free(img);
+    }
+    iris_vae_free(vae);
+    safetensors_close(sf);
+    return rc;
+}
+

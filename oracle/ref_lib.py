@@ -58,9 +58,29 @@ class RefLib:
         L.ref_sample_euler_zimage.argtypes = [C.c_void_p, _fp, C.c_int, C.c_int, C.c_int, C.c_int,
                                               _fp, C.c_int, _fp, C.c_int, _fp]
         L.ref_set_threads.argtypes = [C.c_int]
+        L.ref_vae_decode.argtypes = [C.c_char_p, C.c_int, _fp, C.c_int, C.c_int, C.POINTER(C.c_uint8),
+                                     C.POINTER(C.c_int), C.POINTER(C.c_int)]
 
     def set_threads(self, n: int):
         self.lib.ref_set_threads(n)
+
+    def vae_decode(self, vae_file: str, latent: np.ndarray, z: int = 32) -> np.ndarray:
+        """Reference CPU decode (iris_vae_decode) of a [4z, h, w] latent -> uint8 [16h, 16w, 3]."""
+        lat = np.ascontiguousarray(latent, np.float32)
+        _, h, w = lat.shape
+        out = np.zeros(3 * 16 * h * 16 * w, np.uint8)
+        ow, oh = C.c_int(0), C.c_int(0)
+        rc = self.lib.ref_vae_decode(vae_file.encode(), z, _f(lat), h, w,
+                                     out.ctypes.data_as(C.POINTER(C.c_uint8)), C.byref(ow), C.byref(oh))
+        if rc != 3:
+            raise RuntimeError(f"reference VAE decode failed ({rc})")
+        return out[: oh.value * ow.value * 3].reshape(oh.value, ow.value, 3)
+
+
+def psnr(a: np.ndarray, b: np.ndarray) -> float:
+    """PSNR (dB) of two uint8 images."""
+    mse = np.mean((a.astype(np.float64) - b.astype(np.float64)) ** 2)
+    return float("inf") if mse == 0 else float(10.0 * np.log10(255.0 ** 2 / mse))
 
 
 class RefFlux:
