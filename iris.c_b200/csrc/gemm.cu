@@ -217,7 +217,18 @@ __device__ __forceinline__ void epi_plain_chunk(const IrisGemmParams& p, uint32_
 #pragma unroll
       for (int e = 0; e < 32; e++) v[e] += __ldg(p.bias + c + e);
     }
-    if (p.mode == IRIS_EPI_BF16) {
+    if (p.mode == IRIS_EPI_BF16 || p.mode == IRIS_EPI_GATE_BF16) {
+      if (p.mode == IRIS_EPI_GATE_BF16) {
+        const float4* gp = reinterpret_cast<const float4*>(p.gate[g] + c);
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          const float4 gg = __ldg(gp + e);
+          v[4 * e] *= gg.x;
+          v[4 * e + 1] *= gg.y;
+          v[4 * e + 2] *= gg.z;
+          v[4 * e + 3] *= gg.w;
+        }
+      }
       store_bf16x32(reinterpret_cast<__nv_bfloat16*>(p.out) + (size_t)row * p.ldo + c, v);
     } else if (p.mode == IRIS_EPI_F32) {
       float4* d = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (size_t)row * p.ldo + c);
@@ -241,6 +252,17 @@ __device__ __forceinline__ void epi_plain_chunk(const IrisGemmParams& p, uint32_
       }
     }
   }
+}
+
+// Gated-residual epilogues read the residual rows of their tile: each
+// epilogue thread asks L2 for its row's slice of the tile one main loop ahead
+// (the weights streaming through L2 would otherwise leave it a DRAM miss
+// right when the tensor pipe waits for the accumulator).
+__device__ __forceinline__ void prefetch_resid_row(const IrisGemmParams& p, int g, int row_local, int n0) {
+  if (p.mode != IRIS_EPI_RESID_GATE || p.resid_store || row_local >= p.rows[g]) return;
+  const float* a = reinterpret_cast<const float*>(p.out) + (size_t)(p.row0[g] + row_local) * p.ldo + n0;
+  const int bytes = min(p.bn, p.N - n0) * 4;
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(a), "r"(bytes) : "memory");
 }
 
 // Epilogue of one accumulator tile for this thread's row (all modes); the
@@ -385,9 +407,19 @@ gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     float* stage = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES + 1024 + (warp - 2) * EPI_WARP_BYTES);
     int it = 0;
+    if (blockIdx.x < total) {
+      int g, ml, n0;
+      tile_coords(p, blockIdx.x, mt0, mtot, g, ml, n0);
+      prefetch_resid_row(p, g, ml * BM + quarter * 32 + lane, n0);
+    }
     for (int t = blockIdx.x; t < total; t += gridDim.x, it++) {
       int buf = it & 1;
       uint32_t use = (uint32_t)(it >> 1);
+      if (t + (int)gridDim.x < total) {
+        int g2, ml2, n02;
+        tile_coords(p, t + gridDim.x, mt0, mtot, g2, ml2, n02);
+        prefetch_resid_row(p, g2, ml2 * BM + quarter * 32 + lane, n02);
+      }
       if (!iris::mbar_wait(&bars->tfull[buf], use & 1, abort_flag, p.status, IRIS_DEV_ERR_GEMM_EPILOGUE)) break;
       iris::tc_fence_after();
       int g, ml, n0;
@@ -554,9 +586,19 @@ gemm_tc2_kernel(const __grid_constant__ IrisGemmParams p) {
     const uint32_t tempty_c0 = iris::mapa_shared(&bars->tempty[0], 0);
     const uint32_t tempty_c1 = iris::mapa_shared(&bars->tempty[1], 0);
     int it = 0;
+    if (pair < total) {
+      int g, ml, n0;
+      tile_coords(p, pair, mt0, mtot, g, ml, n0);
+      prefetch_resid_row(p, g, ml * BM2 + 128 * (int)rank + quarter * 32 + lane, n0);
+    }
     for (int t = pair; t < total; t += npairs, it++) {
       int buf = it & 1;
       uint32_t use = (uint32_t)(it >> 1);
+      if (t + npairs < total) {
+        int g2, ml2, n02;
+        tile_coords(p, t + npairs, mt0, mtot, g2, ml2, n02);
+        prefetch_resid_row(p, g2, ml2 * BM2 + 128 * (int)rank + quarter * 32 + lane, n02);
+      }
       if (!iris::mbar_wait(&bars->tfull[buf], use & 1, abort_flag, p.status, IRIS_DEV_ERR_GEMM_EPILOGUE)) break;
       iris::tc_fence_after();
       int g, ml, n0;

@@ -30,6 +30,8 @@ enum {
                                  then pair RoPE from rope_cos/sin[row][64]; bf16 stores     */
     IRIS_EPI_SWIGLU = 5,      /* 256-col tiles hold [gate 128 | up 128] of 128 features:
                                  mlp_out[row, mlp_col0 + f] = SiLU(gate) * up (bf16)       */
+    IRIS_EPI_GATE_BF16 = 7,   /* out bf16 [row, ldo] = gate[g][col] * acc (tensor-parallel
+                                 partial of a gated residual update)                      */
     IRIS_EPI_SINGLE = 6,      /* cols < 3H as IRIS_EPI_QKV, cols >= 3H as IRIS_EPI_SWIGLU   */
 };
 
@@ -95,6 +97,15 @@ void iris_attention_set_status(int *status);
 
 /* ------------------------------------------------------------------ row kernels */
 /* out_bf16[r] = (1 + scale_g) * LayerNorm(x[r]) + shift_g, g = (r >= split) */
+/* as iris_launch_adaln, first adding a pending bf16 residual update to x
+ * (x += delta, written back) when delta is not NULL */
+cudaError_t iris_launch_adaln_delta(float *x, int ldx, const void *delta, int ld_delta, void *out, int ldout,
+                                    int rows, int cols, const float *shift0, const float *scale0,
+                                    const float *shift1, const float *scale1, int split, float eps,
+                                    cudaStream_t stream);
+/* x[row, col] += delta[row, col] (f32 += bf16) */
+cudaError_t iris_launch_add_bf16_rows(float *x, int ldx, const void *delta, int ld_delta, int rows, int cols,
+                                      cudaStream_t stream);
 cudaError_t iris_launch_adaln(const float *x, int ldx, void *out, int ldout, int rows, int cols,
                               const float *shift0, const float *scale0, const float *shift1,
                               const float *scale1, int split, float eps, cudaStream_t stream);

@@ -106,17 +106,32 @@ adaln_kernel(const float* __restrict__ x, int ldx, __nv_bfloat16* __restrict__ o
 // as the block kernel above.
 template <int NV>
 __global__ void __launch_bounds__(32)
-adaln_warp_kernel(const float* __restrict__ x, int ldx, __nv_bfloat16* __restrict__ out, int ldout, int rows,
+adaln_warp_kernel(float* __restrict__ x, int ldx, const __nv_bfloat16* __restrict__ delta, int ld_delta,
+                  __nv_bfloat16* __restrict__ out, int ldout, int rows,
                   const float* __restrict__ shift0, const float* __restrict__ scale0,
                   const float* __restrict__ shift1, const float* __restrict__ scale1, int split, float eps) {
   const int row = blockIdx.x;
   const int lane = threadIdx.x;
   if (row >= rows) return;
   constexpr int cols = NV * 128;
-  const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * ldx);
+  float4* xr = reinterpret_cast<float4*>(x + (size_t)row * ldx);
   float4 v[NV];
 #pragma unroll
   for (int i = 0; i < NV; i++) v[i] = xr[lane + 32 * i];
+  if (delta) {  // pending tensor-parallel residual update, folded in here
+    const uint2* dr = reinterpret_cast<const uint2*>(delta + (size_t)row * ld_delta);
+#pragma unroll
+    for (int i = 0; i < NV; i++) {
+      const uint2 d = dr[lane + 32 * i];
+      const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&d.x));
+      const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&d.y));
+      v[i].x += a.x;
+      v[i].y += a.y;
+      v[i].z += b.x;
+      v[i].w += b.y;
+      xr[lane + 32 * i] = v[i];
+    }
+  }
   float s = 0.f;
 #pragma unroll
   for (int i = 0; i < NV; i++) s += (v[i].x + v[i].y) + (v[i].z + v[i].w);
@@ -146,6 +161,23 @@ adaln_warp_kernel(const float* __restrict__ x, int ldx, __nv_bfloat16* __restric
     float y3 = (1.0f + b.w) * ((v[i].w - mean) * rstd) + a.w;
     o[c] = make_uint2(pack2(y0, y1), pack2(y2, y3));
   }
+}
+
+__global__ void add_bf16_rows_kernel(float* __restrict__ x, int ldx, const __nv_bfloat16* __restrict__ d, int ldd,
+                                     int cols) {
+  const int row = blockIdx.y;
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (c >= cols) return;
+  float4* xp = reinterpret_cast<float4*>(x + (size_t)row * ldx + c);
+  const uint2 dv = *reinterpret_cast<const uint2*>(d + (size_t)row * ldd + c);
+  const float2 a = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&dv.x));
+  const float2 b = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&dv.y));
+  float4 v = *xp;
+  v.x += a.x;
+  v.y += a.y;
+  v.z += b.x;
+  v.w += b.y;
+  *xp = v;
 }
 
 // ------------------------------------------------------------------ GEMV
@@ -438,17 +470,42 @@ extern "C" {
 cudaError_t iris_launch_adaln(const float* x, int ldx, void* out, int ldout, int rows, int cols,
                               const float* shift0, const float* scale0, const float* shift1,
                               const float* scale1, int split, float eps, cudaStream_t stream) {
+  return iris_launch_adaln_delta(const_cast<float*>(x), ldx, nullptr, 0, out, ldout, rows, cols, shift0, scale0,
+                                 shift1, scale1, split, eps, stream);
+}
+
+cudaError_t iris_launch_add_bf16_rows(float* x, int ldx, const void* delta, int ld_delta, int rows, int cols,
+                                      cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
-  if ((cols & 3) || cols > 256 * 4 * ADALN_MAXV || (ldx & 3) || (ldout & 3))
+  if ((cols & 3) || (ldx & 3) || (ld_delta & 3)) return cudaErrorInvalidValue;
+  add_bf16_rows_kernel<<<dim3((cols / 4 + 255) / 256, rows), 256, 0, stream>>>(
+      x, ldx, static_cast<const __nv_bfloat16*>(delta), ld_delta, cols);
+  return cudaGetLastError();
+}
+
+cudaError_t iris_launch_adaln_delta(float* x, int ldx, const void* delta_v, int ld_delta, void* out, int ldout,
+                                    int rows, int cols, const float* shift0, const float* scale0,
+                                    const float* shift1, const float* scale1, int split, float eps,
+                                    cudaStream_t stream) {
+  if (rows <= 0) return cudaSuccess;
+  if ((cols & 3) || cols > 256 * 4 * ADALN_MAXV || (ldx & 3) || (ldout & 3) || (ld_delta & 3))
     return cudaErrorInvalidValue;
+  const __nv_bfloat16* delta = static_cast<const __nv_bfloat16*>(delta_v);
+  if (delta && cols != 3072 && cols != 4096) {
+    cudaError_t e = iris_launch_add_bf16_rows(x, ldx, delta, ld_delta, rows, cols, stream);
+    if (e != cudaSuccess) return e;
+    delta = nullptr;
+  }
   if (cols == 3072 || cols == 4096) {
     const float* sh1 = shift1 ? shift1 : shift0;
     const float* sc1 = scale1 ? scale1 : scale0;
     __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out);
     if (cols == 3072)
-      adaln_warp_kernel<24><<<rows, 32, 0, stream>>>(x, ldx, o, ldout, rows, shift0, scale0, sh1, sc1, split, eps);
+      adaln_warp_kernel<24><<<rows, 32, 0, stream>>>(x, ldx, delta, ld_delta, o, ldout, rows, shift0, scale0, sh1,
+                                                     sc1, split, eps);
     else
-      adaln_warp_kernel<32><<<rows, 32, 0, stream>>>(x, ldx, o, ldout, rows, shift0, scale0, sh1, sc1, split, eps);
+      adaln_warp_kernel<32><<<rows, 32, 0, stream>>>(x, ldx, delta, ld_delta, o, ldout, rows, shift0, scale0, sh1,
+                                                     sc1, split, eps);
     return cudaGetLastError();
   }
   adaln_kernel<<<rows, 256, 0, stream>>>(x, ldx, static_cast<__nv_bfloat16*>(out), ldout, cols,
