@@ -560,6 +560,7 @@ def run_config(args):
             ms, launches = timed(rc_fn, args.steps)
             per = ms / args.steps
             wb = model.weight_bytes()
+            out["by_launch_name"] = by_name(prof)
             out.update(metric="transformer forwards/s (Klein-4B 64x64, 16 img + 64 txt tokens, t=1.0)",
                        value=units * 1000.0 / per, unit="forwards/s", ms_per_step=per, gpu_launches=int(launches),
                        roofline={"bound": "hbm", "achieved": wb / (per / 1000.0) / 1e9, "peak": peaks["hbm_gbs"],

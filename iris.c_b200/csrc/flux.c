@@ -53,6 +53,8 @@ typedef struct {
     float *hidden, *lat_in, *out, *txt_f32, *rope_cos, *rope_sin;
     uint16_t *xmod, *q, *k, *v, *attn, *mlp, *cat, *tok_img, *tok_txt;
     uint16_t *delta;        /* tensor parallelism: summed bf16 residual update [S, H] */
+    float *ws;              /* split-K workspace of short sequences (NULL otherwise) */
+    size_t ws_bytes;
     int delta_pending;      /* (while enqueueing) delta not yet added to hidden */
     CUtensorMap tm_xmod, tm_attn, tm_mlp, tm_cat, tm_tok_img, tm_tok_txt;
     cudaGraph_t graph;
@@ -432,6 +434,7 @@ static void plan_free(flux_plan_t *P) {
     iris_dfree(P->rope_cos); iris_dfree(P->rope_sin); iris_dfree(P->xmod); iris_dfree(P->q);
     iris_dfree(P->k); iris_dfree(P->v); iris_dfree(P->attn); iris_dfree(P->mlp);
     iris_dfree(P->cat); iris_dfree(P->tok_img); iris_dfree(P->tok_txt); iris_dfree(P->delta);
+    iris_dfree(P->ws);
     memset(P, 0, sizeof(*P));
 }
 
@@ -513,6 +516,10 @@ static int plan_ensure(iris_cuda_flux_t *tf, int s_txt, int img_h, int img_w,
     PA(P->tok_img, (size_t)P->n_img_total * C * 2);
     PA(P->tok_txt, (size_t)s_txt * T * 2);
     if (tf->tp > 1) PA(P->delta, sH * 2);
+    if (S < 512) {  /* few GEMM tiles: room for 16 K splits of the widest linear */
+        P->ws_bytes = (size_t)16 * S * (size_t)(H + tf->F > T ? H + tf->F : T) * 4;
+        PA(P->ws, P->ws_bytes);
+    }
 #undef PA
     if (iris_mk_tmap(&P->tm_xmod, P->xmod, S, H, H, 128) ||
         iris_mk_tmap(&P->tm_attn, P->attn, S, Hl, Hl, 128) ||
@@ -541,8 +548,10 @@ oom:
 }
 
 /* ------------------------------------------------------------------ forward */
-static void gp_init(IrisGemmParams *p, const CUtensorMap *ta, int N, int K, int mode) {
+static void gp_init(IrisGemmParams *p, const flux_plan_t *P, const CUtensorMap *ta, int N, int K, int mode) {
     memset(p, 0, sizeof(*p));
+    p->ws = P->ws;  /* split-K workspace of short sequences */
+    p->ws_bytes = P->ws_bytes;
     p->tmap_a = *ta;
     p->N = N;
     p->K = K;
@@ -594,7 +603,9 @@ static void enq_gemm(enq_t *E, const IrisGemmParams *p, const char *what) {
         out_bytes = (3.0 * p->H * 2.0 + (p->N - 3.0 * p->H)) / p->N;
     }
     double bytes = rows * p->K * 2.0 + (double)p->ngroups * p->N * p->K * 2.0 + rows * p->N * out_bytes;
-    enq_x(E, iris_launch_gemm(p, g_rt.num_sms, g_rt.stream), what, 2.0 * rows * p->N * p->K, bytes);
+    int launches = 1;
+    enq_x(E, iris_launch_gemm_ex(p, g_rt.num_sms, g_rt.stream, &launches), what, 2.0 * rows * p->N * p->K, bytes);
+    E->kernels += (uint64_t)(launches - 1);
 }
 
 /* Tensor parallelism: the output projections of a shard write their gated
@@ -655,12 +666,12 @@ static void enq_embed(iris_cuda_flux_t *tf, enq_t *E) {
         row += n;
     }
     enq(E, iris_launch_f32_to_bf16(P->txt_f32, P->tok_txt, (long)St * T, st), "txt_bf16");
-    gp_init(&gp, &P->tm_tok_txt, H, T, IRIS_EPI_F32);
+    gp_init(&gp, P, &P->tm_tok_txt, H, T, IRIS_EPI_F32);
     gp_group(&gp, 0, &tf->tm_ctx, 0, St);
     gp.out = P->hidden;
     gp.ldo = H;
     enq_gemm(E, &gp, "txt_in");
-    gp_init(&gp, &P->tm_tok_img, H, C, IRIS_EPI_F32);
+    gp_init(&gp, P, &P->tm_tok_img, H, C, IRIS_EPI_F32);
     gp_group(&gp, 0, &tf->tm_x, 0, Si);
     gp.out = P->hidden + (size_t)St * H;
     gp.ldo = H;
@@ -677,7 +688,7 @@ static void enq_double(iris_cuda_flux_t *tf, int i, enq_t *E) {
     flux_dbl_t *b = &tf->dbl[i];
     IrisGemmParams gp;
     enq_x(E, adaln_rows(tf, 0, S, mt, mt + H, mi, mi + H, St), "adaln1", 0.0, 6.0 * S * (double)H);
-    gp_init(&gp, &P->tm_xmod, 3 * Hl, H, IRIS_EPI_QKV);
+    gp_init(&gp, P, &P->tm_xmod, 3 * Hl, H, IRIS_EPI_QKV);
     gp.bn = bn_for(3 * Hl);
     gp_group(&gp, 0, &b->tm_qkv[0], 0, St);
     gp_group(&gp, 1, &b->tm_qkv[1], St, Si);
@@ -689,7 +700,7 @@ static void enq_double(iris_cuda_flux_t *tf, int i, enq_t *E) {
     enq_x(E, iris_launch_attention(P->q, Hl, P->k, P->v, Hl, P->attn, Hl, S, S, NHl,
                                    1.0f / sqrtf(128.0f), NULL, st), "dbl_attn",
           4.0 * S * S * (double)Hl, 8.0 * S * (double)Hl);
-    gp_init(&gp, &P->tm_attn, H, Hl, IRIS_EPI_RESID_GATE);
+    gp_init(&gp, P, &P->tm_attn, H, Hl, IRIS_EPI_RESID_GATE);
     gp_group(&gp, 0, &b->tm_out[0], 0, St);
     gp_group(&gp, 1, &b->tm_out[1], St, Si);
     gp.out = P->hidden; gp.ldo = H;
@@ -699,12 +710,12 @@ static void enq_double(iris_cuda_flux_t *tf, int i, enq_t *E) {
     enq_allreduce(tf, E);
     enq_x(E, adaln_rows(tf, 0, S, mt + 3 * H, mt + 4 * H, mi + 3 * H, mi + 4 * H, St), "adaln2", 0.0,
           6.0 * S * (double)H);
-    gp_init(&gp, &P->tm_xmod, 2 * Fl, H, IRIS_EPI_SWIGLU);
+    gp_init(&gp, P, &P->tm_xmod, 2 * Fl, H, IRIS_EPI_SWIGLU);
     gp_group(&gp, 0, &b->tm_in[0], 0, St);
     gp_group(&gp, 1, &b->tm_in[1], St, Si);
     gp.mlp_out = P->mlp; gp.ld_mlp = Fl; gp.mlp_col0 = 0; gp.swiglu_base = 0;
     enq_gemm(E, &gp, "dbl_mlp_in");
-    gp_init(&gp, &P->tm_mlp, H, Fl, IRIS_EPI_RESID_GATE);
+    gp_init(&gp, P, &P->tm_mlp, H, Fl, IRIS_EPI_RESID_GATE);
     gp_group(&gp, 0, &b->tm_down[0], 0, St);
     gp_group(&gp, 1, &b->tm_down[1], St, Si);
     gp.out = P->hidden; gp.ldo = H;
@@ -723,7 +734,7 @@ static void enq_single(iris_cuda_flux_t *tf, int i, enq_t *E) {
     flux_sgl_t *b = &tf->sgl[i];
     IrisGemmParams gp;
     enq_x(E, adaln_rows(tf, 0, S, ms, ms + H, NULL, NULL, S), "adaln_s", 0.0, 6.0 * S * (double)H);
-    gp_init(&gp, &P->tm_xmod, 3 * Hl + 2 * Fl, H, IRIS_EPI_SINGLE);
+    gp_init(&gp, P, &P->tm_xmod, 3 * Hl + 2 * Fl, H, IRIS_EPI_SINGLE);
     gp_group(&gp, 0, &b->tm_fused, 0, S);
     gp.qnorm[0] = b->qn; gp.knorm[0] = b->kn;
     gp.rope_cos = P->rope_cos; gp.rope_sin = P->rope_sin;
@@ -733,7 +744,7 @@ static void enq_single(iris_cuda_flux_t *tf, int i, enq_t *E) {
     enq_x(E, iris_launch_attention(P->q, Hl, P->k, P->v, Hl, P->cat, Hl + Fl, S, S, NHl,
                                    1.0f / sqrtf(128.0f), NULL, st), "sgl_attn",
           4.0 * S * S * (double)Hl, 8.0 * S * (double)Hl);
-    gp_init(&gp, &P->tm_cat, H, Hl + Fl, IRIS_EPI_RESID_GATE);
+    gp_init(&gp, P, &P->tm_cat, H, Hl + Fl, IRIS_EPI_RESID_GATE);
     gp_group(&gp, 0, &b->tm_out, 0, S);
     gp.out = P->hidden; gp.ldo = H;
     gp.gate[0] = ms + 2 * H;
@@ -749,7 +760,7 @@ static void enq_final(iris_cuda_flux_t *tf, enq_t *E) {
     const float *mf = tf->mods + (size_t)15 * H;
     IrisGemmParams gp;
     enq(E, adaln_rows(tf, St, P->n_img, mf + H, mf, NULL, NULL, P->n_img), "adaln_final");
-    gp_init(&gp, &P->tm_xmod, C, H, IRIS_EPI_F32_NCHW);
+    gp_init(&gp, P, &P->tm_xmod, C, H, IRIS_EPI_F32_NCHW);
     gp.bn = 128;
     gp_group(&gp, 0, &tf->tm_proj, 0, P->n_img);
     gp.out = P->out;

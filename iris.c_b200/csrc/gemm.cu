@@ -163,15 +163,15 @@ __device__ __forceinline__ void epi_swiglu_tile(const IrisGemmParams& p, uint32_
 // this warp's shared staging tile so that every global access covers 4 rows x
 // 128 contiguous bytes (one thread per row would touch 32 rows per access).
 __device__ __forceinline__ void epi_f32_block(const IrisGemmParams& p, int g, float* stage, const float* v,
-                                              int lane, int row_first, int rows_valid, int c) {
+                                              int lane, int row_first, int rows_valid, int c, float* out_base,
+                                              int ldo, bool resid) {
   float4* st = reinterpret_cast<float4*>(stage + lane * EPI_LD);
 #pragma unroll
   for (int q = 0; q < 8; q++) st[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
   __syncwarp();
   const int rr = lane >> 3, c4 = (lane & 7) * 4;
-  const bool resid = p.mode == IRIS_EPI_RESID_GATE;
-  float* base = reinterpret_cast<float*>(p.out) + (size_t)(row_first + rr) * p.ldo + c + c4;
-  const size_t step = (size_t)4 * p.ldo;  // 4 rows per pass
+  float* base = out_base + (size_t)(row_first + rr) * ldo + c + c4;
+  const size_t step = (size_t)4 * ldo;  // 4 rows per pass
   // all residual loads in flight before the first store
   float4 h[8];
 #pragma unroll
@@ -197,19 +197,27 @@ __device__ __forceinline__ void epi_f32_block(const IrisGemmParams& p, int g, fl
 
 __device__ __forceinline__ void epi_plain_chunk(const IrisGemmParams& p, uint32_t taddr, int g,
                                                 int row, int row_local, bool valid, int col0, float* stage,
-                                                int lane, int rows_valid) {
+                                                int lane, int rows_valid, int split) {
 #pragma unroll 1
   for (int j = 0; j < 4; j++) {
     float v[32];
     iris::tmem_ld32(taddr + 32 * j, v);
     int c = col0 + 32 * j;
+    if (p.splitk > 1) {
+      // raw partial of this K range -> workspace slice `split` (reduced later)
+      const size_t span = (size_t)(p.ngroups > 1 ? p.row0[1] + p.rows[1] : p.row0[0] + p.rows[0]);
+      epi_f32_block(p, g, stage, v, lane, row - lane, rows_valid, c, p.ws + (size_t)split * span * p.N, p.N,
+                    false);
+      continue;
+    }
     if (p.mode == IRIS_EPI_RESID_GATE || p.mode == IRIS_EPI_F32) {
       if (p.bias) {
 #pragma unroll
         for (int e = 0; e < 32; e++) v[e] += __ldg(p.bias + c + e);
       }
       // warp-collective: every lane takes part, rows_valid masks the stores
-      epi_f32_block(p, g, stage, v, lane, row - lane, rows_valid, c);
+      epi_f32_block(p, g, stage, v, lane, row - lane, rows_valid, c, reinterpret_cast<float*>(p.out), p.ldo,
+                    p.mode == IRIS_EPI_RESID_GATE);
       continue;
     }
     if (!valid) continue;
@@ -268,7 +276,8 @@ __device__ __forceinline__ void prefetch_resid_row(const IrisGemmParams& p, int 
 // Epilogue of one accumulator tile for this thread's row (all modes); the
 // warp's 32 rows start at row - lane, rows_valid of them are real.
 __device__ __forceinline__ void epi_tile(const IrisGemmParams& p, uint32_t taddr, int g, int row, int row_local,
-                                         bool valid, int n0, float* stage, int lane, int rows_valid) {
+                                         bool valid, int n0, float* stage, int lane, int rows_valid,
+                                         int split = 0) {
   bool swiglu_tile = (p.mode == IRIS_EPI_SWIGLU) || (p.mode == IRIS_EPI_SINGLE && n0 >= p.swiglu_base);
   if (swiglu_tile) {
     epi_swiglu_tile(p, taddr, row, valid, n0);
@@ -279,7 +288,7 @@ __device__ __forceinline__ void epi_tile(const IrisGemmParams& p, uint32_t taddr
       if (p.mode == IRIS_EPI_QKV || p.mode == IRIS_EPI_SINGLE)
         epi_qkv_chunk(p, taddr + c * 128, g, row, valid, col0);
       else
-        epi_plain_chunk(p, taddr + c * 128, g, row, row_local, valid, col0, stage, lane, rows_valid);
+        epi_plain_chunk(p, taddr + c * 128, g, row, row_local, valid, col0, stage, lane, rows_valid, split);
     }
   }
 }
@@ -298,7 +307,8 @@ gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
   const int mt1 = p.ngroups > 1 ? (p.rows[1] + BM - 1) / BM : 0;
   const int mtot = mt0 + mt1;
   const int ntiles_n = (p.N + p.bn - 1) / p.bn;
-  const int total = mtot * ntiles_n;
+  const int nsplit = p.splitk > 1 ? p.splitk : 1;
+  const int total = mtot * ntiles_n * nsplit;  // work units: (tile, K split)
   const int num_kb = (p.K + BK - 1) / BK;
   const uint32_t b_bytes = (uint32_t)p.bn * BK * 2;
   const uint32_t idesc = iris::umma_idesc_bf16_f32(BM, p.bn);
@@ -331,11 +341,12 @@ gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
     uint32_t phase = 0;
     long issued = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
+    for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
       int g, ml, n0;
-      tile_coords(p, t, mt0, mtot, g, ml, n0);
+      tile_coords(p, u / nsplit, mt0, mtot, g, ml, n0);
       int arow = p.row0[g] + ml * BM;
-      for (int kb = 0; kb < num_kb; kb++) {
+      const int sp = u % nsplit, kb0 = sp * num_kb / nsplit, kb1 = (sp + 1) * num_kb / nsplit;
+      for (int kb = kb0; kb < kb1; kb++) {
         if (!iris::mbar_wait(&bars->empty[stage], phase ^ 1, abort_flag, p.status, IRIS_DEV_ERR_GEMM_PRODUCER)) {
           ok = false;
           break;
@@ -368,7 +379,7 @@ gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
     uint32_t phase = 0;
     int it = 0;
     bool ok = true;
-    for (int t = blockIdx.x; t < total && ok; t += gridDim.x, it++) {
+    for (int u = blockIdx.x; u < total && ok; u += gridDim.x, it++) {
       int buf = it & 1;
       uint32_t use = (uint32_t)(it >> 1);
       if (!iris::mbar_wait(&bars->tempty[buf], (use & 1) ^ 1, abort_flag, p.status, IRIS_DEV_ERR_GEMM_MMA)) {
@@ -377,7 +388,8 @@ gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
       }
       iris::tc_fence_after();
       uint32_t d_tmem = tmem_base + buf * 256;
-      for (int kb = 0; kb < num_kb; kb++) {
+      const int sp = u % nsplit, kb0 = sp * num_kb / nsplit, kb1 = (sp + 1) * num_kb / nsplit;
+      for (int kb = kb0; kb < kb1; kb++) {
         if (!iris::mbar_wait(&bars->full[stage], phase, abort_flag, p.status, IRIS_DEV_ERR_GEMM_MMA)) {
           ok = false;
           break;
@@ -390,7 +402,7 @@ gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
 #pragma unroll
         for (int kk = 0; kk < BK / 16; kk++) {
           // +32 bytes along K inside the 128B swizzle atom = +2 in the >>4 address field
-          iris::umma_bf16(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0);
+          iris::umma_bf16(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb != kb0 || kk != 0));
         }
         iris::umma_commit(&bars->empty[stage]);
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -407,29 +419,29 @@ gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     float* stage = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES + 1024 + (warp - 2) * EPI_WARP_BYTES);
     int it = 0;
-    if (blockIdx.x < total) {
+    if (blockIdx.x < total && nsplit == 1) {
       int g, ml, n0;
       tile_coords(p, blockIdx.x, mt0, mtot, g, ml, n0);
       prefetch_resid_row(p, g, ml * BM + quarter * 32 + lane, n0);
     }
-    for (int t = blockIdx.x; t < total; t += gridDim.x, it++) {
+    for (int u = blockIdx.x; u < total; u += gridDim.x, it++) {
       int buf = it & 1;
       uint32_t use = (uint32_t)(it >> 1);
-      if (t + (int)gridDim.x < total) {
+      if (u + (int)gridDim.x < total && nsplit == 1) {
         int g2, ml2, n02;
-        tile_coords(p, t + gridDim.x, mt0, mtot, g2, ml2, n02);
+        tile_coords(p, u + gridDim.x, mt0, mtot, g2, ml2, n02);
         prefetch_resid_row(p, g2, ml2 * BM + quarter * 32 + lane, n02);
       }
       if (!iris::mbar_wait(&bars->tfull[buf], use & 1, abort_flag, p.status, IRIS_DEV_ERR_GEMM_EPILOGUE)) break;
       iris::tc_fence_after();
       int g, ml, n0;
-      tile_coords(p, t, mt0, mtot, g, ml, n0);
+      tile_coords(p, u / nsplit, mt0, mtot, g, ml, n0);
       int row_local = ml * BM + quarter * 32 + lane;
       bool valid = row_local < p.rows[g];
       int row = p.row0[g] + row_local;
       uint32_t taddr = tmem_base + buf * 256 + ((uint32_t)(quarter * 32) << 16);
       const int rows_valid = min(32, max(0, p.rows[g] - (row_local - lane)));
-      epi_tile(p, taddr, g, row, row_local, valid, n0, stage, lane, rows_valid);
+      epi_tile(p, taddr, g, row, row_local, valid, n0, stage, lane, rows_valid, u % nsplit);
       iris::tc_fence_before();
       iris::mbar_arrive(&bars->tempty[buf]);
     }
@@ -623,6 +635,49 @@ gemm_tc2_kernel(const __grid_constant__ IrisGemmParams p) {
   }
 }
 
+// Split-K reduction: out = epilogue(sum of the K-range partials) for every
+// real row (fixed summation order, so results do not depend on scheduling).
+__global__ void splitk_reduce_kernel(const __grid_constant__ IrisGemmParams p, int span) {
+  const int row = blockIdx.y;
+  const int g = (p.ngroups > 1 && row >= p.row0[1]) ? 1 : 0;
+  const int local = row - p.row0[g];
+  if (local < 0 || local >= p.rows[g]) return;
+  const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
+  if (c >= p.N) return;
+  const size_t slice = (size_t)span * p.N;
+  const float* w = p.ws + (size_t)row * p.N + c;
+  float4 acc = *reinterpret_cast<const float4*>(w);
+  for (int s = 1; s < p.splitk; s++) {
+    const float4 b = *reinterpret_cast<const float4*>(w + s * slice);
+    acc.x += b.x;
+    acc.y += b.y;
+    acc.z += b.z;
+    acc.w += b.w;
+  }
+  if (p.bias) {
+    const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + c));
+    acc.x += b.x;
+    acc.y += b.y;
+    acc.z += b.z;
+    acc.w += b.w;
+  }
+  if (p.mode == IRIS_EPI_RESID_GATE) {
+    float4* d = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (size_t)row * p.ldo + c);
+    const float4 gg = __ldg(reinterpret_cast<const float4*>(p.gate[g] + c));
+    float4 h = p.resid_store ? make_float4(0.f, 0.f, 0.f, 0.f) : *d;
+    h.x += gg.x * acc.x;
+    h.y += gg.y * acc.y;
+    h.z += gg.z * acc.z;
+    h.w += gg.w * acc.w;
+    *d = h;
+  } else if (p.mode == IRIS_EPI_F32) {
+    *reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (size_t)row * p.ldo + c) = acc;
+  } else {  // IRIS_EPI_BF16
+    uint2 o = make_uint2(pack_bf16(acc.x, acc.y), pack_bf16(acc.z, acc.w));
+    *reinterpret_cast<uint2*>(reinterpret_cast<__nv_bfloat16*>(p.out) + (size_t)row * p.ldo + c) = o;
+  }
+}
+
 }  // namespace
 
 extern "C" int iris_make_tmap_bf16(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t cols,
@@ -686,6 +741,12 @@ extern "C" cudaError_t iris_gemm_init(void) {
 }
 
 extern "C" cudaError_t iris_launch_gemm(const IrisGemmParams* p, int num_sms, cudaStream_t stream) {
+  return iris_launch_gemm_ex(p, num_sms, stream, nullptr);
+}
+
+extern "C" cudaError_t iris_launch_gemm_ex(const IrisGemmParams* p, int num_sms, cudaStream_t stream,
+                                           int* launches) {
+  if (launches) *launches = 1;
   if (!g_gemm_attr) {
     cudaError_t e = iris_gemm_init();
     if (e != cudaSuccess) return e;
@@ -707,10 +768,29 @@ extern "C" cudaError_t iris_launch_gemm(const IrisGemmParams* p, int num_sms, cu
     return cudaGetLastError();
   }
   int mt = (p->rows[0] + BM - 1) / BM + (p->ngroups > 1 ? (p->rows[1] + BM - 1) / BM : 0);
-  long total = (long)mt * ((p->N + p->bn - 1) / p->bn);
-  if (total <= 0) return cudaSuccess;
+  long tiles = (long)mt * ((p->N + p->bn - 1) / p->bn);
+  if (tiles <= 0) return cudaSuccess;
+  // Few output tiles (a short sequence): split K so that enough CTAs stream
+  // the weights, when the caller gave a workspace and the epilogue is linear.
+  IrisGemmParams q = *p;
+  q.splitk = 1;
+  const int num_kb = (p->K + BK - 1) / BK;
+  const int span = p->ngroups > 1 ? p->row0[1] + p->rows[1] : p->row0[0] + p->rows[0];
+  if (p->ws && tiles < num_sms / 2 && num_kb >= 8 &&
+      (p->mode == IRIS_EPI_BF16 || p->mode == IRIS_EPI_F32 || p->mode == IRIS_EPI_RESID_GATE)) {
+    long s = num_sms / tiles;
+    if (s > num_kb / 4) s = num_kb / 4;
+    const long fit = (long)(p->ws_bytes / ((size_t)span * p->N * sizeof(float)));
+    if (s > fit) s = fit;
+    if (s >= 2) q.splitk = (int)s;
+  }
+  const long total = tiles * q.splitk;
   int grid = (int)(total < num_sms ? total : num_sms);
-  gemm_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(*p);
+  gemm_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(q);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess || q.splitk == 1) return e;
+  if (launches) *launches = 2;
+  splitk_reduce_kernel<<<dim3((p->N / 4 + 255) / 256, span), 256, 0, stream>>>(q, span);
   return cudaGetLastError();
 }
 

@@ -63,6 +63,12 @@ typedef struct {
     int mlp_col0;
     int swiglu_base;          /* first column of the gate/up region in N              */
     int *status;              /* device status word for bounded-wait failures         */
+    /* optional split-K workspace (f32) for launches with few output tiles: the
+       K range is split over CTAs, partial tiles go to ws [split][row][N] and a
+       reduction pass applies the epilogue (BF16, F32 and RESID_GATE modes) */
+    float *ws;
+    size_t ws_bytes;
+    int splitk;               /* set by iris_launch_gemm                              */
 } IrisGemmParams;
 
 /* Encodes a 2-D bf16 tensor map over a row-major [rows, cols] matrix with
@@ -71,6 +77,9 @@ int iris_make_tmap_bf16(CUtensorMap *m, const void *ptr, uint64_t rows, uint64_t
                         uint64_t ld, uint32_t box_rows);
 
 cudaError_t iris_launch_gemm(const IrisGemmParams *p, int num_sms, cudaStream_t stream);
+/* as iris_launch_gemm; *launches = kernels queued (2 when a split-K
+ * reduction pass follows the GEMM) */
+cudaError_t iris_launch_gemm_ex(const IrisGemmParams *p, int num_sms, cudaStream_t stream, int *launches);
 
 /* one-time kernel attribute setup (dynamic shared memory limits); called at
  * library init so that nothing but launches happens during graph capture */
