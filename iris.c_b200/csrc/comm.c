@@ -139,7 +139,11 @@ int iris_cuda_comm_init(const void *id, int world, int rank) {
     return comm_wait("communicator init");
 }
 
+static void sym_release(void);
+
 void iris_cuda_comm_destroy(void) {
+    if (g_comm.comm && g_nccl.so) iris_comm_sync_stream();
+    sym_release();
     if (g_comm.comm && g_nccl.so) {
         /* a collective that never completes (a peer gone) ends in an abort */
         if (iris_comm_sync_stream() == 0 && g_comm.comm) g_nccl.destroy(g_comm.comm);
@@ -203,3 +207,85 @@ int iris_comm_allgather_f32(const float *send, float *recv, size_t n) {
     if (r != ncclSuccess && r != ncclInProgress) return iris_fail(IRIS_CUDA_ERR_CUDA, "allgather: %s", g_nccl.error_string(r));
     return r == ncclInProgress ? comm_wait("allgather enqueue") : 0;
 }
+
+/* ------------------------------------------------------------------ symmetric memory
+ * One device arena per rank, mapped into every peer process (CUDA IPC over
+ * NVLink), bump-allocated in the same order on every rank so that an object
+ * has the same offset everywhere: a kernel reaches the peer's copy of an
+ * object by adding the offset to the peer's arena base.  The handles are
+ * exchanged with one NCCL all-gather, so no host channel is needed beyond
+ * the communicator's. */
+static struct {
+    char *local;
+    size_t bytes, used;
+    char *peer[IRIS_COMM_MAX_PEERS];
+} g_sym;
+
+static void sym_release(void) {
+    for (int p = 0; p < IRIS_COMM_MAX_PEERS; p++) {
+        if (g_sym.peer[p] && g_sym.peer[p] != g_sym.local) cudaIpcCloseMemHandle(g_sym.peer[p]);
+        g_sym.peer[p] = NULL;
+    }
+    if (g_sym.local) cudaFree(g_sym.local);
+    memset(&g_sym, 0, sizeof(g_sym));
+}
+
+int iris_comm_sym_init(size_t bytes) {
+    if (!g_comm.comm) return iris_fail(IRIS_CUDA_ERR_ARG, "no communicator");
+    if (g_comm.world > IRIS_COMM_MAX_PEERS) return iris_fail(IRIS_CUDA_ERR_ARG, "at most %d ranks", IRIS_COMM_MAX_PEERS);
+    bytes = (bytes + 4095) & ~(size_t)4095;
+    if (g_sym.local && g_sym.bytes >= bytes) { g_sym.used = 0; return 0; }
+    int rc = iris_comm_sync_stream();
+    if (rc) return rc;
+    sym_release();
+    if ((rc = iris_cuda_check(cudaMalloc((void **)&g_sym.local, bytes), "symmetric arena"))) return rc;
+    g_sym.bytes = bytes;
+    if ((rc = iris_cuda_check(cudaMemset(g_sym.local, 0, bytes), "symmetric arena"))) return rc;
+    cudaIpcMemHandle_t h;
+    if ((rc = iris_cuda_check(cudaIpcGetMemHandle(&h, g_sym.local), "ipc handle"))) return rc;
+    const size_t hb = sizeof(cudaIpcMemHandle_t);
+    uint8_t *d = NULL;
+    uint8_t all[IRIS_COMM_MAX_PEERS * sizeof(cudaIpcMemHandle_t)];
+    if ((rc = iris_cuda_check(cudaMalloc((void **)&d, hb * g_comm.world), "handle exchange"))) return rc;
+    rc = iris_cuda_check(cudaMemcpy(d + hb * g_comm.rank, &h, hb, cudaMemcpyHostToDevice), "handle exchange");
+    if (!rc) {
+        ncclResult_t r = g_nccl.all_gather(d + hb * g_comm.rank, d, hb, ncclUint8, g_comm.comm, g_rt.stream);
+        if (r != ncclSuccess && r != ncclInProgress) rc = iris_fail(IRIS_CUDA_ERR_CUDA, "handle all-gather: %s", g_nccl.error_string(r));
+        else if (r == ncclInProgress) rc = comm_wait("handle all-gather");
+    }
+    if (!rc) rc = iris_comm_sync_stream();
+    if (!rc) rc = iris_cuda_check(cudaMemcpy(all, d, hb * g_comm.world, cudaMemcpyDeviceToHost), "handle exchange");
+    cudaFree(d);
+    for (int p = 0; !rc && p < g_comm.world; p++) {
+        if (p == g_comm.rank) { g_sym.peer[p] = g_sym.local; continue; }
+        cudaIpcMemHandle_t ph;
+        memcpy(&ph, all + hb * p, hb);
+        rc = iris_cuda_check(cudaIpcOpenMemHandle((void **)&g_sym.peer[p], ph, cudaIpcMemLazyEnablePeerAccess),
+                             "open peer arena");
+    }
+    if (rc) sym_release();
+    return rc;
+}
+
+void *iris_comm_sym_alloc(size_t bytes) {
+    size_t off = (g_sym.used + 255) & ~(size_t)255;
+    if (!g_sym.local || off + bytes > g_sym.bytes) {
+        iris_fail(IRIS_CUDA_ERR_OOM, "symmetric arena exhausted (%zu + %zu > %zu)", off, bytes, g_sym.bytes);
+        return NULL;
+    }
+    g_sym.used = off + bytes;
+    return g_sym.local + off;
+}
+
+void *iris_comm_sym_peer(const void *local_ptr, int peer) {
+    if (!g_sym.local || peer < 0 || peer >= IRIS_COMM_MAX_PEERS || !g_sym.peer[peer]) return NULL;
+    return g_sym.peer[peer] + ((const char *)local_ptr - g_sym.local);
+}
+
+int iris_comm_allgather_bytes(const void *send, void *recv, size_t bytes) {
+    if (!g_comm.comm) return iris_fail(IRIS_CUDA_ERR_ARG, "no communicator");
+    ncclResult_t r = g_nccl.all_gather(send, recv, bytes, ncclUint8, g_comm.comm, g_rt.stream);
+    if (r != ncclSuccess && r != ncclInProgress) return iris_fail(IRIS_CUDA_ERR_CUDA, "allgather: %s", g_nccl.error_string(r));
+    return r == ncclInProgress ? comm_wait("allgather enqueue") : 0;
+}
+

@@ -52,10 +52,15 @@ typedef struct {
     int num_refs, ref_h[MAXREFS], ref_w[MAXREFS], ref_t[MAXREFS];
     float *hidden, *lat_in, *out, *txt_f32, *rope_cos, *rope_sin;
     uint16_t *xmod, *q, *k, *v, *attn, *mlp, *cat, *tok_img, *tok_txt;
-    uint16_t *delta;        /* tensor parallelism: summed bf16 residual update [S, H] */
+    /* tensor parallelism (symmetric memory, see comm.c): rows owned in chunks,
+       partial updates received in recv [tp][chunk][H] f32, xmod shared */
+    int chunk;
+    float *recv;
+    unsigned *flags;
+    unsigned part_i, x_i;   /* (while enqueueing) partial / xmod syncs queued in this call */
+    int part_pending;       /* a scattered update awaits the next adaLN */
     float *ws;              /* split-K workspace of short sequences (NULL otherwise) */
     size_t ws_bytes;
-    int delta_pending;      /* (while enqueueing) delta not yet added to hidden */
     CUtensorMap tm_xmod, tm_attn, tm_mlp, tm_cat, tm_tok_img, tm_tok_txt;
     cudaGraph_t graph;
     cudaGraphExec_t gexec;
@@ -430,10 +435,11 @@ static void plan_free(flux_plan_t *P) {
         cudaGraphExecDestroy(P->gexec);
         cudaGraphDestroy(P->graph);
     }
+    if (P->recv) P->xmod = NULL;  /* tensor-parallel xmod lives in the symmetric arena */
     iris_dfree(P->hidden); iris_dfree(P->lat_in); iris_dfree(P->out); iris_dfree(P->txt_f32);
     iris_dfree(P->rope_cos); iris_dfree(P->rope_sin); iris_dfree(P->xmod); iris_dfree(P->q);
     iris_dfree(P->k); iris_dfree(P->v); iris_dfree(P->attn); iris_dfree(P->mlp);
-    iris_dfree(P->cat); iris_dfree(P->tok_img); iris_dfree(P->tok_txt); iris_dfree(P->delta);
+    iris_dfree(P->cat); iris_dfree(P->tok_img); iris_dfree(P->tok_txt);
     iris_dfree(P->ws);
     memset(P, 0, sizeof(*P));
 }
@@ -499,14 +505,32 @@ static int plan_ensure(iris_cuda_flux_t *tf, int s_txt, int img_h, int img_w,
     }
     int S = P->S = s_txt + P->n_img_total;
     size_t sH = (size_t)S * H, sHl = (size_t)S * Hl;
+    const int tp = tf->tp;
+    P->chunk = (S + tp - 1) / tp;
 #define PA(p, bytes) do { if (!((p) = iris_dmalloc(bytes))) goto oom; } while (0)
-    PA(P->hidden, sH * 4);
+    PA(P->hidden, (size_t)P->chunk * tp * H * 4);  /* whole chunks: the row all-gather of run_block */
     PA(P->lat_in, (size_t)C * P->n_img_total * 4);
     PA(P->out, (size_t)C * P->n_img * 4);
     PA(P->txt_f32, (size_t)s_txt * T * 4);
     PA(P->rope_cos, (size_t)S * 64 * 4);
     PA(P->rope_sin, (size_t)S * 64 * 4);
-    PA(P->xmod, sH * 2);
+    if (tp > 1) {
+        /* collective: every rank plans the same shape at the same point */
+        const size_t recv_b = (size_t)tp * P->chunk * H * 4, xmod_b = sH * 2;
+        int rc = iris_comm_sym_init(4096 + recv_b + xmod_b + 1024);
+        if (rc) { plan_free(P); return rc; }
+        P->flags = (unsigned *)iris_comm_sym_alloc(4096);
+        P->recv = (float *)iris_comm_sym_alloc(recv_b);
+        P->xmod = (uint16_t *)iris_comm_sym_alloc(xmod_b);
+        if (!P->flags || !P->recv || !P->xmod) { plan_free(P); return IRIS_CUDA_ERR_OOM; }
+        for (int p = 0; p < tp; p++)  /* every peer's arena must be mapped before a kernel writes to it */
+            if (!iris_comm_sym_peer(P->flags, p)) {
+                plan_free(P);
+                return iris_fail(IRIS_CUDA_ERR_CUDA, "peer %d arena not mapped", p);
+            }
+    } else {
+        PA(P->xmod, sH * 2);
+    }
     PA(P->q, sHl * 2);
     PA(P->k, sHl * 2);
     PA(P->v, sHl * 2);
@@ -515,7 +539,6 @@ static int plan_ensure(iris_cuda_flux_t *tf, int s_txt, int img_h, int img_w,
     PA(P->cat, (size_t)S * (Hl + Fl) * 2);
     PA(P->tok_img, (size_t)P->n_img_total * C * 2);
     PA(P->tok_txt, (size_t)s_txt * T * 2);
-    if (tf->tp > 1) PA(P->delta, sH * 2);
     if (S < 512) {  /* few GEMM tiles: room for 16 K splits of the widest linear */
         P->ws_bytes = (size_t)16 * S * (size_t)(H + tf->F > T ? H + tf->F : T) * 4;
         PA(P->ws, P->ws_bytes);
@@ -608,35 +631,82 @@ static void enq_gemm(enq_t *E, const IrisGemmParams *p, const char *what) {
     E->kernels += (uint64_t)(launches - 1);
 }
 
-/* Tensor parallelism: the output projections of a shard write their gated
- * partial update gate * (this shard's heads / MLP columns) as bf16 into
- * `delta`; one in-place bf16 sum all-reduce gives every rank the full update,
- * which the next adaLN adds to the f32 residual stream as it reads it (so the
- * all-reduce moves 2 bytes per element instead of 4, and no extra pass over
- * the hidden state is needed). */
-static void tp_resid(const iris_cuda_flux_t *tf, IrisGemmParams *gp) {
+/* Tensor parallelism over NVLink peer memory (no collective library in the
+ * forward).  Rows are owned in chunks (rank r: [r*chunk, (r+1)*chunk)).
+ *  - an output projection scatters gate * (this shard's partial) of every row
+ *    straight into the owning rank's receive buffer (slot = this rank) from
+ *    its GEMM epilogue, so the transfer overlaps the remaining tiles, then
+ *    signals arrival;
+ *  - the next adaLN runs on the owned rows only: it waits for all ranks'
+ *    partials, adds them in rank order to the f32 residual stream, normalises
+ *    and writes the bf16 row into every rank's xmod, then signals;
+ *  - a GEMM that reads xmod waits for every rank's rows before its first load.
+ * Sync indices count from per-rank device bases advanced at the end of each
+ * call, so a captured forward graph replays correctly. */
+static void tp_fill(const iris_cuda_flux_t *tf, IrisTpParams *t, unsigned wait_x) {
+    const flux_plan_t *P = &tf->plan;
+    memset(t, 0, sizeof(*t));
     if (tf->tp <= 1) return;
-    gp->mode = IRIS_EPI_GATE_BF16;
-    gp->out = tf->plan.delta;
-    gp->ldo = tf->H;
+    t->size = tf->tp;
+    t->rank = tf->tp_rank;
+    t->chunk = P->chunk;
+    for (int p = 0; p < tf->tp; p++) {
+        t->recv[p] = (float *)iris_comm_sym_peer(P->recv, p);
+        t->flags[p] = (unsigned *)iris_comm_sym_peer(P->flags, p);
+    }
+    t->wait_x = wait_x;
+}
+
+/* an output projection: gated residual update, or its scattered partial */
+static void tp_resid(iris_cuda_flux_t *tf, IrisGemmParams *gp) {
+    if (tf->tp <= 1) return;
+    gp->mode = IRIS_EPI_TP_SCATTER;
+    tp_fill(tf, &gp->tp, 0);
 }
 
 static void enq_allreduce(iris_cuda_flux_t *tf, enq_t *E) {
-    if (tf->tp <= 1 || E->rc) return;
-    E->rc = iris_comm_allreduce_sum(tf->plan.delta, (size_t)tf->plan.S * tf->H, 1);
-    tf->plan.delta_pending = 1;
+    (void)E;
+    if (tf->tp <= 1) return;
+    tf->plan.part_i++;  /* the GEMM just queued signals partial sync part_i */
+    tf->plan.part_pending = 1;
 }
 
-/* adaLN of rows [row0, row0 + rows) of the hidden state, folding in a pending
- * tensor-parallel update of those rows first */
+/* a GEMM whose A operand is xmod: wait for every rank's rows */
+static void tp_reads_xmod(iris_cuda_flux_t *tf, IrisGemmParams *gp) {
+    if (tf->tp > 1) tp_fill(tf, &gp->tp, tf->plan.x_i);
+}
+
+/* adaLN of rows [row0, row0 + rows) into xmod (same rows); tensor-parallel:
+ * this rank's chunk of them, with the pending partial update folded in */
 static cudaError_t adaln_rows(iris_cuda_flux_t *tf, int row0, int rows, const float *sh0, const float *sc0,
                               const float *sh1, const float *sc1, int split) {
     flux_plan_t *P = &tf->plan;
     const int H = tf->H;
-    const void *d = P->delta_pending ? (const void *)(P->delta + (size_t)row0 * H) : NULL;
-    P->delta_pending = 0;
-    return iris_launch_adaln_delta(P->hidden + (size_t)row0 * H, H, d, H, P->xmod, H, rows, H, sh0, sc0, sh1,
-                                   sc1, split, 1e-6f, g_rt.stream);
+    if (tf->tp <= 1)
+        return iris_launch_adaln(P->hidden + (size_t)row0 * H, H, P->xmod + (size_t)row0 * H, H, rows, H, sh0,
+                                 sc0, sh1, sc1, split - row0, 1e-6f, g_rt.stream);
+    IrisAdalnTpArgs a;
+    memset(&a, 0, sizeof(a));
+    a.x = P->hidden;
+    a.row0 = tf->tp_rank * P->chunk;
+    a.rows = P->S - a.row0 < P->chunk ? P->S - a.row0 : P->chunk;
+    if (a.rows < 0) a.rows = 0;
+    a.row_lo = row0;
+    a.chunk = P->chunk;
+    a.H = H;
+    a.recv = P->recv;
+    a.has_part = P->part_pending;
+    a.part_index = P->part_i;
+    for (int p = 0; p < tf->tp; p++) a.xmod[p] = iris_comm_sym_peer(P->xmod, p);
+    a.shift0 = sh0; a.scale0 = sc0;
+    a.shift1 = sh1 ? sh1 : sh0; a.scale1 = sc1 ? sc1 : sc0;
+    a.split = split;
+    a.eps = 1e-6f;
+    tp_fill(tf, &a.tp, 0);
+    a.status = g_rt.d_status;
+    P->part_pending = 0;
+    P->x_i++;  /* this launch signals xmod sync x_i */
+    return iris_launch_adaln_tp(&a, g_rt.stream);
 }
 
 /* timestep embedding and every modulation vector of the step */
@@ -689,6 +759,7 @@ static void enq_double(iris_cuda_flux_t *tf, int i, enq_t *E) {
     IrisGemmParams gp;
     enq_x(E, adaln_rows(tf, 0, S, mt, mt + H, mi, mi + H, St), "adaln1", 0.0, 6.0 * S * (double)H);
     gp_init(&gp, P, &P->tm_xmod, 3 * Hl, H, IRIS_EPI_QKV);
+    tp_reads_xmod(tf, &gp);
     gp.bn = bn_for(3 * Hl);
     gp_group(&gp, 0, &b->tm_qkv[0], 0, St);
     gp_group(&gp, 1, &b->tm_qkv[1], St, Si);
@@ -711,6 +782,7 @@ static void enq_double(iris_cuda_flux_t *tf, int i, enq_t *E) {
     enq_x(E, adaln_rows(tf, 0, S, mt + 3 * H, mt + 4 * H, mi + 3 * H, mi + 4 * H, St), "adaln2", 0.0,
           6.0 * S * (double)H);
     gp_init(&gp, P, &P->tm_xmod, 2 * Fl, H, IRIS_EPI_SWIGLU);
+    tp_reads_xmod(tf, &gp);
     gp_group(&gp, 0, &b->tm_in[0], 0, St);
     gp_group(&gp, 1, &b->tm_in[1], St, Si);
     gp.mlp_out = P->mlp; gp.ld_mlp = Fl; gp.mlp_col0 = 0; gp.swiglu_base = 0;
@@ -735,6 +807,7 @@ static void enq_single(iris_cuda_flux_t *tf, int i, enq_t *E) {
     IrisGemmParams gp;
     enq_x(E, adaln_rows(tf, 0, S, ms, ms + H, NULL, NULL, S), "adaln_s", 0.0, 6.0 * S * (double)H);
     gp_init(&gp, P, &P->tm_xmod, 3 * Hl + 2 * Fl, H, IRIS_EPI_SINGLE);
+    tp_reads_xmod(tf, &gp);
     gp_group(&gp, 0, &b->tm_fused, 0, S);
     gp.qnorm[0] = b->qn; gp.knorm[0] = b->kn;
     gp.rope_cos = P->rope_cos; gp.rope_sin = P->rope_sin;
@@ -759,24 +832,43 @@ static void enq_final(iris_cuda_flux_t *tf, enq_t *E) {
     const int H = tf->H, C = tf->C, St = P->s_txt;
     const float *mf = tf->mods + (size_t)15 * H;
     IrisGemmParams gp;
-    enq(E, adaln_rows(tf, St, P->n_img, mf + H, mf, NULL, NULL, P->n_img), "adaln_final");
+    enq(E, adaln_rows(tf, St, P->n_img, mf + H, mf, NULL, NULL, P->S), "adaln_final");
     gp_init(&gp, P, &P->tm_xmod, C, H, IRIS_EPI_F32_NCHW);
+    tp_reads_xmod(tf, &gp);
     gp.bn = 128;
-    gp_group(&gp, 0, &tf->tm_proj, 0, P->n_img);
+    gp_group(&gp, 0, &tf->tm_proj, St, P->n_img);  /* xmod holds the image rows at their own index */
     gp.out = P->out;
     gp.nchw_rows = P->n_img;
     enq_gemm(E, &gp, "proj_out");
 }
 
+/* start / end of a call that may exchange over peer memory */
+static void tp_begin(iris_cuda_flux_t *tf, enq_t *E) {
+    tf->plan.part_i = tf->plan.x_i = 0;
+    tf->plan.part_pending = 0;
+    if (tf->tp <= 1) return;
+    /* no rank writes into a peer's buffers before every rank finished its
+       previous call (which may still be reading them) */
+    IrisTpParams t;
+    tp_fill(tf, &t, 0);
+    enq(E, iris_launch_tp_barrier(&t, g_rt.d_status, g_rt.stream), "tp_barrier");
+}
+
+static void tp_end(iris_cuda_flux_t *tf, enq_t *E) {
+    if (tf->tp <= 1) return;
+    enq(E, iris_launch_tp_advance(tf->plan.flags, tf->plan.part_i, tf->plan.x_i, g_rt.stream), "tp_advance");
+}
+
 /* Queue one forward over the current plan: reads P->lat_in, P->txt_f32 and
  * tf->t_dev, writes P->out. */
 static int enqueue_forward(iris_cuda_flux_t *tf, enq_t *E) {
-    tf->plan.delta_pending = 0;
+    tp_begin(tf, E);
     enq_mods(tf, E);
     enq_embed(tf, E);
     for (int i = 0; i < tf->cfg.n_double; i++) enq_double(tf, i, E);
     for (int i = 0; i < tf->cfg.n_single; i++) enq_single(tf, i, E);
     enq_final(tf, E);
+    tp_end(tf, E);
     return E->rc;
 }
 
@@ -799,15 +891,32 @@ int iris_cuda_flux_run_block(iris_cuda_flux_t *tf, int kind, int idx, float *hid
     if (!rc) rc = iris_cuda_check(cudaMemcpyAsync(tf->t_dev, &t, 4, cudaMemcpyHostToDevice, g_rt.stream), "t");
     if (rc) return rc;
     enq_t E = {0};
-    P->delta_pending = 0;
+    tp_begin(tf, &E);
     enq_mods(tf, &E);
     if (kind == 0) enq_double(tf, idx, &E);
     else enq_single(tf, idx, &E);
-    if (P->delta_pending) {  /* the block's last update, normally folded into the next adaLN */
-        P->delta_pending = 0;
-        enq(&E, iris_launch_add_bf16_rows(P->hidden, tf->H, P->delta, tf->H, P->S, tf->H, g_rt.stream),
-            "tp_residual");
+    if (tf->tp > 1 && P->part_pending && !E.rc) {
+        /* the block's last update (normally folded into the next adaLN): fold it
+           into this rank's rows, then gather every rank's rows */
+        IrisAdalnTpArgs a;
+        memset(&a, 0, sizeof(a));
+        a.x = P->hidden;
+        a.row0 = tf->tp_rank * P->chunk;
+        a.rows = P->S - a.row0 < P->chunk ? P->S - a.row0 : P->chunk;
+        if (a.rows < 0) a.rows = 0;
+        a.chunk = P->chunk;
+        a.H = tf->H;
+        a.recv = P->recv;
+        a.has_part = 1;
+        a.part_index = P->part_i;
+        tp_fill(tf, &a.tp, 0);
+        a.status = g_rt.d_status;
+        enq(&E, iris_launch_adaln_tp(&a, g_rt.stream), "tp_fold");
+        if (!E.rc)
+            E.rc = iris_comm_allgather_bytes(P->hidden + (size_t)a.row0 * tf->H, P->hidden,
+                                             (size_t)P->chunk * tf->H * 4);
     }
+    tp_end(tf, &E);
     iris_count_launch(E.kernels);
     if (E.rc) return E.rc;
     rc = iris_cuda_check(cudaMemcpyAsync(hidden, P->hidden, bytes, cudaMemcpyDeviceToHost, g_rt.stream), "d2h");
@@ -847,9 +956,7 @@ int iris_cuda_flux_profile(iris_cuda_flux_t *tf, float timestep, iris_cuda_kerne
     return rc ? rc : n;
 }
 
-/* Run the forward of the current plan (captured once into a CUDA graph; a
- * tensor-parallel shard launches eagerly, its all-reduces between the blocks'
- * kernels). */
+/* Run the forward of the current plan (captured once into a CUDA graph). */
 static int run_forward(iris_cuda_flux_t *tf) {
     flux_plan_t *P = &tf->plan;
     if (iris_fault("launch"))
@@ -861,7 +968,7 @@ static int run_forward(iris_cuda_flux_t *tf) {
         static int no_graph = -1;
         if (no_graph < 0) no_graph = getenv("IRIS_CUDA_NO_GRAPH") ? 1 : 0;
         enq_t E = {0};
-        if (no_graph || tf->tp > 1) {
+        if (no_graph) {
             int rc = enqueue_forward(tf, &E);
             iris_count_launch(E.kernels);
             return rc;

@@ -158,6 +158,32 @@ __device__ __forceinline__ void epi_swiglu_tile(const IrisGemmParams& p, uint32_
   }
 }
 
+// ---------------------------------------------------------------- tensor parallelism
+// IRIS_EPI_TP_SCATTER: gate * acc of a 32 x 32 block straight into the
+// owning ranks' receive buffers (peer memory), transposed through the warp's
+// staging tile so that each store covers 4 rows x 128 contiguous bytes.
+__device__ __forceinline__ void epi_scatter_block(const IrisGemmParams& p, int g, float* stage, const float* v,
+                                                  int lane, int row_first, int rows_valid, int c) {
+  float4* st = reinterpret_cast<float4*>(stage + lane * EPI_LD);
+#pragma unroll
+  for (int q = 0; q < 8; q++) st[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+  __syncwarp();
+  const int rr = lane >> 3, c4 = (lane & 7) * 4;
+  const float4 gg = __ldg(reinterpret_cast<const float4*>(p.gate[g] + c + c4));
+  const int chunk = p.tp.chunk;
+#pragma unroll
+  for (int it = 0; it < 8; it++) {
+    const int r = it * 4 + rr;
+    if (r < rows_valid) {
+      const int row = row_first + r, o = row / chunk;
+      const float4 a = *reinterpret_cast<const float4*>(stage + r * EPI_LD + c4);
+      float* d = p.tp.recv[o] + ((size_t)p.tp.rank * chunk + (row - o * chunk)) * p.N + c + c4;
+      *reinterpret_cast<float4*>(d) = make_float4(gg.x * a.x, gg.y * a.y, gg.z * a.z, gg.w * a.w);
+    }
+  }
+  __syncwarp();
+}
+
 // f32 outputs (plain store or gated residual update) of a 32-row x 32-column
 // block: lane i holds row row_first + i in v.  The block is transposed through
 // this warp's shared staging tile so that every global access covers 4 rows x
@@ -203,6 +229,10 @@ __device__ __forceinline__ void epi_plain_chunk(const IrisGemmParams& p, uint32_
     float v[32];
     iris::tmem_ld32(taddr + 32 * j, v);
     int c = col0 + 32 * j;
+    if (p.mode == IRIS_EPI_TP_SCATTER) {
+      epi_scatter_block(p, g, stage, v, lane, row - lane, rows_valid, c);
+      continue;
+    }
     if (p.splitk > 1) {
       // raw partial of this K range -> workspace slice `split` (reduced later)
       const size_t span = (size_t)(p.ngroups > 1 ? p.row0[1] + p.rows[1] : p.row0[0] + p.rows[0]);
@@ -341,6 +371,11 @@ gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
     uint32_t phase = 0;
     long issued = 0;
     bool ok = true;
+    if (p.tp.size > 1 && p.tp.wait_x) {  // A rows written by peer GPUs: wait for all of them
+      ok = iris::tp_wait(p.tp, IRIS_TP_X, IRIS_TP_BASE_X, p.tp.wait_x, p.status);
+      if (!ok) *abort_flag = 1;
+      iris::fence_proxy_async_global();
+    }
     for (int u = blockIdx.x; u < total && ok; u += gridDim.x) {
       int g, ml, n0;
       tile_coords(p, u / nsplit, mt0, mtot, g, ml, n0);
@@ -445,6 +480,10 @@ gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
       iris::tc_fence_before();
       iris::mbar_arrive(&bars->tempty[buf]);
     }
+    if (p.mode == IRIS_EPI_TP_SCATTER) {
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 epilogue warps' stores are issued
+      if (warp == 2 && lane == 0) iris::tp_signal(p.tp, IRIS_TP_DONE_GEMM, IRIS_TP_PART, gridDim.x);
+    }
   }
 
   __syncthreads();
@@ -526,6 +565,11 @@ gemm_tc2_kernel(const __grid_constant__ IrisGemmParams p) {
     int stage = 0;
     uint32_t phase = 0;
     bool ok = true, issued_any = false;
+    if (p.tp.size > 1 && p.tp.wait_x) {  // A rows written by peer GPUs: wait for all of them
+      ok = iris::tp_wait(p.tp, IRIS_TP_X, IRIS_TP_BASE_X, p.tp.wait_x, p.status);
+      if (!ok) *abort_flag = 1;
+      iris::fence_proxy_async_global();
+    }
     for (int t = pair; t < total && ok; t += npairs) {
       int g, ml, n0;
       tile_coords(p, t, mt0, mtot, g, ml, n0);
@@ -624,6 +668,10 @@ gemm_tc2_kernel(const __grid_constant__ IrisGemmParams p) {
       iris::tc_fence_before();
       __syncwarp();
       if (lane == 0) iris::mbar_arrive_cluster(buf ? tempty_c1 : tempty_c0);
+    }
+    if (p.mode == IRIS_EPI_TP_SCATTER) {
+      asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 epilogue warps' stores are issued
+      if (warp == 2 && lane == 0) iris::tp_signal(p.tp, IRIS_TP_DONE_GEMM, IRIS_TP_PART, gridDim.x);
     }
   }
 

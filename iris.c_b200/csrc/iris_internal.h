@@ -54,6 +54,14 @@ int iris_comm_allgather_f32(const float *send, float *recv, size_t n);
 int iris_comm_sync_stream(void);
 /* wait for the library stream (bounded when a communicator exists) */
 int iris_stream_drain(void);
+/* symmetric device memory: an arena per rank mapped into every peer (CUDA IPC);
+ * init is collective and (re)starts the bump allocation, alloc must follow the
+ * same order on every rank; sym_peer maps a local object to peer's copy */
+#define IRIS_COMM_MAX_PEERS 8
+int iris_comm_sym_init(size_t bytes);
+void *iris_comm_sym_alloc(size_t bytes);
+void *iris_comm_sym_peer(const void *local_ptr, int peer);
+int iris_comm_allgather_bytes(const void *send, void *recv, size_t bytes);
 
 /* ---------------- safetensors (own reader) ---------------- */
 typedef enum { ST_F32 = 0, ST_F16 = 1, ST_BF16 = 2, ST_OTHER = 3 } st_dtype_t;

@@ -32,8 +32,41 @@ enum {
                                  mlp_out[row, mlp_col0 + f] = SiLU(gate) * up (bf16)       */
     IRIS_EPI_GATE_BF16 = 7,   /* out bf16 [row, ldo] = gate[g][col] * acc (tensor-parallel
                                  partial of a gated residual update)                      */
+    IRIS_EPI_TP_SCATTER = 8,  /* f32 gate[g][col] * acc -> the owning rank's receive slot
+                                 tp.recv[row / chunk][tp.rank] over NVLink, then a
+                                 partial-arrival signal to every rank                     */
     IRIS_EPI_SINGLE = 6,      /* cols < 3H as IRIS_EPI_QKV, cols >= 3H as IRIS_EPI_SWIGLU   */
 };
+
+/* Tensor-parallel exchange over NVLink peer memory (size > 1).  Rows of the
+ * sequence are owned in chunks of `chunk` rows by rank row / chunk.  Each
+ * rank's flag block (uint32 words, in symmetric memory):
+ *   [0, 8)   partial-update arrivals, by sender rank
+ *   [8, 16)  adaLN-output (xmod) arrivals, by sender rank
+ *   16, 17   CTA completion counters of the signalling GEMM / adaLN launch
+ *   18, 19   sync bases: partial / xmod syncs completed before this call
+ *   [20, 28) call-start barrier arrivals by sender, 28 its base (a call's
+ *            first writes into peer memory wait until every rank has
+ *            finished its previous call)
+ * A signalling launch adds 1 to slot [sender] of every rank's block once all
+ * its CTAs' stores are out (system-scope release); a waiting launch polls
+ * its own block until every sender's slot reaches base + index.        */
+#define IRIS_TP_MAX 8
+#define IRIS_TP_PART 0
+#define IRIS_TP_X 8
+#define IRIS_TP_DONE_GEMM 16
+#define IRIS_TP_DONE_ADALN 17
+#define IRIS_TP_BASE_PART 18
+#define IRIS_TP_BASE_X 19
+#define IRIS_TP_BAR 20        /* [20, 28): call-start barrier arrivals, by sender */
+#define IRIS_TP_BASE_BAR 28
+typedef struct {
+    int size, rank;           /* size > 1 enables the peer-memory paths          */
+    int chunk;                /* rows owned per rank                              */
+    float *recv[IRIS_TP_MAX]; /* rank p's partial receive buffer [size][chunk][N] (peer-mapped) */
+    unsigned *flags[IRIS_TP_MAX];  /* rank p's flag block (peer-mapped; [rank] = own) */
+    unsigned wait_x;          /* GEMM: xmod sync index to wait for before loading A (0 = none) */
+} IrisTpParams;
 
 typedef struct {
     CUtensorMap tmap_a;       /* A: box {64, 128} rows, 128B swizzle                  */
@@ -69,6 +102,7 @@ typedef struct {
     float *ws;
     size_t ws_bytes;
     int splitk;               /* set by iris_launch_gemm                              */
+    IrisTpParams tp;          /* IRIS_EPI_TP_SCATTER destination and xmod wait        */
 } IrisGemmParams;
 
 /* Encodes a 2-D bf16 tensor map over a row-major [rows, cols] matrix with
@@ -112,6 +146,31 @@ cudaError_t iris_launch_adaln_delta(float *x, int ldx, const void *delta, int ld
                                     int rows, int cols, const float *shift0, const float *scale0,
                                     const float *shift1, const float *scale1, int split, float eps,
                                     cudaStream_t stream);
+/* Tensor-parallel adaLN over this rank's rows (one warp per row).
+ * Rows [row0, row0 + rows) of x belong to this rank; rows below row_lo are
+ * skipped.  If has_part, first waits for the partial updates of partial sync
+ * `part_index` from every rank and adds them (rank order) from recv
+ * [size][chunk][H] into x.  If xmod[0] is not NULL, then applies adaLN (shift/
+ * scale per row group, split = first row of group 1) and stores the bf16 row
+ * into xmod[p] of every rank p (peer memory), then signals xmod arrival. */
+typedef struct {
+    float *x;
+    int row0, rows, row_lo, chunk, H;
+    const float *recv;
+    int has_part;
+    unsigned part_index;
+    void *xmod[IRIS_TP_MAX];
+    const float *shift0, *scale0, *shift1, *scale1;
+    int split;
+    float eps;
+    IrisTpParams tp;
+    int *status;
+} IrisAdalnTpArgs;
+cudaError_t iris_launch_adaln_tp(const IrisAdalnTpArgs *a, cudaStream_t stream);
+/* call-start barrier over all ranks (one thread; bounded wait) */
+cudaError_t iris_launch_tp_barrier(const IrisTpParams *tp, int *status, cudaStream_t stream);
+/* advance this rank's sync bases by the syncs one call queued */
+cudaError_t iris_launch_tp_advance(unsigned *flags, unsigned parts, unsigned xs, cudaStream_t stream);
 /* x[row, col] += delta[row, col] (f32 += bf16) */
 cudaError_t iris_launch_add_bf16_rows(float *x, int ldx, const void *delta, int ld_delta, int rows, int cols,
                                       cudaStream_t stream);

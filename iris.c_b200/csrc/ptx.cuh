@@ -13,6 +13,8 @@
 #include <cuda.h>
 #include <stdint.h>
 
+#include "iris_kernels.h"
+
 #ifndef IRIS_WAIT_NS
 #define IRIS_WAIT_NS 2000000000ull  // 2 s: every legitimate wait here is microseconds
 #endif
@@ -106,6 +108,61 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
       " [%0], [%1, {%3, %4}], [%2];" ::"r"(smem_u32(smem_dst)),
       "l"(reinterpret_cast<uint64_t>(m)), "r"(smem_u32(bar)), "r"(x), "r"(y)
       : "memory");
+}
+
+// ---------------------------------------------------------------- peer GPUs
+// Flags exchanged with other GPUs over NVLink: system-scope acquire loads,
+// release reductions and fences (IrisTpParams in iris_kernels.h).
+__device__ __forceinline__ unsigned ld_acquire_sys(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void red_release_sys_add(unsigned* p, unsigned v) {
+  asm volatile("red.release.sys.global.add.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ unsigned atom_acq_rel_gpu_add(unsigned* p, unsigned v) {
+  unsigned old;
+  asm volatile("atom.acq_rel.gpu.global.add.u32 %0, [%1], %2;" : "=r"(old) : "l"(p), "r"(v) : "memory");
+  return old;
+}
+__device__ __forceinline__ void fence_acq_rel_sys() { asm volatile("fence.acq_rel.sys;" ::: "memory"); }
+__device__ __forceinline__ void fence_proxy_async_global() {
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+}
+
+#define IRIS_DEV_ERR_TP_WAIT 0x301
+
+// Wait (bounded) until every sender's slot [slot0 + s] of this rank's flag
+// block reaches base + index, base read from word base_slot.
+__device__ __noinline__ inline bool tp_wait(const IrisTpParams& tp, int slot0, int base_slot, unsigned index, int* status) {
+  const unsigned* own = tp.flags[tp.rank];
+  const unsigned target = ld_acquire_sys(own + base_slot) + index;
+  const uint64_t t0 = globaltimer();
+  for (int s = 0; s < tp.size; s++) {
+    uint32_t n = 0;
+    while (ld_acquire_sys(own + slot0 + s) < target) {
+      if ((++n & 63u) == 0 && globaltimer() - t0 > IRIS_WAIT_NS) {
+        record_error(status, IRIS_DEV_ERR_TP_WAIT);
+        return false;
+      }
+    }
+  }
+  return true;
+}
+
+// One thread per CTA, after every store of its CTA is issued (and a CTA
+// barrier): the launch's last CTA adds 1 to slot [arrive_slot0 + rank] of
+// every rank's flag block, with release semantics at system scope that cover
+// all CTAs' stores (their fences and the completion counter chain them).
+__device__ __noinline__ inline void tp_signal(const IrisTpParams& tp, int done_slot, int arrive_slot0, unsigned ncta) {
+  unsigned* own = tp.flags[tp.rank];
+  fence_acq_rel_sys();
+  if (atom_acq_rel_gpu_add(own + done_slot, 1u) == ncta - 1) {
+    *reinterpret_cast<volatile unsigned*>(own + done_slot) = 0u;  // the next signalling launch starts after this one
+    fence_acq_rel_sys();
+    for (int p = 0; p < tp.size; p++) red_release_sys_add(tp.flags[p] + arrive_slot0 + tp.rank, 1u);
+  }
 }
 
 // ---------------------------------------------------------------- CTA pairs

@@ -12,6 +12,7 @@
 //                    op-level iris_gpu_* surface
 //   rmsnorm          zi_rms_norm             iris_transformer_zimage.c:657
 #include "iris_kernels.h"
+#include "ptx.cuh"
 
 #include <cuda_bf16.h>
 #include <math.h>
@@ -178,6 +179,90 @@ __global__ void add_bf16_rows_kernel(float* __restrict__ x, int ldx, const __nv_
   v.z += b.x;
   v.w += b.y;
   *xp = v;
+}
+
+// Tensor-parallel adaLN (see IrisAdalnTpArgs): one warp per owned row, the
+// partial updates of every rank summed in rank order (exact f32 sums, the
+// same order on every rank), the bf16 output row stored into every rank's
+// xmod buffer over NVLink, then one xmod-arrival signal per launch.
+template <int NV>
+__global__ void __launch_bounds__(32) adaln_tp_kernel(const __grid_constant__ IrisAdalnTpArgs a) {
+  const int i = blockIdx.x, lane = threadIdx.x;
+  const int row = a.row0 + i;
+  bool ok = true;
+  if (a.has_part) {
+    if (lane == 0) ok = iris::tp_wait(a.tp, IRIS_TP_PART, IRIS_TP_BASE_PART, a.part_index, a.status);
+    ok = __shfl_sync(0xffffffffu, ok, 0);
+  }
+  if (ok && i < a.rows && row >= a.row_lo) {
+    constexpr int cols = NV * 128;
+    float4* xr = reinterpret_cast<float4*>(a.x + (size_t)row * a.H);
+    float4 v[NV];
+#pragma unroll
+    for (int q = 0; q < NV; q++) v[q] = xr[lane + 32 * q];
+    if (a.has_part) {
+      for (int s = 0; s < a.tp.size; s++) {
+        const float4* pr = reinterpret_cast<const float4*>(a.recv + ((size_t)s * a.chunk + i) * a.H);
+#pragma unroll
+        for (int q = 0; q < NV; q++) {
+          const float4 d = pr[lane + 32 * q];
+          v[q].x += d.x;
+          v[q].y += d.y;
+          v[q].z += d.z;
+          v[q].w += d.w;
+        }
+      }
+#pragma unroll
+      for (int q = 0; q < NV; q++) xr[lane + 32 * q] = v[q];
+    }
+    if (a.xmod[0]) {
+      float sum = 0.f;
+#pragma unroll
+      for (int q = 0; q < NV; q++) sum += (v[q].x + v[q].y) + (v[q].z + v[q].w);
+#pragma unroll
+      for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+      const float mean = sum / (float)cols;
+      float sq = 0.f;
+#pragma unroll
+      for (int q = 0; q < NV; q++) {
+        float b0 = v[q].x - mean, b1 = v[q].y - mean, b2 = v[q].z - mean, b3 = v[q].w - mean;
+        sq += (b0 * b0 + b1 * b1) + (b2 * b2 + b3 * b3);
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) sq += __shfl_xor_sync(0xffffffffu, sq, o);
+      const float rstd = 1.0f / sqrtf(sq / (float)cols + a.eps);
+      const bool g1 = row >= a.split;
+      const float4* sh = reinterpret_cast<const float4*>(g1 ? a.shift1 : a.shift0);
+      const float4* sc = reinterpret_cast<const float4*>(g1 ? a.scale1 : a.scale0);
+#pragma unroll
+      for (int q = 0; q < NV; q++) {
+        const int c = lane + 32 * q;
+        const float4 s4 = __ldg(sh + c), k4 = __ldg(sc + c);
+        const uint2 o = make_uint2(pack2((1.0f + k4.x) * ((v[q].x - mean) * rstd) + s4.x,
+                                         (1.0f + k4.y) * ((v[q].y - mean) * rstd) + s4.y),
+                                   pack2((1.0f + k4.z) * ((v[q].z - mean) * rstd) + s4.z,
+                                         (1.0f + k4.w) * ((v[q].w - mean) * rstd) + s4.w));
+        for (int p = 0; p < a.tp.size; p++)
+          reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(a.xmod[p]) + (size_t)row * a.H)[c] = o;
+      }
+    }
+  }
+  if (a.xmod[0]) {
+    __syncwarp();
+    if (lane == 0) iris::tp_signal(a.tp, IRIS_TP_DONE_ADALN, IRIS_TP_X, gridDim.x);
+  }
+}
+
+__global__ void tp_barrier_kernel(const __grid_constant__ IrisTpParams tp, int* status) {
+  unsigned* own = tp.flags[tp.rank];
+  iris::fence_acq_rel_sys();
+  for (int p = 0; p < tp.size; p++) iris::red_release_sys_add(tp.flags[p] + IRIS_TP_BAR + tp.rank, 1u);
+  if (iris::tp_wait(tp, IRIS_TP_BAR, IRIS_TP_BASE_BAR, 1u, status)) own[IRIS_TP_BASE_BAR] += 1u;
+}
+
+__global__ void tp_advance_kernel(unsigned* flags, unsigned parts, unsigned xs) {
+  flags[IRIS_TP_BASE_PART] += parts;
+  flags[IRIS_TP_BASE_X] += xs;
 }
 
 // ------------------------------------------------------------------ GEMV
@@ -472,6 +557,33 @@ cudaError_t iris_launch_adaln(const float* x, int ldx, void* out, int ldout, int
                               const float* scale1, int split, float eps, cudaStream_t stream) {
   return iris_launch_adaln_delta(const_cast<float*>(x), ldx, nullptr, 0, out, ldout, rows, cols, shift0, scale0,
                                  shift1, scale1, split, eps, stream);
+}
+
+cudaError_t iris_launch_adaln_tp(const IrisAdalnTpArgs* a, cudaStream_t stream) {
+  if (a->chunk <= 0) return cudaSuccess;
+  if (a->H == 3072)
+    adaln_tp_kernel<24><<<a->chunk, 32, 0, stream>>>(*a);
+  else if (a->H == 4096)
+    adaln_tp_kernel<32><<<a->chunk, 32, 0, stream>>>(*a);
+  else if (a->H == 1024)
+    adaln_tp_kernel<8><<<a->chunk, 32, 0, stream>>>(*a);
+  else if (a->H == 2048)
+    adaln_tp_kernel<16><<<a->chunk, 32, 0, stream>>>(*a);
+  else if (a->H == 512)
+    adaln_tp_kernel<4><<<a->chunk, 32, 0, stream>>>(*a);
+  else
+    return cudaErrorInvalidValue;
+  return cudaGetLastError();
+}
+
+cudaError_t iris_launch_tp_barrier(const IrisTpParams* tp, int* status, cudaStream_t stream) {
+  tp_barrier_kernel<<<1, 1, 0, stream>>>(*tp, status);
+  return cudaGetLastError();
+}
+
+cudaError_t iris_launch_tp_advance(unsigned* flags, unsigned parts, unsigned xs, cudaStream_t stream) {
+  tp_advance_kernel<<<1, 1, 0, stream>>>(flags, parts, xs);
+  return cudaGetLastError();
 }
 
 cudaError_t iris_launch_add_bf16_rows(float* x, int ldx, const void* delta, int ld_delta, int rows, int cols,
