@@ -210,7 +210,11 @@ __device__ __forceinline__ void softmax_role(const AttnParams& p, uint32_t tmem,
     }
     iris::tc_fence_after();
     const int kbase = j * BKV;
-    const bool full = kbase + BKV <= p.sk && !p.kmask;
+    bool full = kbase + BKV <= p.sk;
+    if (full && p.kmask) {  // a masked sequence: tiles without padding keys still take the fast path
+      const uint32_t m4 = reinterpret_cast<const uint32_t*>(p.kmask + kbase)[lane];
+      full = __all_sync(0xffffffffu, m4 == 0x01010101u);
+    }
     uint32_t pw[BKV / 2];
     float rsum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     float alpha = 1.f;
