@@ -285,6 +285,53 @@ int iris_cuda_sample_euler_zimage_dev(iris_cuda_zimage_t *z, float *d_z, int h, 
                                       const float *d_cap, int cap_seq, const float *schedule,
                                       int num_steps);
 
+/* ------------------------------------------------------------------ 2d. autoencoder decoder
+ * The step after the denoising loop: latent -> RGB image on the GPU.  The
+ * decoder of AutoencoderKLFlux2 (32 latent channels, batch-norm latent
+ * statistics, post-quant conv) and of the Z-Image autoencoder (16 channels,
+ * scaling / shift), base 128 channels, multipliers 1/2/4/4, three resnets per
+ * level, one single-head attention in the mid block (iris_vae.c:1-30). */
+typedef struct iris_cuda_vae iris_cuda_vae_t;
+
+/* Same layout as the reference's iris_image (iris.h:73-78): width x height
+ * pixels, channel-interleaved uint8, row-major. */
+typedef struct {
+    int width;
+    int height;
+    int channels;
+    uint8_t *data;
+} iris_cuda_image_t;
+
+/* Replaces iris_vae_load_safetensors_ex (iris_vae.c:1227) on the decoder
+ * weights of vae_dir (diffusion_pytorch_model.safetensors).  z_channels <= 0
+ * reads latent_channels, scaling_factor and shift_factor from
+ * vae_dir/config.json as iris_parse_vae_config does (iris_vae_config.h);
+ * scaling == 0 selects the Flux batch-norm branch (eps 1e-4), else Z-Image's
+ * x / scaling + shift (eps 1e-6). */
+iris_cuda_vae_t *iris_cuda_vae_load(const char *vae_dir, int z_channels, float scaling, float shift);
+/* Replaces iris_vae_free (iris_vae.c:1024). */
+void iris_cuda_vae_free(iris_cuda_vae_t *vae);
+size_t iris_cuda_vae_weight_bytes(const iris_cuda_vae_t *vae);
+/* Replaces iris_vae_decode (iris_vae.c:835): latent [4 z, latent_h, latent_w]
+ * f32 (the transformer's patchified layout) -> image of 16 latent_w x
+ * 16 latent_h RGB pixels, rounded as the reference does.  batch must be 1
+ * (the reference's GPU decoder has the same limit, iris_vae.c:568).  Free
+ * with iris_cuda_image_free. */
+iris_cuda_image_t *iris_cuda_vae_decode(iris_cuda_vae_t *vae, const float *latent, int batch,
+                                        int latent_h, int latent_w);
+void iris_cuda_image_free(iris_cuda_image_t *img);
+/* The f32 RGB planes [3, 16 latent_h, 16 latent_w] in [-1, 1] before the
+ * uint8 conversion (host buffer). */
+int iris_cuda_vae_decode_f32(iris_cuda_vae_t *vae, const float *latent, int latent_h, int latent_w,
+                             float *out);
+/* Device-resident decode (enqueued on the library stream): d_latent device
+ * f32; d_rgb8 (uint8 [16 h, 16 w, 3]) and / or d_rgb_f32 ([3, 16 h, 16 w])
+ * device outputs, either may be NULL. */
+int iris_cuda_vae_decode_dev(iris_cuda_vae_t *vae, const float *d_latent, int latent_h, int latent_w,
+                             uint8_t *d_rgb8, float *d_rgb_f32);
+/* kernels in one captured decode (0 before the first decode) */
+uint64_t iris_cuda_vae_graph_kernels(const iris_cuda_vae_t *vae);
+
 /* ------------------------------------------------------------------ 3. iris_gpu_* surface
  * Device-resident tensors and ops with the names and signatures of
  * iris_metal.h.  Tensors are f32 or bf16 device buffers; "host" weight

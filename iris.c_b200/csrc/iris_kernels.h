@@ -224,6 +224,59 @@ cudaError_t iris_launch_interleave_gate_up(void *dst, const void *src, int F, in
 cudaError_t iris_launch_copy_rows_bf16(void *dst, int ldd, const void *src, int lds, int rows,
                                        int cols, cudaStream_t stream);
 
+/* ------------------------------------------------------------------ autoencoder decoder
+ * Stride-1 convolution with zero padding as an implicit GEMM on the tensor
+ * cores.  Activations are NHWC bf16 [H, W, C]; output pixel p, channel n:
+ *   out[p, n] = bias[n] (+ resid[p, n]) + sum over K of A(p, k) W[n, k]
+ * where K runs over segment 0 (taps0 = 9: the 3x3 taps (dy, dx) row-major,
+ * each over cin0 channels of tmap_a[0] at the shifted pixel; taps0 = 1: the
+ * pixel itself) and then segment 1 (cin1 channels of tmap_a[1] at the pixel:
+ * a fused 1x1 shortcut convolution).  W is bf16 [cout_pad, K] row-major,
+ * K = taps0 * cin0 + cin1.  Tiles: 128 pixels (a bw x bh block, bw * bh =
+ * 128) x bn output channels. */
+enum {
+    IRIS_CONV_F32 = 0,        /* out f32 NHWC [H * W, cout]                               */
+    IRIS_CONV_BF16 = 1,       /* out bf16 NHWC [H * W, cout]                              */
+    IRIS_CONV_F32_NCHW = 2,   /* out f32 channel planes [cout, H * W] (cout <= 32)        */
+};
+typedef struct {
+    CUtensorMap tmap_a[2];    /* NHWC bf16 activations: 3-D {C, W, H}, box {64, bw, bh}    */
+    CUtensorMap tmap_b;       /* weights: 2-D [cout_pad, K], box {64, min(bn, 128)}        */
+    int H, W;
+    int bw, bh;
+    int taps0;                /* 9 or 1 */
+    int cin0, cin1;           /* multiples of 64; cin1 = 0: no second segment */
+    int cout, cout_pad, bn;   /* bn in {16, 32, 64, 128, 256}; cout_pad % bn == 0 */
+    int mode;
+    void *out;
+    const float *bias;        /* [cout_pad] */
+    const float *resid;       /* optional f32 NHWC [H * W, cout]; may be `out` (F32 mode) */
+    int *status;
+} IrisConvParams;
+/* 3-D tensor map over an NHWC bf16 tensor [H, W, C] (C % 64 == 0), box {64, bw, bh} */
+int iris_make_tmap_nhwc_bf16(CUtensorMap *m, const void *ptr, int H, int W, int C, int bw, int bh);
+cudaError_t iris_conv_init(void);
+cudaError_t iris_launch_conv(const IrisConvParams *p, int num_sms, cudaStream_t stream);
+/* GroupNorm statistics (32 groups) of NHWC f32 [P, C]: stats[2g] = mean,
+ * stats[2g + 1] = 1 / sqrt(var + eps); part holds nblocks * 64 doubles,
+ * *counter must be 0 (the kernel leaves it 0) */
+cudaError_t iris_launch_gn_stats(const float *x, long P, int C, double *part, int nblocks, unsigned *counter,
+                                 float *stats, float eps, cudaStream_t stream);
+/* NHWC f32 [P, C] -> bf16: optional GroupNorm apply (stats, gamma, beta), SiLU
+ * and 2x nearest upsampling (W = input width; output [2H, 2W, C]) */
+cudaError_t iris_launch_nhwc_to_bf16(const float *x, long P, int C, int W, const float *stats, const float *gamma,
+                                     const float *beta, int silu, int up2, void *out, cudaStream_t stream);
+/* latent [4z, h, w] -> denormalised (bn_std/bn_mean, else x / scaling + shift),
+ * unpatchified, optional f32 post-quant 1x1 conv -> bf16 NHWC [2h, 2w, 64] */
+cudaError_t iris_launch_vae_latent_prep(const float *lat, int z, int h, int w, const float *bn_mean,
+                                        const float *bn_std, float scaling, float shift, const float *pq_w,
+                                        const float *pq_b, void *out, cudaStream_t stream);
+/* rows of f32 scores [rows, ld]: bf16 softmax(scale * s) over the first n columns, zeros after */
+cudaError_t iris_launch_vae_softmax(const float *s, int rows, int ld, int n, float scale, void *out,
+                                    cudaStream_t stream);
+/* f32 planes [3, P] -> uint8 [P, 3] (reference rounding) */
+cudaError_t iris_launch_vae_rgb8(const float *x, long P, uint8_t *out, cudaStream_t stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -1,0 +1,665 @@
+/*
+ * Autoencoder decoder on the GPU: latent -> RGB image, the step after the
+ * denoising loop.  Replaces iris_vae_decode (iris_vae.c:835-990) and its
+ * loader iris_vae_load_safetensors_ex (iris_vae.c:1227-1385).
+ *
+ * Layout: every activation is NHWC (pixel rows of channels).  The residual
+ * stream between resnet blocks stays f32; the inputs of the convolutions
+ * (GroupNorm + SiLU outputs, the upsampled tensor, the shortcut input) are
+ * bf16.  Convolutions run as implicit GEMMs (vae.cu) with their bias, the
+ * residual add and the 1x1 shortcut convolution fused; the mid-block
+ * attention (one head of 512 channels over the H*W latent pixels) runs as
+ * tensor-core GEMMs around an f32 row softmax.  One decode of a given size
+ * is captured once into a CUDA graph and replayed.
+ */
+#include "iris_internal.h"
+
+#include <math.h>
+#include <stdio.h>
+#include <stdlib.h>
+#include <string.h>
+
+#define VAE_BASE 128
+#define VAE_MID 512
+#define VAE_GN_BLOCKS 592            /* 4 x 148 SMs: GroupNorm statistics blocks (max) */
+#define VAE_MAX_MID_PIXELS 65536     /* 2x2-unpatchified latent pixels (4 MP images) */
+
+static const int k_mult[4] = {1, 2, 4, 4};  /* iris_vae.c:1236 */
+
+typedef struct {
+    uint16_t *w;     /* bf16 [cout_pad, k] */
+    float *b;        /* [cout_pad] (conv bias + shortcut bias) */
+    CUtensorMap tm;
+    int taps0, cin0, cin1, cout, cout_pad, bn, k;
+} vconv_t;
+
+typedef struct {
+    float *g, *b;
+} vgn_t;
+
+typedef struct {
+    int cin, cout;
+    vgn_t n1, n2;
+    vconv_t c1, c2;  /* c2 carries the 1x1 shortcut as its second K segment */
+} vres_t;
+
+typedef struct {
+    int valid, lh, lw;
+    int H[4], W[4];  /* level l: H[3] = 2 lh (after unpatchify), H[l - 1] = 2 H[l] */
+    int P3p;         /* mid-level pixels rounded up to 128 (attention GEMM extents) */
+    float *lat;
+    uint16_t *xin;
+    float *X, *T;
+    uint16_t *Hb, *Xb;
+    uint16_t *hA, *qk, *vT, *Pm, *O;
+    float *S;
+    double *part;
+    unsigned *counter;
+    float *stats;
+    float *rgb;
+    uint8_t *rgb8;
+    cudaGraph_t graph;
+    cudaGraphExec_t gexec;
+    int graph_ok;
+    uint64_t graph_kernels;
+} vplan_t;
+
+struct iris_cuda_vae {
+    int z, lat_ch;
+    float eps, scaling, shift;
+    float *bn_mean, *bn_std, *pq_w, *pq_b;
+    vconv_t conv_in, upc[3], conv_out;
+    vres_t mid[2], up[12];
+    vgn_t attn_gn, out_gn;
+    uint16_t *w_qk, *w_v, *w_o;
+    float *b_qk, *b_v, *b_o, *ones;
+    vplan_t plan;
+    size_t weight_bytes;
+    void *allocs[256];
+    int nallocs;
+};
+
+/* ------------------------------------------------------------------ loading */
+static void *vae_alloc(iris_cuda_vae_t *v, size_t bytes) {
+    if (v->nallocs >= (int)(sizeof(v->allocs) / sizeof(v->allocs[0]))) return NULL;
+    void *p = iris_dmalloc(bytes);
+    if (p) v->allocs[v->nallocs++] = p;
+    return p;
+}
+
+static void *vae_upload(iris_cuda_vae_t *v, const void *host, size_t bytes) {
+    void *d = vae_alloc(v, bytes);
+    if (!d) return NULL;
+    if (cudaMemcpy(d, host, bytes, cudaMemcpyHostToDevice) != cudaSuccess) return NULL;
+    v->weight_bytes += bytes;
+    return d;
+}
+
+/* f32 host copy of tensor `name` with `numel` elements (NULL if absent or mis-sized) */
+static float *read_host(const st_model_t *st, const char *name, size_t numel) {
+    const st_tensor_t *t = st_find(st, name);
+    if (!t) return NULL;
+    float *h = (float *)malloc(numel * sizeof(float));
+    if (!h) return NULL;
+    if (st_read_f32(st, t, h, numel)) { free(h); return NULL; }
+    return h;
+}
+
+static int missing(const char *name) { return iris_fail(IRIS_CUDA_ERR_IO, "VAE tensor %s missing or mis-sized", name); }
+
+static int load_vec(iris_cuda_vae_t *v, const st_model_t *st, const char *name, int n, float **dst) {
+    float *h = read_host(st, name, (size_t)n);
+    if (!h) return missing(name);
+    *dst = (float *)vae_upload(v, h, (size_t)n * 4);
+    free(h);
+    return *dst ? 0 : iris_fail(IRIS_CUDA_ERR_OOM, "VAE upload");
+}
+
+static int load_gn(iris_cuda_vae_t *v, const st_model_t *st, const char *prefix, int c, vgn_t *gn) {
+    char n[300];
+    snprintf(n, sizeof(n), "%s.weight", prefix);
+    int rc = load_vec(v, st, n, c, &gn->g);
+    snprintf(n, sizeof(n), "%s.bias", prefix);
+    return rc ? rc : load_vec(v, st, n, c, &gn->b);
+}
+
+/* Convolution `prefix` (OIHW [cout, cin, k, k], k = 3 if taps == 9 else 1)
+ * repacked as the GEMM operand [cout_pad, taps * cin_pad (+ skip_cin)]
+ * with K ordered (tap, channel); an optional 1x1 shortcut `skip` ([cout,
+ * skip_cin]) appended as extra K columns, its bias added to the conv bias. */
+static int load_conv(iris_cuda_vae_t *v, const st_model_t *st, const char *prefix, int cin, int cin_pad, int cout,
+                     int taps, const char *skip, int skip_cin, int bn, vconv_t *cv) {
+    char n[300];
+    const int cout_pad = (cout + bn - 1) / bn * bn;
+    const int k = taps * cin_pad + (skip ? skip_cin : 0);
+    snprintf(n, sizeof(n), "%s.weight", prefix);
+    float *w = read_host(st, n, (size_t)cout * cin * taps);
+    if (!w) return missing(n);
+    snprintf(n, sizeof(n), "%s.bias", prefix);
+    float *b = read_host(st, n, (size_t)cout);
+    if (!b) { free(w); return missing(n); }
+    float *ws = NULL, *bs = NULL;
+    if (skip) {
+        snprintf(n, sizeof(n), "%s.weight", skip);
+        ws = read_host(st, n, (size_t)cout * skip_cin);
+        snprintf(n, sizeof(n), "%s.bias", skip);
+        bs = read_host(st, n, (size_t)cout);
+        if (!ws || !bs) { free(w); free(b); free(ws); free(bs); return missing(n); }
+    }
+    uint16_t *m = (uint16_t *)calloc((size_t)cout_pad * k, sizeof(uint16_t));
+    float *bias = (float *)calloc((size_t)cout_pad, sizeof(float));
+    int rc = 0;
+    if (!m || !bias) rc = iris_fail(IRIS_CUDA_ERR_OOM, "VAE weight staging");
+    for (int o = 0; !rc && o < cout; o++) {
+        for (int c = 0; c < cin; c++)
+            for (int t = 0; t < taps; t++)  /* OIHW: weight[o][c][ky][kx], t = ky * 3 + kx */
+                m[(size_t)o * k + (size_t)t * cin_pad + c] = f32_to_bf16_bits(w[((size_t)o * cin + c) * taps + t]);
+        if (skip)
+            for (int c = 0; c < skip_cin; c++)
+                m[(size_t)o * k + (size_t)taps * cin_pad + c] = f32_to_bf16_bits(ws[(size_t)o * skip_cin + c]);
+        bias[o] = b[o] + (skip ? bs[o] : 0.0f);
+    }
+    if (!rc) {
+        cv->w = (uint16_t *)vae_upload(v, m, (size_t)cout_pad * k * 2);
+        cv->b = (float *)vae_upload(v, bias, (size_t)cout_pad * 4);
+        if (!cv->w || !cv->b) rc = iris_fail(IRIS_CUDA_ERR_OOM, "VAE upload");
+    }
+    if (!rc && iris_make_tmap_bf16(&cv->tm, cv->w, (uint64_t)cout_pad, (uint64_t)k, (uint64_t)k,
+                                   (uint32_t)(bn < 128 ? bn : 128)))
+        rc = iris_fail(IRIS_CUDA_ERR_CUDA, "VAE weight tensor map");
+    cv->taps0 = taps;
+    cv->cin0 = cin_pad;
+    cv->cin1 = skip ? skip_cin : 0;
+    cv->cout = cout;
+    cv->cout_pad = cout_pad;
+    cv->bn = bn;
+    cv->k = k;
+    free(w); free(b); free(ws); free(bs); free(m); free(bias);
+    return rc;
+}
+
+static int conv_bn(int cout) { return cout >= 256 ? 256 : cout >= 128 ? 128 : 16; }
+
+static int load_res(iris_cuda_vae_t *v, const st_model_t *st, const char *prefix, int cin, int cout, vres_t *r) {
+    char n[300], n2[300];
+    r->cin = cin;
+    r->cout = cout;
+    int rc;
+    snprintf(n, sizeof(n), "%s.norm1", prefix);
+    if ((rc = load_gn(v, st, n, cin, &r->n1))) return rc;
+    snprintf(n, sizeof(n), "%s.norm2", prefix);
+    if ((rc = load_gn(v, st, n, cout, &r->n2))) return rc;
+    snprintf(n, sizeof(n), "%s.conv1", prefix);
+    if ((rc = load_conv(v, st, n, cin, cin, cout, 9, NULL, 0, conv_bn(cout), &r->c1))) return rc;
+    snprintf(n, sizeof(n), "%s.conv2", prefix);
+    snprintf(n2, sizeof(n2), "%s.conv_shortcut", prefix);
+    return load_conv(v, st, n, cout, cout, cout, 9, cin != cout ? n2 : NULL, cin, conv_bn(cout), &r->c2);
+}
+
+/* [c, c] (or [c, c, 1, 1]) projections of the mid-block attention */
+static int load_attn(iris_cuda_vae_t *v, const st_model_t *st, const char *prefix) {
+    const int c = VAE_MID;
+    char n[300];
+    const char *names[4] = {"to_q", "to_k", "to_v", "to_out.0"};
+    float *w[4] = {0}, *b[4] = {0};
+    int rc = 0;
+    for (int i = 0; i < 4 && !rc; i++) {
+        snprintf(n, sizeof(n), "%s.%s.weight", prefix, names[i]);
+        if (!(w[i] = read_host(st, n, (size_t)c * c))) rc = missing(n);
+        snprintf(n, sizeof(n), "%s.%s.bias", prefix, names[i]);
+        if (!rc && !(b[i] = read_host(st, n, (size_t)c))) rc = missing(n);
+    }
+    uint16_t *m = rc ? NULL : (uint16_t *)malloc((size_t)2 * c * c * 2);
+    float *bb = rc ? NULL : (float *)malloc((size_t)2 * c * 4);
+    float *ones = rc ? NULL : (float *)malloc((size_t)c * 4);
+    if (!rc && (!m || !bb || !ones)) rc = iris_fail(IRIS_CUDA_ERR_OOM, "VAE staging");
+    if (!rc) {
+        for (size_t i = 0; i < (size_t)c * c; i++) {
+            m[i] = f32_to_bf16_bits(w[0][i]);
+            m[(size_t)c * c + i] = f32_to_bf16_bits(w[1][i]);
+        }
+        memcpy(bb, b[0], (size_t)c * 4);
+        memcpy(bb + c, b[1], (size_t)c * 4);
+        v->w_qk = (uint16_t *)vae_upload(v, m, (size_t)2 * c * c * 2);
+        v->b_qk = (float *)vae_upload(v, bb, (size_t)2 * c * 4);
+        for (size_t i = 0; i < (size_t)c * c; i++) m[i] = f32_to_bf16_bits(w[2][i]);
+        v->w_v = (uint16_t *)vae_upload(v, m, (size_t)c * c * 2);
+        v->b_v = (float *)vae_upload(v, b[2], (size_t)c * 4);
+        for (size_t i = 0; i < (size_t)c * c; i++) m[i] = f32_to_bf16_bits(w[3][i]);
+        v->w_o = (uint16_t *)vae_upload(v, m, (size_t)c * c * 2);
+        v->b_o = (float *)vae_upload(v, b[3], (size_t)c * 4);
+        for (int i = 0; i < c; i++) ones[i] = 1.0f;
+        v->ones = (float *)vae_upload(v, ones, (size_t)c * 4);
+        if (!v->w_qk || !v->b_qk || !v->w_v || !v->b_v || !v->w_o || !v->b_o || !v->ones)
+            rc = iris_fail(IRIS_CUDA_ERR_OOM, "VAE upload");
+    }
+    for (int i = 0; i < 4; i++) { free(w[i]); free(b[i]); }
+    free(m); free(bb); free(ones);
+    return rc;
+}
+
+static int vae_load_all(iris_cuda_vae_t *v, const st_model_t *st) {
+    int rc;
+    char n[300];
+    const int z = v->z;
+    if (!v->scaling) {  /* Flux: batch-norm statistics -> (mean, sqrt(var + eps)) */
+        float *mean = read_host(st, "bn.running_mean", (size_t)v->lat_ch);
+        float *var = read_host(st, "bn.running_var", (size_t)v->lat_ch);
+        float *sd = (float *)malloc((size_t)v->lat_ch * 4);
+        rc = 0;
+        if (!sd) rc = iris_fail(IRIS_CUDA_ERR_OOM, "VAE staging");
+        /* no statistics in the file: identity (iris_vae.c:1367-1374) */
+        for (int i = 0; !rc && i < v->lat_ch; i++) sd[i] = sqrtf((var ? var[i] : 1.0f) + v->eps);
+        if (!rc && !mean) {
+            mean = (float *)calloc((size_t)v->lat_ch, 4);
+            if (!mean) rc = iris_fail(IRIS_CUDA_ERR_OOM, "VAE staging");
+        }
+        if (!rc) {
+            v->bn_mean = (float *)vae_upload(v, mean, (size_t)v->lat_ch * 4);
+            v->bn_std = (float *)vae_upload(v, sd, (size_t)v->lat_ch * 4);
+            if (!v->bn_mean || !v->bn_std) rc = iris_fail(IRIS_CUDA_ERR_OOM, "VAE upload");
+        }
+        free(mean); free(var); free(sd);
+        if (rc) return rc;
+    }
+    if (st_find(st, "post_quant_conv.weight")) {
+        if ((rc = load_vec(v, st, "post_quant_conv.weight", z * z, &v->pq_w))) return rc;
+        if ((rc = load_vec(v, st, "post_quant_conv.bias", z, &v->pq_b))) return rc;
+    }
+    if ((rc = load_conv(v, st, "decoder.conv_in", z, 64, VAE_MID, 9, NULL, 0, 256, &v->conv_in))) return rc;
+    if ((rc = load_res(v, st, "decoder.mid_block.resnets.0", VAE_MID, VAE_MID, &v->mid[0]))) return rc;
+    if ((rc = load_gn(v, st, "decoder.mid_block.attentions.0.group_norm", VAE_MID, &v->attn_gn))) return rc;
+    if ((rc = load_attn(v, st, "decoder.mid_block.attentions.0"))) return rc;
+    if ((rc = load_res(v, st, "decoder.mid_block.resnets.1", VAE_MID, VAE_MID, &v->mid[1]))) return rc;
+    int bi = 0;
+    for (int level = 3; level >= 0; level--) {  /* iris_vae.c:1318-1329 */
+        const int ch = VAE_BASE * k_mult[level];
+        const int prev = level == 3 ? VAE_MID : VAE_BASE * k_mult[level + 1];
+        for (int r = 0; r < 3; r++) {
+            snprintf(n, sizeof(n), "decoder.up_blocks.%d.resnets.%d", 3 - level, r);
+            if ((rc = load_res(v, st, n, r == 0 ? prev : ch, ch, &v->up[bi++]))) return rc;
+        }
+    }
+    for (int i = 0; i < 3; i++) {
+        const int ch = VAE_BASE * k_mult[3 - i];
+        snprintf(n, sizeof(n), "decoder.up_blocks.%d.upsamplers.0.conv", i);
+        if ((rc = load_conv(v, st, n, ch, ch, ch, 9, NULL, 0, conv_bn(ch), &v->upc[i]))) return rc;
+    }
+    if ((rc = load_gn(v, st, "decoder.conv_norm_out", VAE_BASE, &v->out_gn))) return rc;
+    return load_conv(v, st, "decoder.conv_out", VAE_BASE, VAE_BASE, 3, 9, NULL, 0, 16, &v->conv_out);
+}
+
+static void plan_free(vplan_t *P) {
+    if (P->graph_ok) {
+        cudaGraphExecDestroy(P->gexec);
+        cudaGraphDestroy(P->graph);
+    }
+    void *bufs[] = {P->lat, P->xin, P->X, P->T, P->Hb, P->Xb, P->hA, P->qk, P->vT, P->Pm, P->O,
+                    P->S, P->part, P->counter, P->stats, P->rgb, P->rgb8};
+    for (size_t i = 0; i < sizeof(bufs) / sizeof(bufs[0]); i++) iris_dfree(bufs[i]);
+    memset(P, 0, sizeof(*P));
+}
+
+void iris_cuda_vae_free(iris_cuda_vae_t *v) {
+    if (!v) return;
+    if (g_rt.initialized) cudaStreamSynchronize(g_rt.stream);
+    plan_free(&v->plan);
+    for (int i = 0; i < v->nallocs; i++) iris_dfree(v->allocs[i]);
+    free(v);
+}
+
+iris_cuda_vae_t *iris_cuda_vae_load(const char *vae_dir, int z_channels, float scaling, float shift) {
+    if (!vae_dir) { iris_fail(IRIS_CUDA_ERR_ARG, "null VAE directory"); return NULL; }
+    if (iris_rt_ensure()) return NULL;
+    /* config.json overrides, as iris_parse_vae_config (iris_vae_config.h) does */
+    int z = z_channels > 0 ? z_channels : 32;
+    char path[4200];
+    snprintf(path, sizeof(path), "%s/config.json", vae_dir);
+    FILE *f = fopen(path, "rb");
+    if (f && z_channels <= 0) {
+        char buf[8192];
+        size_t got = fread(buf, 1, sizeof(buf) - 1, f);
+        buf[got] = 0;
+        double d;
+        if (!json_get_number(buf, "latent_channels", &d) && d > 0) z = (int)d;
+        if (!json_get_number(buf, "scaling_factor", &d)) scaling = (float)d;
+        if (!json_get_number(buf, "shift_factor", &d)) shift = (float)d;
+    }
+    if (f) fclose(f);
+    if (z < 1 || z > 32) { iris_fail(IRIS_CUDA_ERR_ARG, "latent channels %d (1..32 supported)", z); return NULL; }
+    st_model_t st;
+    if (st_open_dir(&st, vae_dir)) { iris_fail(IRIS_CUDA_ERR_IO, "cannot open VAE weights in %s", vae_dir); return NULL; }
+    iris_cuda_vae_t *v = (iris_cuda_vae_t *)calloc(1, sizeof(*v));
+    if (!v) { st_close(&st); iris_fail(IRIS_CUDA_ERR_OOM, "VAE struct"); return NULL; }
+    v->z = z;
+    v->lat_ch = 4 * z;
+    v->scaling = scaling;
+    v->shift = shift;
+    v->eps = scaling != 0.0f ? 1e-6f : 1e-4f;  /* iris_vae.c:1245 */
+    int rc = vae_load_all(v, &st);
+    st_close(&st);
+    if (rc) { iris_cuda_vae_free(v); return NULL; }
+    return v;
+}
+
+size_t iris_cuda_vae_weight_bytes(const iris_cuda_vae_t *v) { return v ? v->weight_bytes : 0; }
+
+/* ------------------------------------------------------------------ plan */
+static int plan_ensure(iris_cuda_vae_t *v, int lh, int lw) {
+    vplan_t *P = &v->plan;
+    if (P->valid && P->lh == lh && P->lw == lw) return 0;
+    plan_free(P);
+    P->lh = lh;
+    P->lw = lw;
+    P->H[3] = 2 * lh;
+    P->W[3] = 2 * lw;
+    for (int l = 2; l >= 0; l--) {
+        P->H[l] = 2 * P->H[l + 1];
+        P->W[l] = 2 * P->W[l + 1];
+    }
+    const size_t p3 = (size_t)P->H[3] * P->W[3], p0 = (size_t)P->H[0] * P->W[0];
+    P->P3p = (int)((p3 + 127) / 128 * 128);
+    const size_t p3p = (size_t)P->P3p;
+    /* largest activation of each buffer over the levels (channels 512/512/256/128) */
+    const size_t x_elems = p0 * 256;           /* upsampled conv output entering level 0 */
+    const size_t t_elems = p0 * 128;           /* conv1 outputs: P_l * cout_l <= P0 * 128 */
+    const size_t hb_elems = p0 * 256;          /* GroupNorm outputs / upsampled input */
+    const size_t xb_elems = p0 * 256;          /* shortcut inputs (bf16 copy of a block input) */
+    int rc = 0;
+#define ALLOC(dst, bytes) \
+    do { if (!rc && !((dst) = iris_dmalloc(bytes))) rc = iris_fail(IRIS_CUDA_ERR_OOM, "VAE plan (%zu bytes)", (size_t)(bytes)); } while (0)
+    ALLOC(P->lat, (size_t)v->lat_ch * lh * lw * 4);
+    ALLOC(P->xin, p3 * 64 * 2);
+    ALLOC(P->X, x_elems * 4);
+    ALLOC(P->T, t_elems * 4);
+    ALLOC(P->Hb, hb_elems * 2);
+    ALLOC(P->Xb, xb_elems * 2);
+    ALLOC(P->hA, p3p * VAE_MID * 2);
+    ALLOC(P->qk, p3p * 2 * VAE_MID * 2);
+    ALLOC(P->vT, (size_t)VAE_MID * p3p * 2);
+    ALLOC(P->S, p3 * p3p * 4);
+    ALLOC(P->Pm, p3 * p3p * 2);
+    ALLOC(P->O, p3 * VAE_MID * 2);
+    ALLOC(P->part, (size_t)VAE_GN_BLOCKS * 64 * sizeof(double));
+    ALLOC(P->counter, 64);
+    ALLOC(P->stats, 64 * 4);
+    ALLOC(P->rgb, 3 * p0 * 4);
+    ALLOC(P->rgb8, 3 * p0);
+#undef ALLOC
+    /* the attention's padding rows (pixels P3 .. P3p - 1) feed GEMM operands: zero once */
+    if (!rc) rc = iris_cuda_check(cudaMemset(P->hA, 0, p3p * VAE_MID * 2), "memset");
+    if (!rc) rc = iris_cuda_check(cudaMemset(P->qk, 0, p3p * 2 * VAE_MID * 2), "memset");
+    if (!rc) rc = iris_cuda_check(cudaMemset(P->counter, 0, 64), "memset");
+    if (rc) { plan_free(P); return rc; }
+    P->valid = 1;
+    return 0;
+}
+
+/* ------------------------------------------------------------------ enqueue */
+typedef struct {
+    int rc;
+    uint64_t kernels;
+} venq_t;
+
+static void enq_check(venq_t *E, cudaError_t e, const char *what) {
+    if (E->rc) return;
+    if (e != cudaSuccess) E->rc = iris_cuda_check(e, what);
+    else E->kernels++;
+}
+
+static int pow2_at_least(int x) {
+    int p = 1;
+    while (p < x) p <<= 1;
+    return p;
+}
+
+/* conv over an H x W image: segment 0 from in0 (in0_c channels), optional
+ * shortcut segment from in1 (in1_c channels) */
+static void enq_conv(venq_t *E, const vconv_t *cv, const void *in0, int in0_c, const void *in1, int in1_c, int H,
+                     int W, int mode, void *out, const float *resid) {
+    if (E->rc) return;
+    IrisConvParams p;
+    memset(&p, 0, sizeof(p));
+    p.bw = pow2_at_least(W) < 128 ? pow2_at_least(W) : 128;
+    p.bh = 128 / p.bw;
+    if (iris_make_tmap_nhwc_bf16(&p.tmap_a[0], in0, H, W, in0_c, p.bw, p.bh) ||
+        (in1 && iris_make_tmap_nhwc_bf16(&p.tmap_a[1], in1, H, W, in1_c, p.bw, p.bh))) {
+        E->rc = iris_fail(IRIS_CUDA_ERR_CUDA, "VAE activation tensor map");
+        return;
+    }
+    p.tmap_b = cv->tm;
+    p.H = H;
+    p.W = W;
+    p.taps0 = cv->taps0;
+    p.cin0 = cv->cin0;
+    p.cin1 = in1 ? cv->cin1 : 0;
+    p.cout = cv->cout;
+    p.cout_pad = cv->cout_pad;
+    p.bn = cv->bn;
+    p.mode = mode;
+    p.out = out;
+    p.bias = cv->b;
+    p.resid = resid;
+    p.status = g_rt.d_status;
+    enq_check(E, iris_launch_conv(&p, g_rt.num_sms, g_rt.stream), "conv");
+}
+
+/* GroupNorm statistics of x [P, C] into P->stats, then the bf16 normalised (and SiLU) copy */
+static void enq_gn(venq_t *E, iris_cuda_vae_t *v, const float *x, long pix, int C, const vgn_t *gn, int silu,
+                   void *out) {
+    vplan_t *P = &v->plan;
+    const long ppi = 256 / (C / 4);
+    long nb = (pix + ppi - 1) / ppi;
+    if (nb > VAE_GN_BLOCKS) nb = VAE_GN_BLOCKS;
+    if (!E->rc)
+        enq_check(E, iris_launch_gn_stats(x, pix, C, P->part, (int)nb, P->counter, P->stats, v->eps, g_rt.stream),
+                  "gn stats");
+    if (!E->rc)
+        enq_check(E, iris_launch_nhwc_to_bf16(x, pix, C, 0, P->stats, gn->g, gn->b, silu, 0, out, g_rt.stream),
+                  "gn apply");
+}
+
+/* resnet block on P->X (H x W, r->cin channels) -> P->X (r->cout channels) */
+static void enq_res(venq_t *E, iris_cuda_vae_t *v, const vres_t *r, int H, int W) {
+    vplan_t *P = &v->plan;
+    const long pix = (long)H * W;
+    enq_gn(E, v, P->X, pix, r->cin, &r->n1, 1, P->Hb);
+    const int skip = r->cin != r->cout;
+    if (skip && !E->rc)
+        enq_check(E, iris_launch_nhwc_to_bf16(P->X, pix, r->cin, 0, NULL, NULL, NULL, 0, 0, P->Xb, g_rt.stream),
+                  "shortcut input");
+    enq_conv(E, &r->c1, P->Hb, r->cin, NULL, 0, H, W, IRIS_CONV_F32, P->T, NULL);
+    enq_gn(E, v, P->T, pix, r->cout, &r->n2, 1, P->Hb);
+    enq_conv(E, &r->c2, P->Hb, r->cout, skip ? P->Xb : NULL, r->cin, H, W, IRIS_CONV_F32, P->X,
+             skip ? NULL : P->X);
+}
+
+static void enq_gemm(venq_t *E, const void *a, int a_rows, int a_ld, const void *b, int b_rows, int b_ld, int K,
+                     int mode, void *out, int ldo, const float *bias, const float *gate) {
+    if (E->rc) return;
+    IrisGemmParams p;
+    memset(&p, 0, sizeof(p));
+    const int bn = b_rows % 256 == 0 ? 256 : 128;
+    if (iris_make_tmap_bf16(&p.tmap_a, a, (uint64_t)a_rows, (uint64_t)K, (uint64_t)a_ld, 128) ||
+        iris_make_tmap_bf16(&p.tmap_b[0], b, (uint64_t)b_rows, (uint64_t)K, (uint64_t)b_ld, (uint32_t)bn)) {
+        E->rc = iris_fail(IRIS_CUDA_ERR_CUDA, "VAE attention tensor map");
+        return;
+    }
+    p.ngroups = 1;
+    p.row0[0] = 0;
+    p.rows[0] = a_rows;
+    p.N = b_rows;
+    p.K = K;
+    p.bn = bn;
+    p.mode = mode;
+    p.out = out;
+    p.ldo = ldo;
+    p.bias = bias;
+    p.gate[0] = gate;
+    p.status = g_rt.d_status;
+    int n = 1;
+    cudaError_t e = iris_launch_gemm_ex(&p, g_rt.num_sms, g_rt.stream, &n);
+    enq_check(E, e, "attention gemm");
+    if (!E->rc && n > 1) E->kernels += (uint64_t)(n - 1);
+}
+
+/* mid-block attention on P->X [P3, 512], in place (attnblock_forward, iris_vae.c:260) */
+static void enq_attn(venq_t *E, iris_cuda_vae_t *v) {
+    vplan_t *P = &v->plan;
+    const int c = VAE_MID, p3 = P->H[3] * P->W[3], p3p = P->P3p;
+    enq_gn(E, v, P->X, p3, c, &v->attn_gn, 0, P->hA);
+    /* [q | k] = h Wqk^T + b  -> bf16 [P3, 1024] */
+    enq_gemm(E, P->hA, p3, c, v->w_qk, 2 * c, c, c, IRIS_EPI_BF16, P->qk, 2 * c, v->b_qk, NULL);
+    /* V^T = Wv h^T -> bf16 [512, P3p] (its bias is added after P V: the rows of P sum to 1) */
+    enq_gemm(E, v->w_v, c, c, P->hA, p3p, c, c, IRIS_EPI_BF16, P->vT, p3p, NULL, NULL);
+    /* S = q k^T -> f32 [P3, P3p] */
+    enq_gemm(E, P->qk, p3, 2 * c, P->qk + c, p3p, 2 * c, c, IRIS_EPI_F32, P->S, p3p, NULL, NULL);
+    if (!E->rc)
+        enq_check(E, iris_launch_vae_softmax(P->S, p3, p3p, p3, 1.0f / sqrtf((float)c), P->Pm, g_rt.stream),
+                  "softmax");
+    /* O = P V + bv -> bf16 [P3, 512] */
+    enq_gemm(E, P->Pm, p3, p3p, P->vT, c, p3p, p3p, IRIS_EPI_BF16, P->O, c, v->b_v, NULL);
+    /* x += O Wo^T + bo */
+    enq_gemm(E, P->O, p3, c, v->w_o, c, c, c, IRIS_EPI_RESID_GATE, P->X, c, v->b_o, v->ones);
+}
+
+static int enqueue_decode(iris_cuda_vae_t *v, venq_t *E) {
+    vplan_t *P = &v->plan;
+    if (!E->rc)
+        enq_check(E, iris_launch_vae_latent_prep(P->lat, v->z, P->lh, P->lw, v->bn_mean, v->bn_std, v->scaling,
+                                                 v->shift, v->pq_w, v->pq_b, P->xin, g_rt.stream),
+                  "latent prep");
+    enq_conv(E, &v->conv_in, P->xin, 64, NULL, 0, P->H[3], P->W[3], IRIS_CONV_F32, P->X, NULL);
+    enq_res(E, v, &v->mid[0], P->H[3], P->W[3]);
+    enq_attn(E, v);
+    enq_res(E, v, &v->mid[1], P->H[3], P->W[3]);
+    int bi = 0;
+    for (int level = 3; level >= 0; level--) {
+        const int ch = VAE_BASE * k_mult[level];
+        for (int r = 0; r < 3; r++) enq_res(E, v, &v->up[bi++], P->H[level], P->W[level]);
+        if (level > 0) {
+            const long pix = (long)P->H[level] * P->W[level];
+            if (!E->rc)
+                enq_check(E, iris_launch_nhwc_to_bf16(P->X, pix, ch, P->W[level], NULL, NULL, NULL, 0, 1, P->Hb,
+                                                      g_rt.stream),
+                          "upsample");
+            enq_conv(E, &v->upc[3 - level], P->Hb, ch, NULL, 0, P->H[level - 1], P->W[level - 1], IRIS_CONV_F32,
+                     P->X, NULL);
+        }
+    }
+    const long p0 = (long)P->H[0] * P->W[0];
+    enq_gn(E, v, P->X, p0, VAE_BASE, &v->out_gn, 1, P->Hb);
+    enq_conv(E, &v->conv_out, P->Hb, VAE_BASE, NULL, 0, P->H[0], P->W[0], IRIS_CONV_F32_NCHW, P->rgb, NULL);
+    if (!E->rc) enq_check(E, iris_launch_vae_rgb8(P->rgb, p0, P->rgb8, g_rt.stream), "rgb8");
+    return E->rc;
+}
+
+static int run_decode(iris_cuda_vae_t *v) {
+    vplan_t *P = &v->plan;
+    if (iris_fault("launch")) return iris_fail(IRIS_CUDA_ERR_INJECTED, "injected launch failure");
+    if (!P->graph_ok) {
+        static int no_graph = -1;
+        if (no_graph < 0) no_graph = getenv("IRIS_CUDA_NO_GRAPH") ? 1 : 0;
+        venq_t E = {0};
+        if (no_graph) {
+            int rc = enqueue_decode(v, &E);
+            iris_count_launch(E.kernels);
+            return rc;
+        }
+        cudaError_t e = cudaStreamBeginCapture(g_rt.stream, cudaStreamCaptureModeThreadLocal);
+        if (e != cudaSuccess) return iris_cuda_check(e, "begin capture");
+        int rc = enqueue_decode(v, &E);
+        cudaGraph_t g = NULL;
+        e = cudaStreamEndCapture(g_rt.stream, &g);
+        if (rc) { if (g) cudaGraphDestroy(g); return rc; }
+        if (e != cudaSuccess) return iris_cuda_check(e, "end capture");
+        e = cudaGraphInstantiate(&P->gexec, g, 0);
+        if (e != cudaSuccess) { cudaGraphDestroy(g); return iris_cuda_check(e, "graph instantiate"); }
+        P->graph = g;
+        P->graph_ok = 1;
+        P->graph_kernels = E.kernels;
+    }
+    iris_count_launch(P->graph_kernels);
+    return iris_cuda_check(cudaGraphLaunch(P->gexec, g_rt.stream), "graph launch");
+}
+
+static int check_args(iris_cuda_vae_t *v, int batch, int lh, int lw) {
+    if (!v) return iris_fail(IRIS_CUDA_ERR_ARG, "null VAE");
+    if (batch != 1) return iris_fail(IRIS_CUDA_ERR_ARG, "batch %d (1 supported)", batch);
+    if (lh < 1 || lw < 1 || (long)4 * lh * lw > VAE_MAX_MID_PIXELS)
+        return iris_fail(IRIS_CUDA_ERR_ARG, "latent %dx%d (up to %d latent pixels)", lh, lw, VAE_MAX_MID_PIXELS / 4);
+    return 0;
+}
+
+int iris_cuda_vae_decode_dev(iris_cuda_vae_t *v, const float *d_latent, int lh, int lw, uint8_t *d_rgb8,
+                             float *d_rgb_f32) {
+    int rc = check_args(v, 1, lh, lw);
+    if (rc) return rc;
+    if (!d_latent) return iris_fail(IRIS_CUDA_ERR_ARG, "null latent");
+    if ((rc = plan_ensure(v, lh, lw))) return rc;
+    vplan_t *P = &v->plan;
+    const size_t p0 = (size_t)P->H[0] * P->W[0];
+    rc = iris_cuda_check(cudaMemcpyAsync(P->lat, d_latent, (size_t)v->lat_ch * lh * lw * 4,
+                                         cudaMemcpyDeviceToDevice, g_rt.stream), "latent copy");
+    if (!rc) rc = run_decode(v);
+    if (!rc && d_rgb8)
+        rc = iris_cuda_check(cudaMemcpyAsync(d_rgb8, P->rgb8, 3 * p0, cudaMemcpyDeviceToDevice, g_rt.stream), "rgb8");
+    if (!rc && d_rgb_f32)
+        rc = iris_cuda_check(cudaMemcpyAsync(d_rgb_f32, P->rgb, 3 * p0 * 4, cudaMemcpyDeviceToDevice, g_rt.stream),
+                             "rgb");
+    return rc;
+}
+
+/* host latent -> device plan -> decode; out8 / outf (host) receive the results */
+static int decode_host(iris_cuda_vae_t *v, const float *latent, int lh, int lw, uint8_t *out8, float *outf) {
+    int rc = check_args(v, 1, lh, lw);
+    if (rc) return rc;
+    if (!latent) return iris_fail(IRIS_CUDA_ERR_ARG, "null latent");
+    if ((rc = plan_ensure(v, lh, lw))) return rc;
+    vplan_t *P = &v->plan;
+    const size_t p0 = (size_t)P->H[0] * P->W[0];
+    if (iris_fault("h2d")) return iris_fail(IRIS_CUDA_ERR_INJECTED, "injected h2d failure");
+    rc = iris_cuda_check(cudaMemcpyAsync(P->lat, latent, (size_t)v->lat_ch * lh * lw * 4, cudaMemcpyHostToDevice,
+                                         g_rt.stream), "h2d");
+    if (!rc) rc = run_decode(v);
+    if (!rc && out8) rc = iris_cuda_check(cudaMemcpyAsync(out8, P->rgb8, 3 * p0, cudaMemcpyDeviceToHost, g_rt.stream), "d2h");
+    if (!rc && outf)
+        rc = iris_cuda_check(cudaMemcpyAsync(outf, P->rgb, 3 * p0 * 4, cudaMemcpyDeviceToHost, g_rt.stream), "d2h");
+    if (!rc) rc = iris_cuda_synchronize();
+    return rc;
+}
+
+iris_cuda_image_t *iris_cuda_vae_decode(iris_cuda_vae_t *v, const float *latent, int batch, int lh, int lw) {
+    if (check_args(v, batch, lh, lw)) return NULL;
+    iris_cuda_image_t *img = (iris_cuda_image_t *)calloc(1, sizeof(*img));
+    uint8_t *data = (uint8_t *)malloc((size_t)3 * 256 * lh * lw);
+    if (!img || !data) {
+        free(img);
+        free(data);
+        iris_fail(IRIS_CUDA_ERR_OOM, "image");
+        return NULL;
+    }
+    if (decode_host(v, latent, lh, lw, data, NULL)) {
+        free(img);
+        free(data);
+        return NULL;
+    }
+    img->width = 16 * lw;
+    img->height = 16 * lh;
+    img->channels = 3;
+    img->data = data;
+    return img;
+}
+
+int iris_cuda_vae_decode_f32(iris_cuda_vae_t *v, const float *latent, int lh, int lw, float *out) {
+    if (!out) return iris_fail(IRIS_CUDA_ERR_ARG, "null output");
+    return decode_host(v, latent, lh, lw, NULL, out);
+}
+
+void iris_cuda_image_free(iris_cuda_image_t *img) {
+    if (!img) return;
+    free(img->data);
+    free(img);
+}
+
+uint64_t iris_cuda_vae_graph_kernels(const iris_cuda_vae_t *v) { return v ? v->plan.graph_kernels : 0; }

@@ -53,6 +53,12 @@ class ZImageConfig(C.Structure):
                    rope_theta=float(c["rope_theta"]), axes_dims=(C.c_int * 3)(*c["axes_dims"]))
 
 
+class Image(C.Structure):
+    """iris_cuda_image_t (the reference's iris_image layout, iris.h:73-78)."""
+    _fields_ = [("width", C.c_int), ("height", C.c_int), ("channels", C.c_int),
+                ("data", C.POINTER(C.c_uint8))]
+
+
 class Ref(C.Structure):
     _fields_ = [("latent", _fp), ("h", C.c_int), ("w", C.c_int), ("t_offset", C.c_int)]
 
@@ -125,6 +131,15 @@ SIGNATURES = {
                                                    C.c_int, _fp, C.c_int, _fp, C.c_int, PROGRESS_CB]),
     "iris_cuda_sample_euler_zimage_dev": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p,
                                                     C.c_int, _fp, C.c_int]),
+    "iris_cuda_vae_load": (C.c_void_p, [C.c_char_p, C.c_int, C.c_float, C.c_float]),
+    "iris_cuda_vae_free": (None, [C.c_void_p]),
+    "iris_cuda_vae_weight_bytes": (C.c_size_t, [C.c_void_p]),
+    "iris_cuda_vae_decode": (C.c_void_p, [C.c_void_p, _fp, C.c_int, C.c_int, C.c_int]),
+    "iris_cuda_image_free": (None, [C.c_void_p]),
+    "iris_cuda_vae_decode_f32": (C.c_int, [C.c_void_p, _fp, C.c_int, C.c_int, _fp]),
+    "iris_cuda_vae_decode_dev": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p,
+                                           C.c_void_p]),
+    "iris_cuda_vae_graph_kernels": (C.c_uint64, [C.c_void_p]),
     # iris_gpu_* surface (iris_metal.h names)
     "iris_gpu_tensor_create": (C.c_void_p, [_fp, C.c_size_t]),
     "iris_gpu_tensor_alloc": (C.c_void_p, [C.c_size_t]),
@@ -417,3 +432,63 @@ class ZImage:
         p = lib().iris_cuda_sample_euler_zimage(self.h, _f(zz), 1, c, h, w, self.cfg.patch_size, _f(cp),
                                                 cp.shape[0], _f(sc), len(sc) - 1, PROGRESS_CB(0))
         return _take_floats(p, c * h * w, (c, h, w))
+
+
+class Vae:
+    """Resident autoencoder decoder (libiris_cuda): latent -> RGB image."""
+
+    def __init__(self, handle, z: int):
+        if not handle:
+            raise IrisCudaError(last_error() or "VAE load failed")
+        self.h = handle
+        self.z = z
+
+    @classmethod
+    def load(cls, vae_dir: str, z: int = 0, scaling: float = 0.0, shift: float = 0.0) -> "Vae":
+        """z <= 0: latent channels, scaling and shift from vae_dir/config.json."""
+        h = lib().iris_cuda_vae_load(vae_dir.encode(), z, scaling, shift)
+        zz = z
+        if zz <= 0:
+            import json
+            import os
+            cfg = os.path.join(vae_dir, "config.json")
+            zz = json.load(open(cfg)).get("latent_channels", 32) if os.path.exists(cfg) else 32
+        return cls(h, zz)
+
+    def close(self):
+        if self.h:
+            lib().iris_cuda_vae_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def weight_bytes(self) -> int:
+        return lib().iris_cuda_vae_weight_bytes(self.h)
+
+    def decode(self, latent: np.ndarray) -> np.ndarray:
+        """[4z, h, w] latent -> uint8 [16h, 16w, 3] (iris_vae_decode)."""
+        lat = np.ascontiguousarray(latent, np.float32)
+        _, h, w = lat.shape
+        p = lib().iris_cuda_vae_decode(self.h, _f(lat), 1, h, w)
+        if not p:
+            raise IrisCudaError(last_error())
+        img = C.cast(p, C.POINTER(Image)).contents
+        out = np.ctypeslib.as_array(img.data, shape=(img.height, img.width, img.channels)).copy()
+        lib().iris_cuda_image_free(p)
+        return out
+
+    def decode_f32(self, latent: np.ndarray) -> np.ndarray:
+        """[4z, h, w] latent -> f32 RGB planes [3, 16h, 16w] before the uint8 conversion."""
+        lat = np.ascontiguousarray(latent, np.float32)
+        _, h, w = lat.shape
+        out = np.zeros((3, 16 * h, 16 * w), np.float32)
+        if lib().iris_cuda_vae_decode_f32(self.h, _f(lat), h, w, _f(out)):
+            raise IrisCudaError(last_error())
+        return out
+
+    def graph_kernels(self) -> int:
+        return lib().iris_cuda_vae_graph_kernels(self.h)

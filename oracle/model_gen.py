@@ -253,11 +253,14 @@ def zimage_ffn_dim(dim: int) -> int:
 
 
 # ------------------------------------------------------------------ Flux VAE
-def vae_tensor_specs(z: int = 32) -> list[tuple[str, tuple, str]]:
+def vae_tensor_specs(z: int = 32, zimage: bool = False) -> list[tuple[str, tuple, str]]:
     """Tensors of the Flux autoencoder as the reference's loader reads them
     (iris_vae_load_safetensors_ex, iris_vae.c:1227-1385: base 128 channels,
     multipliers 1/2/4/4, two resnets per encoder level and three per decoder
-    level, one attention in each mid block, batch-norm latent statistics)."""
+    level, one attention in each mid block, batch-norm latent statistics).
+    zimage: the Z-Image autoencoder, which has neither the batch-norm latent
+    statistics nor the quant / post-quant 1x1 convolutions (the loader treats
+    both as optional, :1333-1363)."""
     mult = [1, 2, 4, 4]
     s = []
 
@@ -289,8 +292,9 @@ def vae_tensor_specs(z: int = 32) -> list[tuple[str, tuple, str]]:
     attn("encoder.mid_block.attentions.0", 512)
     resblock("encoder.mid_block.resnets.1", 512, 512)
     s.extend([("encoder.conv_norm_out.weight", (512,), "gn_w"), ("encoder.conv_norm_out.bias", (512,), "bias"),
-              ("encoder.conv_out.weight", (2 * z, 512, 3, 3), "conv"), ("encoder.conv_out.bias", (2 * z,), "bias"),
-              ("quant_conv.weight", (2 * z, 2 * z, 1, 1), "conv"), ("quant_conv.bias", (2 * z,), "bias")])
+              ("encoder.conv_out.weight", (2 * z, 512, 3, 3), "conv"), ("encoder.conv_out.bias", (2 * z,), "bias")])
+    if not zimage:
+        s.extend([("quant_conv.weight", (2 * z, 2 * z, 1, 1), "conv"), ("quant_conv.bias", (2 * z,), "bias")])
     s.extend([("decoder.conv_in.weight", (512, z, 3, 3), "conv"), ("decoder.conv_in.bias", (512,), "bias")])
     resblock("decoder.mid_block.resnets.0", 512, 512)
     attn("decoder.mid_block.attentions.0", 512)
@@ -305,35 +309,55 @@ def vae_tensor_specs(z: int = 32) -> list[tuple[str, tuple, str]]:
         s.extend([(f"decoder.up_blocks.{i}.upsamplers.0.conv.weight", (ch, ch, 3, 3), "conv"),
                   (f"decoder.up_blocks.{i}.upsamplers.0.conv.bias", (ch,), "bias")])
     s.extend([("decoder.conv_norm_out.weight", (128,), "gn_w"), ("decoder.conv_norm_out.bias", (128,), "bias"),
-              ("decoder.conv_out.weight", (3, 128, 3, 3), "conv"), ("decoder.conv_out.bias", (3,), "bias"),
-              ("bn.running_mean", (4 * z,), "bn_mean"), ("bn.running_var", (4 * z,), "bn_var"),
-              ("post_quant_conv.weight", (z, z, 1, 1), "conv"), ("post_quant_conv.bias", (z,), "bias")])
+              ("decoder.conv_out.weight", (3, 128, 3, 3), "conv"), ("decoder.conv_out.bias", (3,), "bias")])
+    if not zimage:
+        s.extend([("bn.running_mean", (4 * z,), "bn_mean"), ("bn.running_var", (4 * z,), "bn_var"),
+                  ("post_quant_conv.weight", (z, z, 1, 1), "conv"), ("post_quant_conv.bias", (z,), "bias")])
     return s
 
 
-def make_vae_model(model_dir: str, seed: int, z: int = 32) -> str:
-    """Random Flux VAE (bf16 safetensors) under model_dir/vae/; returns the
+# Z-Image autoencoder latent scaling (its vae/config.json; read by the
+# reference through iris_parse_vae_config, iris_vae_config.h)
+ZIMAGE_VAE_SCALING = 0.3611
+ZIMAGE_VAE_SHIFT = 0.1159
+
+
+def _vae_tensor(seed: int, name: str, shp: tuple, kind: str) -> np.ndarray:
+    rng = np.random.default_rng([seed, zlib.crc32(name.encode())])
+    g = rng.standard_normal(shp, dtype=np.float32)
+    if kind == "conv":
+        x = g / np.float32(np.sqrt(np.prod(shp[1:])))
+    elif kind == "gn_w":
+        x = 1.0 + 0.1 * g
+    elif kind == "bn_mean":
+        x = 0.5 * g
+    elif kind == "bn_var":
+        x = 1.0 + np.abs(0.2 * g)
+    else:
+        x = 0.02 * g
+    return f32_to_bf16_bits(x.astype(np.float32))
+
+
+def vae_weights(seed: int, z: int = 32, zimage: bool = False) -> dict[str, np.ndarray]:
+    """f32 (bf16-valued) tensors of make_vae_model without disk I/O."""
+    return {n: bf16_bits_to_f32(_vae_tensor(seed, n, shp, kind)) for n, shp, kind in vae_tensor_specs(z, zimage)}
+
+
+def make_vae_model(model_dir: str, seed: int, z: int = 32, zimage: bool = False) -> str:
+    """Random autoencoder (bf16 safetensors) under model_dir/vae/; returns the
     weights file.  Convolutions ~ N(0, 1/fan_in) so activations keep O(1)
     scale through the decoder; GroupNorm scales 1 + N(0, 0.1); batch-norm
-    latent statistics mean N(0, 0.5), variance 1 + |N(0, 0.2)|."""
+    latent statistics mean N(0, 0.5), variance 1 + |N(0, 0.2)|.  zimage: the
+    Z-Image variant (no batch-norm statistics or quant convolutions; latent
+    scaling and shift in config.json)."""
     os.makedirs(os.path.join(model_dir, "vae"), exist_ok=True)
+    cfg = {"_class_name": "AutoencoderKLFlux2", "latent_channels": z}
+    if zimage:
+        cfg = {"_class_name": "AutoencoderKL", "latent_channels": z,
+               "scaling_factor": ZIMAGE_VAE_SCALING, "shift_factor": ZIMAGE_VAE_SHIFT}
     with open(os.path.join(model_dir, "vae", "config.json"), "w") as f:
-        json.dump({"_class_name": "AutoencoderKLFlux2", "latent_channels": z}, f)
-    bits = {}
-    for name, shp, kind in vae_tensor_specs(z):
-        rng = np.random.default_rng([seed, zlib.crc32(name.encode())])
-        g = rng.standard_normal(shp, dtype=np.float32)
-        if kind == "conv":
-            x = g / np.float32(np.sqrt(np.prod(shp[1:])))
-        elif kind == "gn_w":
-            x = 1.0 + 0.1 * g
-        elif kind == "bn_mean":
-            x = 0.5 * g
-        elif kind == "bn_var":
-            x = 1.0 + np.abs(0.2 * g)
-        else:
-            x = 0.02 * g
-        bits[name] = f32_to_bf16_bits(x.astype(np.float32))
+        json.dump(cfg, f)
+    bits = {name: _vae_tensor(seed, name, shp, kind) for name, shp, kind in vae_tensor_specs(z, zimage)}
     path = os.path.join(model_dir, "vae", "diffusion_pytorch_model.safetensors")
     write_safetensors(path, bits)
     return path

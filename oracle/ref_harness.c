@@ -252,8 +252,10 @@ int ref_sample_euler_zimage(void *tf, float *z, int c, int h, int w, int ps,
 /* ------------------------------------------------------------------ VAE decode
  * The reference's CPU decoder on a model file (Flux layout: batch-norm latent
  * statistics, post-quant conv, z_channels latent channels before the 2x2
- * patchify).  Writes the uint8 RGB image (height x width x 3) to out_rgb,
- * which must hold 3 * (16 lh) * (16 lw) bytes. */
+ * patchify; scaling != 0 selects the Z-Image latent scaling instead, as
+ * iris_vae_load_safetensors_ex does).  Writes the uint8 RGB image
+ * (height x width x 3) to out_rgb, which must hold 3 * (16 lh) * (16 lw)
+ * bytes. */
 typedef struct iris_vae iris_vae_t;
 extern iris_vae_t *iris_vae_load_safetensors_ex(safetensors_file_t *sf, int z_channels,
                                                 float scaling_factor, float shift_factor);
@@ -261,11 +263,11 @@ extern void iris_vae_free(iris_vae_t *vae);
 extern iris_image *iris_vae_decode(iris_vae_t *vae, const float *latent, int batch,
                                    int latent_h, int latent_w);
 
-int ref_vae_decode(const char *vae_file, int z_channels, const float *latent, int lh, int lw,
-                   uint8_t *out_rgb, int *out_w, int *out_h) {
+int ref_vae_decode_ex(const char *vae_file, int z_channels, float scaling, float shift,
+                      const float *latent, int lh, int lw, uint8_t *out_rgb, int *out_w, int *out_h) {
     safetensors_file_t *sf = safetensors_open(vae_file);
     if (!sf) return -1;
-    iris_vae_t *vae = iris_vae_load_safetensors_ex(sf, z_channels, 0.0f, 0.0f);
+    iris_vae_t *vae = iris_vae_load_safetensors_ex(sf, z_channels, scaling, shift);
     if (!vae) { safetensors_close(sf); return -2; }
     iris_image *img = iris_vae_decode(vae, latent, 1, lh, lw);
     int rc = -3;
@@ -279,5 +281,11 @@ int ref_vae_decode(const char *vae_file, int z_channels, const float *latent, in
     iris_vae_free(vae);
     safetensors_close(sf);
     return rc;
+}
+
+/* Flux layout (batch-norm statistics, scaling 0) */
+int ref_vae_decode(const char *vae_file, int z_channels, const float *latent, int lh, int lw,
+                   uint8_t *out_rgb, int *out_w, int *out_h) {
+    return ref_vae_decode_ex(vae_file, z_channels, 0.0f, 0.0f, latent, lh, lw, out_rgb, out_w, out_h);
 }
 

@@ -60,18 +60,22 @@ class RefLib:
         L.ref_set_threads.argtypes = [C.c_int]
         L.ref_vae_decode.argtypes = [C.c_char_p, C.c_int, _fp, C.c_int, C.c_int, C.POINTER(C.c_uint8),
                                      C.POINTER(C.c_int), C.POINTER(C.c_int)]
+        L.ref_vae_decode_ex.argtypes = [C.c_char_p, C.c_int, C.c_float, C.c_float, _fp, C.c_int, C.c_int,
+                                        C.POINTER(C.c_uint8), C.POINTER(C.c_int), C.POINTER(C.c_int)]
 
     def set_threads(self, n: int):
         self.lib.ref_set_threads(n)
 
-    def vae_decode(self, vae_file: str, latent: np.ndarray, z: int = 32) -> np.ndarray:
-        """Reference CPU decode (iris_vae_decode) of a [4z, h, w] latent -> uint8 [16h, 16w, 3]."""
+    def vae_decode(self, vae_file: str, latent: np.ndarray, z: int = 32, scaling: float = 0.0,
+                   shift: float = 0.0) -> np.ndarray:
+        """Reference CPU decode (iris_vae_decode) of a [4z, h, w] latent -> uint8 [16h, 16w, 3].
+        scaling != 0: Z-Image latent scaling/shift instead of batch-norm statistics."""
         lat = np.ascontiguousarray(latent, np.float32)
         _, h, w = lat.shape
         out = np.zeros(3 * 16 * h * 16 * w, np.uint8)
         ow, oh = C.c_int(0), C.c_int(0)
-        rc = self.lib.ref_vae_decode(vae_file.encode(), z, _f(lat), h, w,
-                                     out.ctypes.data_as(C.POINTER(C.c_uint8)), C.byref(ow), C.byref(oh))
+        rc = self.lib.ref_vae_decode_ex(vae_file.encode(), z, scaling, shift, _f(lat), h, w,
+                                        out.ctypes.data_as(C.POINTER(C.c_uint8)), C.byref(ow), C.byref(oh))
         if rc != 3:
             raise RuntimeError(f"reference VAE decode failed ({rc})")
         return out[: oh.value * ow.value * 3].reshape(oh.value, ow.value, 3)
