@@ -64,7 +64,7 @@ def parse_args(argv=None):
                     help="profiling case: a Klein-4B-shaped model truncated to DOUBLE + SINGLE blocks "
                          "(same kernels and shapes, less memory); not a benchmark number")
     ap.add_argument("--profile-out", default=None, help="write the per-kernel CUDA-event profile (JSON)")
-    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "c5b"],
+    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "c5b", "vae512", "vae1024"],
                     help="c2 (default) is the benchmark; the others measure the remaining SURVEY configs "
                          "on one GPU (c1 K4B 64x64 single forward, c3 K4B 1024x1024 CFG 4.0, c4 K9B "
                          "1792x1792, c5 Z-Image 1024x1024, c5b K4B + 2 references)")
@@ -637,8 +637,180 @@ def run_config(args):
     return 0
 
 
+# ----------------------------------------------------------------------------- autoencoder decode
+VAE_LATENT = {"vae512": 32, "vae1024": 64}  # latent patches per side (image pixels / 16)
+
+
+def vae_metric(config):
+    px = 16 * VAE_LATENT[config]
+    return f"VAE decodes/s (Flux.2 autoencoder, {px}x{px})", px
+
+
+class RefVaeSample:
+    """The reference's CPU decoder (iris_vae_decode from its make-blas build,
+    oracle/_ref) on a random Flux autoencoder, one decode of a latent of
+    `lat` patches per side per sample."""
+
+    def __init__(self, lat):
+        from oracle import model_gen as mg
+        from oracle.ref_lib import RefLib
+        self.tmp = tempfile.TemporaryDirectory()
+        self.path = mg.make_vae_model(self.tmp.name, WEIGHT_SEED % 1000)
+        self.ref = RefLib("blas")
+        self.cores = len(os.sched_getaffinity(0))
+        self.ref.set_threads(self.cores)
+        self.lat = np.random.default_rng(11).standard_normal((128, lat, lat)).astype(np.float32)
+
+    def seconds(self):
+        t0 = time.perf_counter()
+        self.ref.vae_decode(self.path, self.lat)
+        return time.perf_counter() - t0
+
+    def close(self):
+        self.tmp.cleanup()
+
+
+def run_vae_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    metric, px = vae_metric(args.config)
+    # 1024x1024 is sampled at 512x512 and scaled by the pixel count (the decoder is
+    # linear in pixels apart from the mid-block attention, < 2% of its FLOPs at 512x512)
+    lat = min(VAE_LATENT[args.config], 32)
+    scale = (VAE_LATENT[args.config] / lat) ** 2
+    rs = RefVaeSample(lat)
+    secs = [rs.seconds() * scale for _ in range(max(1, min(args.steps, 2)))]
+    rs.close()
+    value = 1.0 / statistics.mean(secs)
+    sample = (f"reference make-blas build (oracle/_ref, OpenBLAS 0.3.15), iris_vae_decode of one "
+              f"{16 * lat}x{16 * lat} latent per sample" + (f", scaled x{scale:g} by pixels" if scale != 1 else ""))
+    line = {"impl": "reference", "metric": metric, "value": value, "unit": "decodes/s", "n_gpus": world,
+            "steps": len(secs), "warmup": 0, "ms_per_step": 1000.0 / value, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": {"workload": f"autoencoder decode {px}x{px}", "latent": [128, VAE_LATENT[args.config], VAE_LATENT[args.config]]},
+            "cpu_baseline": {"value": value, "unit": "decodes/s", "cores": rs.cores, "kind": "reference",
+                             "sample": sample},
+            "e2e": {"value": value, "unit": "decodes/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
+def run_vae(args):
+    """Autoencoder decode (the step after the denoising loop): decodes/s of the
+    whole job, one latent per rank per step (seed replicas at N > 1)."""
+    import torch
+
+    import iris_cuda
+    rank, world, local = dist_env()
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist = dist_init(world, "nccl", dev)
+    lib = iris_cuda.lib()
+    assert lib.iris_cuda_init(local) == 0, iris_cuda.last_error()
+    stream = torch.cuda.ExternalStream(lib.iris_cuda_stream(), device=dev)
+    peaks, peak_src = load_peaks()
+    metric, px = vae_metric(args.config)
+    lh = lw = VAE_LATENT[args.config]
+    vae = iris_cuda.Vae.random(32, seed=WEIGHT_SEED)
+    lat = np.random.default_rng(11 + rank).standard_normal((128, lh, lw)).astype(np.float32)
+    lat_d = torch.from_numpy(lat).to(dev)
+    rgb_d = torch.empty(3 * 256 * lh * lw, dtype=torch.uint8, device=dev)
+
+    def run(i):
+        rc = lib.iris_cuda_vae_decode_dev(vae.h, lat_d.data_ptr(), lh, lw, rgb_d.data_ptr(), None)
+        assert rc == 0, iris_cuda.last_error()
+
+    def timed(fn, n):
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        l0 = lib.iris_cuda_kernel_launches()
+        e0.record(stream)
+        for i in range(n):
+            fn(i)
+        e1.record(stream)
+        e1.synchronize()
+        torch.cuda.synchronize()
+        if dist:
+            dist.barrier()
+        return reduce_max(e0.elapsed_time(e1), world, dev), lib.iris_cuda_kernel_launches() - l0
+
+    for i in range(max(3, args.warmup)):
+        run(i)
+    with ClockSampler(gpu_smi_id(local)) as clk:
+        ms, launches = timed(run, args.steps)
+    per = ms / args.steps
+    # end to end through the host API: latent H2D, decode, uint8 image D2H every step
+    pin = torch.from_numpy(lat).pin_memory()
+    img = np.empty((16 * lh, 16 * lw, 3), np.uint8)
+
+    def run_host(i):
+        vae_img = vae.decode(pin.numpy())
+        img[...] = vae_img
+
+    run_host(0)
+    ms_e2e, _ = timed(run_host, max(3, args.steps // 2))
+    per_e2e = ms_e2e / max(3, args.steps // 2)
+    prof = vae.profile()
+    conv = [e for e in prof if e["name"].startswith("conv")]
+    conv_flops = sum(e["flops"] for e in conv)
+    conv_ms = sum(e["ms"] for e in conv)
+    tot_flops = sum(e["flops"] for e in prof)
+    tot_ms = sum(e["ms"] for e in prof)
+    shares = {}
+    for e in prof:
+        k = e["name"]
+        d = shares.setdefault(k, {"launches": 0, "ms": 0.0, "flops": 0.0, "bytes": 0.0})
+        d["launches"] += 1
+        d["ms"] += e["ms"]
+        d["flops"] += e["flops"]
+        d["bytes"] += e["bytes"]
+    for d in shares.values():
+        d["share"] = d["ms"] / tot_ms if tot_ms else None
+        d["tflops"] = d["flops"] / (d["ms"] / 1e3) / 1e12 if d["ms"] and d["flops"] else None
+        d["gbs"] = d["bytes"] / (d["ms"] / 1e3) / 1e9 if d["ms"] else None
+    achieved = conv_flops / (conv_ms / 1e3) / 1e12
+    line = {"impl": "ours", "metric": metric, "value": world * 1000.0 / per, "unit": "decodes/s", "n_gpus": world,
+            "steps": args.steps, "warmup": max(3, args.warmup), "ms_per_step": per, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": f"Flux.2 autoencoder decode of one {px}x{px} image per GPU "
+                                   f"(latent [128, {lh}, {lw}])", "model": "AutoencoderKLFlux2 decoder, random init",
+                       "global_batch": world, "parallelism": f"seed-replicas x{world}",
+                       "l2": "inputs resident; every decode streams > 126 MB of activations through HBM"},
+            "clocks": clk.summary(),
+            "e2e": {"value": world * 1000.0 / per_e2e, "unit": "decodes/s", "h2d_bytes_per_step": int(lat.nbytes),
+                    "d2h_bytes_per_step": int(img.nbytes)},
+            "gpu_launches": int(launches),
+            "roofline": {"kernel": "conv_tc_kernel (3x3 convolutions, implicit GEMM)", "bound": "tensor",
+                         "achieved": achieved, "peak": peaks["bf16_tflops"], "unit": "TFLOP/s",
+                         "frac": achieved / peaks["bf16_tflops"], "peak_source": peak_src, "traffic": None,
+                         "conv_tflop_per_decode": conv_flops / 1e12, "tflop_per_decode": tot_flops / 1e12,
+                         "decode_ms_unfused_launches": tot_ms, "by_launch_name": shares},
+            "cpu_baseline": None}
+    if rank == 0 and not args.no_cpu_baseline:
+        lat_s = min(lh, 32)
+        scale = (lh / lat_s) ** 2
+        rs = RefVaeSample(lat_s)
+        sec = rs.seconds() * scale
+        rs.close()
+        line["cpu_baseline"] = {"value": 1.0 / sec, "unit": "decodes/s", "cores": rs.cores, "kind": "reference",
+                                "sample": f"one reference iris_vae_decode at {16 * lat_s}x{16 * lat_s}"
+                                          + (f", scaled x{scale:g} by pixels" if scale != 1 else "")}
+    vae.close()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+    if dist:
+        dist.barrier()
+        dist.destroy_process_group()
+    return 0
+
+
 def main(argv=None):
     args = parse_args(argv)
+    if args.config.startswith("vae"):
+        return run_vae_reference(args) if args.impl == "reference" else run_vae(args)
     if args.impl == "reference":
         return run_reference(args)
     if args.config != "c2":

@@ -309,6 +309,11 @@ typedef struct {
  * scaling == 0 selects the Flux batch-norm branch (eps 1e-4), else Z-Image's
  * x / scaling + shift (eps 1e-6). */
 iris_cuda_vae_t *iris_cuda_vae_load(const char *vae_dir, int z_channels, float scaling, float shift);
+/* Random-init decoder (seeded host RNG: projections N(0, 1/fan_in), norm
+ * scales 1 + N(0, 0.1), biases N(0, 0.02)) for benchmarks; no reference
+ * counterpart.  scaling == 0: Flux layout (batch-norm statistics, post-quant
+ * conv), else Z-Image's. */
+iris_cuda_vae_t *iris_cuda_vae_random(int z_channels, float scaling, float shift, uint64_t seed);
 /* Replaces iris_vae_free (iris_vae.c:1024). */
 void iris_cuda_vae_free(iris_cuda_vae_t *vae);
 size_t iris_cuda_vae_weight_bytes(const iris_cuda_vae_t *vae);
@@ -331,6 +336,10 @@ int iris_cuda_vae_decode_dev(iris_cuda_vae_t *vae, const float *d_latent, int la
                              uint8_t *d_rgb8, float *d_rgb_f32);
 /* kernels in one captured decode (0 before the first decode) */
 uint64_t iris_cuda_vae_graph_kernels(const iris_cuda_vae_t *vae);
+/* Time every kernel of one decode at the most recent latent size (no graph;
+ * an event after each launch), as iris_cuda_flux_profile does for the
+ * transformer.  Returns the number of entries or a negative status. */
+int iris_cuda_vae_profile(iris_cuda_vae_t *vae, iris_cuda_kernel_time_t *out, int max_entries);
 
 /* ------------------------------------------------------------------ 3. iris_gpu_* surface
  * Device-resident tensors and ops with the names and signatures of

@@ -31,6 +31,7 @@ typedef struct {
     float *b;        /* [cout_pad] (conv bias + shortcut bias) */
     CUtensorMap tm;
     int taps0, cin0, cin1, cout, cout_pad, bn, k;
+    int cin_real;    /* segment-0 channels before padding to 64 */
 } vconv_t;
 
 typedef struct {
@@ -95,55 +96,101 @@ static void *vae_upload(iris_cuda_vae_t *v, const void *host, size_t bytes) {
     return d;
 }
 
-/* f32 host copy of tensor `name` with `numel` elements (NULL if absent or mis-sized) */
-static float *read_host(const st_model_t *st, const char *name, size_t numel) {
-    const st_tensor_t *t = st_find(st, name);
-    if (!t) return NULL;
+/* Where the weights come from: a safetensors file, or (st == NULL) a seeded
+ * host RNG for benchmarks: convolution / projection weights N(0, 1/fan_in),
+ * norm scales 1 + N(0, 0.1), biases N(0, 0.02), latent statistics mean
+ * N(0, 0.5) and variance 1 + |N(0, 0.2)|. */
+typedef struct {
+    const st_model_t *st;
+    uint64_t seed;
+} vsrc_t;
+
+static uint64_t splitmix(uint64_t *x) {
+    uint64_t z = (*x += 0x9E3779B97F4A7C15ull);
+    z = (z ^ (z >> 30)) * 0xBF58476D1CE4E5B9ull;
+    z = (z ^ (z >> 27)) * 0x94D049BB133111EBull;
+    return z ^ (z >> 31);
+}
+
+static float rand_normal(uint64_t *x) {  /* Box-Muller on two 24-bit uniforms */
+    const float u1 = ((float)(splitmix(x) >> 40) + 0.5f) * (1.0f / 16777216.0f);
+    const float u2 = (float)(splitmix(x) >> 40) * (1.0f / 16777216.0f);
+    return sqrtf(-2.0f * logf(u1)) * cosf(6.28318530718f * u2);
+}
+
+static int ends_with(const char *s, const char *suf) {
+    size_t a = strlen(s), b = strlen(suf);
+    return a >= b && strcmp(s + a - b, suf) == 0;
+}
+
+/* f32 host copy of tensor `name` with `numel` elements (NULL if absent or
+ * mis-sized); fan_in scales random projection weights */
+static float *read_host(const vsrc_t *src, const char *name, size_t numel, int fan_in) {
+    if (src->st) {
+        const st_tensor_t *t = st_find(src->st, name);
+        if (!t) return NULL;
+        float *h = (float *)malloc(numel * sizeof(float));
+        if (!h) return NULL;
+        if (st_read_f32(src->st, t, h, numel)) { free(h); return NULL; }
+        return h;
+    }
     float *h = (float *)malloc(numel * sizeof(float));
     if (!h) return NULL;
-    if (st_read_f32(st, t, h, numel)) { free(h); return NULL; }
+    uint64_t x = src->seed * 0x2545F4914F6CDD1Dull ^ (uint64_t)iris_crc32(name);
+    const int is_bias = ends_with(name, ".bias");
+    const int is_norm = !is_bias && (strstr(name, "norm") != NULL);
+    for (size_t i = 0; i < numel; i++) {
+        const float g = rand_normal(&x);
+        if (strcmp(name, "bn.running_mean") == 0) h[i] = 0.5f * g;
+        else if (strcmp(name, "bn.running_var") == 0) h[i] = 1.0f + fabsf(0.2f * g);
+        else if (is_bias) h[i] = 0.02f * g;
+        else if (is_norm) h[i] = 1.0f + 0.1f * g;
+        else h[i] = g / sqrtf((float)(fan_in > 0 ? fan_in : 1));
+    }
     return h;
 }
 
+static int has_tensor(const vsrc_t *src, const char *name) { return src->st ? st_find(src->st, name) != NULL : 1; }
+
 static int missing(const char *name) { return iris_fail(IRIS_CUDA_ERR_IO, "VAE tensor %s missing or mis-sized", name); }
 
-static int load_vec(iris_cuda_vae_t *v, const st_model_t *st, const char *name, int n, float **dst) {
-    float *h = read_host(st, name, (size_t)n);
+static int load_vec(iris_cuda_vae_t *v, const vsrc_t *st, const char *name, int n, int fan_in, float **dst) {
+    float *h = read_host(st, name, (size_t)n, fan_in);
     if (!h) return missing(name);
     *dst = (float *)vae_upload(v, h, (size_t)n * 4);
     free(h);
     return *dst ? 0 : iris_fail(IRIS_CUDA_ERR_OOM, "VAE upload");
 }
 
-static int load_gn(iris_cuda_vae_t *v, const st_model_t *st, const char *prefix, int c, vgn_t *gn) {
+static int load_gn(iris_cuda_vae_t *v, const vsrc_t *st, const char *prefix, int c, vgn_t *gn) {
     char n[300];
     snprintf(n, sizeof(n), "%s.weight", prefix);
-    int rc = load_vec(v, st, n, c, &gn->g);
+    int rc = load_vec(v, st, n, c, 0, &gn->g);
     snprintf(n, sizeof(n), "%s.bias", prefix);
-    return rc ? rc : load_vec(v, st, n, c, &gn->b);
+    return rc ? rc : load_vec(v, st, n, c, 0, &gn->b);
 }
 
 /* Convolution `prefix` (OIHW [cout, cin, k, k], k = 3 if taps == 9 else 1)
  * repacked as the GEMM operand [cout_pad, taps * cin_pad (+ skip_cin)]
  * with K ordered (tap, channel); an optional 1x1 shortcut `skip` ([cout,
  * skip_cin]) appended as extra K columns, its bias added to the conv bias. */
-static int load_conv(iris_cuda_vae_t *v, const st_model_t *st, const char *prefix, int cin, int cin_pad, int cout,
+static int load_conv(iris_cuda_vae_t *v, const vsrc_t *st, const char *prefix, int cin, int cin_pad, int cout,
                      int taps, const char *skip, int skip_cin, int bn, vconv_t *cv) {
     char n[300];
     const int cout_pad = (cout + bn - 1) / bn * bn;
     const int k = taps * cin_pad + (skip ? skip_cin : 0);
     snprintf(n, sizeof(n), "%s.weight", prefix);
-    float *w = read_host(st, n, (size_t)cout * cin * taps);
+    float *w = read_host(st, n, (size_t)cout * cin * taps, cin * taps);
     if (!w) return missing(n);
     snprintf(n, sizeof(n), "%s.bias", prefix);
-    float *b = read_host(st, n, (size_t)cout);
+    float *b = read_host(st, n, (size_t)cout, 0);
     if (!b) { free(w); return missing(n); }
     float *ws = NULL, *bs = NULL;
     if (skip) {
         snprintf(n, sizeof(n), "%s.weight", skip);
-        ws = read_host(st, n, (size_t)cout * skip_cin);
+        ws = read_host(st, n, (size_t)cout * skip_cin, skip_cin);
         snprintf(n, sizeof(n), "%s.bias", skip);
-        bs = read_host(st, n, (size_t)cout);
+        bs = read_host(st, n, (size_t)cout, 0);
         if (!ws || !bs) { free(w); free(b); free(ws); free(bs); return missing(n); }
     }
     uint16_t *m = (uint16_t *)calloc((size_t)cout_pad * k, sizeof(uint16_t));
@@ -168,6 +215,7 @@ static int load_conv(iris_cuda_vae_t *v, const st_model_t *st, const char *prefi
                                    (uint32_t)(bn < 128 ? bn : 128)))
         rc = iris_fail(IRIS_CUDA_ERR_CUDA, "VAE weight tensor map");
     cv->taps0 = taps;
+    cv->cin_real = cin;
     cv->cin0 = cin_pad;
     cv->cin1 = skip ? skip_cin : 0;
     cv->cout = cout;
@@ -180,7 +228,7 @@ static int load_conv(iris_cuda_vae_t *v, const st_model_t *st, const char *prefi
 
 static int conv_bn(int cout) { return cout >= 256 ? 256 : cout >= 128 ? 128 : 16; }
 
-static int load_res(iris_cuda_vae_t *v, const st_model_t *st, const char *prefix, int cin, int cout, vres_t *r) {
+static int load_res(iris_cuda_vae_t *v, const vsrc_t *st, const char *prefix, int cin, int cout, vres_t *r) {
     char n[300], n2[300];
     r->cin = cin;
     r->cout = cout;
@@ -197,7 +245,7 @@ static int load_res(iris_cuda_vae_t *v, const st_model_t *st, const char *prefix
 }
 
 /* [c, c] (or [c, c, 1, 1]) projections of the mid-block attention */
-static int load_attn(iris_cuda_vae_t *v, const st_model_t *st, const char *prefix) {
+static int load_attn(iris_cuda_vae_t *v, const vsrc_t *st, const char *prefix) {
     const int c = VAE_MID;
     char n[300];
     const char *names[4] = {"to_q", "to_k", "to_v", "to_out.0"};
@@ -205,9 +253,9 @@ static int load_attn(iris_cuda_vae_t *v, const st_model_t *st, const char *prefi
     int rc = 0;
     for (int i = 0; i < 4 && !rc; i++) {
         snprintf(n, sizeof(n), "%s.%s.weight", prefix, names[i]);
-        if (!(w[i] = read_host(st, n, (size_t)c * c))) rc = missing(n);
+        if (!(w[i] = read_host(st, n, (size_t)c * c, c))) rc = missing(n);
         snprintf(n, sizeof(n), "%s.%s.bias", prefix, names[i]);
-        if (!rc && !(b[i] = read_host(st, n, (size_t)c))) rc = missing(n);
+        if (!rc && !(b[i] = read_host(st, n, (size_t)c, 0))) rc = missing(n);
     }
     uint16_t *m = rc ? NULL : (uint16_t *)malloc((size_t)2 * c * c * 2);
     float *bb = rc ? NULL : (float *)malloc((size_t)2 * c * 4);
@@ -238,13 +286,13 @@ static int load_attn(iris_cuda_vae_t *v, const st_model_t *st, const char *prefi
     return rc;
 }
 
-static int vae_load_all(iris_cuda_vae_t *v, const st_model_t *st) {
+static int vae_load_all(iris_cuda_vae_t *v, const vsrc_t *st) {
     int rc;
     char n[300];
     const int z = v->z;
     if (!v->scaling) {  /* Flux: batch-norm statistics -> (mean, sqrt(var + eps)) */
-        float *mean = read_host(st, "bn.running_mean", (size_t)v->lat_ch);
-        float *var = read_host(st, "bn.running_var", (size_t)v->lat_ch);
+        float *mean = read_host(st, "bn.running_mean", (size_t)v->lat_ch, 0);
+        float *var = read_host(st, "bn.running_var", (size_t)v->lat_ch, 0);
         float *sd = (float *)malloc((size_t)v->lat_ch * 4);
         rc = 0;
         if (!sd) rc = iris_fail(IRIS_CUDA_ERR_OOM, "VAE staging");
@@ -262,9 +310,10 @@ static int vae_load_all(iris_cuda_vae_t *v, const st_model_t *st) {
         free(mean); free(var); free(sd);
         if (rc) return rc;
     }
-    if (st_find(st, "post_quant_conv.weight")) {
-        if ((rc = load_vec(v, st, "post_quant_conv.weight", z * z, &v->pq_w))) return rc;
-        if ((rc = load_vec(v, st, "post_quant_conv.bias", z, &v->pq_b))) return rc;
+    /* present in Flux files only; the random source follows the Flux layout when scaling == 0 */
+    if (st->st ? has_tensor(st, "post_quant_conv.weight") : !v->scaling) {
+        if ((rc = load_vec(v, st, "post_quant_conv.weight", z * z, z, &v->pq_w))) return rc;
+        if ((rc = load_vec(v, st, "post_quant_conv.bias", z, 0, &v->pq_b))) return rc;
     }
     if ((rc = load_conv(v, st, "decoder.conv_in", z, 64, VAE_MID, 9, NULL, 0, 256, &v->conv_in))) return rc;
     if ((rc = load_res(v, st, "decoder.mid_block.resnets.0", VAE_MID, VAE_MID, &v->mid[0]))) return rc;
@@ -308,6 +357,18 @@ void iris_cuda_vae_free(iris_cuda_vae_t *v) {
     free(v);
 }
 
+static iris_cuda_vae_t *vae_create(const vsrc_t *src, int z, float scaling, float shift) {
+    iris_cuda_vae_t *v = (iris_cuda_vae_t *)calloc(1, sizeof(*v));
+    if (!v) { iris_fail(IRIS_CUDA_ERR_OOM, "VAE struct"); return NULL; }
+    v->z = z;
+    v->lat_ch = 4 * z;
+    v->scaling = scaling;
+    v->shift = shift;
+    v->eps = scaling != 0.0f ? 1e-6f : 1e-4f;  /* iris_vae.c:1245 */
+    if (vae_load_all(v, src)) { iris_cuda_vae_free(v); return NULL; }
+    return v;
+}
+
 iris_cuda_vae_t *iris_cuda_vae_load(const char *vae_dir, int z_channels, float scaling, float shift) {
     if (!vae_dir) { iris_fail(IRIS_CUDA_ERR_ARG, "null VAE directory"); return NULL; }
     if (iris_rt_ensure()) return NULL;
@@ -329,17 +390,20 @@ iris_cuda_vae_t *iris_cuda_vae_load(const char *vae_dir, int z_channels, float s
     if (z < 1 || z > 32) { iris_fail(IRIS_CUDA_ERR_ARG, "latent channels %d (1..32 supported)", z); return NULL; }
     st_model_t st;
     if (st_open_dir(&st, vae_dir)) { iris_fail(IRIS_CUDA_ERR_IO, "cannot open VAE weights in %s", vae_dir); return NULL; }
-    iris_cuda_vae_t *v = (iris_cuda_vae_t *)calloc(1, sizeof(*v));
-    if (!v) { st_close(&st); iris_fail(IRIS_CUDA_ERR_OOM, "VAE struct"); return NULL; }
-    v->z = z;
-    v->lat_ch = 4 * z;
-    v->scaling = scaling;
-    v->shift = shift;
-    v->eps = scaling != 0.0f ? 1e-6f : 1e-4f;  /* iris_vae.c:1245 */
-    int rc = vae_load_all(v, &st);
+    vsrc_t src = {&st, 0};
+    iris_cuda_vae_t *v = vae_create(&src, z, scaling, shift);
     st_close(&st);
-    if (rc) { iris_cuda_vae_free(v); return NULL; }
     return v;
+}
+
+iris_cuda_vae_t *iris_cuda_vae_random(int z_channels, float scaling, float shift, uint64_t seed) {
+    if (iris_rt_ensure()) return NULL;
+    if (z_channels < 1 || z_channels > 32) {
+        iris_fail(IRIS_CUDA_ERR_ARG, "latent channels %d (1..32 supported)", z_channels);
+        return NULL;
+    }
+    vsrc_t src = {NULL, seed};
+    return vae_create(&src, z_channels, scaling, shift);
 }
 
 size_t iris_cuda_vae_weight_bytes(const iris_cuda_vae_t *v) { return v ? v->weight_bytes : 0; }
@@ -399,13 +463,28 @@ static int plan_ensure(iris_cuda_vae_t *v, int lh, int lw) {
 typedef struct {
     int rc;
     uint64_t kernels;
+    /* profiling (iris_cuda_vae_profile): an event after every launch */
+    iris_cuda_kernel_time_t *prof;
+    cudaEvent_t *ev;
+    int nprof, maxprof;
 } venq_t;
 
-static void enq_check(venq_t *E, cudaError_t e, const char *what) {
+/* account one launch: name, algorithmic FLOPs and HBM bytes for the profile */
+static void enq_done(venq_t *E, cudaError_t e, const char *what, double flops, double bytes) {
     if (E->rc) return;
-    if (e != cudaSuccess) E->rc = iris_cuda_check(e, what);
-    else E->kernels++;
+    if (e != cudaSuccess) { E->rc = iris_cuda_check(e, what); return; }
+    E->kernels++;
+    if (E->prof && E->nprof < E->maxprof) {
+        iris_cuda_kernel_time_t *k = &E->prof[E->nprof];
+        snprintf(k->name, sizeof(k->name), "%s", what);
+        k->flops = flops;
+        k->bytes = bytes;
+        cudaEventRecord(E->ev[E->nprof + 1], g_rt.stream);
+        E->nprof++;
+    }
 }
+
+static void enq_check(venq_t *E, cudaError_t e, const char *what) { enq_done(E, e, what, 0.0, 0.0); }
 
 static int pow2_at_least(int x) {
     int p = 1;
@@ -441,7 +520,12 @@ static void enq_conv(venq_t *E, const vconv_t *cv, const void *in0, int in0_c, c
     p.bias = cv->b;
     p.resid = resid;
     p.status = g_rt.d_status;
-    enq_check(E, iris_launch_conv(&p, g_rt.num_sms, g_rt.stream), "conv");
+    const double pix = (double)H * W;
+    const double kreal = (double)cv->taps0 * cv->cin_real + p.cin1;
+    const double bytes = pix * (cv->cin_real + p.cin1) * 2 + (double)cv->cout * kreal * 2 +
+                         pix * cv->cout * (mode == IRIS_CONV_BF16 ? 2 : 4) * (resid ? 2 : 1);
+    enq_done(E, iris_launch_conv(&p, g_rt.num_sms, g_rt.stream), cv->taps0 == 9 ? "conv3x3" : "conv1x1",
+             2.0 * pix * cv->cout * kreal, bytes);
 }
 
 /* GroupNorm statistics of x [P, C] into P->stats, then the bf16 normalised (and SiLU) copy */
@@ -452,11 +536,11 @@ static void enq_gn(venq_t *E, iris_cuda_vae_t *v, const float *x, long pix, int 
     long nb = (pix + ppi - 1) / ppi;
     if (nb > VAE_GN_BLOCKS) nb = VAE_GN_BLOCKS;
     if (!E->rc)
-        enq_check(E, iris_launch_gn_stats(x, pix, C, P->part, (int)nb, P->counter, P->stats, v->eps, g_rt.stream),
-                  "gn stats");
+        enq_done(E, iris_launch_gn_stats(x, pix, C, P->part, (int)nb, P->counter, P->stats, v->eps, g_rt.stream),
+                 "gn_stats", 0.0, (double)pix * C * 4);
     if (!E->rc)
-        enq_check(E, iris_launch_nhwc_to_bf16(x, pix, C, 0, P->stats, gn->g, gn->b, silu, 0, out, g_rt.stream),
-                  "gn apply");
+        enq_done(E, iris_launch_nhwc_to_bf16(x, pix, C, 0, P->stats, gn->g, gn->b, silu, 0, out, g_rt.stream),
+                 "gn_apply", 0.0, (double)pix * C * 6);
 }
 
 /* resnet block on P->X (H x W, r->cin channels) -> P->X (r->cout channels) */
@@ -466,8 +550,8 @@ static void enq_res(venq_t *E, iris_cuda_vae_t *v, const vres_t *r, int H, int W
     enq_gn(E, v, P->X, pix, r->cin, &r->n1, 1, P->Hb);
     const int skip = r->cin != r->cout;
     if (skip && !E->rc)
-        enq_check(E, iris_launch_nhwc_to_bf16(P->X, pix, r->cin, 0, NULL, NULL, NULL, 0, 0, P->Xb, g_rt.stream),
-                  "shortcut input");
+        enq_done(E, iris_launch_nhwc_to_bf16(P->X, pix, r->cin, 0, NULL, NULL, NULL, 0, 0, P->Xb, g_rt.stream),
+                 "to_bf16", 0.0, (double)pix * r->cin * 6);
     enq_conv(E, &r->c1, P->Hb, r->cin, NULL, 0, H, W, IRIS_CONV_F32, P->T, NULL);
     enq_gn(E, v, P->T, pix, r->cout, &r->n2, 1, P->Hb);
     enq_conv(E, &r->c2, P->Hb, r->cout, skip ? P->Xb : NULL, r->cin, H, W, IRIS_CONV_F32, P->X,
@@ -499,7 +583,8 @@ static void enq_gemm(venq_t *E, const void *a, int a_rows, int a_ld, const void 
     p.status = g_rt.d_status;
     int n = 1;
     cudaError_t e = iris_launch_gemm_ex(&p, g_rt.num_sms, g_rt.stream, &n);
-    enq_check(E, e, "attention gemm");
+    const double by = ((double)a_rows + b_rows) * K * 2 + (double)a_rows * b_rows * (mode == IRIS_EPI_BF16 ? 2 : 4);
+    enq_done(E, e, "attn_gemm", 2.0 * a_rows * b_rows * K, by);
     if (!E->rc && n > 1) E->kernels += (uint64_t)(n - 1);
 }
 
@@ -515,8 +600,8 @@ static void enq_attn(venq_t *E, iris_cuda_vae_t *v) {
     /* S = q k^T -> f32 [P3, P3p] */
     enq_gemm(E, P->qk, p3, 2 * c, P->qk + c, p3p, 2 * c, c, IRIS_EPI_F32, P->S, p3p, NULL, NULL);
     if (!E->rc)
-        enq_check(E, iris_launch_vae_softmax(P->S, p3, p3p, p3, 1.0f / sqrtf((float)c), P->Pm, g_rt.stream),
-                  "softmax");
+        enq_done(E, iris_launch_vae_softmax(P->S, p3, p3p, p3, 1.0f / sqrtf((float)c), P->Pm, g_rt.stream),
+                 "attn_softmax", 0.0, (double)p3 * p3p * 6);
     /* O = P V + bv -> bf16 [P3, 512] */
     enq_gemm(E, P->Pm, p3, p3p, P->vT, c, p3p, p3p, IRIS_EPI_BF16, P->O, c, v->b_v, NULL);
     /* x += O Wo^T + bo */
@@ -540,9 +625,9 @@ static int enqueue_decode(iris_cuda_vae_t *v, venq_t *E) {
         if (level > 0) {
             const long pix = (long)P->H[level] * P->W[level];
             if (!E->rc)
-                enq_check(E, iris_launch_nhwc_to_bf16(P->X, pix, ch, P->W[level], NULL, NULL, NULL, 0, 1, P->Hb,
-                                                      g_rt.stream),
-                          "upsample");
+                enq_done(E, iris_launch_nhwc_to_bf16(P->X, pix, ch, P->W[level], NULL, NULL, NULL, 0, 1, P->Hb,
+                                                     g_rt.stream),
+                         "upsample", 0.0, (double)pix * ch * 12);
             enq_conv(E, &v->upc[3 - level], P->Hb, ch, NULL, 0, P->H[level - 1], P->W[level - 1], IRIS_CONV_F32,
                      P->X, NULL);
         }
@@ -663,3 +748,31 @@ void iris_cuda_image_free(iris_cuda_image_t *img) {
 }
 
 uint64_t iris_cuda_vae_graph_kernels(const iris_cuda_vae_t *v) { return v ? v->plan.graph_kernels : 0; }
+
+/* Time every kernel of one decode of the current plan size (no graph; an
+ * event after each launch).  Returns the number of entries or a negative
+ * status. */
+int iris_cuda_vae_profile(iris_cuda_vae_t *v, iris_cuda_kernel_time_t *out, int max_entries) {
+    if (!v || !out || max_entries <= 0) return iris_fail(IRIS_CUDA_ERR_ARG, "null argument");
+    if (!v->plan.valid) return iris_fail(IRIS_CUDA_ERR_ARG, "decode once first (no plan)");
+    cudaEvent_t *ev = (cudaEvent_t *)calloc((size_t)max_entries + 1, sizeof(cudaEvent_t));
+    if (!ev) return iris_fail(IRIS_CUDA_ERR_OOM, "events");
+    int rc = 0, n = 0;
+    for (int i = 0; i <= max_entries && !rc; i++) rc = iris_cuda_check(cudaEventCreate(&ev[i]), "event");
+    if (!rc) {
+        venq_t E = {0};
+        E.prof = out;
+        E.ev = ev;
+        E.maxprof = max_entries;
+        cudaEventRecord(ev[0], g_rt.stream);
+        rc = enqueue_decode(v, &E);
+        iris_count_launch(E.kernels);
+        if (!rc) rc = iris_cuda_synchronize();
+        for (int i = 0; !rc && i < E.nprof; i++) cudaEventElapsedTime(&out[i].ms, ev[i], ev[i + 1]);
+        n = E.nprof;
+    }
+    for (int i = 0; i <= max_entries; i++)
+        if (ev[i]) cudaEventDestroy(ev[i]);
+    free(ev);
+    return rc ? rc : n;
+}

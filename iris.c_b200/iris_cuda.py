@@ -140,6 +140,8 @@ SIGNATURES = {
     "iris_cuda_vae_decode_dev": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_void_p,
                                            C.c_void_p]),
     "iris_cuda_vae_graph_kernels": (C.c_uint64, [C.c_void_p]),
+    "iris_cuda_vae_random": (C.c_void_p, [C.c_int, C.c_float, C.c_float, C.c_uint64]),
+    "iris_cuda_vae_profile": (C.c_int, [C.c_void_p, C.POINTER(KernelTime), C.c_int]),
     # iris_gpu_* surface (iris_metal.h names)
     "iris_gpu_tensor_create": (C.c_void_p, [_fp, C.c_size_t]),
     "iris_gpu_tensor_alloc": (C.c_void_p, [C.c_size_t]),
@@ -454,6 +456,19 @@ class Vae:
             cfg = os.path.join(vae_dir, "config.json")
             zz = json.load(open(cfg)).get("latent_channels", 32) if os.path.exists(cfg) else 32
         return cls(h, zz)
+
+    @classmethod
+    def random(cls, z: int = 32, seed: int = 1, scaling: float = 0.0, shift: float = 0.0) -> "Vae":
+        return cls(lib().iris_cuda_vae_random(z, scaling, shift, seed), z)
+
+    def profile(self, max_entries: int = 512):
+        """Per-kernel CUDA-event times of one decode at the last latent size."""
+        arr = (KernelTime * max_entries)()
+        n = lib().iris_cuda_vae_profile(self.h, arr, max_entries)
+        if n < 0:
+            raise IrisCudaError(last_error())
+        return [dict(name=arr[i].name.decode(), ms=arr[i].ms, flops=arr[i].flops, bytes=arr[i].bytes)
+                for i in range(n)]
 
     def close(self):
         if self.h:

@@ -118,3 +118,17 @@ def test_bad_arguments_fail_loudly(iris, flux_vae):
     assert iris.lib().iris_cuda_vae_decode_f32(v.h, iris._f(big), 200, 200, iris._f(np.zeros(1, np.float32))) != 0
     with pytest.raises(iris.IrisCudaError):
         iris.Vae.load("/nonexistent/vae")
+
+
+def test_random_init_decoder_is_finite_and_profiles(iris):
+    v = iris.Vae.random(32, seed=5)
+    lat = latent(32, 4, 4, seed=2)
+    img = v.decode(lat)
+    f = v.decode_f32(lat)
+    assert np.isfinite(f).all() and 0.05 < f.std() < 10
+    assert img.shape == (64, 64, 3)
+    prof = v.profile()
+    names = {e["name"] for e in prof}
+    assert {"conv3x3", "gn_stats", "gn_apply", "attn_gemm", "attn_softmax", "upsample"} <= names
+    assert len(prof) == v.graph_kernels()
+    v.close()
