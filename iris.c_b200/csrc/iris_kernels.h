@@ -242,8 +242,11 @@ enum {
 typedef struct {
     CUtensorMap tmap_a[2];    /* NHWC bf16 activations: 3-D {C, W, H}, box {64, bw, bh}    */
     CUtensorMap tmap_b;       /* weights: 2-D [cout_pad, K], box {64, min(bn, 128)}        */
+    CUtensorMap tmap_b_half;  /* the same weights, box {64, bn / 2} (CTA-pair launches)    */
+    int pair;                 /* 1: CTA-pair kernel (bn 128 or 256; 256-pixel units)       */
     int H, W;
-    int bw, bh;
+    int bw, bh;               /* bw a power of two */
+    int bw_log2;
     int taps0;                /* 9 or 1 */
     int cin0, cin1;           /* multiples of 64; cin1 = 0: no second segment */
     int cout, cout_pad, bn;   /* bn in {16, 32, 64, 128, 256}; cout_pad % bn == 0 */
@@ -251,21 +254,33 @@ typedef struct {
     void *out;
     const float *bias;        /* [cout_pad] */
     const float *resid;       /* optional f32 NHWC [H * W, cout]; may be `out` (F32 mode) */
+    double *gn_part;          /* optional: GroupNorm partial sums of the outputs, one slot of
+                                 64 doubles (32 groups x {sum, sum of squares}) per CTA;
+                                 iris_conv_grid slots                               */
+    int gn_cg;                /* channels per group (cout / 32: 4, 8 or 16)        */
     int *status;
 } IrisConvParams;
 /* 3-D tensor map over an NHWC bf16 tensor [H, W, C] (C % 64 == 0), box {64, bw, bh} */
 int iris_make_tmap_nhwc_bf16(CUtensorMap *m, const void *ptr, int H, int W, int C, int bw, int bh);
 cudaError_t iris_conv_init(void);
 cudaError_t iris_launch_conv(const IrisConvParams *p, int num_sms, cudaStream_t stream);
-/* GroupNorm statistics (32 groups) of NHWC f32 [P, C]: stats[2g] = mean,
- * stats[2g + 1] = 1 / sqrt(var + eps); part holds nblocks * 64 doubles,
- * *counter must be 0 (the kernel leaves it 0) */
-cudaError_t iris_launch_gn_stats(const float *x, long P, int C, double *part, int nblocks, unsigned *counter,
-                                 float *stats, float eps, cudaStream_t stream);
-/* NHWC f32 [P, C] -> bf16: optional GroupNorm apply (stats, gamma, beta), SiLU
- * and 2x nearest upsampling (W = input width; output [2H, 2W, C]) */
-cudaError_t iris_launch_nhwc_to_bf16(const float *x, long P, int C, int W, const float *stats, const float *gamma,
-                                     const float *beta, int silu, int up2, void *out, cudaStream_t stream);
+/* CTAs iris_launch_conv starts for p */
+int iris_conv_grid(const IrisConvParams *p, int num_sms);
+/* CTA pairs of the pair kernel that fit on the device at once (0: none) */
+int iris_conv_pairs_available(void);
+/* GroupNorm (32 groups) of a convolution's output from its gn_part partials
+ * (nparts slots, count = pixels * C / 32 values per group): per-channel affine
+ * ab[c] = gamma[c] * rstd_g, ab[C + c] = beta[c] - mean_g * ab[c] */
+cudaError_t iris_launch_gn_finalize(const double *part, int nparts, int C, const float *gamma, const float *beta,
+                                    float eps, long count, float *ab, cudaStream_t stream);
+/* NHWC f32 [P, C] -> bf16 x * ab[c] + ab[C + c] (+ SiLU); raw (optional) gets the plain bf16 copy */
+cudaError_t iris_launch_gn_affine(const float *x, long P, int C, const float *ab, int silu, void *out, void *raw,
+                                  cudaStream_t stream);
+/* GroupNorm partial sums (32 groups) of NHWC f32 [P, C] when no convolution
+ * epilogue produced them: one slot of 64 doubles per block (gn_part layout) */
+cudaError_t iris_launch_gn_stats(const float *x, long P, int C, double *part, int nblocks, cudaStream_t stream);
+/* NHWC f32 [P, C] -> bf16, optionally 2x nearest upsampled (W = input width; output [2H, 2W, C]) */
+cudaError_t iris_launch_nhwc_to_bf16(const float *x, long P, int C, int W, int up2, void *out, cudaStream_t stream);
 /* latent [4z, h, w] -> denormalised (bn_std/bn_mean, else x / scaling + shift),
  * unpatchified, optional f32 post-quant 1x1 conv -> bf16 NHWC [2h, 2w, 64] */
 cudaError_t iris_launch_vae_latent_prep(const float *lat, int z, int h, int w, const float *bn_mean,

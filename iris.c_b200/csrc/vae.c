@@ -21,7 +21,8 @@
 
 #define VAE_BASE 128
 #define VAE_MID 512
-#define VAE_GN_BLOCKS 592            /* 4 x 148 SMs: GroupNorm statistics blocks (max) */
+#define VAE_GN_BLOCKS 592            /* GroupNorm statistics-pass blocks (max) */
+#define VAE_GN_SLOTS 1024            /* GroupNorm partial slots: >= SMs and >= VAE_GN_BLOCKS */
 #define VAE_MAX_MID_PIXELS 65536     /* 2x2-unpatchified latent pixels (4 MP images) */
 
 static const int k_mult[4] = {1, 2, 4, 4};  /* iris_vae.c:1236 */
@@ -29,7 +30,8 @@ static const int k_mult[4] = {1, 2, 4, 4};  /* iris_vae.c:1236 */
 typedef struct {
     uint16_t *w;     /* bf16 [cout_pad, k] */
     float *b;        /* [cout_pad] (conv bias + shortcut bias) */
-    CUtensorMap tm;
+    CUtensorMap tm;      /* weight boxes of min(bn, 128) rows */
+    CUtensorMap tm64;    /* weight boxes of 64 rows (CTA-pair tiles of N = 128) */
     int taps0, cin0, cin1, cout, cout_pad, bn, k;
     int cin_real;    /* segment-0 channels before padding to 64 */
 } vconv_t;
@@ -54,9 +56,9 @@ typedef struct {
     uint16_t *Hb, *Xb;
     uint16_t *hA, *qk, *vT, *Pm, *O;
     float *S;
-    double *part;
-    unsigned *counter;
-    float *stats;
+    double *part;    /* GroupNorm partial sums of the last convolution (or stats pass) */
+    int gn_nparts;   /* slots in part */
+    float *ab;       /* per-channel GroupNorm affine [2 * 512] */
     float *rgb;
     uint8_t *rgb8;
     cudaGraph_t graph;
@@ -211,8 +213,9 @@ static int load_conv(iris_cuda_vae_t *v, const vsrc_t *st, const char *prefix, i
         cv->b = (float *)vae_upload(v, bias, (size_t)cout_pad * 4);
         if (!cv->w || !cv->b) rc = iris_fail(IRIS_CUDA_ERR_OOM, "VAE upload");
     }
-    if (!rc && iris_make_tmap_bf16(&cv->tm, cv->w, (uint64_t)cout_pad, (uint64_t)k, (uint64_t)k,
-                                   (uint32_t)(bn < 128 ? bn : 128)))
+    if (!rc && (iris_make_tmap_bf16(&cv->tm, cv->w, (uint64_t)cout_pad, (uint64_t)k, (uint64_t)k,
+                                    (uint32_t)(bn < 128 ? bn : 128)) ||
+                iris_make_tmap_bf16(&cv->tm64, cv->w, (uint64_t)cout_pad, (uint64_t)k, (uint64_t)k, 64)))
         rc = iris_fail(IRIS_CUDA_ERR_CUDA, "VAE weight tensor map");
     cv->taps0 = taps;
     cv->cin_real = cin;
@@ -344,7 +347,7 @@ static void plan_free(vplan_t *P) {
         cudaGraphDestroy(P->graph);
     }
     void *bufs[] = {P->lat, P->xin, P->X, P->T, P->Hb, P->Xb, P->hA, P->qk, P->vT, P->Pm, P->O,
-                    P->S, P->part, P->counter, P->stats, P->rgb, P->rgb8};
+                    P->S, P->part, P->ab, P->rgb, P->rgb8};
     for (size_t i = 0; i < sizeof(bufs) / sizeof(bufs[0]); i++) iris_dfree(bufs[i]);
     memset(P, 0, sizeof(*P));
 }
@@ -444,16 +447,14 @@ static int plan_ensure(iris_cuda_vae_t *v, int lh, int lw) {
     ALLOC(P->S, p3 * p3p * 4);
     ALLOC(P->Pm, p3 * p3p * 2);
     ALLOC(P->O, p3 * VAE_MID * 2);
-    ALLOC(P->part, (size_t)VAE_GN_BLOCKS * 64 * sizeof(double));
-    ALLOC(P->counter, 64);
-    ALLOC(P->stats, 64 * 4);
+    ALLOC(P->part, (size_t)VAE_GN_SLOTS * 64 * sizeof(double));
+    ALLOC(P->ab, 2 * VAE_MID * 4);
     ALLOC(P->rgb, 3 * p0 * 4);
     ALLOC(P->rgb8, 3 * p0);
 #undef ALLOC
     /* the attention's padding rows (pixels P3 .. P3p - 1) feed GEMM operands: zero once */
     if (!rc) rc = iris_cuda_check(cudaMemset(P->hA, 0, p3p * VAE_MID * 2), "memset");
     if (!rc) rc = iris_cuda_check(cudaMemset(P->qk, 0, p3p * 2 * VAE_MID * 2), "memset");
-    if (!rc) rc = iris_cuda_check(cudaMemset(P->counter, 0, 64), "memset");
     if (rc) { plan_free(P); return rc; }
     P->valid = 1;
     return 0;
@@ -492,15 +493,51 @@ static int pow2_at_least(int x) {
     return p;
 }
 
+/* Tile shape of a convolution launch: single CTA with N = 256 or 128, or a
+ * CTA pair (M = 256) with N = 256 or 128, whichever the wave count and the
+ * shapes' relative throughputs on B200 (tensor-pipe share reached by each
+ * shape; a single CTA at N = 128 is bound by shared-memory reads) predict to
+ * finish first.  IRIS_VAE_CONV=1cta keeps every launch on the single-CTA form. */
+static void conv_shape(IrisConvParams *p, const vconv_t *cv) {
+    static int force1 = -1;
+    if (force1 < 0) {
+        const char *e = getenv("IRIS_VAE_CONV");
+        force1 = (e && strcmp(e, "1cta") == 0) ? 1 : 0;
+    }
+    if (cv->bn < 128) return;
+    const int sms = g_rt.num_sms;
+    const int pairs = iris_conv_pairs_available() < sms / 2 ? iris_conv_pairs_available() : sms / 2;
+    const long tx = (p->W + p->bw - 1) / p->bw;
+    const long ty1 = (p->H + p->bh - 1) / p->bh, ty2 = (p->H + 2 * p->bh - 1) / (2 * p->bh);
+    struct { int pair, bn; double rate; } opt[4] = {{0, 256, 0.80}, {0, 128, 0.55}, {1, 256, 0.78}, {1, 128, 0.62}};
+    double best = 1e30;
+    for (int i = 0; i < 4; i++) {
+        if (opt[i].bn > cv->bn || cv->cout_pad % opt[i].bn) continue;
+        if (opt[i].pair && (force1 || pairs <= 0)) continue;
+        const long units = tx * (opt[i].pair ? ty2 : ty1) * (cv->cout_pad / opt[i].bn);
+        const long slots = opt[i].pair ? pairs : sms;
+        const double est = (double)((units + slots - 1) / slots) * opt[i].bn / opt[i].rate;
+        if (est < best) {
+            best = est;
+            p->pair = opt[i].pair;
+            p->bn = opt[i].bn;
+        }
+    }
+    p->tmap_b = cv->tm;          /* boxes of min(bn, 128) rows: single CTA, or pair halves of N = 256 */
+    if (p->pair) p->tmap_b_half = p->bn == 256 ? cv->tm : cv->tm64;
+}
+
 /* conv over an H x W image: segment 0 from in0 (in0_c channels), optional
  * shortcut segment from in1 (in1_c channels) */
-static void enq_conv(venq_t *E, const vconv_t *cv, const void *in0, int in0_c, const void *in1, int in1_c, int H,
-                     int W, int mode, void *out, const float *resid) {
+static void enq_conv(venq_t *E, iris_cuda_vae_t *v, const vconv_t *cv, const void *in0, int in0_c, const void *in1,
+                     int in1_c, int H, int W, int mode, void *out, const float *resid, const vgn_t *gn_next) {
+    vplan_t *P = &v->plan;
     if (E->rc) return;
     IrisConvParams p;
     memset(&p, 0, sizeof(p));
     p.bw = pow2_at_least(W) < 128 ? pow2_at_least(W) : 128;
     p.bh = 128 / p.bw;
+    while ((1 << p.bw_log2) < p.bw) p.bw_log2++;
     if (iris_make_tmap_nhwc_bf16(&p.tmap_a[0], in0, H, W, in0_c, p.bw, p.bh) ||
         (in1 && iris_make_tmap_nhwc_bf16(&p.tmap_a[1], in1, H, W, in1_c, p.bw, p.bh))) {
         E->rc = iris_fail(IRIS_CUDA_ERR_CUDA, "VAE activation tensor map");
@@ -515,47 +552,64 @@ static void enq_conv(venq_t *E, const vconv_t *cv, const void *in0, int in0_c, c
     p.cout = cv->cout;
     p.cout_pad = cv->cout_pad;
     p.bn = cv->bn;
+    conv_shape(&p, cv);
     p.mode = mode;
     p.out = out;
     p.bias = cv->b;
     p.resid = resid;
     p.status = g_rt.d_status;
+    if (gn_next) {  /* the consuming GroupNorm's partial sums come from this epilogue */
+        const int slots = iris_conv_grid(&p, g_rt.num_sms);
+        if (slots > VAE_GN_SLOTS) { E->rc = iris_fail(IRIS_CUDA_ERR_ARG, "GroupNorm slots"); return; }
+        p.gn_part = P->part;
+        p.gn_cg = cv->cout / 32;
+        P->gn_nparts = slots;
+    }
     const double pix = (double)H * W;
     const double kreal = (double)cv->taps0 * cv->cin_real + p.cin1;
     const double bytes = pix * (cv->cin_real + p.cin1) * 2 + (double)cv->cout * kreal * 2 +
                          pix * cv->cout * (mode == IRIS_CONV_BF16 ? 2 : 4) * (resid ? 2 : 1);
-    enq_done(E, iris_launch_conv(&p, g_rt.num_sms, g_rt.stream), cv->taps0 == 9 ? "conv3x3" : "conv1x1",
-             2.0 * pix * cv->cout * kreal, bytes);
+    char name[32];
+    snprintf(name, sizeof(name), "conv%s_c%d_%d", cv->taps0 == 9 ? "3x3" : "1x1", cv->cout, H);
+    enq_done(E, iris_launch_conv(&p, g_rt.num_sms, g_rt.stream), name, 2.0 * pix * cv->cout * kreal, bytes);
 }
 
-/* GroupNorm statistics of x [P, C] into P->stats, then the bf16 normalised (and SiLU) copy */
+/* GroupNorm of x [pix, C] whose partial sums are in P->part (from the
+ * convolution that wrote x, or from a statistics pass when stats != 0): the
+ * per-channel affine, then the bf16 normalised (and SiLU) copy; raw
+ * (optional) gets the plain bf16 x */
 static void enq_gn(venq_t *E, iris_cuda_vae_t *v, const float *x, long pix, int C, const vgn_t *gn, int silu,
-                   void *out) {
+                   void *out, void *raw, int stats) {
     vplan_t *P = &v->plan;
-    const long ppi = 256 / (C / 4);
-    long nb = (pix + ppi - 1) / ppi;
-    if (nb > VAE_GN_BLOCKS) nb = VAE_GN_BLOCKS;
+    if (stats && !E->rc) {
+        const long ppi = 256 / (C / 4);
+        long nb = (pix + ppi - 1) / ppi;
+        if (nb > VAE_GN_BLOCKS) nb = VAE_GN_BLOCKS;
+        enq_done(E, iris_launch_gn_stats(x, pix, C, P->part, (int)nb, g_rt.stream), "gn_stats", 0.0,
+                 (double)pix * C * 4);
+        P->gn_nparts = (int)nb;
+    }
     if (!E->rc)
-        enq_done(E, iris_launch_gn_stats(x, pix, C, P->part, (int)nb, P->counter, P->stats, v->eps, g_rt.stream),
-                 "gn_stats", 0.0, (double)pix * C * 4);
+        enq_done(E, iris_launch_gn_finalize(P->part, P->gn_nparts, C, gn->g, gn->b, v->eps, pix * (C / 32), P->ab,
+                                            g_rt.stream),
+                 "gn_finalize", 0.0, (double)P->gn_nparts * 512);
     if (!E->rc)
-        enq_done(E, iris_launch_nhwc_to_bf16(x, pix, C, 0, P->stats, gn->g, gn->b, silu, 0, out, g_rt.stream),
-                 "gn_apply", 0.0, (double)pix * C * 6);
+        enq_done(E, iris_launch_gn_affine(x, pix, C, P->ab, silu, out, raw, g_rt.stream), "gn_apply", 0.0,
+                 (double)pix * C * (raw ? 8 : 6));
 }
 
-/* resnet block on P->X (H x W, r->cin channels) -> P->X (r->cout channels) */
-static void enq_res(venq_t *E, iris_cuda_vae_t *v, const vres_t *r, int H, int W) {
+/* resnet block on P->X (H x W, r->cin channels) -> P->X (r->cout channels);
+ * gn_next: the GroupNorm that consumes the block's output (its statistics
+ * and affine come from the last convolution), or NULL */
+static void enq_res(venq_t *E, iris_cuda_vae_t *v, const vres_t *r, int H, int W, const vgn_t *gn_next) {
     vplan_t *P = &v->plan;
     const long pix = (long)H * W;
-    enq_gn(E, v, P->X, pix, r->cin, &r->n1, 1, P->Hb);
     const int skip = r->cin != r->cout;
-    if (skip && !E->rc)
-        enq_done(E, iris_launch_nhwc_to_bf16(P->X, pix, r->cin, 0, NULL, NULL, NULL, 0, 0, P->Xb, g_rt.stream),
-                 "to_bf16", 0.0, (double)pix * r->cin * 6);
-    enq_conv(E, &r->c1, P->Hb, r->cin, NULL, 0, H, W, IRIS_CONV_F32, P->T, NULL);
-    enq_gn(E, v, P->T, pix, r->cout, &r->n2, 1, P->Hb);
-    enq_conv(E, &r->c2, P->Hb, r->cout, skip ? P->Xb : NULL, r->cin, H, W, IRIS_CONV_F32, P->X,
-             skip ? NULL : P->X);
+    enq_gn(E, v, P->X, pix, r->cin, &r->n1, 1, P->Hb, skip ? P->Xb : NULL, 0);
+    enq_conv(E, v, &r->c1, P->Hb, r->cin, NULL, 0, H, W, IRIS_CONV_F32, P->T, NULL, &r->n2);
+    enq_gn(E, v, P->T, pix, r->cout, &r->n2, 1, P->Hb, NULL, 0);
+    enq_conv(E, v, &r->c2, P->Hb, r->cout, skip ? P->Xb : NULL, r->cin, H, W, IRIS_CONV_F32, P->X,
+             skip ? NULL : P->X, gn_next);
 }
 
 static void enq_gemm(venq_t *E, const void *a, int a_rows, int a_ld, const void *b, int b_rows, int b_ld, int K,
@@ -592,7 +646,7 @@ static void enq_gemm(venq_t *E, const void *a, int a_rows, int a_ld, const void 
 static void enq_attn(venq_t *E, iris_cuda_vae_t *v) {
     vplan_t *P = &v->plan;
     const int c = VAE_MID, p3 = P->H[3] * P->W[3], p3p = P->P3p;
-    enq_gn(E, v, P->X, p3, c, &v->attn_gn, 0, P->hA);
+    enq_gn(E, v, P->X, p3, c, &v->attn_gn, 0, P->hA, NULL, 0);
     /* [q | k] = h Wqk^T + b  -> bf16 [P3, 1024] */
     enq_gemm(E, P->hA, p3, c, v->w_qk, 2 * c, c, c, IRIS_EPI_BF16, P->qk, 2 * c, v->b_qk, NULL);
     /* V^T = Wv h^T -> bf16 [512, P3p] (its bias is added after P V: the rows of P sum to 1) */
@@ -614,27 +668,39 @@ static int enqueue_decode(iris_cuda_vae_t *v, venq_t *E) {
         enq_check(E, iris_launch_vae_latent_prep(P->lat, v->z, P->lh, P->lw, v->bn_mean, v->bn_std, v->scaling,
                                                  v->shift, v->pq_w, v->pq_b, P->xin, g_rt.stream),
                   "latent prep");
-    enq_conv(E, &v->conv_in, P->xin, 64, NULL, 0, P->H[3], P->W[3], IRIS_CONV_F32, P->X, NULL);
-    enq_res(E, v, &v->mid[0], P->H[3], P->W[3]);
+    enq_conv(E, v, &v->conv_in, P->xin, 64, NULL, 0, P->H[3], P->W[3], IRIS_CONV_F32, P->X, NULL, &v->mid[0].n1);
+    enq_res(E, v, &v->mid[0], P->H[3], P->W[3], &v->attn_gn);
     enq_attn(E, v);
-    enq_res(E, v, &v->mid[1], P->H[3], P->W[3]);
+    /* the attention's output projection (a GEMM) sums no GroupNorm statistics */
+    const int p3 = P->H[3] * P->W[3];
+    enq_gn(E, v, P->X, p3, VAE_MID, &v->mid[1].n1, 1, P->Hb, NULL, 1);
+    {
+        const vres_t *r = &v->mid[1];
+        enq_conv(E, v, &r->c1, P->Hb, r->cin, NULL, 0, P->H[3], P->W[3], IRIS_CONV_F32, P->T, NULL, &r->n2);
+        enq_gn(E, v, P->T, p3, r->cout, &r->n2, 1, P->Hb, NULL, 0);
+        enq_conv(E, v, &r->c2, P->Hb, r->cout, NULL, 0, P->H[3], P->W[3], IRIS_CONV_F32, P->X, P->X, &v->up[0].n1);
+    }
     int bi = 0;
     for (int level = 3; level >= 0; level--) {
         const int ch = VAE_BASE * k_mult[level];
-        for (int r = 0; r < 3; r++) enq_res(E, v, &v->up[bi++], P->H[level], P->W[level]);
+        for (int r = 0; r < 3; r++, bi++) {
+            /* consumer of the block's output: the next block's norm1, nothing
+             * before an upsample, the output norm after the last block */
+            const vgn_t *next = r < 2 ? &v->up[bi + 1].n1 : level == 0 ? &v->out_gn : NULL;
+            enq_res(E, v, &v->up[bi], P->H[level], P->W[level], next);
+        }
         if (level > 0) {
             const long pix = (long)P->H[level] * P->W[level];
             if (!E->rc)
-                enq_done(E, iris_launch_nhwc_to_bf16(P->X, pix, ch, P->W[level], NULL, NULL, NULL, 0, 1, P->Hb,
-                                                     g_rt.stream),
-                         "upsample", 0.0, (double)pix * ch * 12);
-            enq_conv(E, &v->upc[3 - level], P->Hb, ch, NULL, 0, P->H[level - 1], P->W[level - 1], IRIS_CONV_F32,
-                     P->X, NULL);
+                enq_done(E, iris_launch_nhwc_to_bf16(P->X, pix, ch, P->W[level], 1, P->Hb, g_rt.stream), "upsample",
+                         0.0, (double)pix * ch * 12);
+            enq_conv(E, v, &v->upc[3 - level], P->Hb, ch, NULL, 0, P->H[level - 1], P->W[level - 1], IRIS_CONV_F32,
+                     P->X, NULL, &v->up[bi].n1);
         }
     }
     const long p0 = (long)P->H[0] * P->W[0];
-    enq_gn(E, v, P->X, p0, VAE_BASE, &v->out_gn, 1, P->Hb);
-    enq_conv(E, &v->conv_out, P->Hb, VAE_BASE, NULL, 0, P->H[0], P->W[0], IRIS_CONV_F32_NCHW, P->rgb, NULL);
+    enq_gn(E, v, P->X, p0, VAE_BASE, &v->out_gn, 1, P->Hb, NULL, 0);
+    enq_conv(E, v, &v->conv_out, P->Hb, VAE_BASE, NULL, 0, P->H[0], P->W[0], IRIS_CONV_F32_NCHW, P->rgb, NULL, NULL);
     if (!E->rc) enq_check(E, iris_launch_vae_rgb8(P->rgb, p0, P->rgb8, g_rt.stream), "rgb8");
     return E->rc;
 }

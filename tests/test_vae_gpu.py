@@ -129,6 +129,7 @@ def test_random_init_decoder_is_finite_and_profiles(iris):
     assert img.shape == (64, 64, 3)
     prof = v.profile()
     names = {e["name"] for e in prof}
-    assert {"conv3x3", "gn_stats", "gn_apply", "attn_gemm", "attn_softmax", "upsample"} <= names
+    assert {"gn_stats", "gn_finalize", "gn_apply", "attn_gemm", "attn_softmax", "upsample"} <= names
+    assert any(n.startswith("conv3x3_c512") for n in names)
     assert len(prof) == v.graph_kernels()
     v.close()
