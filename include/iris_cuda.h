@@ -12,7 +12,8 @@
  *                         (iris_metal.h:23-33, :309)
  *   2. model + sampler    iris_transformer_* (iris_transformer_flux.c:3939, :4579,
  *                         :5300), zi_transformer_* (iris_transformer_zimage.c:1696,
- *                         :2164), iris_sample_* (iris_sample.c:171-1188)
+ *                         :2164), iris_sample_* (iris_sample.c:171-1188), and the
+ *                         autoencoder decoder iris_vae_decode (iris_vae.c:835)
  *   3. tensor/op surface  the iris_gpu_* device-resident API of iris_metal.h
  *                         (:155-600), same names and signatures, so the
  *                         reference's bf16 block code can link against it.
