@@ -152,7 +152,9 @@ __device__ __forceinline__ float sum_f32x2(uint64_t v) {
 // lazy reference max; at the end O_t / l -> bf16 rows [row0, row0 + 128).
 // kPair: the P-ready barrier lives in the even CTA of a pair (one arrival per
 // warp through its cluster address), otherwise in this CTA (128 arrivals).
-template <bool kPair>
+// kMasked: a key mask exists (a separate instantiation, so the unmasked
+// softmax carries no mask test).
+template <bool kPair, bool kMasked>
 __device__ __forceinline__ void softmax_role(const AttnParams& p, uint32_t tmem, int t, int warp, int lane,
                                              uint64_t* s_full, uint64_t* p_full, uint32_t p_full_cluster,
                                              uint64_t* o_done, volatile int* abort_flag, int row0, int col0,
@@ -169,7 +171,7 @@ __device__ __forceinline__ void softmax_role(const AttnParams& p, uint32_t tmem,
   auto logit = [&](float sv, int key, bool full) -> float {
     if (full) return sv * p.scale_log2;
     if (key >= p.sk) return -INFINITY;
-    if (p.kmask && !p.kmask[key]) return -1e9f * LOG2E;
+    if (kMasked && !p.kmask[key]) return -1e9f * LOG2E;
     return sv * p.scale_log2;
   };
   // exponentials of 64 keys (half h of the tile) against reference max -nm
@@ -211,7 +213,7 @@ __device__ __forceinline__ void softmax_role(const AttnParams& p, uint32_t tmem,
     iris::tc_fence_after();
     const int kbase = j * BKV;
     bool full = kbase + BKV <= p.sk;
-    if (full && p.kmask) {  // a masked sequence: tiles without padding keys still take the fast path
+    if (kMasked && full) {  // a masked sequence: tiles without padding keys still take the fast path
       const uint32_t m4 = reinterpret_cast<const uint32_t*>(p.kmask + kbase)[lane];
       full = __all_sync(0xffffffffu, m4 == 0x01010101u);
     }
@@ -303,6 +305,7 @@ __device__ __forceinline__ void softmax_role(const AttnParams& p, uint32_t tmem,
   }
 }
 
+template <bool kMasked>
 __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -471,7 +474,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
   } else if (warp >= 2 && (warp < 6 || has1)) {
     // ------------------------------------------------------------ softmax + epilogue
     const int t = warp >= 6 ? 1 : 0;  // query tile
-    softmax_role<false>(p, tmem, t, warp, lane, &bars->s_full[t], &bars->p_full[t], 0u, &bars->o_done, abort_flag,
+    softmax_role<false, kMasked>(p, tmem, t, warp, lane, &bars->s_full[t], &bars->p_full[t], 0u, &bars->o_done, abort_flag,
                         q0 + t * BQ, col0, n);
   }
 
@@ -512,6 +515,7 @@ struct PairBars {
   int abort;
 };
 
+template <bool kMasked>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
 attn_pair_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -674,7 +678,7 @@ attn_pair_kernel(const __grid_constant__ AttnParams p) {
   } else if (warp >= 2) {
     // ------------------------------------------------------------ softmax + epilogue (both CTAs)
     const int t = warp >= 6 ? 1 : 0;
-    softmax_role<true>(p, tmem, t, warp, lane, &bars->s_full[t], nullptr, iris::mapa_shared(&bars->p_full[t], 0),
+    softmax_role<true, kMasked>(p, tmem, t, warp, lane, &bars->s_full[t], nullptr, iris::mapa_shared(&bars->p_full[t], 0),
                        &bars->o_done, abort_flag, q0 + t * BQ, col0, n);
   }
 
@@ -694,9 +698,13 @@ extern "C" void iris_attention_set_status(int* status) { g_attn_status = status;
 
 extern "C" cudaError_t iris_attention_tc_init(void) {
   if (g_attn_tc_attr) return cudaSuccess;
-  cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  cudaError_t e = cudaFuncSetAttribute(attn_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(attn_pair_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES);
+    e = cudaFuncSetAttribute(attn_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attn_pair_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attn_pair_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES);
   if (e == cudaSuccess) g_attn_tc_attr = true;
   return e;
 }
@@ -731,10 +739,12 @@ extern "C" cudaError_t iris_launch_attention_tc(const void* q, int ldq, const vo
   p.status = g_attn_status;
   if (single) {
     dim3 grid((sq + 2 * BQ - 1) / (2 * BQ), heads);
-    attn_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(p);
+    if (key_mask) attn_tc_kernel<true><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(p);
+    else attn_tc_kernel<false><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(p);
   } else {
     dim3 grid(2 * ((sq + 4 * BQ - 1) / (4 * BQ)), heads);
-    attn_pair_kernel<<<grid, NUM_THREADS, P_SMEM_BYTES, stream>>>(p);
+    if (key_mask) attn_pair_kernel<true><<<grid, NUM_THREADS, P_SMEM_BYTES, stream>>>(p);
+    else attn_pair_kernel<false><<<grid, NUM_THREADS, P_SMEM_BYTES, stream>>>(p);
   }
   return cudaGetLastError();
 }

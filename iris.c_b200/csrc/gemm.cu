@@ -31,7 +31,9 @@ constexpr int STAGES = 4;
 constexpr int A_BYTES = BM * BK * 2;        // 16 KB
 constexpr int B_BYTES_MAX = 256 * BK * 2;   // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES_MAX;
-constexpr int NUM_THREADS = 192;
+constexpr int NUM_THREADS = 192;          // single-CTA kernel: producer, MMA, 4 epilogue warps
+constexpr int EPI_WARPS2 = 8;             // CTA-pair kernel: two epilogue warps per TMEM lane quarter
+constexpr int NUM_THREADS2 = 64 + 32 * EPI_WARPS2;
 constexpr int TMEM_COLS = 512;
 // f32 epilogue staging: 32 rows x (32 + 4) floats per epilogue warp, so that
 // 16-byte shared accesses run in conflict-free 8-lane phases
@@ -143,12 +145,12 @@ __device__ __forceinline__ void epi_qkv_chunk(const IrisGemmParams& p, uint32_t 
 
 // Epilogue for a 256-column tile laid out as [gate 128 | up 128].
 __device__ __forceinline__ void epi_swiglu_tile(const IrisGemmParams& p, uint32_t taddr, int row,
-                                                bool valid, int n0) {
+                                                bool valid, int n0, int j0 = 0, int j1 = 4) {
   int f0 = (n0 - p.swiglu_base) >> 1;
   __nv_bfloat16* dst =
       reinterpret_cast<__nv_bfloat16*>(p.mlp_out) + (size_t)row * p.ld_mlp + p.mlp_col0 + f0;
 #pragma unroll 1
-  for (int j = 0; j < 4; j++) {
+  for (int j = j0; j < j1; j++) {
     float gv[32], uv[32];
     iris::tmem_ld32(taddr + 32 * j, gv);
     iris::tmem_ld32(taddr + 128 + 32 * j, uv);
@@ -223,9 +225,9 @@ __device__ __forceinline__ void epi_f32_block(const IrisGemmParams& p, int g, fl
 
 __device__ __forceinline__ void epi_plain_chunk(const IrisGemmParams& p, uint32_t taddr, int g,
                                                 int row, int row_local, bool valid, int col0, float* stage,
-                                                int lane, int rows_valid, int split) {
+                                                int lane, int rows_valid, int split, int j0 = 0, int j1 = 4) {
 #pragma unroll 1
-  for (int j = 0; j < 4; j++) {
+  for (int j = j0; j < j1; j++) {
     float v[32];
     iris::tmem_ld32(taddr + 32 * j, v);
     int c = col0 + 32 * j;
@@ -304,21 +306,33 @@ __device__ __forceinline__ void prefetch_resid_row(const IrisGemmParams& p, int 
 }
 
 // Epilogue of one accumulator tile for this thread's row (all modes); the
-// warp's 32 rows start at row - lane, rows_valid of them are real.
+// warp's 32 rows start at row - lane, rows_valid of them are real.  With two
+// epilogue warps per lane quarter (halves = 2), warp `half` takes the
+// 128-column chunk `half` of a 256-wide tile, or half of the 32-column blocks
+// of a 128-wide one (a Q/K head's RMSNorm needs its whole chunk in one warp).
 __device__ __forceinline__ void epi_tile(const IrisGemmParams& p, uint32_t taddr, int g, int row, int row_local,
                                          bool valid, int n0, float* stage, int lane, int rows_valid,
-                                         int split = 0) {
+                                         int split = 0, int half = 0, int halves = 1) {
   bool swiglu_tile = (p.mode == IRIS_EPI_SWIGLU) || (p.mode == IRIS_EPI_SINGLE && n0 >= p.swiglu_base);
   if (swiglu_tile) {
-    epi_swiglu_tile(p, taddr, row, valid, n0);
+    if (halves == 2) epi_swiglu_tile(p, taddr, row, valid, n0, 2 * half, 2 * half + 2);
+    else epi_swiglu_tile(p, taddr, row, valid, n0);
   } else {
-    for (int c = 0; c < p.bn / 128; c++) {
+    const int nchunks = p.bn / 128;
+    for (int c = 0; c < nchunks; c++) {
       int col0 = n0 + c * 128;
       if (col0 >= p.N) break;
-      if (p.mode == IRIS_EPI_QKV || p.mode == IRIS_EPI_SINGLE)
+      const bool qkv = p.mode == IRIS_EPI_QKV || p.mode == IRIS_EPI_SINGLE;
+      if (halves == 2 && nchunks == 2 && c != half) continue;
+      if (qkv) {
+        if (halves == 2 && nchunks == 1 && half) continue;
         epi_qkv_chunk(p, taddr + c * 128, g, row, valid, col0);
-      else
+      } else if (halves == 2 && nchunks == 1) {
+        epi_plain_chunk(p, taddr + c * 128, g, row, row_local, valid, col0, stage, lane, rows_valid, split,
+                        2 * half, 2 * half + 2);
+      } else {
         epi_plain_chunk(p, taddr + c * 128, g, row, row_local, valid, col0, stage, lane, rows_valid, split);
+      }
     }
   }
 }
@@ -503,9 +517,9 @@ gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
 // CTA's TMEM holds the accumulator of its own 128 rows; both epilogues run as
 // in the single-CTA kernel.
 constexpr int BM2 = 256;
-constexpr int STAGES2 = 6;
+constexpr int STAGES2 = 5;
 constexpr int STAGE2_BYTES = A_BYTES + 128 * BK * 2;  // 32 KB
-constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + EPI_BYTES + 1024;
+constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + EPI_WARPS2 * EPI_WARP_BYTES + 1024;
 
 struct Bars2 {
   uint64_t full[STAGES2];   // even CTA: both CTAs' tiles of the stage landed (2 arrivals + bytes)
@@ -517,7 +531,7 @@ struct Bars2 {
   int abort;
 };
 
-__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS2, 1)
 gemm_tc2_kernel(const __grid_constant__ IrisGemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -544,7 +558,7 @@ gemm_tc2_kernel(const __grid_constant__ IrisGemmParams p) {
     }
     for (int b = 0; b < 2; b++) {
       iris::mbar_init(&bars->tfull[b], 1);
-      iris::mbar_init(&bars->tempty[b], 8);
+      iris::mbar_init(&bars->tempty[b], 2 * EPI_WARPS2);
     }
     iris::mbar_init(&bars->drain, 1);
     bars->abort = 0;
@@ -636,13 +650,15 @@ gemm_tc2_kernel(const __grid_constant__ IrisGemmParams p) {
       iris::mbar_wait(&bars->drain, 0, &no_abort, p.status, IRIS_DEV_ERR_GEMM_DRAIN);
     }
   } else if (warp >= 2) {
-    // ------------------------------------------------ epilogue (both CTAs)
+    // ------------------------------------------------ epilogue (both CTAs, 8 warps)
+    const int ew = warp - 2;
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    float* stage = reinterpret_cast<float*>(smem + STAGES2 * STAGE2_BYTES + 1024 + (warp - 2) * EPI_WARP_BYTES);
+    const int half = ew >> 2;      // which half of the tile's columns
+    float* stage = reinterpret_cast<float*>(smem + STAGES2 * STAGE2_BYTES + 1024 + ew * EPI_WARP_BYTES);
     const uint32_t tempty_c0 = iris::mapa_shared(&bars->tempty[0], 0);
     const uint32_t tempty_c1 = iris::mapa_shared(&bars->tempty[1], 0);
     int it = 0;
-    if (pair < total) {
+    if (pair < total && half == 0) {
       int g, ml, n0;
       tile_coords(p, pair, mt0, mtot, g, ml, n0);
       prefetch_resid_row(p, g, ml * BM2 + 128 * (int)rank + quarter * 32 + lane, n0);
@@ -650,7 +666,7 @@ gemm_tc2_kernel(const __grid_constant__ IrisGemmParams p) {
     for (int t = pair; t < total; t += npairs, it++) {
       int buf = it & 1;
       uint32_t use = (uint32_t)(it >> 1);
-      if (t + npairs < total) {
+      if (t + npairs < total && half == 0) {
         int g2, ml2, n02;
         tile_coords(p, t + npairs, mt0, mtot, g2, ml2, n02);
         prefetch_resid_row(p, g2, ml2 * BM2 + 128 * (int)rank + quarter * 32 + lane, n02);
@@ -664,14 +680,14 @@ gemm_tc2_kernel(const __grid_constant__ IrisGemmParams p) {
       int row = p.row0[g] + row_local;
       uint32_t taddr = tmem_base + buf * 256 + ((uint32_t)(quarter * 32) << 16);
       const int rows_valid = min(32, max(0, p.rows[g] - (row_local - lane)));
-      epi_tile(p, taddr, g, row, row_local, valid, n0, stage, lane, rows_valid);
+      epi_tile(p, taddr, g, row, row_local, valid, n0, stage, lane, rows_valid, 0, half, 2);
       iris::tc_fence_before();
       __syncwarp();
       if (lane == 0) iris::mbar_arrive_cluster(buf ? tempty_c1 : tempty_c0);
     }
     if (p.mode == IRIS_EPI_TP_SCATTER) {
-      asm volatile("bar.sync 1, 128;" ::: "memory");  // the 4 epilogue warps' stores are issued
-      if (warp == 2 && lane == 0) iris::tp_signal(p.tp, IRIS_TP_DONE_GEMM, IRIS_TP_PART, gridDim.x);
+      asm volatile("bar.sync 1, %0;" ::"r"(32 * EPI_WARPS2) : "memory");  // every epilogue warp's stores are issued
+      if (ew == 0 && lane == 0) iris::tp_signal(p.tp, IRIS_TP_DONE_GEMM, IRIS_TP_PART, gridDim.x);
     }
   }
 
@@ -776,7 +792,7 @@ extern "C" cudaError_t iris_gemm_init(void) {
     cudaLaunchConfig_t cfg;
     memset(&cfg, 0, sizeof(cfg));
     cfg.gridDim = dim3(2 * (sms / 2), 1, 1);
-    cfg.blockDim = dim3(NUM_THREADS, 1, 1);
+    cfg.blockDim = dim3(NUM_THREADS2, 1, 1);
     cfg.dynamicSmemBytes = SMEM2_BYTES;
     int n = 0;
     e = cudaOccupancyMaxActiveClusters(&n, gemm_tc2_kernel, &cfg);
@@ -812,7 +828,7 @@ extern "C" cudaError_t iris_launch_gemm_ex(const IrisGemmParams* p, int num_sms,
     long total = (long)mt * ((p->N + 255) / 256);
     long cap = g_max_pairs < num_sms / 2 ? g_max_pairs : num_sms / 2;
     long pairs = total < cap ? total : cap;
-    gemm_tc2_kernel<<<(int)(2 * pairs), NUM_THREADS, SMEM2_BYTES, stream>>>(*p);
+    gemm_tc2_kernel<<<(int)(2 * pairs), NUM_THREADS2, SMEM2_BYTES, stream>>>(*p);
     return cudaGetLastError();
   }
   int mt = (p->rows[0] + BM - 1) / BM + (p->ngroups > 1 ? (p->rows[1] + BM - 1) / BM : 0);
