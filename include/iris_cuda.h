@@ -286,6 +286,52 @@ int iris_cuda_sample_euler_zimage_dev(iris_cuda_zimage_t *z, float *d_z, int h, 
                                       const float *d_cap, int cap_seq, const float *schedule,
                                       int num_steps);
 
+/* ------------------------------------------------------------------ 2e. text encoder (Qwen3)
+ * The step before the denoising loop: token ids -> text embeddings.  The
+ * tokenizer (qwen3_tokenize_chat / qwen3_pad_tokens, iris_qwen3.h) stays on
+ * the host; this layer replaces the model half of iris_qwen3.c. */
+typedef struct iris_cuda_qwen3 iris_cuda_qwen3_t;
+
+typedef struct {
+    int hidden;          /* hidden_size (2560 for Qwen3-4B)         */
+    int intermediate;    /* intermediate_size (9728)                */
+    int heads;           /* num_attention_heads (32)                */
+    int kv_heads;        /* num_key_value_heads (8)                 */
+    int head_dim;        /* must be 128                             */
+    int vocab;           /* vocab_size (151936)                     */
+    int layers;          /* num_hidden_layers (36)                  */
+    float rope_theta;    /* 1e6                                     */
+} iris_cuda_qwen3_config_t;
+
+/* Replaces qwen3_model_load (iris_qwen3.c:1578): model_dir is the
+ * text_encoder directory (config.json, model.safetensors.index.json and
+ * shards); weights resident in HBM as bf16 (the layers up to the last one
+ * either extraction mode reads). */
+iris_cuda_qwen3_t *iris_cuda_qwen3_load(const char *model_dir);
+/* Random-init encoder (device RNG; projections N(0, 1/fan_in), norm scales
+ * 1 + N(0, 0.1), embeddings N(0, 1)); no reference counterpart. */
+iris_cuda_qwen3_t *iris_cuda_qwen3_random(const iris_cuda_qwen3_config_t *cfg, uint64_t seed);
+/* Replaces qwen3_model_free (iris_qwen3.c:1754). */
+void iris_cuda_qwen3_free(iris_cuda_qwen3_t *m);
+int iris_cuda_qwen3_get_config(const iris_cuda_qwen3_t *m, iris_cuda_qwen3_config_t *out);
+size_t iris_cuda_qwen3_weight_bytes(const iris_cuda_qwen3_t *m);
+/* Replaces qwen3_set_extraction_mode (iris_qwen3.c:1849): 0 Flux (hidden
+ * states after layers 8, 17, 26 concatenated, text_dim 3 * hidden), 1 Z-Image
+ * (after layer num_layers - 2, text_dim hidden). */
+int iris_cuda_qwen3_set_extraction_mode(iris_cuda_qwen3_t *m, int mode);
+int iris_cuda_qwen3_text_dim(const iris_cuda_qwen3_t *m);
+/* Replaces qwen3_forward (iris_qwen3.c:1072): input_ids / attention_mask
+ * [seq_len] host int arrays (mask 1 = real token; NULL = all real), seq_len
+ * <= 512; causal attention with masked keys at -1e9 as the reference.
+ * Returns malloc'd f32 [seq_len, text_dim] or NULL. */
+float *iris_cuda_qwen3_forward(iris_cuda_qwen3_t *m, const int *input_ids, const int *attention_mask, int seq_len);
+/* Same with the embeddings written to device memory d_out [seq_len, text_dim]
+ * (queued on the library stream; feeds iris_cuda_sample_euler_dev directly). */
+int iris_cuda_qwen3_forward_dev(iris_cuda_qwen3_t *m, const int *input_ids, const int *attention_mask, int seq_len,
+                                float *d_out);
+/* kernels in one captured forward (0 before the first) */
+uint64_t iris_cuda_qwen3_graph_kernels(const iris_cuda_qwen3_t *m);
+
 /* ------------------------------------------------------------------ 2d. autoencoder decoder
  * The step after the denoising loop: latent -> RGB image on the GPU.  The
  * decoder of AutoencoderKLFlux2 (32 latent channels, batch-norm latent

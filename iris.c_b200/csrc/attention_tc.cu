@@ -90,6 +90,8 @@ struct AttnParams {
   int sq, sk;
   float scale_log2;
   const uint8_t* kmask;
+  int causal;     // key j of query row i masked when j > i (masked instantiation only)
+  int kv_group;   // query heads per key/value head (grouped-query attention)
   int* status;
 };
 
@@ -168,10 +170,12 @@ __device__ __forceinline__ void softmax_role(const AttnParams& p, uint32_t tmem,
   bool ok = true;
   // S row -> scaled logits (log2 units): padding keys -inf, masked keys
   // -1e9 (in natural-log units, as the reference's masked softmax)
+  const int qrow = row0 + r;
   auto logit = [&](float sv, int key, bool full) -> float {
     if (full) return sv * p.scale_log2;
     if (key >= p.sk) return -INFINITY;
-    if (kMasked && !p.kmask[key]) return -1e9f * LOG2E;
+    if (kMasked && p.kmask && !p.kmask[key]) return -1e9f * LOG2E;
+    if (kMasked && p.causal && key > qrow) return -1e9f * LOG2E;
     return sv * p.scale_log2;
   };
   // exponentials of 64 keys (half h of the tile) against reference max -nm
@@ -213,7 +217,9 @@ __device__ __forceinline__ void softmax_role(const AttnParams& p, uint32_t tmem,
     iris::tc_fence_after();
     const int kbase = j * BKV;
     bool full = kbase + BKV <= p.sk;
-    if (kMasked && full) {  // a masked sequence: tiles without padding keys still take the fast path
+    // causal: a key tile reaching past the tile's first query row is masked per element
+    if (kMasked && p.causal && kbase + BKV - 1 > row0) full = false;
+    if (kMasked && full && p.kmask) {  // a masked sequence: tiles without padding keys still take the fast path
       const uint32_t m4 = reinterpret_cast<const uint32_t*>(p.kmask + kbase)[lane];
       full = __all_sync(0xffffffffu, m4 == 0x01010101u);
     }
@@ -317,6 +323,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
   const int q0 = blockIdx.x * (2 * BQ);
   const bool has1 = q0 + BQ < p.sq;  // second query tile holds rows
   const int col0 = head * HD;
+  const int kvcol0 = (head / p.kv_group) * HD;
   const int n = (p.sk + BKV - 1) / BKV;
 
   if (threadIdx.x == 0) {
@@ -366,8 +373,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
       if (!iris::mbar_wait(&bars->k_empty[s], (u & 1) ^ 1, abort_flag, p.status, IRIS_DEV_ERR_ATTN_PRODUCER))
         return false;
       iris::mbar_arrive_expect_tx(&bars->k_full[s], TILE);
-      iris::tma_load_2d(smem + OFF_K + s * TILE, &p.tk, &bars->k_full[s], col0, nk * BKV);
-      iris::tma_load_2d(smem + OFF_K + s * TILE + BOX, &p.tk, &bars->k_full[s], col0 + 64, nk * BKV);
+      iris::tma_load_2d(smem + OFF_K + s * TILE, &p.tk, &bars->k_full[s], kvcol0, nk * BKV);
+      iris::tma_load_2d(smem + OFF_K + s * TILE + BOX, &p.tk, &bars->k_full[s], kvcol0 + 64, nk * BKV);
       nk++;
       return true;
     };
@@ -377,8 +384,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
       if (!iris::mbar_wait(&bars->v_empty[s], (u & 1) ^ 1, abort_flag, p.status, IRIS_DEV_ERR_ATTN_PRODUCER))
         return false;
       iris::mbar_arrive_expect_tx(&bars->v_full[s], TILE);
-      iris::tma_load_2d(smem + OFF_V + s * TILE, &p.tv, &bars->v_full[s], col0, nv * BKV);
-      iris::tma_load_2d(smem + OFF_V + s * TILE + BOX, &p.tv, &bars->v_full[s], col0 + 64, nv * BKV);
+      iris::tma_load_2d(smem + OFF_V + s * TILE, &p.tv, &bars->v_full[s], kvcol0, nv * BKV);
+      iris::tma_load_2d(smem + OFF_V + s * TILE + BOX, &p.tv, &bars->v_full[s], kvcol0 + 64, nv * BKV);
       nv++;
       return true;
     };
@@ -528,6 +535,7 @@ attn_pair_kernel(const __grid_constant__ AttnParams p) {
   const uint32_t rank = iris::cluster_ctarank();
   const int q0 = (blockIdx.x >> 1) * (4 * BQ) + (int)rank * (2 * BQ);  // this CTA's two query tiles
   const int col0 = head * HD;
+  const int kvcol0 = (head / p.kv_group) * HD;
   const int n = (p.sk + BKV - 1) / BKV;
 
   if (threadIdx.x == 0) {
@@ -577,8 +585,8 @@ attn_pair_kernel(const __grid_constant__ AttnParams p) {
       const uint32_t kf = iris::mapa_shared(&bars->k_full[s], 0);
       iris::mbar_arrive_expect_tx_cluster(kf, HALF);
       const int krow = nk * BKV + 64 * (int)rank;
-      iris::tma_load_2d_pair(smem + P_OFF_K + s * HALF, &p.tk, kf, col0, krow);
-      iris::tma_load_2d_pair(smem + P_OFF_K + s * HALF + HALF / 2, &p.tk, kf, col0 + 64, krow);
+      iris::tma_load_2d_pair(smem + P_OFF_K + s * HALF, &p.tk, kf, kvcol0, krow);
+      iris::tma_load_2d_pair(smem + P_OFF_K + s * HALF + HALF / 2, &p.tk, kf, kvcol0 + 64, krow);
       nk++;
       return true;
     };
@@ -589,7 +597,7 @@ attn_pair_kernel(const __grid_constant__ AttnParams p) {
         return false;
       const uint32_t vf = iris::mapa_shared(&bars->v_full[s], 0);
       iris::mbar_arrive_expect_tx_cluster(vf, HALF);
-      iris::tma_load_2d_pair(smem + P_OFF_V + s * HALF, &p.tv, vf, col0 + 64 * (int)rank, nv * BKV);
+      iris::tma_load_2d_pair(smem + P_OFF_V + s * HALF, &p.tv, vf, kvcol0 + 64 * (int)rank, nv * BKV);
       nv++;
       return true;
     };
@@ -712,7 +720,15 @@ extern "C" cudaError_t iris_attention_tc_init(void) {
 extern "C" cudaError_t iris_launch_attention_tc(const void* q, int ldq, const void* k, const void* v, int ldk,
                                                 void* o, int ldo, int sq, int sk, int heads, float scale,
                                                 const uint8_t* key_mask, cudaStream_t stream) {
+  return iris_launch_attention_gqa(q, ldq, k, v, ldk, o, ldo, sq, sk, heads, 1, 0, scale, key_mask, stream);
+}
+
+extern "C" cudaError_t iris_launch_attention_gqa(const void* q, int ldq, const void* k, const void* v, int ldk,
+                                                 void* o, int ldo, int sq, int sk, int heads, int kv_group,
+                                                 int causal, float scale, const uint8_t* key_mask,
+                                                 cudaStream_t stream) {
   if (sq <= 0 || sk <= 0 || heads <= 0) return cudaSuccess;
+  if (kv_group < 1 || heads % kv_group) return cudaErrorInvalidValue;
   if ((ldq | ldk | ldo) & 7) return cudaErrorInvalidValue;
   if (!g_attn_tc_attr) {
     cudaError_t e = iris_attention_tc_init();
@@ -727,8 +743,9 @@ extern "C" cudaError_t iris_launch_attention_tc(const void* q, int ldq, const vo
   memset(&p, 0, sizeof(p));
   // the pair kernel loads 64-key halves of each key tile
   if (iris_make_tmap_bf16(&p.tq, q, (uint64_t)sq, (uint64_t)heads * HD, (uint64_t)ldq, BQ) ||
-      iris_make_tmap_bf16(&p.tk, k, (uint64_t)sk, (uint64_t)heads * HD, (uint64_t)ldk, single ? BKV : 64) ||
-      iris_make_tmap_bf16(&p.tv, v, (uint64_t)sk, (uint64_t)heads * HD, (uint64_t)ldk, BKV))
+      iris_make_tmap_bf16(&p.tk, k, (uint64_t)sk, (uint64_t)(heads / kv_group) * HD, (uint64_t)ldk,
+                          single ? BKV : 64) ||
+      iris_make_tmap_bf16(&p.tv, v, (uint64_t)sk, (uint64_t)(heads / kv_group) * HD, (uint64_t)ldk, BKV))
     return cudaErrorInvalidValue;
   p.o = static_cast<__nv_bfloat16*>(o);
   p.ldo = ldo;
@@ -736,14 +753,17 @@ extern "C" cudaError_t iris_launch_attention_tc(const void* q, int ldq, const vo
   p.sk = sk;
   p.scale_log2 = scale * LOG2E;
   p.kmask = key_mask;
+  p.causal = causal;
+  p.kv_group = kv_group;
   p.status = g_attn_status;
+  const bool masked = key_mask != nullptr || causal;
   if (single) {
     dim3 grid((sq + 2 * BQ - 1) / (2 * BQ), heads);
-    if (key_mask) attn_tc_kernel<true><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(p);
+    if (masked) attn_tc_kernel<true><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(p);
     else attn_tc_kernel<false><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(p);
   } else {
     dim3 grid(2 * ((sq + 4 * BQ - 1) / (4 * BQ)), heads);
-    if (key_mask) attn_pair_kernel<true><<<grid, NUM_THREADS, P_SMEM_BYTES, stream>>>(p);
+    if (masked) attn_pair_kernel<true><<<grid, NUM_THREADS, P_SMEM_BYTES, stream>>>(p);
     else attn_pair_kernel<false><<<grid, NUM_THREADS, P_SMEM_BYTES, stream>>>(p);
   }
   return cudaGetLastError();

@@ -240,14 +240,14 @@ int iris_comm_sym_init(size_t bytes) {
     sym_release();
     if ((rc = iris_cuda_check(cudaMalloc((void **)&g_sym.local, bytes), "symmetric arena"))) return rc;
     g_sym.bytes = bytes;
-    if ((rc = iris_cuda_check(cudaMemset(g_sym.local, 0, bytes), "symmetric arena"))) return rc;
+    if ((rc = iris_cuda_check(cudaMemsetAsync(g_sym.local, 0, bytes, g_rt.stream), "symmetric arena"))) return rc;
     cudaIpcMemHandle_t h;
     if ((rc = iris_cuda_check(cudaIpcGetMemHandle(&h, g_sym.local), "ipc handle"))) return rc;
     const size_t hb = sizeof(cudaIpcMemHandle_t);
     uint8_t *d = NULL;
     uint8_t all[IRIS_COMM_MAX_PEERS * sizeof(cudaIpcMemHandle_t)];
     if ((rc = iris_cuda_check(cudaMalloc((void **)&d, hb * g_comm.world), "handle exchange"))) return rc;
-    rc = iris_cuda_check(cudaMemcpy(d + hb * g_comm.rank, &h, hb, cudaMemcpyHostToDevice), "handle exchange");
+    rc = iris_h2d(d + hb * g_comm.rank, &h, hb);
     if (!rc) {
         ncclResult_t r = g_nccl.all_gather(d + hb * g_comm.rank, d, hb, ncclUint8, g_comm.comm, g_rt.stream);
         if (r != ncclSuccess && r != ncclInProgress) rc = iris_fail(IRIS_CUDA_ERR_CUDA, "handle all-gather: %s", g_nccl.error_string(r));

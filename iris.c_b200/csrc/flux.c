@@ -557,8 +557,7 @@ static int plan_ensure(iris_cuda_flux_t *tf, int s_txt, int img_h, int img_w,
         float *cs = (float *)malloc((size_t)S * 64 * 4), *sn = (float *)malloc((size_t)S * 64 * 4);
         if (!cs || !sn) { free(cs); free(sn); goto oom; }
         fill_rope(tf, P, cs, sn);
-        int rc = iris_cuda_check(cudaMemcpy(P->rope_cos, cs, (size_t)S * 64 * 4, cudaMemcpyHostToDevice), "rope") ||
-                 iris_cuda_check(cudaMemcpy(P->rope_sin, sn, (size_t)S * 64 * 4, cudaMemcpyHostToDevice), "rope");
+        int rc = iris_h2d(P->rope_cos, cs, (size_t)S * 64 * 4) || iris_h2d(P->rope_sin, sn, (size_t)S * 64 * 4);
         free(cs);
         free(sn);
         if (rc) { plan_free(P); return IRIS_CUDA_ERR_CUDA; }

@@ -199,7 +199,7 @@ static wcache_t *weight_lookup(const uint16_t *w, int rows, int cols) {
     e->n = (size_t)rows * cols;
     e->dev = (uint16_t *)iris_dmalloc(e->n * 2);
     if (!e->dev) return NULL;
-    if (iris_cuda_check(cudaMemcpy(e->dev, w, e->n * 2, cudaMemcpyHostToDevice), "weight upload") ||
+    if (iris_h2d(e->dev, w, e->n * 2) ||
         iris_make_tmap_bf16(&e->tm, e->dev, (uint64_t)rows, (uint64_t)cols, (uint64_t)cols,
                             (rows % 256 == 0) ? 256 : 128)) {
         iris_dfree(e->dev);
@@ -304,8 +304,7 @@ static int upload_rope(float *dc, float *ds, const float *hc, const float *hs, i
         tmp[i] = hc[2 * i];
         tmp[n + i] = hs[2 * i];
     }
-    int rc = iris_cuda_check(cudaMemcpy(dc, tmp, n * 4, cudaMemcpyHostToDevice), "rope") ||
-             iris_cuda_check(cudaMemcpy(ds, tmp + n, n * 4, cudaMemcpyHostToDevice), "rope");
+    int rc = iris_h2d(dc, tmp, n * 4) || iris_h2d(ds, tmp + n, n * 4);
     free(tmp);
     return rc;
 }
@@ -326,8 +325,8 @@ void iris_gpu_rope_unified_bf16(iris_gpu_tensor_t q, iris_gpu_tensor_t k, const 
         return;
     const float *kcp = qc, *ksp = qs;
     if (img_cos_k && img_sin_k) {
-        cudaMemcpy(kc, qc, (size_t)img_offset * 64 * 4, cudaMemcpyDeviceToDevice);
-        cudaMemcpy(ks, qs, (size_t)img_offset * 64 * 4, cudaMemcpyDeviceToDevice);
+        cudaMemcpyAsync(kc, qc, (size_t)img_offset * 64 * 4, cudaMemcpyDeviceToDevice, g_rt.stream);
+        cudaMemcpyAsync(ks, qs, (size_t)img_offset * 64 * 4, cudaMemcpyDeviceToDevice, g_rt.stream);
         if (n_img && upload_rope(kc + (size_t)img_offset * 64, ks + (size_t)img_offset * 64, img_cos_k,
                                  img_sin_k, n_img))
             return;

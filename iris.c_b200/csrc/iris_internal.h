@@ -41,6 +41,9 @@ static inline void iris_count_launch(uint64_t n) { g_rt.launches += n; }
 
 /* ensure the runtime is up; returns status */
 int iris_rt_ensure(void);
+/* host -> device copy on the library stream, complete when it returns (use
+ * instead of cudaMemcpy, whose DMA is not ordered with the library stream) */
+int iris_h2d(void *dst, const void *src, size_t bytes);
 
 /* ---------------- NCCL communicator (comm.c) ---------------- */
 int iris_comm_world(void);  /* 1 without a communicator */

@@ -136,6 +136,13 @@ cudaError_t iris_launch_attention_mma(const void *q, int ldq, const void *k, con
                                       void *o, int ldo, int sq, int sk, int heads, float scale,
                                       const uint8_t *key_mask, cudaStream_t stream);
 cudaError_t iris_attention_tc_init(void);
+/* tcgen05 attention with grouped-query heads (query head h reads key/value
+ * head h / kv_group; K and V hold heads / kv_group heads) and an optional
+ * causal mask (key j > query i scores -1e9, as the reference's encoder
+ * attention does) */
+cudaError_t iris_launch_attention_gqa(const void *q, int ldq, const void *k, const void *v, int ldk, void *o,
+                                      int ldo, int sq, int sk, int heads, int kv_group, int causal, float scale,
+                                      const uint8_t *key_mask, cudaStream_t stream);
 void iris_attention_set_status(int *status);
 
 /* ------------------------------------------------------------------ row kernels */
@@ -223,6 +230,17 @@ cudaError_t iris_launch_interleave_gate_up(void *dst, const void *src, int F, in
                                            cudaStream_t stream);
 cudaError_t iris_launch_copy_rows_bf16(void *dst, int ldd, const void *src, int lds, int rows,
                                        int cols, cudaStream_t stream);
+
+/* ------------------------------------------------------------------ text encoder (Qwen3) */
+/* x[s] = f32 of table[ids[s]] (bf16 [vocab, H]); ids outside [0, vocab) -> zeros */
+cudaError_t iris_launch_embed_rows(const int *ids, int S, const void *table, int vocab, int H, float *x,
+                                   cudaStream_t stream);
+/* f32 QKV projection [S, ld] (nh Q heads, nkv K heads, nkv V heads of 128) ->
+ * bf16 q [S, nh*128], k / v [S, nkv*128]: per-head RMSNorm (qw / kw) and
+ * split-half RoPE (cos/sin [S, 64]) on Q and K */
+cudaError_t iris_launch_qk_norm_rope_half(const float *qkv, int ld, int S, int nh, int nkv, const float *qw,
+                                          const float *kw, const float *cosb, const float *sinb, float eps, void *q,
+                                          void *k, void *v, cudaStream_t stream);
 
 /* ------------------------------------------------------------------ autoencoder decoder
  * Stride-1 convolution with zero padding as an implicit GEMM on the tensor

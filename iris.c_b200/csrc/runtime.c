@@ -96,7 +96,8 @@ int iris_cuda_init(int device) {
         return iris_cuda_check(e, "cudaStreamCreate");
     if ((e = cudaMalloc((void **)&g_rt.d_status, sizeof(int))) != cudaSuccess)
         return iris_cuda_check(e, "cudaMalloc(status)");
-    cudaMemset(g_rt.d_status, 0, sizeof(int));
+    cudaMemsetAsync(g_rt.d_status, 0, sizeof(int), g_rt.stream);
+    cudaStreamSynchronize(g_rt.stream);
     if ((e = iris_gemm_init()) != cudaSuccess) return iris_cuda_check(e, "gemm init");
     if ((e = iris_attention_init()) != cudaSuccess) return iris_cuda_check(e, "attention init");
     if ((e = iris_attention_tc_init()) != cudaSuccess) return iris_cuda_check(e, "attention init");
@@ -119,13 +120,25 @@ int iris_cuda_device_status(int clear) {
     if (!g_rt.initialized) return 0;
     int v = 0;
     cudaMemcpy(&v, g_rt.d_status, sizeof(int), cudaMemcpyDeviceToHost);
-    if (clear && v) cudaMemset(g_rt.d_status, 0, sizeof(int));
+    if (clear && v) {
+        cudaMemsetAsync(g_rt.d_status, 0, sizeof(int), g_rt.stream);
+        cudaStreamSynchronize(g_rt.stream);
+    }
     return v;
 }
 
 int iris_stream_drain(void) {
     return iris_comm_active() ? iris_comm_sync_stream()
                               : iris_cuda_check(cudaStreamSynchronize(g_rt.stream), "cudaStreamSynchronize");
+}
+
+/* Host -> device copy ordered on the library stream and complete on return.
+ * (A plain cudaMemcpy from pageable memory may return before its DMA lands,
+ * and it is not ordered with the library's non-blocking stream, so a kernel
+ * queued right after it could read the old contents.) */
+int iris_h2d(void *dst, const void *src, size_t bytes) {
+    int rc = iris_cuda_check(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyHostToDevice, g_rt.stream), "host to device");
+    return rc ? rc : iris_stream_drain();
 }
 
 int iris_cuda_synchronize(void) {

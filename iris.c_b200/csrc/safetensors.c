@@ -175,11 +175,20 @@ static int open_file(st_model_t *m, const char *path) {
     return rc;
 }
 
+/* Opens the weights of a model directory: the shards named by a diffusers
+ * (diffusion_pytorch_model.safetensors.index.json) or transformers
+ * (model.safetensors.index.json, the text encoder's) index, else the single
+ * diffusion_pytorch_model.safetensors or model.safetensors. */
 int st_open_dir(st_model_t *m, const char *dir) {
     memset(m, 0, sizeof(*m));
     char path[4200];
-    snprintf(path, sizeof(path), "%s/diffusion_pytorch_model.safetensors.index.json", dir);
-    FILE *fp = fopen(path, "rb");
+    static const char *const index_names[2] = {"diffusion_pytorch_model.safetensors.index.json",
+                                               "model.safetensors.index.json"};
+    FILE *fp = NULL;
+    for (int k = 0; k < 2 && !fp; k++) {
+        snprintf(path, sizeof(path), "%s/%s", dir, index_names[k]);
+        fp = fopen(path, "rb");
+    }
     if (fp) {
         fseek(fp, 0, SEEK_END);
         long len = ftell(fp);
@@ -218,6 +227,9 @@ int st_open_dir(st_model_t *m, const char *dir) {
         if (nn > 0) return 0;
     }
     snprintf(path, sizeof(path), "%s/diffusion_pytorch_model.safetensors", dir);
+    FILE *single = fopen(path, "rb");
+    if (!single) snprintf(path, sizeof(path), "%s/model.safetensors", dir);
+    else fclose(single);
     if (open_file(m, path) != 0) { st_close(m); return -1; }
     return 0;
 }

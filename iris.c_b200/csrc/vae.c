@@ -93,7 +93,7 @@ static void *vae_alloc(iris_cuda_vae_t *v, size_t bytes) {
 static void *vae_upload(iris_cuda_vae_t *v, const void *host, size_t bytes) {
     void *d = vae_alloc(v, bytes);
     if (!d) return NULL;
-    if (cudaMemcpy(d, host, bytes, cudaMemcpyHostToDevice) != cudaSuccess) return NULL;
+    if (iris_h2d(d, host, bytes)) return NULL;
     v->weight_bytes += bytes;
     return d;
 }
@@ -453,8 +453,8 @@ static int plan_ensure(iris_cuda_vae_t *v, int lh, int lw) {
     ALLOC(P->rgb8, 3 * p0);
 #undef ALLOC
     /* the attention's padding rows (pixels P3 .. P3p - 1) feed GEMM operands: zero once */
-    if (!rc) rc = iris_cuda_check(cudaMemset(P->hA, 0, p3p * VAE_MID * 2), "memset");
-    if (!rc) rc = iris_cuda_check(cudaMemset(P->qk, 0, p3p * 2 * VAE_MID * 2), "memset");
+    if (!rc) rc = iris_cuda_check(cudaMemsetAsync(P->hA, 0, p3p * VAE_MID * 2, g_rt.stream), "memset");
+    if (!rc) rc = iris_cuda_check(cudaMemsetAsync(P->qk, 0, p3p * 2 * VAE_MID * 2, g_rt.stream), "memset");
     if (rc) { plan_free(P); return rc; }
     P->valid = 1;
     return 0;

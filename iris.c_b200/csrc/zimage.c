@@ -434,8 +434,8 @@ static int zi_plan_ensure(iris_cuda_zimage_t *z, int lat_h, int lat_w, int cap_s
     PA(P->mask, (size_t)S);
 #undef PA
     /* padding rows of the embedder inputs stay zero (their embeddings are replaced by pad tokens) */
-    cudaMemset(P->tok_img, 0, (size_t)P->ni * z->pf * 2);
-    cudaMemset(P->cap_bf16, 0, (size_t)P->nc * cap * 2);
+    cudaMemsetAsync(P->tok_img, 0, (size_t)P->ni * z->pf * 2, g_rt.stream);
+    cudaMemsetAsync(P->cap_bf16, 0, (size_t)P->nc * cap * 2, g_rt.stream);
     if (iris_mk_tmap(&P->tm_xmod, P->xmod, S, D, D, 128) || iris_mk_tmap(&P->tm_attn, P->attn, S, D, D, 128) ||
         iris_mk_tmap(&P->tm_mlp, P->mlp, S, F, F, 128) ||
         iris_mk_tmap(&P->tm_tok_img, P->tok_img, P->ni, z->pf, z->pf, 128) ||
@@ -448,9 +448,8 @@ static int zi_plan_ensure(iris_cuda_zimage_t *z, int lat_h, int lat_w, int cap_s
         uint8_t *mk = (uint8_t *)malloc((size_t)S);
         if (!cs || !sn || !mk) { free(cs); free(sn); free(mk); goto oom; }
         zi_fill_rope(z, P, cs, sn, mk);
-        int rc = iris_cuda_check(cudaMemcpy(P->rope_cos, cs, (size_t)S * 64 * 4, cudaMemcpyHostToDevice), "rope") ||
-                 iris_cuda_check(cudaMemcpy(P->rope_sin, sn, (size_t)S * 64 * 4, cudaMemcpyHostToDevice), "rope") ||
-                 iris_cuda_check(cudaMemcpy(P->mask, mk, (size_t)S, cudaMemcpyHostToDevice), "mask");
+        int rc = iris_h2d(P->rope_cos, cs, (size_t)S * 64 * 4) || iris_h2d(P->rope_sin, sn, (size_t)S * 64 * 4) ||
+                 iris_h2d(P->mask, mk, (size_t)S);
         free(cs); free(sn); free(mk);
         if (rc) { zi_plan_free(P); return IRIS_CUDA_ERR_CUDA; }
     }

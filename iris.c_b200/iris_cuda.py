@@ -53,6 +53,17 @@ class ZImageConfig(C.Structure):
                    rope_theta=float(c["rope_theta"]), axes_dims=(C.c_int * 3)(*c["axes_dims"]))
 
 
+class Qwen3Config(C.Structure):
+    """iris_cuda_qwen3_config_t."""
+    _fields_ = [("hidden", C.c_int), ("intermediate", C.c_int), ("heads", C.c_int), ("kv_heads", C.c_int),
+                ("head_dim", C.c_int), ("vocab", C.c_int), ("layers", C.c_int), ("rope_theta", C.c_float)]
+
+    @classmethod
+    def from_hf(cls, c: dict) -> "Qwen3Config":
+        return cls(c["hidden_size"], c["intermediate_size"], c["num_attention_heads"], c["num_key_value_heads"],
+                   c.get("head_dim", 128), c["vocab_size"], c["num_hidden_layers"], c.get("rope_theta", 1e6))
+
+
 class Image(C.Structure):
     """iris_cuda_image_t (the reference's iris_image layout, iris.h:73-78)."""
     _fields_ = [("width", C.c_int), ("height", C.c_int), ("channels", C.c_int),
@@ -141,6 +152,17 @@ SIGNATURES = {
                                            C.c_void_p]),
     "iris_cuda_vae_graph_kernels": (C.c_uint64, [C.c_void_p]),
     "iris_cuda_vae_random": (C.c_void_p, [C.c_int, C.c_float, C.c_float, C.c_uint64]),
+    "iris_cuda_qwen3_load": (C.c_void_p, [C.c_char_p]),
+    "iris_cuda_qwen3_random": (C.c_void_p, [C.POINTER(Qwen3Config), C.c_uint64]),
+    "iris_cuda_qwen3_free": (None, [C.c_void_p]),
+    "iris_cuda_qwen3_get_config": (C.c_int, [C.c_void_p, C.POINTER(Qwen3Config)]),
+    "iris_cuda_qwen3_weight_bytes": (C.c_size_t, [C.c_void_p]),
+    "iris_cuda_qwen3_set_extraction_mode": (C.c_int, [C.c_void_p, C.c_int]),
+    "iris_cuda_qwen3_text_dim": (C.c_int, [C.c_void_p]),
+    "iris_cuda_qwen3_forward": (C.c_void_p, [C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int), C.c_int]),
+    "iris_cuda_qwen3_forward_dev": (C.c_int, [C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int), C.c_int,
+                                              C.c_void_p]),
+    "iris_cuda_qwen3_graph_kernels": (C.c_uint64, [C.c_void_p]),
     "iris_cuda_vae_profile": (C.c_int, [C.c_void_p, C.POINTER(KernelTime), C.c_int]),
     # iris_gpu_* surface (iris_metal.h names)
     "iris_gpu_tensor_create": (C.c_void_p, [_fp, C.c_size_t]),
@@ -507,3 +529,47 @@ class Vae:
 
     def graph_kernels(self) -> int:
         return lib().iris_cuda_vae_graph_kernels(self.h)
+
+
+class Qwen3:
+    """Resident Qwen3 text encoder (libiris_cuda): token ids -> text embeddings."""
+
+    def __init__(self, handle):
+        if not handle:
+            raise IrisCudaError(last_error() or "text encoder creation failed")
+        self.h = handle
+
+    @classmethod
+    def load(cls, model_dir: str) -> "Qwen3":
+        return cls(lib().iris_cuda_qwen3_load(model_dir.encode()))
+
+    @classmethod
+    def random(cls, cfg: Qwen3Config, seed: int) -> "Qwen3":
+        return cls(lib().iris_cuda_qwen3_random(C.byref(cfg), seed))
+
+    def close(self):
+        if self.h:
+            lib().iris_cuda_qwen3_free(self.h)
+            self.h = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
+
+    def set_extraction_mode(self, mode: int) -> None:
+        if lib().iris_cuda_qwen3_set_extraction_mode(self.h, mode):
+            raise IrisCudaError(last_error())
+
+    def text_dim(self) -> int:
+        return lib().iris_cuda_qwen3_text_dim(self.h)
+
+    def forward(self, ids, mask=None) -> np.ndarray:
+        """ids / mask [S] -> f32 [S, text_dim] (qwen3_forward)."""
+        ip = C.POINTER(C.c_int)
+        ids = np.ascontiguousarray(ids, np.int32)
+        m = None if mask is None else np.ascontiguousarray(mask, np.int32)
+        p = lib().iris_cuda_qwen3_forward(self.h, ids.ctypes.data_as(ip),
+                                          None if m is None else m.ctypes.data_as(ip), len(ids))
+        return _take_floats(p, len(ids) * self.text_dim(), (len(ids), self.text_dim()))

@@ -362,3 +362,64 @@ def make_vae_model(model_dir: str, seed: int, z: int = 32, zimage: bool = False)
     write_safetensors(path, bits)
     return path
 
+
+
+# ------------------------------------------------------------------ Qwen3 text encoder
+# Qwen3-4B as Flux.2 Klein uses it (iris_qwen3.c:1436-1447 defaults)
+QWEN3_4B = dict(hidden_size=2560, intermediate_size=9728, num_attention_heads=32, num_key_value_heads=8,
+                head_dim=128, vocab_size=151936, num_hidden_layers=36, rope_theta=1000000.0)
+
+
+def qwen3_tensor_specs(cfg: dict, layers: int | None = None) -> list[tuple[str, tuple, str]]:
+    """Tensors of the Qwen3 text encoder as the reference's loader reads them
+    (load_layer_weights / qwen3_model_load, iris_qwen3.c:1254-1300, :1604-1619).
+    layers: how many decoder layers to emit (default: all)."""
+    H, F = cfg["hidden_size"], cfg["intermediate_size"]
+    q, kv = cfg["num_attention_heads"] * cfg["head_dim"], cfg["num_key_value_heads"] * cfg["head_dim"]
+    s = [("model.embed_tokens.weight", (cfg["vocab_size"], H), "embed")]
+    for i in range(cfg["num_hidden_layers"] if layers is None else layers):
+        p = f"model.layers.{i}."
+        s += [(p + "input_layernorm.weight", (H,), "norm"), (p + "post_attention_layernorm.weight", (H,), "norm"),
+              (p + "self_attn.q_proj.weight", (q, H), "linear"), (p + "self_attn.k_proj.weight", (kv, H), "linear"),
+              (p + "self_attn.v_proj.weight", (kv, H), "linear"), (p + "self_attn.o_proj.weight", (H, q), "linear"),
+              (p + "self_attn.q_norm.weight", (cfg["head_dim"],), "norm"),
+              (p + "self_attn.k_norm.weight", (cfg["head_dim"],), "norm"),
+              (p + "mlp.gate_proj.weight", (F, H), "linear"), (p + "mlp.up_proj.weight", (F, H), "linear"),
+              (p + "mlp.down_proj.weight", (H, F), "linear")]
+    s += [("model.norm.weight", (H,), "norm")]
+    return s
+
+
+def _qwen3_tensor(seed: int, name: str, shp: tuple, kind: str) -> np.ndarray:
+    rng = np.random.default_rng([seed, zlib.crc32(name.encode())])
+    g = rng.standard_normal(shp, dtype=np.float32)
+    if kind == "linear":
+        x = g / np.float32(np.sqrt(shp[1]))
+    elif kind == "norm":
+        x = 1.0 + 0.1 * g
+    else:  # embeddings
+        x = g
+    return f32_to_bf16_bits(x.astype(np.float32))
+
+
+def qwen3_weights(cfg: dict, seed: int) -> dict[str, np.ndarray]:
+    """f32 (bf16-valued) tensors of make_qwen3_model without disk I/O."""
+    return {n: bf16_bits_to_f32(_qwen3_tensor(seed, n, shp, kind)) for n, shp, kind in qwen3_tensor_specs(cfg)}
+
+
+def make_qwen3_model(model_dir: str, cfg: dict, seed: int) -> str:
+    """Random Qwen3 text encoder (bf16) under model_dir/text_encoder/ in the
+    layout the reference opens (config.json, model.safetensors.index.json and
+    model-00001-of-00001.safetensors, iris_qwen3.c:1450-1520); projections
+    N(0, 1/fan_in), norm scales 1 + N(0, 0.1), embeddings N(0, 1).  Returns
+    the text_encoder directory."""
+    d = os.path.join(model_dir, "text_encoder")
+    os.makedirs(d, exist_ok=True)
+    with open(os.path.join(d, "config.json"), "w") as f:
+        json.dump(dict(cfg, architectures=["Qwen3ForCausalLM"]), f, indent=1)
+    bits = {name: _qwen3_tensor(seed, name, shp, kind) for name, shp, kind in qwen3_tensor_specs(cfg)}
+    shard = "model-00001-of-00001.safetensors"
+    write_safetensors(os.path.join(d, shard), bits)
+    with open(os.path.join(d, "model.safetensors.index.json"), "w") as f:
+        json.dump({"metadata": {}, "weight_map": {n: shard for n in bits}}, f)
+    return d

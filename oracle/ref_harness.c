@@ -289,3 +289,26 @@ int ref_vae_decode(const char *vae_file, int z_channels, const float *latent, in
     return ref_vae_decode_ex(vae_file, z_channels, 0.0f, 0.0f, latent, lh, lw, out_rgb, out_w, out_h);
 }
 
+
+/* ------------------------------------------------------------------ Qwen3 text encoder
+ * The reference's CPU text encoder (qwen3_model_load + qwen3_forward,
+ * iris_qwen3.c:1578, :1072) on a model directory (config.json + shards):
+ * ids / mask [seq] -> out [seq, text_dim] (text_dim = 3 * hidden for Flux,
+ * hidden for Z-Image extraction).  Returns text_dim or a negative status. */
+#include "iris_qwen3.h"
+
+int ref_qwen3_forward(const char *model_dir, int zimage, const int *ids, const int *mask, int seq, float *out,
+                      int out_cap) {
+    qwen3_model_t *m = qwen3_model_load(model_dir);
+    if (!m) return -1;
+    qwen3_encoder_t enc = {NULL, m};
+    qwen3_set_extraction_mode(&enc, zimage ? 1 : 0);
+    float *r = qwen3_forward(m, ids, mask, seq);
+    if (!r) { qwen3_model_free(m); return -2; }
+    /* out_cap = seq * text_dim floats (the caller knows the hidden size) */
+    int text_dim = out_cap / seq;
+    memcpy(out, r, (size_t)seq * text_dim * sizeof(float));
+    free(r);
+    qwen3_model_free(m);
+    return text_dim;
+}

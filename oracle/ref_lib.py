@@ -58,10 +58,25 @@ class RefLib:
         L.ref_sample_euler_zimage.argtypes = [C.c_void_p, _fp, C.c_int, C.c_int, C.c_int, C.c_int,
                                               _fp, C.c_int, _fp, C.c_int, _fp]
         L.ref_set_threads.argtypes = [C.c_int]
+        L.ref_qwen3_forward.argtypes = [C.c_char_p, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int), C.c_int, _fp,
+                                        C.c_int]
         L.ref_vae_decode.argtypes = [C.c_char_p, C.c_int, _fp, C.c_int, C.c_int, C.POINTER(C.c_uint8),
                                      C.POINTER(C.c_int), C.POINTER(C.c_int)]
         L.ref_vae_decode_ex.argtypes = [C.c_char_p, C.c_int, C.c_float, C.c_float, _fp, C.c_int, C.c_int,
                                         C.POINTER(C.c_uint8), C.POINTER(C.c_int), C.POINTER(C.c_int)]
+
+    def qwen3_forward(self, model_dir: str, ids, mask, text_dim: int, zimage: bool = False) -> np.ndarray:
+        """Reference CPU text encoder (qwen3_model_load + qwen3_forward) -> [seq, text_dim]."""
+        ids = np.ascontiguousarray(ids, np.int32)
+        mask = np.ascontiguousarray(mask, np.int32)
+        seq = len(ids)
+        out = np.zeros(seq * text_dim, np.float32)
+        ip = C.POINTER(C.c_int)
+        rc = self.lib.ref_qwen3_forward(model_dir.encode(), int(zimage), ids.ctypes.data_as(ip),
+                                        mask.ctypes.data_as(ip), seq, _f(out), seq * text_dim)
+        if rc != text_dim:
+            raise RuntimeError(f"reference qwen3_forward failed ({rc})")
+        return out.reshape(seq, text_dim)
 
     def set_threads(self, n: int):
         self.lib.ref_set_threads(n)
