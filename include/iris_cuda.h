@@ -331,6 +331,10 @@ int iris_cuda_qwen3_forward_dev(iris_cuda_qwen3_t *m, const int *input_ids, cons
                                 float *d_out);
 /* kernels in one captured forward (0 before the first) */
 uint64_t iris_cuda_qwen3_graph_kernels(const iris_cuda_qwen3_t *m);
+/* Time every kernel of one forward at the last sequence length (no graph;
+ * an event after each launch).  Returns the number of entries or a negative
+ * status. */
+int iris_cuda_qwen3_profile(iris_cuda_qwen3_t *m, iris_cuda_kernel_time_t *out, int max_entries);
 
 /* ------------------------------------------------------------------ 2d. autoencoder decoder
  * The step after the denoising loop: latent -> RGB image on the GPU.  The

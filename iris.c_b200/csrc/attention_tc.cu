@@ -223,6 +223,36 @@ __device__ __forceinline__ void softmax_role(const AttnParams& p, uint32_t tmem,
       const uint32_t m4 = reinterpret_cast<const uint32_t*>(p.kmask + kbase)[lane];
       full = __all_sync(0xffffffffu, m4 == 0x01010101u);
     }
+    if (kMasked && !full) {
+      // A tile every key of which is masked for every row of the query tile
+      // (entirely after the diagonal, or all padding) contributes exp(-1e9 - m)
+      // = 0 once a row has seen a real key (m > -1e8): P = 0, l and O unchanged.
+      // (A row whose keys are all masked keeps the exact path: the reference's
+      // softmax then spreads uniformly over its masked keys.)
+      bool dead = p.causal && kbase > row0 + BQ - 1;
+      if (!dead && p.kmask) {
+        uint32_t m4 = 0;
+        const int k4 = kbase + 4 * lane;
+        if (k4 + 3 < p.sk) m4 = reinterpret_cast<const uint32_t*>(p.kmask + kbase)[lane];
+        else
+          for (int e = 0; e < 4; e++) m4 |= (k4 + e < p.sk) ? (uint32_t)p.kmask[k4 + e] << (8 * e) : 0u;
+        dead = __all_sync(0xffffffffu, m4 == 0u);
+      }
+      if (__all_sync(0xffffffffu, dead && m > -1e8f)) {
+        uint32_t z[BKV / 2];
+#pragma unroll
+        for (int i = 0; i < BKV / 2; i++) z[i] = 0u;
+        iris::tmem_st64(s_addr, z);  // P_j = 0 over the first 64 columns of S_j
+        iris::tc_fence_before();
+        if (kPair) {
+          __syncwarp();
+          if (lane == 0) iris::mbar_arrive_cluster(p_full_cluster);
+        } else {
+          iris::mbar_arrive(p_full);
+        }
+        continue;
+      }
+    }
     uint32_t pw[BKV / 2];
     float rsum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
     float alpha = 1.f;

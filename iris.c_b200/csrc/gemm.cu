@@ -823,13 +823,19 @@ extern "C" cudaError_t iris_launch_gemm_ex(const IrisGemmParams* p, int num_sms,
     mode = (e && strcmp(e, "1cta") == 0) ? 1 : 0;
   }
   const int rows = p->rows[0] + (p->ngroups > 1 ? p->rows[1] : 0);
+  const bool linear = p->mode == IRIS_EPI_BF16 || p->mode == IRIS_EPI_F32 || p->mode == IRIS_EPI_RESID_GATE;
   if (mode == 0 && p->bn == 256 && rows >= 512 && g_max_pairs > 0) {
     int mt = (p->rows[0] + BM2 - 1) / BM2 + (p->ngroups > 1 ? (p->rows[1] + BM2 - 1) / BM2 : 0);
     long total = (long)mt * ((p->N + 255) / 256);
     long cap = g_max_pairs < num_sms / 2 ? g_max_pairs : num_sms / 2;
-    long pairs = total < cap ? total : cap;
-    gemm_tc2_kernel<<<(int)(2 * pairs), NUM_THREADS2, SMEM2_BYTES, stream>>>(*p);
-    return cudaGetLastError();
+    // a pair grid under half the pairs leaves SMs idle: a linear epilogue with a
+    // workspace goes to the single-CTA kernel below, which splits K instead
+    const bool split_instead = p->ws && linear && 2 * total < cap && p->K / BK >= 8;
+    if (!split_instead) {
+      long pairs = total < cap ? total : cap;
+      gemm_tc2_kernel<<<(int)(2 * pairs), NUM_THREADS2, SMEM2_BYTES, stream>>>(*p);
+      return cudaGetLastError();
+    }
   }
   int mt = (p->rows[0] + BM - 1) / BM + (p->ngroups > 1 ? (p->rows[1] + BM - 1) / BM : 0);
   long tiles = (long)mt * ((p->N + p->bn - 1) / p->bn);
@@ -840,8 +846,7 @@ extern "C" cudaError_t iris_launch_gemm_ex(const IrisGemmParams* p, int num_sms,
   q.splitk = 1;
   const int num_kb = (p->K + BK - 1) / BK;
   const int span = p->ngroups > 1 ? p->row0[1] + p->rows[1] : p->row0[0] + p->rows[0];
-  if (p->ws && tiles < num_sms / 2 && num_kb >= 8 &&
-      (p->mode == IRIS_EPI_BF16 || p->mode == IRIS_EPI_F32 || p->mode == IRIS_EPI_RESID_GATE)) {
+  if (p->ws && tiles < num_sms / 2 && num_kb >= 8 && linear) {
     long s = num_sms / tiles;
     if (s > num_kb / 4) s = num_kb / 4;
     const long fit = (long)(p->ws_bytes / ((size_t)span * p->N * sizeof(float)));

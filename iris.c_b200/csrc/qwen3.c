@@ -38,6 +38,8 @@ typedef struct {
     int *ids;
     uint8_t *mask;
     float *x, *qkv, *out, *cosb, *sinb;
+    float *ws;          /* split-K workspace of the H-wide projections (few output tiles at 512 rows) */
+    size_t ws_bytes;
     uint16_t *xn, *q, *k, *v, *attn, *mlp;
     CUtensorMap tm_xn, tm_attn, tm_mlp;
     cudaGraph_t graph;
@@ -286,7 +288,8 @@ static void q3_plan_free(q3_plan_t *P) {
         cudaGraphExecDestroy(P->gexec);
         cudaGraphDestroy(P->graph);
     }
-    void *b[] = {P->ids, P->mask, P->x, P->qkv, P->out, P->cosb, P->sinb, P->xn, P->q, P->k, P->v, P->attn, P->mlp};
+    void *b[] = {P->ids, P->mask, P->x, P->qkv, P->out, P->cosb, P->sinb, P->xn, P->q, P->k, P->v, P->attn, P->mlp,
+                 P->ws};
     for (size_t i = 0; i < sizeof(b) / sizeof(b[0]); i++) iris_dfree(b[i]);
     memset(P, 0, sizeof(*P));
 }
@@ -314,6 +317,8 @@ static int q3_plan_ensure(iris_cuda_qwen3_t *m, int S) {
     ALLOC(P->v, S * kvd * 2);
     ALLOC(P->attn, S * qd * 2);
     ALLOC(P->mlp, S * F * 2);
+    P->ws_bytes = (size_t)4 * S * H * 4;  /* up to 4 K splits */
+    ALLOC(P->ws, P->ws_bytes);
 #undef ALLOC
     if (!rc) {
         /* RoPE tables with the reference's float formulas (compute_rope_freqs, iris_qwen3.c:258-275) */
@@ -345,19 +350,36 @@ static int q3_plan_ensure(iris_cuda_qwen3_t *m, int S) {
 typedef struct {
     int rc;
     uint64_t kernels;
+    /* profiling (iris_cuda_qwen3_profile): an event after every launch */
+    iris_cuda_kernel_time_t *prof;
+    cudaEvent_t *ev;
+    int nprof, maxprof;
+    double flops;  /* algorithmic FLOPs of the next accounted launch */
 } q3_enq_t;
 
 static void q3_done(q3_enq_t *E, cudaError_t e, const char *what, int n) {
     if (E->rc) return;
-    if (e != cudaSuccess) E->rc = iris_cuda_check(e, what);
-    else E->kernels += (uint64_t)n;
+    if (e != cudaSuccess) { E->rc = iris_cuda_check(e, what); return; }
+    E->kernels += (uint64_t)n;
+    if (E->prof && E->nprof < E->maxprof) {
+        iris_cuda_kernel_time_t *k = &E->prof[E->nprof];
+        snprintf(k->name, sizeof(k->name), "%s", what);
+        k->flops = E->flops;
+        k->bytes = 0.0;
+        cudaEventRecord(E->ev[E->nprof + 1], g_rt.stream);
+        E->nprof++;
+    }
+    E->flops = 0.0;
 }
 
-static void q3_gemm(q3_enq_t *E, const CUtensorMap *ta, const CUtensorMap *tb, int M, int N, int K, int mode,
-                    void *out, int ldo, const float *gate, void *mlp_out, int ld_mlp) {
+static void q3_gemm(q3_enq_t *E, const char *name, const CUtensorMap *ta, const CUtensorMap *tb, int M, int N,
+                    int K, int mode, void *out, int ldo, const float *gate, void *mlp_out, int ld_mlp, float *ws,
+                    size_t ws_bytes) {
     if (E->rc) return;
     IrisGemmParams p;
     memset(&p, 0, sizeof(p));
+    p.ws = ws;
+    p.ws_bytes = ws_bytes;
     p.tmap_a = *ta;
     p.tmap_b[0] = *tb;
     p.ngroups = 1;
@@ -374,7 +396,8 @@ static void q3_gemm(q3_enq_t *E, const CUtensorMap *ta, const CUtensorMap *tb, i
     p.status = g_rt.d_status;
     int n = 1;
     cudaError_t e = iris_launch_gemm_ex(&p, g_rt.num_sms, g_rt.stream, &n);
-    q3_done(E, e, "text encoder gemm", n);
+    E->flops = 2.0 * M * N * K;
+    q3_done(E, e, name, n);
 }
 
 static int q3_enqueue(iris_cuda_qwen3_t *m, q3_enq_t *E) {
@@ -388,17 +411,18 @@ static int q3_enqueue(iris_cuda_qwen3_t *m, q3_enq_t *E) {
     for (int i = 0; i <= last && !E->rc; i++) {
         const q3_layer_t *L = &m->layers[i];
         q3_done(E, iris_launch_rmsnorm(P->x, H, L->ln1, NULL, P->xn, H, S, H, Q3_EPS, NULL, st), "rmsnorm", 1);
-        q3_gemm(E, &P->tm_xn, &L->tm_qkv, S, nq, H, IRIS_EPI_F32, P->qkv, nq, NULL, NULL, 0);
+        q3_gemm(E, "qkv", &P->tm_xn, &L->tm_qkv, S, nq, H, IRIS_EPI_F32, P->qkv, nq, NULL, NULL, 0, NULL, 0);
         q3_done(E, iris_launch_qk_norm_rope_half(P->qkv, nq, S, c->heads, c->kv_heads, L->qn, L->kn, P->cosb, P->sinb,
                                                  Q3_EPS, P->q, P->k, P->v, st),
                 "qk norm rope", 1);
+        E->flops = 2.0 * S * S * qd;  /* causal: half of 4 S^2 d per head */
         q3_done(E, iris_launch_attention_gqa(P->q, qd, P->k, P->v, kvd, P->attn, qd, S, S, c->heads,
                                              c->heads / c->kv_heads, 1, 1.0f / sqrtf(128.0f), P->mask, st),
                 "attention", 1);
-        q3_gemm(E, &P->tm_attn, &L->tm_o, S, H, qd, IRIS_EPI_RESID_GATE, P->x, H, m->ones, NULL, 0);
+        q3_gemm(E, "o_proj", &P->tm_attn, &L->tm_o, S, H, qd, IRIS_EPI_RESID_GATE, P->x, H, m->ones, NULL, 0, P->ws, P->ws_bytes);
         q3_done(E, iris_launch_rmsnorm(P->x, H, L->ln2, NULL, P->xn, H, S, H, Q3_EPS, NULL, st), "rmsnorm", 1);
-        q3_gemm(E, &P->tm_xn, &L->tm_gu, S, 2 * F, H, IRIS_EPI_SWIGLU, NULL, 0, NULL, P->mlp, F);
-        q3_gemm(E, &P->tm_mlp, &L->tm_down, S, H, F, IRIS_EPI_RESID_GATE, P->x, H, m->ones, NULL, 0);
+        q3_gemm(E, "gate_up", &P->tm_xn, &L->tm_gu, S, 2 * F, H, IRIS_EPI_SWIGLU, NULL, 0, NULL, P->mlp, F, NULL, 0);
+        q3_gemm(E, "down", &P->tm_mlp, &L->tm_down, S, H, F, IRIS_EPI_RESID_GATE, P->x, H, m->ones, NULL, 0, P->ws, P->ws_bytes);
         const int extract = m->mode ? (i == last) : (i == k_flux_layers[0] || i == k_flux_layers[1] || i == k_flux_layers[2]);
         if (extract && !E->rc) {
             q3_done(E, cudaMemcpy2DAsync(P->out + (size_t)slot * H, (size_t)td * 4, P->x, (size_t)H * 4,
@@ -421,7 +445,8 @@ static int q3_run(iris_cuda_qwen3_t *m) {
     if (!P->graph_ok) {
         static int no_graph = -1;
         if (no_graph < 0) no_graph = getenv("IRIS_CUDA_NO_GRAPH") ? 1 : 0;
-        q3_enq_t E = {0, 0};
+        q3_enq_t E;
+        memset(&E, 0, sizeof(E));
         if (no_graph) {
             int rc = q3_enqueue(m, &E);
             iris_count_launch(E.kernels);
@@ -486,3 +511,32 @@ float *iris_cuda_qwen3_forward(iris_cuda_qwen3_t *m, const int *input_ids, const
 }
 
 uint64_t iris_cuda_qwen3_graph_kernels(const iris_cuda_qwen3_t *m) { return m ? m->plan.graph_kernels : 0; }
+
+/* Time every kernel of one forward at the last sequence length (no graph; an
+ * event after each launch).  Returns the number of entries or a negative
+ * status. */
+int iris_cuda_qwen3_profile(iris_cuda_qwen3_t *m, iris_cuda_kernel_time_t *out, int max_entries) {
+    if (!m || !out || max_entries <= 0) return iris_fail(IRIS_CUDA_ERR_ARG, "null argument");
+    if (!m->plan.valid) return iris_fail(IRIS_CUDA_ERR_ARG, "run a forward first (no plan)");
+    cudaEvent_t *ev = (cudaEvent_t *)calloc((size_t)max_entries + 1, sizeof(cudaEvent_t));
+    if (!ev) return iris_fail(IRIS_CUDA_ERR_OOM, "events");
+    int rc = 0, n = 0;
+    for (int i = 0; i <= max_entries && !rc; i++) rc = iris_cuda_check(cudaEventCreate(&ev[i]), "event");
+    if (!rc) {
+        q3_enq_t E;
+        memset(&E, 0, sizeof(E));
+        E.prof = out;
+        E.ev = ev;
+        E.maxprof = max_entries;
+        cudaEventRecord(ev[0], g_rt.stream);
+        rc = q3_enqueue(m, &E);
+        iris_count_launch(E.kernels);
+        if (!rc) rc = iris_cuda_synchronize();
+        for (int i = 0; !rc && i < E.nprof; i++) cudaEventElapsedTime(&out[i].ms, ev[i], ev[i + 1]);
+        n = E.nprof;
+    }
+    for (int i = 0; i <= max_entries; i++)
+        if (ev[i]) cudaEventDestroy(ev[i]);
+    free(ev);
+    return rc ? rc : n;
+}

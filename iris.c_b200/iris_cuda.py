@@ -163,6 +163,7 @@ SIGNATURES = {
     "iris_cuda_qwen3_forward_dev": (C.c_int, [C.c_void_p, C.POINTER(C.c_int), C.POINTER(C.c_int), C.c_int,
                                               C.c_void_p]),
     "iris_cuda_qwen3_graph_kernels": (C.c_uint64, [C.c_void_p]),
+    "iris_cuda_qwen3_profile": (C.c_int, [C.c_void_p, C.POINTER(KernelTime), C.c_int]),
     "iris_cuda_vae_profile": (C.c_int, [C.c_void_p, C.POINTER(KernelTime), C.c_int]),
     # iris_gpu_* surface (iris_metal.h names)
     "iris_gpu_tensor_create": (C.c_void_p, [_fp, C.c_size_t]),
@@ -564,6 +565,14 @@ class Qwen3:
 
     def text_dim(self) -> int:
         return lib().iris_cuda_qwen3_text_dim(self.h)
+
+    def profile(self, max_entries: int = 1024):
+        """Per-kernel CUDA-event times of one forward at the last sequence length."""
+        arr = (KernelTime * max_entries)()
+        n = lib().iris_cuda_qwen3_profile(self.h, arr, max_entries)
+        if n < 0:
+            raise IrisCudaError(last_error())
+        return [dict(name=arr[i].name.decode(), ms=arr[i].ms, flops=arr[i].flops) for i in range(n)]
 
     def forward(self, ids, mask=None) -> np.ndarray:
         """ids / mask [S] -> f32 [S, text_dim] (qwen3_forward)."""

@@ -296,6 +296,11 @@ int ref_vae_decode(const char *vae_file, int z_channels, const float *latent, in
  * ids / mask [seq] -> out [seq, text_dim] (text_dim = 3 * hidden for Flux,
  * hidden for Z-Image extraction).  Returns text_dim or a negative status. */
 #include "iris_qwen3.h"
+#include <time.h>
+
+static double g_qwen3_forward_s;
+/* wall time of the last ref_qwen3_forward's qwen3_forward call (model load excluded) */
+double ref_qwen3_last_forward_s(void) { return g_qwen3_forward_s; }
 
 int ref_qwen3_forward(const char *model_dir, int zimage, const int *ids, const int *mask, int seq, float *out,
                       int out_cap) {
@@ -303,7 +308,11 @@ int ref_qwen3_forward(const char *model_dir, int zimage, const int *ids, const i
     if (!m) return -1;
     qwen3_encoder_t enc = {NULL, m};
     qwen3_set_extraction_mode(&enc, zimage ? 1 : 0);
+    struct timespec t0, t1;
+    clock_gettime(CLOCK_MONOTONIC, &t0);
     float *r = qwen3_forward(m, ids, mask, seq);
+    clock_gettime(CLOCK_MONOTONIC, &t1);
+    g_qwen3_forward_s = (double)(t1.tv_sec - t0.tv_sec) + 1e-9 * (double)(t1.tv_nsec - t0.tv_nsec);
     if (!r) { qwen3_model_free(m); return -2; }
     /* out_cap = seq * text_dim floats (the caller knows the hidden size) */
     int text_dim = out_cap / seq;

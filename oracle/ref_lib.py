@@ -60,6 +60,7 @@ class RefLib:
         L.ref_set_threads.argtypes = [C.c_int]
         L.ref_qwen3_forward.argtypes = [C.c_char_p, C.c_int, C.POINTER(C.c_int), C.POINTER(C.c_int), C.c_int, _fp,
                                         C.c_int]
+        L.ref_qwen3_last_forward_s.restype = C.c_double
         L.ref_vae_decode.argtypes = [C.c_char_p, C.c_int, _fp, C.c_int, C.c_int, C.POINTER(C.c_uint8),
                                      C.POINTER(C.c_int), C.POINTER(C.c_int)]
         L.ref_vae_decode_ex.argtypes = [C.c_char_p, C.c_int, C.c_float, C.c_float, _fp, C.c_int, C.c_int,
@@ -76,6 +77,7 @@ class RefLib:
                                         mask.ctypes.data_as(ip), seq, _f(out), seq * text_dim)
         if rc != text_dim:
             raise RuntimeError(f"reference qwen3_forward failed ({rc})")
+        self.qwen3_forward_s = self.lib.ref_qwen3_last_forward_s()
         return out.reshape(seq, text_dim)
 
     def set_threads(self, n: int):
