@@ -51,6 +51,12 @@ WEIGHT_SEED = 20261201
 METRIC = "denoise steps/s (Klein-4B 512x512, 4-step Euler)"
 UNIT = "steps/s"
 PEAKS_FALLBACK = dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=1400.0)
+# config "lora": the C2 workload with a full-coverage adapter (BFL layout: every
+# double block's img/txt fused QKV + output projection, every single block's
+# linear1 + linear2) of rank 32 at strength 1.0
+LORA_RANK = 32
+LORA_SEED = 77
+METRIC_LORA = "denoise steps/s (Klein-4B 512x512, 4-step Euler, rank-32 LoRA)"
 
 
 def parse_args(argv=None):
@@ -64,10 +70,12 @@ def parse_args(argv=None):
                     help="profiling case: a Klein-4B-shaped model truncated to DOUBLE + SINGLE blocks "
                          "(same kernels and shapes, less memory); not a benchmark number")
     ap.add_argument("--profile-out", default=None, help="write the per-kernel CUDA-event profile (JSON)")
-    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "c5b", "vae512", "vae1024", "qwen3"],
+    ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "c5b", "vae512", "vae1024", "qwen3",
+                                                     "lora"],
                     help="c2 (default) is the benchmark; the others measure the remaining SURVEY configs "
                          "on one GPU (c1 K4B 64x64 single forward, c3 K4B 1024x1024 CFG 4.0, c4 K9B "
-                         "1792x1792, c5 Z-Image 1024x1024, c5b K4B + 2 references)")
+                         "1792x1792, c5 Z-Image 1024x1024, c5b K4B + 2 references, lora: c2 with a "
+                         "rank-32 LoRA folded into the weights)")
     return ap.parse_args(argv)
 
 
@@ -206,13 +214,49 @@ def load_peaks():
     return PEAKS_FALLBACK, "fallback"
 
 
+# ----------------------------------------------------------------------------- synthetic LoRA file
+def write_bfl_lora(path, mcfg, rank, seed, std=0.02):
+    """A full-coverage adapter in the BFL key layout (diffusion_model.double_blocks.N.{img,txt}_attn.
+    {qkv,proj}.lora_A/B, diffusion_model.single_blocks.N.linear{1,2}.lora_A/B): seeded N(0, std)
+    values stored as bf16, one generator per tensor keyed by (seed, crc32(name))."""
+    import struct
+    import zlib
+    H = mcfg["num_attention_heads"] * mcfg["attention_head_dim"]
+    F = int(H * mcfg.get("mlp_ratio", 3.0))
+    shapes = []
+    for i in range(mcfg["num_layers"]):
+        for st in ("img", "txt"):
+            for what, out in (("qkv", 3 * H), ("proj", H)):
+                p = f"diffusion_model.double_blocks.{i}.{st}_attn.{what}."
+                shapes += [(p + "lora_A.weight", (rank, H)), (p + "lora_B.weight", (out, rank))]
+    for i in range(mcfg["num_single_layers"]):
+        for k, (din, dout) in ((1, (H, 3 * H + 2 * F)), (2, (H + F, H))):
+            p = f"diffusion_model.single_blocks.{i}.linear{k}."
+            shapes += [(p + "lora_A.weight", (rank, din)), (p + "lora_B.weight", (dout, rank))]
+    header, blobs, off = {}, [], 0
+    for name, shp in shapes:
+        x = std * np.random.default_rng([seed, zlib.crc32(name.encode())]).standard_normal(shp, dtype=np.float32)
+        u = x.view(np.uint32).astype(np.uint64)
+        b = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)  # round to nearest even
+        header[name] = {"dtype": "BF16", "shape": list(shp), "data_offsets": [off, off + b.nbytes]}
+        blobs.append(b)
+        off += b.nbytes
+    hj = json.dumps(header).encode()
+    hj += b" " * ((8 - len(hj) % 8) % 8)
+    with open(path, "wb") as f:
+        f.write(struct.pack("<Q", len(hj)))
+        f.write(hj)
+        for b in blobs:
+            f.write(b.tobytes())
+
+
 # ----------------------------------------------------------------------------- CPU reference arm
 class RefSample:
     """The reference's own BLAS build timed on one double + one single block of
     Klein-4B at the 512x512 shapes; a full denoising step is extrapolated as
     5 double + 20 single blocks (embedders and final layer are < 1% of it)."""
 
-    def __init__(self):
+    def __init__(self, lora: bool = False):
         from oracle import model_gen as mg
         from oracle.ref_lib import RefFlux, RefLib
         self.tmp = tempfile.TemporaryDirectory()
@@ -222,6 +266,11 @@ class RefSample:
         self.cores = len(os.sched_getaffinity(0))
         self.ref.set_threads(self.cores)
         self.rf = RefFlux(self.ref, self.tmp.name)
+        if lora:  # the runtime hooks of lora_apply inside both blocks
+            path = os.path.join(self.tmp.name, "lora.safetensors")
+            write_bfl_lora(path, cfg, LORA_RANK, LORA_SEED)
+            if not self.rf.set_lora(path, 1.0):
+                raise RuntimeError("reference lora_load failed")
         r = np.random.default_rng(7)
         H = self.rf.hidden
         self.img = r.standard_normal((IMG_H * IMG_W, H)).astype(np.float32)
@@ -249,7 +298,8 @@ def run_reference(args):
     rank, world, _ = dist_env()
     if rank != 0:
         return 0
-    rs = RefSample()
+    lora = args.config == "lora"
+    rs = RefSample(lora=lora)
     for _ in range(args.warmup):
         rs.step_seconds()
     est, wall = [], 0.0
@@ -261,28 +311,63 @@ def run_reference(args):
     step_s = statistics.mean(est)
     value = 1.0 / step_s
     line = {
-        "impl": "reference", "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "impl": "reference", "metric": METRIC_LORA if lora else METRIC, "value": value, "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1000.0 * STEPS_PER_IMAGE,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": bench_config(world),
+        "config": bench_config(world, lora),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": rs.cores, "kind": "reference",
-                         "sample": RefSample.SAMPLE, "measured_wall_s": wall},
+                         "sample": RefSample.SAMPLE + (LORA_SAMPLE if lora else ""), "measured_wall_s": wall},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
     return 0
 
 
-def bench_config(world):
-    return {"workload": "Flux.2 Klein-4B distilled, 512x512 (32x32 latent patches = 1024 image tokens) + "
+LORA_SAMPLE = (", with the rank-32 BFL adapter of both blocks applied by the reference's runtime hooks "
+               "(lora_apply after every adapted linear)")
+
+
+def bench_config(world, lora=False):
+    c = {"workload": "Flux.2 Klein-4B distilled, 512x512 (32x32 latent patches = 1024 image tokens) + "
                         "512 text tokens, 4-step Euler, guidance 1.0, batch 1 per GPU",
             "model": "klein-4b (random-init bf16 N(0,0.02))", "image_tokens": IMG_H * IMG_W,
             "text_tokens": TXT, "denoise_steps_per_image": STEPS_PER_IMAGE, "global_batch": world,
             "parallelism": f"seed-replicas x{world}",
             "l2": "no flush needed: every forward streams all 7.7 GB of weights (> 126 MB L2)"}
+    if lora:
+        c["lora"] = {"rank": LORA_RANK, "layout": "BFL (diffusion_model.*)", "scale": 1.0,
+                     "coverage": "every double block img/txt qkv + proj, every single block linear1 + linear2",
+                     "values": "seeded N(0, 0.02) bf16"}
+    return c
 
 
 # ----------------------------------------------------------------------------- our arm
+def measure_lora_fold(model, mcfg, warmup, reps=5):
+    """Write the config's adapter file, then time iris_cuda_flux_load_lora:
+    device time of its fold kernels (iris_cuda_flux_lora_stats) and the wall
+    time of the whole call (file read, f32 conversion, row/column reorder,
+    upload, restore of the base rows, fold).  Strengths alternate so every
+    call really refolds; the last call leaves strength 1.0 active."""
+    tmp = tempfile.TemporaryDirectory()
+    path = os.path.join(tmp.name, "lora.safetensors")
+    write_bfl_lora(path, mcfg, LORA_RANK, LORA_SEED)
+    for _ in range(max(warmup, 1)):
+        model.load_lora(path, 0.5)
+    dev_ms, wall_ms = [], []
+    for i in range(reps):
+        t0 = time.perf_counter()
+        n = model.load_lora(path, 1.0 if i == reps - 1 else 0.5 + 0.1 * i)
+        wall_ms.append((time.perf_counter() - t0) * 1000.0)
+        ms, nbytes = model.lora_stats()
+        dev_ms.append(ms)
+    file_bytes = os.path.getsize(path)
+    tmp.cleanup()
+    return {"adapters": n, "rank": LORA_RANK, "file_bytes": file_bytes, "device_ms": statistics.mean(dev_ms),
+            "api_wall_ms": statistics.mean(wall_ms), "bytes": nbytes,
+            "note": "bytes = weight rows read (base copy) + written (live) + adapter operands; the "
+                    "denoising steps below run with this adapter folded in"}
+
+
 def run_ours(args):
     import ctypes as C
 
@@ -301,6 +386,10 @@ def run_ours(args):
         mcfg.update(num_layers=args.blocks[0], num_single_layers=args.blocks[1])
     model = iris_cuda.Flux.random(iris_cuda.FluxConfig.from_hf(mcfg), seed=WEIGHT_SEED, std=0.02)
     stream = torch.cuda.ExternalStream(lib.iris_cuda_stream(), device=torch.device("cuda", local))
+    lora = args.config == "lora"
+    fold = None
+    if lora:
+        fold = measure_lora_fold(model, mcfg, args.warmup)
 
     rng = np.random.default_rng(500 + rank)
     txt = rng.standard_normal((TXT, K4B["joint_attention_dim"])).astype(np.float32)
@@ -427,22 +516,28 @@ def run_ours(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.blocks:
         try:
-            rs = RefSample()
+            rs = RefSample(lora=lora)
             rs.step_seconds()
             est = [rs.step_seconds()[0] for _ in range(2)]
             cpu = {"value": 1.0 / statistics.mean(est), "unit": UNIT, "cores": rs.cores,
-                   "kind": "reference", "sample": RefSample.SAMPLE}
+                   "kind": "reference", "sample": RefSample.SAMPLE + (LORA_SAMPLE if lora else "")}
             rs.close()
         except Exception as ex:  # the reference build is optional on a box without it
             cpu = {"value": None, "unit": UNIT, "cores": None, "kind": "reference",
                    "sample": f"unavailable: {type(ex).__name__}: {ex}"}
 
+    if fold is not None:
+        fold["gbs"] = fold["bytes"] / (fold["device_ms"] / 1000.0) / 1e9
+        fold["roofline"] = {"kernel": "lora_merge_kernel", "bound": "hbm", "achieved": fold["gbs"],
+                            "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": fold["gbs"] / peaks["hbm_gbs"],
+                            "peak_source": peak_src}
     line = {
-        "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+        "metric": METRIC_LORA if lora else METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "images_per_s": value / STEPS_PER_IMAGE,
-        "config": dict(bench_config(world), **({"truncated_blocks": args.blocks} if args.blocks else {})),
+        "config": dict(bench_config(world, lora), **({"truncated_blocks": args.blocks} if args.blocks else {})),
         "clocks": clocks.summary(),
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "wall_s": e2e_wall},
@@ -450,6 +545,8 @@ def run_ours(args):
         "roofline": roofline,
         "cpu_baseline": cpu,
     }
+    if fold is not None:
+        line["lora_fold"] = fold
     if rank == 0:
         print(json.dumps(line), flush=True)
     model.close()
@@ -968,7 +1065,7 @@ def main(argv=None):
         return run_vae_reference(args) if args.impl == "reference" else run_vae(args)
     if args.impl == "reference":
         return run_reference(args)
-    if args.config != "c2":
+    if args.config not in ("c2", "lora"):
         return run_config(args)
     return run_ours(args)
 

@@ -124,6 +124,31 @@ int iris_cuda_flux_read_weight(iris_cuda_flux_t *tf, const char *name, uint16_t 
 /* Bytes of HBM held by the model's weights. */
 size_t iris_cuda_flux_weight_bytes(const iris_cuda_flux_t *tf);
 
+/* LoRA.  Replaces iris_load_lora (iris.h:163; lora_load iris_lora.c:504 +
+ * iris_transformer_set_lora iris_transformer_flux.c:5131): reads an adapter
+ * file in any of the reference's four formats (XLabs, Kohya, Diffusers, BFL,
+ * detected from the tensor names like the reference) and applies it with
+ * strength `scale`, replacing any adapter loaded before.  The adapter is
+ * folded into the resident weights (W + scale * B A, once), so forwards and
+ * samplers run at the speed of the base model; the base weights it touched are
+ * kept on the device for the next load / unload.  Returns 0, or an error with
+ * the previous state unchanged when the file has no adapter matching the model
+ * (adapters whose shapes do not match are skipped, with a message on stderr). */
+int iris_cuda_flux_load_lora(iris_cuda_flux_t *tf, const char *path, float scale);
+/* Replaces iris_unload_lora (iris.h:168): back to the base weights. */
+int iris_cuda_flux_unload_lora(iris_cuda_flux_t *tf);
+/* Adapters applied by the last iris_cuda_flux_load_lora (0 without a LoRA). */
+int iris_cuda_flux_lora_adapters(const iris_cuda_flux_t *tf);
+/* Device time of the last load's fold kernels and the bytes they moved. */
+int iris_cuda_flux_lora_stats(const iris_cuda_flux_t *tf, double *fold_ms, double *fold_bytes);
+/* Host only (no device needed): the adapters of a LoRA file that match a model
+ * of this shape (n_double / n_single blocks, hidden and MLP widths), like the
+ * reference's "LoRA: loaded N adapters" report (iris_lora.c:276).  Returns
+ * their number (a fused Q|K|V counts once) or an error; per_kind (5 ints, may
+ * be NULL) receives the format (1 XLabs, 2 Kohya, 3 Diffusers, 4 BFL) and the
+ * counts of Q/K/V, output-projection, single linear1 and linear2 adapters. */
+int iris_cuda_lora_probe(const char *path, int n_double, int n_single, int hidden, int mlp, int *per_kind);
+
 /* One denoising step: velocity v(z, t, ctx), host buffers in and out.
  * Replaces iris_transformer_forward (iris_transformer_flux.c:3939); returns
  * malloc'd NCHW [C, h, w] or NULL. */

@@ -88,6 +88,7 @@ typedef struct {
 } st_model_t;
 
 int st_open_dir(st_model_t *m, const char *transformer_dir);
+int st_open_file(st_model_t *m, const char *path);
 void st_close(st_model_t *m);
 const st_tensor_t *st_find(const st_model_t *m, const char *name);
 /* convert a tensor to bf16 bits into out (numel elements); returns 0 on success */

@@ -230,6 +230,12 @@ cudaError_t iris_launch_interleave_gate_up(void *dst, const void *src, int F, in
                                            cudaStream_t stream);
 cudaError_t iris_launch_copy_rows_bf16(void *dst, int ldd, const void *src, int lds, int rows,
                                        int cols, cudaStream_t stream);
+/* LoRA fold: w[rowmap[i], 0:cols] = bf16(w0[rowmap[i], 0:cols] + scale * (B A)[i]) for
+ * i < nrows; B f32 [nrows, rank], A f32 [rank, cols]; w / w0 bf16 with row stride ld
+ * (may alias); cols and ld multiples of 8, w and w0 16-byte aligned. */
+cudaError_t iris_launch_lora_merge(void *w, const void *w0, int ld, const float *B, const float *A,
+                                   const int *rowmap, int nrows, int cols, int rank, float scale,
+                                   cudaStream_t stream);
 
 /* ------------------------------------------------------------------ text encoder (Qwen3) */
 /* x[s] = f32 of table[ids[s]] (bf16 [vocab, H]); ids outside [0, vocab) -> zeros */

@@ -172,6 +172,13 @@ static int open_file(st_model_t *m, const char *path) {
     m->nfiles++;
     int rc = parse_header(m, f, hdr);
     free(hdr);
+    /* a tensor whose data runs past the end of the file (truncated download) fails the open */
+    for (int i = 0; rc == 0 && i < m->ntensors; i++) {
+        const st_tensor_t *t = &m->tensors[i];
+        size_t avail = m->sizes[f] - m->data_start[f];  /* data_start <= size checked above */
+        if (t->file == f && (t->offset > avail || t->nbytes > avail - t->offset))
+            rc = -1;
+    }
     return rc;
 }
 
@@ -234,6 +241,13 @@ int st_open_dir(st_model_t *m, const char *dir) {
     return 0;
 }
 
+/* Opens one .safetensors file (a LoRA adapter, a single-file model). */
+int st_open_file(st_model_t *m, const char *path) {
+    memset(m, 0, sizeof(*m));
+    if (open_file(m, path) != 0) { st_close(m); return -1; }
+    return 0;
+}
+
 void st_close(st_model_t *m) {
     for (int i = 0; i < m->nfiles; i++) munmap(m->maps[i], m->sizes[i]);
     free(m->tensors);
@@ -274,7 +288,7 @@ static float f16_to_f32(uint16_t h) {
 }
 
 int st_read_bf16(const st_model_t *m, const st_tensor_t *t, uint16_t *out, size_t numel) {
-    if (st_numel(t) != numel) return -1;
+    if (st_numel(t) != numel || t->nbytes != numel * (t->dtype == ST_F32 ? 4 : 2)) return -1;
     const uint8_t *d = st_data(m, t);
     if (!d) return -1;
     if (t->dtype == ST_BF16) { memcpy(out, d, numel * 2); return 0; }
@@ -292,7 +306,7 @@ int st_read_bf16(const st_model_t *m, const st_tensor_t *t, uint16_t *out, size_
 }
 
 int st_read_f32(const st_model_t *m, const st_tensor_t *t, float *out, size_t numel) {
-    if (st_numel(t) != numel) return -1;
+    if (st_numel(t) != numel || t->nbytes != numel * (t->dtype == ST_F32 ? 4 : 2)) return -1;
     const uint8_t *d = st_data(m, t);
     if (!d) return -1;
     if (t->dtype == ST_F32) { memcpy(out, d, numel * 4); return 0; }

@@ -95,6 +95,11 @@ SIGNATURES = {
     "iris_cuda_flux_get_config": (C.c_int, [C.c_void_p, C.POINTER(FluxConfig)]),
     "iris_cuda_flux_read_weight": (C.c_int, [C.c_void_p, C.c_char_p, _u16p, C.c_size_t]),
     "iris_cuda_flux_weight_bytes": (C.c_size_t, [C.c_void_p]),
+    "iris_cuda_flux_load_lora": (C.c_int, [C.c_void_p, C.c_char_p, C.c_float]),
+    "iris_cuda_flux_unload_lora": (C.c_int, [C.c_void_p]),
+    "iris_cuda_flux_lora_adapters": (C.c_int, [C.c_void_p]),
+    "iris_cuda_flux_lora_stats": (C.c_int, [C.c_void_p, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
+    "iris_cuda_lora_probe": (C.c_int, [C.c_char_p, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int)]),
     "iris_cuda_transformer_forward": (C.c_void_p, [C.c_void_p, _fp, C.c_int, C.c_int, _fp, C.c_int,
                                                    C.c_float]),
     "iris_cuda_transformer_forward_with_multi_refs": (C.c_void_p, [C.c_void_p, _fp, C.c_int, C.c_int,
@@ -302,6 +307,27 @@ class Flux:
             raise IrisCudaError(last_error())
         return out.reshape(shape)
 
+    def load_lora(self, path: str, scale: float = 1.0) -> int:
+        """iris_load_lora: fold a LoRA file (XLabs / Kohya / Diffusers / BFL) into
+        the weights at strength `scale`; returns the number of adapters applied."""
+        if lib().iris_cuda_flux_load_lora(self.h, path.encode(), float(scale)):
+            raise IrisCudaError(last_error())
+        return lib().iris_cuda_flux_lora_adapters(self.h)
+
+    def unload_lora(self) -> None:
+        if lib().iris_cuda_flux_unload_lora(self.h):
+            raise IrisCudaError(last_error())
+
+    @property
+    def lora_adapters(self) -> int:
+        return lib().iris_cuda_flux_lora_adapters(self.h)
+
+    def lora_stats(self) -> tuple[float, float]:
+        """(device ms, bytes moved) of the last LoRA fold."""
+        ms, nb = C.c_double(), C.c_double()
+        lib().iris_cuda_flux_lora_stats(self.h, C.byref(ms), C.byref(nb))
+        return ms.value, nb.value
+
     def run_block(self, kind: int, idx: int, hidden: np.ndarray, txt_seq: int, img_h: int, img_w: int,
                   t: float) -> np.ndarray:
         hid = np.ascontiguousarray(hidden, np.float32).copy()
@@ -398,6 +424,19 @@ def comm_init_group(exchange, rank: int, world: int, group_size: int) -> tuple:
     ids = exchange(mine)
     comm_init(ids[group[0]], len(group), group.index(rank))
     return group, group.index(rank)
+
+
+LORA_FORMATS = {1: "xlabs", 2: "kohya", 3: "diffusers", 4: "bfl"}
+
+
+def lora_probe(path: str, n_double: int, n_single: int, hidden: int, mlp: int) -> dict:
+    """Host-only: adapters of a LoRA file matching a model of this shape."""
+    k = (C.c_int * 5)()
+    n = lib().iris_cuda_lora_probe(path.encode(), n_double, n_single, hidden, mlp, k)
+    if n < 0:
+        raise IrisCudaError(last_error())
+    return {"format": LORA_FORMATS[k[0]], "adapters": n, "qkv": k[1], "proj": k[2], "linear1": k[3],
+            "linear2": k[4]}
 
 
 def official_schedule(steps: int, seq: int) -> np.ndarray:

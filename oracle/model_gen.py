@@ -165,6 +165,81 @@ def flux_weights_bits(cfg: dict, seed: int, std: float = 0.02, norm_mode: str = 
 
 
 # ---------------------------------------------------------------------------
+# Flux LoRA adapters (the four key layouts lora_load reads, iris_lora.c:240-486)
+# ---------------------------------------------------------------------------
+
+LORA_FORMATS = ("xlabs", "kohya", "diffusers", "bfl")
+
+
+def flux_lora_specs(cfg: dict, fmt: str, rank: int, singles: bool = True,
+                    prefix: str = "diffusion_model", single_out: str = "to_out",
+                    blocks: tuple | None = None) -> list[tuple[str, tuple]]:
+    """(name, shape) of every adapter tensor of a full-coverage LoRA.
+
+    fmt: "xlabs" (double blocks only, fused Q|K|V), "kohya", "bfl" (fused
+    Q|K|V, single linear1/linear2), "diffusers" (separate Q/K/V, single
+    to_qkv_mlp_proj and `single_out` = "to_out" or the fallback "proj_out").
+    blocks: double-block indices to cover (all by default)."""
+    d = flux_dims(cfg)
+    H, F, r = d["hidden"], d["mlp"], rank
+    dbl = range(d["n_double"]) if blocks is None else blocks
+    out = []
+    for i in dbl:
+        for st, n in (("img", 1), ("txt", 2)):
+            if fmt == "xlabs":
+                p = f"double_blocks.{i}.processor."
+                out += [(p + f"qkv_lora{n}.down.weight", (r, H)), (p + f"qkv_lora{n}.up.weight", (3 * H, r)),
+                        (p + f"proj_lora{n}.down.weight", (r, H)), (p + f"proj_lora{n}.up.weight", (H, r))]
+            elif fmt == "kohya":
+                for what, o in (("qkv", 3 * H), ("proj", H)):
+                    p = f"lora_unet_double_blocks_{i}_{st}_attn_{what}."
+                    out += [(p + "lora_down.weight", (r, H)), (p + "lora_up.weight", (o, r))]
+            elif fmt == "bfl":
+                for what, o in (("qkv", 3 * H), ("proj", H)):
+                    p = f"{prefix}.double_blocks.{i}.{st}_attn.{what}."
+                    out += [(p + "lora_A.weight", (r, H)), (p + "lora_B.weight", (o, r))]
+            else:
+                names = (("to_q", "to_k", "to_v", "to_out.0") if st == "img"
+                         else ("add_q_proj", "add_k_proj", "add_v_proj", "to_add_out"))
+                for nm in names:
+                    p = f"transformer.transformer_blocks.{i}.attn.{nm}."
+                    out += [(p + "lora_A.weight", (r, H)), (p + "lora_B.weight", (H, r))]
+    if singles and fmt != "xlabs":
+        for i in range(d["n_single"]):
+            for k, (din, dout) in ((1, (H, 3 * H + 2 * F)), (2, (H + F, H))):
+                if fmt == "kohya":
+                    p = f"lora_unet_single_blocks_{i}_linear{k}."
+                    dn, up = p + "lora_down.weight", p + "lora_up.weight"
+                elif fmt == "bfl":
+                    p = f"{prefix}.single_blocks.{i}.linear{k}."
+                    dn, up = p + "lora_A.weight", p + "lora_B.weight"
+                else:
+                    p = (f"transformer.single_transformer_blocks.{i}.attn.to_qkv_mlp_proj." if k == 1 else
+                         f"transformer.single_transformer_blocks.{i}." +
+                         ("attn.to_out." if single_out == "to_out" else "proj_out."))
+                    dn, up = p + "lora_A.weight", p + "lora_B.weight"
+                out += [(dn, (r, din)), (up, (dout, r))]
+    return out
+
+
+def make_flux_lora(path: str, cfg: dict, fmt: str, rank: int = 8, seed: int = 0, std: float = 0.06,
+                   dtype: str = "bf16", **kw) -> dict[str, np.ndarray]:
+    """Write a seeded LoRA file; returns {name: f32 values as stored}."""
+    tensors, vals = {}, {}
+    for name, shp in flux_lora_specs(cfg, fmt, rank, **kw):
+        rng = np.random.default_rng([seed, zlib.crc32(name.encode())])
+        x = std * rng.standard_normal(shp, dtype=np.float32)
+        if dtype == "bf16":
+            tensors[name] = f32_to_bf16_bits(x)
+            vals[name] = bf16_bits_to_f32(tensors[name])
+        else:
+            tensors[name] = x
+            vals[name] = x
+    write_safetensors(path, tensors)
+    return vals
+
+
+# ---------------------------------------------------------------------------
 # Z-Image S3-DiT
 # ---------------------------------------------------------------------------
 

@@ -16,6 +16,8 @@
  *   ref_flux_double_block    -> double_block_forward                (:2366)
  *   ref_flux_single_block    -> single_block_forward                (:3761)
  *   ref_flux_rope_img/_txt   -> compute_rope_2d / compute_rope_text (:897, :1055)
+ *   ref_flux_set_lora        -> lora_load + iris_transformer_set_lora (iris_lora.c:504, :5131)
+ *   ref_lora_get             -> one adapter of lora_load's table     (iris_lora.h:28-49)
  *   ref_sample_euler(_cfg)   -> iris_sample_euler / _cfg            (iris_sample.c:313, :717)
  *   ref_init_noise           -> iris_init_noise                     (iris_sample.c:1146)
  *   ref_official_schedule    -> iris_official_schedule              (iris_sample.c:171)
@@ -113,6 +115,43 @@ int ref_flux_forward_refs(void *p, const float *latent, int h, int w,
     memcpy(out, v, (size_t)tf->latent_channels * h * w * sizeof(float));
     free(v);
     return 0;
+}
+
+/* LoRA: lora_load (iris_lora.c:504) + iris_transformer_set_lora (:5131), the
+ * body of iris_load_lora (iris.c:460).  Returns 0, -1 when nothing loaded. */
+int ref_flux_set_lora(void *p, const char *path, float scale) {
+    iris_transformer_t *tf = (iris_transformer_t *)p;
+    lora_state_t *l = lora_load(path, tf->num_double_layers, tf->num_single_layers, tf->hidden_size, scale);
+    if (!l) return -1;
+    iris_transformer_set_lora(tf, l);
+    return 0;
+}
+
+void ref_flux_clear_lora(void *p) { iris_transformer_set_lora((iris_transformer_t *)p, NULL); }
+
+/* One adapter of the table lora_load builds: kind 0..9 = double img q, k, v,
+ * proj, txt q, k, v, proj, single linear1, linear2.  dims = {rank, in, out};
+ * A / B copied when they fit.  Returns 1 present, 0 absent, -1 load failed. */
+int ref_lora_get(const char *path, int n_double, int n_single, int hidden, int kind, int block,
+                 int *dims, float *A, size_t a_cap, float *B, size_t b_cap) {
+    lora_state_t *l = lora_load(path, n_double, n_single, hidden, 1.0f);
+    if (!l) return -1;
+    lora_adapter_t *tab[10] = {l->double_img_q, l->double_img_k, l->double_img_v, l->double_img_proj,
+                               l->double_txt_q, l->double_txt_k, l->double_txt_v, l->double_txt_proj,
+                               l->single_linear1, l->single_linear2};
+    int rc = 0;
+    if (kind >= 0 && kind < 10 && block >= 0 && block < (kind < 8 ? n_double : n_single)) {
+        lora_adapter_t *a = &tab[kind][block];
+        if (a->lora_A) {
+            rc = 1;
+            dims[0] = a->rank; dims[1] = a->in_dim; dims[2] = a->out_dim;
+            size_t na = (size_t)a->rank * a->in_dim, nb = (size_t)a->out_dim * a->rank;
+            if (na <= a_cap) memcpy(A, a->lora_A, na * sizeof(float));
+            if (nb <= b_cap) memcpy(B, a->lora_B, nb * sizeof(float));
+        }
+    }
+    lora_free(l);
+    return rc;
 }
 
 void ref_flux_temb(void *p, float t, float *t_emb) {

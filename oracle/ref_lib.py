@@ -65,6 +65,26 @@ class RefLib:
                                      C.POINTER(C.c_int), C.POINTER(C.c_int)]
         L.ref_vae_decode_ex.argtypes = [C.c_char_p, C.c_int, C.c_float, C.c_float, _fp, C.c_int, C.c_int,
                                         C.POINTER(C.c_uint8), C.POINTER(C.c_int), C.POINTER(C.c_int)]
+        L.ref_flux_set_lora.argtypes = [C.c_void_p, C.c_char_p, C.c_float]
+        L.ref_flux_clear_lora.argtypes = [C.c_void_p]
+        L.ref_lora_get.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
+                                   C.POINTER(C.c_int), _fp, C.c_size_t, _fp, C.c_size_t]
+
+    def lora_get(self, path: str, n_double: int, n_single: int, hidden: int, kind: int, block: int,
+                 cap: int = 1 << 22):
+        """(A, B) of one adapter of the reference's lora_load table, None if absent,
+        raises if lora_load failed."""
+        dims = (C.c_int * 3)()
+        a = np.zeros(cap, np.float32)
+        b = np.zeros(cap, np.float32)
+        rc = self.lib.ref_lora_get(path.encode(), n_double, n_single, hidden, kind, block, dims,
+                                   _f(a), cap, _f(b), cap)
+        if rc < 0:
+            raise RuntimeError(f"reference lora_load failed on {path}")
+        if rc == 0:
+            return None
+        r, i, o = dims
+        return a[:r * i].reshape(r, i).copy(), b[:o * r].reshape(o, r).copy()
 
     def qwen3_forward(self, model_dir: str, ids, mask, text_dim: int, zimage: bool = False) -> np.ndarray:
         """Reference CPU text encoder (qwen3_model_load + qwen3_forward) -> [seq, text_dim]."""
@@ -131,6 +151,12 @@ class RefFlux:
         rc = self.ref.lib.ref_flux_forward(self.h, _f(lat), h, w, _f(tx), tx.shape[0], t, _f(out))
         assert rc == 0
         return out
+
+    def set_lora(self, path: str, scale: float) -> bool:
+        return self.ref.lib.ref_flux_set_lora(self.h, path.encode(), scale) == 0
+
+    def clear_lora(self):
+        self.ref.lib.ref_flux_clear_lora(self.h)
 
     def forward_refs(self, latent, refs, txt, t):
         c, h, w = latent.shape

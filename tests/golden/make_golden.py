@@ -2,7 +2,8 @@
 
 Run where the reference tree exists (it is read-only and absent on GPU boxes):
 
-    make -C oracle && python tests/golden/make_golden.py
+    make -C oracle && python tests/golden/make_golden.py        # everything
+    python tests/golden/make_golden.py lora                      # lora_fixture.npz only
 
 Each fixture is produced by the reference's own C code, compiled from its
 unmodified sources by oracle/Makefile and driven through
@@ -116,7 +117,30 @@ def sampler_case(ref: RefLib) -> dict:
     return out
 
 
+REF_TREE = os.environ.get("IRIS_REFERENCE", "/root/reference")
+
+
+def lora_fixture() -> dict:
+    """The reference's own LoRA golden fixture (debug/fixtures/lora: an MLX
+    LoRALinear export, rank 4, dim 8, seq 5, checked by debug/test_lora.c),
+    stored as arrays: every tensor of lora.safetensors under its name, the
+    input x [5, 8] and the goldens (to_q delta [5, 8], single linear1 delta
+    [5, 12], single linear2 delta [5, 8])."""
+    from oracle.lora_oracle import read_safetensors
+    d = os.path.join(REF_TREE, "debug", "fixtures", "lora")
+    out = {f"t:{k}": v for k, v in read_safetensors(os.path.join(d, "lora.safetensors")).items()}
+    out["x"] = np.fromfile(os.path.join(d, "x.bin"), "<f4").reshape(5, 8)
+    out["golden"] = np.fromfile(os.path.join(d, "golden.bin"), "<f4").reshape(5, 8)
+    out["golden_single1"] = np.fromfile(os.path.join(d, "golden_single1.bin"), "<f4").reshape(5, 12)
+    out["golden_single2"] = np.fromfile(os.path.join(d, "golden_single2.bin"), "<f4").reshape(5, 8)
+    return out
+
+
 def main():
+    if sys.argv[1:] == ["lora"]:
+        np.savez_compressed(os.path.join(OUT, "lora_fixture.npz"), **lora_fixture())
+        print("wrote lora_fixture")
+        return
     ref = RefLib("generic")
     for name, spec in FLUX_CASES.items():
         data = flux_case(ref, name, spec)
@@ -128,6 +152,8 @@ def main():
         print("wrote", name, {k: v.shape for k, v in data.items() if k != "meta"})
     np.savez_compressed(os.path.join(OUT, "sampler.npz"), **sampler_case(ref))
     print("wrote sampler")
+    np.savez_compressed(os.path.join(OUT, "lora_fixture.npz"), **lora_fixture())
+    print("wrote lora_fixture")
 
 
 if __name__ == "__main__":

@@ -77,6 +77,12 @@ def run_tp(rank, world, out_dir, exchange):
         txt_h = np.random.default_rng(seed + 201).standard_normal((txt, dims["hidden"])).astype(np.float32)
         hid = np.concatenate([txt_h, img_h])
         b_full = [full.run_block(k, 0, hid, txt, h, wd, 0.7) for k in (0, 1)]
+        # a LoRA folded into the shards' rows / columns (fused or separate Q|K|V,
+        # interleaved gate/up rows, split output-projection inputs)
+        lp = os.path.join(out_dir, f"{name}_lora_r{rank}.safetensors")
+        mg.make_flux_lora(lp, cfg, "bfl" if name == "tp_cfg" else "diffusers", rank=8, seed=9, std=0.15)
+        full.load_lora(lp, 0.8)
+        v_full_lora = full.forward(lat, ctx, 0.7)
         full.close()
         shard = iris_cuda.Flux.load(d, tp_rank=r, tp_size=world)
         entry = {}
@@ -93,6 +99,8 @@ def run_tp(rank, world, out_dir, exchange):
             entry["v_t1.0_vs_golden"] = rel_l2(shard.forward(lat, ctx, 1.0), g["v_t1.0"])
             z = shard.sample_euler(g["z0"], ctx, g["sched4"])
             entry["z4_vs_golden"] = rel_l2(z, g["z4"])
+        shard.load_lora(lp, 0.8)
+        entry["lora_v_t0.7_vs_full"] = rel_l2(shard.forward(lat, ctx, 0.7), v_full_lora)
         entry["weight_bytes"] = shard.weight_bytes()
         shard.close()
         res[name] = entry
