@@ -528,7 +528,9 @@ def run_ours(args):
 
     if fold is not None:
         fold["gbs"] = fold["bytes"] / (fold["device_ms"] / 1000.0) / 1e9
-        fold["roofline"] = {"kernel": "lora_merge_kernel", "bound": "hbm", "achieved": fold["gbs"],
+        fold["roofline"] = {"kernel": "LoRA fold: gemm_tc2_kernel<fold> (tcgen05, K = rank padded to 64, "
+                                      "IRIS_EPI_LORA_FOLD epilogue) + 2 operand prep kernels per adapter",
+                            "bound": "hbm", "achieved": fold["gbs"],
                             "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": fold["gbs"] / peaks["hbm_gbs"],
                             "peak_source": peak_src}
     line = {

@@ -223,6 +223,60 @@ __device__ __forceinline__ void epi_f32_block(const IrisGemmParams& p, int g, fl
   __syncwarp();  // the stage is rewritten by the next block
 }
 
+// IRIS_EPI_LORA_FOLD, 32-column blocks j0..j1-1 of a 128-column chunk:
+// out = bf16(w0 + scale * acc) at each row's target row.  The warp's 32 x 32
+// accumulator block is transposed through its shared staging tile so that
+// four lanes cover one row's 64 contiguous bytes (every base-weight and output
+// sector fully used, 8 rows per access), and the base values of all the
+// chunk's blocks are loaded before the first accumulator block is read.
+__device__ __forceinline__ void epi_fold_chunk(const IrisGemmParams& p, uint32_t taddr, int row, bool valid,
+                                               int col0, int j0, int j1, float* stage, int lane) {
+  const int my_drow = valid ? __ldg(p.fold_rows + row) : -1;
+  const int rr = lane >> 2, c8 = (lane & 3) * 8;
+  int dr[4];
+#pragma unroll
+  for (int it = 0; it < 4; it++) dr[it] = __shfl_sync(0xffffffffu, my_drow, it * 8 + rr);
+  const __nv_bfloat16* w0 = static_cast<const __nv_bfloat16*>(p.fold_w0);
+  __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
+  uint4 base[16];
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    if (j < j0 || j >= j1) continue;
+#pragma unroll
+    for (int it = 0; it < 4; it++)
+      if (dr[it] >= 0)
+        base[4 * j + it] = *reinterpret_cast<const uint4*>(w0 + (size_t)dr[it] * p.ldo + col0 + 32 * j + c8);
+  }
+#pragma unroll
+  for (int j = 0; j < 4; j++) {
+    if (j < j0 || j >= j1) continue;
+    float v[32];
+    iris::tmem_ld32(taddr + 32 * j, v);  // warp-collective: every lane
+    float4* st = reinterpret_cast<float4*>(stage + lane * EPI_LD);
+#pragma unroll
+    for (int q = 0; q < 8; q++) st[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+    __syncwarp();
+#pragma unroll
+    for (int it = 0; it < 4; it++) {
+      if (dr[it] < 0) continue;
+      const float* a = stage + (it * 8 + rr) * EPI_LD + c8;
+      const float4 a0 = *reinterpret_cast<const float4*>(a), a1 = *reinterpret_cast<const float4*>(a + 4);
+      const float acc[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+      const uint4 b = base[4 * j + it];
+      const uint32_t u[4] = {b.x, b.y, b.z, b.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const float lo = __uint_as_float(u[q] << 16) + p.fold_scale * acc[2 * q];
+        const float hi = __uint_as_float(u[q] & 0xFFFF0000u) + p.fold_scale * acc[2 * q + 1];
+        o[q] = pack_bf16(lo, hi);
+      }
+      *reinterpret_cast<uint4*>(out + (size_t)dr[it] * p.ldo + col0 + 32 * j + c8) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+    __syncwarp();  // the stage is rewritten by the next block
+  }
+}
+
 __device__ __forceinline__ void epi_plain_chunk(const IrisGemmParams& p, uint32_t taddr, int g,
                                                 int row, int row_local, bool valid, int col0, float* stage,
                                                 int lane, int rows_valid, int split, int j0 = 0, int j1 = 4) {
@@ -299,6 +353,14 @@ __device__ __forceinline__ void epi_plain_chunk(const IrisGemmParams& p, uint32_
 // (the weights streaming through L2 would otherwise leave it a DRAM miss
 // right when the tensor pipe waits for the accumulator).
 __device__ __forceinline__ void prefetch_resid_row(const IrisGemmParams& p, int g, int row_local, int n0) {
+  if (p.mode == IRIS_EPI_LORA_FOLD) {  // the base weight row segment the fold reads
+    if (row_local >= p.rows[g]) return;
+    const __nv_bfloat16* w = static_cast<const __nv_bfloat16*>(p.fold_w0) +
+                             (size_t)__ldg(p.fold_rows + p.row0[g] + row_local) * p.ldo + n0;
+    const int bytes = min(p.bn, p.N - n0) * 2;
+    asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(w), "r"(bytes) : "memory");
+    return;
+  }
   if (p.mode != IRIS_EPI_RESID_GATE || p.resid_store || row_local >= p.rows[g]) return;
   const float* a = reinterpret_cast<const float*>(p.out) + (size_t)(p.row0[g] + row_local) * p.ldo + n0;
   const int bytes = min(p.bn, p.N - n0) * 4;
@@ -310,9 +372,25 @@ __device__ __forceinline__ void prefetch_resid_row(const IrisGemmParams& p, int 
 // epilogue warps per lane quarter (halves = 2), warp `half` takes the
 // 128-column chunk `half` of a 256-wide tile, or half of the 32-column blocks
 // of a 128-wide one (a Q/K head's RMSNorm needs its whole chunk in one warp).
+// kFold: the IRIS_EPI_LORA_FOLD instantiation of the kernels (its epilogue
+// keeps a whole base-weight chunk in registers; compiled apart so that the
+// other epilogues keep their register allocation).
+template <bool kFold>
 __device__ __forceinline__ void epi_tile(const IrisGemmParams& p, uint32_t taddr, int g, int row, int row_local,
                                          bool valid, int n0, float* stage, int lane, int rows_valid,
                                          int split = 0, int half = 0, int halves = 1) {
+  if constexpr (kFold) {
+    const int nchunks = p.bn / 128;
+    for (int c = 0; c < nchunks; c++) {
+      const int col0 = n0 + c * 128;
+      if (col0 >= p.N) break;
+      if (halves == 2 && nchunks == 2 && c != half) continue;
+      if (halves == 2 && nchunks == 1)
+        epi_fold_chunk(p, taddr + c * 128, row, valid, col0, 2 * half, 2 * half + 2, stage, lane);
+      else epi_fold_chunk(p, taddr + c * 128, row, valid, col0, 0, 4, stage, lane);
+    }
+    return;
+  }
   bool swiglu_tile = (p.mode == IRIS_EPI_SWIGLU) || (p.mode == IRIS_EPI_SINGLE && n0 >= p.swiglu_base);
   if (swiglu_tile) {
     if (halves == 2) epi_swiglu_tile(p, taddr, row, valid, n0, 2 * half, 2 * half + 2);
@@ -337,6 +415,7 @@ __device__ __forceinline__ void epi_tile(const IrisGemmParams& p, uint32_t taddr
   }
 }
 
+template <bool kFold>
 __global__ void __launch_bounds__(NUM_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -490,7 +569,7 @@ gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
       int row = p.row0[g] + row_local;
       uint32_t taddr = tmem_base + buf * 256 + ((uint32_t)(quarter * 32) << 16);
       const int rows_valid = min(32, max(0, p.rows[g] - (row_local - lane)));
-      epi_tile(p, taddr, g, row, row_local, valid, n0, stage, lane, rows_valid, u % nsplit);
+      epi_tile<kFold>(p, taddr, g, row, row_local, valid, n0, stage, lane, rows_valid, u % nsplit);
       iris::tc_fence_before();
       iris::mbar_arrive(&bars->tempty[buf]);
     }
@@ -520,6 +599,12 @@ constexpr int BM2 = 256;
 constexpr int STAGES2 = 5;
 constexpr int STAGE2_BYTES = A_BYTES + 128 * BK * 2;  // 32 KB
 constexpr int SMEM2_BYTES = STAGES2 * STAGE2_BYTES + 1024 + EPI_WARPS2 * EPI_WARP_BYTES + 1024;
+// IRIS_EPI_LORA_FOLD instantiation: 2 stages, and per epilogue warp a landing
+// buffer for the next tile's base-weight block (32 rows x 128 columns bf16)
+constexpr int FOLD_STAGES2 = 2;
+constexpr int FOLD_LANDING_BYTES = 32 * 128 * 2;
+constexpr int FOLD_SMEM2_BYTES = FOLD_STAGES2 * STAGE2_BYTES + 1024 + EPI_WARPS2 * EPI_WARP_BYTES +
+                                 EPI_WARPS2 * FOLD_LANDING_BYTES + 1024;
 
 struct Bars2 {
   uint64_t full[STAGES2];   // even CTA: both CTAs' tiles of the stage landed (2 arrivals + bytes)
@@ -531,11 +616,110 @@ struct Bars2 {
   int abort;
 };
 
+// Fold epilogue of one pair-kernel warp (rows quarter*32.. of this CTA's 128,
+// column half `half` of each 256-wide tile).  The base-weight block of the
+// next tile is copied into this warp's landing buffer (cp.async, 16 bytes per
+// lane and piece) while the current tile is combined, so every SM keeps
+// 8 x 8 KB of base-weight reads in flight.  The pieces are laid out so that
+// each lane reads back exactly the slots it copied: no cross-lane hazard.
+__device__ __forceinline__ void fold_issue(const IrisGemmParams& p, uint4* landing, int t, int mt0, int mtot,
+                                           uint32_t rank, int quarter, int half, int lane, int* dr) {
+  int g, ml, n0;
+  tile_coords(p, t, mt0, mtot, g, ml, n0);
+  const int row_local = ml * BM2 + 128 * (int)rank + quarter * 32 + lane;
+  const int my = row_local < p.rows[g] ? __ldg(p.fold_rows + p.row0[g] + row_local) : -1;
+  const int rr = lane >> 2, c8 = (lane & 3) * 8, col0 = n0 + half * 128;
+#pragma unroll
+  for (int it = 0; it < 4; it++) dr[it] = __shfl_sync(0xffffffffu, my, it * 8 + rr);
+  const __nv_bfloat16* w0 = static_cast<const __nv_bfloat16*>(p.fold_w0);
+#pragma unroll
+  for (int j = 0; j < 4; j++)
+#pragma unroll
+    for (int it = 0; it < 4; it++)
+      if (dr[it] >= 0) {
+        const void* src = w0 + (size_t)dr[it] * p.ldo + col0 + 32 * j + c8;
+        asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(iris::smem_u32(landing + (4 * j + it) * 32 + lane)),
+                     "l"(src) : "memory");
+      }
+  asm volatile("cp.async.commit_group;" ::: "memory");
+}
+
+__device__ __forceinline__ void fold_epilogue_pair(const IrisGemmParams& p, uint64_t* tfull, uint32_t tempty_c0,
+                                                   uint32_t tempty_c1, volatile int* abort_flag, uint32_t tmem_base,
+                                                   float* stage, uint4* landing, int pair, int npairs, int total,
+                                                   int mt0, int mtot, uint32_t rank, int quarter, int half,
+                                                   int lane) {
+  int dr[4], drn[4];
+  if (pair < total) fold_issue(p, landing, pair, mt0, mtot, rank, quarter, half, lane, drn);
+  const int rr = lane >> 2, c8 = (lane & 3) * 8;
+  int it = 0;
+  for (int t = pair; t < total; t += npairs, it++) {
+    const int buf = it & 1;
+    const uint32_t use = (uint32_t)(it >> 1);
+    if (!iris::mbar_wait(&tfull[buf], use & 1, abort_flag, p.status, IRIS_DEV_ERR_GEMM_EPILOGUE)) break;
+    iris::tc_fence_after();
+    // this tile's base block: landed copies -> registers, then the next tile's copies
+    asm volatile("cp.async.wait_group 0;" ::: "memory");
+    uint4 base[16];
+#pragma unroll
+    for (int q = 0; q < 16; q++) base[q] = landing[q * 32 + lane];
+#pragma unroll
+    for (int q = 0; q < 4; q++) dr[q] = drn[q];
+    if (t + 2 * npairs < total) {  // the tile after next: its base rows into L2
+      int g2, ml2, n02;
+      tile_coords(p, t + 2 * npairs, mt0, mtot, g2, ml2, n02);
+      if (half == 0) prefetch_resid_row(p, g2, ml2 * BM2 + 128 * (int)rank + quarter * 32 + lane, n02);
+    }
+    if (t + npairs < total) fold_issue(p, landing, t + npairs, mt0, mtot, rank, quarter, half, lane, drn);
+    int g, ml, n0;
+    tile_coords(p, t, mt0, mtot, g, ml, n0);
+    const int col0 = n0 + half * 128;
+    const uint32_t taddr = tmem_base + buf * 256 + ((uint32_t)(quarter * 32) << 16) + half * 128;
+    __nv_bfloat16* out = static_cast<__nv_bfloat16*>(p.out);
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      float v[32];
+      iris::tmem_ld32(taddr + 32 * j, v);
+      float4* st = reinterpret_cast<float4*>(stage + lane * EPI_LD);
+#pragma unroll
+      for (int q = 0; q < 8; q++) st[q] = make_float4(v[4 * q], v[4 * q + 1], v[4 * q + 2], v[4 * q + 3]);
+      __syncwarp();
+#pragma unroll
+      for (int r = 0; r < 4; r++) {
+        if (dr[r] < 0) continue;
+        const float* a = stage + (r * 8 + rr) * EPI_LD + c8;
+        const float4 a0 = *reinterpret_cast<const float4*>(a), a1 = *reinterpret_cast<const float4*>(a + 4);
+        const float acc[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+        const uint4 b = base[4 * j + r];
+        const uint32_t u[4] = {b.x, b.y, b.z, b.w};
+        uint32_t o[4];
+#pragma unroll
+        for (int q = 0; q < 4; q++) {
+          const float lo = __uint_as_float(u[q] << 16) + p.fold_scale * acc[2 * q];
+          const float hi = __uint_as_float(u[q] & 0xFFFF0000u) + p.fold_scale * acc[2 * q + 1];
+          o[q] = pack_bf16(lo, hi);
+        }
+        *reinterpret_cast<uint4*>(out + (size_t)dr[r] * p.ldo + col0 + 32 * j + c8) =
+            make_uint4(o[0], o[1], o[2], o[3]);
+      }
+      __syncwarp();  // the stage is rewritten by the next block
+    }
+    iris::tc_fence_before();
+    __syncwarp();
+    if (lane == 0) iris::mbar_arrive_cluster(buf ? tempty_c1 : tempty_c0);
+  }
+  asm volatile("cp.async.wait_group 0;" ::: "memory");  // no copy lands after the CTA has moved on
+}
+
+template <bool kFold>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS2, 1)
 gemm_tc2_kernel(const __grid_constant__ IrisGemmParams p) {
+  // the fold's K is one block: two stages free the shared memory for its
+  // base-weight landing buffers
+  constexpr int kStages = kFold ? FOLD_STAGES2 : STAGES2;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  Bars2* bars = reinterpret_cast<Bars2*>(smem + STAGES2 * STAGE2_BYTES);
+  Bars2* bars = reinterpret_cast<Bars2*>(smem + kStages * STAGE2_BYTES);
   volatile int* abort_flag = &bars->abort;
 
   const int warp = threadIdx.x >> 5;
@@ -552,7 +736,7 @@ gemm_tc2_kernel(const __grid_constant__ IrisGemmParams p) {
   const uint32_t idesc = iris::umma_idesc_bf16_f32(BM2, 256);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES2; s++) {
+    for (int s = 0; s < kStages; s++) {
       iris::mbar_init(&bars->full[s], 2);
       iris::mbar_init(&bars->empty[s], 1);
     }
@@ -601,7 +785,7 @@ gemm_tc2_kernel(const __grid_constant__ IrisGemmParams p) {
         iris::tma_load_2d_pair(sa, &p.tmap_a, full_c, kb * BK, arow);
         iris::tma_load_2d_pair(sb, &p.tmap_b[g], full_c, kb * BK, brow);
         issued_any = true;
-        if (++stage == STAGES2) { stage = 0; phase ^= 1; }
+        if (++stage == kStages) { stage = 0; phase ^= 1; }
       }
     }
     if (!ok && issued_any) {
@@ -640,7 +824,7 @@ gemm_tc2_kernel(const __grid_constant__ IrisGemmParams p) {
         for (int kk = 0; kk < BK / 16; kk++)
           iris::umma_bf16_pair(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb | kk) != 0);
         iris::umma_commit_pair(&bars->empty[stage]);
-        if (++stage == STAGES2) { stage = 0; phase ^= 1; }
+        if (++stage == kStages) { stage = 0; phase ^= 1; }
       }
       if (ok) iris::umma_commit_pair(&bars->tfull[buf]);
     }
@@ -654,10 +838,16 @@ gemm_tc2_kernel(const __grid_constant__ IrisGemmParams p) {
     const int ew = warp - 2;
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
     const int half = ew >> 2;      // which half of the tile's columns
-    float* stage = reinterpret_cast<float*>(smem + STAGES2 * STAGE2_BYTES + 1024 + ew * EPI_WARP_BYTES);
+    float* stage = reinterpret_cast<float*>(smem + kStages * STAGE2_BYTES + 1024 + ew * EPI_WARP_BYTES);
     const uint32_t tempty_c0 = iris::mapa_shared(&bars->tempty[0], 0);
     const uint32_t tempty_c1 = iris::mapa_shared(&bars->tempty[1], 0);
     int it = 0;
+    if constexpr (kFold) {
+      uint4* landing = reinterpret_cast<uint4*>(smem + kStages * STAGE2_BYTES + 1024 +
+                                                EPI_WARPS2 * EPI_WARP_BYTES + ew * FOLD_LANDING_BYTES);
+      fold_epilogue_pair(p, bars->tfull, tempty_c0, tempty_c1, abort_flag, tmem_base, stage, landing, pair, npairs,
+                         total, mt0, mtot, rank, quarter, half, lane);
+    } else {
     if (pair < total && half == 0) {
       int g, ml, n0;
       tile_coords(p, pair, mt0, mtot, g, ml, n0);
@@ -680,10 +870,11 @@ gemm_tc2_kernel(const __grid_constant__ IrisGemmParams p) {
       int row = p.row0[g] + row_local;
       uint32_t taddr = tmem_base + buf * 256 + ((uint32_t)(quarter * 32) << 16);
       const int rows_valid = min(32, max(0, p.rows[g] - (row_local - lane)));
-      epi_tile(p, taddr, g, row, row_local, valid, n0, stage, lane, rows_valid, 0, half, 2);
+      epi_tile<kFold>(p, taddr, g, row, row_local, valid, n0, stage, lane, rows_valid, 0, half, 2);
       iris::tc_fence_before();
       __syncwarp();
       if (lane == 0) iris::mbar_arrive_cluster(buf ? tempty_c1 : tempty_c0);
+    }
     }
     if (p.mode == IRIS_EPI_TP_SCATTER) {
       asm volatile("bar.sync 1, %0;" ::"r"(32 * EPI_WARPS2) : "memory");  // every epilogue warp's stores are issued
@@ -778,10 +969,14 @@ static int g_max_pairs = 0;  // CTA pairs that can be resident at once
 
 extern "C" cudaError_t iris_gemm_init(void) {
   if (g_gemm_attr) return cudaSuccess;
-  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+  cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                        SMEM_BYTES);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(gemm_tc2_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
+    e = cudaFuncSetAttribute(gemm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gemm_tc2_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(gemm_tc2_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, FOLD_SMEM2_BYTES);
   if (e == cudaSuccess) {
     // clusters are placed within GPCs: ask how many pairs fit at once rather
     // than assuming SMs / 2 (a persistent grid larger than that would run its
@@ -795,7 +990,7 @@ extern "C" cudaError_t iris_gemm_init(void) {
     cfg.blockDim = dim3(NUM_THREADS2, 1, 1);
     cfg.dynamicSmemBytes = SMEM2_BYTES;
     int n = 0;
-    e = cudaOccupancyMaxActiveClusters(&n, gemm_tc2_kernel, &cfg);
+    e = cudaOccupancyMaxActiveClusters(&n, gemm_tc2_kernel<false>, &cfg);
     g_max_pairs = (e == cudaSuccess && n > 0) ? n : 0;
     e = cudaSuccess;
     cudaGetLastError();
@@ -833,7 +1028,10 @@ extern "C" cudaError_t iris_launch_gemm_ex(const IrisGemmParams* p, int num_sms,
     const bool split_instead = p->ws && linear && 2 * total < cap && p->K / BK >= 8;
     if (!split_instead) {
       long pairs = total < cap ? total : cap;
-      gemm_tc2_kernel<<<(int)(2 * pairs), NUM_THREADS2, SMEM2_BYTES, stream>>>(*p);
+      if (p->mode == IRIS_EPI_LORA_FOLD)
+        gemm_tc2_kernel<true><<<(int)(2 * pairs), NUM_THREADS2, FOLD_SMEM2_BYTES, stream>>>(*p);
+      else
+        gemm_tc2_kernel<false><<<(int)(2 * pairs), NUM_THREADS2, SMEM2_BYTES, stream>>>(*p);
       return cudaGetLastError();
     }
   }
@@ -855,7 +1053,8 @@ extern "C" cudaError_t iris_launch_gemm_ex(const IrisGemmParams* p, int num_sms,
   }
   const long total = tiles * q.splitk;
   int grid = (int)(total < num_sms ? total : num_sms);
-  gemm_tc_kernel<<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(q);
+  if (q.mode == IRIS_EPI_LORA_FOLD) gemm_tc_kernel<true><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(q);
+  else gemm_tc_kernel<false><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(q);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess || q.splitk == 1) return e;
   if (launches) *launches = 2;

@@ -36,6 +36,8 @@ enum {
                                  tp.recv[row / chunk][tp.rank] over NVLink, then a
                                  partial-arrival signal to every rank                     */
     IRIS_EPI_SINGLE = 6,      /* cols < 3H as IRIS_EPI_QKV, cols >= 3H as IRIS_EPI_SWIGLU   */
+    IRIS_EPI_LORA_FOLD = 9,   /* bf16 out[fold_rows[row], col] = bf16(fold_w0[same] +
+                                 fold_scale * acc): a low-rank update folded into a weight */
 };
 
 /* Tensor-parallel exchange over NVLink peer memory (size > 1).  Rows of the
@@ -103,6 +105,9 @@ typedef struct {
     size_t ws_bytes;
     int splitk;               /* set by iris_launch_gemm                              */
     IrisTpParams tp;          /* IRIS_EPI_TP_SCATTER destination and xmod wait        */
+    const int *fold_rows;     /* IRIS_EPI_LORA_FOLD: output row of each A row          */
+    const void *fold_w0;      /* IRIS_EPI_LORA_FOLD: base weight (bf16, row stride ldo) */
+    float fold_scale;
 } IrisGemmParams;
 
 /* Encodes a 2-D bf16 tensor map over a row-major [rows, cols] matrix with
@@ -230,12 +235,31 @@ cudaError_t iris_launch_interleave_gate_up(void *dst, const void *src, int F, in
                                            cudaStream_t stream);
 cudaError_t iris_launch_copy_rows_bf16(void *dst, int ldd, const void *src, int lds, int rows,
                                        int cols, cudaStream_t stream);
-/* LoRA fold: w[rowmap[i], 0:cols] = bf16(w0[rowmap[i], 0:cols] + scale * (B A)[i]) for
- * i < nrows; B f32 [nrows, rank], A f32 [rank, cols]; w / w0 bf16 with row stride ld
- * (may alias); cols and ld multiples of 8, w and w0 16-byte aligned. */
-cudaError_t iris_launch_lora_merge(void *w, const void *w0, int ld, const float *B, const float *A,
-                                   const int *rowmap, int nrows, int cols, int rank, float scale,
-                                   cudaStream_t stream);
+/* LoRA fold (lora_kernels.cu): w[drow[i], 0:cols] = bf16(w0[drow[i], 0:cols] +
+ * scale * (B A)[bsrc[i], acol(0:cols)]) for i < nrows, on the tcgen05 GEMM.
+ * B [*, rank] and A [rank, in_dim] are the adapter's matrices as stored
+ * (IRIS_LORA_BF16 / F16 / F32); acol(c) = c < acol_seg ? acol_off0 + c :
+ * acol_off1 + (c - acol_seg).  cols % 128 == 0, ld % 8 == 0, w / w0
+ * 16-byte aligned (may alias).  Scratch: iris_lora_fold_scratch_bytes. */
+#define IRIS_LORA_BF16 0
+#define IRIS_LORA_F16 1
+#define IRIS_LORA_F32 2
+typedef struct {
+    void *w;
+    const void *w0;
+    int ld, cols, nrows;
+    const void *B;
+    int b_dtype, rank;
+    const int *bsrc, *drow;     /* device [nrows] */
+    const void *A;
+    int a_dtype, in_dim;
+    int acol_seg, acol_off0, acol_off1;
+    float scale;
+} IrisLoraFold;
+size_t iris_lora_fold_scratch_bytes(int nrows, int cols, int rank, int split);
+/* prep kernels + one GEMM; *launches = kernels queued */
+cudaError_t iris_launch_lora_fold(const IrisLoraFold *f, void *scratch, size_t scratch_bytes, int *status,
+                                  int num_sms, cudaStream_t stream, int *launches);
 
 /* ------------------------------------------------------------------ text encoder (Qwen3) */
 /* x[s] = f32 of table[ids[s]] (bf16 [vocab, H]); ids outside [0, vocab) -> zeros */

@@ -46,7 +46,8 @@ typedef struct {
     int tgt, block, stream;  /* stream (double blocks): 1 image, 0 text */
     int row_off;             /* first reference row of the target this B covers */
     int rank, in_dim, out_dim;
-    float *A, *B;            /* host f32: A [rank, in_dim], B [out_dim, rank] */
+    const st_tensor_t *ta, *tb;  /* A [rank, in_dim], B [out_dim, rank] in the open file */
+    size_t a_off, b_off;     /* their bytes in the device copy of the file's tensors */
 } lora_ad_t;
 
 typedef struct {
@@ -61,6 +62,11 @@ struct iris_flux_lora {
     lora_saved_t *saved;
     double merge_ms, merge_bytes;
 };
+
+/* safetensors dtype -> the fold kernels' operand type (-1: unsupported) */
+static int fold_dtype(st_dtype_t d) {
+    return d == ST_BF16 ? IRIS_LORA_BF16 : d == ST_F16 ? IRIS_LORA_F16 : d == ST_F32 ? IRIS_LORA_F32 : -1;
+}
 
 typedef enum { FMT_UNKNOWN = 0, FMT_XLABS, FMT_KOHYA, FMT_DIFFUSERS, FMT_BFL } lora_fmt_t;
 
@@ -86,18 +92,23 @@ typedef struct {
 } ad_list_t;
 
 static void ads_free(ad_list_t *l) {
-    for (int i = 0; i < l->n; i++) { free(l->v[i].A); free(l->v[i].B); }
     free(l->v);
     memset(l, 0, sizeof(*l));
 }
 
-/* Read one (down, up) pair.  Returns 1 when added, 0 when absent or skipped,
+/* Record one (down, up) pair.  Returns 1 when added, 0 when absent or skipped,
  * < 0 on an allocation failure.  exp_in / exp_out: the shapes the target needs. */
 static int add_adapter(ad_list_t *l, const st_model_t *st, const char *down_key, const char *up_key,
                        int tgt, int block, int stream, int row_off, int exp_in, int exp_out) {
     const st_tensor_t *dn = st_find(st, down_key), *up = st_find(st, up_key);
     if (!dn || !up || dn->ndim != 2 || up->ndim != 2) return 0;
     int rank = (int)dn->shape[0], in = (int)dn->shape[1], out = (int)up->shape[0];
+    if (fold_dtype(dn->dtype) < 0 || fold_dtype(up->dtype) < 0 ||
+        dn->nbytes != (size_t)rank * in * (dn->dtype == ST_F32 ? 4 : 2) ||
+        up->nbytes != (size_t)out * rank * (up->dtype == ST_F32 ? 4 : 2)) {
+        fprintf(stderr, "iris_cuda LoRA: skipping %s: unsupported data type or size\n", down_key);
+        return 0;
+    }
     if (rank <= 0 || up->shape[1] != rank || in != exp_in || out != exp_out) {
         fprintf(stderr, "iris_cuda LoRA: skipping %s: A [%lld, %lld], B [%lld, %lld], expected in %d, out %d\n",
                 down_key, (long long)dn->shape[0], (long long)dn->shape[1], (long long)up->shape[0],
@@ -115,14 +126,8 @@ static int add_adapter(ad_list_t *l, const st_model_t *st, const char *down_key,
     memset(a, 0, sizeof(*a));
     a->tgt = tgt; a->block = block; a->stream = stream; a->row_off = row_off;
     a->rank = rank; a->in_dim = in; a->out_dim = out;
-    a->A = (float *)malloc((size_t)rank * in * sizeof(float));
-    a->B = (float *)malloc((size_t)out * rank * sizeof(float));
-    if (!a->A || !a->B) { free(a->A); free(a->B); return IRIS_CUDA_ERR_OOM; }
-    if (st_read_f32(st, dn, a->A, (size_t)rank * in) || st_read_f32(st, up, a->B, (size_t)out * rank)) {
-        fprintf(stderr, "iris_cuda LoRA: skipping %s: unreadable data\n", down_key);
-        free(a->A); free(a->B);
-        return 0;
-    }
+    a->ta = dn;
+    a->tb = up;
     l->n++;
     return 1;
 }
@@ -256,20 +261,20 @@ static int ref_col(const iris_cuda_flux_t *tf, int tgt, int c) {
 
 /* ---------------------------------------------------------------- state */
 
-static int restore_all(struct iris_flux_lora *L) {
-    for (int i = 0; i < L->nsaved; i++) {
-        int rc = iris_cuda_check(cudaMemcpyAsync(L->saved[i].live, L->saved[i].orig, L->saved[i].numel * 2,
-                                                 cudaMemcpyDeviceToDevice, g_rt.stream), "LoRA restore");
-        if (rc) return rc;
-    }
-    return 0;
+static int copy_d2d(void *dst, const void *src, size_t bytes, const char *what) {
+    return iris_cuda_check(cudaMemcpyAsync(dst, src, bytes, cudaMemcpyDeviceToDevice, g_rt.stream), what);
 }
 
-/* the saved original of a live weight, created (a copy of the live weight,
- * which is still the base model's) the first time an adapter targets it */
-static const uint16_t *saved_orig(struct iris_flux_lora *L, uint16_t *live, size_t numel) {
+/* the saved copy of a live weight, or NULL */
+static lora_saved_t *find_saved(struct iris_flux_lora *L, const uint16_t *live) {
     for (int i = 0; i < L->nsaved; i++)
-        if (L->saved[i].live == live) return L->saved[i].orig;
+        if (L->saved[i].live == live) return &L->saved[i];
+    return NULL;
+}
+
+/* Save a live weight (still the base model's) the first time an adapter
+ * targets it. */
+static lora_saved_t *save_weight(struct iris_flux_lora *L, uint16_t *live, size_t numel) {
     if (L->nsaved == L->cap) {
         int nc = L->cap ? 2 * L->cap : 32;
         lora_saved_t *nv = (lora_saved_t *)realloc(L->saved, (size_t)nc * sizeof(*nv));
@@ -279,15 +284,23 @@ static const uint16_t *saved_orig(struct iris_flux_lora *L, uint16_t *live, size
     }
     uint16_t *o = (uint16_t *)iris_dmalloc(numel * 2);
     if (!o) return NULL;
-    if (iris_cuda_check(cudaMemcpyAsync(o, live, numel * 2, cudaMemcpyDeviceToDevice, g_rt.stream), "LoRA save")) {
+    if (copy_d2d(o, live, numel * 2, "LoRA save")) {
         iris_dfree(o);
         return NULL;
     }
-    L->saved[L->nsaved].live = live;
-    L->saved[L->nsaved].orig = o;
-    L->saved[L->nsaved].numel = numel;
-    L->nsaved++;
-    return o;
+    lora_saved_t *sv = &L->saved[L->nsaved++];
+    sv->live = live;
+    sv->orig = o;
+    sv->numel = numel;
+    return sv;
+}
+
+static int restore_all(struct iris_flux_lora *L) {
+    for (int i = 0; i < L->nsaved; i++) {
+        int rc = copy_d2d(L->saved[i].live, L->saved[i].orig, L->saved[i].numel * 2, "LoRA restore");
+        if (rc) return rc;
+    }
+    return 0;
 }
 
 void iris_flux_lora_release(iris_cuda_flux_t *tf) {
@@ -300,69 +313,144 @@ void iris_flux_lora_release(iris_cuda_flux_t *tf) {
     tf->lora = NULL;
 }
 
-/* Fold every adapter: W = bf16(W_orig + scale * B' A') per target, B' the
- * rows this rank holds in device row order, A' the columns in device order. */
-static int fold(iris_cuda_flux_t *tf, struct iris_flux_lora *L, const ad_list_t *ads, float scale) {
-    int rc = 0, max_rows = 0, max_cols = 0, max_rank = 0;
+/* Device rows this rank holds of an adapter's B: raw row bsrc[i] -> row drow[i]
+ * of the target weight.  Returns the count. */
+static int adapter_rows(const iris_cuda_flux_t *tf, const lora_ad_t *a, int rows, int *bsrc, int *drow) {
+    int n = 0;
+    for (int r = 0; r < a->out_dim; r++) {
+        int d = device_row(tf, a->tgt, a->row_off + r);
+        if (d < 0 || d >= rows) continue;
+        bsrc[n] = r;
+        drow[n] = d;
+        n++;
+    }
+    return n;
+}
+
+/* Fold every adapter into the live weights.  Device work, in stream order:
+ *  1. the adapters' A / B bytes, as stored in the file, in one device buffer;
+ *  2. for each target weight: first use -> save the base copy; a weight the
+ *     previous adapter changed and the new one does not cover entirely ->
+ *     restore it from the base copy;
+ *  3. per adapter: prep kernels + the tcgen05 GEMM with the fold epilogue
+ *     (reads the base rows, writes the live rows). */
+static int fold(iris_cuda_flux_t *tf, struct iris_flux_lora *L, ad_list_t *ads, const st_model_t *st,
+                float scale) {
+    int rc = 0, max_rows = 0;
+    size_t raw_bytes = 0, scratch = 0;
+    for (int i = 0; i < ads->n; i++) {
+        lora_ad_t *a = &ads->v[i];
+        int rows, cols;
+        target_weight(tf, a, &rows, &cols);
+        if (a->out_dim > max_rows) max_rows = a->out_dim;
+        a->a_off = raw_bytes;
+        raw_bytes += (a->ta->nbytes + 255) & ~(size_t)255;
+        a->b_off = raw_bytes;
+        raw_bytes += (a->tb->nbytes + 255) & ~(size_t)255;
+        const int split = a->ta->dtype != ST_BF16 || a->tb->dtype != ST_BF16;
+        size_t sb = iris_lora_fold_scratch_bytes(a->out_dim, cols, a->rank, split);
+        if (sb > scratch) scratch = sb;
+    }
+    int *hmap = (int *)malloc((size_t)ads->n * 2 * max_rows * sizeof(int));
+    int *nrow = (int *)calloc((size_t)ads->n, sizeof(int));
+    uint8_t *raw = (uint8_t *)iris_dmalloc(raw_bytes + scratch + (size_t)ads->n * 2 * max_rows * sizeof(int) + 512);
+    cudaEvent_t e0 = NULL, e1 = NULL;
+    double bytes = 0;
+    if (!hmap || !nrow || !raw) { rc = iris_fail(IRIS_CUDA_ERR_OOM, "LoRA staging"); goto out; }
+    uint8_t *dscratch = raw + ((raw_bytes + 255) & ~(size_t)255);
+    int *dmap = (int *)(dscratch + ((scratch + 255) & ~(size_t)255));
+    /* row maps (host) */
     for (int i = 0; i < ads->n; i++) {
         int rows, cols;
         target_weight(tf, &ads->v[i], &rows, &cols);
-        if (ads->v[i].out_dim > max_rows) max_rows = ads->v[i].out_dim;
-        if (cols > max_cols) max_cols = cols;
-        if (ads->v[i].rank > max_rank) max_rank = ads->v[i].rank;
+        int *bs = hmap + (size_t)i * 2 * max_rows;
+        nrow[i] = adapter_rows(tf, &ads->v[i], rows, bs, bs + max_rows);
     }
-    size_t nb = (size_t)max_rows * max_rank, na = (size_t)max_rank * max_cols;
-    float *hB = (float *)malloc(nb * 4), *hA = (float *)malloc(na * 4);
-    int *hmap = (int *)malloc((size_t)max_rows * sizeof(int));
-    char *dbuf = (char *)iris_dmalloc(nb * 4 + na * 4 + (size_t)max_rows * 4 + 256);
-    cudaEvent_t e0 = NULL, e1 = NULL;
-    double bytes = 0;
-    if (!hB || !hA || !hmap || !dbuf) { rc = iris_fail(IRIS_CUDA_ERR_OOM, "LoRA staging"); goto out; }
-    float *dB = (float *)dbuf, *dA = dB + nb;
-    int *dmap = (int *)(dA + na);
     cudaEventCreate(&e0);
     cudaEventCreate(&e1);
-    float ms_total = 0.f;
+    /* 1. uploads (stream-ordered copies straight from the mapped file) */
+    for (int i = 0; i < ads->n && !rc; i++) {
+        const lora_ad_t *a = &ads->v[i];
+        const uint8_t *base = (const uint8_t *)st->maps[a->ta->file] + st->data_start[a->ta->file];
+        rc = iris_cuda_check(cudaMemcpyAsync(raw + a->a_off, base + a->ta->offset, a->ta->nbytes,
+                                             cudaMemcpyHostToDevice, g_rt.stream), "LoRA upload");
+        base = (const uint8_t *)st->maps[a->tb->file] + st->data_start[a->tb->file];
+        if (!rc)
+            rc = iris_cuda_check(cudaMemcpyAsync(raw + a->b_off, base + a->tb->offset, a->tb->nbytes,
+                                                 cudaMemcpyHostToDevice, g_rt.stream), "LoRA upload");
+    }
+    if (!rc)
+        rc = iris_cuda_check(cudaMemcpyAsync(dmap, hmap, (size_t)ads->n * 2 * max_rows * sizeof(int),
+                                             cudaMemcpyHostToDevice, g_rt.stream), "LoRA upload");
+    if (!rc) rc = iris_stream_drain();  /* the pageable sources must stay valid until copied */
+    if (rc) goto out;
+    cudaEventRecord(e0, g_rt.stream);
+    /* 2. base copies: save on first use, restore what the new adapter does not rewrite */
+    for (int i = 0; i < ads->n; i++) {
+        int rows, cols;
+        uint16_t *live = target_weight(tf, &ads->v[i], &rows, &cols);
+        if (!find_saved(L, live)) {
+            if (!save_weight(L, live, (size_t)rows * cols)) { rc = iris_fail(IRIS_CUDA_ERR_OOM, "LoRA base copy"); goto out; }
+            bytes += 4.0 * rows * cols;
+        }
+    }
+    for (int s = 0; s < L->nsaved; s++) {
+        long covered = 0;
+        for (int i = 0; i < ads->n; i++) {
+            int rows, cols;
+            if (target_weight(tf, &ads->v[i], &rows, &cols) == L->saved[s].live) covered += (long)nrow[i] * cols;
+        }
+        if ((size_t)covered != L->saved[s].numel) {
+            if ((rc = copy_d2d(L->saved[s].live, L->saved[s].orig, L->saved[s].numel * 2, "LoRA restore"))) goto out;
+            bytes += 4.0 * L->saved[s].numel;
+        }
+    }
+    /* 3. folds */
+    const int H = tf->H, Hl = tf->Hl, h0 = tf->tp_rank * tf->Hl, f0 = tf->tp_rank * tf->Fl;
     for (int i = 0; i < ads->n; i++) {
         const lora_ad_t *a = &ads->v[i];
+        if (!nrow[i]) continue;
         int rows, cols;
-        uint16_t *live = target_weight(tf, a, &rows, &cols);
-        const uint16_t *orig = saved_orig(L, live, (size_t)rows * cols);
-        if (!orig) { rc = iris_fail(IRIS_CUDA_ERR_OOM, "LoRA original weight copy"); goto out; }
+        IrisLoraFold f;
+        memset(&f, 0, sizeof(f));
+        f.w = target_weight(tf, a, &rows, &cols);
+        f.w0 = find_saved(L, (uint16_t *)f.w)->orig;
+        f.ld = cols;
+        f.cols = cols;
+        f.nrows = nrow[i];
+        f.B = raw + a->b_off;
+        f.b_dtype = fold_dtype(a->tb->dtype);
+        f.rank = a->rank;
+        f.bsrc = dmap + (size_t)i * 2 * max_rows;
+        f.drow = f.bsrc + max_rows;
+        f.A = raw + a->a_off;
+        f.a_dtype = fold_dtype(a->ta->dtype);
+        f.in_dim = a->in_dim;
+        /* device column c of the target reads A's column acol(c) */
+        f.acol_seg = (a->tgt == TGT_L2) ? Hl : cols;
+        f.acol_off0 = (a->tgt == TGT_PROJ || a->tgt == TGT_L2) ? h0 : 0;
+        f.acol_off1 = H + f0;
+        f.scale = scale;
         int n = 0;
-        for (int r = 0; r < a->out_dim; r++) {
-            int d = device_row(tf, a->tgt, a->row_off + r);
-            if (d < 0) continue;
-            if (d >= rows) { rc = iris_fail(IRIS_CUDA_ERR_ARG, "LoRA row map out of range"); goto out; }
-            memcpy(hB + (size_t)n * a->rank, a->B + (size_t)r * a->rank, (size_t)a->rank * 4);
-            hmap[n++] = d;
-        }
-        if (!n) continue;
-        for (int k = 0; k < a->rank; k++)
-            for (int c = 0; c < cols; c++) hA[(size_t)k * cols + c] = a->A[(size_t)k * a->in_dim + ref_col(tf, a->tgt, c)];
-        if ((rc = iris_h2d(dB, hB, (size_t)n * a->rank * 4)) || (rc = iris_h2d(dA, hA, (size_t)a->rank * cols * 4)) ||
-            (rc = iris_h2d(dmap, hmap, (size_t)n * 4)))
-            goto out;
-        cudaEventRecord(e0, g_rt.stream);
-        iris_count_launch(1);
-        rc = iris_cuda_check(iris_launch_lora_merge(live, orig, cols, dB, dA, dmap, n, cols, a->rank, scale,
-                                                    g_rt.stream), "LoRA fold");
+        rc = iris_cuda_check(iris_launch_lora_fold(&f, dscratch, scratch, g_rt.d_status, g_rt.num_sms, g_rt.stream,
+                                                   &n), "LoRA fold");
+        iris_count_launch((uint64_t)n);
         if (rc) goto out;
-        cudaEventRecord(e1, g_rt.stream);
-        if ((rc = iris_cuda_check(cudaEventSynchronize(e1), "LoRA fold"))) goto out;
-        float ms = 0.f;
-        cudaEventElapsedTime(&ms, e0, e1);
-        ms_total += ms;
-        bytes += 4.0 * n * cols + 4.0 * ((double)n * a->rank + (double)a->rank * cols + n);
+        bytes += 4.0 * nrow[i] * cols + (double)a->ta->nbytes + (double)a->tb->nbytes;
     }
-    L->merge_ms = ms_total;
+    cudaEventRecord(e1, g_rt.stream);
+    if ((rc = iris_cuda_check(cudaEventSynchronize(e1), "LoRA fold"))) goto out;
+    float ms = 0.f;
+    cudaEventElapsedTime(&ms, e0, e1);
+    L->merge_ms = ms;
     L->merge_bytes = bytes;
 out:
+    iris_stream_drain();
     if (e0) cudaEventDestroy(e0);
     if (e1) cudaEventDestroy(e1);
-    iris_stream_drain();
-    iris_dfree(dbuf);
-    free(hB); free(hA); free(hmap);
+    iris_dfree(raw);
+    free(hmap);
+    free(nrow);
     return rc;
 }
 
@@ -379,23 +467,23 @@ int iris_cuda_flux_load_lora(iris_cuda_flux_t *tf, const char *path, float scale
     ad_list_t ads;
     memset(&ads, 0, sizeof(ads));
     int rc = collect(&ads, &st, fmt, tf->cfg.n_double, tf->cfg.n_single, tf->H, tf->F);
-    st_close(&st);
-    if (rc) { ads_free(&ads); return iris_fail(rc, "LoRA: out of host memory"); }
+    if (rc) { st_close(&st); ads_free(&ads); return iris_fail(rc, "LoRA: out of host memory"); }
     if (!ads.n) {
         /* like lora_load (iris_lora.c:578): nothing usable leaves the current state */
+        st_close(&st);
         ads_free(&ads);
         return iris_fail(IRIS_CUDA_ERR_ARG, "LoRA %s: no adapters match this model", path);
     }
     if (!tf->lora) {
         tf->lora = (struct iris_flux_lora *)calloc(1, sizeof(*tf->lora));
-        if (!tf->lora) { ads_free(&ads); return iris_fail(IRIS_CUDA_ERR_OOM, "LoRA state"); }
+        if (!tf->lora) { st_close(&st); ads_free(&ads); return iris_fail(IRIS_CUDA_ERR_OOM, "LoRA state"); }
     }
     struct iris_flux_lora *L = tf->lora;
-    rc = restore_all(L);
     L->adapters = 0;
     L->merge_ms = 0;
     L->merge_bytes = 0;
-    if (!rc && scale != 0.0f) rc = fold(tf, L, &ads, scale);
+    if (scale == 0.0f) rc = restore_all(L);  /* strength 0: the base model exactly */
+    else rc = fold(tf, L, &ads, &st, scale);
     if (!rc) {
         L->adapters = ads.n;
         L->scale = scale;
@@ -403,6 +491,7 @@ int iris_cuda_flux_load_lora(iris_cuda_flux_t *tf, const char *path, float scale
         restore_all(L);  /* never leave a half-folded model */
     }
     iris_stream_drain();
+    st_close(&st);
     ads_free(&ads);
     return rc;
 }

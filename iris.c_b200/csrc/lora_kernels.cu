@@ -1,110 +1,150 @@
-// LoRA merge: W[rowmap[i], :] = bf16( f32(W0[rowmap[i], :]) + scale * (B A)[i, :] )
+// LoRA fold on the tensor cores:
+//   W[drow[i], :] = bf16( W0[drow[i], :] + scale * (B A)[bsrc[i], :] )
 //
 // The reference applies an adapter at run time after every adapted linear,
 // out += scale * B (A x)  (lora_apply, iris_lora.c:43; hooks
 // iris_transformer_flux.c:2429-2532, :3818, :3909).  Since the product is
 // linear in x, W x + scale * B (A x) = (W + scale * B A) x: the backend folds
 // each adapter into its resident bf16 weight once, so a step with a LoRA costs
-// exactly what a step without one costs.  This kernel is that fold.
+// exactly what a step without one costs.
 //
-//   B    f32 [nrows, rank]  the adapter's up matrix, rows already in the
-//                            device weight's row order (gate/up interleave,
-//                            tensor-parallel shard)
-//   A    f32 [rank, cols]   the down matrix, columns in the device order
-//   rowmap int [nrows]      device row of B's row i
-//   W0 / W bf16 [*, ld]     original and live weight (may alias)
-//
-// Tile 64 rows x 128 columns per 256-thread block, rank consumed in chunks of
-// 32 through shared memory; each thread owns 4 rows x 8 contiguous columns, so
-// its weight loads and stores are 16-byte vectors and a warp covers two
-// 256-byte row segments.  The weight traffic (read W0, write W: 4 bytes per
-// element) is the roofline for ranks up to ~32; the rank-r product is
-// 2r FLOPs per element on the FP32 pipes.
+// The rank-r product B A is a GEMM with K = r: two small prep kernels gather
+// the adapter's operands straight from the file's bytes (bf16, f16 or f32) into
+// K-major bf16 tiles, padded to K = 64 —
+//   Bp [n, Kp]     row i = B's row bsrc[i] (the device row order: gate/up
+//                  interleave, tensor-parallel shard)
+//   At [cols, Kp]  row c = A's column acol(c)
+// — and the tcgen05 GEMM (gemm.cu) runs with its IRIS_EPI_LORA_FOLD
+// epilogue, which reads the base row from W0, adds scale * acc and stores the
+// bf16 result.  bf16 adapters are exact operands.  f16 / f32 adapters are split
+// into bf16 hi + lo parts, K = 4r: Bh·Ah + Bh·Al + Bl·Ah + Bl·Al — exact for f16
+// (11 significant bits fit in hi + lo), 16 of f32's 24 bits otherwise.  With K
+// this short the GEMM is bound by the weight traffic, 2 bytes read + 2 written
+// per element.
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
+#include <string.h>
+
+#include "iris_kernels.h"
 
 namespace {
 
-constexpr int LM_ROWS = 64;
-constexpr int LM_COLS = 128;
-constexpr int LM_KC = 32;
+__device__ __forceinline__ float lora_load(const void* p, size_t i, int dtype) {
+  if (dtype == IRIS_LORA_BF16) return __uint_as_float((uint32_t) static_cast<const uint16_t*>(p)[i] << 16);
+  if (dtype == IRIS_LORA_F16) return __half2float(static_cast<const __half*>(p)[i]);
+  return static_cast<const float*>(p)[i];
+}
 
-__global__ void __launch_bounds__(256)
-lora_merge_kernel(uint16_t* __restrict__ w, const uint16_t* __restrict__ w0, int ld,
-                  const float* __restrict__ B, const float* __restrict__ A,
-                  const int* __restrict__ rowmap, int nrows, int cols, int rank, float scale) {
-  __shared__ float Bs[LM_ROWS][LM_KC + 1];
-  __shared__ __align__(16) float As[LM_KC][LM_COLS];
-  const int tid = threadIdx.x;
-  const int tx = tid & 15, ty = tid >> 4;  // 16 column groups x 16 row groups
-  const int row0 = blockIdx.y * LM_ROWS, col0 = blockIdx.x * LM_COLS;
-  float acc[4][8];
-#pragma unroll
-  for (int i = 0; i < 4; i++)
-#pragma unroll
-    for (int j = 0; j < 8; j++) acc[i][j] = 0.f;
+__device__ __forceinline__ uint16_t bf16_bits(float x) {
+  __nv_bfloat16 h = __float2bfloat16_rn(x);
+  return *reinterpret_cast<uint16_t*>(&h);
+}
 
-  for (int k0 = 0; k0 < rank; k0 += LM_KC) {
-    // B chunk: 64 x 32 (8 per thread), zero outside [nrows, rank)
-    for (int e = tid; e < LM_ROWS * LM_KC; e += 256) {
-      int r = e / LM_KC, k = e % LM_KC;
-      int gr = row0 + r, gk = k0 + k;
-      Bs[r][k] = (gr < nrows && gk < rank) ? B[(size_t)gr * rank + gk] : 0.f;
-    }
-    // A chunk: 32 x 128 (16 per thread), zero outside [rank, cols)
-    for (int e = tid; e < LM_KC * LM_COLS; e += 256) {
-      int k = e / LM_COLS, c = e % LM_COLS;
-      int gk = k0 + k, gc = col0 + c;
-      As[k][c] = (gk < rank && gc < cols) ? A[(size_t)gk * cols + gc] : 0.f;
-    }
-    __syncthreads();
-#pragma unroll 8
-    for (int k = 0; k < LM_KC; k++) {
-      float4 a0 = *reinterpret_cast<const float4*>(&As[k][tx * 8]);
-      float4 a1 = *reinterpret_cast<const float4*>(&As[k][tx * 8 + 4]);
-      float a[8] = {a0.x, a0.y, a0.z, a0.w, a1.x, a1.y, a1.z, a1.w};
+// K column k of an operand row with rank-r entries x(0..r-1): unsplit, k < r
+// holds bf16(x_k); split, part = k / r holds the bf16 hi or lo part of
+// x_{k mod r} (B parts hi, hi, lo, lo against A parts hi, lo, hi, lo).
+__device__ __forceinline__ uint16_t lora_part(float x, bool lo_part) {
+  const uint16_t hi = bf16_bits(x);
+  if (!lo_part) return hi;
+  return bf16_bits(x - __uint_as_float((uint32_t)hi << 16));
+}
+
+// one K-major operand row of kp bf16 values: value k from x(part, k mod r)
+// via `get`, written as 16-byte stores
+template <typename Get>
+__device__ __forceinline__ void lora_row(uint16_t* __restrict__ row, int kp, int rank, int nparts, Get get) {
+  uint4* d = reinterpret_cast<uint4*>(row);
+  for (int k8 = 0; k8 < kp; k8 += 8) {
+    uint32_t w[4];
 #pragma unroll
-      for (int i = 0; i < 4; i++) {
-        float b = Bs[ty * 4 + i][k];
+    for (int q = 0; q < 4; q++) {
+      uint32_t h[2];
 #pragma unroll
-        for (int j = 0; j < 8; j++) acc[i][j] = fmaf(b, a[j], acc[i][j]);
+      for (int e = 0; e < 2; e++) {
+        const int k = k8 + 2 * q + e, part = k / rank;
+        h[e] = part < nparts ? get(part, k - part * rank) : 0u;
       }
+      w[q] = h[0] | (h[1] << 16);
     }
-    __syncthreads();
+    d[k8 >> 3] = make_uint4(w[0], w[1], w[2], w[3]);
   }
+}
 
-  const int c = col0 + tx * 8;
+// Bp row i <- B row bsrc[i]; one thread per row (B parts: hi, hi, lo, lo)
+__global__ void lora_prep_b_kernel(uint16_t* __restrict__ dst, int kp, const void* __restrict__ B, int dtype,
+                                   int rank, const int* __restrict__ bsrc, int n, int split) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  const size_t src = (size_t)__ldg(bsrc + i) * rank;
+  lora_row(dst + (size_t)i * kp, kp, rank, split ? 4 : 1, [&](int part, int kk) -> uint32_t {
+    return lora_part(lora_load(B, src + kk, dtype), split && part >= 2);
+  });
+}
+
+// At row c <- A column acol(c); one thread per column, so that the threads of
+// a warp read consecutive columns of A (A parts: hi, lo, hi, lo)
+__global__ void lora_prep_a_kernel(uint16_t* __restrict__ dst, int kp, const void* __restrict__ A, int dtype,
+                                   int rank, int in_dim, int cols, int seg, int off0, int off1, int split) {
+  const int c = blockIdx.x * blockDim.x + threadIdx.x;
   if (c >= cols) return;
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    int r = row0 + ty * 4 + i;
-    if (r >= nrows) break;
-    size_t off = (size_t)rowmap[r] * ld + c;
-    uint4 v = *reinterpret_cast<const uint4*>(w0 + off);
-    uint32_t u[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-    for (int j = 0; j < 4; j++) {
-      float lo = __uint_as_float(u[j] << 16) + scale * acc[i][2 * j];
-      float hi = __uint_as_float(u[j] & 0xFFFF0000u) + scale * acc[i][2 * j + 1];
-      __nv_bfloat162 p = __floats2bfloat162_rn(lo, hi);
-      u[j] = *reinterpret_cast<uint32_t*>(&p);
-    }
-    *reinterpret_cast<uint4*>(w + off) = make_uint4(u[0], u[1], u[2], u[3]);
-  }
+  const int sc = c < seg ? off0 + c : off1 + (c - seg);
+  lora_row(dst + (size_t)c * kp, kp, rank, split ? 4 : 1, [&](int part, int kk) -> uint32_t {
+    return lora_part(lora_load(A, (size_t)kk * in_dim + sc, dtype), split && (part & 1));
+  });
 }
 
 }  // namespace
 
-extern "C" cudaError_t iris_launch_lora_merge(void* w, const void* w0, int ld, const float* B,
-                                              const float* A, const int* rowmap, int nrows, int cols,
-                                              int rank, float scale, cudaStream_t stream) {
-  if (nrows <= 0 || cols <= 0) return cudaSuccess;
-  if (rank <= 0 || (cols & 7) || (ld & 7) || ld < cols) return cudaErrorInvalidValue;
-  if ((reinterpret_cast<uintptr_t>(w) | reinterpret_cast<uintptr_t>(w0)) & 15) return cudaErrorInvalidValue;
-  dim3 grid((cols + LM_COLS - 1) / LM_COLS, (nrows + LM_ROWS - 1) / LM_ROWS);
-  if (grid.y > 65535) return cudaErrorInvalidValue;
-  lora_merge_kernel<<<grid, 256, 0, stream>>>(static_cast<uint16_t*>(w), static_cast<const uint16_t*>(w0),
-                                              ld, B, A, rowmap, nrows, cols, rank, scale);
-  return cudaGetLastError();
+extern "C" size_t iris_lora_fold_scratch_bytes(int nrows, int cols, int rank, int split) {
+  const int K = split ? 4 * rank : rank;
+  const size_t kp = (size_t)((K + 63) / 64) * 64;
+  return ((size_t)nrows + (size_t)cols) * kp * 2 + 256;
+}
+
+extern "C" cudaError_t iris_launch_lora_fold(const IrisLoraFold* f, void* scratch, size_t scratch_bytes,
+                                             int* status, int num_sms, cudaStream_t stream, int* launches) {
+  if (launches) *launches = 0;
+  if (!f || f->nrows <= 0 || f->cols <= 0) return cudaSuccess;
+  if (f->rank <= 0 || f->cols % 128 || f->ld % 8 || f->ld < f->cols || f->in_dim <= 0) return cudaErrorInvalidValue;
+  if (f->b_dtype < 0 || f->b_dtype > 2 || f->a_dtype < 0 || f->a_dtype > 2) return cudaErrorInvalidValue;
+  if (f->acol_seg < 0 || f->acol_seg > f->cols) return cudaErrorInvalidValue;
+  if (((uintptr_t)f->w | (uintptr_t)f->w0) & 15) return cudaErrorInvalidValue;
+  const int split = (f->b_dtype != IRIS_LORA_BF16 || f->a_dtype != IRIS_LORA_BF16) ? 1 : 0;
+  const int K = split ? 4 * f->rank : f->rank;
+  const int kp = (K + 63) / 64 * 64;
+  if (iris_lora_fold_scratch_bytes(f->nrows, f->cols, f->rank, split) > scratch_bytes) return cudaErrorInvalidValue;
+  uint16_t* bp = reinterpret_cast<uint16_t*>((reinterpret_cast<uintptr_t>(scratch) + 127) & ~uintptr_t(127));
+  uint16_t* at = bp + (size_t)f->nrows * kp;  // nrows * kp * 2 bytes: a multiple of 128
+  lora_prep_b_kernel<<<(f->nrows + 127) / 128, 128, 0, stream>>>(bp, kp, f->B, f->b_dtype, f->rank, f->bsrc,
+                                                                  f->nrows, split);
+  lora_prep_a_kernel<<<(f->cols + 127) / 128, 128, 0, stream>>>(at, kp, f->A, f->a_dtype, f->rank, f->in_dim,
+                                                                f->cols, f->acol_seg, f->acol_off0, f->acol_off1,
+                                                                split);
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return e;
+  IrisGemmParams p;
+  memset(&p, 0, sizeof(p));
+  if (iris_make_tmap_bf16(&p.tmap_a, bp, f->nrows, kp, kp, 128) ||
+      iris_make_tmap_bf16(&p.tmap_b[0], at, f->cols, kp, kp, 128))
+    return cudaErrorInvalidValue;
+  p.ngroups = 1;
+  p.row0[0] = 0;
+  p.rows[0] = f->nrows;
+  p.N = f->cols;
+  p.K = kp;
+  p.bn = f->cols % 256 == 0 ? 256 : 128;
+  p.mode = IRIS_EPI_LORA_FOLD;
+  p.out = f->w;
+  p.ldo = f->ld;
+  p.fold_rows = f->drow;
+  p.fold_w0 = f->w0;
+  p.fold_scale = f->scale;
+  p.status = status;
+  p.splitk = 1;
+  int n = 0;
+  e = iris_launch_gemm_ex(&p, num_sms, stream, &n);
+  if (launches) *launches = 2 + n;
+  return e;
 }

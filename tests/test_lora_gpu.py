@@ -154,62 +154,110 @@ def test_sampler_with_lora_matches_reference(iris, tmp_path):
 # ---------------------------------------------------------------- fold kernel
 
 
-def _merge(iris, w, w0, ld, B, A, rowmap, nrows, cols, rank, scale):
+class LoraFold(C.Structure):
+    """IrisLoraFold (csrc/iris_kernels.h)."""
+    _fields_ = [("w", C.c_void_p), ("w0", C.c_void_p), ("ld", C.c_int), ("cols", C.c_int), ("nrows", C.c_int),
+                ("B", C.c_void_p), ("b_dtype", C.c_int), ("rank", C.c_int), ("bsrc", C.c_void_p),
+                ("drow", C.c_void_p), ("A", C.c_void_p), ("a_dtype", C.c_int), ("in_dim", C.c_int),
+                ("acol_seg", C.c_int), ("acol_off0", C.c_int), ("acol_off1", C.c_int), ("scale", C.c_float)]
+
+
+DT = {"bf16": 0, "f16": 1, "f32": 2}
+
+
+def _fold(iris, w, w0, B, A, bsrc, drow, scale, seg=None, off0=0, off1=0):
+    """iris_launch_lora_fold on torch tensors; returns the CUDA error code."""
     import torch
-    fn = iris.lib().iris_launch_lora_merge
-    fn.restype = C.c_int
-    fn.argtypes = [C.c_void_p, C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_void_p, C.c_int, C.c_int,
-                   C.c_int, C.c_float, C.c_void_p]
-    rc = fn(w.data_ptr(), w0.data_ptr(), ld, B.data_ptr(), A.data_ptr(), rowmap.data_ptr(), nrows, cols, rank,
-            scale, torch.cuda.current_stream().cuda_stream)
+    lib = iris.lib()
+    lib.iris_launch_lora_fold.restype = C.c_int
+    lib.iris_launch_lora_fold.argtypes = [C.POINTER(LoraFold), C.c_void_p, C.c_size_t, C.c_void_p, C.c_int,
+                                          C.c_void_p, C.POINTER(C.c_int)]
+    lib.iris_lora_fold_scratch_bytes.restype = C.c_size_t
+    lib.iris_lora_fold_scratch_bytes.argtypes = [C.c_int, C.c_int, C.c_int, C.c_int]
+    dt = {torch.bfloat16: "bf16", torch.float16: "f16", torch.float32: "f32"}
+    cols = w.shape[1]
+    f = LoraFold(w.data_ptr(), w0.data_ptr(), cols, cols, bsrc.numel(), B.data_ptr(), DT[dt[B.dtype]], B.shape[1],
+                 bsrc.data_ptr(), drow.data_ptr(), A.data_ptr(), DT[dt[A.dtype]], A.shape[1],
+                 cols if seg is None else seg, off0, off1, scale)
+    split = int(B.dtype != torch.bfloat16 or A.dtype != torch.bfloat16)
+    nb = lib.iris_lora_fold_scratch_bytes(bsrc.numel(), cols, B.shape[1], split)
+    scratch = torch.empty(max(nb, 1), dtype=torch.uint8, device=w.device)
+    status = torch.zeros(1, dtype=torch.int32, device=w.device)
+    n = C.c_int(0)
+    rc = lib.iris_launch_lora_fold(C.byref(f), scratch.data_ptr(), nb, status.data_ptr(), 148,
+                                   torch.cuda.current_stream().cuda_stream, C.byref(n))
     torch.cuda.synchronize()
+    assert int(status.item()) == 0
     return rc
 
 
 def test_fold_kernel_reproduces_reference_fixture(iris):
     """debug/fixtures/lora: W' = 0 + B A, then x W'^T equals the MLX golden
-    delta (to within the bf16 rounding of the folded weight)."""
+    delta (to within the bf16 rounding of the folded weight); f32 operands (the
+    fixture's type) take the hi/lo split path."""
     import torch
     g = dict(np.load(os.path.join(GOLDEN, "lora_fixture.npz")))
     dev = torch.device("cuda:0")
     for key, gold, rows in (("transformer.transformer_blocks.0.attn.to_q", "golden", 8),
                             ("transformer.single_transformer_blocks.0.attn.to_qkv_mlp_proj", "golden_single1", 12),
                             ("transformer.single_transformer_blocks.0.attn.to_out", "golden_single2", 8)):
-        A = torch.from_numpy(g[f"t:{key}.lora_A.weight"]).to(dev).contiguous()
+        a = np.zeros((4, 128), np.float32)  # fold widths are multiples of 128: the 8 real columns, zeros after
+        a[:, :8] = g[f"t:{key}.lora_A.weight"]
+        A = torch.from_numpy(a).to(dev)
         B = torch.from_numpy(g[f"t:{key}.lora_B.weight"]).to(dev).contiguous()
-        w0 = torch.zeros(rows, 8, dtype=torch.bfloat16, device=dev)
+        w0 = torch.zeros(rows, 128, dtype=torch.bfloat16, device=dev)
         w = torch.zeros_like(w0)
-        rowmap = torch.arange(rows, dtype=torch.int32, device=dev)
-        assert _merge(iris, w, w0, 8, B, A, rowmap, rows, 8, 4, 1.0) == 0
-        out = torch.from_numpy(g["x"]).to(dev) @ w.float().T
+        idx = torch.arange(rows, dtype=torch.int32, device=dev)
+        assert _fold(iris, w, w0, B, A, idx, idx, 1.0) == 0
+        out = torch.from_numpy(g["x"]).to(dev) @ w[:, :8].float().T
         assert rel_l2(out.cpu().numpy(), g[gold]) < TOL
 
 
-def test_fold_kernel_matches_torch(iris):
-    """Scattered rows (a permuted subset), rank 40 (two rank chunks, ragged),
-    ragged row and column tiles, negative scale, w and w0 distinct: each folded
-    element is within one bf16 step of the f64 fold, 99.9 % are its exact bf16
-    rounding, and rows outside the map are untouched."""
+@pytest.mark.parametrize("dtype,cols", [("bf16", 3072), ("f32", 3200), ("f16", 3072)])
+def test_fold_kernel_matches_torch(iris, dtype, cols):
+    """Gathered B rows onto scattered target rows (517 of 700), a two-segment
+    column map, rank 40, negative scale, w and w0 distinct; 3072 columns run
+    on the CTA-pair GEMM, 3200 on the single-CTA one.  Each folded element is
+    within one bf16 step of the f64 fold, 99.9 % are its exact bf16 rounding,
+    and rows outside the map are untouched (f32 operands: 99 %)."""
     import torch
     dev = torch.device("cuda:0")
+    tdt = {"bf16": torch.bfloat16, "f32": torch.float32, "f16": torch.float16}[dtype]
     gen = torch.Generator(device="cpu").manual_seed(3)
-    R, Cc, r, n = 700, 3072 + 136, 40, 517
-    w0 = (0.05 * torch.randn(R, Cc, generator=gen)).bfloat16().to(dev)
+    R, r, n, nb, ind = 700, 40, 517, 900, cols + 300
+    seg, off0, off1 = cols // 2, 100, cols // 2 + 250
+    w0 = (0.05 * torch.randn(R, cols, generator=gen)).bfloat16().to(dev)
     w = torch.full_like(w0, 7.0)
-    B = (0.1 * torch.randn(n, r, generator=gen)).to(dev)
-    A = (0.1 * torch.randn(r, Cc, generator=gen)).to(dev)
-    rows = torch.randperm(R, generator=gen)[:n].to(torch.int32).to(dev)
-    assert _merge(iris, w, w0, Cc, B, A, rows, n, Cc, r, -0.7) == 0
-    exp = w0.float()[rows.long()] + (-0.7) * (B.double() @ A.double()).float()
-    got = w.float()[rows.long()]
+    B = (0.1 * torch.randn(nb, r, generator=gen)).to(tdt).to(dev)
+    A = (0.1 * torch.randn(r, ind, generator=gen)).to(tdt).to(dev)
+    drow = torch.randperm(R, generator=gen)[:n].to(torch.int32).to(dev)
+    bsrc = torch.randperm(nb, generator=gen)[:n].to(torch.int32).to(dev)
+    assert _fold(iris, w, w0, B, A, bsrc, drow, -0.7, seg, off0, off1) == 0
+    acol = torch.cat([torch.arange(seg) + off0, torch.arange(cols - seg) + off1]).to(dev)
+    delta = (B.double()[bsrc.long()] @ A.double()[:, acol]) * -0.7
+    exp = w0.double()[drow.long()] + delta
+    got = w.double()[drow.long()]
     err = (got - exp).abs()
-    # one bf16 step (2^-7 relative; a sum on the other side of a rounding
-    # boundary) plus f32 summation noise where w0 and the update cancel
+    # one bf16 step (2^-7 relative; a sum on the other side of a rounding boundary)
+    # plus f32 accumulation noise where w0 and the update cancel
     assert bool((err <= exp.abs() * 2.0 ** -7 + 1e-6).all()), float((err - exp.abs() * 2.0 ** -7).max())
-    assert float((got == exp.bfloat16().float()).float().mean()) > 0.999
+    # bf16 and f16 operands are exact; f32 ones keep 16 of 24 bits (hi + lo)
+    exact = float((got == exp.float().bfloat16().double()).double().mean())
+    assert exact > (0.99 if dtype == "f32" else 0.999), exact
     mask = torch.ones(R, dtype=torch.bool, device=dev)
-    mask[rows.long()] = False
+    mask[drow.long()] = False
     assert bool((w[mask] == 7.0).all())
-    # argument checks: columns not a multiple of 8, rank 0
-    assert _merge(iris, w, w0, Cc, B, A, rows, n, Cc - 4, r, 1.0) != 0
-    assert _merge(iris, w, w0, Cc, B, A, rows, n, Cc, 0, 1.0) != 0
+
+
+def test_fold_kernel_rejects_bad_shapes(iris):
+    import torch
+    dev = torch.device("cuda:0")
+    w0 = torch.zeros(64, 256, dtype=torch.bfloat16, device=dev)
+    w = torch.zeros_like(w0)
+    B = torch.zeros(64, 8, dtype=torch.bfloat16, device=dev)
+    A = torch.zeros(8, 256, dtype=torch.bfloat16, device=dev)
+    idx = torch.arange(64, dtype=torch.int32, device=dev)
+    assert _fold(iris, w[:, :200], w0[:, :200], B, A, idx, idx, 1.0) != 0  # columns not a multiple of 128
+    assert _fold(iris, w, w0, B[:, :0], A[:0], idx, idx, 1.0) != 0          # rank 0
+    flat = torch.zeros(64 * 256 + 8, dtype=torch.bfloat16, device=dev)
+    assert _fold(iris, flat[1:1 + 64 * 256].view(64, 256), w0, B, A, idx, idx, 1.0) != 0  # misaligned w
