@@ -71,11 +71,11 @@ def parse_args(argv=None):
                          "(same kernels and shapes, less memory); not a benchmark number")
     ap.add_argument("--profile-out", default=None, help="write the per-kernel CUDA-event profile (JSON)")
     ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "c5b", "vae512", "vae1024", "qwen3",
-                                                     "lora"],
+                                                     "lora", "load"],
                     help="c2 (default) is the benchmark; the others measure the remaining SURVEY configs "
                          "on one GPU (c1 K4B 64x64 single forward, c3 K4B 1024x1024 CFG 4.0, c4 K9B "
                          "1792x1792, c5 Z-Image 1024x1024, c5b K4B + 2 references, lora: c2 with a "
-                         "rank-32 LoRA folded into the weights)")
+                         "rank-32 LoRA folded into the weights, load: Klein-4B safetensors -> resident)")
     return ap.parse_args(argv)
 
 
@@ -248,6 +248,189 @@ def write_bfl_lora(path, mcfg, rank, seed, std=0.02):
         f.write(hj)
         for b in blobs:
             f.write(b.tobytes())
+
+
+# ----------------------------------------------------------------------------- config "load"
+def klein_tensor_shapes(mcfg):
+    """(name, shape) of every tensor the Flux loaders read, in the diffusers layout."""
+    H = mcfg["num_attention_heads"] * mcfg["attention_head_dim"]
+    F = int(H * mcfg.get("mlp_ratio", 3.0))
+    D, C, T = mcfg["attention_head_dim"], mcfg["in_channels"], mcfg["joint_attention_dim"]
+    s = [("x_embedder.weight", (H, C)), ("context_embedder.weight", (H, T)),
+         ("time_guidance_embed.timestep_embedder.linear_1.weight", (H, 256)),
+         ("time_guidance_embed.timestep_embedder.linear_2.weight", (H, H)),
+         ("double_stream_modulation_img.linear.weight", (6 * H, H)),
+         ("double_stream_modulation_txt.linear.weight", (6 * H, H)),
+         ("single_stream_modulation.linear.weight", (3 * H, H))]
+    for i in range(mcfg["num_layers"]):
+        p = f"transformer_blocks.{i}."
+        for a in ("norm_q", "norm_k", "norm_added_q", "norm_added_k"):
+            s.append((p + f"attn.{a}.weight", (D,)))
+        for a in ("to_q", "to_k", "to_v", "to_out.0", "add_q_proj", "add_k_proj", "add_v_proj", "to_add_out"):
+            s.append((p + f"attn.{a}.weight", (H, H)))
+        for f in ("ff", "ff_context"):
+            s += [(p + f"{f}.linear_in.weight", (2 * F, H)), (p + f"{f}.linear_out.weight", (H, F))]
+    for i in range(mcfg["num_single_layers"]):
+        p = f"single_transformer_blocks.{i}."
+        s += [(p + "attn.norm_q.weight", (D,)), (p + "attn.norm_k.weight", (D,)),
+              (p + "attn.to_qkv_mlp_proj.weight", (3 * H + 2 * F, H)), (p + "attn.to_out.weight", (H, H + F))]
+    s += [("norm_out.linear.weight", (2 * H, H)), ("proj_out.weight", (C, H))]
+    return s
+
+
+def write_klein_files(model_dir, mcfg, shards=2):
+    """A Klein-shaped transformer/ directory in the released layout (bf16 shards
+    + diffusion_pytorch_model.safetensors.index.json + config.json); values are a
+    seeded N(0, 0.02) pattern repeated over each tensor (the load path does not
+    look at them).  Returns the bytes of tensor data."""
+    import struct
+    tdir = os.path.join(model_dir, "transformer")
+    os.makedirs(tdir, exist_ok=True)
+    with open(os.path.join(tdir, "config.json"), "w") as f:
+        json.dump(dict(_class_name="Flux2Transformer2DModel", **mcfg), f)
+    specs = klein_tensor_shapes(mcfg)
+    x = 0.02 * np.random.default_rng(WEIGHT_SEED).standard_normal(1 << 20, dtype=np.float32)
+    u = x.view(np.uint32).astype(np.uint64)
+    pattern = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+    total = sum(int(np.prod(shp)) * 2 for _, shp in specs)
+    per, groups, cur, acc = total / shards, [], [], 0
+    for name, shp in specs:
+        cur.append((name, shp))
+        acc += int(np.prod(shp)) * 2
+        if acc >= per * (len(groups) + 1) and len(groups) < shards - 1:
+            groups.append(cur)
+            cur = []
+    groups.append(cur)
+    weight_map = {}
+    for gi, grp in enumerate(groups):
+        fname = f"diffusion_pytorch_model-{gi + 1:05d}-of-{len(groups):05d}.safetensors"
+        header, off = {}, 0
+        for name, shp in grp:
+            n = int(np.prod(shp)) * 2
+            header[name] = {"dtype": "BF16", "shape": list(shp), "data_offsets": [off, off + n]}
+            weight_map[name] = fname
+            off += n
+        hj = json.dumps(header).encode()
+        hj += b" " * ((8 - len(hj) % 8) % 8)
+        with open(os.path.join(tdir, fname), "wb") as f:
+            f.write(struct.pack("<Q", len(hj)))
+            f.write(hj)
+            for name, shp in grp:
+                f.write(np.resize(pattern, int(np.prod(shp))).tobytes())
+    with open(os.path.join(tdir, "diffusion_pytorch_model.safetensors.index.json"), "w") as f:
+        json.dump({"metadata": {"total_size": total}, "weight_map": weight_map}, f)
+    return total
+
+
+def pinned_h2d_gbs(nbytes=1 << 30, reps=5):
+    """Measured host-to-device copy bandwidth from pinned memory (the load path's ceiling)."""
+    import torch
+    h = torch.empty(nbytes, dtype=torch.uint8).pin_memory()
+    d = torch.empty(nbytes, dtype=torch.uint8, device="cuda")
+    d.copy_(h, non_blocking=True)
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        d.copy_(h, non_blocking=True)
+    e1.record()
+    e1.synchronize()
+    return reps * nbytes / (e0.elapsed_time(e1) / 1000.0) / 1e9
+
+
+LOAD_METRIC = "Klein-4B transformer loads/s (bf16 safetensors, 2 shards, page cache -> resident in HBM)"
+
+
+def load_config(nbytes):
+    return {"workload": "iris_transformer_load_safetensors equivalent: Klein-4B transformer/ directory, "
+                        "2 bf16 shards + index, files already in the host page cache",
+            "model": "klein-4b layout (synthetic values)", "file_bytes": nbytes, "global_batch": 1,
+            "parallelism": "single GPU"}
+
+
+def run_load(args):
+    """Model load: the reference's iris_transformer_load_safetensors against
+    iris_cuda_flux_load on the same files (written once, then in the page cache)."""
+    import torch
+    import iris_cuda
+    rank, world, local = dist_env()
+    if rank != 0:
+        return 0
+    torch.cuda.set_device(local)
+    lib = iris_cuda.lib()
+    if lib.iris_cuda_init(local) != 0:
+        raise iris_cuda.IrisCudaError(iris_cuda.last_error())
+    tmp = tempfile.TemporaryDirectory(dir=os.environ.get("IRIS_BENCH_TMP"))
+    nbytes = write_klein_files(tmp.name, K4B)
+    times = []
+    for i in range(args.warmup + args.steps):
+        t0 = time.perf_counter()
+        m = iris_cuda.Flux.load(tmp.name)
+        dt = time.perf_counter() - t0
+        if i >= args.warmup:
+            times.append(dt)
+        m.close()
+    peak = pinned_h2d_gbs()
+    per = statistics.mean(times)
+    gbs = nbytes / per / 1e9
+    cpu = None
+    if not args.no_cpu_baseline:
+        cpu = ref_load_seconds(tmp.name)
+        cpu = {"value": 1.0 / cpu[0], "unit": "loads/s", "cores": cpu[1], "kind": "reference",
+               "sample": "reference make-blas build (oracle/_ref): iris_transformer_load_safetensors on the same "
+                         "files, one load"}
+    line = {"metric": LOAD_METRIC, "value": 1.0 / per, "unit": "loads/s", "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": per * 1000.0, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": load_config(nbytes),
+            "e2e": {"value": 1.0 / per, "unit": "loads/s", "h2d_bytes_per_step": nbytes, "d2h_bytes_per_step": 0,
+                    "note": "the load is host-to-device by nature: value and e2e are the same API call"},
+            "gpu_launches": None,
+            "roofline": {"kernel": "pinned-ring upload (copy threads + cudaMemcpyAsync)", "bound": "h2d",
+                         "achieved": gbs, "peak": peak, "unit": "GB/s", "frac": gbs / peak,
+                         "peak_source": "pinned host->device copy measured in this run", "traffic": None},
+            "cpu_baseline": cpu}
+    print(json.dumps(line), flush=True)
+    tmp.cleanup()
+    return 0
+
+
+def ref_load_seconds(model_dir):
+    from oracle.ref_lib import RefLib
+    ref = RefLib("blas")
+    cores = len(os.sched_getaffinity(0))
+    ref.set_threads(cores)
+    t0 = time.perf_counter()
+    h = ref.lib.ref_flux_load(model_dir.encode())
+    dt = time.perf_counter() - t0
+    if not h:
+        raise RuntimeError("reference load failed")
+    ref.lib.ref_flux_free(h)
+    return dt, cores
+
+
+def run_load_reference(args):
+    rank, world, _ = dist_env()
+    if rank != 0:
+        return 0
+    tmp = tempfile.TemporaryDirectory(dir=os.environ.get("IRIS_BENCH_TMP"))
+    nbytes = write_klein_files(tmp.name, K4B)
+    ts = []
+    cores = 1
+    for i in range(args.warmup + args.steps):
+        dt, cores = ref_load_seconds(tmp.name)
+        if i >= args.warmup:
+            ts.append(dt)
+    per = statistics.mean(ts)
+    line = {"impl": "reference", "metric": LOAD_METRIC, "value": 1.0 / per, "unit": "loads/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": per * 1000.0, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": load_config(nbytes),
+            "cpu_baseline": {"value": 1.0 / per, "unit": "loads/s", "cores": cores, "kind": "reference",
+                             "sample": "iris_transformer_load_safetensors (make-blas build), whole model"},
+            "e2e": {"value": 1.0 / per, "unit": "loads/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+    tmp.cleanup()
+    return 0
 
 
 # ----------------------------------------------------------------------------- CPU reference arm
@@ -1065,6 +1248,8 @@ def main(argv=None):
         return run_qwen3_reference(args) if args.impl == "reference" else run_qwen3(args)
     if args.config.startswith("vae"):
         return run_vae_reference(args) if args.impl == "reference" else run_vae(args)
+    if args.config == "load":
+        return run_load_reference(args) if args.impl == "reference" else run_load(args)
     if args.impl == "reference":
         return run_reference(args)
     if args.config not in ("c2", "lora"):

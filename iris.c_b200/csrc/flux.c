@@ -312,7 +312,7 @@ iris_cuda_flux_t *iris_cuda_flux_load_tp(const char *model_dir, int tp_rank, int
     }
     int rc = load_weights(tf, &ws);
     st_close(&ws.st);
-    if (ws.host_stage) cudaFreeHost(ws.host_stage);
+    iris_wsrc_free(&ws);
     if (rc) { iris_cuda_flux_free(tf); return NULL; }
     return tf;
 }

@@ -81,6 +81,7 @@ typedef struct {
 typedef struct {
     int nfiles;
     void *maps[16];
+    int fds[16];          /* kept open for pread (the weight uploads read with it) */
     size_t sizes[16];
     size_t data_start[16];
     int ntensors;
@@ -102,9 +103,21 @@ typedef struct {
     uint64_t seed;
     float std;
     int norm_unit;        /* norm-scale tensors drawn as 1 + N(0, 0.1)       */
-    uint16_t *host_stage;
-    size_t host_stage_n;
+    /* file uploads (weights.c): a ring of pinned chunks filled by a pool of
+       copy threads while earlier chunks are in flight to the device */
+    uint8_t *ring[4];
+    cudaEvent_t ring_ev[4];
+    int ring_i;
+    struct iris_cpool *pool;
+    void *d_raw;          /* device landing for f32 / f16 tensors (converted there) */
+    size_t d_raw_n;
+    double bytes;         /* file bytes uploaded */
 } iris_wsrc_t;
+
+/* finish a weight source's uploads and release its device landing */
+void iris_wsrc_free(iris_wsrc_t *ws);
+/* the process-wide upload ring and reader threads (iris_cuda_cleanup) */
+void iris_wsrc_release_staging(void);
 
 /* Write the reference-layout tensor `name` ([numel] bf16) to device memory. */
 int iris_wsrc_get(iris_wsrc_t *ws, const char *name, size_t numel, uint16_t *d_dst);

@@ -200,6 +200,7 @@ cudaError_t iris_launch_nchw_to_tokens(const float *x, int c, int n, void *out, 
                                        cudaStream_t stream);
 cudaError_t iris_launch_f32_to_bf16(const float *x, void *out, long n, cudaStream_t stream);
 cudaError_t iris_launch_bf16_to_f32(const void *x, float *out, long n, cudaStream_t stream);
+cudaError_t iris_launch_f16_to_bf16(const void *x, void *out, long n, cudaStream_t stream);
 /* z += dt * v ; or with CFG: z += dt * (vu + g (vc - vu)) */
 cudaError_t iris_launch_euler(float *z, const float *v, const float *v_uncond, float guidance,
                               float dt, long n, cudaStream_t stream);

@@ -77,35 +77,24 @@ static void *q3_dalloc(iris_cuda_qwen3_t *m, size_t bytes) {
 
 /* ------------------------------------------------------------------ loading */
 typedef struct {
-    const st_model_t *st;   /* NULL: seeded device RNG */
+    iris_wsrc_t *file;      /* NULL: seeded device RNG (the file path shares the
+                               pipelined upload of the DiT loaders, weights.c) */
     uint64_t seed;
-    uint16_t *stage;        /* host staging for file tensors */
-    size_t stage_n;
 } q3_src_t;
 
 /* bf16 tensor `name` of numel values to d_dst: from the file, or random
  * N(0, std) (+ mean) from the device RNG keyed by the name */
 static int q3_get_bf16(q3_src_t *src, const char *name, size_t numel, uint16_t *d_dst, float mean, float std) {
-    if (!src->st) {
+    if (!src->file) {
         cudaError_t e = iris_launch_randn_bf16(d_dst, (long)numel, src->seed, iris_crc32(name), mean, std, g_rt.stream);
         return iris_cuda_check(e, "randn");
     }
-    const st_tensor_t *t = st_find(src->st, name);
-    if (!t) return iris_fail(IRIS_CUDA_ERR_IO, "text encoder tensor %s missing", name);
-    if (src->stage_n < numel) {
-        free(src->stage);
-        src->stage = (uint16_t *)malloc(numel * 2);
-        src->stage_n = src->stage ? numel : 0;
-        if (!src->stage) return iris_fail(IRIS_CUDA_ERR_OOM, "staging");
-    }
-    if (st_read_bf16(src->st, t, src->stage, numel))
-        return iris_fail(IRIS_CUDA_ERR_IO, "text encoder tensor %s mis-sized", name);
-    return iris_h2d(d_dst, src->stage, numel * 2);
+    return iris_wsrc_get(src->file, name, numel, d_dst);
 }
 
 /* f32 vector `name` (norm scales) through a bf16 device temp */
 static int q3_get_vec(q3_src_t *src, const char *name, int n, float *d_dst, uint16_t *tmp) {
-    int rc = q3_get_bf16(src, name, (size_t)n, tmp, src->st ? 0.f : 1.0f, src->st ? 0.f : 0.1f);
+    int rc = q3_get_bf16(src, name, (size_t)n, tmp, src->file ? 0.f : 1.0f, src->file ? 0.f : 0.1f);
     if (!rc) rc = iris_cuda_check(iris_launch_bf16_to_f32(tmp, d_dst, n, g_rt.stream), "bf16 to f32");
     /* tmp is rewritten by the next (host-synchronous) upload */
     if (!rc) rc = iris_cuda_check(cudaStreamSynchronize(g_rt.stream), "bf16 to f32");
@@ -217,8 +206,7 @@ static iris_cuda_qwen3_t *q3_create(const iris_cuda_qwen3_config_t *cfg, q3_src_
     }
     free(ones);
     if (!rc) rc = q3_load_layers(m, src);
-    free(src->stage);
-    src->stage = NULL;
+    if (!rc) rc = iris_cuda_check(cudaStreamSynchronize(g_rt.stream), "text encoder upload");
     if (rc) { iris_cuda_qwen3_free(m); return NULL; }
     return m;
 }
@@ -246,21 +234,23 @@ iris_cuda_qwen3_t *iris_cuda_qwen3_load(const char *model_dir) {
         if (!json_get_number(buf, "num_hidden_layers", &d) && d > 0) c.layers = (int)d;
         if (!json_get_number(buf, "rope_theta", &d) && d > 0) c.rope_theta = (float)d;
     }
-    st_model_t st;
-    if (st_open_dir(&st, model_dir)) {
+    iris_wsrc_t ws;
+    memset(&ws, 0, sizeof(ws));
+    if (st_open_dir(&ws.st, model_dir)) {
         iris_fail(IRIS_CUDA_ERR_IO, "cannot open text encoder weights in %s", model_dir);
         return NULL;
     }
-    q3_src_t src = {&st, 0, NULL, 0};
+    q3_src_t src = {&ws, 0};
     iris_cuda_qwen3_t *m = q3_create(&c, &src);
-    st_close(&st);
+    iris_wsrc_free(&ws);  /* waits for the last uploads */
+    st_close(&ws.st);
     return m;
 }
 
 iris_cuda_qwen3_t *iris_cuda_qwen3_random(const iris_cuda_qwen3_config_t *cfg, uint64_t seed) {
     if (!cfg) { iris_fail(IRIS_CUDA_ERR_ARG, "null config"); return NULL; }
     if (iris_rt_ensure()) return NULL;
-    q3_src_t src = {NULL, seed, NULL, 0};
+    q3_src_t src = {NULL, seed};
     iris_cuda_qwen3_t *m = q3_create(cfg, &src);
     if (m && iris_cuda_synchronize()) { iris_cuda_qwen3_free(m); return NULL; }
     return m;

@@ -15,6 +15,7 @@
 #include "ptx.cuh"
 
 #include <cuda_bf16.h>
+#include <cuda_fp16.h>
 #include <math.h>
 #include <stdint.h>
 
@@ -335,6 +336,12 @@ __global__ void f32_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* _
   long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
   long stride = (long)gridDim.x * blockDim.x;
   for (; i < n; i += stride) out[i] = __float2bfloat16_rn(x[i]);
+}
+
+__global__ void f16_to_bf16_kernel(const __half* __restrict__ x, __nv_bfloat16* __restrict__ out, long n) {
+  long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
+  long stride = (long)gridDim.x * blockDim.x;
+  for (; i < n; i += stride) out[i] = __float2bfloat16_rn(__half2float(x[i]));
 }
 
 __global__ void bf16_to_f32_kernel(const __nv_bfloat16* __restrict__ x, float* __restrict__ out,
@@ -695,6 +702,13 @@ cudaError_t iris_launch_nchw_to_tokens(const float* x, int c, int n, void* out, 
 cudaError_t iris_launch_f32_to_bf16(const float* x, void* out, long n, cudaStream_t stream) {
   if (n <= 0) return cudaSuccess;
   f32_to_bf16_kernel<<<grid_for(n, 256), 256, 0, stream>>>(x, static_cast<__nv_bfloat16*>(out), n);
+  return cudaGetLastError();
+}
+
+cudaError_t iris_launch_f16_to_bf16(const void* x, void* out, long n, cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  f16_to_bf16_kernel<<<grid_for(n, 256), 256, 0, stream>>>(static_cast<const __half*>(x),
+                                                           static_cast<__nv_bfloat16*>(out), n);
   return cudaGetLastError();
 }
 

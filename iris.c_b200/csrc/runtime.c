@@ -111,6 +111,7 @@ int iris_cuda_available(void) { return iris_rt_ensure() == IRIS_CUDA_OK; }
 void iris_cuda_cleanup(void) {
     if (!g_rt.initialized) return;
     cudaStreamSynchronize(g_rt.stream);
+    iris_wsrc_release_staging();
     cudaFree(g_rt.d_status);
     cudaStreamDestroy(g_rt.stream);
     memset(&g_rt, 0, sizeof(g_rt));

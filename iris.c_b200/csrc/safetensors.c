@@ -156,17 +156,17 @@ static int open_file(st_model_t *m, const char *path) {
     struct stat sb;
     if (fstat(fd, &sb) != 0 || sb.st_size < 8) { close(fd); return -1; }
     void *map = mmap(NULL, (size_t)sb.st_size, PROT_READ, MAP_PRIVATE, fd, 0);
-    close(fd);
-    if (map == MAP_FAILED) return -1;
+    if (map == MAP_FAILED) { close(fd); return -1; }
     uint64_t hlen;
     memcpy(&hlen, map, 8);
-    if (hlen + 8 > (uint64_t)sb.st_size) { munmap(map, (size_t)sb.st_size); return -1; }
+    if (hlen + 8 > (uint64_t)sb.st_size) { munmap(map, (size_t)sb.st_size); close(fd); return -1; }
     char *hdr = malloc(hlen + 1);
-    if (!hdr) { munmap(map, (size_t)sb.st_size); return -1; }
+    if (!hdr) { munmap(map, (size_t)sb.st_size); close(fd); return -1; }
     memcpy(hdr, (char *)map + 8, hlen);
     hdr[hlen] = 0;
     int f = m->nfiles;
     m->maps[f] = map;
+    m->fds[f] = fd;
     m->sizes[f] = (size_t)sb.st_size;
     m->data_start[f] = 8 + hlen;
     m->nfiles++;
@@ -249,7 +249,10 @@ int st_open_file(st_model_t *m, const char *path) {
 }
 
 void st_close(st_model_t *m) {
-    for (int i = 0; i < m->nfiles; i++) munmap(m->maps[i], m->sizes[i]);
+    for (int i = 0; i < m->nfiles; i++) {
+        munmap(m->maps[i], m->sizes[i]);
+        close(m->fds[i]);
+    }
     free(m->tensors);
     memset(m, 0, sizeof(*m));
 }

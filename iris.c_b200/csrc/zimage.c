@@ -324,7 +324,7 @@ iris_cuda_zimage_t *iris_cuda_zimage_load(const char *model_dir) {
     iris_cuda_zimage_t *z = zi_new(&cfg);
     int rc = z ? load_all(z, &ws) : IRIS_CUDA_ERR_ARG;
     st_close(&ws.st);
-    if (ws.host_stage) cudaFreeHost(ws.host_stage);
+    iris_wsrc_free(&ws);
     if (rc) { iris_cuda_zimage_free(z); return NULL; }
     return z;
 }
