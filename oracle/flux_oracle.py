@@ -147,8 +147,18 @@ def swiglu(x, w_in, w_out, mlp):
     return linear(silu(gu[:, :mlp]) * gu[:, mlp:], w_out)
 
 
-def double_block(w, i, img, txt, mod_img, mod_txt, rope_i, rope_t, d):
-    """One MM-DiT double block (double_block_forward :2366-2614). Returns new (img, txt)."""
+def _ip_add(ip, blk, q_pre, rows):
+    """IP-Adapter contribution after block blk (ip_inject_block :2355): rows +=
+    s * SDPA(pre-RoPE image Q, k_ip, v_ip) (oracle/ip_oracle.py)."""
+    from oracle import ip_oracle
+    k, v = ip["kv"][blk]
+    return ip_oracle.inject(ip["adapter"], blk, q_pre, k, v, rows)
+
+
+def double_block(w, i, img, txt, mod_img, mod_txt, rope_i, rope_t, d, ip=None):
+    """One MM-DiT double block (double_block_forward :2366-2614). Returns new (img, txt).
+    ``ip``: an ip_oracle.ip_context; its contribution goes to the image rows
+    after the block, from the post-QK-norm, pre-RoPE image Q (:2440-2446, :2607-2612)."""
     H, heads, F = d["hidden"], d["heads"], d["mlp"]
     p = f"transformer_blocks.{i}."
     mi = [mod_img[j * H:(j + 1) * H] for j in range(6)]
@@ -158,7 +168,9 @@ def double_block(w, i, img, txt, mod_img, mod_txt, rope_i, rope_t, d):
     qi = linear(xi, w[p + "attn.to_q.weight"])
     ki = linear(xi, w[p + "attn.to_k.weight"])
     vi = linear(xi, w[p + "attn.to_v.weight"])
-    qi = apply_rope(head_rms_norm(qi, w[p + "attn.norm_q.weight"], heads), *rope_i, heads)
+    qi = head_rms_norm(qi, w[p + "attn.norm_q.weight"], heads)
+    qi_pre = qi
+    qi = apply_rope(qi, *rope_i, heads)
     ki = apply_rope(head_rms_norm(ki, w[p + "attn.norm_k.weight"], heads), *rope_i, heads)
 
     xt = adaln(txt, mt[0], mt[1])
@@ -179,11 +191,16 @@ def double_block(w, i, img, txt, mod_img, mod_txt, rope_i, rope_t, d):
                                w[p + "ff.linear_out.weight"], F)
     txt = txt + mt[5] * swiglu(adaln(txt, mt[3], mt[4]), w[p + "ff_context.linear_in.weight"],
                                w[p + "ff_context.linear_out.weight"], F)
-    return img.astype(F32), txt.astype(F32)
+    img = img.astype(F32)
+    if ip is not None:
+        img = _ip_add(ip, i, qi_pre, img)
+    return img, txt.astype(F32)
 
 
-def single_block(w, i, hidden, mod_single, rope_all, d):
-    """One parallel DiT block over [TXT, IMG] (single_block_forward :3761-3928)."""
+def single_block(w, i, hidden, mod_single, rope_all, d, ip=None, n_txt=0):
+    """One parallel DiT block over [TXT, IMG] (single_block_forward :3761-3928).
+    ``ip``: contribution to the rows after the n_txt text rows, adapter block
+    n_double + i (:3848-3855, :3921-3926)."""
     H, heads, F = d["hidden"], d["heads"], d["mlp"]
     p = f"single_transformer_blocks.{i}."
     shift, scale, gate = (mod_single[j * H:(j + 1) * H] for j in range(3))
@@ -191,14 +208,19 @@ def single_block(w, i, hidden, mod_single, rope_all, d):
     fused = linear(x, w[p + "attn.to_qkv_mlp_proj.weight"])
     q, k, v = fused[:, :H], fused[:, H:2 * H], fused[:, 2 * H:3 * H]
     g, u = fused[:, 3 * H:3 * H + F], fused[:, 3 * H + F:]
-    q = apply_rope(head_rms_norm(q, w[p + "attn.norm_q.weight"], heads), *rope_all, heads)
+    q = head_rms_norm(q, w[p + "attn.norm_q.weight"], heads)
+    q_pre = q
+    q = apply_rope(q, *rope_all, heads)
     k = apply_rope(head_rms_norm(k, w[p + "attn.norm_k.weight"], heads), *rope_all, heads)
     a = attention(q, k, v, heads)
     cat = np.concatenate([a, silu(g) * u], axis=1)
-    return (hidden + gate * linear(cat, w[p + "attn.to_out.weight"])).astype(F32)
+    out = (hidden + gate * linear(cat, w[p + "attn.to_out.weight"])).astype(F32)
+    if ip is not None:
+        out[n_txt:] = _ip_add(ip, d["n_double"] + i, q_pre[n_txt:], out[n_txt:])
+    return out
 
 
-def forward(w, cfg, latent, txt_emb, t, refs=(), return_blocks=False):
+def forward(w, cfg, latent, txt_emb, t, refs=(), return_blocks=False, ip=None):
     """Velocity v(z, t, ctx) for one denoising step.
 
     iris_transformer_forward (:3939-4326); with ``refs`` (list of NCHW
@@ -227,13 +249,13 @@ def forward(w, cfg, latent, txt_emb, t, refs=(), return_blocks=False):
     txt = linear(txt_emb.astype(F32), w["context_embedder.weight"])
     blocks = []
     for i in range(d["n_double"]):
-        img, txt = double_block(w, i, img, txt, mods["dbl_img"], mods["dbl_txt"], rope_i, rope_t, d)
+        img, txt = double_block(w, i, img, txt, mods["dbl_img"], mods["dbl_txt"], rope_i, rope_t, d, ip)
         if return_blocks:
             blocks.append(np.concatenate([txt, img]))
     hidden = np.concatenate([txt, img])
     rope_all = (np.concatenate([rope_t[0], rope_i[0]]), np.concatenate([rope_t[1], rope_i[1]]))
     for i in range(d["n_single"]):
-        hidden = single_block(w, i, hidden, mods["single"], rope_all, d)
+        hidden = single_block(w, i, hidden, mods["single"], rope_all, d, ip, n_txt)
         if return_blocks:
             blocks.append(hidden)
     img = hidden[n_txt:n_txt + n_img]

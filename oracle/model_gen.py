@@ -120,11 +120,11 @@ def gen_tensor(seed: int, name: str, shape: tuple, kind: str, std: float = 0.02,
 
 
 def write_safetensors(path: str, tensors: dict[str, np.ndarray]) -> None:
-    """Write uint16 (bf16) / float32 arrays in the safetensors container format."""
+    """Write uint16 (bf16) / float16 / int8 / float32 arrays in the safetensors container format."""
     header = {}
     off = 0
     for name, arr in tensors.items():
-        dt = "BF16" if arr.dtype == np.uint16 else "F32"
+        dt = {np.dtype(np.uint16): "BF16", np.dtype(np.float16): "F16", np.dtype(np.int8): "I8"}.get(arr.dtype, "F32")
         n = arr.nbytes
         header[name] = {"dtype": dt, "shape": list(arr.shape), "data_offsets": [off, off + n]}
         off += n
@@ -237,6 +237,98 @@ def make_flux_lora(path: str, cfg: dict, fmt: str, rank: int = 8, seed: int = 0,
             vals[name] = x
     write_safetensors(path, tensors)
     return vals
+
+
+# ---------------------------------------------------------------------------
+# Flux IP-Adapter bundles (the layout iris_ip_adapter_load reads,
+# iris_ip_adapter.c:113-216: adapter_meta.json + adapter_weights.safetensors)
+# ---------------------------------------------------------------------------
+
+
+def make_ip_bundle(bundle_dir: str, cfg: dict, mode: str = "siglip", tokens: int = 8, siglip_dim: int = 64,
+                   csd_dim: int = 32, perceiver_heads: int = 4, seed: int = 0, quant: str = "bfloat16",
+                   in_norm: bool = True, gate: bool = True, style_only: bool = False,
+                   kv_std: float = 0.25) -> dict:
+    """Write a seeded IP-Adapter bundle for a Flux model of config cfg (one IP
+    block per double and single block).  mode: siglip | csd | hybrid; quant:
+    bfloat16 | float16 | float32 | int8 (large matrices as int8 + per-row
+    f32 .scale).  Returns the meta dict."""
+    d = flux_dims(cfg)
+    H, nb = d["hidden"], d["n_double"] + d["n_single"]
+    rng = np.random.default_rng(seed)
+    f32 = {}
+
+    def r(name, shape, std, mean=0.0):
+        f32[name] = (mean + std * rng.standard_normal(shape)).astype(np.float32)
+
+    T = tokens
+    r("perceiver.query_tokens", (T, H), 1.0)
+    r("perceiver.norm_weight", (H,), 0.1, 1.0)
+    r("perceiver.norm_bias", (H,), 0.1)
+    if mode == "csd":
+        r("perceiver.film_weight", (2 * H, csd_dim), 0.2)
+        r("perceiver.film_bias", (2 * H,), 0.1)
+    else:
+        for n_, shp in (("query_proj", (H, H)), ("key_proj", (H, siglip_dim)), ("value_proj", (H, siglip_dim)),
+                        ("out_proj", (H, H))):
+            r("perceiver." + n_, shp, 1.0 / np.sqrt(shp[1]))
+        if in_norm:
+            r("perceiver.in_gamma", (siglip_dim,), 0.1, 1.0)
+            r("perceiver.in_beta", (siglip_dim,), 0.1)
+    if mode == "hybrid":
+        r("csd.query_tokens", (T // 2, H), 1.0)
+        r("csd.film_weight", (2 * H, csd_dim), 0.2)
+        r("csd.film_bias", (2 * H,), 0.1)
+        r("csd.norm_weight", (H,), 0.1, 1.0)
+        r("csd.norm_bias", (H,), 0.1)
+        if gate:
+            f32["group_gate"] = rng.uniform(0.3, 1.2, (nb, 2)).astype(np.float32)
+    r("ip_k_stacked", (nb, H, H), kv_std / np.sqrt(H))
+    r("ip_v_stacked", (nb, H, H), kv_std / np.sqrt(H))
+    sc = rng.uniform(0.4, 1.0, nb).astype(np.float32)
+    if style_only:
+        sc[:d["n_double"]] = 0.0
+    f32["ip_scale"] = sc
+    big = {"perceiver.query_proj", "perceiver.key_proj", "perceiver.value_proj", "perceiver.out_proj",
+           "ip_k_stacked", "ip_v_stacked"}
+    out = {}
+    for name, x in f32.items():
+        if quant == "int8" and name in big:
+            rows = x.reshape(-1, x.shape[-1])
+            s_ = np.maximum(np.abs(rows).max(axis=1), 1e-12) / 127.0
+            out[name] = np.clip(np.rint(rows / s_[:, None]), -127, 127).astype(np.int8).reshape(x.shape)
+            out[name + ".scale"] = s_.astype(np.float32)
+        elif name in ("ip_scale", "group_gate") or quant == "float32":
+            out[name] = x
+        elif quant == "float16":
+            out[name] = x.astype(np.float16)
+        else:
+            out[name] = f32_to_bf16_bits(x)
+    meta = dict(version=1, adapter_type="ip_adapter_klein", num_blocks=nb, num_double_blocks=d["n_double"],
+                num_single_blocks=d["n_single"], hidden_dim=H, num_image_tokens=T,
+                siglip_dim=0 if mode == "csd" else siglip_dim, cond_mode=mode,
+                csd_dim=0 if mode == "siglip" else csd_dim, perceiver_heads=perceiver_heads,
+                style_only=style_only, quant=quant)
+    os.makedirs(bundle_dir, exist_ok=True)
+    with open(os.path.join(bundle_dir, "adapter_meta.json"), "w") as f:
+        json.dump(meta, f, indent=1)
+    write_safetensors(os.path.join(bundle_dir, "adapter_weights.safetensors"), out)
+    return meta
+
+
+def ip_features(mode: str, siglip_seq: int = 16, siglip_dim: int = 64, csd_dim: int = 32, seed: int = 1):
+    """Conditioning features as iris_load_ip_adapter reads them (iris.c:546-567):
+    siglip [n, siglip_dim]; csd [1, csd_dim]; hybrid [n + 1, siglip_dim], last row
+    the CSD vector zero-padded."""
+    rng = np.random.default_rng(seed)
+    if mode == "csd":
+        return rng.standard_normal((1, csd_dim)).astype(np.float32)
+    sig = (rng.standard_normal((siglip_seq, siglip_dim)) * rng.uniform(0.5, 3.0, siglip_dim)).astype(np.float32)
+    if mode == "siglip":
+        return sig
+    last = np.zeros((1, siglip_dim), np.float32)
+    last[0, :csd_dim] = rng.standard_normal(csd_dim)
+    return np.concatenate([sig, last])
 
 
 # ---------------------------------------------------------------------------

@@ -18,6 +18,8 @@
  *   ref_flux_rope_img/_txt   -> compute_rope_2d / compute_rope_text (:897, :1055)
  *   ref_flux_set_lora        -> lora_load + iris_transformer_set_lora (iris_lora.c:504, :5131)
  *   ref_lora_get             -> one adapter of lora_load's table     (iris_lora.h:28-49)
+ *   ref_ip_perceive/get_kv/inject -> iris_ip_adapter_perceive/_get_kv/_inject (iris_ip_adapter.c:331-386)
+ *   ref_flux_set_ip          -> iris_load_ip_adapter minus the file read (iris.c:520)
  *   ref_sample_euler(_cfg)   -> iris_sample_euler / _cfg            (iris_sample.c:313, :717)
  *   ref_init_noise           -> iris_init_noise                     (iris_sample.c:1146)
  *   ref_official_schedule    -> iris_official_schedule              (iris_sample.c:171)
@@ -153,6 +155,65 @@ int ref_lora_get(const char *path, int n_double, int n_single, int hidden, int k
     lora_free(l);
     return rc;
 }
+
+/* IP-Adapter stages (iris_ip_adapter.c): perceive (:331), get_kv (:366),
+ * inject (:386) with an optional schedule spec applied at (step, nsteps). */
+int ref_ip_perceive(const char *bundle, const float *feats, int n, float *out, int cap) {
+    iris_ip_adapter_t *a = iris_ip_adapter_load(bundle);
+    if (!a) return -1;
+    int need = a->num_image_tokens * a->hidden_dim;
+    int rc = need <= cap ? iris_ip_adapter_perceive(a, feats, n, out) : -2;
+    iris_ip_adapter_free(a);
+    return rc ? rc : need;
+}
+
+int ref_ip_get_kv(const char *bundle, int blk, const float *embeds, float *k, float *v) {
+    iris_ip_adapter_t *a = iris_ip_adapter_load(bundle);
+    if (!a) return -1;
+    if (blk < 0 || blk >= a->num_blocks) { iris_ip_adapter_free(a); return -2; }
+    iris_ip_adapter_get_kv(a, blk, embeds, k, v);
+    iris_ip_adapter_free(a);
+    return 0;
+}
+
+int ref_ip_inject(const char *bundle, int blk, const float *q, int seq, const float *k, const float *v,
+                  float *hidden, const char *sched, int step, int nsteps) {
+    iris_ip_adapter_t *a = iris_ip_adapter_load(bundle);
+    if (!a) return -1;
+    int rc = 0;
+    if (sched && iris_ip_adapter_set_schedule(a, sched)) rc = -3;
+    if (sched) iris_ip_adapter_set_step(a, step, nsteps);
+    if (!rc) iris_ip_adapter_inject(a, blk, q, seq, k, v, hidden);
+    iris_ip_adapter_free(a);
+    return rc;
+}
+
+/* iris_load_ip_adapter (iris.c:520) with the features in memory instead of a
+ * file: load, block-count check, ip_scale *= scale_mult, perceive, attach. */
+int ref_flux_set_ip(void *p, const char *bundle, const float *feats, int n, float scale_mult) {
+    iris_transformer_t *tf = (iris_transformer_t *)p;
+    iris_ip_adapter_t *ip = iris_ip_adapter_load(bundle);
+    if (!ip) return -1;
+    if (ip->hidden_dim != tf->hidden_size || ip->num_blocks != tf->num_double_layers + tf->num_single_layers) {
+        iris_ip_adapter_free(ip);
+        return -2;
+    }
+    if (scale_mult != 1.0f)
+        for (int i = 0; i < ip->num_blocks; i++) ip->ip_scale[i] *= scale_mult;
+    float *emb = malloc((size_t)ip->num_image_tokens * ip->hidden_dim * sizeof(float));
+    if (!emb || iris_ip_adapter_perceive(ip, feats, n, emb)) {
+        free(emb);
+        iris_ip_adapter_free(ip);
+        return -3;
+    }
+    return iris_transformer_set_ip_adapter(tf, ip, emb);
+}
+
+int ref_flux_set_ip_schedule(void *p, const char *spec) {
+    return iris_transformer_set_ip_schedule((iris_transformer_t *)p, spec);
+}
+
+void ref_flux_clear_ip(void *p) { iris_transformer_set_ip_adapter((iris_transformer_t *)p, NULL, NULL); }
 
 void ref_flux_temb(void *p, float t, float *t_emb) {
     iris_transformer_t *tf = (iris_transformer_t *)p;

@@ -65,10 +65,42 @@ class RefLib:
                                      C.POINTER(C.c_int), C.POINTER(C.c_int)]
         L.ref_vae_decode_ex.argtypes = [C.c_char_p, C.c_int, C.c_float, C.c_float, _fp, C.c_int, C.c_int,
                                         C.POINTER(C.c_uint8), C.POINTER(C.c_int), C.POINTER(C.c_int)]
+        L.ref_ip_perceive.argtypes = [C.c_char_p, _fp, C.c_int, _fp, C.c_int]
+        L.ref_ip_get_kv.argtypes = [C.c_char_p, C.c_int, _fp, _fp, _fp]
+        L.ref_ip_inject.argtypes = [C.c_char_p, C.c_int, _fp, C.c_int, _fp, _fp, _fp, C.c_char_p, C.c_int,
+                                    C.c_int]
+        L.ref_flux_set_ip.argtypes = [C.c_void_p, C.c_char_p, _fp, C.c_int, C.c_float]
+        L.ref_flux_set_ip_schedule.argtypes = [C.c_void_p, C.c_char_p]
+        L.ref_flux_clear_ip.argtypes = [C.c_void_p]
         L.ref_flux_set_lora.argtypes = [C.c_void_p, C.c_char_p, C.c_float]
         L.ref_flux_clear_lora.argtypes = [C.c_void_p]
         L.ref_lora_get.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
                                    C.POINTER(C.c_int), _fp, C.c_size_t, _fp, C.c_size_t]
+
+    def ip_perceive(self, bundle: str, feats: np.ndarray, tokens: int, hidden: int) -> np.ndarray:
+        f = np.ascontiguousarray(feats, np.float32)
+        out = np.zeros(tokens * hidden, np.float32)
+        n = f.shape[0] if f.ndim > 1 else 1
+        rc = self.lib.ref_ip_perceive(bundle.encode(), _f(f), n, _f(out), out.size)
+        if rc < 0:
+            raise RuntimeError(f"reference perceive failed ({rc})")
+        return out.reshape(tokens, hidden)
+
+    def ip_get_kv(self, bundle: str, blk: int, embeds: np.ndarray):
+        e = np.ascontiguousarray(embeds, np.float32)
+        k, v = np.zeros_like(e), np.zeros_like(e)
+        if self.lib.ref_ip_get_kv(bundle.encode(), blk, _f(e), _f(k), _f(v)):
+            raise RuntimeError("reference get_kv failed")
+        return k, v
+
+    def ip_inject(self, bundle: str, blk: int, q, k, v, hidden, sched=None, step=0, nsteps=0):
+        q, k, v = (np.ascontiguousarray(x, np.float32) for x in (q, k, v))
+        h = np.ascontiguousarray(hidden, np.float32).copy()
+        rc = self.lib.ref_ip_inject(bundle.encode(), blk, _f(q), q.shape[0], _f(k), _f(v), _f(h),
+                                    sched.encode() if sched else None, step, nsteps)
+        if rc:
+            raise RuntimeError(f"reference inject failed ({rc})")
+        return h
 
     def lora_get(self, path: str, n_double: int, n_single: int, hidden: int, kind: int, block: int,
                  cap: int = 1 << 22):
@@ -151,6 +183,17 @@ class RefFlux:
         rc = self.ref.lib.ref_flux_forward(self.h, _f(lat), h, w, _f(tx), tx.shape[0], t, _f(out))
         assert rc == 0
         return out
+
+    def set_ip(self, bundle: str, feats: np.ndarray, scale_mult: float = 1.0) -> int:
+        f = np.ascontiguousarray(feats, np.float32)
+        return self.ref.lib.ref_flux_set_ip(self.h, bundle.encode(), _f(f), f.shape[0] if f.ndim > 1 else 1,
+                                            scale_mult)
+
+    def set_ip_schedule(self, spec: str) -> int:
+        return self.ref.lib.ref_flux_set_ip_schedule(self.h, spec.encode())
+
+    def clear_ip(self):
+        self.ref.lib.ref_flux_clear_ip(self.h)
 
     def set_lora(self, path: str, scale: float) -> bool:
         return self.ref.lib.ref_flux_set_lora(self.h, path.encode(), scale) == 0

@@ -4,6 +4,7 @@ Run where the reference tree exists (it is read-only and absent on GPU boxes):
 
     make -C oracle && python tests/golden/make_golden.py        # everything
     python tests/golden/make_golden.py lora                      # lora_fixture.npz only
+    python tests/golden/make_golden.py ip                        # ip_fixture.npz only
 
 Each fixture is produced by the reference's own C code, compiled from its
 unmodified sources by oracle/Makefile and driven through
@@ -136,7 +137,40 @@ def lora_fixture() -> dict:
     return out
 
 
+IP_BUNDLES = ("bundle", "bundle_csd", "bundle_hybrid", "bundle_int8")
+IP_BINS = ("in_siglip", "in_csd", "in_hybrid", "in_img_q",
+           "gold_ip_embeds", "gold_k_ip_b0", "gold_v_ip_b0", "gold_inject_b0",
+           "gold_ip_embeds_csd", "gold_k_ip_b0_csd", "gold_v_ip_b0_csd", "gold_inject_b0_csd",
+           "gold_ip_embeds_hybrid", "gold_k_ip_b0_hybrid", "gold_v_ip_b0_hybrid", "gold_inject_b0_hybrid",
+           "gold_ip_embeds_int8", "gold_k_ip_b0_int8", "gold_v_ip_b0_int8", "gold_inject_b0_int8")
+
+
+def ip_fixture() -> dict:
+    """The reference's own IP-Adapter golden fixture (debug/fixtures/ip_adapter,
+    checked by debug/test_ip_adapter.c): the siglip, csd, hybrid and int8
+    bundles byte for byte (adapter_meta.json text and adapter_weights.safetensors
+    as uint8 arrays, to be written back to a directory by the tests), the inputs
+    and the goldens (f32, shapes from shapes.json)."""
+    d = os.path.join(REF_TREE, "debug", "fixtures", "ip_adapter")
+    out = {}
+    for b in IP_BUNDLES:
+        for fn, key in (("adapter_meta.json", "meta"), ("adapter_weights.safetensors", "weights")):
+            with open(os.path.join(d, b, fn), "rb") as f:
+                out[f"{b}:{key}"] = np.frombuffer(f.read(), np.uint8).copy()
+    with open(os.path.join(d, "shapes.json")) as f:
+        shapes = json.load(f)
+    out["shapes_json"] = np.frombuffer(json.dumps(shapes).encode(), np.uint8).copy()
+    for n in IP_BINS:
+        x = np.fromfile(os.path.join(d, n + ".bin"), "<f4")
+        out[n] = x.reshape(shapes[n]) if n in shapes else x
+    return out
+
+
 def main():
+    if sys.argv[1:] == ["ip"]:
+        np.savez_compressed(os.path.join(OUT, "ip_fixture.npz"), **ip_fixture())
+        print("wrote ip_fixture")
+        return
     if sys.argv[1:] == ["lora"]:
         np.savez_compressed(os.path.join(OUT, "lora_fixture.npz"), **lora_fixture())
         print("wrote lora_fixture")
@@ -154,6 +188,8 @@ def main():
     print("wrote sampler")
     np.savez_compressed(os.path.join(OUT, "lora_fixture.npz"), **lora_fixture())
     print("wrote lora_fixture")
+    np.savez_compressed(os.path.join(OUT, "ip_fixture.npz"), **ip_fixture())
+    print("wrote ip_fixture")
 
 
 if __name__ == "__main__":
