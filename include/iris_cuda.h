@@ -141,6 +141,31 @@ int iris_cuda_flux_unload_lora(iris_cuda_flux_t *tf);
 int iris_cuda_flux_lora_adapters(const iris_cuda_flux_t *tf);
 /* Device time of the last load's fold kernels and the bytes they moved. */
 int iris_cuda_flux_lora_stats(const iris_cuda_flux_t *tf, double *fold_ms, double *fold_bytes);
+/* IP-Adapter.  Replaces iris_load_ip_adapter (iris.h; iris.c:520): loads the
+ * bundle (adapter_meta.json + adapter_weights.safetensors, bf16 / f16 / f32 /
+ * int8; cond_mode siglip, csd or hybrid), reads the conditioning features (raw
+ * f32 rows of siglip_dim — csd: one csd_dim vector; hybrid: the SigLIP rows and
+ * the zero-padded CSD vector as the last row), perceives them once and keeps
+ * every block's k / v on the device; each forward then adds
+ * ip_scale[block] * scale_mult * schedule * SDPA(pre-RoPE image Q, k, v) to the
+ * image rows after every double and single block.  Replaces any adapter attached
+ * before; returns 0 or an error (bundle / model mismatch: hidden size and block
+ * counts must match; tensor-parallel shards are not supported). */
+int iris_cuda_flux_load_ip_adapter(iris_cuda_flux_t *tf, const char *bundle_dir, const char *features_path,
+                                   float scale_mult);
+/* The same with the features in host memory ([n_rows, row width] f32). */
+int iris_cuda_flux_load_ip_adapter_mem(iris_cuda_flux_t *tf, const char *bundle_dir, const float *features,
+                                       int n_rows, float scale_mult);
+/* Replaces iris_unload_ip_adapter. */
+int iris_cuda_flux_unload_ip_adapter(iris_cuda_flux_t *tf);
+/* Replaces iris_set_ip_schedule: "none", "late:F" (inject from step fraction F
+ * on) or "early:F" (before F); a bad spec returns an error and leaves "none". */
+int iris_cuda_flux_set_ip_schedule(iris_cuda_flux_t *tf, const char *spec);
+/* Replaces iris_transformer_set_ip_step (the samplers call it every step). */
+int iris_cuda_flux_set_ip_step(iris_cuda_flux_t *tf, int step, int num_steps);
+/* The perceived embeddings [T, H] (f32) of the attached adapter; returns T*H. */
+int iris_cuda_flux_ip_embeds(const iris_cuda_flux_t *tf, float *out, int cap);
+
 /* Host only (no device needed): the adapters of a LoRA file that match a model
  * of this shape (n_double / n_single blocks, hidden and MLP widths), like the
  * reference's "LoRA: loaded N adapters" report (iris_lora.c:276).  Returns

@@ -206,6 +206,7 @@ void iris_cuda_flux_free(iris_cuda_flux_t *tf) {
     if (!tf) return;
     iris_stream_drain();
     iris_flux_lora_release(tf);
+    iris_flux_ip_release(tf);
     plan_free(&tf->plan);
     iris_dfree(tf->w_x); iris_dfree(tf->w_ctx); iris_dfree(tf->w_t1); iris_dfree(tf->w_t2);
     iris_dfree(tf->w_mod); iris_dfree(tf->w_proj);
@@ -386,7 +387,13 @@ static void plan_free(flux_plan_t *P) {
     iris_dfree(P->k); iris_dfree(P->v); iris_dfree(P->attn); iris_dfree(P->mlp);
     iris_dfree(P->cat); iris_dfree(P->tok_img); iris_dfree(P->tok_txt);
     iris_dfree(P->ws);
+    iris_dfree(P->ip_q); iris_dfree(P->ip_o);
     memset(P, 0, sizeof(*P));
+}
+
+void iris_flux_invalidate_plan(iris_cuda_flux_t *tf) {
+    iris_stream_drain();
+    plan_free(&tf->plan);
 }
 
 /* RoPE per token and rotation pair, computed exactly like the reference's
@@ -482,6 +489,10 @@ static int plan_ensure(iris_cuda_flux_t *tf, int s_txt, int img_h, int img_w,
     PA(P->attn, sHl * 2);
     PA(P->mlp, (size_t)S * Fl * 2);
     PA(P->cat, (size_t)S * (Hl + Fl) * 2);
+    if (tf->ip) {
+        PA(P->ip_q, (size_t)S * H * 2);
+        PA(P->ip_o, (size_t)S * H * 2);
+    }
     PA(P->tok_img, (size_t)P->n_img_total * C * 2);
     PA(P->tok_txt, (size_t)s_txt * T * 2);
     if (S < 512) {  /* few GEMM tiles: room for 16 K splits of the widest linear */
@@ -692,6 +703,8 @@ static void enq_embed(iris_cuda_flux_t *tf, enq_t *E) {
     enq_gemm(E, &gp, "img_in");
 }
 
+static void enq_ip(iris_cuda_flux_t *tf, enq_t *E, int blk, int row0, int rows);
+
 /* double-stream block i: group 0 = text rows [0, St), group 1 = image rows */
 static void enq_double(iris_cuda_flux_t *tf, int i, enq_t *E) {
     flux_plan_t *P = &tf->plan;
@@ -739,6 +752,26 @@ static void enq_double(iris_cuda_flux_t *tf, int i, enq_t *E) {
     tp_resid(tf, &gp);
     enq_gemm(E, &gp, "dbl_mlp_out");
     enq_allreduce(tf, E);
+    enq_ip(tf, E, i, St, Si);
+}
+
+/* IP-Adapter contribution of adapter block blk to rows [row0, row0 + rows) of
+ * the hidden state, after the block (ip_inject_block, iris_transformer_flux.c:2355):
+ * the block's post-RoPE Q of those rows rotated back to the pre-RoPE Q, attention
+ * over the block's T adapter tokens, hidden += scale[blk] * O.  A block whose
+ * static scale is 0 (style-only export) adds nothing, as in the reference. */
+static void enq_ip(iris_cuda_flux_t *tf, enq_t *E, int blk, int row0, int rows) {
+    struct iris_flux_ip *ip = tf->ip;
+    if (!ip || blk >= ip->nb || ip->h_scale[blk] == 0.0f || rows <= 0) return;
+    flux_plan_t *P = &tf->plan;
+    cudaStream_t st = g_rt.stream;
+    const int H = tf->H, T = ip->T;
+    const uint16_t *k = ip->kv + (size_t)blk * 2 * T * H, *v = k + (size_t)T * H;
+    enq(E, iris_launch_ip_unrope(P->q + (size_t)row0 * H, H, P->rope_cos + (size_t)row0 * 64,
+                                 P->rope_sin + (size_t)row0 * 64, rows, H, P->ip_q, st), "ip_unrope");
+    enq_x(E, iris_launch_attention(P->ip_q, H, k, v, H, P->ip_o, H, rows, T, tf->NH, 1.0f / sqrtf(128.0f), NULL,
+                                   st), "ip_attn", 4.0 * rows * T * (double)H, 2.0 * (rows + 2.0 * T) * H * 2.0);
+    enq(E, iris_launch_ip_add(P->hidden + (size_t)row0 * H, H, P->ip_o, rows, H, ip->d_scale + blk, st), "ip_add");
 }
 
 /* single-stream block i over the whole [TXT, IMG] sequence */
@@ -768,6 +801,7 @@ static void enq_single(iris_cuda_flux_t *tf, int i, enq_t *E) {
     tp_resid(tf, &gp);
     enq_gemm(E, &gp, "sgl_out");
     enq_allreduce(tf, E);
+    enq_ip(tf, E, tf->cfg.n_double + i, P->s_txt, S - P->s_txt);
 }
 
 /* final layer on the target image rows only (scale first, then shift: :4277-4281) */

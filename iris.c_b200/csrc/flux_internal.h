@@ -34,6 +34,7 @@ typedef struct {
     unsigned *flags;
     unsigned part_i, x_i;   /* (while enqueueing) partial / xmod syncs queued in this call */
     int part_pending;       /* a scattered update awaits the next adaLN */
+    uint16_t *ip_q, *ip_o;  /* IP-Adapter: pre-RoPE image Q and its attention output [S, H] */
     float *ws;              /* split-K workspace of short sequences (NULL otherwise) */
     size_t ws_bytes;
     CUtensorMap tm_xmod, tm_attn, tm_mlp, tm_cat, tm_tok_img, tm_tok_txt;
@@ -63,7 +64,25 @@ struct iris_cuda_flux {
     char model_dir[1024];
     /* folded LoRA (NULL without one) */
     struct iris_flux_lora *lora;
+    /* attached IP-Adapter (NULL without one) */
+    struct iris_flux_ip *ip;
 };
+
+/* IP-Adapter state (ipadapter.c), read by the forward's hooks (flux.c) */
+struct iris_flux_ip {
+    int nb, nd, T;         /* adapter blocks (double then single), double blocks, image tokens */
+    uint16_t *kv;          /* bf16 [nb][2][T][H]: each block's k then v */
+    float *d_scale;        /* [nb] ip_scale * scale_mult * schedule multiplier (device) */
+    float *h_scale;        /* [nb] ip_scale * scale_mult */
+    float *h_cur;          /* [nb] staging of d_scale */
+    float *embeds;         /* f32 [T, H] perceived embeddings */
+    float mult;            /* current schedule multiplier */
+    int sched_kind;        /* 0 none, 1 late, 2 early */
+    float sched_param;
+};
+void iris_flux_ip_release(iris_cuda_flux_t *tf);
+/* drop the plan (and its graph) so the next call rebuilds it with the current hooks */
+void iris_flux_invalidate_plan(iris_cuda_flux_t *tf);
 
 /* LoRA state (lora.c): the originals of the weights an adapter was folded
  * into, so a new adapter or an unload starts from the base model. */

@@ -67,7 +67,7 @@ void *iris_comm_sym_peer(const void *local_ptr, int peer);
 int iris_comm_allgather_bytes(const void *send, void *recv, size_t bytes);
 
 /* ---------------- safetensors (own reader) ---------------- */
-typedef enum { ST_F32 = 0, ST_F16 = 1, ST_BF16 = 2, ST_OTHER = 3 } st_dtype_t;
+typedef enum { ST_F32 = 0, ST_F16 = 1, ST_BF16 = 2, ST_OTHER = 3, ST_I8 = 4 } st_dtype_t;
 
 typedef struct {
     char name[256];
@@ -95,6 +95,8 @@ const st_tensor_t *st_find(const st_model_t *m, const char *name);
 /* convert a tensor to bf16 bits into out (numel elements); returns 0 on success */
 int st_read_bf16(const st_model_t *m, const st_tensor_t *t, uint16_t *out, size_t numel);
 int st_read_f32(const st_model_t *m, const st_tensor_t *t, float *out, size_t numel);
+/* the tensor's bytes in the mapped file (NULL when out of range) */
+const void *st_raw(const st_model_t *m, const st_tensor_t *t);
 
 /* ---------------- weight sources (weights.c) ---------------- */
 typedef struct {

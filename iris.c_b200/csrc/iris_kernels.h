@@ -262,6 +262,26 @@ size_t iris_lora_fold_scratch_bytes(int nrows, int cols, int rank, int split);
 cudaError_t iris_launch_lora_fold(const IrisLoraFold *f, void *scratch, size_t scratch_bytes, int *status,
                                   int num_sms, cudaStream_t stream, int *launches);
 
+/* ------------------------------------------------------------------ IP-Adapter (ip_kernels.cu) */
+/* f32 C[M, N] = A[M, K] (B[N, K])^T (transB) or A B[K, N], + bias[N] */
+cudaError_t iris_launch_ip_sgemm(const float *A, int lda, const float *B, int ldb, int transB, const float *bias,
+                                 float *C, int ldc, int M, int N, int K, cudaStream_t stream);
+cudaError_t iris_launch_ip_colnorm(const float *x, int n, int S, const float *g, const float *b, float *out,
+                                   cudaStream_t stream);
+cudaError_t iris_launch_ip_layernorm(float *x, int rows, int H, const float *w, const float *b, cudaStream_t stream);
+cudaError_t iris_launch_ip_film_tokens(const float *q, const float *film, int T, int H, float *out,
+                                       cudaStream_t stream);
+cudaError_t iris_launch_ip_mha(const float *Q, const float *K, const float *V, int T, int n, int H, int heads,
+                               float *out, cudaStream_t stream);
+cudaError_t iris_launch_ip_scale_rows(float *x, int rows, int H, int row_split, float s0, float s1,
+                                      cudaStream_t stream);
+/* bf16 q [rows, ldq] after the pair RoPE of tables cos/sin [rows, 64] -> bf16 [rows, H] before it */
+cudaError_t iris_launch_ip_unrope(const void *q, int ldq, const float *cosb, const float *sinb, int rows, int H,
+                                  void *out, cudaStream_t stream);
+/* f32 hidden[rows, ldh] += *scale * bf16 o[rows, H] */
+cudaError_t iris_launch_ip_add(float *hidden, int ldh, const void *o, int rows, int H, const float *scale,
+                               cudaStream_t stream);
+
 /* ------------------------------------------------------------------ text encoder (Qwen3) */
 /* x[s] = f32 of table[ids[s]] (bf16 [vocab, H]); ids outside [0, vocab) -> zeros */
 cudaError_t iris_launch_embed_rows(const int *ids, int S, const void *table, int vocab, int H, float *x,

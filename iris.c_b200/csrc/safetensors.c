@@ -105,7 +105,7 @@ static int parse_header(st_model_t *m, int file, const char *hdr) {
                     p = parse_str(p, d, sizeof(d));
                     if (!p) return -1;
                     t.dtype = !strcmp(d, "F32") ? ST_F32 : !strcmp(d, "F16") ? ST_F16
-                            : !strcmp(d, "BF16") ? ST_BF16 : ST_OTHER;
+                            : !strcmp(d, "BF16") ? ST_BF16 : !strcmp(d, "I8") ? ST_I8 : ST_OTHER;
                 } else if (strcmp(f, "shape") == 0) {
                     if (*p != '[') return -1;
                     p++;
@@ -274,6 +274,8 @@ static const uint8_t *st_data(const st_model_t *m, const st_tensor_t *t) {
     return (const uint8_t *)m->maps[t->file] + m->data_start[t->file] + t->offset;
 }
 
+const void *st_raw(const st_model_t *m, const st_tensor_t *t) { return st_data(m, t); }
+
 static float f16_to_f32(uint16_t h) {
     uint32_t s = (uint32_t)(h & 0x8000) << 16, e = (h >> 10) & 0x1F, f = h & 0x3FF, u;
     if (e == 0) {
@@ -291,7 +293,7 @@ static float f16_to_f32(uint16_t h) {
 }
 
 int st_read_bf16(const st_model_t *m, const st_tensor_t *t, uint16_t *out, size_t numel) {
-    if (st_numel(t) != numel || t->nbytes != numel * (t->dtype == ST_F32 ? 4 : 2)) return -1;
+    if (t->dtype == ST_I8 || st_numel(t) != numel || t->nbytes != numel * (t->dtype == ST_F32 ? 4 : 2)) return -1;
     const uint8_t *d = st_data(m, t);
     if (!d) return -1;
     if (t->dtype == ST_BF16) { memcpy(out, d, numel * 2); return 0; }
@@ -309,7 +311,7 @@ int st_read_bf16(const st_model_t *m, const st_tensor_t *t, uint16_t *out, size_
 }
 
 int st_read_f32(const st_model_t *m, const st_tensor_t *t, float *out, size_t numel) {
-    if (st_numel(t) != numel || t->nbytes != numel * (t->dtype == ST_F32 ? 4 : 2)) return -1;
+    if (t->dtype == ST_I8 || st_numel(t) != numel || t->nbytes != numel * (t->dtype == ST_F32 ? 4 : 2)) return -1;
     const uint8_t *d = st_data(m, t);
     if (!d) return -1;
     if (t->dtype == ST_F32) { memcpy(out, d, numel * 4); return 0; }

@@ -199,6 +199,8 @@ static int euler_core(iris_cuda_flux_t *tf, int h, int w, const float *txt_c, co
         return rc;
     for (int s = 0; s < steps; s++) {
         float dt = schedule[s + 1] - schedule[s];
+        /* the IP-Adapter schedule's multiplier for this step (iris_sample.c:351, :751) */
+        if ((rc = iris_cuda_flux_set_ip_step(tf, s, steps))) return rc;
         if (txt_u) {
             if ((rc = iris_cuda_check(cudaMemcpyAsync(iris_flux_plan_txt(tf), g_sws.txt_u, txt_n * 4,
                                                       cudaMemcpyDeviceToDevice, st), "txt_u")))
@@ -313,6 +315,7 @@ static int euler_pair_core(iris_cuda_flux_t *tf, int h, int w, float guidance, c
                                               cudaMemcpyHostToDevice, st), "schedule")))
         return rc;
     for (int s = 0; s < steps; s++) {
+        if ((rc = iris_cuda_flux_set_ip_step(tf, s, steps))) return rc;
         if ((rc = iris_flux_run(tf, g_sws.sched + s, cudaMemcpyDeviceToDevice))) return rc;
         if ((rc = iris_comm_allgather_f32(v, g_sws.vpair, n))) return rc;
         iris_count_launch(1);

@@ -250,7 +250,7 @@ int iris_wsrc_get(iris_wsrc_t *ws, const char *name, size_t numel, uint16_t *d_d
     size_t n = 1;
     for (int i = 0; i < t->ndim; i++) n *= (size_t)t->shape[i];
     const size_t esz = t->dtype == ST_F32 ? 4 : 2;
-    if (n != numel || t->dtype == ST_OTHER || t->nbytes != numel * esz)
+    if (n != numel || (t->dtype != ST_F32 && t->dtype != ST_F16 && t->dtype != ST_BF16) || t->nbytes != numel * esz)
         return iris_fail(IRIS_CUDA_ERR_IO, "tensor %s: bad shape or dtype", name);
     const int fd = ws->st.fds[t->file];
     const off_t src = (off_t)(ws->st.data_start[t->file] + t->offset);

@@ -100,6 +100,12 @@ SIGNATURES = {
     "iris_cuda_flux_lora_adapters": (C.c_int, [C.c_void_p]),
     "iris_cuda_flux_lora_stats": (C.c_int, [C.c_void_p, C.POINTER(C.c_double), C.POINTER(C.c_double)]),
     "iris_cuda_lora_probe": (C.c_int, [C.c_char_p, C.c_int, C.c_int, C.c_int, C.c_int, C.POINTER(C.c_int)]),
+    "iris_cuda_flux_load_ip_adapter": (C.c_int, [C.c_void_p, C.c_char_p, C.c_char_p, C.c_float]),
+    "iris_cuda_flux_load_ip_adapter_mem": (C.c_int, [C.c_void_p, C.c_char_p, _fp, C.c_int, C.c_float]),
+    "iris_cuda_flux_unload_ip_adapter": (C.c_int, [C.c_void_p]),
+    "iris_cuda_flux_set_ip_schedule": (C.c_int, [C.c_void_p, C.c_char_p]),
+    "iris_cuda_flux_set_ip_step": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
+    "iris_cuda_flux_ip_embeds": (C.c_int, [C.c_void_p, _fp, C.c_int]),
     "iris_cuda_transformer_forward": (C.c_void_p, [C.c_void_p, _fp, C.c_int, C.c_int, _fp, C.c_int,
                                                    C.c_float]),
     "iris_cuda_transformer_forward_with_multi_refs": (C.c_void_p, [C.c_void_p, _fp, C.c_int, C.c_int,
@@ -327,6 +333,36 @@ class Flux:
         ms, nb = C.c_double(), C.c_double()
         lib().iris_cuda_flux_lora_stats(self.h, C.byref(ms), C.byref(nb))
         return ms.value, nb.value
+
+    def load_ip_adapter(self, bundle_dir: str, features, scale_mult: float = 1.0) -> None:
+        """iris_load_ip_adapter: features = a path to raw f32 rows, or an array."""
+        if isinstance(features, str):
+            rc = lib().iris_cuda_flux_load_ip_adapter(self.h, bundle_dir.encode(), features.encode(), scale_mult)
+        else:
+            f = np.ascontiguousarray(features, np.float32)
+            n = f.shape[0] if f.ndim > 1 else 1
+            rc = lib().iris_cuda_flux_load_ip_adapter_mem(self.h, bundle_dir.encode(), _f(f), n, scale_mult)
+        if rc:
+            raise IrisCudaError(last_error())
+
+    def unload_ip_adapter(self) -> None:
+        if lib().iris_cuda_flux_unload_ip_adapter(self.h):
+            raise IrisCudaError(last_error())
+
+    def set_ip_schedule(self, spec: str) -> None:
+        if lib().iris_cuda_flux_set_ip_schedule(self.h, spec.encode()):
+            raise IrisCudaError(last_error())
+
+    def set_ip_step(self, step: int, num_steps: int) -> None:
+        if lib().iris_cuda_flux_set_ip_step(self.h, step, num_steps):
+            raise IrisCudaError(last_error())
+
+    def ip_embeds(self, tokens: int) -> np.ndarray:
+        out = np.zeros(tokens * self.cfg.hidden, np.float32)
+        n = lib().iris_cuda_flux_ip_embeds(self.h, _f(out), out.size)
+        if n < 0:
+            raise IrisCudaError(last_error())
+        return out[:n].reshape(-1, self.cfg.hidden)
 
     def run_block(self, kind: int, idx: int, hidden: np.ndarray, txt_seq: int, img_h: int, img_w: int,
                   t: float) -> np.ndarray:
