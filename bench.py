@@ -57,6 +57,10 @@ PEAKS_FALLBACK = dict(hbm_gbs=6650.0, bf16_tflops=1590.0, bf16_tflops_sustained=
 LORA_RANK = 32
 LORA_SEED = 77
 METRIC_LORA = "denoise steps/s (Klein-4B 512x512, 4-step Euler, rank-32 LoRA)"
+# config "ip": the C2 workload with an IP-Adapter (SigLIP conditioning: 729 x 1152
+# features, a 16-head perceiver to 64 image tokens, injection after all 25 blocks)
+IP_TOKENS, IP_SIGLIP_SEQ, IP_SIGLIP_DIM, IP_PHEADS = 64, 729, 1152, 16
+METRIC_IP = "denoise steps/s (Klein-4B 512x512, 4-step Euler, SigLIP IP-Adapter, 64 tokens)"
 
 
 def parse_args(argv=None):
@@ -71,11 +75,12 @@ def parse_args(argv=None):
                          "(same kernels and shapes, less memory); not a benchmark number")
     ap.add_argument("--profile-out", default=None, help="write the per-kernel CUDA-event profile (JSON)")
     ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "c5b", "vae512", "vae1024", "qwen3",
-                                                     "lora", "load"],
+                                                     "lora", "load", "ip"],
                     help="c2 (default) is the benchmark; the others measure the remaining SURVEY configs "
                          "on one GPU (c1 K4B 64x64 single forward, c3 K4B 1024x1024 CFG 4.0, c4 K9B "
                          "1792x1792, c5 Z-Image 1024x1024, c5b K4B + 2 references, lora: c2 with a "
-                         "rank-32 LoRA folded into the weights, load: Klein-4B safetensors -> resident)")
+                         "rank-32 LoRA folded into the weights, load: Klein-4B safetensors -> resident, "
+                         "ip: c2 with a SigLIP IP-Adapter attached)")
     return ap.parse_args(argv)
 
 
@@ -248,6 +253,55 @@ def write_bfl_lora(path, mcfg, rank, seed, std=0.02):
         f.write(hj)
         for b in blobs:
             f.write(b.tobytes())
+
+
+# ----------------------------------------------------------------------------- IP-Adapter bundle
+def write_ip_bundle(bundle_dir, mcfg, seed=91):
+    """A SigLIP IP-Adapter bundle in the layout iris_ip_adapter_load reads
+    (adapter_meta.json + bf16 adapter_weights.safetensors) for a Flux model of
+    config mcfg, plus features [729, 1152] f32; values: seeded patterns repeated
+    over each tensor, scaled like trained weights.  Returns the features."""
+    import struct
+    H = mcfg["num_attention_heads"] * mcfg["attention_head_dim"]
+    nb = mcfg["num_layers"] + mcfg["num_single_layers"]
+    T, S = IP_TOKENS, IP_SIGLIP_DIM
+    rng = np.random.default_rng(seed)
+    pat = rng.standard_normal(1 << 20).astype(np.float32)
+    shapes = [("perceiver.query_tokens", (T, H), 1.0, 0.0), ("perceiver.norm_weight", (H,), 0.1, 1.0),
+              ("perceiver.norm_bias", (H,), 0.1, 0.0), ("perceiver.query_proj", (H, H), H ** -0.5, 0.0),
+              ("perceiver.key_proj", (H, S), S ** -0.5, 0.0), ("perceiver.value_proj", (H, S), S ** -0.5, 0.0),
+              ("perceiver.out_proj", (H, H), H ** -0.5, 0.0), ("perceiver.in_gamma", (S,), 0.1, 1.0),
+              ("perceiver.in_beta", (S,), 0.1, 0.0), ("ip_k_stacked", (nb, H, H), 0.25 * H ** -0.5, 0.0),
+              ("ip_v_stacked", (nb, H, H), 0.25 * H ** -0.5, 0.0)]
+    header, blobs, off = {}, [], 0
+    for i, (name, shp, std, mean) in enumerate(shapes):
+        x = (mean + std * np.resize(np.roll(pat, 977 * i), int(np.prod(shp)))).astype(np.float32)
+        u = x.view(np.uint32).astype(np.uint64)
+        b = ((u + 0x7FFF + ((u >> 16) & 1)) >> 16).astype(np.uint16)
+        header[name] = {"dtype": "BF16", "shape": list(shp), "data_offsets": [off, off + b.nbytes]}
+        blobs.append(b)
+        off += b.nbytes
+    sc = rng.uniform(0.4, 1.0, nb).astype(np.float32)
+    header["ip_scale"] = {"dtype": "F32", "shape": [nb], "data_offsets": [off, off + sc.nbytes]}
+    blobs.append(sc)
+    os.makedirs(bundle_dir, exist_ok=True)
+    hj = json.dumps(header).encode()
+    hj += b" " * ((8 - len(hj) % 8) % 8)
+    with open(os.path.join(bundle_dir, "adapter_weights.safetensors"), "wb") as f:
+        f.write(struct.pack("<Q", len(hj)))
+        f.write(hj)
+        for b in blobs:
+            f.write(b.tobytes())
+    with open(os.path.join(bundle_dir, "adapter_meta.json"), "w") as f:
+        json.dump(dict(version=1, adapter_type="ip_adapter_klein", num_blocks=nb,
+                       num_double_blocks=mcfg["num_layers"], num_single_blocks=mcfg["num_single_layers"],
+                       hidden_dim=H, num_image_tokens=T, siglip_dim=S, cond_mode="siglip", csd_dim=0,
+                       perceiver_heads=IP_PHEADS, style_only=False, quant="bfloat16"), f)
+    return (rng.standard_normal((IP_SIGLIP_SEQ, S)) * rng.uniform(0.5, 3.0, S)).astype(np.float32)
+
+
+IP_SAMPLE = (", with a SigLIP IP-Adapter (64 tokens) attached to both blocks: the reference's hooks "
+             "(per-step k/v projection of the adapter tokens + SDPA, added after each block)")
 
 
 # ----------------------------------------------------------------------------- config "load"
@@ -439,7 +493,7 @@ class RefSample:
     Klein-4B at the 512x512 shapes; a full denoising step is extrapolated as
     5 double + 20 single blocks (embedders and final layer are < 1% of it)."""
 
-    def __init__(self, lora: bool = False):
+    def __init__(self, lora: bool = False, ip: bool = False):
         from oracle import model_gen as mg
         from oracle.ref_lib import RefFlux, RefLib
         self.tmp = tempfile.TemporaryDirectory()
@@ -454,6 +508,11 @@ class RefSample:
             write_bfl_lora(path, cfg, LORA_RANK, LORA_SEED)
             if not self.rf.set_lora(path, 1.0):
                 raise RuntimeError("reference lora_load failed")
+        if ip:  # the IP-Adapter hooks of both blocks
+            bdir = os.path.join(self.tmp.name, "ip")
+            feats = write_ip_bundle(bdir, cfg)
+            if self.rf.set_ip(bdir, feats, 1.0) != 0:
+                raise RuntimeError("reference IP-Adapter attach failed")
         r = np.random.default_rng(7)
         H = self.rf.hidden
         self.img = r.standard_normal((IMG_H * IMG_W, H)).astype(np.float32)
@@ -482,7 +541,8 @@ def run_reference(args):
     if rank != 0:
         return 0
     lora = args.config == "lora"
-    rs = RefSample(lora=lora)
+    ipc = args.config == "ip"
+    rs = RefSample(lora=lora, ip=ipc)
     for _ in range(args.warmup):
         rs.step_seconds()
     est, wall = [], 0.0
@@ -494,12 +554,14 @@ def run_reference(args):
     step_s = statistics.mean(est)
     value = 1.0 / step_s
     line = {
-        "impl": "reference", "metric": METRIC_LORA if lora else METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "impl": "reference", "metric": METRIC_LORA if lora else METRIC_IP if ipc else METRIC, "value": value,
+        "unit": UNIT, "n_gpus": world,
         "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1000.0 * STEPS_PER_IMAGE,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": bench_config(world, lora),
+        "config": bench_config(world, lora, ipc),
         "cpu_baseline": {"value": value, "unit": UNIT, "cores": rs.cores, "kind": "reference",
-                         "sample": RefSample.SAMPLE + (LORA_SAMPLE if lora else ""), "measured_wall_s": wall},
+                         "sample": RefSample.SAMPLE + (LORA_SAMPLE if lora else "") + (IP_SAMPLE if ipc else ""),
+                         "measured_wall_s": wall},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(line), flush=True)
@@ -510,7 +572,7 @@ LORA_SAMPLE = (", with the rank-32 BFL adapter of both blocks applied by the ref
                "(lora_apply after every adapted linear)")
 
 
-def bench_config(world, lora=False):
+def bench_config(world, lora=False, ip=False):
     c = {"workload": "Flux.2 Klein-4B distilled, 512x512 (32x32 latent patches = 1024 image tokens) + "
                         "512 text tokens, 4-step Euler, guidance 1.0, batch 1 per GPU",
             "model": "klein-4b (random-init bf16 N(0,0.02))", "image_tokens": IMG_H * IMG_W,
@@ -521,6 +583,10 @@ def bench_config(world, lora=False):
         c["lora"] = {"rank": LORA_RANK, "layout": "BFL (diffusion_model.*)", "scale": 1.0,
                      "coverage": "every double block img/txt qkv + proj, every single block linear1 + linear2",
                      "values": "seeded N(0, 0.02) bf16"}
+    if ip:
+        c["ip_adapter"] = {"cond_mode": "siglip", "image_tokens": IP_TOKENS, "siglip_rows": IP_SIGLIP_SEQ,
+                           "siglip_dim": IP_SIGLIP_DIM, "perceiver_heads": IP_PHEADS, "blocks": "all 25",
+                           "weights": "synthetic bf16"}
     return c
 
 
@@ -570,9 +636,21 @@ def run_ours(args):
     model = iris_cuda.Flux.random(iris_cuda.FluxConfig.from_hf(mcfg), seed=WEIGHT_SEED, std=0.02)
     stream = torch.cuda.ExternalStream(lib.iris_cuda_stream(), device=torch.device("cuda", local))
     lora = args.config == "lora"
-    fold = None
+    ipc = args.config == "ip"
+    fold = ip_attach = None
     if lora:
         fold = measure_lora_fold(model, mcfg, args.warmup)
+    if ipc:
+        ip_tmp = tempfile.TemporaryDirectory()
+        feats = write_ip_bundle(ip_tmp.name, mcfg)
+        att = []
+        for _ in range(3):
+            t0 = time.perf_counter()
+            model.load_ip_adapter(ip_tmp.name, feats, 1.0)
+            att.append((time.perf_counter() - t0) * 1000.0)
+        ip_attach = {"attach_ms": min(att), "note": "iris_cuda_flux_load_ip_adapter_mem: bundle read + upload, "
+                                                        "perceiver and every block's k/v (f32), once per image"}
+        ip_tmp.cleanup()
 
     rng = np.random.default_rng(500 + rank)
     txt = rng.standard_normal((TXT, K4B["joint_attention_dim"])).astype(np.float32)
@@ -699,11 +777,12 @@ def run_ours(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.blocks:
         try:
-            rs = RefSample(lora=lora)
+            rs = RefSample(lora=lora, ip=ipc)
             rs.step_seconds()
             est = [rs.step_seconds()[0] for _ in range(2)]
             cpu = {"value": 1.0 / statistics.mean(est), "unit": UNIT, "cores": rs.cores,
-                   "kind": "reference", "sample": RefSample.SAMPLE + (LORA_SAMPLE if lora else "")}
+                   "kind": "reference",
+                   "sample": RefSample.SAMPLE + (LORA_SAMPLE if lora else "") + (IP_SAMPLE if ipc else "")}
             rs.close()
         except Exception as ex:  # the reference build is optional on a box without it
             cpu = {"value": None, "unit": UNIT, "cores": None, "kind": "reference",
@@ -717,12 +796,13 @@ def run_ours(args):
                             "peak": peaks["hbm_gbs"], "unit": "GB/s", "frac": fold["gbs"] / peaks["hbm_gbs"],
                             "peak_source": peak_src}
     line = {
-        "metric": METRIC_LORA if lora else METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+        "metric": METRIC_LORA if lora else METRIC_IP if ipc else METRIC, "value": value, "unit": UNIT,
+        "n_gpus": world,
         "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": ms_max / args.steps, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
         "images_per_s": value / STEPS_PER_IMAGE,
-        "config": dict(bench_config(world, lora), **({"truncated_blocks": args.blocks} if args.blocks else {})),
+        "config": dict(bench_config(world, lora, ipc), **({"truncated_blocks": args.blocks} if args.blocks else {})),
         "clocks": clocks.summary(),
         "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
                 "wall_s": e2e_wall},
@@ -732,6 +812,8 @@ def run_ours(args):
     }
     if fold is not None:
         line["lora_fold"] = fold
+    if ip_attach is not None:
+        line["ip_adapter"] = ip_attach
     if rank == 0:
         print(json.dumps(line), flush=True)
     model.close()
@@ -1252,7 +1334,7 @@ def main(argv=None):
         return run_load_reference(args) if args.impl == "reference" else run_load(args)
     if args.impl == "reference":
         return run_reference(args)
-    if args.config not in ("c2", "lora"):
+    if args.config not in ("c2", "lora", "ip"):
         return run_config(args)
     return run_ours(args)
 

@@ -175,27 +175,34 @@ __global__ void ip_scale_rows_kernel(float* __restrict__ x, int rows, int H, int
   x[i] *= (i / H) < row_split ? s0 : s1;
 }
 
-// q_pre = R^-1 q: each rotated pair (x0 c - x1 s, x1 c + x0 s) back to (x0, x1)
+// q_pre = R^-1 q: each rotated pair (x0 c - x1 s, x1 c + x0 s) back to (x0, x1);
+// grid (pairs / 256, rows): one thread per pair of one row
 __global__ void ip_unrope_kernel(const __nv_bfloat16* __restrict__ q, int ldq, const float* __restrict__ cosb,
-                                 const float* __restrict__ sinb, int rows, int H, __nv_bfloat16* __restrict__ out) {
-  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;  // one pair
-  const int pairs = H / 2;
-  if (i >= (long)rows * pairs) return;
-  const int r = (int)(i / pairs), p = (int)(i % pairs);
-  const int pr = p % 64;  // pair index inside its 128-wide head
+                                 const float* __restrict__ sinb, int H, __nv_bfloat16* __restrict__ out) {
+  const int p = blockIdx.x * blockDim.x + threadIdx.x, r = blockIdx.y;
+  if (p >= H / 2) return;
+  const int pr = p & 63;  // pair index inside its 128-wide head
   const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(q + (size_t)r * ldq + 2 * p);
   const float y0 = __bfloat162float(v.x), y1 = __bfloat162float(v.y);
-  const float c = cosb[(size_t)r * 64 + pr], s = sinb[(size_t)r * 64 + pr];
+  const float c = __ldg(cosb + (size_t)r * 64 + pr), s = __ldg(sinb + (size_t)r * 64 + pr);
   *reinterpret_cast<__nv_bfloat162*>(out + (size_t)r * H + 2 * p) =
       __floats2bfloat162_rn(y0 * c + y1 * s, y1 * c - y0 * s);
 }
 
-__global__ void ip_add_kernel(float* __restrict__ hidden, int ldh, const __nv_bfloat16* __restrict__ o, int rows,
-                              int H, const float* __restrict__ scale) {
-  const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
-  if (i >= (long)rows * H) return;
-  const int r = (int)(i / H), d = (int)(i % H);
-  hidden[(size_t)r * ldh + d] += *scale * __bfloat162float(o[i]);
+// grid (H / 4 / 256, rows): 4 columns per thread
+__global__ void ip_add_kernel(float* __restrict__ hidden, int ldh, const __nv_bfloat16* __restrict__ o, int H,
+                              const float* __restrict__ scale) {
+  const int c4 = blockIdx.x * blockDim.x + threadIdx.x, r = blockIdx.y;
+  if (c4 >= H / 4) return;
+  const float s = __ldg(scale);
+  const uint2 u = *reinterpret_cast<const uint2*>(o + (size_t)r * H + 4 * c4);
+  float4* h = reinterpret_cast<float4*>(hidden + (size_t)r * ldh) + c4;
+  float4 v = *h;
+  v.x += s * __uint_as_float(u.x << 16);
+  v.y += s * __uint_as_float(u.x & 0xFFFF0000u);
+  v.z += s * __uint_as_float(u.y << 16);
+  v.w += s * __uint_as_float(u.y & 0xFFFF0000u);
+  *h = v;
 }
 
 inline unsigned blocks_for(long n, int threads) { return (unsigned)((n + threads - 1) / threads); }
@@ -258,18 +265,19 @@ cudaError_t iris_launch_ip_scale_rows(float* x, int rows, int H, int row_split, 
 cudaError_t iris_launch_ip_unrope(const void* q, int ldq, const float* cosb, const float* sinb, int rows, int H,
                                   void* out, cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
-  if ((H & 127) || (ldq & 1)) return cudaErrorInvalidValue;
-  ip_unrope_kernel<<<blocks_for((long)rows * (H / 2), 256), 256, 0, stream>>>(
-      static_cast<const __nv_bfloat16*>(q), ldq, cosb, sinb, rows, H, static_cast<__nv_bfloat16*>(out));
+  if ((H & 127) || (ldq & 1) || rows > 65535) return cudaErrorInvalidValue;
+  ip_unrope_kernel<<<dim3(blocks_for(H / 2, 256), rows), 256, 0, stream>>>(
+      static_cast<const __nv_bfloat16*>(q), ldq, cosb, sinb, H, static_cast<__nv_bfloat16*>(out));
   return cudaGetLastError();
 }
 
 cudaError_t iris_launch_ip_add(float* hidden, int ldh, const void* o, int rows, int H, const float* scale,
                                cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
-  ip_add_kernel<<<blocks_for((long)rows * H, 256), 256, 0, stream>>>(hidden, ldh,
-                                                                     static_cast<const __nv_bfloat16*>(o), rows,
-                                                                     H, scale);
+  if ((H & 3) || (ldh & 3) || rows > 65535) return cudaErrorInvalidValue;
+  ip_add_kernel<<<dim3(blocks_for(H / 4, 256), rows), 256, 0, stream>>>(hidden, ldh,
+                                                                        static_cast<const __nv_bfloat16*>(o), H,
+                                                                        scale);
   return cudaGetLastError();
 }
 

@@ -68,11 +68,24 @@ static void meta_str(const char *json, const char *key, char *out, size_t cap) {
 /* f32 copy of a bundle tensor on the device (NULL when absent or malformed);
  * int8 tensors are dequantised with "<name>.scale", one entry per row
  * (load_tensor_f32, iris_ip_adapter.c:80) */
-static float *dev_tensor(const st_model_t *st, const char *name, size_t *numel_out) {
+static float *dev_tensor(iris_wsrc_t *ws, const char *name, size_t *numel_out) {
+    const st_model_t *st = &ws->st;
     const st_tensor_t *t = st_find(st, name);
     if (!t) return NULL;
     size_t n = 1;
     for (int i = 0; i < t->ndim; i++) n *= (size_t)t->shape[i];
+    if (t->dtype == ST_BF16 && t->nbytes == n * 2) {
+        /* the bulk of a bundle: the pipelined file upload, widened to f32 on the device */
+        float *d = (float *)iris_dmalloc(n * sizeof(float));
+        uint16_t *tmp = (uint16_t *)iris_dmalloc(n * 2);
+        int rc = (!d || !tmp) ? IRIS_CUDA_ERR_OOM : iris_wsrc_get(ws, name, n, tmp);
+        if (!rc) rc = iris_cuda_check(iris_launch_bf16_to_f32(tmp, d, (long)n, g_rt.stream), name);
+        if (!rc) rc = iris_stream_drain();
+        iris_dfree(tmp);
+        if (rc) { iris_dfree(d); return NULL; }
+        if (numel_out) *numel_out = n;
+        return d;
+    }
     float *h = (float *)malloc(n * sizeof(float) + 4);
     if (!h) return NULL;
     int ok = 0;
@@ -146,36 +159,39 @@ static int bundle_load(ip_bundle_t *b, const char *dir) {
     const int csd = !strcmp(b->mode, "csd"), hybrid = !strcmp(b->mode, "hybrid");
     if (!csd && !hybrid && strcmp(b->mode, "siglip"))
         return iris_fail(IRIS_CUDA_ERR_IO, "IP-Adapter: unknown cond_mode %s", b->mode);
-    st_model_t st;
+    iris_wsrc_t ws;
+    memset(&ws, 0, sizeof(ws));
     snprintf(path, sizeof(path), "%s/adapter_weights.safetensors", dir);
-    if (st_open_file(&st, path)) return iris_fail(IRIS_CUDA_ERR_IO, "IP-Adapter: cannot open %s", path);
-    b->qtok = dev_tensor(&st, "perceiver.query_tokens", NULL);
-    b->nw = dev_tensor(&st, "perceiver.norm_weight", NULL);
-    b->nbias = dev_tensor(&st, "perceiver.norm_bias", NULL);
+    if (st_open_file(&ws.st, path)) return iris_fail(IRIS_CUDA_ERR_IO, "IP-Adapter: cannot open %s", path);
+    iris_wsrc_t *st = &ws;
+    b->qtok = dev_tensor(st, "perceiver.query_tokens", NULL);
+    b->nw = dev_tensor(st, "perceiver.norm_weight", NULL);
+    b->nbias = dev_tensor(st, "perceiver.norm_bias", NULL);
     if (csd) {
-        b->fw = dev_tensor(&st, "perceiver.film_weight", NULL);
-        b->fb = dev_tensor(&st, "perceiver.film_bias", NULL);
+        b->fw = dev_tensor(st, "perceiver.film_weight", NULL);
+        b->fb = dev_tensor(st, "perceiver.film_bias", NULL);
     } else {
-        b->wq = dev_tensor(&st, "perceiver.query_proj", NULL);
-        b->wk = dev_tensor(&st, "perceiver.key_proj", NULL);
-        b->wv = dev_tensor(&st, "perceiver.value_proj", NULL);
-        b->wo = dev_tensor(&st, "perceiver.out_proj", NULL);
-        b->in_g = dev_tensor(&st, "perceiver.in_gamma", NULL);
-        b->in_b = dev_tensor(&st, "perceiver.in_beta", NULL);
+        b->wq = dev_tensor(st, "perceiver.query_proj", NULL);
+        b->wk = dev_tensor(st, "perceiver.key_proj", NULL);
+        b->wv = dev_tensor(st, "perceiver.value_proj", NULL);
+        b->wo = dev_tensor(st, "perceiver.out_proj", NULL);
+        b->in_g = dev_tensor(st, "perceiver.in_gamma", NULL);
+        b->in_b = dev_tensor(st, "perceiver.in_beta", NULL);
     }
     if (hybrid) {
-        b->cq = dev_tensor(&st, "csd.query_tokens", NULL);
-        b->cfw = dev_tensor(&st, "csd.film_weight", NULL);
-        b->cfb = dev_tensor(&st, "csd.film_bias", NULL);
-        b->cnw = dev_tensor(&st, "csd.norm_weight", NULL);
-        b->cnb = dev_tensor(&st, "csd.norm_bias", NULL);
-        b->gate = dev_tensor(&st, "group_gate", NULL);
+        b->cq = dev_tensor(st, "csd.query_tokens", NULL);
+        b->cfw = dev_tensor(st, "csd.film_weight", NULL);
+        b->cfb = dev_tensor(st, "csd.film_bias", NULL);
+        b->cnw = dev_tensor(st, "csd.norm_weight", NULL);
+        b->cnb = dev_tensor(st, "csd.norm_bias", NULL);
+        b->gate = dev_tensor(st, "group_gate", NULL);
     }
     size_t nk = 0, nv = 0, ns = 0;
-    b->ipk = dev_tensor(&st, "ip_k_stacked", &nk);
-    b->ipv = dev_tensor(&st, "ip_v_stacked", &nv);
-    b->ipscale = dev_tensor(&st, "ip_scale", &ns);
-    st_close(&st);
+    b->ipk = dev_tensor(st, "ip_k_stacked", &nk);
+    b->ipv = dev_tensor(st, "ip_v_stacked", &nv);
+    b->ipscale = dev_tensor(&ws, "ip_scale", &ns);
+    iris_wsrc_free(&ws);
+    st_close(&ws.st);
     int ok = b->qtok && b->nw && b->nbias && b->ipk && b->ipv && b->ipscale;
     ok = ok && (csd ? (b->fw && b->fb) : (b->wq && b->wk && b->wv && b->wo));
     if (hybrid) ok = ok && b->cq && b->cfw && b->cfb && b->cnw && b->cnb;
