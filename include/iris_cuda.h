@@ -166,6 +166,24 @@ int iris_cuda_flux_set_ip_step(iris_cuda_flux_t *tf, int step, int num_steps);
 /* The perceived embeddings [T, H] (f32) of the attached adapter; returns T*H. */
 int iris_cuda_flux_ip_embeds(const iris_cuda_flux_t *tf, float *out, int cap);
 
+/* SREF style controls.  iris_set_sref_csd (iris.h:178; iris.c:487): run the
+ * CSDModulation MLP (csd_mod.safetensors: fc1 -> SiLU -> fc2) on the
+ * reference's L2-normalised CSD vector [csd_dim], times scale, and add the
+ * result to the timestep embedding of every forward (the CFG samplers leave it
+ * out of the unconditional branch).  A NULL path / vector or scale 0 turns it
+ * off.  Returns 0 or an error (dimension mismatch). */
+int iris_cuda_flux_set_sref_csd(iris_cuda_flux_t *tf, const char *csdmod_path, const float *csd, int csd_dim,
+                                float scale);
+/* iris_transformer_set_csd_delta: a host delta [hidden] (copied), NULL = off. */
+int iris_cuda_flux_set_csd_delta(iris_cuda_flux_t *tf, const float *delta);
+/* iris_transformer_set_csd_skip: 1 leaves the delta out of the next forwards. */
+int iris_cuda_flux_set_csd_skip(iris_cuda_flux_t *tf, int skip);
+/* iris_transformer_set_sref_bands: the single blocks rotate the K of
+ * reference-image rows with their H / W RoPE pairs scaled by
+ * shf + (slf - shf) * (d / 15)^2 (high frequencies attenuated, low amplified);
+ * shf outside [0, 1] or slf < 1 means 1 (off). */
+int iris_cuda_flux_set_sref_bands(iris_cuda_flux_t *tf, float shf, float slf);
+
 /* Host only (no device needed): the adapters of a LoRA file that match a model
  * of this shape (n_double / n_single blocks, hidden and MLP widths), like the
  * reference's "LoRA: loaded N adapters" report (iris_lora.c:276).  Returns

@@ -207,6 +207,7 @@ void iris_cuda_flux_free(iris_cuda_flux_t *tf) {
     iris_stream_drain();
     iris_flux_lora_release(tf);
     iris_flux_ip_release(tf);
+    iris_flux_sref_release(tf);
     plan_free(&tf->plan);
     iris_dfree(tf->w_x); iris_dfree(tf->w_ctx); iris_dfree(tf->w_t1); iris_dfree(tf->w_t2);
     iris_dfree(tf->w_mod); iris_dfree(tf->w_proj);
@@ -253,6 +254,7 @@ static iris_cuda_flux_t *flux_new(const iris_cuda_flux_config_t *cfg, int tp_ran
     tf->NH = cfg->heads;
     tf->tp = tp;
     tf->tp_rank = tp_rank;
+    tf->sref_shf = tf->sref_slf = 1.0f;
     tf->NHl = cfg->heads / tp;
     tf->Hl = tf->NHl * 128;
     tf->Fl = cfg->mlp / tp;
@@ -388,6 +390,7 @@ static void plan_free(flux_plan_t *P) {
     iris_dfree(P->cat); iris_dfree(P->tok_img); iris_dfree(P->tok_txt);
     iris_dfree(P->ws);
     iris_dfree(P->ip_q); iris_dfree(P->ip_o);
+    iris_dfree(P->rope_cos_k); iris_dfree(P->rope_sin_k);
     memset(P, 0, sizeof(*P));
 }
 
@@ -514,6 +517,21 @@ static int plan_ensure(iris_cuda_flux_t *tf, int s_txt, int img_h, int img_w,
         if (!cs || !sn) { free(cs); free(sn); goto oom; }
         fill_rope(tf, P, cs, sn);
         int rc = iris_h2d(P->rope_cos, cs, (size_t)S * 64 * 4) || iris_h2d(P->rope_sin, sn, (size_t)S * 64 * 4);
+        /* SREF band control (set_kside_krope, iris_transformer_flux.c:1297): single
+           blocks rotate K of the reference rows with H / W pairs scaled by s(d) */
+        const int ref0 = P->s_txt + P->n_img;
+        if (!rc && num_refs > 0 && (tf->sref_shf != 1.0f || tf->sref_slf != 1.0f)) {
+            for (int r = ref0; r < S; r++)
+                for (int d = 0; d < 16; d++) {
+                    const float f = iris_flux_sref_band(tf, d);
+                    cs[(size_t)r * 64 + 16 + d] *= f; sn[(size_t)r * 64 + 16 + d] *= f;
+                    cs[(size_t)r * 64 + 32 + d] *= f; sn[(size_t)r * 64 + 32 + d] *= f;
+                }
+            P->rope_cos_k = (float *)iris_dmalloc((size_t)S * 64 * 4);
+            P->rope_sin_k = (float *)iris_dmalloc((size_t)S * 64 * 4);
+            rc = !P->rope_cos_k || !P->rope_sin_k || iris_h2d(P->rope_cos_k, cs, (size_t)S * 64 * 4) ||
+                 iris_h2d(P->rope_sin_k, sn, (size_t)S * 64 * 4);
+        }
         free(cs);
         free(sn);
         if (rc) { plan_free(P); return IRIS_CUDA_ERR_CUDA; }
@@ -671,6 +689,8 @@ static void enq_mods(iris_cuda_flux_t *tf, enq_t *E) {
     enq(E, iris_launch_timestep_sincos(tf->t_dev, 1000.0f, tf->sincos, 256, st), "sincos");
     enq(E, iris_launch_gemv(tf->w_t1, tf->sincos, NULL, tf->temb_h, H, 256, 0, 1, st), "t_fc1");
     enq(E, iris_launch_gemv(tf->w_t2, tf->temb_h, NULL, tf->temb, H, H, 0, 0, st), "t_fc2");
+    if (tf->csd_delta)  /* SREF CSD modulation: temb += delta unless skipped (:3972) */
+        enq(E, iris_launch_axpy_dev(tf->temb, tf->csd_delta, tf->csd_on, H, st), "csd_delta");
     enq_x(E, iris_launch_gemv(tf->w_mod, tf->temb, NULL, tf->mods, 17 * H, H, 1, 0, st), "mods",
           2.0 * 17 * H * (double)H, 2.0 * 17 * H * (double)H);
 }
@@ -788,6 +808,7 @@ static void enq_single(iris_cuda_flux_t *tf, int i, enq_t *E) {
     gp_group(&gp, 0, &b->tm_fused, 0, S);
     gp.qnorm[0] = b->qn; gp.knorm[0] = b->kn;
     gp.rope_cos = P->rope_cos; gp.rope_sin = P->rope_sin;
+    gp.rope_cos_k = P->rope_cos_k; gp.rope_sin_k = P->rope_sin_k;
     gp.q = P->q; gp.k = P->k; gp.v = P->v; gp.ldqkv = Hl; gp.H = Hl;
     gp.mlp_out = P->cat; gp.ld_mlp = Hl + Fl; gp.mlp_col0 = Hl; gp.swiglu_base = 3 * Hl;
     enq_gemm(E, &gp, "sgl_fused");

@@ -35,6 +35,7 @@ typedef struct {
     unsigned part_i, x_i;   /* (while enqueueing) partial / xmod syncs queued in this call */
     int part_pending;       /* a scattered update awaits the next adaLN */
     uint16_t *ip_q, *ip_o;  /* IP-Adapter: pre-RoPE image Q and its attention output [S, H] */
+    float *rope_cos_k, *rope_sin_k;  /* SREF K-side tables (NULL = the Q tables) */
     float *ws;              /* split-K workspace of short sequences (NULL otherwise) */
     size_t ws_bytes;
     CUtensorMap tm_xmod, tm_attn, tm_mlp, tm_cat, tm_tok_img, tm_tok_txt;
@@ -66,7 +67,18 @@ struct iris_cuda_flux {
     struct iris_flux_lora *lora;
     /* attached IP-Adapter (NULL without one) */
     struct iris_flux_ip *ip;
+    /* SREF (sref.c): CSD temb delta [H] (NULL = off) and the device flag that
+       gates it per forward (0 on the CFG sampler's unconditional branch);
+       K-side RoPE band scaling of reference rows (1, 1 = off) */
+    float *csd_delta, *csd_on;
+    float sref_shf, sref_slf;
 };
+
+void iris_flux_sref_release(iris_cuda_flux_t *tf);
+/* gate the CSD delta for the next forwards (stream-ordered): on = 0 or 1 */
+int iris_flux_csd_branch(iris_cuda_flux_t *tf, int on);
+/* K-side band scale of rotation pair d (0..15) of the H and W axes */
+float iris_flux_sref_band(const iris_cuda_flux_t *tf, int d);
 
 /* IP-Adapter state (ipadapter.c), read by the forward's hooks (flux.c) */
 struct iris_flux_ip {

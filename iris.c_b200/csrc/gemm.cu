@@ -123,8 +123,9 @@ __device__ __forceinline__ void epi_qkv_chunk(const IrisGemmParams& p, uint32_t 
         v[4 * e + 3] = v[4 * e + 3] * r * w.w;
       }
       if (p.rope_cos) {
-        const float4* cp = reinterpret_cast<const float4*>(p.rope_cos + (size_t)row * 64 + 16 * j);
-        const float4* sp = reinterpret_cast<const float4*>(p.rope_sin + (size_t)row * 64 + 16 * j);
+        const bool kt = which == 1 && p.rope_cos_k;  // K-side tables (reference-row band scaling)
+        const float4* cp = reinterpret_cast<const float4*>((kt ? p.rope_cos_k : p.rope_cos) + (size_t)row * 64 + 16 * j);
+        const float4* sp = reinterpret_cast<const float4*>((kt ? p.rope_sin_k : p.rope_sin) + (size_t)row * 64 + 16 * j);
 #pragma unroll
         for (int q4 = 0; q4 < 4; q4++) {
           float4 c = __ldg(cp + q4), s = __ldg(sp + q4);

@@ -16,6 +16,7 @@
 //   (tcgen05 attention over the adapter's T keys, attention_tc.cu)
 //   ip_add            hidden += scale[block] * O  (scale read from device memory,
 //                     so a per-step schedule needs no new graph)
+// SREF: axpy_dev (temb += flag * CSD delta), silu_f32 (the CSD modulation MLP).
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <math.h>
@@ -205,6 +206,18 @@ __global__ void ip_add_kernel(float* __restrict__ hidden, int ldh, const __nv_bf
   *h = v;
 }
 
+// y += (*a) * x  (SREF: the CSD temb delta, gated per forward by a device flag)
+__global__ void axpy_dev_kernel(float* __restrict__ y, const float* __restrict__ x, const float* __restrict__ a,
+                                int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) y[i] += __ldg(a) * x[i];
+}
+
+__global__ void silu_f32_kernel(float* __restrict__ x, int n) {
+  const int i = blockIdx.x * blockDim.x + threadIdx.x;
+  if (i < n) x[i] = x[i] / (1.0f + expf(-x[i]));
+}
+
 inline unsigned blocks_for(long n, int threads) { return (unsigned)((n + threads - 1) / threads); }
 
 }  // namespace
@@ -278,6 +291,18 @@ cudaError_t iris_launch_ip_add(float* hidden, int ldh, const void* o, int rows, 
   ip_add_kernel<<<dim3(blocks_for(H / 4, 256), rows), 256, 0, stream>>>(hidden, ldh,
                                                                         static_cast<const __nv_bfloat16*>(o), H,
                                                                         scale);
+  return cudaGetLastError();
+}
+
+cudaError_t iris_launch_axpy_dev(float* y, const float* x, const float* a, int n, cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  axpy_dev_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(y, x, a, n);
+  return cudaGetLastError();
+}
+
+cudaError_t iris_launch_silu_f32(float* x, int n, cudaStream_t stream) {
+  if (n <= 0) return cudaSuccess;
+  silu_f32_kernel<<<blocks_for(n, 256), 256, 0, stream>>>(x, n);
   return cudaGetLastError();
 }
 

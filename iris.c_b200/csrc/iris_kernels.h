@@ -89,6 +89,8 @@ typedef struct {
     const float *knorm[2];
     const float *rope_cos;    /* QKV: [rows_total, 64] by absolute row (NULL = no RoPE) */
     const float *rope_sin;
+    const float *rope_cos_k;  /* QKV: K-side tables (NULL = the Q tables)               */
+    const float *rope_sin_k;
     void *q, *k, *v;          /* QKV destinations (bf16) with row stride ldqkv         */
     int ldqkv;
     int H;                    /* width of Q, K and V blocks (heads * 128)              */
@@ -281,6 +283,10 @@ cudaError_t iris_launch_ip_unrope(const void *q, int ldq, const float *cosb, con
 /* f32 hidden[rows, ldh] += *scale * bf16 o[rows, H] */
 cudaError_t iris_launch_ip_add(float *hidden, int ldh, const void *o, int rows, int H, const float *scale,
                                cudaStream_t stream);
+
+/* y[n] += (*a) * x[n], a in device memory; in-place SiLU */
+cudaError_t iris_launch_axpy_dev(float *y, const float *x, const float *a, int n, cudaStream_t stream);
+cudaError_t iris_launch_silu_f32(float *x, int n, cudaStream_t stream);
 
 /* ------------------------------------------------------------------ text encoder (Qwen3) */
 /* x[s] = f32 of table[ids[s]] (bf16 [vocab, H]); ids outside [0, vocab) -> zeros */

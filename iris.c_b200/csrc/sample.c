@@ -25,6 +25,7 @@ int iris_flux_run(iris_cuda_flux_t *tf, const float *t_src, enum cudaMemcpyKind 
 int iris_flux_channels(iris_cuda_flux_t *tf);
 int iris_flux_text_dim(iris_cuda_flux_t *tf);
 int iris_flux_tp(iris_cuda_flux_t *tf);
+int iris_flux_csd_branch(iris_cuda_flux_t *tf, int on);
 
 #define IRIS_CUDA_MAX_STEPS 1000
 
@@ -205,7 +206,10 @@ static int euler_core(iris_cuda_flux_t *tf, int h, int w, const float *txt_c, co
             if ((rc = iris_cuda_check(cudaMemcpyAsync(iris_flux_plan_txt(tf), g_sws.txt_u, txt_n * 4,
                                                       cudaMemcpyDeviceToDevice, st), "txt_u")))
                 return rc;
+            /* style CFG: the unconditional branch runs without the CSD delta (iris_sample.c:754) */
+            if ((rc = iris_flux_csd_branch(tf, 0))) return rc;
             if ((rc = iris_flux_run(tf, g_sws.sched + s, cudaMemcpyDeviceToDevice))) return rc;
+            if ((rc = iris_flux_csd_branch(tf, 1))) return rc;
             if ((rc = iris_cuda_check(cudaMemcpyAsync(g_sws.vu, v, n * 4, cudaMemcpyDeviceToDevice, st),
                                       "v_u")))
                 return rc;
@@ -314,6 +318,8 @@ static int euler_pair_core(iris_cuda_flux_t *tf, int h, int w, float guidance, c
     if ((rc = iris_cuda_check(cudaMemcpyAsync(g_sws.sched, schedule, (size_t)(steps + 1) * 4,
                                               cudaMemcpyHostToDevice, st), "schedule")))
         return rc;
+    /* rank 2p runs the unconditional branch: no CSD delta there */
+    if ((rc = iris_flux_csd_branch(tf, iris_comm_rank() % 2))) return rc;
     for (int s = 0; s < steps; s++) {
         if ((rc = iris_cuda_flux_set_ip_step(tf, s, steps))) return rc;
         if ((rc = iris_flux_run(tf, g_sws.sched + s, cudaMemcpyDeviceToDevice))) return rc;
@@ -324,7 +330,7 @@ static int euler_pair_core(iris_cuda_flux_t *tf, int h, int w, float guidance, c
             return rc;
         if (progress) progress(s + 1, steps);
     }
-    return 0;
+    return iris_flux_csd_branch(tf, 1);
 }
 
 static int pair_check(iris_cuda_flux_t *tf, const void *c, const void *u, int seq_c, int seq_u,

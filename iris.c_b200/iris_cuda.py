@@ -106,6 +106,10 @@ SIGNATURES = {
     "iris_cuda_flux_set_ip_schedule": (C.c_int, [C.c_void_p, C.c_char_p]),
     "iris_cuda_flux_set_ip_step": (C.c_int, [C.c_void_p, C.c_int, C.c_int]),
     "iris_cuda_flux_ip_embeds": (C.c_int, [C.c_void_p, _fp, C.c_int]),
+    "iris_cuda_flux_set_sref_csd": (C.c_int, [C.c_void_p, C.c_char_p, _fp, C.c_int, C.c_float]),
+    "iris_cuda_flux_set_csd_delta": (C.c_int, [C.c_void_p, _fp]),
+    "iris_cuda_flux_set_csd_skip": (C.c_int, [C.c_void_p, C.c_int]),
+    "iris_cuda_flux_set_sref_bands": (C.c_int, [C.c_void_p, C.c_float, C.c_float]),
     "iris_cuda_transformer_forward": (C.c_void_p, [C.c_void_p, _fp, C.c_int, C.c_int, _fp, C.c_int,
                                                    C.c_float]),
     "iris_cuda_transformer_forward_with_multi_refs": (C.c_void_p, [C.c_void_p, _fp, C.c_int, C.c_int,
@@ -363,6 +367,20 @@ class Flux:
         if n < 0:
             raise IrisCudaError(last_error())
         return out[:n].reshape(-1, self.cfg.hidden)
+
+    def set_sref_csd(self, csdmod_path, csd, scale: float) -> None:
+        """iris_set_sref_csd: the CSD modulation delta on the timestep embedding (None: off)."""
+        if csdmod_path is None:
+            rc = lib().iris_cuda_flux_set_sref_csd(self.h, None, None, 0, 0.0)
+        else:
+            c = np.ascontiguousarray(csd, np.float32).ravel()
+            rc = lib().iris_cuda_flux_set_sref_csd(self.h, csdmod_path.encode(), _f(c), c.size, scale)
+        if rc:
+            raise IrisCudaError(last_error())
+
+    def set_sref_bands(self, shf: float, slf: float) -> None:
+        if lib().iris_cuda_flux_set_sref_bands(self.h, shf, slf):
+            raise IrisCudaError(last_error())
 
     def run_block(self, kind: int, idx: int, hidden: np.ndarray, txt_seq: int, img_h: int, img_w: int,
                   t: float) -> np.ndarray:

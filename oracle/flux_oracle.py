@@ -197,7 +197,7 @@ def double_block(w, i, img, txt, mod_img, mod_txt, rope_i, rope_t, d, ip=None):
     return img, txt.astype(F32)
 
 
-def single_block(w, i, hidden, mod_single, rope_all, d, ip=None, n_txt=0):
+def single_block(w, i, hidden, mod_single, rope_all, d, ip=None, n_txt=0, rope_k=None):
     """One parallel DiT block over [TXT, IMG] (single_block_forward :3761-3928).
     ``ip``: contribution to the rows after the n_txt text rows, adapter block
     n_double + i (:3848-3855, :3921-3926)."""
@@ -211,7 +211,8 @@ def single_block(w, i, hidden, mod_single, rope_all, d, ip=None, n_txt=0):
     q = head_rms_norm(q, w[p + "attn.norm_q.weight"], heads)
     q_pre = q
     q = apply_rope(q, *rope_all, heads)
-    k = apply_rope(head_rms_norm(k, w[p + "attn.norm_k.weight"], heads), *rope_all, heads)
+    # SREF band control: K of reference rows rotated with the band-scaled table (:3872)
+    k = apply_rope(head_rms_norm(k, w[p + "attn.norm_k.weight"], heads), *(rope_k or rope_all), heads)
     a = attention(q, k, v, heads)
     cat = np.concatenate([a, silu(g) * u], axis=1)
     out = (hidden + gate * linear(cat, w[p + "attn.to_out.weight"])).astype(F32)
@@ -220,7 +221,28 @@ def single_block(w, i, hidden, mod_single, rope_all, d, ip=None, n_txt=0):
     return out
 
 
-def forward(w, cfg, latent, txt_emb, t, refs=(), return_blocks=False, ip=None):
+def sref_band_table(cos, sin, ref_start, shf, slf, axis_dim=32):
+    """band_scale_ref_krope (:1272): rows >= ref_start get their H and W pairs
+    scaled by s(d) = shf + (slf - shf) (d / (half - 1))^2."""
+    half = axis_dim // 2
+    dn = np.arange(half, dtype=F32) / F32(half - 1)
+    sd = (F32(shf) + (F32(slf) - F32(shf)) * dn * dn).astype(F32)
+    f = np.repeat(sd, 2)
+    c, s = cos.copy(), sin.copy()
+    for a in (1, 2):
+        c[ref_start:, a * axis_dim:(a + 1) * axis_dim] *= f
+        s[ref_start:, a * axis_dim:(a + 1) * axis_dim] *= f
+    return c, s
+
+
+def csd_mod_forward(m, csd):
+    """csd_mod_forward (iris_csdmod.c): fc2(SiLU(fc1(csd)))."""
+    h = m["fc1.weight"].astype(np.float64) @ csd.astype(np.float64) + m["fc1.bias"]
+    h = h / (1.0 + np.exp(-h))
+    return (m["fc2.weight"].astype(np.float64) @ h + m["fc2.bias"]).astype(F32)
+
+
+def forward(w, cfg, latent, txt_emb, t, refs=(), return_blocks=False, ip=None, temb_delta=None, bands=None):
     """Velocity v(z, t, ctx) for one denoising step.
 
     iris_transformer_forward (:3939-4326); with ``refs`` (list of NCHW
@@ -244,6 +266,8 @@ def forward(w, cfg, latent, txt_emb, t, refs=(), return_blocks=False, ip=None):
     rope_t = rope_txt(n_txt, d["theta"])
 
     t_emb = time_embed(w, t)
+    if temb_delta is not None:  # SREF CSD modulation (:3972)
+        t_emb = (t_emb + temb_delta).astype(F32)
     mods = modulations(w, t_emb)
     img = linear(img_tok, w["x_embedder.weight"])
     txt = linear(txt_emb.astype(F32), w["context_embedder.weight"])
@@ -254,8 +278,11 @@ def forward(w, cfg, latent, txt_emb, t, refs=(), return_blocks=False, ip=None):
             blocks.append(np.concatenate([txt, img]))
     hidden = np.concatenate([txt, img])
     rope_all = (np.concatenate([rope_t[0], rope_i[0]]), np.concatenate([rope_t[1], rope_i[1]]))
+    rope_k = None
+    if bands is not None and refs and (bands[0] != 1.0 or bands[1] != 1.0):
+        rope_k = sref_band_table(*rope_all, n_txt + n_img, *bands)
     for i in range(d["n_single"]):
-        hidden = single_block(w, i, hidden, mods["single"], rope_all, d, ip, n_txt)
+        hidden = single_block(w, i, hidden, mods["single"], rope_all, d, ip, n_txt, rope_k)
         if return_blocks:
             blocks.append(hidden)
     img = hidden[n_txt:n_txt + n_img]

@@ -316,6 +316,18 @@ def make_ip_bundle(bundle_dir: str, cfg: dict, mode: str = "siglip", tokens: int
     return meta
 
 
+def make_csd_mod(path: str, csd_dim: int, mlp: int, hidden: int, seed: int = 0) -> dict:
+    """A CSDModulation MLP file (csd_mod.safetensors: fc1 [mlp, csd], fc2 [hidden, mlp],
+    biases; read by csd_mod_load, iris_csdmod.c); returns the f32 tensors."""
+    rng = np.random.default_rng(seed)
+    t = {"fc1.weight": (rng.standard_normal((mlp, csd_dim)) / np.sqrt(csd_dim)).astype(np.float32),
+         "fc1.bias": (0.1 * rng.standard_normal(mlp)).astype(np.float32),
+         "fc2.weight": (rng.standard_normal((hidden, mlp)) / np.sqrt(mlp)).astype(np.float32),
+         "fc2.bias": (0.1 * rng.standard_normal(hidden)).astype(np.float32)}
+    write_safetensors(path, t)
+    return t
+
+
 def ip_features(mode: str, siglip_seq: int = 16, siglip_dim: int = 64, csd_dim: int = 32, seed: int = 1):
     """Conditioning features as iris_load_ip_adapter reads them (iris.c:546-567):
     siglip [n, siglip_dim]; csd [1, csd_dim]; hybrid [n + 1, siglip_dim], last row

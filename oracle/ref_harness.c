@@ -20,6 +20,7 @@
  *   ref_lora_get             -> one adapter of lora_load's table     (iris_lora.h:28-49)
  *   ref_ip_perceive/get_kv/inject -> iris_ip_adapter_perceive/_get_kv/_inject (iris_ip_adapter.c:331-386)
  *   ref_flux_set_ip          -> iris_load_ip_adapter minus the file read (iris.c:520)
+ *   ref_flux_set_sref_csd/_bands -> iris_set_sref_csd (iris.c:487), iris_transformer_set_sref_bands (:5153)
  *   ref_sample_euler(_cfg)   -> iris_sample_euler / _cfg            (iris_sample.c:313, :717)
  *   ref_init_noise           -> iris_init_noise                     (iris_sample.c:1146)
  *   ref_official_schedule    -> iris_official_schedule              (iris_sample.c:171)
@@ -32,6 +33,7 @@
  * Build: see oracle/Makefile.  Outputs go to oracle/_ref/ only.
  */
 #include "iris_transformer_flux.c"
+#include "iris_csdmod.h"
 
 extern float *iris_official_schedule(int num_steps, int image_seq_len);
 extern float *iris_zimage_schedule(int num_steps, int image_seq_len);
@@ -214,6 +216,29 @@ int ref_flux_set_ip_schedule(void *p, const char *spec) {
 }
 
 void ref_flux_clear_ip(void *p) { iris_transformer_set_ip_adapter((iris_transformer_t *)p, NULL, NULL); }
+
+/* iris_set_sref_csd (iris.c:487) minus the context: csd_mod MLP -> delta * scale
+ * -> iris_transformer_set_csd_delta; NULL path / csd or scale 0 clears. */
+int ref_flux_set_sref_csd(void *p, const char *csdmod, const float *csd, int csd_dim, float scale) {
+    iris_transformer_t *tf = (iris_transformer_t *)p;
+    if (!csdmod || !*csdmod || !csd || scale == 0.0f) { iris_transformer_set_csd_delta(tf, NULL); return 0; }
+    csd_mod_t m;
+    if (csd_mod_load(&m, csdmod)) return -1;
+    if (m.csd_dim != csd_dim || m.hidden_dim != tf->hidden_size) { csd_mod_free(&m); return -2; }
+    float *delta = malloc((size_t)m.hidden_dim * sizeof(float));
+    float *work = malloc((size_t)m.mlp_dim * sizeof(float));
+    if (!delta || !work) { free(delta); free(work); csd_mod_free(&m); return -3; }
+    csd_mod_forward(&m, csd, delta, work);
+    for (int i = 0; i < m.hidden_dim; i++) delta[i] *= scale;
+    free(work);
+    csd_mod_free(&m);
+    iris_transformer_set_csd_delta(tf, delta);
+    return 0;
+}
+
+void ref_flux_set_sref_bands(void *p, float shf, float slf) {
+    iris_transformer_set_sref_bands((iris_transformer_t *)p, shf, slf);
+}
 
 void ref_flux_temb(void *p, float t, float *t_emb) {
     iris_transformer_t *tf = (iris_transformer_t *)p;

@@ -72,6 +72,8 @@ class RefLib:
         L.ref_flux_set_ip.argtypes = [C.c_void_p, C.c_char_p, _fp, C.c_int, C.c_float]
         L.ref_flux_set_ip_schedule.argtypes = [C.c_void_p, C.c_char_p]
         L.ref_flux_clear_ip.argtypes = [C.c_void_p]
+        L.ref_flux_set_sref_csd.argtypes = [C.c_void_p, C.c_char_p, _fp, C.c_int, C.c_float]
+        L.ref_flux_set_sref_bands.argtypes = [C.c_void_p, C.c_float, C.c_float]
         L.ref_flux_set_lora.argtypes = [C.c_void_p, C.c_char_p, C.c_float]
         L.ref_flux_clear_lora.argtypes = [C.c_void_p]
         L.ref_lora_get.argtypes = [C.c_char_p, C.c_int, C.c_int, C.c_int, C.c_int, C.c_int,
@@ -194,6 +196,13 @@ class RefFlux:
 
     def clear_ip(self):
         self.ref.lib.ref_flux_clear_ip(self.h)
+
+    def set_sref_csd(self, csdmod, csd, scale) -> int:
+        c = np.ascontiguousarray(csd, np.float32).ravel()
+        return self.ref.lib.ref_flux_set_sref_csd(self.h, csdmod.encode() if csdmod else None, _f(c), c.size, scale)
+
+    def set_sref_bands(self, shf, slf):
+        self.ref.lib.ref_flux_set_sref_bands(self.h, shf, slf)
 
     def set_lora(self, path: str, scale: float) -> bool:
         return self.ref.lib.ref_flux_set_lora(self.h, path.encode(), scale) == 0
