@@ -92,6 +92,7 @@ struct AttnParams {
   const uint8_t* kmask;
   int causal;     // key j of query row i masked when j > i (masked instantiation only)
   int kv_group;   // query heads per key/value head (grouped-query attention)
+  int one_tile;   // single-CTA kernel: one 128-row query tile per CTA instead of two
   int* status;
 };
 
@@ -350,8 +351,8 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int head = blockIdx.y;
-  const int q0 = blockIdx.x * (2 * BQ);
-  const bool has1 = q0 + BQ < p.sq;  // second query tile holds rows
+  const int q0 = blockIdx.x * (p.one_tile ? BQ : 2 * BQ);
+  const bool has1 = !p.one_tile && q0 + BQ < p.sq;  // second query tile holds rows
   const int col0 = head * HD;
   const int kvcol0 = (head / p.kv_group) * HD;
   const int n = (p.sk + BKV - 1) / BKV;
@@ -764,11 +765,22 @@ extern "C" cudaError_t iris_launch_attention_gqa(const void* q, int ldq, const v
     cudaError_t e = iris_attention_tc_init();
     if (e != cudaSuccess) return e;
   }
-  static int single = -1;  // IRIS_ATTN=1cta keeps the single-CTA kernel (A/B measurements)
-  if (single < 0) {
+  static int mode = -1;  // IRIS_ATTN=1cta: always the single-CTA kernel; =pair: always pairs (A/B)
+  static int sms = 148;
+  if (mode < 0) {
     const char* e = getenv("IRIS_ATTN");
-    single = (e && strcmp(e, "1cta") == 0) ? 1 : 0;
+    mode = (e && strcmp(e, "1cta") == 0) ? 1 : (e && strcmp(e, "pair") == 0) ? 2 : 0;
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
   }
+  // Pairs take four 128-row query tiles each.  A short sequence (a 512-token
+  // prompt) would leave most SMs idle with pairs: one query tile per CTA on
+  // the single-CTA kernel then spreads the work over four times the CTAs and
+  // shortens each CTA's chain of key tiles.
+  const long pair_ctas = 2L * ((sq + 4 * BQ - 1) / (4 * BQ)) * heads;
+  const int one_tile = mode == 0 && pair_ctas <= sms / 2;
+  const int single = mode == 1 || one_tile;
   AttnParams p;
   memset(&p, 0, sizeof(p));
   // the pair kernel loads 64-key halves of each key tile
@@ -785,10 +797,12 @@ extern "C" cudaError_t iris_launch_attention_gqa(const void* q, int ldq, const v
   p.kmask = key_mask;
   p.causal = causal;
   p.kv_group = kv_group;
+  p.one_tile = one_tile;
   p.status = g_attn_status;
   const bool masked = key_mask != nullptr || causal;
   if (single) {
-    dim3 grid((sq + 2 * BQ - 1) / (2 * BQ), heads);
+    const int rows = one_tile ? BQ : 2 * BQ;
+    dim3 grid((sq + rows - 1) / rows, heads);
     if (masked) attn_tc_kernel<true><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(p);
     else attn_tc_kernel<false><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(p);
   } else {
