@@ -786,7 +786,7 @@ static void enq_ip(iris_cuda_flux_t *tf, enq_t *E, int blk, int row0, int rows) 
     flux_plan_t *P = &tf->plan;
     cudaStream_t st = g_rt.stream;
     const int H = tf->H, T = ip->T;
-    const uint16_t *k = ip->kv + (size_t)blk * 2 * T * H, *v = k + (size_t)T * H;
+    const uint16_t *k = ip->kv + (size_t)blk * T * H, *v = ip->kv + (size_t)(ip->nb + blk) * T * H;
     enq(E, iris_launch_ip_unrope(P->q + (size_t)row0 * H, H, P->rope_cos + (size_t)row0 * 64,
                                  P->rope_sin + (size_t)row0 * 64, rows, H, P->ip_q, st), "ip_unrope");
     enq_x(E, iris_launch_attention(P->ip_q, H, k, v, H, P->ip_o, H, rows, T, tf->NH, 1.0f / sqrtf(128.0f), NULL,

@@ -83,7 +83,7 @@ float iris_flux_sref_band(const iris_cuda_flux_t *tf, int d);
 /* IP-Adapter state (ipadapter.c), read by the forward's hooks (flux.c) */
 struct iris_flux_ip {
     int nb, nd, T;         /* adapter blocks (double then single), double blocks, image tokens */
-    uint16_t *kv;          /* bf16 [nb][2][T][H]: each block's k then v */
+    uint16_t *kv;          /* bf16 [2][nb][T][H]: every block's k, then every block's v */
     float *d_scale;        /* [nb] ip_scale * scale_mult * schedule multiplier (device) */
     float *h_scale;        /* [nb] ip_scale * scale_mult */
     float *h_cur;          /* [nb] staging of d_scale */

@@ -31,9 +31,13 @@ constexpr int SG_K = 16;
 
 __global__ void __launch_bounds__(256)
 ip_sgemm_kernel(const float* __restrict__ A, int lda, const float* __restrict__ B, int ldb, int transB,
-                const float* __restrict__ bias, float* __restrict__ C, int ldc, int M, int N, int K) {
+                const float* __restrict__ bias, float* __restrict__ C, int ldc, int M, int N, int K, long sA,
+                long sB, long sC) {
   __shared__ float As[SG_K][SG_T + 1];
   __shared__ float Bs[SG_K][SG_T + 1];
+  A += sA * blockIdx.z;  // batch: one (A, B, C) triple per z
+  B += sB * blockIdx.z;
+  C += sC * blockIdx.z;
   const int tx = threadIdx.x & 15, ty = threadIdx.x >> 4;
   const int m0 = blockIdx.y * SG_T, n0 = blockIdx.x * SG_T;
   float acc[4][4] = {};
@@ -226,10 +230,16 @@ extern "C" {
 
 cudaError_t iris_launch_ip_sgemm(const float* A, int lda, const float* B, int ldb, int transB, const float* bias,
                                  float* C, int ldc, int M, int N, int K, cudaStream_t stream) {
-  if (M <= 0 || N <= 0) return cudaSuccess;
-  if (K <= 0) return cudaErrorInvalidValue;
-  dim3 grid((N + SG_T - 1) / SG_T, (M + SG_T - 1) / SG_T);
-  ip_sgemm_kernel<<<grid, 256, 0, stream>>>(A, lda, B, ldb, transB, bias, C, ldc, M, N, K);
+  return iris_launch_ip_sgemm_batched(A, lda, 0, B, ldb, 0, transB, bias, C, ldc, 0, M, N, K, 1, stream);
+}
+
+cudaError_t iris_launch_ip_sgemm_batched(const float* A, int lda, long sA, const float* B, int ldb, long sB,
+                                         int transB, const float* bias, float* C, int ldc, long sC, int M, int N,
+                                         int K, int batch, cudaStream_t stream) {
+  if (M <= 0 || N <= 0 || batch <= 0) return cudaSuccess;
+  if (K <= 0 || batch > 65535) return cudaErrorInvalidValue;
+  dim3 grid((N + SG_T - 1) / SG_T, (M + SG_T - 1) / SG_T, batch);
+  ip_sgemm_kernel<<<grid, 256, 0, stream>>>(A, lda, B, ldb, transB, bias, C, ldc, M, N, K, sA, sB, sC);
   return cudaGetLastError();
 }
 

@@ -13,7 +13,7 @@
  * scale) and uploaded, the perceiver (SigLIP cross-attention, CSD FiLM, or the
  * hybrid of both) turns the features into ip_embeds [T, H], and every adapted
  * block's k = ip_embeds @ Wk[b], v = ip_embeds @ Wv[b] (hybrid: V groups gated)
- * is computed and kept in bf16 [nb][2][T][H] (20 MB for Klein-4B, T = 64).  The
+ * is computed and kept in bf16 [2][nb][T][H] (20 MB for Klein-4B, T = 64).  The
  * reference recomputes k / v inside every block of every step; here they are
  * constants of the attachment.
  *
@@ -312,8 +312,8 @@ int iris_cuda_flux_load_ip_adapter_mem(iris_cuda_flux_t *tf, const char *bundle_
     const int n = csd ? 1 : n_rows;
     feat = (float *)iris_dmalloc((size_t)n * row * sizeof(float));
     emb = (float *)iris_dmalloc((size_t)T * H * sizeof(float));
-    kf = (float *)iris_dmalloc((size_t)T * H * sizeof(float));
-    vf = (float *)iris_dmalloc((size_t)T * H * sizeof(float));
+    kf = (float *)iris_dmalloc((size_t)b.nb * T * H * sizeof(float));
+    vf = (float *)iris_dmalloc((size_t)b.nb * T * H * sizeof(float));
     ip = (struct iris_flux_ip *)calloc(1, sizeof(*ip));
     if (!feat || !emb || !kf || !vf || !ip) { rc = iris_fail(IRIS_CUDA_ERR_OOM, "IP-Adapter"); goto out; }
     if ((rc = iris_h2d(feat, features, (size_t)n * row * sizeof(float)))) goto out;
@@ -338,19 +338,21 @@ int iris_cuda_flux_load_ip_adapter_mem(iris_cuda_flux_t *tf, const char *bundle_
         rc = iris_cuda_check(cudaMemcpyAsync(hg, b.gate, (size_t)b.nb * 2 * sizeof(float), cudaMemcpyDeviceToHost,
                                              g_rt.stream), "IP gate");
     if (!rc) rc = iris_stream_drain();
-    for (int i = 0; !rc && i < b.nb; i++) {
-        ip->h_scale[i] *= scale_mult;
-        const size_t off = (size_t)i * H * H;
-        uint16_t *kb = ip->kv + (size_t)i * 2 * T * H, *vb = kb + (size_t)T * H;
-        /* einsum btd,de->te: embeds @ stacked[block] (iris_ip_adapter.c:366) */
-        rc = iris_cuda_check(iris_launch_ip_sgemm(emb, H, b.ipk + off, H, 0, NULL, kf, H, T, H, H, g_rt.stream), "k");
-        if (!rc) rc = iris_cuda_check(iris_launch_ip_sgemm(emb, H, b.ipv + off, H, 0, NULL, vf, H, T, H, H, g_rt.stream), "v");
-        if (!rc && hg)
-            rc = iris_cuda_check(iris_launch_ip_scale_rows(vf, T, H, T / 2, hg[2 * i], hg[2 * i + 1], g_rt.stream), "gate");
-        if (!rc) rc = iris_cuda_check(iris_launch_f32_to_bf16(kf, kb, (long)T * H, g_rt.stream), "k bf16");
-        if (!rc) rc = iris_cuda_check(iris_launch_f32_to_bf16(vf, vb, (long)T * H, g_rt.stream), "v bf16");
-        iris_count_launch(hg ? 5 : 4);
-    }
+    for (int i = 0; i < b.nb; i++) ip->h_scale[i] *= scale_mult;
+    /* every block at once: k[b] = embeds @ Wk[b], v[b] = embeds @ Wv[b] (einsum btd,de->te,
+       iris_ip_adapter.c:366), f32, then the hybrid gate on V and bf16 [2][nb][T][H] */
+    const long THl = (long)T * H, HHl = (long)H * H;
+    if (!rc) rc = iris_cuda_check(iris_launch_ip_sgemm_batched(emb, H, 0, b.ipk, H, HHl, 0, NULL, kf, H, THl, T, H, H,
+                                                               b.nb, g_rt.stream), "k");
+    if (!rc) rc = iris_cuda_check(iris_launch_ip_sgemm_batched(emb, H, 0, b.ipv, H, HHl, 0, NULL, vf, H, THl, T, H, H,
+                                                               b.nb, g_rt.stream), "v");
+    for (int i = 0; !rc && hg && i < b.nb; i++)
+        rc = iris_cuda_check(iris_launch_ip_scale_rows(vf + (size_t)i * THl, T, H, T / 2, hg[2 * i], hg[2 * i + 1],
+                                                       g_rt.stream), "gate");
+    if (!rc) rc = iris_cuda_check(iris_launch_f32_to_bf16(kf, ip->kv, (long)b.nb * THl, g_rt.stream), "k bf16");
+    if (!rc) rc = iris_cuda_check(iris_launch_f32_to_bf16(vf, ip->kv + (size_t)b.nb * THl, (long)b.nb * THl,
+                                                          g_rt.stream), "v bf16");
+    iris_count_launch(4 + (hg ? b.nb : 0));
     free(hg);
     if (!rc) rc = upload_scales(ip);
     if (rc) goto out;

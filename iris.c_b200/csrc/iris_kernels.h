@@ -268,6 +268,10 @@ cudaError_t iris_launch_lora_fold(const IrisLoraFold *f, void *scratch, size_t s
 /* f32 C[M, N] = A[M, K] (B[N, K])^T (transB) or A B[K, N], + bias[N] */
 cudaError_t iris_launch_ip_sgemm(const float *A, int lda, const float *B, int ldb, int transB, const float *bias,
                                  float *C, int ldc, int M, int N, int K, cudaStream_t stream);
+/* the same for `batch` problems, operand z at A + z*sA, B + z*sB, C + z*sC */
+cudaError_t iris_launch_ip_sgemm_batched(const float *A, int lda, long sA, const float *B, int ldb, long sB,
+                                         int transB, const float *bias, float *C, int ldc, long sC, int M, int N,
+                                         int K, int batch, cudaStream_t stream);
 cudaError_t iris_launch_ip_colnorm(const float *x, int n, int S, const float *g, const float *b, float *out,
                                    cudaStream_t stream);
 cudaError_t iris_launch_ip_layernorm(float *x, int rows, int H, const float *w, const float *b, cudaStream_t stream);
