@@ -173,3 +173,35 @@ def test_sampler_with_schedule_matches_reference(model, tmp_path, spec):
     assert rf.set_ip(b, feats, 1.0) == 0 and rf.set_ip_schedule(spec) == 0
     assert rel_l2(z, rf.sample_euler(z0, ctx, sched)) < TOL
     rf.close()
+
+
+def test_lora_ip_and_references_together(model, tmp_path):
+    """A LoRA folded into the weights, an IP-Adapter on the image rows (target
+    and reference tokens, as the reference's img_seq includes them) and two
+    reference latents in one forward, against the reference with its hooks and
+    the oracle (folded weights + ip_context + refs)."""
+    from oracle import lora_oracle as lo
+    from oracle.ref_lib import RefFlux
+    d, w, m = model
+    dims = mg.flux_dims(CFG)
+    lp = str(tmp_path / "l.safetensors")
+    mg.make_flux_lora(lp, CFG, "bfl", rank=8, seed=9, std=0.15)
+    b = str(tmp_path / "ip")
+    mg.make_ip_bundle(b, CFG, "siglip", seed=12)
+    feats = mg.ip_features("siglip", seed=6)
+    lat, ctx = _inputs()
+    refs = [np.random.default_rng(30 + i).standard_normal((128, 2, 3)).astype(np.float32) for i in range(2)]
+    m.load_lora(lp, 0.7)
+    m.load_ip_adapter(b, feats, 1.1)
+    v = m.forward(lat, ctx, 0.6, refs=refs)
+    m.unload_ip_adapter()
+    m.unload_lora()
+    L = lo.load_lora(lp, dims["n_double"], dims["n_single"], dims["hidden"])
+    v_or = fo.forward(lo.merge(w, L, 0.7), CFG, lat, ctx, 0.6, refs=refs,
+                      ip=io.ip_context(io.load_bundle(b), feats, 1.1))
+    assert rel_l2(v, v_or) < TOL
+    ref = pu.ref_lib_or_skip()
+    rf = RefFlux(ref, d)
+    assert rf.set_lora(lp, 0.7) and rf.set_ip(b, feats, 1.1) == 0
+    assert rel_l2(v, rf.forward_refs(lat, refs, ctx, 0.6)) < TOL
+    rf.close()
