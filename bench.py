@@ -1114,7 +1114,8 @@ def run_vae(args):
         vae_img = vae.decode(pin.numpy())
         img[...] = vae_img
 
-    run_host(0)
+    for i in range(max(3, args.warmup)):
+        run_host(i)
     ms_e2e, _ = timed(run_host, max(3, args.steps // 2))
     per_e2e = ms_e2e / max(3, args.steps // 2)
     prof = vae.profile()
@@ -1277,6 +1278,8 @@ def run_qwen3(args):
     with ClockSampler(gpu_smi_id(local)) as clk:
         ms, launches = timed(run, args.steps)
     per = ms / args.steps
+    for i in range(max(3, args.warmup)):  # the first host call pins the staging ring
+        m.forward(ids, mask)
     ms_e2e, _ = timed(lambda i: m.forward(ids, mask), max(3, args.steps // 2))
     per_e2e = ms_e2e / max(3, args.steps // 2)
     fl = qwen3_flops(QWEN3_4B)

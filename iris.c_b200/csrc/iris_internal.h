@@ -120,6 +120,9 @@ typedef struct {
 void iris_wsrc_free(iris_wsrc_t *ws);
 /* the process-wide upload ring and reader threads (iris_cuda_cleanup) */
 void iris_wsrc_release_staging(void);
+/* device bytes -> pageable host memory through the pinned ring and the copy
+ * threads, after the work queued on the library stream; synchronous */
+int iris_d2h_staged(void *dst, const void *d_src, size_t bytes, const char *name);
 
 /* Write the reference-layout tensor `name` ([numel] bf16) to device memory. */
 int iris_wsrc_get(iris_wsrc_t *ws, const char *name, size_t numel, uint16_t *d_dst);

@@ -494,8 +494,7 @@ float *iris_cuda_qwen3_forward(iris_cuda_qwen3_t *m, const int *input_ids, const
     float *out = (float *)malloc(n * 4);
     if (!out) { iris_fail(IRIS_CUDA_ERR_OOM, "output"); return NULL; }
     int rc = q3_run(m);
-    if (!rc) rc = iris_cuda_check(cudaMemcpyAsync(out, m->plan.out, n * 4, cudaMemcpyDeviceToHost, g_rt.stream), "d2h");
-    if (!rc) rc = iris_cuda_synchronize();
+    if (!rc) rc = iris_d2h_staged(out, m->plan.out, n * 4, "d2h");
     if (rc) { free(out); return NULL; }
     return out;
 }

@@ -45,8 +45,9 @@ struct iris_cpool {
     int n;
     pthread_mutex_t mu;
     pthread_cond_t cv_job, cv_done;
-    int fd;               /* the job: len bytes at file offset foff -> dst */
+    int fd;               /* the job: len bytes at file offset foff (or of msrc) -> dst */
     off_t foff;
+    const uint8_t *msrc;
     uint8_t *dst;
     size_t len;
     unsigned gen;
@@ -95,9 +96,12 @@ static void *cpool_worker(void *arg) {
         cpool_slice(p, idx, &a, &b);
         const int fd = p->fd;
         const off_t off = p->foff;
+        const uint8_t *msrc = p->msrc;
         uint8_t *dst = p->dst;
         pthread_mutex_unlock(&p->mu);
-        int bad = b > a ? read_range(fd, dst + a, off + (off_t)a, b - a) : 0;
+        int bad = 0;
+        if (b > a && msrc) memcpy(dst + a, msrc + a, b - a);
+        else if (b > a) bad = read_range(fd, dst + a, off + (off_t)a, b - a);
         pthread_mutex_lock(&p->mu);
         if (bad) p->err = 1;
         if (--p->pending == 0) pthread_cond_signal(&p->cv_done);
@@ -125,12 +129,18 @@ static struct iris_cpool *cpool_new(void) {
     return p;
 }
 
-/* len bytes of file fd at offset off -> dst, split over the pool; 0 or -1 */
-static int cpool_read(struct iris_cpool *p, uint8_t *dst, int fd, off_t off, size_t len) {
-    if (!p || p->n == 0 || len < ((size_t)1 << 20)) return read_range(fd, dst, off, len);
+/* len bytes of file fd at offset off (msrc == NULL) or of host memory msrc ->
+ * dst, split over the pool; 0 or -1 */
+static int cpool_run(struct iris_cpool *p, uint8_t *dst, const uint8_t *msrc, int fd, off_t off, size_t len) {
+    if (!p || p->n == 0 || len < ((size_t)1 << 20)) {
+        if (!msrc) return read_range(fd, dst, off, len);
+        memcpy(dst, msrc, len);
+        return 0;
+    }
     pthread_mutex_lock(&p->mu);
     p->fd = fd;
     p->foff = off;
+    p->msrc = msrc;
     p->dst = dst;
     p->len = len;
     p->err = 0;
@@ -140,7 +150,9 @@ static int cpool_read(struct iris_cpool *p, uint8_t *dst, int fd, off_t off, siz
     size_t a, b;
     cpool_slice(p, p->n, &a, &b);
     pthread_mutex_unlock(&p->mu);
-    int bad = b > a ? read_range(fd, dst + a, off + (off_t)a, b - a) : 0;
+    int bad = 0;
+    if (b > a && msrc) memcpy(dst + a, msrc + a, b - a);
+    else if (b > a) bad = read_range(fd, dst + a, off + (off_t)a, b - a);
     pthread_mutex_lock(&p->mu);
     while (p->pending) pthread_cond_wait(&p->cv_done, &p->mu);
     bad |= p->err;
@@ -192,19 +204,24 @@ void iris_wsrc_release_staging(void) {
     g_pool = NULL;
 }
 
+static int ring_ensure(void) {
+    if (g_ring[0]) return 0;
+    for (int i = 0; i < WS_RING; i++) {
+        if (cudaMallocHost((void **)&g_ring[i], WS_CHUNK) != cudaSuccess ||
+            cudaEventCreateWithFlags(&g_ring_ev[i], cudaEventDisableTiming) != cudaSuccess) {
+            cudaGetLastError();
+            iris_wsrc_release_staging();
+            return iris_fail(IRIS_CUDA_ERR_OOM, "pinned staging ring");
+        }
+    }
+    g_pool = cpool_new();
+    return 0;
+}
+
 static int ws_ring_init(iris_wsrc_t *ws) {
     if (ws->ring[0]) return 0;
-    if (!g_ring[0]) {
-        for (int i = 0; i < WS_RING; i++) {
-            if (cudaMallocHost((void **)&g_ring[i], WS_CHUNK) != cudaSuccess ||
-                cudaEventCreateWithFlags(&g_ring_ev[i], cudaEventDisableTiming) != cudaSuccess) {
-                cudaGetLastError();
-                iris_wsrc_release_staging();
-                return iris_fail(IRIS_CUDA_ERR_OOM, "pinned upload ring");
-            }
-        }
-        g_pool = cpool_new();
-    }
+    int rc = ring_ensure();
+    if (rc) return rc;
     for (int i = 0; i < WS_RING; i++) {
         ws->ring[i] = g_ring[i];
         ws->ring_ev[i] = g_ring_ev[i];
@@ -212,6 +229,36 @@ static int ws_ring_init(iris_wsrc_t *ws) {
     ws->pool = g_pool;
     ws->ring_i = 0;
     return 0;
+}
+
+/* bytes of device memory d_src -> pageable host memory dst, after the work
+ * already queued on the library stream.  Chunks are DMA'd into the pinned ring
+ * up to WS_RING ahead while the pool copies earlier chunks out of their slots
+ * (and takes the first-touch page faults of a fresh malloc'd dst in parallel);
+ * a pageable cudaMemcpy instead stages through the driver's own buffers on one
+ * thread.  Returns when dst holds the bytes. */
+#define D2H_CHUNK ((size_t)8 << 20)
+int iris_d2h_staged(void *dst, const void *d_src, size_t bytes, const char *name) {
+    int rc = ring_ensure();
+    const size_t nch = (bytes + D2H_CHUNK - 1) / D2H_CHUNK;
+    size_t issued = 0;
+    for (size_t c = 0; !rc && c < nch; c++) {
+        for (; !rc && issued < nch && issued < c + WS_RING; issued++) {
+            const int slot = (int)(issued % WS_RING);
+            const size_t off = issued * D2H_CHUNK, n = bytes - off < D2H_CHUNK ? bytes - off : D2H_CHUNK;
+            rc = iris_cuda_check(cudaEventSynchronize(g_ring_ev[slot]), name);
+            if (!rc) rc = iris_cuda_check(cudaMemcpyAsync(g_ring[slot], (const uint8_t *)d_src + off, n,
+                                                          cudaMemcpyDeviceToHost, g_rt.stream), name);
+            if (!rc) rc = iris_cuda_check(cudaEventRecord(g_ring_ev[slot], g_rt.stream), name);
+        }
+        if (rc) break;
+        const int slot = (int)(c % WS_RING);
+        const size_t off = c * D2H_CHUNK, n = bytes - off < D2H_CHUNK ? bytes - off : D2H_CHUNK;
+        rc = iris_cuda_check(cudaEventSynchronize(g_ring_ev[slot]), name);
+        if (!rc) cpool_run(g_pool, (uint8_t *)dst + off, g_ring[slot], -1, 0, n);
+    }
+    if (rc) iris_cuda_synchronize();  /* no DMA into a slot outlives the call */
+    return rc;
 }
 
 /* bytes of a file (fd, offset) -> device, through the ring */
@@ -223,7 +270,7 @@ static int ws_upload(iris_wsrc_t *ws, void *d_dst, int fd, off_t src, size_t byt
         ws->ring_i = (slot + 1) % WS_RING;
         rc = iris_cuda_check(cudaEventSynchronize(ws->ring_ev[slot]), name);  /* the slot's last DMA is done */
         if (rc) break;
-        if (cpool_read(ws->pool, ws->ring[slot], fd, src + (off_t)off, n)) {
+        if (cpool_run(ws->pool, ws->ring[slot], NULL, fd, src + (off_t)off, n)) {
             rc = iris_fail(IRIS_CUDA_ERR_IO, "tensor %s: read failed", name);
             break;
         }

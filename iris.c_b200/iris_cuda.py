@@ -8,6 +8,7 @@ from __future__ import annotations
 
 import ctypes as C
 import os
+import weakref
 
 import numpy as np
 
@@ -267,8 +268,11 @@ def _f(a: np.ndarray):
 def _take_floats(ptr, n, shape=None) -> np.ndarray:
     if not ptr:
         raise IrisCudaError(last_error() or "call failed")
-    arr = np.ctypeslib.as_array(C.cast(ptr, _fp), shape=(n,)).copy()
-    _libc.free(ptr)
+    # the library's malloc'd buffer becomes the array's memory (no copy); it is
+    # freed when the last view of it goes away
+    buf = (C.c_float * n).from_address(ptr)
+    weakref.finalize(buf, _libc.free, ptr)
+    arr = np.frombuffer(buf, np.float32)
     return arr.reshape(shape) if shape is not None else arr
 
 
