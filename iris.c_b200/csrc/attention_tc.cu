@@ -81,6 +81,7 @@ struct AttnBars {
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
+  int nkv;  // key tiles this CTA visits (live_key_tiles)
 };
 
 struct AttnParams {
@@ -342,6 +343,47 @@ __device__ __forceinline__ void softmax_role(const AttnParams& p, uint32_t tmem,
   }
 }
 
+// Key tiles a CTA (or CTA pair) whose query rows are [row_first, row_last]
+// visits; one warp computes it.  Tiles after the last key the mask keeps,
+// and under the causal mask tiles after row_last, are masked for every row:
+// once a row has seen a kept key such a tile adds exactly nothing (P = 0, the
+// dead-tile path of the softmax), so the loops end before them.  A row that
+// sees no kept key at all (a causal row before the first kept key, or a mask
+// that keeps none) takes the exact path over every key tile, so a CTA holding
+// one visits them all.  Mask bytes are read four at a time from 4-byte
+// aligned offsets, as the softmax reads them.
+template <bool kMasked>
+__device__ int live_key_tiles(const AttnParams& p, int row_first, int row_last, int lane) {
+  const int n = (p.sk + BKV - 1) / BKV;
+  if (!kMasked) return n;
+  int first = 0, last = p.sk - 1;
+  if (p.kmask) {
+    int lo = 0x7fffffff, hi = -1;
+    for (int k = 4 * lane; k < p.sk; k += 128) {
+      uint32_t m4 = 0;
+      if (k + 3 < p.sk) m4 = *reinterpret_cast<const uint32_t*>(p.kmask + k);
+      else
+        for (int e = 0; e < 4; e++) m4 |= (k + e < p.sk) ? (uint32_t)p.kmask[k + e] << (8 * e) : 0u;
+      if (m4) {
+        lo = min(lo, k + (__ffs(m4) - 1) / 8);
+        hi = max(hi, k + (31 - __clz(m4)) / 8);
+      }
+    }
+    for (int o = 16; o; o >>= 1) {
+      lo = min(lo, __shfl_xor_sync(0xffffffffu, lo, o));
+      hi = max(hi, __shfl_xor_sync(0xffffffffu, hi, o));
+    }
+    if (hi < 0) return n;
+    first = lo;
+    last = hi;
+  }
+  if (p.causal) {
+    if (row_first < first) return n;
+    last = min(last, row_last);
+  }
+  return min(n, last / BKV + 1);
+}
+
 template <bool kMasked>
 __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_constant__ AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -355,8 +397,11 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
   const bool has1 = !p.one_tile && q0 + BQ < p.sq;  // second query tile holds rows
   const int col0 = head * HD;
   const int kvcol0 = (head / p.kv_group) * HD;
-  const int n = (p.sk + BKV - 1) / BKV;
 
+  if (warp == 2) {
+    const int nkv = live_key_tiles<kMasked>(p, q0, min(p.sq, q0 + (has1 ? 2 : 1) * BQ) - 1, lane);
+    if (lane == 0) bars->nkv = nkv;
+  }
   if (threadIdx.x == 0) {
     iris::mbar_init(&bars->q_full, 1);
     for (int s = 0; s < KST; s++) {
@@ -384,6 +429,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
   __syncthreads();
   iris::tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
+  const int n = bars->nkv;
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer
@@ -551,7 +597,10 @@ struct PairBars {
   uint64_t drain;
   uint32_t tmem_base;
   int abort;
+  int nkv;                                   // key tiles the pair visits (live_key_tiles)
 };
+
+static_assert(sizeof(AttnBars) <= 256 && sizeof(PairBars) <= 512, "barrier blocks fit their reserved shared bytes");
 
 template <bool kMasked>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
@@ -567,8 +616,12 @@ attn_pair_kernel(const __grid_constant__ AttnParams p) {
   const int q0 = (blockIdx.x >> 1) * (4 * BQ) + (int)rank * (2 * BQ);  // this CTA's two query tiles
   const int col0 = head * HD;
   const int kvcol0 = (head / p.kv_group) * HD;
-  const int n = (p.sk + BKV - 1) / BKV;
 
+  if (warp == 2) {  // both CTAs of the pair: the same rows, the same count
+    const int r0 = (blockIdx.x >> 1) * (4 * BQ);
+    const int nkv = live_key_tiles<kMasked>(p, r0, min(p.sq, r0 + 4 * BQ) - 1, lane);
+    if (lane == 0) bars->nkv = nkv;
+  }
   if (threadIdx.x == 0) {
     iris::mbar_init(&bars->q_full, 2);
     for (int s = 0; s < PK_ST; s++) {
@@ -597,6 +650,7 @@ attn_pair_kernel(const __grid_constant__ AttnParams p) {
   iris::cluster_sync();  // both CTAs' barriers exist before any remote arrive
   iris::tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
+  const int n = bars->nkv;
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------------------ producer (both CTAs)
@@ -761,6 +815,7 @@ extern "C" cudaError_t iris_launch_attention_gqa(const void* q, int ldq, const v
   if (sq <= 0 || sk <= 0 || heads <= 0) return cudaSuccess;
   if (kv_group < 1 || heads % kv_group) return cudaErrorInvalidValue;
   if ((ldq | ldk | ldo) & 7) return cudaErrorInvalidValue;
+  if (reinterpret_cast<uintptr_t>(key_mask) & 3) return cudaErrorInvalidValue;  // read four bytes at a time
   if (!g_attn_tc_attr) {
     cudaError_t e = iris_attention_tc_init();
     if (e != cudaSuccess) return e;

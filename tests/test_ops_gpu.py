@@ -103,3 +103,61 @@ def test_silu_mul_gated_add_and_layout_ops(iris):
     S = Dev(n=4 * hid)
     iris.lib().iris_gpu_slice_seq_bf16(S.h, AB.h, 4, hid, 2)
     np.testing.assert_array_equal(S.read((4, hid)), np.concatenate([a, b])[2:6])
+
+
+def _masked_ref(q, k, v, heads, group, keep, causal, scale):
+    """fp32 causal / key-masked grouped-query attention: masked scores are
+    -1e9 (the reference encoder's value), so a row with no kept key averages
+    every value row."""
+    import torch
+    S, Sk = q.shape[0], k.shape[0]
+    qh = q.float().view(S, heads, 128).transpose(0, 1)
+    kh = k.float().view(Sk, heads // group, 128).transpose(0, 1).repeat_interleave(group, 0)
+    vh = v.float().view(Sk, heads // group, 128).transpose(0, 1).repeat_interleave(group, 0)
+    s = qh @ kh.transpose(1, 2) * scale
+    dead = ~keep.bool()[None, None, :].expand(1, S, Sk)
+    if causal:
+        i = torch.arange(S, device=q.device)
+        dead = dead | (i[None, None, :] > i[None, :, None])
+    s = s.masked_fill(dead, -1e9)
+    return (torch.softmax(s, -1) @ vh).transpose(0, 1).reshape(S, heads * 128)
+
+
+@pytest.mark.parametrize("S,heads,group", [(512, 32, 4), (2560, 16, 2)])
+@pytest.mark.parametrize("mask", ["right", "left", "holes", "none_kept", "all_kept"])
+@pytest.mark.parametrize("causal", [1, 0])
+def test_masked_attention_key_tile_bound(iris, S, heads, group, mask, causal):
+    """iris_launch_attention_gqa with a key mask and / or the causal mask: CTAs
+    stop after the last key tile any of their rows can use (the last kept key,
+    and under the causal mask their last row), except where a row keeps no key
+    and averages all of them.  512 rows x 32 heads runs one query tile per
+    CTA, 2560 x 16 the CTA pairs; fp32 reference, relative L2 <= 1e-2."""
+    import torch
+    g = torch.Generator(device="cuda").manual_seed(S + heads + causal)
+    kvh = heads // group
+    q = torch.randn(S, heads * 128, device="cuda", generator=g).bfloat16()
+    k = torch.randn(S, kvh * 128, device="cuda", generator=g).bfloat16()
+    v = torch.randn(S, kvh * 128, device="cuda", generator=g).bfloat16()
+    keep = torch.zeros(S, dtype=torch.uint8, device="cuda")
+    if mask == "right":
+        keep[:77] = 1
+    elif mask == "left":
+        keep[300:] = 1
+    elif mask == "holes":
+        keep[5:40] = 1
+        keep[200:260] = 1
+    elif mask == "all_kept":
+        keep[:] = 1
+    o = torch.empty_like(q)
+    scale = 1.0 / np.sqrt(128.0)
+    st = torch.cuda.current_stream().cuda_stream
+    rc = iris.lib().iris_launch_attention_gqa(
+        C.c_void_p(q.data_ptr()), heads * 128, C.c_void_p(k.data_ptr()), C.c_void_p(v.data_ptr()), kvh * 128,
+        C.c_void_p(o.data_ptr()), heads * 128, S, S, heads, group, causal, C.c_float(scale),
+        C.c_void_p(keep.data_ptr()), C.c_void_p(st))
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert iris.lib().iris_cuda_device_status(0) == 0
+    ref = _masked_ref(q, k, v, heads, group, keep, causal, scale)
+    err = float((o.float() - ref).norm() / ref.norm())
+    assert err < 1e-2, err
