@@ -180,6 +180,33 @@ __device__ __forceinline__ void softmax_role(const AttnParams& p, uint32_t tmem,
     if (kMasked && p.causal && key > qrow) return -1e9f * LOG2E;
     return sv * p.scale_log2;
   };
+  // A tile with masked or padding keys is rewritten in place once
+  // (mask_tile) and then takes the full-tile path instead of testing every
+  // key in each pass: a masked key's S becomes masked_s, whose logit is -1e9
+  // in natural-log units (the value above), a padding key's -inf.  Every
+  // masked key of a row carries the same logit, so a row without a kept key
+  // still spreads uniformly over them.  kw: the tile's kept-key bits, the
+  // same for every row (word e bit l = key 4l + e).
+  const float masked_s = -1e9f * LOG2E / p.scale_log2;
+  auto mask_tile = [&](int kbase, const uint32_t* kw) {
+    const int lim_c = (kMasked && p.causal) ? qrow - kbase : BKV;  // causal: keys past this row's own
+    const int lim_s = p.sk - kbase;                                  // padding from here on
+#pragma unroll 1
+    for (int c = 0; c < 4; c++) {
+      float sv[32];
+      iris::tmem_ld32(s_addr + 32 * c, sv);
+      uint32_t kc[4];  // the chunk's 32 keys: word e bit l = key 32c + 4l + e
+#pragma unroll
+      for (int e = 0; e < 4; e++) kc[e] = kw[e] >> (8 * c);
+#pragma unroll
+      for (int i = 0; i < 32; i++) {
+        const int kk = 32 * c + i;
+        const bool kept = ((kc[i & 3] >> (i >> 2)) & 1u) && kk <= lim_c;
+        sv[i] = kk >= lim_s ? -INFINITY : (kept ? sv[i] : masked_s);
+      }
+      iris::tmem_st32(s_addr + 32 * c, sv);
+    }
+  };
   // exponentials of 64 keys (half h of the tile) against reference max -nm
   // -> 32 packed bf16 words; returns the largest exponent argument
   auto half_exps = [&](int h, int kbase, bool full, float nm, uint32_t* pw, float* rsum) -> float {
@@ -254,6 +281,21 @@ __device__ __forceinline__ void softmax_role(const AttnParams& p, uint32_t tmem,
         }
         continue;
       }
+    }
+    if (kMasked && !full && IRIS_ATTN_EMU_PER8 == 0) {
+      uint32_t m4 = 0x01010101u;  // this lane's 4 keys, one byte each (non-zero = kept)
+      if (kMasked && p.kmask) {
+        const int k4 = kbase + 4 * lane;
+        m4 = 0;
+        if (k4 + 3 < p.sk) m4 = reinterpret_cast<const uint32_t*>(p.kmask + kbase)[lane];
+        else
+          for (int e = 0; e < 4; e++) m4 |= (k4 + e < p.sk) ? (uint32_t)p.kmask[k4 + e] << (8 * e) : 0u;
+      }
+      uint32_t kw[4];
+#pragma unroll
+      for (int e = 0; e < 4; e++) kw[e] = __ballot_sync(0xffffffffu, (m4 >> (8 * e)) & 0xffu);
+      mask_tile(kbase, kw);
+      full = true;
     }
     uint32_t pw[BKV / 2];
     float rsum[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
