@@ -76,7 +76,7 @@ def parse_args(argv=None):
     ap.add_argument("--profile-out", default=None, help="write the per-kernel CUDA-event profile (JSON)")
     ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "c5b", "vae512", "vae1024", "qwen3",
                                                      "lora", "load", "ip"],
-                    help="c2 (default) is the benchmark; the others measure the remaining SURVEY configs "
+                    help="c2 (default) is the benchmark; the others measure the remaining benchmark configs "
                          "on one GPU (c1 K4B 64x64 single forward, c3 K4B 1024x1024 CFG 4.0, c4 K9B "
                          "1792x1792, c5 Z-Image 1024x1024, c5b K4B + 2 references, lora: c2 with a "
                          "rank-32 LoRA folded into the weights, load: Klein-4B safetensors -> resident, "

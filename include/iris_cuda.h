@@ -498,12 +498,12 @@ void iris_gpu_adaln_norm_bf16(iris_gpu_tensor_t out, iris_gpu_tensor_t x,
                               int seq, int hidden, float eps);
 /* Same result as iris_gpu_adaln_norm_bf16, for callers that cannot allocate
  * device memory (a host application whose pool allocator owns all device
- * memory, code running while a stream capture is open, or latency-critical
- * loops that cannot take cudaMalloc/cudaFree's implicit synchronisation).  No
- * counterpart in the reference.  Takes raw bf16 device pointers the caller
- * owns (x, out [seq, hidden]; shift, scale [hidden]) and a cudaStream_t
- * (void *, 0 = default stream); queues work without synchronising and calls
- * no allocating routine.  Its scratch is one fixed array inside the library
+ * memory, or latency-critical loops that cannot take cudaMalloc/cudaFree's
+ * implicit synchronisation).  No counterpart in the reference.  Takes raw
+ * bf16 device pointers the caller owns (x, out [seq, hidden]; shift, scale
+ * [hidden]; out 8-byte aligned, the others 2-byte aligned, else
+ * IRIS_CUDA_ERR_ARG) and a cudaStream_t (void *, 0 = default stream); queues
+ * work without synchronising and calls no allocating routine.  Its scratch is one fixed array inside the library
  * (about 16.8 MB per GPU, held until exit): seq * hidden <= 4194304 and
  * hidden <= 8192, larger calls return IRIS_CUDA_ERR_ARG.  All calls share that
  * array, so calls whose GPU work overlaps race; the first call on a device
@@ -546,6 +546,116 @@ void iris_gpu_concat_attn_mlp_bf16(iris_gpu_tensor_t attn, iris_gpu_tensor_t mlp
 int iris_metal_available(void);
 int iris_metal_shaders_available(void);
 int iris_bf16_pipeline_available(void);
+
+/* The rest of the C surface of iris_metal.h that the reference's
+ * iris_transformer_flux.c and iris_transformer_zimage.c call when built with
+ * -DUSE_METAL (iris.c_b200/dropin builds them that way and links them here).
+ * f32 linears and attention run on the bf16 tensor cores with f32
+ * accumulation: f32 operands are rounded to bf16 on the way in. */
+void iris_gpu_add_bf16(iris_gpu_tensor_t out, iris_gpu_tensor_t a, iris_gpu_tensor_t b, int n); /* :451 */
+void iris_gpu_copy_bf16(iris_gpu_tensor_t dst, iris_gpu_tensor_t src, size_t n);     /* :454 */
+/* per-head RMSNorm of a bf16 tensor in place, bf16 weight [128].  :443 */
+int iris_gpu_head_rms_norm_bf16(iris_gpu_tensor_t x, iris_gpu_tensor_t weight_bf16, int seq, int heads,
+                                int head_dim, float eps);
+/* x (f32 or bf16) W^T -> new bf16 tensor.  :269 */
+iris_gpu_tensor_t iris_gpu_linear_bf16_bf16out(iris_gpu_tensor_t x, const uint16_t *W_bf16, int seq_len,
+                                               int in_dim, int out_dim);
+/* the other names of iris_gpu_attention_fused_bf16:  :291, :415 */
+int iris_gpu_attention_mps_bf16(iris_gpu_tensor_t out, iris_gpu_tensor_t Q, iris_gpu_tensor_t K,
+                                iris_gpu_tensor_t V, int seq_q, int seq_k, int num_heads, int head_dim,
+                                float scale);
+int iris_gpu_attention_bf16_native(iris_gpu_tensor_t out, iris_gpu_tensor_t Q, iris_gpu_tensor_t K,
+                                   iris_gpu_tensor_t V, int seq_q, int seq_k, int num_heads, int head_dim,
+                                   float scale);
+/* f32 host view of a tensor: the first call after GPU work copies it out;
+ * host writes to it are copied back before the next op that uses the tensor.
+ * Valid until the tensor is freed.  :208 */
+float *iris_gpu_tensor_data(iris_gpu_tensor_t tensor);
+/* f32 tensor ops; W / b / shift / scale / gate / norm weights / RoPE tables
+ * are host pointers.  Weights are cached on the device by address (like the
+ * Metal weight cache), RoPE tables by (address, size) until
+ * iris_metal_rope_cache_begin. */
+iris_gpu_tensor_t iris_gpu_linear(iris_gpu_tensor_t x, const float *W, const float *b, int seq_len,
+                                  int in_dim, int out_dim);                                /* :239 */
+iris_gpu_tensor_t iris_gpu_linear_bf16(iris_gpu_tensor_t x, const uint16_t *W_bf16, int seq_len,
+                                       int in_dim, int out_dim);                           /* :250 */
+int iris_gpu_linear_bf16_into(iris_gpu_tensor_t out, iris_gpu_tensor_t x, const uint16_t *W_bf16,
+                              int seq_len, int in_dim, int out_dim);                       /* :260 */
+void iris_gpu_adaln_norm(iris_gpu_tensor_t out, iris_gpu_tensor_t x, const float *shift,
+                         const float *scale, int seq, int hidden, float eps);              /* :353 */
+void iris_gpu_rms_norm_f32(iris_gpu_tensor_t out, iris_gpu_tensor_t x, const float *weight, int seq,
+                           int hidden, float eps);                                         /* :358 */
+void iris_gpu_qk_rms_norm(iris_gpu_tensor_t q, iris_gpu_tensor_t k, const float *q_weight,
+                          const float *k_weight, int seq, int heads, int head_dim, float eps); /* :362 */
+void iris_gpu_rope_single_f32(iris_gpu_tensor_t x, const float *cos_freq, const float *sin_freq, int seq,
+                              int heads, int head_dim);                                    /* :368 */
+void iris_gpu_rope_single_pair_f32(iris_gpu_tensor_t q, iris_gpu_tensor_t k, const float *cos_freq,
+                                   const float *sin_freq, int seq, int heads, int head_dim); /* :374 */
+void iris_gpu_rope_unified(iris_gpu_tensor_t q, iris_gpu_tensor_t k, const float *txt_cos,
+                           const float *txt_sin, const float *img_cos, const float *img_sin, int seq,
+                           int img_offset, int heads, int head_dim, int axis_dim);         /* :379 */
+void iris_gpu_silu_mul(iris_gpu_tensor_t gate, iris_gpu_tensor_t up, int n);           /* :385 */
+void iris_gpu_gated_add(iris_gpu_tensor_t out, const float *gate, iris_gpu_tensor_t proj, int seq,
+                        int hidden);                                                       /* :388 */
+void iris_gpu_split_qkv_mlp(iris_gpu_tensor_t fused, iris_gpu_tensor_t q, iris_gpu_tensor_t k,
+                            iris_gpu_tensor_t v, iris_gpu_tensor_t gate, iris_gpu_tensor_t up, int seq,
+                            int hidden, int mlp_hidden);                                   /* :392 */
+void iris_gpu_concat_attn_mlp(iris_gpu_tensor_t attn, iris_gpu_tensor_t mlp, iris_gpu_tensor_t out,
+                              int seq, int hidden, int mlp_hidden);                        /* :398 */
+int iris_gpu_attention_fused(iris_gpu_tensor_t out, iris_gpu_tensor_t Q, iris_gpu_tensor_t K,
+                             iris_gpu_tensor_t V, int seq_q, int seq_k, int num_heads, int head_dim,
+                             float scale);                                                 /* :402 */
+int iris_gpu_attention_bf16(iris_gpu_tensor_t out, iris_gpu_tensor_t Q, iris_gpu_tensor_t K,
+                            iris_gpu_tensor_t V, int seq_q, int seq_k, int num_heads, int head_dim,
+                            float scale);                                                  /* :301 */
+void iris_gpu_add_f32(iris_gpu_tensor_t out, iris_gpu_tensor_t a, iris_gpu_tensor_t b, int n); /* :537 */
+void iris_gpu_copy_f32(iris_gpu_tensor_t dst, iris_gpu_tensor_t src, size_t n);       /* :556 */
+void iris_gpu_copy_region_f32(iris_gpu_tensor_t dst, size_t dst_offset, iris_gpu_tensor_t src,
+                              size_t src_offset, size_t n);                                /* :566 */
+/* Host-pointer attention: Q, K, V, out f32 [seq, heads * 128] (fused) or
+ * [heads, seq, 128] (scores_scratch unused).  :649, :613 */
+int iris_metal_attention_fused(float *out, const float *Q, const float *K, const float *V, int seq_q,
+                               int seq_k, int num_heads, int head_dim, float scale);
+void iris_metal_attention(float *out, const float *Q, const float *K, const float *V,
+                          float *scores_scratch, int heads, int seq_q, int seq_k, int head_dim,
+                          float scale);
+/* The reference-token key bias of the SREF strength control (Metal-only in
+ * the reference).  Stored; while it is non-zero the attention ops return
+ * failure, and the reference's callers fall back to their CPU path, which
+ * does not apply it either.  :409 */
+void iris_metal_set_attention_bias(int ref_start, float bias);
+/* batching: work is queued on one stream in order, an end waits for it.  :315-344, :125-149 */
+void iris_gpu_chain_begin(void);
+void iris_gpu_chain_end(void);
+int iris_gpu_in_chain(void);
+void iris_metal_begin_batch(void);
+void iris_metal_end_batch(void);
+int iris_metal_in_batch(void);
+void iris_metal_sync(void);
+void iris_metal_wait_idle(void);
+/* runtime and caches (:23-54, :154): init returns 1 on success; reset drops
+ * the weight caches, RoPE tables and pooled tensor blocks; the "weight" cache
+ * is the one of f32 host weights, "bf16" the one of bf16 host weights; there
+ * is no f16 cache (a no-op); rope_cache_begin forgets the RoPE tables. */
+int iris_metal_init(void);
+void iris_metal_cleanup(void);
+void iris_metal_reset(void);
+void iris_metal_reset_transient(void);
+void iris_metal_rope_cache_begin(void);
+void iris_metal_clear_weight_cache_only(void);
+void iris_metal_clear_bf16_cache_only(void);
+void iris_metal_clear_f16_cache_only(void);
+void iris_metal_clear_activation_pool_only(void);
+size_t iris_metal_memory_used(void);
+/* upload host bf16 weights into the cache ahead of the first linear.  :710-725 */
+void iris_metal_warmup_bf16(const uint16_t *bf16_weights, size_t num_elements);
+void iris_metal_warmup_bf16_buffer(const uint16_t *bf16_weights, size_t num_elements);
+void iris_metal_warmup_bf16_buffers_parallel(const uint16_t **ptrs, const size_t *counts, int n);
+/* Ops of this surface that reported a failure (NULL / 0 / an error string)
+ * since the library was loaded.  No counterpart in the reference: a caller
+ * that falls back to its CPU path when an op fails (as the reference does)
+ * can check that the GPU path really ran. */
+unsigned long iris_gpu_op_failures(void);
 
 #ifdef __cplusplus
 }

@@ -862,22 +862,20 @@ extern "C" cudaError_t iris_launch_attention_gqa(const void* q, int ldq, const v
     cudaError_t e = iris_attention_tc_init();
     if (e != cudaSuccess) return e;
   }
-  static int mode = -1;  // IRIS_ATTN=1cta: always the single-CTA kernel; =pair: always pairs (A/B)
-  static int sms = 148;
-  if (mode < 0) {
-    const char* e = getenv("IRIS_ATTN");
-    mode = (e && strcmp(e, "1cta") == 0) ? 1 : (e && strcmp(e, "pair") == 0) ? 2 : 0;
-    int dev = 0;
+  static int sms = 0;
+  if (!sms) {
+    int dev = 0, n = 148;
     cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    sms = n;
   }
   // Pairs take four 128-row query tiles each.  A short sequence (a 512-token
   // prompt) would leave most SMs idle with pairs: one query tile per CTA on
   // the single-CTA kernel then spreads the work over four times the CTAs and
   // shortens each CTA's chain of key tiles.
   const long pair_ctas = 2L * ((sq + 4 * BQ - 1) / (4 * BQ)) * heads;
-  const int one_tile = mode == 0 && pair_ctas <= sms / 2;
-  const int single = mode == 1 || one_tile;
+  const int one_tile = pair_ctas <= sms / 2;
+  const int single = one_tile;
   AttnParams p;
   memset(&p, 0, sizeof(p));
   // the pair kernel loads 64-key halves of each key tile
@@ -910,17 +908,9 @@ extern "C" cudaError_t iris_launch_attention_gqa(const void* q, int ldq, const v
   return cudaGetLastError();
 }
 
-// Attention entry point: the tcgen05 kernel above; IRIS_ATTN=mma selects the
-// mma.sync kernel of attention.cu instead (kept for A/B measurements).
+// Attention entry point (the tcgen05 kernels above).
 extern "C" cudaError_t iris_launch_attention(const void* q, int ldq, const void* k, const void* v, int ldk,
                                              void* o, int ldo, int sq, int sk, int heads, float scale,
                                              const uint8_t* key_mask, cudaStream_t stream) {
-  static int use_mma = -1;
-  if (use_mma < 0) {
-    const char* e = getenv("IRIS_ATTN");
-    use_mma = (e && strcmp(e, "mma") == 0) ? 1 : 0;
-  }
-  if (use_mma)
-    return iris_launch_attention_mma(q, ldq, k, v, ldk, o, ldo, sq, sk, heads, scale, key_mask, stream);
   return iris_launch_attention_tc(q, ldq, k, v, ldk, o, ldo, sq, sk, heads, scale, key_mask, stream);
 }

@@ -1013,14 +1013,9 @@ extern "C" cudaError_t iris_launch_gemm_ex(const IrisGemmParams* p, int num_sms,
   }
   if (p->bn != 128 && p->bn != 256) return cudaErrorInvalidValue;
   if (p->K % BK != 0 || p->N % 128 != 0) return cudaErrorInvalidValue;
-  static int mode = -1;  // IRIS_GEMM=1cta keeps every launch on the single-CTA kernel
-  if (mode < 0) {
-    const char* e = getenv("IRIS_GEMM");
-    mode = (e && strcmp(e, "1cta") == 0) ? 1 : 0;
-  }
   const int rows = p->rows[0] + (p->ngroups > 1 ? p->rows[1] : 0);
   const bool linear = p->mode == IRIS_EPI_BF16 || p->mode == IRIS_EPI_F32 || p->mode == IRIS_EPI_RESID_GATE;
-  if (mode == 0 && p->bn == 256 && rows >= 512 && g_max_pairs > 0) {
+  if (p->bn == 256 && rows >= 512 && g_max_pairs > 0) {
     int mt = (p->rows[0] + BM2 - 1) / BM2 + (p->ngroups > 1 ? (p->rows[1] + BM2 - 1) / BM2 : 0);
     long total = (long)mt * ((p->N + 255) / 256);
     long cap = g_max_pairs < num_sms / 2 ? g_max_pairs : num_sms / 2;

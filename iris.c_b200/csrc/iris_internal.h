@@ -38,6 +38,8 @@ void iris_dfree(void *p);
 
 /* note `n` kernel launches (for iris_cuda_kernel_launches) */
 static inline void iris_count_launch(uint64_t n) { g_rt.launches += n; }
+/* the same, callable from the CUDA C++ translation units */
+void iris_note_launches(uint64_t n);
 
 /* ensure the runtime is up; returns status */
 int iris_rt_ensure(void);

@@ -125,7 +125,6 @@ cudaError_t iris_launch_gemm_ex(const IrisGemmParams *p, int num_sms, cudaStream
 /* one-time kernel attribute setup (dynamic shared memory limits); called at
  * library init so that nothing but launches happens during graph capture */
 cudaError_t iris_gemm_init(void);
-cudaError_t iris_attention_init(void);
 
 /* ------------------------------------------------------------------ attention
  * O = softmax(Q K^T * scale) V for every head, bf16 in/out, f32 softmax.
@@ -135,13 +134,10 @@ cudaError_t iris_attention_init(void);
 cudaError_t iris_launch_attention(const void *q, int ldq, const void *k, const void *v, int ldk,
                                   void *o, int ldo, int sq, int sk, int heads, float scale,
                                   const uint8_t *key_mask, cudaStream_t stream);
-/* the two implementations behind it: tcgen05/TMEM (default) and mma.sync */
+/* the tcgen05/TMEM implementation behind it */
 cudaError_t iris_launch_attention_tc(const void *q, int ldq, const void *k, const void *v, int ldk,
                                      void *o, int ldo, int sq, int sk, int heads, float scale,
                                      const uint8_t *key_mask, cudaStream_t stream);
-cudaError_t iris_launch_attention_mma(const void *q, int ldq, const void *k, const void *v, int ldk,
-                                      void *o, int ldo, int sq, int sk, int heads, float scale,
-                                      const uint8_t *key_mask, cudaStream_t stream);
 cudaError_t iris_attention_tc_init(void);
 /* tcgen05 attention with grouped-query heads (query head h reads key/value
  * head h / kv_group; K and V hold heads / kv_group heads) and an optional
@@ -370,6 +366,24 @@ cudaError_t iris_launch_vae_softmax(const float *s, int rows, int ld, int n, flo
                                     cudaStream_t stream);
 /* f32 planes [3, P] -> uint8 [P, 3] (reference rounding) */
 cudaError_t iris_launch_vae_rgb8(const float *x, long P, uint8_t *out, cudaStream_t stream);
+
+/* f32 row kernels of the op-level surface (compat_kernels.cu) */
+/* out = (1 + scale) * LayerNorm(x) + shift, rows of `cols` f32, eps inside the sqrt */
+cudaError_t iris_launch_layernorm_mod_f32(float *out, const float *x, const float *shift, const float *scale,
+                                          int rows, int cols, float eps, cudaStream_t stream);
+/* per-head (128) RMSNorm of f32 [rows, heads * 128] in place; x and w 16-byte aligned */
+cudaError_t iris_launch_head_rmsnorm_f32(float *x, int rows, int heads, const float *w, float eps,
+                                         cudaStream_t stream);
+/* consecutive-pair RoPE in place on [rows, heads * hd] (bf16 != 0: bf16 data) from
+ * [rows, table_ld] cos/sin tables, pair i using column 2i */
+cudaError_t iris_launch_rope_pairs(void *x, int bf16, int rows, int heads, int hd, const float *cs,
+                                   const float *sn, int table_ld, cudaStream_t stream);
+cudaError_t iris_launch_silu_mul_f32(float *gate, const float *up, long n, cudaStream_t stream);
+/* out[r, c] += gate[c] * proj[r, c] */
+cudaError_t iris_launch_gated_add_f32(float *out, const float *gate, const float *proj, int rows, int cols,
+                                      cudaStream_t stream);
+cudaError_t iris_launch_add_f32(float *out, const float *a, const float *b, long n, cudaStream_t stream);
+cudaError_t iris_launch_add_bf16(void *out, const void *a, const void *b, long n, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

@@ -497,13 +497,8 @@ static int pow2_at_least(int x) {
  * CTA pair (M = 256) with N = 256 or 128, whichever the wave count and the
  * shapes' relative throughputs on B200 (tensor-pipe share reached by each
  * shape; a single CTA at N = 128 is bound by shared-memory reads) predict to
- * finish first.  IRIS_VAE_CONV=1cta keeps every launch on the single-CTA form. */
+ * finish first. */
 static void conv_shape(IrisConvParams *p, const vconv_t *cv) {
-    static int force1 = -1;
-    if (force1 < 0) {
-        const char *e = getenv("IRIS_VAE_CONV");
-        force1 = (e && strcmp(e, "1cta") == 0) ? 1 : 0;
-    }
     if (cv->bn < 128) return;
     const int sms = g_rt.num_sms;
     const int pairs = iris_conv_pairs_available() < sms / 2 ? iris_conv_pairs_available() : sms / 2;
@@ -513,7 +508,7 @@ static void conv_shape(IrisConvParams *p, const vconv_t *cv) {
     double best = 1e30;
     for (int i = 0; i < 4; i++) {
         if (opt[i].bn > cv->bn || cv->cout_pad % opt[i].bn) continue;
-        if (opt[i].pair && (force1 || pairs <= 0)) continue;
+        if (opt[i].pair && pairs <= 0) continue;
         const long units = tx * (opt[i].pair ? ty2 : ty1) * (cv->cout_pad / opt[i].bn);
         const long slots = opt[i].pair ? pairs : sms;
         const double est = (double)((units + slots - 1) / slots) * opt[i].bn / opt[i].rate;

@@ -224,6 +224,56 @@ SIGNATURES = {
     "iris_metal_available": (C.c_int, []),
     "iris_metal_shaders_available": (C.c_int, []),
     "iris_bf16_pipeline_available": (C.c_int, []),
+    "iris_gpu_add_bf16": (None, [C.c_void_p] * 3 + [C.c_int]),
+    "iris_gpu_copy_bf16": (None, [C.c_void_p, C.c_void_p, C.c_size_t]),
+    "iris_gpu_head_rms_norm_bf16": (C.c_int, [C.c_void_p, C.c_void_p, C.c_int, C.c_int, C.c_int, C.c_float]),
+    "iris_gpu_linear_bf16_bf16out": (C.c_void_p, [C.c_void_p, _u16p, C.c_int, C.c_int, C.c_int]),
+    "iris_gpu_attention_mps_bf16": (C.c_int, [C.c_void_p] * 4 + [C.c_int] * 4 + [C.c_float]),
+    "iris_gpu_attention_bf16_native": (C.c_int, [C.c_void_p] * 4 + [C.c_int] * 4 + [C.c_float]),
+    "iris_gpu_tensor_data": (_fp, [C.c_void_p]),
+    "iris_gpu_linear": (C.c_void_p, [C.c_void_p, _fp, _fp, C.c_int, C.c_int, C.c_int]),
+    "iris_gpu_linear_bf16": (C.c_void_p, [C.c_void_p, _u16p, C.c_int, C.c_int, C.c_int]),
+    "iris_gpu_linear_bf16_into": (C.c_int, [C.c_void_p, C.c_void_p, _u16p, C.c_int, C.c_int, C.c_int]),
+    "iris_gpu_adaln_norm": (None, [C.c_void_p, C.c_void_p, _fp, _fp, C.c_int, C.c_int, C.c_float]),
+    "iris_gpu_rms_norm_f32": (None, [C.c_void_p, C.c_void_p, _fp, C.c_int, C.c_int, C.c_float]),
+    "iris_gpu_qk_rms_norm": (None, [C.c_void_p, C.c_void_p, _fp, _fp, C.c_int, C.c_int, C.c_int, C.c_float]),
+    "iris_gpu_rope_single_f32": (None, [C.c_void_p, _fp, _fp, C.c_int, C.c_int, C.c_int]),
+    "iris_gpu_rope_single_pair_f32": (None, [C.c_void_p, C.c_void_p, _fp, _fp, C.c_int, C.c_int, C.c_int]),
+    "iris_gpu_rope_unified": (None, [C.c_void_p, C.c_void_p, _fp, _fp, _fp, _fp] + [C.c_int] * 5),
+    "iris_gpu_silu_mul": (None, [C.c_void_p, C.c_void_p, C.c_int]),
+    "iris_gpu_gated_add": (None, [C.c_void_p, _fp, C.c_void_p, C.c_int, C.c_int]),
+    "iris_gpu_split_qkv_mlp": (None, [C.c_void_p] * 6 + [C.c_int] * 3),
+    "iris_gpu_concat_attn_mlp": (None, [C.c_void_p] * 3 + [C.c_int] * 3),
+    "iris_gpu_attention_fused": (C.c_int, [C.c_void_p] * 4 + [C.c_int] * 4 + [C.c_float]),
+    "iris_gpu_attention_bf16": (C.c_int, [C.c_void_p] * 4 + [C.c_int] * 4 + [C.c_float]),
+    "iris_gpu_add_f32": (None, [C.c_void_p] * 3 + [C.c_int]),
+    "iris_gpu_copy_f32": (None, [C.c_void_p, C.c_void_p, C.c_size_t]),
+    "iris_gpu_copy_region_f32": (None, [C.c_void_p, C.c_size_t, C.c_void_p, C.c_size_t, C.c_size_t]),
+    "iris_metal_attention_fused": (C.c_int, [_fp] * 4 + [C.c_int] * 4 + [C.c_float]),
+    "iris_metal_attention": (None, [_fp] * 5 + [C.c_int] * 4 + [C.c_float]),
+    "iris_metal_set_attention_bias": (None, [C.c_int, C.c_float]),
+    "iris_gpu_chain_begin": (None, []),
+    "iris_gpu_chain_end": (None, []),
+    "iris_gpu_in_chain": (C.c_int, []),
+    "iris_metal_begin_batch": (None, []),
+    "iris_metal_end_batch": (None, []),
+    "iris_metal_in_batch": (C.c_int, []),
+    "iris_metal_sync": (None, []),
+    "iris_metal_wait_idle": (None, []),
+    "iris_metal_init": (C.c_int, []),
+    "iris_metal_cleanup": (None, []),
+    "iris_metal_reset": (None, []),
+    "iris_metal_reset_transient": (None, []),
+    "iris_metal_rope_cache_begin": (None, []),
+    "iris_metal_clear_weight_cache_only": (None, []),
+    "iris_metal_clear_bf16_cache_only": (None, []),
+    "iris_metal_clear_f16_cache_only": (None, []),
+    "iris_metal_clear_activation_pool_only": (None, []),
+    "iris_metal_memory_used": (C.c_size_t, []),
+    "iris_metal_warmup_bf16": (None, [_u16p, C.c_size_t]),
+    "iris_metal_warmup_bf16_buffer": (None, [_u16p, C.c_size_t]),
+    "iris_metal_warmup_bf16_buffers_parallel": (None, [C.POINTER(_u16p), C.POINTER(C.c_size_t), C.c_int]),
+    "iris_gpu_op_failures": (C.c_ulong, []),
 }
 
 _libc = C.CDLL(None)

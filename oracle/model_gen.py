@@ -30,10 +30,17 @@ import numpy as np
 
 
 def f32_to_bf16_bits(x: np.ndarray) -> np.ndarray:
-    """Round-to-nearest-even f32 -> bf16, returned as uint16 bit patterns."""
-    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32).astype(np.uint64)
-    u = (u + 0x7FFF + ((u >> 16) & 1)) >> 16
-    return u.astype(np.uint16)
+    """Round-to-nearest-even f32 -> bf16, returned as uint16 bit patterns.
+
+    Computed in uint32: exact for every finite value and for infinities (the
+    largest finite pattern plus the rounding bias is below 2^32); only
+    negative NaN payloads above 0xFFFF7FFF would wrap, and no generator here
+    produces NaN."""
+    u = np.ascontiguousarray(x, dtype=np.float32).view(np.uint32)
+    r = u + np.uint32(0x7FFF)
+    r += (u >> np.uint32(16)) & np.uint32(1)
+    r >>= np.uint32(16)
+    return r.astype(np.uint16)
 
 
 def bf16_bits_to_f32(b: np.ndarray) -> np.ndarray:
@@ -119,6 +126,37 @@ def gen_tensor(seed: int, name: str, shape: tuple, kind: str, std: float = 0.02,
     return f32_to_bf16_bits(x)
 
 
+def write_safetensors_generated(path: str, specs, make, threads: int | None = None) -> None:
+    """Stream a bf16 safetensors file whose tensors are produced by make(name, shape, kind)
+    (uint16 bit patterns), generating up to 2*threads tensors ahead on a thread pool
+    (numpy's generators and ufuncs release the GIL) and writing them in order.  Used for
+    the full-width models (Klein-4B: 7.7 GB), which must not be held in memory whole."""
+    from concurrent.futures import ThreadPoolExecutor
+
+    header, off = {}, 0
+    for name, shp, _ in specs:
+        n = 2 * int(np.prod(shp))
+        header[name] = {"dtype": "BF16", "shape": list(shp), "data_offsets": [off, off + n]}
+        off += n
+    hj = json.dumps(header).encode()
+    hj += b" " * ((8 - len(hj) % 8) % 8)
+    threads = threads or min(32, os.cpu_count() or 1)
+    with open(path, "wb") as f, ThreadPoolExecutor(threads) as ex:
+        f.write(struct.pack("<Q", len(hj)))
+        f.write(hj)
+        pending = []
+        it = iter(specs)
+        for spec in it:
+            pending.append(ex.submit(make, *spec))
+            if len(pending) >= 2 * threads:
+                break
+        for spec in it:
+            f.write(pending.pop(0).result().tobytes())
+            pending.append(ex.submit(make, *spec))
+        for fut in pending:
+            f.write(fut.result().tobytes())
+
+
 def write_safetensors(path: str, tensors: dict[str, np.ndarray]) -> None:
     """Write uint16 (bf16) / float16 / int8 / float32 arrays in the safetensors container format."""
     header = {}
@@ -138,18 +176,23 @@ def write_safetensors(path: str, tensors: dict[str, np.ndarray]) -> None:
 
 
 def make_flux_model(model_dir: str, cfg: dict, seed: int, std: float = 0.02,
-                    norm_mode: str = "random") -> dict[str, np.ndarray]:
-    """Create a random Flux model directory; returns {name: f32 values}."""
+                    norm_mode: str = "random", keep: bool = True) -> dict[str, np.ndarray] | None:
+    """Create a random Flux model directory; returns {name: f32 values}, or None
+    with keep=False (full-width models: the file is streamed, nothing is held)."""
     os.makedirs(os.path.join(model_dir, "transformer"), exist_ok=True)
     full = dict(_class_name="Flux2Transformer2DModel", **cfg)
     with open(os.path.join(model_dir, "transformer", "config.json"), "w") as f:
         json.dump(full, f, indent=1)
     with open(os.path.join(model_dir, "model_index.json"), "w") as f:
         json.dump({"_class_name": "Flux2KleinPipeline"}, f)
+    path = os.path.join(model_dir, "transformer", "diffusion_pytorch_model.safetensors")
+    if not keep:
+        write_safetensors_generated(path, flux_tensor_specs(cfg),
+                                    lambda n, shp, kind: gen_tensor(seed, n, shp, kind, std, norm_mode))
+        return None
     bits = {n: gen_tensor(seed, n, shp, kind, std, norm_mode)
             for n, shp, kind in flux_tensor_specs(cfg)}
-    write_safetensors(os.path.join(model_dir, "transformer",
-                                   "diffusion_pytorch_model.safetensors"), bits)
+    write_safetensors(path, bits)
     return {n: bf16_bits_to_f32(b) for n, b in bits.items()}
 
 
@@ -404,7 +447,7 @@ def zimage_tensor_specs(cfg: dict) -> list[tuple[str, tuple, str]]:
 
 
 def make_zimage_model(model_dir: str, cfg: dict, seed: int, std: float = 0.02,
-                      norm_mode: str = "random") -> dict[str, np.ndarray]:
+                      norm_mode: str = "random", keep: bool = True) -> dict[str, np.ndarray] | None:
     """Random Z-Image model directory (config keys as read by the reference's
     model autodetection, iris.c:300-330); returns {name: f32 values}."""
     os.makedirs(os.path.join(model_dir, "transformer"), exist_ok=True)
@@ -416,8 +459,13 @@ def make_zimage_model(model_dir: str, cfg: dict, seed: int, std: float = 0.02,
         json.dump(conf, f, indent=1)
     with open(os.path.join(model_dir, "model_index.json"), "w") as f:
         json.dump({"_class_name": "ZImagePipeline"}, f)
+    path = os.path.join(model_dir, "transformer", "diffusion_pytorch_model.safetensors")
+    if not keep:
+        write_safetensors_generated(path, zimage_tensor_specs(cfg),
+                                    lambda n, shp, kind: gen_tensor(seed, n, shp, kind, std, norm_mode))
+        return None
     bits = {n: gen_tensor(seed, n, shp, kind, std, norm_mode) for n, shp, kind in zimage_tensor_specs(cfg)}
-    write_safetensors(os.path.join(model_dir, "transformer", "diffusion_pytorch_model.safetensors"), bits)
+    write_safetensors(path, bits)
     return {n: bf16_bits_to_f32(b) for n, b in bits.items()}
 
 

@@ -118,7 +118,7 @@ def sampler_case(ref: RefLib) -> dict:
     return out
 
 
-REF_TREE = os.environ.get("IRIS_REFERENCE", "/root/reference")
+REF_TREE = os.environ.get("IRIS_REFERENCE", os.path.join(os.path.dirname(ROOT), "reference"))
 
 
 def lora_fixture() -> dict:

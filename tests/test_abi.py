@@ -6,8 +6,11 @@
   reference's values (tests/golden/sampler.npz);
 * without a GPU the library fails loudly (no silent CPU fallback).
 """
+import ctypes
 import os
 import re
+import shutil
+import subprocess
 
 import numpy as np
 import pytest
@@ -71,3 +74,28 @@ def test_fails_loudly_without_gpu(tmp_path):
     assert not lib.iris_cuda_flux_load(str(tmp_path).encode())
     with pytest.raises(iris_cuda.IrisCudaError):
         iris_cuda.Flux.load(str(tmp_path))
+
+
+DROPIN = os.path.join(ROOT, "iris.c_b200", "dropin", "_build", "libiris_refdrive.so")
+
+
+def test_dropin_build_resolves_against_this_library():
+    """The reference's transformer / sampler sources, built unmodified with
+    -DUSE_METAL (iris.c_b200/dropin), link and load against libiris_cuda.so:
+    every iris_metal.h function they import is exported here."""
+    if not os.path.exists(DROPIN):
+        pytest.skip("drop-in build missing (needs the reference tree at build time)")
+    iris_cuda.load()
+    ctypes.CDLL(DROPIN, mode=os.RTLD_NOW)  # fails on any unresolved symbol
+    if not shutil.which("nm"):
+        return
+    und = subprocess.run(["nm", "-D", "--undefined-only", DROPIN], capture_output=True, text=True).stdout
+    imported = {line.split()[-1] for line in und.splitlines() if re.search(r"\biris_(gpu|metal|bf16)_", line)}
+    exported = {line.split()[-1] for line in subprocess.run(["nm", "-D", "--defined-only", iris_cuda.LIB_PATH],
+                                                            capture_output=True, text=True).stdout.splitlines()}
+    assert len(imported) > 50, sorted(imported)
+    assert imported <= exported, sorted(imported - exported)
+    for name in ("iris_gpu_linear_bf16_native", "iris_gpu_attention_fused_bf16", "iris_gpu_rope_unified_bf16",
+                 "iris_gpu_rms_norm_f32", "iris_gpu_rope_single_pair_f32", "iris_gpu_tensor_data",
+                 "iris_metal_warmup_bf16", "iris_metal_set_attention_bias", "iris_metal_rope_cache_begin"):
+        assert name in imported, name

@@ -1,0 +1,137 @@
+"""Parity at the benchmark configurations' full widths, against the reference.
+
+The golden tests (test_flux_gpu.py, test_zimage_gpu.py) pin every kernel and
+fused epilogue on small widths.  These tests run the production widths the
+benchmark configurations use, on seeded random-init bf16 weights, and compare
+the CUDA backend (through the C ABI) with the reference's own `make blas` CPU
+build (oracle/_ref, computed here in a spawned child, tests/ref_worker.py):
+
+* C1, the whole Klein-4B forward (hidden 3072, 24 heads, 5 double + 20 single
+  blocks, context 7680) on 16 image + 64 text tokens at t = 1.0 with every
+  tensor N(0, 0.02) (iris_transformer_forward, iris_transformer_flux.c:3939);
+  on the same model, double block 0 and single block 0 at the C2 shape,
+  1024 image + 512 text rows (double_block_forward :2366,
+  single_block_forward :3761);
+* C2-shape blocks again on a Klein-4B-width model whose QK-norm scales are
+  1 + N(0, 0.1), so that the attention softmax is far from uniform;
+* a Klein-9B-width model (hidden 4096, 32 heads, context 12288): both block
+  kinds and a forward;
+* a Z-Image-6B-width model (dim 3840, 30 heads, FFN 10240, caption 2560) with
+  one refiner of each kind and one main layer, padded image and caption rows
+  (zi_transformer_forward, iris_transformer_zimage.c:1696, on the reference
+  build whose in-place attention output GEMM is made alias-safe).
+
+Tolerances (north_star's bf16 bound): relative L2 <= 1e-2 for every velocity
+and block output, <= 2e-2 for every block delta (output - input).
+"""
+import numpy as np
+import pytest
+
+import psnr_util as pu
+import ref_worker
+from gpu_util import rel_l2
+from oracle import model_gen as mg
+
+pytestmark = pytest.mark.gpu
+
+TOL = 1e-2
+TOL_DELTA = 2e-2
+
+
+@pytest.fixture(scope="module", autouse=True)
+def _reference_present():
+    pu.ref_lib_or_skip()
+
+
+def _inputs(seed, channels, h, w, txt, text_dim):
+    r = np.random.default_rng(seed)
+    lat = r.standard_normal((channels, h, w)).astype(np.float32)
+    ctx = r.standard_normal((txt, text_dim)).astype(np.float32)
+    return lat, ctx
+
+
+def _hidden(seed, img, txt, hidden):
+    r = np.random.default_rng(seed)
+    return (r.standard_normal((img, hidden)).astype(np.float32),
+            r.standard_normal((txt, hidden)).astype(np.float32))
+
+
+def _check_blocks(m, ref_out, idx, img_h, txt_h, ph, pw, t):
+    ri, rt, rs = ref_out
+    hid = np.concatenate([txt_h, img_h])
+    nt = txt_h.shape[0]
+    out = m.run_block(0, idx, hid, nt, ph, pw, t)
+    ot, oi = out[:nt], out[nt:]
+    errs = dict(dbl_img=rel_l2(oi, ri), dbl_txt=rel_l2(ot, rt),
+                dbl_img_delta=rel_l2(oi - img_h, ri - img_h), dbl_txt_delta=rel_l2(ot - txt_h, rt - txt_h))
+    so = m.run_block(1, idx, hid, nt, ph, pw, t)
+    errs.update(sgl=rel_l2(so, rs), sgl_delta=rel_l2(so - hid, rs - hid))
+    for k, e in errs.items():
+        assert e < (TOL_DELTA if k.endswith("delta") else TOL), (k, errs)
+    return errs
+
+
+def test_c1_klein4b_forward_and_c2_blocks(iris, tmp_path):
+    """The whole Klein-4B at BASELINE's init (every tensor N(0, 0.02))."""
+    d = str(tmp_path)
+    cfg = mg.KLEIN_4B
+    mg.make_flux_model(d, cfg, seed=2024, std=0.02, norm_mode="random", keep=False)
+    lat, ctx = _inputs(1, 128, 4, 4, 64, 7680)
+    img_h, txt_h = _hidden(2, 32 * 32, 512, 3072)
+    v_ref, blk_ref = ref_worker.flux(d, [("forward", lat, ctx, 1.0),
+                                         ("blocks", 0, img_h, txt_h, 32, 32, 0.8)])
+    m = iris.Flux.load(d)
+    try:
+        v = m.forward(lat, ctx, 1.0)
+        assert v.shape == (128, 4, 4)
+        assert rel_l2(v, v_ref) < TOL, rel_l2(v, v_ref)
+        _check_blocks(m, blk_ref, 0, img_h, txt_h, 32, 32, 0.8)
+    finally:
+        m.close()
+
+
+def test_c2_blocks_klein4b_sharp_attention(iris, tmp_path):
+    d = str(tmp_path)
+    cfg = dict(mg.KLEIN_4B, num_layers=1, num_single_layers=1)
+    mg.make_flux_model(d, cfg, seed=77, std=0.02, norm_mode="unit", keep=False)
+    img_h, txt_h = _hidden(3, 32 * 32, 512, 3072)
+    (blk_ref,) = ref_worker.flux(d, [("blocks", 0, img_h, txt_h, 32, 32, 0.6)])
+    m = iris.Flux.load(d)
+    try:
+        _check_blocks(m, blk_ref, 0, img_h, txt_h, 32, 32, 0.6)
+    finally:
+        m.close()
+
+
+def test_klein9b_width_blocks_and_forward(iris, tmp_path):
+    d = str(tmp_path)
+    cfg = dict(mg.KLEIN_9B, num_layers=1, num_single_layers=1)
+    mg.make_flux_model(d, cfg, seed=909, std=0.02, norm_mode="unit", keep=False)
+    img_h, txt_h = _hidden(4, 24 * 40, 96, 4096)
+    lat, ctx = _inputs(5, 128, 14, 18, 77, 12288)
+    blk_ref, v_ref = ref_worker.flux(d, [("blocks", 0, img_h, txt_h, 24, 40, 0.9),
+                                         ("forward", lat, ctx, 0.7)])
+    m = iris.Flux.load(d)
+    try:
+        _check_blocks(m, blk_ref, 0, img_h, txt_h, 24, 40, 0.9)
+        v = m.forward(lat, ctx, 0.7)
+        assert rel_l2(v, v_ref) < TOL, rel_l2(v, v_ref)
+    finally:
+        m.close()
+
+
+def test_zimage_6b_width_forward(iris, tmp_path):
+    d = str(tmp_path)
+    cfg = dict(mg.ZIMAGE_6B, n_layers=1, n_refiner=1)
+    mg.make_zimage_model(d, cfg, seed=606, std=0.02, norm_mode="unit", keep=False)
+    r = np.random.default_rng(6)
+    lat = r.standard_normal((16, 30, 34)).astype(np.float32)   # 15 x 17 = 255 patches: 1 padding row
+    cap = r.standard_normal((45, 2560)).astype(np.float32)     # 45 caption rows: 19 padding rows
+    v_ref = ref_worker.zimage_forward(d, cfg, lat, cap, 0.4)
+    m = iris.ZImage.load(d)
+    try:
+        v = m.forward(lat, cap, 0.4)
+        assert v.shape == lat.shape
+        assert rel_l2(v, v_ref) < TOL, rel_l2(v, v_ref)
+    finally:
+        m.close()
