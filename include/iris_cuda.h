@@ -68,6 +68,14 @@ void *iris_cuda_stream(void);
 /* Number of kernels this library has enqueued since load (graph replays
  * count every kernel node).  Used by benchmarks to report launch counts. */
 uint64_t iris_cuda_kernel_launches(void);
+/* Self-test of the device-side failure path (no counterpart in the
+ * reference, whose GPU path has no bounded waits): launches the
+ * tensor-parallel adaLN kernel as a one-rank group whose partial-sum flag is
+ * never raised.  Its bounded wait expires after 2 s, the kernel records
+ * 0x301 in the device status word and returns, and the call returns
+ * IRIS_CUDA_ERR_TIMEOUT from iris_cuda_synchronize.  The status word stays
+ * set until iris_cuda_device_status(1) clears it; the library remains usable. */
+int iris_cuda_selftest_wait_timeout(void);
 
 /* ------------------------------------------------------------------ 2a. Flux.2 Klein */
 typedef struct iris_cuda_flux iris_cuda_flux_t;

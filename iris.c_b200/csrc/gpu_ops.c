@@ -507,9 +507,17 @@ static void wcache_clear(int f32src) {
     g_wc_n = k;
 }
 
-static wentry_t *wcache_find(const void *w, size_t n, int f32src) {
-    for (int i = g_wc_n - 1; i >= 0; i--)
-        if (g_wc[i].host == w && g_wc[i].n == n && g_wc[i].f32src == f32src) return &g_wc[i];
+/* An entry matches on (address, elements, source type) and, once it has been
+ * used as a GEMM operand, on its shape; a warmed-up entry (no shape yet) is
+ * adopted by the first shaped use.  Different shapes at one address (a host
+ * buffer reused for another weight) get separate entries. */
+static wentry_t *wcache_find(const void *w, size_t n, int f32src, int rows, int cols) {
+    for (int i = g_wc_n - 1; i >= 0; i--) {
+        const wentry_t *e = &g_wc[i];
+        if (e->host == w && e->n == n && e->f32src == f32src &&
+            (rows < 0 || e->rows == 0 || (e->rows == rows && e->cols == cols)))
+            return &g_wc[i];
+    }
     return NULL;
 }
 
@@ -559,12 +567,12 @@ static wentry_t *wcache_add(const void *w, size_t n, int f32src, size_t n_alloc)
 static wentry_t *weight_for(const void *W, int f32src, int rows, int cols) {
     const size_t n = (size_t)rows * cols;
     const int rows_pad = (rows + 127) / 128 * 128;
-    wentry_t *e = wcache_find(W, n, f32src);
+    wentry_t *e = wcache_find(W, n, f32src, rows, cols);
     if (!e) e = wcache_add(W, n, f32src, (size_t)rows_pad * cols);
     if (!e) return NULL;
     if (e->rows == rows && e->cols == cols) return e;
-    if (e->rows_pad != 0 || (size_t)rows_pad * cols != n) {
-        /* warmed up without a shape (or used with another shape): re-lay with padding */
+    if ((size_t)rows_pad * cols != n) {
+        /* warmed up without a shape and rows not a multiple of 128: re-lay with padding */
         uint16_t *d = (uint16_t *)iris_dmalloc((size_t)rows_pad * cols * 2);
         if (!d) return NULL;
         cudaMemsetAsync(d, 0, (size_t)rows_pad * cols * 2, g_rt.stream);
@@ -585,7 +593,7 @@ static wentry_t *weight_for(const void *W, int f32src, int rows, int cols) {
 
 void iris_metal_warmup_bf16(const uint16_t *w, size_t n) {
     if (!w || !n || iris_rt_ensure() != IRIS_CUDA_OK) return;
-    if (!wcache_find(w, n, 0)) wcache_add(w, n, 0, n);
+    if (!wcache_find(w, n, 0, -1, -1)) wcache_add(w, n, 0, n);
 }
 void iris_metal_warmup_bf16_buffer(const uint16_t *w, size_t n) { iris_metal_warmup_bf16(w, n); }
 void iris_metal_warmup_bf16_buffers_parallel(const uint16_t **ptrs, const size_t *counts, int n) {

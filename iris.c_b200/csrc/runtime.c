@@ -187,6 +187,49 @@ uint32_t iris_crc32(const char *s) {
     return ~c;
 }
 
+/* Self-test of the device-side failure path (no reference counterpart): one
+ * launch of the tensor-parallel adaLN kernel as a one-rank group whose
+ * partial-sum flag nothing ever raises.  Its bounded wait (IRIS_WAIT_NS,
+ * 2 s of %globaltimer) expires, the kernel records IRIS_DEV_ERR_TP_WAIT in
+ * the device status word and returns without touching its rows, and the
+ * call returns what iris_cuda_synchronize reports (IRIS_CUDA_ERR_TIMEOUT).
+ * The status word is left set for the caller to read and clear
+ * (iris_cuda_device_status); the context stays usable. */
+int iris_cuda_selftest_wait_timeout(void) {
+    int rc = iris_rt_ensure();
+    if (rc) return rc;
+    const int H = 512;
+    float *x = (float *)iris_dmalloc((size_t)2 * H * sizeof(float));
+    unsigned *flags = (unsigned *)iris_dmalloc(64 * sizeof(unsigned));
+    if (!x || !flags) {
+        iris_dfree(x);
+        iris_dfree(flags);
+        return IRIS_CUDA_ERR_OOM;
+    }
+    cudaMemsetAsync(x, 0, (size_t)2 * H * sizeof(float), g_rt.stream);
+    cudaMemsetAsync(flags, 0, 64 * sizeof(unsigned), g_rt.stream);
+    IrisAdalnTpArgs a;
+    memset(&a, 0, sizeof(a));
+    a.x = x;
+    a.recv = x + H;
+    a.rows = a.chunk = 1;
+    a.H = H;
+    a.has_part = 1;
+    a.part_index = 1; /* wait for one partial more than the base: never arrives */
+    a.eps = 1e-6f;
+    a.tp.size = 1;
+    a.tp.chunk = 1;
+    a.tp.flags[0] = flags;
+    a.status = g_rt.d_status;
+    iris_count_launch(1);
+    rc = iris_cuda_check(iris_launch_adaln_tp(&a, g_rt.stream), "self-test launch");
+    if (!rc) rc = iris_cuda_synchronize();
+    cudaStreamSynchronize(g_rt.stream);
+    iris_dfree(x);
+    iris_dfree(flags);
+    return rc;
+}
+
 /* Capability probes answered for the CUDA backend (iris_metal.h:28, :703, :743). */
 int iris_metal_available(void) { return iris_cuda_available(); }
 int iris_metal_shaders_available(void) { return iris_cuda_available(); }

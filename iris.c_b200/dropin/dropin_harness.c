@@ -11,6 +11,7 @@
  *   drive_sample_euler   iris_sample_euler                    (iris_sample.c:313)
  *   drive_zi_load        zi_transformer_load_safetensors      (iris_transformer_zimage.c:2164)
  *   drive_zi_forward     zi_transformer_forward               (:1696; GPU branch :1704)
+ *   drive_*_free         the model's free function, then iris_metal_reset (iris.c:642)
  */
 #include <stdint.h>
 #include <stdlib.h>
@@ -42,7 +43,14 @@ void *drive_flux_load(const char *model_dir, int mmap_mode) {
     return mmap_mode ? iris_transformer_load_safetensors_mmap(model_dir) : iris_transformer_load_safetensors(model_dir);
 }
 
-void drive_flux_free(void *tf) { iris_transformer_free((iris_transformer_t *)tf); }
+/* Freeing a model also resets the backend's caches, as the reference's host
+ * code does between models (iris_metal_reset, iris.c:642): the weight cache
+ * is keyed by host address, and the next model's weights can land at the
+ * addresses of this one's. */
+void drive_flux_free(void *tf) {
+    iris_transformer_free((iris_transformer_t *)tf);
+    iris_metal_reset();
+}
 
 /* out: [channels, h, w] */
 int drive_flux_forward(void *tf, const float *latent, int h, int w, const float *txt, int txt_seq, float t,
@@ -72,7 +80,10 @@ void *drive_zi_load(const char *model_dir, const int *cfg, float rope_theta) {
                                            rope_theta, cfg + 7);
 }
 
-void drive_zi_free(void *tf) { zi_transformer_free((zi_transformer_t *)tf); }
+void drive_zi_free(void *tf) {
+    zi_transformer_free((zi_transformer_t *)tf);
+    iris_metal_reset();
+}
 
 int drive_zi_forward(void *tf, const float *latent, int lh, int lw, float t, const float *cap, int cap_seq,
                      int in_ch, float *out) {

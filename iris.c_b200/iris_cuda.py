@@ -87,6 +87,7 @@ SIGNATURES = {
     "iris_cuda_synchronize": (C.c_int, []),
     "iris_cuda_stream": (C.c_void_p, []),
     "iris_cuda_kernel_launches": (C.c_uint64, []),
+    "iris_cuda_selftest_wait_timeout": (C.c_int, []),
     "iris_cuda_flux_load": (C.c_void_p, [C.c_char_p]),
     "iris_cuda_flux_random": (C.c_void_p, [C.POINTER(FluxConfig), C.c_uint64, C.c_float, C.c_int]),
     "iris_cuda_flux_load_tp": (C.c_void_p, [C.c_char_p, C.c_int, C.c_int]),

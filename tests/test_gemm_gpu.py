@@ -40,8 +40,32 @@ def test_linear_bf16_native(iris, m, k, n):
     iris.lib().iris_gpu_tensor_free(out)
     ref = x @ w.T  # f32 BLAS on bf16-valued operands
     err = rel_l2(y.reshape(m, n), ref)
+    # the weight cache is keyed by host address: forget this test's buffer
+    iris.lib().iris_metal_clear_bf16_cache_only()
     assert err < 4e-3, (m, k, n, err)
     assert iris.lib().iris_cuda_device_status(0) == 0
+
+
+@pytest.mark.parametrize("m,k,n", [(37, 64, 64), (300, 2560, 3840), (5, 128, 200)])
+def test_linear_f32_with_bias(iris, m, k, n):
+    """iris_gpu_linear (iris_metal.h:239): f32 tensors, f32 host weight and
+    bias; N not a multiple of 128 takes the padded-weight path (Z-Image's
+    final projection has N = 64).  Operands are rounded to bf16 on the way in,
+    so the reference product is taken on the rounded values."""
+    rng = np.random.default_rng(m + k + n)
+    x = rng.standard_normal((m, k)).astype(np.float32)
+    w = (rng.standard_normal((n, k)) * 0.05).astype(np.float32)
+    b = rng.standard_normal(n).astype(np.float32)
+    xd = Dev(x, bf16=False)
+    fp = C.POINTER(C.c_float)
+    out = iris.lib().iris_gpu_linear(xd.h, w.ctypes.data_as(fp), b.ctypes.data_as(fp), m, k, n)
+    assert out, iris.last_error()
+    y = np.zeros(m * n, np.float32)
+    iris.lib().iris_gpu_tensor_read(out, y.ctypes.data_as(fp))
+    iris.lib().iris_gpu_tensor_free(out)
+    iris.lib().iris_metal_clear_weight_cache_only()
+    ref = bf16_round(x) @ bf16_round(w).T + b
+    assert rel_l2(y.reshape(m, n), ref) < 2e-3
 
 
 def test_linear_rejects_unsupported_shape(iris):

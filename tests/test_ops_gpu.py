@@ -161,3 +161,104 @@ def test_masked_attention_key_tile_bound(iris, S, heads, group, mask, causal):
     ref = _masked_ref(q, k, v, heads, group, keep, causal, scale)
     err = float((o.float() - ref).norm() / ref.norm())
     assert err < 1e-2, err
+
+
+# ---------------------------------------------------------------- f32 surface
+def test_f32_norms_rope_and_gated_add(iris):
+    """The f32 ops the reference's Z-Image GPU block and the f32 fallbacks of
+    its Flux blocks call (iris_metal.h:353-398), with host-pointer weights and
+    tables, against the oracle.  f32 in and out: tolerance 1e-5 except where
+    noted."""
+    L = iris.lib()
+    seq, heads, H = 40, 3, 384
+    rng = np.random.default_rng(11)
+    x = (rng.standard_normal((seq, H)) * 2 + 0.3).astype(np.float32)
+    sh, sc, g, w = (rng.standard_normal(H).astype(np.float32) * 0.1 for _ in range(4))
+    X, O = Dev(x, bf16=False), Dev(n=seq * H, bf16=False)
+    L.iris_gpu_adaln_norm(O.h, X.h, sh.ctypes.data_as(_fp), sc.ctypes.data_as(_fp), seq, H, 1e-6)
+    assert rel_l2(O.read((seq, H)), fo.adaln(x, sh, sc)) < 1e-5
+    L.iris_gpu_rms_norm_f32(O.h, X.h, w.ctypes.data_as(_fp), seq, H, 1e-5)
+    ref = x / np.sqrt((x.astype(np.float64) ** 2).mean(-1, keepdims=True) + 1e-5) * w
+    assert rel_l2(O.read((seq, H)), ref) < 1e-5
+    # out += gate * proj, gate a host vector
+    L.iris_gpu_gated_add(O.h, g.ctypes.data_as(_fp), X.h, seq, H)
+    assert rel_l2(O.read((seq, H)), ref + g * x) < 1e-5
+    # per-head RMSNorm of q and k, then the unified (text | image) RoPE in f32
+    q = rng.standard_normal((seq, heads * 128)).astype(np.float32)
+    k = rng.standard_normal((seq, heads * 128)).astype(np.float32)
+    wq = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    wk = (1 + 0.1 * rng.standard_normal(128)).astype(np.float32)
+    Q, K = Dev(q, bf16=False), Dev(k, bf16=False)
+    L.iris_gpu_qk_rms_norm(Q.h, K.h, wq.ctypes.data_as(_fp), wk.ctypes.data_as(_fp), seq, heads, 128, 1e-6)
+    qn, kn = fo.head_rms_norm(q, wq, heads), fo.head_rms_norm(k, wk, heads)
+    assert rel_l2(Q.read((seq, heads * 128)), qn) < 1e-5
+    img_off = 8
+    tc, ts = (np.ascontiguousarray(a, np.float32) for a in fo.rope_txt(img_off, 2000.0))
+    ic, isn = (np.ascontiguousarray(a, np.float32) for a in fo.rope_img(4, 8, 2000.0))
+    L.iris_metal_rope_cache_begin()
+    L.iris_gpu_rope_unified(Q.h, K.h, tc.ctypes.data_as(_fp), ts.ctypes.data_as(_fp), ic.ctypes.data_as(_fp),
+                            isn.ctypes.data_as(_fp), seq, img_off, heads, 128, 32)
+    cs = np.concatenate([tc, ic]), np.concatenate([ts, isn])
+    assert rel_l2(Q.read((seq, heads * 128)), fo.apply_rope(qn, *cs, heads)) < 1e-5
+    assert rel_l2(K.read((seq, heads * 128)), fo.apply_rope(kn, *cs, heads)) < 1e-5
+    # one table for all rows, applied to q and k (Z-Image)
+    c2, s2 = (np.ascontiguousarray(a) for a in cs)
+    L.iris_metal_rope_cache_begin()
+    L.iris_gpu_rope_single_pair_f32(Q.h, K.h, c2.ctypes.data_as(_fp), s2.ctypes.data_as(_fp), seq, heads, 128)
+    q2 = fo.apply_rope(fo.apply_rope(qn, *cs, heads), *cs, heads)
+    assert rel_l2(Q.read((seq, heads * 128)), q2) < 1e-5
+    L.iris_metal_rope_cache_begin()
+
+
+def test_f32_attention_and_host_attention(iris):
+    """f32-interface attention (bf16 compute, so bf16 tolerance) on device
+    tensors and on host pointers in both layouts (iris_metal.h:402, :613, :649)."""
+    L = iris.lib()
+    sq, sk, heads = 70, 150, 2
+    rng = np.random.default_rng(5)
+    q = rng.standard_normal((sq, heads * 128)).astype(np.float32)
+    k = rng.standard_normal((sk, heads * 128)).astype(np.float32)
+    v = rng.standard_normal((sk, heads * 128)).astype(np.float32)
+    ref = fo.attention(q, k, v, heads)
+    Q, K, V = Dev(q, bf16=False), Dev(k, bf16=False), Dev(v, bf16=False)
+    O = Dev(n=sq * heads * 128, bf16=False)
+    scale = 1.0 / np.sqrt(128.0)
+    assert L.iris_gpu_attention_fused(O.h, Q.h, K.h, V.h, sq, sk, heads, 128, scale), iris.last_error()
+    assert rel_l2(O.read((sq, heads * 128)), ref) < 1e-2
+    out = np.zeros_like(q)
+    assert L.iris_metal_attention_fused(out.ctypes.data_as(_fp), q.ctypes.data_as(_fp), k.ctypes.data_as(_fp),
+                                        v.ctypes.data_as(_fp), sq, sk, heads, 128, scale)
+    assert rel_l2(out, ref) < 1e-2
+    # [heads, seq, 128] layout
+    qt, kt, vt = (np.ascontiguousarray(a.reshape(-1, heads, 128).transpose(1, 0, 2)) for a in (q, k, v))
+    ot = np.zeros_like(qt)
+    L.iris_metal_attention(ot.ctypes.data_as(_fp), qt.ctypes.data_as(_fp), kt.ctypes.data_as(_fp),
+                           vt.ctypes.data_as(_fp), None, heads, sq, sk, 128, scale)
+    assert rel_l2(ot.transpose(1, 0, 2).reshape(sq, heads * 128), ref) < 1e-2
+    # the SREF key bias is refused (the caller then takes its CPU path)
+    L.iris_metal_set_attention_bias(sk - 10, 0.5)
+    assert L.iris_gpu_attention_fused(O.h, Q.h, K.h, V.h, sq, sk, heads, 128, scale) == 0
+    assert "key bias" in iris.last_error()
+    L.iris_metal_set_attention_bias(0, 0.0)
+
+
+def test_tensor_data_host_view_round_trip(iris):
+    """iris_gpu_tensor_data (iris_metal.h:208): the host view shows the GPU
+    result; host writes reach the next op that uses the tensor."""
+    L = iris.lib()
+    n = 1000
+    a = np.arange(n, dtype=np.float32)
+    A, B, O = Dev(a, bf16=False), Dev(np.ones(n, np.float32), bf16=False), Dev(n=n, bf16=False)
+    L.iris_gpu_add_f32(O.h, A.h, B.h, n)
+    p = L.iris_gpu_tensor_data(O.h)
+    view = np.ctypeslib.as_array(p, shape=(n,))
+    np.testing.assert_array_equal(view, a + 1)
+    view[:10] = -5.0                      # host write through the view
+    L.iris_gpu_add_f32(O.h, O.h, B.h, n)  # the next op sees it
+    got = O.read()
+    np.testing.assert_array_equal(got[:10], -4.0)
+    np.testing.assert_array_equal(got[10:], a[10:] + 2)
+    # bf16 tensors get an f32 view
+    Hb = Dev(a)
+    vb = np.ctypeslib.as_array(L.iris_gpu_tensor_data(Hb.h), shape=(n,))
+    np.testing.assert_array_equal(vb, bf16_round(a))
