@@ -17,8 +17,10 @@ random-init bf16 weights N(0, 0.02), seeded N(0,1) latents and context.
             launches in one forward / their CUDA-event time
             (iris_cuda_flux_profile), against MEASURED_PEAKS.json.
 * cpu_baseline  the reference's own `make blas` build (oracle/_ref) on the
-            host cores: one double + one single block at the same shapes,
-            extrapolated to a full step (5 double + 20 single blocks).
+            host cores: one whole denoising step (a full forward of the
+            whole model) at the same shapes, nothing extrapolated.
+* --impl reference  the reference arm: that build sampling one whole image
+            (4 steps) in each weight mode (--no-mmap headline, mmap beside).
 
 Multi-GPU (torchrun, one process per GPU): independent seeds per rank
 ("replicas", no data-path collective); a barrier brackets the timed region
@@ -300,7 +302,7 @@ def write_ip_bundle(bundle_dir, mcfg, seed=91):
     return (rng.standard_normal((IP_SIGLIP_SEQ, S)) * rng.uniform(0.5, 3.0, S)).astype(np.float32)
 
 
-IP_SAMPLE = (", with a SigLIP IP-Adapter (64 tokens) attached to both blocks: the reference's hooks "
+IP_SAMPLE = (", with a SigLIP IP-Adapter (64 tokens) attached to every block: the reference's hooks "
              "(per-step k/v projection of the adapter tokens + SDPA, added after each block)")
 
 
@@ -488,87 +490,121 @@ def run_load_reference(args):
 
 
 # ----------------------------------------------------------------------------- CPU reference arm
-class RefSample:
-    """The reference's own BLAS build timed on one double + one single block of
-    Klein-4B at the 512x512 shapes; a full denoising step is extrapolated as
-    5 double + 20 single blocks (embedders and final layer are < 1% of it)."""
+class RefModel:
+    """The reference's own `make blas` build (oracle/_ref, OpenBLAS 0.3.15) with
+    the whole Klein-4B (random-init bf16 N(0, 0.02) safetensors, 7.7 GB, the
+    same seeded values in every run) loaded by its own loader, in either weight
+    mode: --no-mmap (f32 weights converted once at load) or mmap (the CLI
+    default, main.c:1250: bf16 block weights converted to f32 on every step).
+    Nothing is extrapolated: a step is a whole iris_transformer_forward (all 25
+    blocks, embedders, final layer), an image is iris_sample_euler's 4 steps."""
 
-    def __init__(self, lora: bool = False, ip: bool = False):
+    _files = None  # one model directory per process
+
+    def __init__(self, mmap: bool = False, lora: bool = False, ip: bool = False):
         from oracle import model_gen as mg
         from oracle.ref_lib import RefFlux, RefLib
-        self.tmp = tempfile.TemporaryDirectory()
-        cfg = dict(K4B, num_layers=1, num_single_layers=1)
-        mg.make_flux_model(self.tmp.name, cfg, WEIGHT_SEED, 0.02, "random")
+        if RefModel._files is None:
+            RefModel._files = tempfile.TemporaryDirectory()
+            mg.make_flux_model(RefModel._files.name, K4B, WEIGHT_SEED, 0.02, "random", keep=False)
+        d = RefModel._files.name
         self.ref = RefLib("blas")
         self.cores = len(os.sched_getaffinity(0))
         self.ref.set_threads(self.cores)
-        self.rf = RefFlux(self.ref, self.tmp.name)
-        if lora:  # the runtime hooks of lora_apply inside both blocks
-            path = os.path.join(self.tmp.name, "lora.safetensors")
-            write_bfl_lora(path, cfg, LORA_RANK, LORA_SEED)
+        t0 = time.perf_counter()
+        self.rf = RefFlux(self.ref, d, mmap=mmap)
+        self.load_s = time.perf_counter() - t0
+        self.mode = "mmap" if mmap else "no-mmap"
+        if lora:  # the runtime hooks of lora_apply after every adapted linear
+            path = os.path.join(d, "lora.safetensors")
+            if not os.path.exists(path):
+                write_bfl_lora(path, K4B, LORA_RANK, LORA_SEED)
             if not self.rf.set_lora(path, 1.0):
                 raise RuntimeError("reference lora_load failed")
-        if ip:  # the IP-Adapter hooks of both blocks
-            bdir = os.path.join(self.tmp.name, "ip")
-            feats = write_ip_bundle(bdir, cfg)
+        if ip:  # the IP-Adapter hooks after every block
+            bdir = os.path.join(d, "ip")
+            feats = write_ip_bundle(bdir, K4B)
             if self.rf.set_ip(bdir, feats, 1.0) != 0:
                 raise RuntimeError("reference IP-Adapter attach failed")
         r = np.random.default_rng(7)
-        H = self.rf.hidden
-        self.img = r.standard_normal((IMG_H * IMG_W, H)).astype(np.float32)
-        self.txt = r.standard_normal((TXT, H)).astype(np.float32)
-        self.t_emb = self.rf.temb(1.0)
-        self.mods = self.rf.mods(self.t_emb)
+        self.ctx = r.standard_normal((TXT, self.rf.text_dim)).astype(np.float32)
+        self.z0 = r.standard_normal((self.rf.channels, IMG_H, IMG_W)).astype(np.float32)
 
-    def step_seconds(self):
+    def step_seconds(self) -> float:
+        """one denoising step: a whole forward at the 512x512 shapes"""
         t0 = time.perf_counter()
-        self.rf.double_block(0, self.img, self.txt, self.mods["dbl_img"], self.mods["dbl_txt"], IMG_H, IMG_W)
-        t1 = time.perf_counter()
-        self.rf.single_block(0, np.concatenate([self.txt, self.img]), self.t_emb, IMG_H, IMG_W, TXT)
-        t2 = time.perf_counter()
-        return 5 * (t1 - t0) + 20 * (t2 - t1), t2 - t0
+        self.rf.forward(self.z0, self.ctx, 1.0)
+        return time.perf_counter() - t0
+
+    def image_seconds(self) -> float:
+        """one image: iris_sample_euler over the 4-step official schedule"""
+        from oracle.ref_lib import ref_official_schedule
+        sched = ref_official_schedule(self.ref, STEPS_PER_IMAGE, IMG_H * IMG_W)
+        t0 = time.perf_counter()
+        self.rf.sample_euler(self.z0, self.ctx, sched)
+        return time.perf_counter() - t0
 
     def close(self):
         self.rf.close()
-        self.tmp.cleanup()
 
-    SAMPLE = ("reference make-blas build (oracle/_ref, OpenBLAS 0.3.15): 1 double + 1 single Klein-4B block "
-              "at 1024 img + 512 txt tokens per sample, extrapolated to 5 double + 20 single blocks per step")
+    @staticmethod
+    def cleanup():
+        if RefModel._files is not None:
+            RefModel._files.cleanup()
+            RefModel._files = None
+
+    SAMPLE_IMAGE = ("reference make-blas build (oracle/_ref, OpenBLAS 0.3.15), whole Klein-4B, one 512x512 image "
+                    "= iris_sample_euler over 4 steps (every step a full iris_transformer_forward), {mode} weights; "
+                    "nothing extrapolated")
+    SAMPLE_STEP = ("reference make-blas build (oracle/_ref, OpenBLAS 0.3.15), whole Klein-4B, one 512x512 "
+                   "denoising step = one full iris_transformer_forward (25 blocks, embedders, final layer), "
+                   "{mode} weights; nothing extrapolated")
 
 
 def run_reference(args):
+    """The reference arm: the reference's own CPU build on this box's host
+    cores, whole images, both weight modes.  What ran is what is printed: one
+    image (4 denoising steps) per mode, no warm-up image (the model load
+    before it is timed separately); `steps` counts the denoising steps of the
+    headline (--no-mmap) image.  --steps / --warmup do not apply: a C2 image
+    takes about two minutes on 16 cores."""
     rank, world, _ = dist_env()
     if rank != 0:
         return 0
     lora = args.config == "lora"
     ipc = args.config == "ip"
-    rs = RefSample(lora=lora, ip=ipc)
-    for _ in range(args.warmup):
-        rs.step_seconds()
-    est, wall = [], 0.0
-    for _ in range(args.steps):
-        s, w = rs.step_seconds()
-        est.append(s)
-        wall += w
-    rs.close()
-    step_s = statistics.mean(est)
-    value = 1.0 / step_s
+    rm = RefModel(mmap=False, lora=lora, ip=ipc)
+    img_s = rm.image_seconds()
+    load_s, cores = rm.load_s, rm.cores
+    rm.close()
+    extra = {"no_mmap": {"image_s": img_s, "load_s": load_s}}
+    if not (lora or ipc):
+        mm = RefModel(mmap=True)
+        mm_img = mm.image_seconds()
+        extra["mmap"] = {"image_s": mm_img, "load_s": mm.load_s, "steps_per_s": STEPS_PER_IMAGE / mm_img}
+        mm.close()
+    RefModel.cleanup()
+    value = STEPS_PER_IMAGE / img_s
     line = {
         "impl": "reference", "metric": METRIC_LORA if lora else METRIC_IP if ipc else METRIC, "value": value,
         "unit": UNIT, "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": step_s * 1000.0 * STEPS_PER_IMAGE,
+        "steps": STEPS_PER_IMAGE, "warmup": 0, "ms_per_step": img_s * 1000.0 / STEPS_PER_IMAGE,
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "images_per_s": 1.0 / img_s,
         "config": bench_config(world, lora, ipc),
-        "cpu_baseline": {"value": value, "unit": UNIT, "cores": rs.cores, "kind": "reference",
-                         "sample": RefSample.SAMPLE + (LORA_SAMPLE if lora else "") + (IP_SAMPLE if ipc else ""),
-                         "measured_wall_s": wall},
+        "cpu_baseline": {"value": value, "unit": UNIT, "cores": cores, "kind": "reference",
+                         "sample": RefModel.SAMPLE_IMAGE.format(mode="--no-mmap")
+                         + (LORA_SAMPLE if lora else "") + (IP_SAMPLE if ipc else "")},
         "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "weight_modes": extra,
+        "note": "steps/warmup are what ran: one whole image (4 denoising steps) after the model load; "
+                "the driver's --steps/--warmup are not applied to this arm",
     }
     print(json.dumps(line), flush=True)
     return 0
 
 
-LORA_SAMPLE = (", with the rank-32 BFL adapter of both blocks applied by the reference's runtime hooks "
+LORA_SAMPLE = (", with the rank-32 BFL adapter of every block applied by the reference's runtime hooks "
                "(lora_apply after every adapted linear)")
 
 
@@ -777,13 +813,14 @@ def run_ours(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline and not args.blocks:
         try:
-            rs = RefSample(lora=lora, ip=ipc)
-            rs.step_seconds()
-            est = [rs.step_seconds()[0] for _ in range(2)]
-            cpu = {"value": 1.0 / statistics.mean(est), "unit": UNIT, "cores": rs.cores,
-                   "kind": "reference",
-                   "sample": RefSample.SAMPLE + (LORA_SAMPLE if lora else "") + (IP_SAMPLE if ipc else "")}
-            rs.close()
+            rm = RefModel(mmap=False, lora=lora, ip=ipc)
+            sec = rm.step_seconds()
+            cpu = {"value": 1.0 / sec, "unit": UNIT, "cores": rm.cores, "kind": "reference",
+                   "sample": RefModel.SAMPLE_STEP.format(mode="--no-mmap")
+                   + (LORA_SAMPLE if lora else "") + (IP_SAMPLE if ipc else ""),
+                   "step_s": sec, "load_s": rm.load_s}
+            rm.close()
+            RefModel.cleanup()
         except Exception as ex:  # the reference build is optional on a box without it
             cpu = {"value": None, "unit": UNIT, "cores": None, "kind": "reference",
                    "sample": f"unavailable: {type(ex).__name__}: {ex}"}

@@ -10,6 +10,7 @@
  *
  * Every entry point is a thin call into reference code:
  *   ref_flux_load            -> iris_transformer_load_safetensors  (iris_transformer_flux.c:5300)
+ *   ref_flux_load_mmap       -> iris_transformer_load_safetensors_mmap (:5550)
  *   ref_flux_forward         -> iris_transformer_forward           (iris_transformer_flux.c:3939)
  *   ref_flux_forward_refs    -> iris_transformer_forward_with_multi_refs (:4579)
  *   ref_flux_temb            -> get_timestep_embedding + time_embed_forward (:1349, :1366)
@@ -78,6 +79,12 @@ void ref_set_threads(int n) {
 
 void *ref_flux_load(const char *model_dir) {
     return iris_transformer_load_safetensors(model_dir);
+}
+
+/* the CLI's default weight mode (main.c:1250): bf16 block weights stay in the
+ * mapped file and are converted to f32 block by block on every step */
+void *ref_flux_load_mmap(const char *model_dir) {
+    return iris_transformer_load_safetensors_mmap(model_dir);
 }
 
 void ref_flux_free(void *tf) { iris_transformer_free((iris_transformer_t *)tf); }

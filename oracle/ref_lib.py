@@ -31,6 +31,8 @@ class RefLib:
         self.lib = L = C.CDLL(path)
         L.ref_flux_load.restype = C.c_void_p
         L.ref_flux_load.argtypes = [C.c_char_p]
+        L.ref_flux_load_mmap.restype = C.c_void_p
+        L.ref_flux_load_mmap.argtypes = [C.c_char_p]
         L.ref_flux_free.argtypes = [C.c_void_p]
         L.ref_flux_config.argtypes = [C.c_void_p, _fp]
         L.ref_flux_forward.argtypes = [C.c_void_p, _fp, C.c_int, C.c_int, _fp, C.c_int, C.c_float, _fp]
@@ -161,9 +163,10 @@ def psnr(a: np.ndarray, b: np.ndarray) -> float:
 class RefFlux:
     """A reference Flux transformer loaded from a model directory."""
 
-    def __init__(self, ref: RefLib, model_dir: str):
+    def __init__(self, ref: RefLib, model_dir: str, mmap: bool = False):
         self.ref = ref
-        self.h = ref.lib.ref_flux_load(model_dir.encode())
+        load = ref.lib.ref_flux_load_mmap if mmap else ref.lib.ref_flux_load
+        self.h = load(model_dir.encode())
         if not self.h:
             raise RuntimeError(f"reference failed to load {model_dir}")
         cfg = np.zeros(10, np.float32)
