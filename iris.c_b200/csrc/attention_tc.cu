@@ -60,12 +60,6 @@ constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: a new reference max mo
 // P <= 2^16, which bf16 P and the f32 O / l accumulators take as they are;
 // only larger sums send the row's warp to the exact max / rescale path.
 constexpr float FAST_SUM_LIMIT = 65536.0f;
-// Of every 8 exponentials, this many are evaluated on the FMA pipe (exp2_fma)
-// instead of the SFU.
-#ifndef IRIS_ATTN_EMU_PER8
-#define IRIS_ATTN_EMU_PER8 0
-#endif
-
 #define IRIS_DEV_ERR_ATTN_PRODUCER 0x201
 #define IRIS_DEV_ERR_ATTN_MMA 0x202
 #define IRIS_DEV_ERR_ATTN_SOFTMAX 0x203
@@ -98,21 +92,6 @@ struct AttnParams {
 };
 
 int* g_attn_status = nullptr;
-
-// 2^x for x <= 8 on the FMA/ALU pipes: x = n + f with n = rint(x) (1.5*2^23
-// rounding constant, so n also sits in the low mantissa bits of t) and
-// f in [-1/2, 1/2]; 2^f by a cubic fitted to minimise the relative error on
-// that interval (max 7.5e-5, far below bf16's 2^-9 rounding of P); 2^n is
-// added to the exponent field.  x is clamped to -125 so the result stays
-// normal (2^-125 instead of 0 for padding and masked keys: irrelevant next
-// to a row sum >= 1; padding keys also have V rows of zeros).
-__device__ __forceinline__ float exp2_fma(float x) {
-  x = fmaxf(x, -125.0f);
-  const float t = x + 12582912.0f;
-  const float f = x - (t - 12582912.0f);
-  float p = fmaf(fmaf(fmaf(0.05517145f, f, 0.24261114f), f, 0.69326103f), f, 0.99992806f);
-  return __uint_as_float(__float_as_uint(p) + (__float_as_uint(t) << 23));
-}
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
@@ -213,7 +192,7 @@ __device__ __forceinline__ void softmax_role(const AttnParams& p, uint32_t tmem,
     float sv[64];
     iris::tmem_ld64(s_addr + 64 * h, sv);
     float xm[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-    if (full && IRIS_ATTN_EMU_PER8 == 0) {
+    if (full) {
       const uint64_t sc2 = f32x2(p.scale_log2, p.scale_log2), nm2 = f32x2(nm, nm);
       uint64_t acc[4] = {0, 0, 0, 0};
 #pragma unroll
@@ -230,7 +209,7 @@ __device__ __forceinline__ void softmax_role(const AttnParams& p, uint32_t tmem,
         const int i = c * 8 + u;
         const float x = full ? fmaf(sv[i], p.scale_log2, nm) : logit(sv[i], kbase + 64 * h + i, false) + nm;
         xm[u & 3] = fmaxf(xm[u & 3], x);
-        e[u] = (u < IRIS_ATTN_EMU_PER8) ? exp2_fma(x) : iris::ex2_approx(x);
+        e[u] = iris::ex2_approx(x);
         rsum[u] += e[u];
       }
 #pragma unroll
@@ -282,7 +261,7 @@ __device__ __forceinline__ void softmax_role(const AttnParams& p, uint32_t tmem,
         continue;
       }
     }
-    if (kMasked && !full && IRIS_ATTN_EMU_PER8 == 0) {
+    if (kMasked && !full) {
       uint32_t m4 = 0x01010101u;  // this lane's 4 keys, one byte each (non-zero = kept)
       if (kMasked && p.kmask) {
         const int k4 = kbase + 4 * lane;
