@@ -77,12 +77,13 @@ def parse_args(argv=None):
                          "(same kernels and shapes, less memory); not a benchmark number")
     ap.add_argument("--profile-out", default=None, help="write the per-kernel CUDA-event profile (JSON)")
     ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "c5b", "vae512", "vae1024", "qwen3",
-                                                     "lora", "load", "ip"],
+                                                     "lora", "load", "ip", "attn"],
                     help="c2 (default) is the benchmark; the others measure the remaining benchmark configs "
                          "on one GPU (c1 K4B 64x64 single forward, c3 K4B 1024x1024 CFG 4.0, c4 K9B "
                          "1792x1792, c5 Z-Image 1024x1024, c5b K4B + 2 references, lora: c2 with a "
                          "rank-32 LoRA folded into the weights, load: Klein-4B safetensors -> resident, "
-                         "ip: c2 with a SigLIP IP-Adapter attached)")
+                         "ip: c2 with a SigLIP IP-Adapter attached, attn: the attention kernel alone at "
+                         "the configs' sequence lengths)")
     return ap.parse_args(argv)
 
 
@@ -1097,6 +1098,68 @@ def run_vae_reference(args):
     return 0
 
 
+ATTN_SHAPES = ((1536, 24, "c2 single block"), (4608, 24, "c3"), (4352, 30, "c5 main blocks"),
+               (13056, 32, "c4"))
+
+
+def run_attn(args):
+    """The tcgen05 attention kernel alone (iris_launch_attention, bf16 [S, heads*128]
+    Q/K/V of seeded N(0,1) values), device-timed per launch at the sequence
+    lengths of the benchmark configs; one line per run with every shape."""
+    import ctypes as C
+
+    import torch
+
+    import iris_cuda
+    rank, world, local = dist_env()
+    if rank != 0:
+        return 0
+    lib = iris_cuda.lib()
+    assert lib.iris_cuda_init(local) == 0, iris_cuda.last_error()
+    lib.iris_launch_attention.argtypes = [C.c_void_p, C.c_int, C.c_void_p, C.c_void_p, C.c_int, C.c_void_p,
+                                          C.c_int, C.c_int, C.c_int, C.c_int, C.c_float, C.c_void_p, C.c_void_p]
+    lib.iris_launch_attention.restype = C.c_int
+    dev = torch.device("cuda", local)
+    peaks, peak_src = load_peaks()
+    shapes = {}
+    clocks = ClockSampler(gpu_smi_id(local))
+    with clocks:
+        for S, heads, what in ATTN_SHAPES:
+            H = heads * 128
+            g = torch.Generator(device=dev).manual_seed(S)
+            q, k, v = (torch.randn(S, H, device=dev, generator=g).bfloat16() for _ in range(3))
+            o = torch.empty(S, H, device=dev, dtype=torch.bfloat16)
+            st = torch.cuda.current_stream(dev).cuda_stream
+
+            def run():
+                rc = lib.iris_launch_attention(q.data_ptr(), H, k.data_ptr(), v.data_ptr(), H, o.data_ptr(), H,
+                                               S, S, heads, 1.0 / 128 ** 0.5, None, st)
+                assert rc == 0
+            for _ in range(max(args.warmup, 3)):
+                run()
+            torch.cuda.synchronize()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(args.steps):
+                run()
+            e1.record()
+            torch.cuda.synchronize()
+            ms = e0.elapsed_time(e1) / args.steps
+            tf = 4.0 * S * S * H / (ms / 1000.0) / 1e12
+            shapes[f"S{S}_h{heads}"] = {"config": what, "us": ms * 1000.0, "tflops": tf,
+                                        "frac": tf / peaks["bf16_tflops"]}
+    c2 = shapes["S1536_h24"]
+    line = {"metric": "attention TFLOP/s (4 S^2 H per launch), c2 single-block shape", "value": c2["tflops"],
+            "unit": "TFLOP/s", "n_gpus": 1, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": c2["us"] / 1000.0, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "bf16", "data": "synthetic",
+            "config": {"workload": "tcgen05 attention kernel alone, head_dim 128, no mask", "l2":
+                       "Q/K/V of the largest shape exceed L2; the S=1536 inputs (28 MB) stay L2-resident"},
+            "shapes": shapes, "peak": peaks["bf16_tflops"], "peak_source": peak_src, "clocks": clocks.summary()}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 def run_vae(args):
     """Autoencoder decode (the step after the denoising loop): decodes/s of the
     whole job, one latent per rank per step (seed replicas at N > 1)."""
@@ -1370,6 +1433,12 @@ def main(argv=None):
         return run_qwen3_reference(args) if args.impl == "reference" else run_qwen3(args)
     if args.config.startswith("vae"):
         return run_vae_reference(args) if args.impl == "reference" else run_vae(args)
+    if args.config == "attn":
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the attn config times this library's kernel "
+                              "alone; the reference's attention runs inside its forward (c2 reference arm)"}))
+            return 0
+        return run_attn(args)
     if args.config == "load":
         return run_load_reference(args) if args.impl == "reference" else run_load(args)
     if args.impl == "reference":

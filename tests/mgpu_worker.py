@@ -8,6 +8,8 @@ usage: python -m torch.distributed.run ... mgpu_worker.py MODE OUT_DIR
             the reference golden
   tp        tensor-parallel shards (tp = world) vs the unsharded model and,
             at tp 2, the reference golden
+  tp_k9b    Klein-9B-width blocks and forward, sharded, vs the unsharded model
+            and the reference's CPU build
   nojoin    rank 0 creates a communicator that rank 1 never joins: the join
             must end in a timeout status, not a hang
 """
@@ -107,6 +109,45 @@ def run_tp(rank, world, out_dir, exchange):
     return res
 
 
+K9B_WIDTH = dict(mg.KLEIN_9B, num_layers=1, num_single_layers=1)
+
+
+def run_tp_k9b(rank, world, out_dir, exchange):
+    """Klein-9B width (hidden 4096, 32 heads, context 12288), one double and
+    one single block, sharded over the ranks: both blocks and a forward
+    against the unsharded model and (rank 0) the reference's own CPU build."""
+    group, r = iris_cuda.comm_init_group(exchange, rank, world, world)
+    d = os.path.join(out_dir, f"k9b_r{rank}")
+    mg.make_flux_model(d, K9B_WIDTH, seed=909, std=0.02, norm_mode="unit", keep=False)
+    rng = np.random.default_rng(4)
+    ph, pw, nt = 24, 40, 96
+    img_h = rng.standard_normal((ph * pw, 4096)).astype(np.float32)
+    txt_h = rng.standard_normal((nt, 4096)).astype(np.float32)
+    hid = np.concatenate([txt_h, img_h])
+    r5 = np.random.default_rng(5)
+    lat = r5.standard_normal((128, 14, 18)).astype(np.float32)
+    ctx = r5.standard_normal((77, 12288)).astype(np.float32)
+    full = iris_cuda.Flux.load(d)
+    b_full = [full.run_block(k, 0, hid, nt, ph, pw, 0.9) for k in (0, 1)]
+    v_full = full.forward(lat, ctx, 0.7)
+    full.close()
+    shard = iris_cuda.Flux.load(d, tp_rank=r, tp_size=world)
+    b = [shard.run_block(k, 0, hid, nt, ph, pw, 0.9) for k in (0, 1)]
+    v = shard.forward(lat, ctx, 0.7)
+    shard.close()
+    res = dict(tp=world, block0_vs_full=rel_l2(b[0], b_full[0]), block1_vs_full=rel_l2(b[1], b_full[1]),
+               v_vs_full=rel_l2(v, v_full))
+    if rank == 0:
+        import ref_worker
+        (ri, rt, rs), v_ref = ref_worker.flux(d, [("blocks", 0, img_h, txt_h, ph, pw, 0.9),
+                                                   ("forward", lat, ctx, 0.7)])
+        res.update(dbl_vs_reference=rel_l2(b[0], np.concatenate([rt, ri])),
+                   dbl_delta_vs_reference=rel_l2(b[0] - hid, np.concatenate([rt, ri]) - hid),
+                   sgl_vs_reference=rel_l2(b[1], rs), sgl_delta_vs_reference=rel_l2(b[1] - hid, rs - hid),
+                   v_vs_reference=rel_l2(v, v_ref))
+    return res
+
+
 def run_nojoin(rank, world, out_dir, exchange):
     if rank == 0:
         uid = iris_cuda.comm_unique_id()
@@ -134,7 +175,7 @@ def main():
         dist.all_gather_object(lst, obj)
         return lst
 
-    fn = dict(cfg_pair=run_cfg_pair, tp=run_tp, nojoin=run_nojoin)[mode]
+    fn = dict(cfg_pair=run_cfg_pair, tp=run_tp, tp_k9b=run_tp_k9b, nojoin=run_nojoin)[mode]
     res = fn(rank, world, out_dir, exchange)
     with open(os.path.join(out_dir, f"rank{rank}.json"), "w") as f:
         json.dump(res, f)

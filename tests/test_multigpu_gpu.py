@@ -10,6 +10,7 @@
   but a changed f32 residual flips bf16 roundings of the next GEMM inputs, so
   the difference is of the size of the one-GPU path's own bf16 error (the
   worker records both).
+* Klein-9B width at tp 2 against the reference's own CPU build.
 * A rank that never joins the communicator: the join returns a timeout
   status after IRIS_COMM_TIMEOUT_MS (host-side failure; no GPU kernel waits).
 Each run is bounded by `timeout`; NVLS is off in the failure test.
@@ -82,6 +83,20 @@ def test_tensor_parallel_matches_unsharded_and_reference(tmp_path, tp):
     # the shards split the block weights evenly
     wb = [x["tp_cfg"]["weight_bytes"] for x in res]
     assert max(wb) == min(wb)
+
+
+@needs2
+def test_tensor_parallel_klein9b_width(tmp_path):
+    """tp 2 at the C4 model's width (hidden 4096, 32 heads, context 12288):
+    blocks and velocity within 1e-2 (deltas 2e-2) of the reference's CPU
+    build and of the unsharded model."""
+    res = run_workers("tp_k9b", 2, tmp_path, limit=900)
+    print(json.dumps(res))
+    for x in res:
+        for k, v in x.items():
+            if k.endswith(("_vs_full", "_vs_reference")):
+                assert v < (2e-2 if "delta" in k else 1e-2), (k, v)
+    assert "v_vs_reference" in res[0]
 
 
 @needs2
