@@ -77,13 +77,14 @@ def parse_args(argv=None):
                          "(same kernels and shapes, less memory); not a benchmark number")
     ap.add_argument("--profile-out", default=None, help="write the per-kernel CUDA-event profile (JSON)")
     ap.add_argument("--config", default="c2", choices=["c1", "c2", "c3", "c4", "c5", "c5b", "vae512", "vae1024", "qwen3",
-                                                     "lora", "load", "ip", "attn"],
+                                                     "lora", "load", "ip", "attn", "dropin"],
                     help="c2 (default) is the benchmark; the others measure the remaining benchmark configs "
                          "on one GPU (c1 K4B 64x64 single forward, c3 K4B 1024x1024 CFG 4.0, c4 K9B "
                          "1792x1792, c5 Z-Image 1024x1024, c5b K4B + 2 references, lora: c2 with a "
                          "rank-32 LoRA folded into the weights, load: Klein-4B safetensors -> resident, "
                          "ip: c2 with a SigLIP IP-Adapter attached, attn: the attention kernel alone at "
-                         "the configs' sequence lengths)")
+                         "the configs' sequence lengths, dropin: c2 run by the reference's own unmodified "
+                         "transformer code on this library)")
     return ap.parse_args(argv)
 
 
@@ -1098,6 +1099,79 @@ def run_vae_reference(args):
     return 0
 
 
+def run_c2_reference_note():
+    print(json.dumps({"impl": "reference", "unavailable": "the dropin config is the reference's own code already; "
+                      "its CPU arm is the c2 reference arm"}))
+    return 0
+
+
+DROPIN_LIB = os.path.join(ROOT, "iris.c_b200", "dropin", "_build", "libiris_refdrive.so")
+METRIC_DROPIN = "denoise steps/s (Klein-4B 512x512, 4-step Euler; the reference's own transformer code)"
+
+
+def run_dropin(args):
+    """The reference's unmodified transformer and sampler (iris.c_b200/dropin: built
+    with -DUSE_METAL against this library) on the C2 workload: its loader keeps
+    bf16 weights, iris_sample_euler runs its bf16 GPU forward, whose every op
+    is queued on this library.  Timed through the reference's host API (wall
+    clock, each image synchronous), as its own CLI would run."""
+    import ctypes as C
+
+    import iris_cuda
+    rank, world, local = dist_env()
+    if rank != 0:
+        return 0
+    if not os.path.exists(DROPIN_LIB):
+        print(json.dumps({"metric": METRIC_DROPIN, "unavailable": "drop-in build missing"}))
+        return 0
+    lib = iris_cuda.lib()
+    assert lib.iris_cuda_init(local) == 0, iris_cuda.last_error()
+    fp = C.POINTER(C.c_float)
+    D = C.CDLL(DROPIN_LIB, mode=os.RTLD_NOW)
+    D.drive_flux_load.restype = C.c_void_p
+    D.drive_flux_load.argtypes = [C.c_char_p, C.c_int]
+    D.drive_flux_free.argtypes = [C.c_void_p]
+    D.drive_sample_euler.argtypes = [C.c_void_p, fp, C.c_int, C.c_int, C.c_int, fp, C.c_int, fp, C.c_int]
+    assert D.drive_init() == 1
+    tmp = tempfile.TemporaryDirectory(dir=os.environ.get("IRIS_BENCH_TMP"))
+    write_klein_files(tmp.name, K4B)
+    t0 = time.perf_counter()
+    tf = D.drive_flux_load(tmp.name.encode(), 0)
+    load_s = time.perf_counter() - t0
+    assert tf
+    r = np.random.default_rng(7)
+    ctx = r.standard_normal((TXT, K4B["joint_attention_dim"])).astype(np.float32)
+    sched = np.ascontiguousarray(iris_cuda.official_schedule(STEPS_PER_IMAGE, IMG_H * IMG_W), np.float32)
+    z0 = r.standard_normal((128, IMG_H, IMG_W)).astype(np.float32)
+
+    def image():
+        z = z0.copy()
+        rc = D.drive_sample_euler(tf, z.ctypes.data_as(fp), 128, IMG_H, IMG_W, ctx.ctypes.data_as(fp), TXT,
+                                  sched.ctypes.data_as(fp), STEPS_PER_IMAGE)
+        assert rc == 0
+    for _ in range(args.warmup):
+        image()
+    f0, k0 = lib.iris_gpu_op_failures(), lib.iris_cuda_kernel_launches()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        image()
+    wall = time.perf_counter() - t0
+    failures, launches = lib.iris_gpu_op_failures() - f0, lib.iris_cuda_kernel_launches() - k0
+    D.drive_flux_free(tf)
+    tmp.cleanup()
+    value = args.steps * STEPS_PER_IMAGE / wall
+    line = {"metric": METRIC_DROPIN, "value": value, "unit": UNIT, "n_gpus": 1, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": wall * 1000.0 / args.steps, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic",
+            "config": dict(bench_config(1), path="iris_sample_euler -> iris_transformer_forward_bf16 of the "
+                           "reference (unmodified, -DUSE_METAL) -> iris_gpu_* ops of this library"),
+            "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": None, "d2h_bytes_per_step": None,
+                    "note": "the reference's host API, wall clock; value and e2e are the same measurement"},
+            "gpu_launches": int(launches), "op_failures": int(failures), "load_s": load_s}
+    print(json.dumps(line), flush=True)
+    return 0
+
+
 ATTN_SHAPES = ((1536, 24, "c2 single block"), (4608, 24, "c3"), (4352, 30, "c5 main blocks"),
                (13056, 32, "c4"))
 
@@ -1433,6 +1507,8 @@ def main(argv=None):
         return run_qwen3_reference(args) if args.impl == "reference" else run_qwen3(args)
     if args.config.startswith("vae"):
         return run_vae_reference(args) if args.impl == "reference" else run_vae(args)
+    if args.config == "dropin":
+        return run_c2_reference_note() if args.impl == "reference" else run_dropin(args)
     if args.config == "attn":
         if args.impl == "reference":
             print(json.dumps({"impl": "reference", "unavailable": "the attn config times this library's kernel "

@@ -501,6 +501,11 @@ static int plan_ensure(iris_cuda_flux_t *tf, int s_txt, int img_h, int img_w,
     if (S < 512) {  /* few GEMM tiles: room for 16 K splits of the widest linear */
         P->ws_bytes = (size_t)16 * S * (size_t)(H + tf->F > T ? H + tf->F : T) * 4;
         PA(P->ws, P->ws_bytes);
+    } else {
+        /* the text embedder alone has few tiles (s_txt rows, K = the text width):
+           room for 4 K splits of it; the other linears fill the GPU as they are */
+        P->ws_bytes = (size_t)4 * s_txt * H * 4;
+        PA(P->ws, P->ws_bytes);
     }
 #undef PA
     if (iris_mk_tmap(&P->tm_xmod, P->xmod, S, H, H, 128) ||

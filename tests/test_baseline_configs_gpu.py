@@ -91,14 +91,19 @@ def test_c1_klein4b_forward_and_c2_blocks(iris, tmp_path):
 
 
 def test_c2_blocks_klein4b_sharp_attention(iris, tmp_path):
+    """C2-shape blocks with a far-from-uniform softmax, and a whole forward at the
+    C2 shape (512 text rows: the text embedder runs split over K)."""
     d = str(tmp_path)
     cfg = dict(mg.KLEIN_4B, num_layers=1, num_single_layers=1)
     mg.make_flux_model(d, cfg, seed=77, std=0.02, norm_mode="unit", keep=False)
     img_h, txt_h = _hidden(3, 32 * 32, 512, 3072)
-    (blk_ref,) = ref_worker.flux(d, [("blocks", 0, img_h, txt_h, 32, 32, 0.6)])
+    lat, ctx = _inputs(8, 128, 32, 32, 512, 7680)
+    blk_ref, v_ref = ref_worker.flux(d, [("blocks", 0, img_h, txt_h, 32, 32, 0.6), ("forward", lat, ctx, 0.6)])
     m = iris.Flux.load(d)
     try:
         _check_blocks(m, blk_ref, 0, img_h, txt_h, 32, 32, 0.6)
+        v = m.forward(lat, ctx, 0.6)
+        assert rel_l2(v, v_ref) < TOL, rel_l2(v, v_ref)
     finally:
         m.close()
 
