@@ -419,6 +419,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
   const int col0 = head * HD;
   const int kvcol0 = (head / p.kv_group) * HD;
 
+  iris::grid_dep_wait();  // the key mask below may come from the previous kernel
   if (warp == 2) {
     const int nkv = live_key_tiles<kMasked>(p, q0, min(p.sq, q0 + (has1 ? 2 : 1) * BQ) - 1, lane);
     if (lane == 0) bars->nkv = nkv;
@@ -450,6 +451,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
   __syncthreads();
   iris::tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
+  iris::grid_dep_launch();  // after this CTA's TMEM allocation
   const int n = bars->nkv;
 
   if (warp == 0 && lane == 0) {
@@ -638,6 +640,7 @@ attn_pair_kernel(const __grid_constant__ AttnParams p) {
   const int col0 = head * HD;
   const int kvcol0 = (head / p.kv_group) * HD;
 
+  iris::grid_dep_wait();  // the key mask below may come from the previous kernel
   if (warp == 2) {  // both CTAs of the pair: the same rows, the same count
     const int r0 = (blockIdx.x >> 1) * (4 * BQ);
     const int nkv = live_key_tiles<kMasked>(p, r0, min(p.sq, r0 + 4 * BQ) - 1, lane);
@@ -671,6 +674,7 @@ attn_pair_kernel(const __grid_constant__ AttnParams p) {
   iris::cluster_sync();  // both CTAs' barriers exist before any remote arrive
   iris::tc_fence_after();
   const uint32_t tmem = bars->tmem_base;
+  iris::grid_dep_launch();  // after this CTA's TMEM allocation
   const int n = bars->nkv;
 
   if (warp == 0 && lane == 0) {
@@ -877,14 +881,12 @@ extern "C" cudaError_t iris_launch_attention_gqa(const void* q, int ldq, const v
   if (single) {
     const int rows = one_tile ? BQ : 2 * BQ;
     dim3 grid((sq + rows - 1) / rows, heads);
-    if (masked) attn_tc_kernel<true><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(p);
-    else attn_tc_kernel<false><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(p);
-  } else {
-    dim3 grid(2 * ((sq + 4 * BQ - 1) / (4 * BQ)), heads);
-    if (masked) attn_pair_kernel<true><<<grid, NUM_THREADS, P_SMEM_BYTES, stream>>>(p);
-    else attn_pair_kernel<false><<<grid, NUM_THREADS, P_SMEM_BYTES, stream>>>(p);
+    return iris::launch_overlapped(masked ? attn_tc_kernel<true> : attn_tc_kernel<false>, grid, dim3(NUM_THREADS),
+                                   SMEM_BYTES, stream, p);
   }
-  return cudaGetLastError();
+  dim3 grid(2 * ((sq + 4 * BQ - 1) / (4 * BQ)), heads);
+  return iris::launch_overlapped(masked ? attn_pair_kernel<true> : attn_pair_kernel<false>, grid, dim3(NUM_THREADS),
+                                 P_SMEM_BYTES, stream, p);
 }
 
 // Attention entry point (the tcgen05 kernels above).

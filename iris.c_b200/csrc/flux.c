@@ -560,6 +560,7 @@ static void gp_init(IrisGemmParams *p, const flux_plan_t *P, const CUtensorMap *
     p->bn = 256;
     p->eps = 1e-6f;
     p->status = g_rt.d_status;
+    p->b_static = 1;  /* every B of the forward is a resident weight */
 }
 
 static void gp_group(IrisGemmParams *p, int g, const CUtensorMap *tb, int row0, int rows) {

@@ -66,7 +66,10 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-__device__ __forceinline__ float silu_f(float x) { return x / (1.0f + __expf(-x)); }
+// x * sigmoid(x) with the fast divide (a reciprocal and a multiply, within 2
+// ulp: far below the bf16 rounding of the result).  For x below about -88,
+// 1 + e^-x is infinite or beyond 2^126 and the quotient is 0, the limit.
+__device__ __forceinline__ float silu_f(float x) { return __fdividef(x, 1.0f + __expf(-x)); }
 
 // Store 32 f32 values (cols j0..j0+31 of a chunk) as bf16 to dst (16B aligned).
 __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float* v) {
@@ -84,7 +87,10 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float* v
 
 // Epilogue for one 128-column chunk that belongs to the Q/K/V region.
 // TMEM loads are warp-collective and always executed by all 32 lanes; only
-// the global-memory traffic is predicated on `valid`.
+// the global-memory traffic is predicated on `valid`.  The RoPE factors of a
+// 32-column block (this row's own, an L2 access) are requested before the
+// block's TMEM load, so their latency overlaps it; the norm weights are the
+// same for every row and come from L1.
 __device__ __forceinline__ void epi_qkv_chunk(const IrisGemmParams& p, uint32_t taddr, int g,
                                               int row, bool valid, int col0) {
   int which = col0 / p.H;
@@ -107,8 +113,22 @@ __device__ __forceinline__ void epi_qkv_chunk(const IrisGemmParams& p, uint32_t 
     }
     r = rsqrtf(ss * (1.0f / 128.0f) + p.eps);
   }
+  const bool kt = which == 1 && p.rope_cos_k;  // K-side tables (reference-row band scaling)
+  const float* rc = p.rope_cos ? (kt ? p.rope_cos_k : p.rope_cos) + (size_t)row * 64 : nullptr;
+  const float* rs = p.rope_cos ? (kt ? p.rope_sin_k : p.rope_sin) + (size_t)row * 64 : nullptr;
+  const bool rope = which < 2 && rc != nullptr && valid;
 #pragma unroll 1
   for (int j = 0; j < 4; j++) {
+    float4 c[4], sn[4];
+    if (rope) {
+      const float4* cp = reinterpret_cast<const float4*>(rc + 16 * j);
+      const float4* sp = reinterpret_cast<const float4*>(rs + 16 * j);
+#pragma unroll
+      for (int q4 = 0; q4 < 4; q4++) {
+        c[q4] = __ldg(cp + q4);
+        sn[q4] = __ldg(sp + q4);
+      }
+    }
     float v[32];
     iris::tmem_ld32(taddr + 32 * j, v);
     if (!valid) continue;
@@ -116,26 +136,22 @@ __device__ __forceinline__ void epi_qkv_chunk(const IrisGemmParams& p, uint32_t 
       const float4* w4 = reinterpret_cast<const float4*>(nw + 32 * j);
 #pragma unroll
       for (int e = 0; e < 8; e++) {
-        float4 w = __ldg(w4 + e);
+        const float4 w = __ldg(w4 + e);
         v[4 * e + 0] = v[4 * e + 0] * r * w.x;
         v[4 * e + 1] = v[4 * e + 1] * r * w.y;
         v[4 * e + 2] = v[4 * e + 2] * r * w.z;
         v[4 * e + 3] = v[4 * e + 3] * r * w.w;
       }
-      if (p.rope_cos) {
-        const bool kt = which == 1 && p.rope_cos_k;  // K-side tables (reference-row band scaling)
-        const float4* cp = reinterpret_cast<const float4*>((kt ? p.rope_cos_k : p.rope_cos) + (size_t)row * 64 + 16 * j);
-        const float4* sp = reinterpret_cast<const float4*>((kt ? p.rope_sin_k : p.rope_sin) + (size_t)row * 64 + 16 * j);
+      if (rope) {
 #pragma unroll
         for (int q4 = 0; q4 < 4; q4++) {
-          float4 c = __ldg(cp + q4), s = __ldg(sp + q4);
-          float cc[4] = {c.x, c.y, c.z, c.w}, sn[4] = {s.x, s.y, s.z, s.w};
+          float cc[4] = {c[q4].x, c[q4].y, c[q4].z, c[q4].w}, ss4[4] = {sn[q4].x, sn[q4].y, sn[q4].z, sn[q4].w};
 #pragma unroll
           for (int e = 0; e < 4; e++) {
             int jj = 2 * (4 * q4 + e);
             float x0 = v[jj], x1 = v[jj + 1];
-            v[jj] = x0 * cc[e] - x1 * sn[e];
-            v[jj + 1] = x1 * cc[e] + x0 * sn[e];
+            v[jj] = x0 * cc[e] - x1 * ss4[e];
+            v[jj + 1] = x1 * cc[e] + x0 * ss4[e];
           }
         }
       }
@@ -153,8 +169,7 @@ __device__ __forceinline__ void epi_swiglu_tile(const IrisGemmParams& p, uint32_
 #pragma unroll 1
   for (int j = j0; j < j1; j++) {
     float gv[32], uv[32];
-    iris::tmem_ld32(taddr + 32 * j, gv);
-    iris::tmem_ld32(taddr + 128 + 32 * j, uv);
+    iris::tmem_ld32x2(taddr + 32 * j, taddr + 128 + 32 * j, gv, uv);
 #pragma unroll
     for (int e = 0; e < 32; e++) gv[e] = silu_f(gv[e]) * uv[e];
     if (valid) store_bf16x32(dst + 32 * j, gv);
@@ -458,6 +473,24 @@ gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
   __syncthreads();
   iris::tc_fence_after();
   const uint32_t tmem_base = bars->tmem_base;
+  // The prologue above overlapped the previous kernel's tail; so do the
+  // weight loads of the first stages when B is a resident weight.
+  const int pre = (p.b_static && p.tp.size <= 1 && blockIdx.x < total && !kFold)
+                      ? min(STAGES, (blockIdx.x % nsplit + 1) * num_kb / nsplit - (blockIdx.x % nsplit) * num_kb / nsplit)
+                      : 0;
+  if (warp == 0 && lane == 0 && pre > 0) {
+    int g, ml, n0;
+    tile_coords(p, blockIdx.x / nsplit, mt0, mtot, g, ml, n0);
+    const int kb0 = (blockIdx.x % nsplit) * num_kb / nsplit;
+    for (int s = 0; s < pre; s++) {
+      iris::mbar_arrive_expect_tx(&bars->full[s], A_BYTES + b_bytes);
+      for (int h = 0; h < p.bn / 128; h++)
+        iris::tma_load_2d(smem + s * STAGE_BYTES + A_BYTES + h * (128 * BK * 2), &p.tmap_b[g], &bars->full[s],
+                          (kb0 + s) * BK, n0 + 128 * h);
+    }
+  }
+  iris::grid_dep_wait();
+  if (!kFold) iris::grid_dep_launch();  // a fold rewrites weights: nothing may start early after it
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------ TMA producer
@@ -482,9 +515,10 @@ gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
         }
         uint8_t* sa = smem + stage * STAGE_BYTES;
         uint8_t* sb = sa + A_BYTES;
-        iris::mbar_arrive_expect_tx(&bars->full[stage], A_BYTES + b_bytes);
+        const bool b_done = issued < pre;  // the first unit's early weight stages
+        if (!b_done) iris::mbar_arrive_expect_tx(&bars->full[stage], A_BYTES + b_bytes);
         iris::tma_load_2d(sa, &p.tmap_a, &bars->full[stage], kb * BK, arow);
-        for (int h = 0; h < p.bn / 128; h++)  // weight tensor maps have 128-row boxes
+        for (int h = 0; h < p.bn / 128 && !b_done; h++)  // weight tensor maps have 128-row boxes
           iris::tma_load_2d(sb + h * (128 * BK * 2), &p.tmap_b[g], &bars->full[stage], kb * BK, n0 + 128 * h);
         issued++;
         if (++stage == STAGES) { stage = 0; phase ^= 1; }
@@ -758,12 +792,26 @@ gemm_tc2_kernel(const __grid_constant__ IrisGemmParams p) {
   iris::cluster_sync();  // both CTAs' barriers are initialised before any remote arrive
   iris::tc_fence_after();
   const uint32_t tmem_base = bars->tmem_base;
+  // The prologue above overlapped the previous kernel's tail; so do the
+  // weight loads of the first stages when B is a resident weight.
+  const int pre = (p.b_static && p.tp.size <= 1 && pair < total && !kFold) ? min(kStages, num_kb) : 0;
+  if (warp == 0 && lane == 0 && pre > 0) {
+    int g, ml, n0;
+    tile_coords(p, pair, mt0, mtot, g, ml, n0);
+    for (int s = 0; s < pre; s++) {
+      const uint32_t full_c = iris::mapa_shared(&bars->full[s], 0);
+      iris::mbar_arrive_expect_tx_cluster(full_c, STAGE2_BYTES);
+      iris::tma_load_2d_pair(smem + s * STAGE2_BYTES + A_BYTES, &p.tmap_b[g], full_c, s * BK, n0 + 128 * (int)rank);
+    }
+  }
+  iris::grid_dep_wait();
+  if (!kFold) iris::grid_dep_launch();  // a fold rewrites weights: nothing may start early after it
 
   if (warp == 0 && lane == 0) {
     // ------------------------------------------------ TMA producer (both CTAs)
     int stage = 0;
     uint32_t phase = 0;
-    bool ok = true, issued_any = false;
+    bool ok = true, issued_any = pre > 0;
     if (p.tp.size > 1 && p.tp.wait_x) {  // A rows written by peer GPUs: wait for all of them
       ok = iris::tp_wait(p.tp, IRIS_TP_X, IRIS_TP_BASE_X, p.tp.wait_x, p.status);
       if (!ok) *abort_flag = 1;
@@ -782,9 +830,10 @@ gemm_tc2_kernel(const __grid_constant__ IrisGemmParams p) {
         uint8_t* sa = smem + stage * STAGE2_BYTES;
         uint8_t* sb = sa + A_BYTES;
         const uint32_t full_c = iris::mapa_shared(&bars->full[stage], 0);
-        iris::mbar_arrive_expect_tx_cluster(full_c, STAGE2_BYTES);
+        const bool b_done = t == pair && kb < pre;  // the first tile's early weight stages
+        if (!b_done) iris::mbar_arrive_expect_tx_cluster(full_c, STAGE2_BYTES);
         iris::tma_load_2d_pair(sa, &p.tmap_a, full_c, kb * BK, arow);
-        iris::tma_load_2d_pair(sb, &p.tmap_b[g], full_c, kb * BK, brow);
+        if (!b_done) iris::tma_load_2d_pair(sb, &p.tmap_b[g], full_c, kb * BK, brow);
         issued_any = true;
         if (++stage == kStages) { stage = 0; phase ^= 1; }
       }
@@ -900,6 +949,8 @@ __global__ void splitk_reduce_kernel(const __grid_constant__ IrisGemmParams p, i
   if (local < 0 || local >= p.rows[g]) return;
   const int c = (blockIdx.x * blockDim.x + threadIdx.x) * 4;
   if (c >= p.N) return;
+  iris::grid_dep_wait();
+  iris::grid_dep_launch();
   const size_t slice = (size_t)span * p.N;
   const float* w = p.ws + (size_t)row * p.N + c;
   float4 acc = *reinterpret_cast<const float4*>(w);
@@ -1015,6 +1066,9 @@ extern "C" cudaError_t iris_launch_gemm_ex(const IrisGemmParams* p, int num_sms,
   if (p->K % BK != 0 || p->N % 128 != 0) return cudaErrorInvalidValue;
   const int rows = p->rows[0] + (p->ngroups > 1 ? p->rows[1] : 0);
   const bool linear = p->mode == IRIS_EPI_BF16 || p->mode == IRIS_EPI_F32 || p->mode == IRIS_EPI_RESID_GATE;
+  // A tensor-parallel launch waits on peer GPUs: it starts only after the
+  // previous kernel has finished, as an ordinary launch does.
+  const bool overlap = p->tp.size <= 1;
   if (p->bn == 256 && rows >= 512 && g_max_pairs > 0) {
     int mt = (p->rows[0] + BM2 - 1) / BM2 + (p->ngroups > 1 ? (p->rows[1] + BM2 - 1) / BM2 : 0);
     long total = (long)mt * ((p->N + 255) / 256);
@@ -1026,6 +1080,9 @@ extern "C" cudaError_t iris_launch_gemm_ex(const IrisGemmParams* p, int num_sms,
       long pairs = total < cap ? total : cap;
       if (p->mode == IRIS_EPI_LORA_FOLD)
         gemm_tc2_kernel<true><<<(int)(2 * pairs), NUM_THREADS2, FOLD_SMEM2_BYTES, stream>>>(*p);
+      else if (overlap)
+        return iris::launch_overlapped(gemm_tc2_kernel<false>, dim3((unsigned)(2 * pairs)), dim3(NUM_THREADS2),
+                                       SMEM2_BYTES, stream, *p);
       else
         gemm_tc2_kernel<false><<<(int)(2 * pairs), NUM_THREADS2, SMEM2_BYTES, stream>>>(*p);
       return cudaGetLastError();
@@ -1049,12 +1106,19 @@ extern "C" cudaError_t iris_launch_gemm_ex(const IrisGemmParams* p, int num_sms,
   }
   const long total = tiles * q.splitk;
   int grid = (int)(total < num_sms ? total : num_sms);
-  if (q.mode == IRIS_EPI_LORA_FOLD) gemm_tc_kernel<true><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(q);
-  else gemm_tc_kernel<false><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(q);
-  cudaError_t e = cudaGetLastError();
+  cudaError_t e;
+  if (q.mode == IRIS_EPI_LORA_FOLD) {
+    gemm_tc_kernel<true><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(q);
+    e = cudaGetLastError();
+  } else if (overlap) {
+    e = iris::launch_overlapped(gemm_tc_kernel<false>, dim3(grid), dim3(NUM_THREADS), SMEM_BYTES, stream, q);
+  } else {
+    gemm_tc_kernel<false><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(q);
+    e = cudaGetLastError();
+  }
   if (e != cudaSuccess || q.splitk == 1) return e;
   if (launches) *launches = 2;
-  splitk_reduce_kernel<<<dim3((p->N / 4 + 255) / 256, span), 256, 0, stream>>>(q, span);
-  return cudaGetLastError();
+  return iris::launch_overlapped(splitk_reduce_kernel, dim3((p->N / 4 + 255) / 256, span), dim3(256), 0, stream,
+                                 q, span);
 }
 

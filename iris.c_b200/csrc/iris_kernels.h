@@ -106,6 +106,9 @@ typedef struct {
     float *ws;
     size_t ws_bytes;
     int splitk;               /* set by iris_launch_gemm                              */
+    int b_static;             /* B is a resident weight that no kernel of the stream
+                                 writes: its first stages may load before the
+                                 previous kernel has finished                         */
     IrisTpParams tp;          /* IRIS_EPI_TP_SCATTER destination and xmod wait        */
     const int *fold_rows;     /* IRIS_EPI_LORA_FOLD: output row of each A row          */
     const void *fold_w0;      /* IRIS_EPI_LORA_FOLD: base weight (bf16, row stride ldo) */

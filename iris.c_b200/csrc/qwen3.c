@@ -377,6 +377,7 @@ static void q3_gemm(q3_enq_t *E, const char *name, const CUtensorMap *ta, const 
     p.N = N;
     p.K = K;
     p.bn = N % 256 == 0 ? 256 : 128;
+    p.b_static = 1;  /* B: a resident weight */
     p.mode = mode;
     p.out = out;
     p.ldo = ldo;

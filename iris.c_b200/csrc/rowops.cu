@@ -57,6 +57,8 @@ adaln_kernel(const float* __restrict__ x, int ldx, __nv_bfloat16* __restrict__ o
              float eps) {
   __shared__ float red[8];
   const int row = blockIdx.x;
+  iris::grid_dep_wait();
+  iris::grid_dep_launch();
   const float4* xr = reinterpret_cast<const float4*>(x + (size_t)row * ldx);
   const int nv = cols >> 2;
   float4 v[ADALN_MAXV];
@@ -115,6 +117,8 @@ adaln_warp_kernel(float* __restrict__ x, int ldx, const __nv_bfloat16* __restric
   const int row = blockIdx.x;
   const int lane = threadIdx.x;
   if (row >= rows) return;
+  iris::grid_dep_wait();
+  iris::grid_dep_launch();
   constexpr int cols = NV * 128;
   float4* xr = reinterpret_cast<float4*>(x + (size_t)row * ldx);
   float4 v[NV];
@@ -655,18 +659,13 @@ cudaError_t iris_launch_adaln_delta(float* x, int ldx, const void* delta_v, int 
     const float* sh1 = shift1 ? shift1 : shift0;
     const float* sc1 = scale1 ? scale1 : scale0;
     __nv_bfloat16* o = static_cast<__nv_bfloat16*>(out);
-    if (cols == 3072)
-      adaln_warp_kernel<24><<<rows, 32, 0, stream>>>(x, ldx, delta, ld_delta, o, ldout, rows, shift0, scale0, sh1,
-                                                     sc1, split, eps);
-    else
-      adaln_warp_kernel<32><<<rows, 32, 0, stream>>>(x, ldx, delta, ld_delta, o, ldout, rows, shift0, scale0, sh1,
-                                                     sc1, split, eps);
-    return cudaGetLastError();
+    return iris::launch_overlapped(cols == 3072 ? adaln_warp_kernel<24> : adaln_warp_kernel<32>, dim3(rows),
+                                   dim3(32), 0, stream, x, ldx, delta, ld_delta, o, ldout, rows, shift0, scale0, sh1,
+                                   sc1, split, eps);
   }
-  adaln_kernel<<<rows, 256, 0, stream>>>(x, ldx, static_cast<__nv_bfloat16*>(out), ldout, cols,
-                                         shift0, scale0, shift1 ? shift1 : shift0,
-                                         scale1 ? scale1 : scale0, split, eps);
-  return cudaGetLastError();
+  return iris::launch_overlapped(adaln_kernel, dim3(rows), dim3(256), 0, stream, (const float*)x, ldx,
+                                 static_cast<__nv_bfloat16*>(out), ldout, cols, shift0, scale0,
+                                 shift1 ? shift1 : shift0, scale1 ? scale1 : scale0, split, eps);
 }
 
 cudaError_t iris_launch_gemv(const void* w, const float* x, const float* bias, float* y, int n,

@@ -483,6 +483,7 @@ static void zgemm(zenq_t *E, const CUtensorMap *ta, const CUtensorMap *tb, int r
     p->mode = mode;
     if (!p->bn) p->bn = 256;
     p->status = g_rt.d_status;
+    p->b_static = 1;  /* B: a resident weight */
     zq(E, iris_launch_gemm(p, g_rt.num_sms, g_rt.stream), what);
 }
 
