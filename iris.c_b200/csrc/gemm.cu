@@ -953,13 +953,26 @@ __global__ void splitk_reduce_kernel(const __grid_constant__ IrisGemmParams p, i
   iris::grid_dep_launch();
   const size_t slice = (size_t)span * p.N;
   const float* w = p.ws + (size_t)row * p.N + c;
-  float4 acc = *reinterpret_cast<const float4*>(w);
-  for (int s = 1; s < p.splitk; s++) {
-    const float4 b = *reinterpret_cast<const float4*>(w + s * slice);
-    acc.x += b.x;
-    acc.y += b.y;
-    acc.z += b.z;
-    acc.w += b.w;
+  // partials requested 8 at a time (one L2 round trip per batch instead of
+  // one per split), added in split order
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s0 = 0; s0 < p.splitk; s0 += 8) {
+    float4 part[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+      if (s0 + i < p.splitk) part[i] = __ldcg(reinterpret_cast<const float4*>(w + (s0 + i) * slice));
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      if (s0 + i >= p.splitk) break;
+      if (s0 + i == 0) {
+        acc = part[0];
+      } else {
+        acc.x += part[i].x;
+        acc.y += part[i].y;
+        acc.z += part[i].z;
+        acc.w += part[i].w;
+      }
+    }
   }
   if (p.bias) {
     const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + c));
