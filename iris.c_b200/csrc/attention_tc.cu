@@ -808,6 +808,171 @@ attn_pair_kernel(const __grid_constant__ AttnParams p) {
   }
 }
 
+// ---------------------------------------------------------------------------
+// Short sequences (at most 128 queries and 128 keys: a 64x64 image with a
+// short prompt, a short text-encoder prompt).  There the tcgen05 kernels'
+// fixed chain (TMEM allocation, TMA round trips, one key tile through
+// S -> P -> O and the epilogue) costs several times the arithmetic.  This
+// kernel takes 16 query rows of one head per CTA on the FMA pipe, in f32: K
+// (transposed) and V staged in shared memory, two rows per warp; a lane owns
+// keys lane + 32i of the scores and head dimensions 4 lane .. 4 lane + 3 of
+// the output.  Masked keys take the logit -1e9 (natural-log units) as in the
+// tensor-core kernels.
+constexpr int SM_ROWS = 16;
+constexpr int SM_WARPS = 8;
+constexpr int SM_KEYS = 128;
+constexpr int SM_SMEM = HD * SM_KEYS * 2 + SM_KEYS * HD * 2 + SM_ROWS * HD * 4 + SM_ROWS * SM_KEYS * 4;
+
+struct SmallAttnArgs {
+  const __nv_bfloat16 *q, *k, *v;
+  __nv_bfloat16* o;
+  int ldq, ldk, ldo, sq, sk, kv_group, causal;
+  float scale_log2;
+  const uint8_t* kmask;
+};
+
+__global__ void __launch_bounds__(SM_WARPS * 32) attn_small_kernel(const __grid_constant__ SmallAttnArgs a) {
+  extern __shared__ __align__(16) uint8_t sm_raw[];
+  __nv_bfloat16* kt = reinterpret_cast<__nv_bfloat16*>(sm_raw);  // [HD][SM_KEYS]
+  __nv_bfloat16* vs = kt + HD * SM_KEYS;                          // [SM_KEYS][HD]
+  float* qs = reinterpret_cast<float*>(vs + SM_KEYS * HD);        // [SM_ROWS][HD]
+  float* ps = qs + SM_ROWS * HD;                                  // [SM_ROWS][SM_KEYS]
+  const int head = blockIdx.y, kvh = head / a.kv_group;
+  const int r0 = blockIdx.x * SM_ROWS;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  iris::grid_dep_wait();
+  // every global load of the CTA's K, V and Q in flight before the first
+  // shared-memory store (one L2 round trip)
+  const int key = tid & (SM_KEYS - 1), dh = (tid >> 7) * (HD / 2);  // K: one key, half its dimensions
+  uint4 kr[HD / 16], vr[SM_KEYS * (HD / 8) / (SM_WARPS * 32)], qr;
+  if (key < a.sk) {
+    const __nv_bfloat16* src = a.k + (size_t)key * a.ldk + kvh * HD + dh;
+#pragma unroll
+    for (int c = 0; c < HD / 16; c++) kr[c] = *reinterpret_cast<const uint4*>(src + 8 * c);
+  }
+#pragma unroll
+  for (int j = 0; j < SM_KEYS * (HD / 8) / (SM_WARPS * 32); j++) {  // V rows, 16-byte chunks
+    const int i = tid + j * SM_WARPS * 32, vk = i >> 4, c = (i & 15) * 8;
+    if (vk < a.sk) vr[j] = *reinterpret_cast<const uint4*>(a.v + (size_t)vk * a.ldk + kvh * HD + c);
+  }
+  const int qrow = r0 + (tid >> 4), qc = (tid & 15) * 8;  // Q: 16 rows x 16 chunks = one per thread
+  if (qrow < a.sq) qr = *reinterpret_cast<const uint4*>(a.q + (size_t)qrow * a.ldq + head * HD + qc);
+  if (key < a.sk) {
+#pragma unroll
+    for (int c = 0; c < HD / 16; c++) {
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&kr[c]);
+#pragma unroll
+      for (int i = 0; i < 8; i++) kt[(dh + 8 * c + i) * SM_KEYS + key] = e[i];
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < SM_KEYS * (HD / 8) / (SM_WARPS * 32); j++) {
+    const int i = tid + j * SM_WARPS * 32, vk = i >> 4, c = (i & 15) * 8;
+    if (vk < a.sk) *reinterpret_cast<uint4*>(vs + vk * HD + c) = vr[j];
+    else if (vk < ((a.sk + 3) & ~3)) *reinterpret_cast<uint4*>(vs + vk * HD + c) = make_uint4(0u, 0u, 0u, 0u);
+  }
+  {
+    float* d = qs + (tid >> 4) * HD + qc;
+    if (qrow < a.sq) {
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&qr);
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const float2 f = __bfloat1622float2(h[j]);
+        d[2 * j] = f.x;
+        d[2 * j + 1] = f.y;
+      }
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; j++) d[j] = 0.f;
+    }
+  }
+  __syncthreads();
+  iris::grid_dep_launch();
+  const int ra = 2 * warp;  // this warp's first row within the CTA
+  float sc[2][4];
+#pragma unroll
+  for (int r = 0; r < 2; r++)
+#pragma unroll
+    for (int i = 0; i < 4; i++) sc[r][i] = 0.f;
+#pragma unroll 2
+  for (int d0 = 0; d0 < HD; d0 += 4) {
+    const float4 q0 = *reinterpret_cast<const float4*>(qs + ra * HD + d0);
+    const float4 q1 = *reinterpret_cast<const float4*>(qs + (ra + 1) * HD + d0);
+    const float qa[4] = {q0.x, q0.y, q0.z, q0.w}, qb[4] = {q1.x, q1.y, q1.z, q1.w};
+#pragma unroll
+    for (int dd = 0; dd < 4; dd++) {
+      const uint2 u = *reinterpret_cast<const uint2*>(kt + (d0 + dd) * SM_KEYS + 4 * lane);  // keys 4 lane ..
+      const float2 ka = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+      const float2 kb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+      const float kv[4] = {ka.x, ka.y, kb.x, kb.y};
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        sc[0][i] = fmaf(qa[dd], kv[i], sc[0][i]);
+        sc[1][i] = fmaf(qb[dd], kv[i], sc[1][i]);
+      }
+    }
+  }
+  float inv[2];
+#pragma unroll
+  for (int r = 0; r < 2; r++) {
+    const int row = r0 + ra + r;
+    float x[4], m = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      const int key = 4 * lane + i;
+      if (key >= a.sk) x[i] = -INFINITY;
+      else if ((a.kmask && !a.kmask[key]) || (a.causal && key > row)) x[i] = -1e9f * LOG2E;
+      else x[i] = sc[r][i] * a.scale_log2;
+      m = fmaxf(m, x[i]);
+    }
+#pragma unroll
+    for (int o = 16; o; o >>= 1) m = fmaxf(m, __shfl_xor_sync(0xffffffffu, m, o));
+    float e[4], l = 0.f;
+#pragma unroll
+    for (int i = 0; i < 4; i++) {
+      e[i] = exp2f(x[i] - m);
+      l += e[i];
+    }
+    *reinterpret_cast<float4*>(ps + (ra + r) * SM_KEYS + 4 * lane) = make_float4(e[0], e[1], e[2], e[3]);
+#pragma unroll
+    for (int o = 16; o; o >>= 1) l += __shfl_xor_sync(0xffffffffu, l, o);
+    inv[r] = 1.0f / l;
+  }
+  __syncwarp();  // the warp reads back its own rows of P
+  float acc[2][4];
+#pragma unroll
+  for (int r = 0; r < 2; r++)
+#pragma unroll
+    for (int i = 0; i < 4; i++) acc[r][i] = 0.f;
+  const int sk4 = (a.sk + 3) & ~3;  // keys past sk: P = 0 and V rows of zeros
+#pragma unroll 2
+  for (int k0 = 0; k0 < sk4; k0 += 4) {
+    const float4 pa = *reinterpret_cast<const float4*>(ps + ra * SM_KEYS + k0);
+    const float4 pb = *reinterpret_cast<const float4*>(ps + (ra + 1) * SM_KEYS + k0);
+    const float p0[4] = {pa.x, pa.y, pa.z, pa.w}, p1[4] = {pb.x, pb.y, pb.z, pb.w};
+#pragma unroll
+    for (int kk = 0; kk < 4; kk++) {
+      const uint2 u = *reinterpret_cast<const uint2*>(vs + (k0 + kk) * HD + 4 * lane);
+      const float2 va = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.x));
+      const float2 vb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
+      const float vv[4] = {va.x, va.y, vb.x, vb.y};
+#pragma unroll
+      for (int i = 0; i < 4; i++) {
+        acc[0][i] = fmaf(p0[kk], vv[i], acc[0][i]);
+        acc[1][i] = fmaf(p1[kk], vv[i], acc[1][i]);
+      }
+    }
+  }
+#pragma unroll
+  for (int r = 0; r < 2; r++) {
+    const int row = r0 + ra + r;
+    if (row < a.sq)
+      *reinterpret_cast<uint2*>(a.o + (size_t)row * a.ldo + head * HD + 4 * lane) =
+          make_uint2(pack_bf16(acc[r][0] * inv[r], acc[r][1] * inv[r]),
+                     pack_bf16(acc[r][2] * inv[r], acc[r][3] * inv[r]));
+  }
+}
+
 bool g_attn_tc_attr = false;
 
 }  // namespace
@@ -823,6 +988,8 @@ extern "C" cudaError_t iris_attention_tc_init(void) {
     e = cudaFuncSetAttribute(attn_pair_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(attn_pair_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, P_SMEM_BYTES);
+  if (e == cudaSuccess)
+    e = cudaFuncSetAttribute(attn_small_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SM_SMEM);
   if (e == cudaSuccess) g_attn_tc_attr = true;
   return e;
 }
@@ -844,6 +1011,27 @@ extern "C" cudaError_t iris_launch_attention_gqa(const void* q, int ldq, const v
   if (!g_attn_tc_attr) {
     cudaError_t e = iris_attention_tc_init();
     if (e != cudaSuccess) return e;
+  }
+  if (sq <= SM_ROWS * 8 && sk <= SM_KEYS) {  // short sequences: the FMA-pipe kernel above
+    SmallAttnArgs a;
+    a.q = static_cast<const __nv_bfloat16*>(q);
+    a.k = static_cast<const __nv_bfloat16*>(k);
+    a.v = static_cast<const __nv_bfloat16*>(v);
+    a.o = static_cast<__nv_bfloat16*>(o);
+    a.ldq = ldq;
+    a.ldk = ldk;
+    a.ldo = ldo;
+    a.sq = sq;
+    a.sk = sk;
+    a.kv_group = kv_group;
+    a.causal = causal;
+    a.scale_log2 = scale * LOG2E;
+    a.kmask = key_mask;
+    if ((reinterpret_cast<uintptr_t>(q) | reinterpret_cast<uintptr_t>(k) | reinterpret_cast<uintptr_t>(v) |
+         reinterpret_cast<uintptr_t>(o)) & 15)
+      return cudaErrorInvalidValue;
+    return iris::launch_overlapped(attn_small_kernel, dim3((sq + SM_ROWS - 1) / SM_ROWS, heads), dim3(SM_WARPS * 32),
+                                   SM_SMEM, stream, a);
   }
   static int sms = 0;
   if (!sms) {

@@ -17,8 +17,8 @@ pytestmark = pytest.mark.gpu
 _fp = C.POINTER(C.c_float)
 
 
-@pytest.mark.parametrize("sq,sk,heads", [(16, 80, 2), (80, 80, 2), (200, 333, 3), (1536, 1536, 4),
-                                         (1, 64, 1), (130, 1, 1)])
+@pytest.mark.parametrize("sq,sk,heads", [(16, 80, 2), (80, 80, 2), (128, 128, 3), (128, 129, 2), (129, 128, 2),
+                                         (200, 333, 3), (1536, 1536, 4), (1, 64, 1), (130, 1, 1)])
 @pytest.mark.parametrize("scale_std", [1.0, 4.0])
 def test_attention(iris, sq, sk, heads, scale_std):
     rng = np.random.default_rng(sq + sk + heads)
@@ -123,7 +123,7 @@ def _masked_ref(q, k, v, heads, group, keep, causal, scale):
     return (torch.softmax(s, -1) @ vh).transpose(0, 1).reshape(S, heads * 128)
 
 
-@pytest.mark.parametrize("S,heads,group", [(512, 32, 4), (2560, 16, 2)])
+@pytest.mark.parametrize("S,heads,group", [(512, 32, 4), (2560, 16, 2), (96, 8, 4), (128, 4, 1)])
 @pytest.mark.parametrize("mask", ["right", "left", "holes", "none_kept", "all_kept"])
 @pytest.mark.parametrize("causal", [1, 0])
 def test_masked_attention_key_tile_bound(iris, S, heads, group, mask, causal):
@@ -131,7 +131,8 @@ def test_masked_attention_key_tile_bound(iris, S, heads, group, mask, causal):
     stop after the last key tile any of their rows can use (the last kept key,
     and under the causal mask their last row), except where a row keeps no key
     and averages all of them.  512 rows x 32 heads runs one query tile per
-    CTA, 2560 x 16 the CTA pairs; fp32 reference, relative L2 <= 1e-2."""
+    CTA, 2560 x 16 the CTA pairs, 96 and 128 rows the short-sequence kernel
+    (f32 on the FMA pipe); fp32 reference, relative L2 <= 1e-2."""
     import torch
     g = torch.Generator(device="cuda").manual_seed(S + heads + causal)
     kvh = heads // group
