@@ -572,6 +572,7 @@ static void gp_group(IrisGemmParams *p, int g, const CUtensorMap *tb, int row0, 
 
 typedef struct {
     int rc;
+    int fuse_ln;  /* a whole forward: a residual GEMM may apply the next block's adaLN */
     uint64_t kernels;
     /* live profiling (iris_cuda_flux_profile): an event after every launch */
     iris_cuda_kernel_time_t *prof;
@@ -732,6 +733,37 @@ static void enq_embed(iris_cuda_flux_t *tf, enq_t *E) {
 static void enq_ip(iris_cuda_flux_t *tf, enq_t *E, int blk, int row0, int rows);
 
 /* double-stream block i: group 0 = text rows [0, St), group 1 = image rows */
+/* Short sequences run the residual GEMMs split over K; their reduction then
+ * also applies the adaLN that reads the updated rows next (one launch fewer
+ * per residual update).  Only on one GPU, in a whole forward, and where the
+ * next operation on the hidden state is that adaLN (no IP-Adapter update in
+ * between). */
+static int ip_active(const iris_cuda_flux_t *tf, int blk) {
+    return tf->ip && blk < tf->ip->nb && tf->ip->h_scale[blk] != 0.0f;
+}
+
+static void fuse_next_adaln(iris_cuda_flux_t *tf, enq_t *E, IrisGemmParams *gp, const float *sh0,
+                            const float *sc0, const float *sh1, const float *sc1, int split) {
+    flux_plan_t *P = &tf->plan;
+    if (!E->fuse_ln || tf->tp > 1 || iris_gemm_splits(gp, g_rt.num_sms) < 2) return;
+    gp->ln_out = P->xmod;
+    gp->ln_ld = tf->H;
+    gp->ln_split = split;
+    gp->ln_shift[0] = sh0;
+    gp->ln_scale[0] = sc0;
+    gp->ln_shift[1] = sh1 ? sh1 : sh0;
+    gp->ln_scale[1] = sc1 ? sc1 : sc0;
+    gp->ln_eps = 1e-6f;
+    P->ln_pending = 1;
+}
+
+/* the adaLN about to be enqueued was applied by the previous reduction */
+static int adaln_done(flux_plan_t *P) {
+    const int d = P->ln_pending;
+    P->ln_pending = 0;
+    return d;
+}
+
 static void enq_double(iris_cuda_flux_t *tf, int i, enq_t *E) {
     flux_plan_t *P = &tf->plan;
     cudaStream_t st = g_rt.stream;
@@ -740,7 +772,8 @@ static void enq_double(iris_cuda_flux_t *tf, int i, enq_t *E) {
     const float *mi = tf->mods, *mt = tf->mods + (size_t)6 * H;
     flux_dbl_t *b = &tf->dbl[i];
     IrisGemmParams gp;
-    enq_x(E, adaln_rows(tf, 0, S, mt, mt + H, mi, mi + H, St), "adaln1", 0.0, 6.0 * S * (double)H);
+    if (!adaln_done(P))
+        enq_x(E, adaln_rows(tf, 0, S, mt, mt + H, mi, mi + H, St), "adaln1", 0.0, 6.0 * S * (double)H);
     gp_init(&gp, P, &P->tm_xmod, 3 * Hl, H, IRIS_EPI_QKV);
     tp_reads_xmod(tf, &gp);
     gp.bn = bn_for(3 * Hl);
@@ -760,10 +793,12 @@ static void enq_double(iris_cuda_flux_t *tf, int i, enq_t *E) {
     gp.out = P->hidden; gp.ldo = H;
     gp.gate[0] = mt + 2 * H; gp.gate[1] = mi + 2 * H;
     tp_resid(tf, &gp);
+    fuse_next_adaln(tf, E, &gp, mt + 3 * H, mt + 4 * H, mi + 3 * H, mi + 4 * H, St);
     enq_gemm(E, &gp, "dbl_out");
     enq_allreduce(tf, E);
-    enq_x(E, adaln_rows(tf, 0, S, mt + 3 * H, mt + 4 * H, mi + 3 * H, mi + 4 * H, St), "adaln2", 0.0,
-          6.0 * S * (double)H);
+    if (!adaln_done(P))
+        enq_x(E, adaln_rows(tf, 0, S, mt + 3 * H, mt + 4 * H, mi + 3 * H, mi + 4 * H, St), "adaln2", 0.0,
+              6.0 * S * (double)H);
     gp_init(&gp, P, &P->tm_xmod, 2 * Fl, H, IRIS_EPI_SWIGLU);
     tp_reads_xmod(tf, &gp);
     gp_group(&gp, 0, &b->tm_in[0], 0, St);
@@ -776,6 +811,11 @@ static void enq_double(iris_cuda_flux_t *tf, int i, enq_t *E) {
     gp.out = P->hidden; gp.ldo = H;
     gp.gate[0] = mt + 5 * H; gp.gate[1] = mi + 5 * H;
     tp_resid(tf, &gp);
+    if (!ip_active(tf, i)) {  /* the next block's adaLN (double blocks share their modulation) */
+        const float *ms = tf->mods + (size_t)12 * H;
+        if (i + 1 < tf->cfg.n_double) fuse_next_adaln(tf, E, &gp, mt, mt + H, mi, mi + H, St);
+        else if (tf->cfg.n_single > 0) fuse_next_adaln(tf, E, &gp, ms, ms + H, NULL, NULL, S);
+    }
     enq_gemm(E, &gp, "dbl_mlp_out");
     enq_allreduce(tf, E);
     enq_ip(tf, E, i, St, Si);
@@ -808,7 +848,8 @@ static void enq_single(iris_cuda_flux_t *tf, int i, enq_t *E) {
     const float *ms = tf->mods + (size_t)12 * H;
     flux_sgl_t *b = &tf->sgl[i];
     IrisGemmParams gp;
-    enq_x(E, adaln_rows(tf, 0, S, ms, ms + H, NULL, NULL, S), "adaln_s", 0.0, 6.0 * S * (double)H);
+    if (!adaln_done(P))
+        enq_x(E, adaln_rows(tf, 0, S, ms, ms + H, NULL, NULL, S), "adaln_s", 0.0, 6.0 * S * (double)H);
     gp_init(&gp, P, &P->tm_xmod, 3 * Hl + 2 * Fl, H, IRIS_EPI_SINGLE);
     tp_reads_xmod(tf, &gp);
     gp_group(&gp, 0, &b->tm_fused, 0, S);
@@ -826,6 +867,8 @@ static void enq_single(iris_cuda_flux_t *tf, int i, enq_t *E) {
     gp.out = P->hidden; gp.ldo = H;
     gp.gate[0] = ms + 2 * H;
     tp_resid(tf, &gp);
+    if (i + 1 < tf->cfg.n_single && !ip_active(tf, tf->cfg.n_double + i))
+        fuse_next_adaln(tf, E, &gp, ms, ms + H, NULL, NULL, S);  /* single blocks share their modulation */
     enq_gemm(E, &gp, "sgl_out");
     enq_allreduce(tf, E);
     enq_ip(tf, E, tf->cfg.n_double + i, P->s_txt, S - P->s_txt);
@@ -867,6 +910,8 @@ static void tp_end(iris_cuda_flux_t *tf, enq_t *E) {
 /* Queue one forward over the current plan: reads P->lat_in, P->txt_f32 and
  * tf->t_dev, writes P->out. */
 static int enqueue_forward(iris_cuda_flux_t *tf, enq_t *E) {
+    E->fuse_ln = 1;
+    tf->plan.ln_pending = 0;
     tp_begin(tf, E);
     enq_mods(tf, E);
     enq_embed(tf, E);

@@ -998,6 +998,82 @@ __global__ void splitk_reduce_kernel(const __grid_constant__ IrisGemmParams p, i
   }
 }
 
+// Split-K reduction of a gated residual update fused with the adaLN that
+// reads the updated rows next: one CTA per row, a thread per 4 columns.  The
+// row's new residual is stored as the plain reduction would store it, then
+// LayerNorm (mean, then the variance around it, eps inside the root) and the
+// row group's modulation give the next GEMM's bf16 operand.
+__global__ void __launch_bounds__(1024) splitk_reduce_ln_kernel(const __grid_constant__ IrisGemmParams p) {
+  const int row = blockIdx.x;
+  const int g = (p.ngroups > 1 && row >= p.row0[1]) ? 1 : 0;
+  const int local = row - p.row0[g];
+  if (local < 0 || local >= p.rows[g]) return;  // the whole CTA
+  const int c = threadIdx.x * 4;
+  const int span = p.ngroups > 1 ? p.row0[1] + p.rows[1] : p.row0[0] + p.rows[0];
+  iris::grid_dep_wait();
+  iris::grid_dep_launch();
+  const size_t slice = (size_t)span * p.N;
+  const float* w = p.ws + (size_t)row * p.N + c;
+  float4* d = reinterpret_cast<float4*>(reinterpret_cast<float*>(p.out) + (size_t)row * p.ldo + c);
+  const float4 gg = __ldg(reinterpret_cast<const float4*>(p.gate[g] + c));
+  float4 h = *d;
+  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+  for (int s0 = 0; s0 < p.splitk; s0 += 8) {
+    float4 part[8];
+#pragma unroll
+    for (int i = 0; i < 8; i++)
+      if (s0 + i < p.splitk) part[i] = __ldcg(reinterpret_cast<const float4*>(w + (s0 + i) * slice));
+#pragma unroll
+    for (int i = 0; i < 8; i++) {
+      if (s0 + i >= p.splitk) break;
+      if (s0 + i == 0) {
+        acc = part[0];
+      } else {
+        acc.x += part[i].x;
+        acc.y += part[i].y;
+        acc.z += part[i].z;
+        acc.w += part[i].w;
+      }
+    }
+  }
+  if (p.bias) {
+    const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + c));
+    acc.x += b.x;
+    acc.y += b.y;
+    acc.z += b.z;
+    acc.w += b.w;
+  }
+  h.x += gg.x * acc.x;
+  h.y += gg.y * acc.y;
+  h.z += gg.z * acc.z;
+  h.w += gg.w * acc.w;
+  *d = h;
+  __shared__ float red[32];
+  const int lane = threadIdx.x & 31, wid = threadIdx.x >> 5, nw = blockDim.x >> 5;
+  auto block_sum = [&](float v) -> float {
+#pragma unroll
+    for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+    __syncthreads();  // red is reused
+    if (lane == 0) red[wid] = v;
+    __syncthreads();
+    float t = lane < nw ? red[lane] : 0.f;
+#pragma unroll
+    for (int o = 16; o; o >>= 1) t += __shfl_xor_sync(0xffffffffu, t, o);
+    return t;
+  };
+  const float mean = block_sum((h.x + h.y) + (h.z + h.w)) / (float)p.N;
+  const float a0 = h.x - mean, a1 = h.y - mean, a2 = h.z - mean, a3 = h.w - mean;
+  const float var = block_sum((a0 * a0 + a1 * a1) + (a2 * a2 + a3 * a3)) / (float)p.N;
+  const float rstd = 1.0f / sqrtf(var + p.ln_eps);
+  const int gl = row >= p.ln_split ? 1 : 0;
+  const float4 sh = __ldg(reinterpret_cast<const float4*>(p.ln_shift[gl] + c));
+  const float4 sc = __ldg(reinterpret_cast<const float4*>(p.ln_scale[gl] + c));
+  const float y0 = (1.0f + sc.x) * (a0 * rstd) + sh.x, y1 = (1.0f + sc.y) * (a1 * rstd) + sh.y;
+  const float y2 = (1.0f + sc.z) * (a2 * rstd) + sh.z, y3 = (1.0f + sc.w) * (a3 * rstd) + sh.w;
+  *reinterpret_cast<uint2*>(static_cast<__nv_bfloat16*>(p.ln_out) + (size_t)row * p.ln_ld + c) =
+      make_uint2(pack_bf16(y0, y1), pack_bf16(y2, y3));
+}
+
 }  // namespace
 
 extern "C" int iris_make_tmap_bf16(CUtensorMap* m, const void* ptr, uint64_t rows, uint64_t cols,
@@ -1068,6 +1144,54 @@ extern "C" cudaError_t iris_launch_gemm(const IrisGemmParams* p, int num_sms, cu
   return iris_launch_gemm_ex(p, num_sms, stream, nullptr);
 }
 
+// Launch plan of a GEMM: the CTA-pair kernel, or the single-CTA kernel with
+// `splitk` K splits (1: none).
+struct GemmPlan {
+  bool pair;
+  long grid;
+  int splitk;
+};
+
+static GemmPlan gemm_plan(const IrisGemmParams* p, int num_sms) {
+  GemmPlan g = {false, 0, 1};
+  const int rows = p->rows[0] + (p->ngroups > 1 ? p->rows[1] : 0);
+  const bool linear = p->mode == IRIS_EPI_BF16 || p->mode == IRIS_EPI_F32 || p->mode == IRIS_EPI_RESID_GATE;
+  if (p->bn == 256 && rows >= 512 && g_max_pairs > 0) {
+    int mt = (p->rows[0] + BM2 - 1) / BM2 + (p->ngroups > 1 ? (p->rows[1] + BM2 - 1) / BM2 : 0);
+    long total = (long)mt * ((p->N + 255) / 256);
+    long cap = g_max_pairs < num_sms / 2 ? g_max_pairs : num_sms / 2;
+    // a pair grid under half the pairs leaves SMs idle: a linear epilogue with a
+    // workspace goes to the single-CTA kernel below, which splits K instead
+    const bool split_instead = p->ws && linear && 2 * total < cap && p->K / BK >= 8;
+    if (!split_instead) {
+      g.pair = true;
+      g.grid = 2 * (total < cap ? total : cap);
+      return g;
+    }
+  }
+  int mt = (p->rows[0] + BM - 1) / BM + (p->ngroups > 1 ? (p->rows[1] + BM - 1) / BM : 0);
+  long tiles = (long)mt * ((p->N + p->bn - 1) / p->bn);
+  // Few output tiles (a short sequence): split K so that enough CTAs stream
+  // the weights, when the caller gave a workspace and the epilogue is linear.
+  const int num_kb = (p->K + BK - 1) / BK;
+  const int span = p->ngroups > 1 ? p->row0[1] + p->rows[1] : p->row0[0] + p->rows[0];
+  if (p->ws && tiles > 0 && tiles < num_sms / 2 && num_kb >= 8 && linear) {
+    long s = num_sms / tiles;
+    if (s > num_kb / 4) s = num_kb / 4;
+    const long fit = (long)(p->ws_bytes / ((size_t)span * p->N * sizeof(float)));
+    if (s > fit) s = fit;
+    if (s >= 2) g.splitk = (int)s;
+  }
+  const long total = tiles * g.splitk;
+  g.grid = total < num_sms ? total : num_sms;
+  return g;
+}
+
+extern "C" int iris_gemm_splits(const IrisGemmParams* p, int num_sms) {
+  if (!g_gemm_attr && iris_gemm_init() != cudaSuccess) return 1;
+  return gemm_plan(p, num_sms).splitk;
+}
+
 extern "C" cudaError_t iris_launch_gemm_ex(const IrisGemmParams* p, int num_sms, cudaStream_t stream,
                                            int* launches) {
   if (launches) *launches = 1;
@@ -1077,48 +1201,29 @@ extern "C" cudaError_t iris_launch_gemm_ex(const IrisGemmParams* p, int num_sms,
   }
   if (p->bn != 128 && p->bn != 256) return cudaErrorInvalidValue;
   if (p->K % BK != 0 || p->N % 128 != 0) return cudaErrorInvalidValue;
-  const int rows = p->rows[0] + (p->ngroups > 1 ? p->rows[1] : 0);
-  const bool linear = p->mode == IRIS_EPI_BF16 || p->mode == IRIS_EPI_F32 || p->mode == IRIS_EPI_RESID_GATE;
   // A tensor-parallel launch waits on peer GPUs: it starts only after the
   // previous kernel has finished, as an ordinary launch does.
   const bool overlap = p->tp.size <= 1;
-  if (p->bn == 256 && rows >= 512 && g_max_pairs > 0) {
-    int mt = (p->rows[0] + BM2 - 1) / BM2 + (p->ngroups > 1 ? (p->rows[1] + BM2 - 1) / BM2 : 0);
-    long total = (long)mt * ((p->N + 255) / 256);
-    long cap = g_max_pairs < num_sms / 2 ? g_max_pairs : num_sms / 2;
-    // a pair grid under half the pairs leaves SMs idle: a linear epilogue with a
-    // workspace goes to the single-CTA kernel below, which splits K instead
-    const bool split_instead = p->ws && linear && 2 * total < cap && p->K / BK >= 8;
-    if (!split_instead) {
-      long pairs = total < cap ? total : cap;
-      if (p->mode == IRIS_EPI_LORA_FOLD)
-        gemm_tc2_kernel<true><<<(int)(2 * pairs), NUM_THREADS2, FOLD_SMEM2_BYTES, stream>>>(*p);
-      else if (overlap)
-        return iris::launch_overlapped(gemm_tc2_kernel<false>, dim3((unsigned)(2 * pairs)), dim3(NUM_THREADS2),
-                                       SMEM2_BYTES, stream, *p);
-      else
-        gemm_tc2_kernel<false><<<(int)(2 * pairs), NUM_THREADS2, SMEM2_BYTES, stream>>>(*p);
-      return cudaGetLastError();
-    }
+  const GemmPlan plan = gemm_plan(p, num_sms);
+  if (plan.pair) {
+    if (p->mode == IRIS_EPI_LORA_FOLD)
+      gemm_tc2_kernel<true><<<(int)plan.grid, NUM_THREADS2, FOLD_SMEM2_BYTES, stream>>>(*p);
+    else if (overlap)
+      return iris::launch_overlapped(gemm_tc2_kernel<false>, dim3((unsigned)plan.grid), dim3(NUM_THREADS2),
+                                     SMEM2_BYTES, stream, *p);
+    else
+      gemm_tc2_kernel<false><<<(int)plan.grid, NUM_THREADS2, SMEM2_BYTES, stream>>>(*p);
+    return cudaGetLastError();
   }
-  int mt = (p->rows[0] + BM - 1) / BM + (p->ngroups > 1 ? (p->rows[1] + BM - 1) / BM : 0);
-  long tiles = (long)mt * ((p->N + p->bn - 1) / p->bn);
-  if (tiles <= 0) return cudaSuccess;
-  // Few output tiles (a short sequence): split K so that enough CTAs stream
-  // the weights, when the caller gave a workspace and the epilogue is linear.
+  if (plan.grid <= 0) return cudaSuccess;
   IrisGemmParams q = *p;
-  q.splitk = 1;
-  const int num_kb = (p->K + BK - 1) / BK;
+  q.splitk = plan.splitk;
   const int span = p->ngroups > 1 ? p->row0[1] + p->rows[1] : p->row0[0] + p->rows[0];
-  if (p->ws && tiles < num_sms / 2 && num_kb >= 8 && linear) {
-    long s = num_sms / tiles;
-    if (s > num_kb / 4) s = num_kb / 4;
-    const long fit = (long)(p->ws_bytes / ((size_t)span * p->N * sizeof(float)));
-    if (s > fit) s = fit;
-    if (s >= 2) q.splitk = (int)s;
-  }
-  const long total = tiles * q.splitk;
-  int grid = (int)(total < num_sms ? total : num_sms);
+  const int grid = (int)plan.grid;
+  // the reduction applies the next adaLN when asked to (one CTA per row)
+  const bool ln = q.splitk > 1 && p->ln_out && p->mode == IRIS_EPI_RESID_GATE && !p->resid_store &&
+                  p->N % 128 == 0 && p->N <= 4 * 1024;
+  if (p->ln_out && !ln) return cudaErrorInvalidValue;  // the caller relies on the adaLN being applied
   cudaError_t e;
   if (q.mode == IRIS_EPI_LORA_FOLD) {
     gemm_tc_kernel<true><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(q);
@@ -1131,6 +1236,8 @@ extern "C" cudaError_t iris_launch_gemm_ex(const IrisGemmParams* p, int num_sms,
   }
   if (e != cudaSuccess || q.splitk == 1) return e;
   if (launches) *launches = 2;
+  if (ln)
+    return iris::launch_overlapped(splitk_reduce_ln_kernel, dim3(span), dim3(p->N / 4), 0, stream, q);
   return iris::launch_overlapped(splitk_reduce_kernel, dim3((p->N / 4 + 255) / 256, span), dim3(256), 0, stream,
                                  q, span);
 }

@@ -106,6 +106,15 @@ typedef struct {
     float *ws;
     size_t ws_bytes;
     int splitk;               /* set by iris_launch_gemm                              */
+    /* optional, RESID_GATE launches that split over K (iris_gemm_splits > 1):
+       the reduction also applies the next adaLN to each finished row,
+       ln_out[r] = bf16((1 + ln_scale[g]) * LayerNorm(out[r]) + ln_shift[g]),
+       g = (r >= ln_split) -- what iris_launch_adaln would do next           */
+    void *ln_out;
+    int ln_ld;
+    int ln_split;
+    const float *ln_shift[2], *ln_scale[2];
+    float ln_eps;
     int b_static;             /* B is a resident weight that no kernel of the stream
                                  writes: its first stages may load before the
                                  previous kernel has finished                         */
@@ -121,6 +130,8 @@ int iris_make_tmap_bf16(CUtensorMap *m, const void *ptr, uint64_t rows, uint64_t
                         uint64_t ld, uint32_t box_rows);
 
 cudaError_t iris_launch_gemm(const IrisGemmParams *p, int num_sms, cudaStream_t stream);
+/* The number of K splits iris_launch_gemm would use for p (1: none). */
+int iris_gemm_splits(const IrisGemmParams *p, int num_sms);
 /* as iris_launch_gemm; *launches = kernels queued (2 when a split-K
  * reduction pass follows the GEMM) */
 cudaError_t iris_launch_gemm_ex(const IrisGemmParams *p, int num_sms, cudaStream_t stream, int *launches);
