@@ -508,12 +508,16 @@ static int plan_ensure(iris_cuda_flux_t *tf, int s_txt, int img_h, int img_w,
         PA(P->ws, P->ws_bytes);
     }
 #undef PA
-    if (iris_mk_tmap(&P->tm_xmod, P->xmod, S, H, H, 128) ||
-        iris_mk_tmap(&P->tm_attn, P->attn, S, Hl, Hl, 128) ||
-        iris_mk_tmap(&P->tm_mlp, P->mlp, S, Fl, Fl, 128) ||
-        iris_mk_tmap(&P->tm_cat, P->cat, S, Hl + Fl, Hl + Fl, 128) ||
-        iris_mk_tmap(&P->tm_tok_img, P->tok_img, P->n_img_total, C, C, 128) ||
-        iris_mk_tmap(&P->tm_tok_txt, P->tok_txt, s_txt, T, T, 128)) {
+    /* a short sequence fits one box of S rows: smaller A stages, more of them
+       in flight while the weights stream */
+    P->a_box = S <= 128 ? (S + 7) & ~7 : 0;
+    const int ab = P->a_box ? P->a_box : 128;
+    if (iris_mk_tmap(&P->tm_xmod, P->xmod, S, H, H, ab) ||
+        iris_mk_tmap(&P->tm_attn, P->attn, S, Hl, Hl, ab) ||
+        iris_mk_tmap(&P->tm_mlp, P->mlp, S, Fl, Fl, ab) ||
+        iris_mk_tmap(&P->tm_cat, P->cat, S, Hl + Fl, Hl + Fl, ab) ||
+        iris_mk_tmap(&P->tm_tok_img, P->tok_img, P->n_img_total, C, C, ab) ||
+        iris_mk_tmap(&P->tm_tok_txt, P->tok_txt, s_txt, T, T, ab)) {
         plan_free(P);
         return IRIS_CUDA_ERR_CUDA;
     }
@@ -561,6 +565,7 @@ static void gp_init(IrisGemmParams *p, const flux_plan_t *P, const CUtensorMap *
     p->eps = 1e-6f;
     p->status = g_rt.d_status;
     p->b_static = 1;  /* every B of the forward is a resident weight */
+    p->a_box = P->a_box;
 }
 
 static void gp_group(IrisGemmParams *p, int g, const CUtensorMap *tb, int row0, int rows) {

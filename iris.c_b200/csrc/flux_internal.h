@@ -35,6 +35,7 @@ typedef struct {
     unsigned part_i, x_i;   /* (while enqueueing) partial / xmod syncs queued in this call */
     int part_pending;       /* a scattered update awaits the next adaLN */
     int ln_pending;         /* the last residual GEMM's reduction already applied the next adaLN */
+    int a_box;              /* rows of the activation tensor maps' boxes (0 = 128): S rounded up to 8 when S <= 128 */
     uint16_t *ip_q, *ip_o;  /* IP-Adapter: pre-RoPE image Q and its attention output [S, H] */
     float *rope_cos_k, *rope_sin_k;  /* SREF K-side tables (NULL = the Q tables) */
     float *ws;              /* split-K workspace of short sequences (NULL otherwise) */

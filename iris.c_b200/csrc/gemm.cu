@@ -27,7 +27,9 @@ namespace {
 
 constexpr int BM = 128;
 constexpr int BK = 64;
-constexpr int STAGES = 4;
+constexpr int STAGES = 4;                   // with 128-row A tiles
+constexpr int MAX_STAGES = 5;               // with A tiles of at most 80 rows
+constexpr int SMEM_LIMIT = 232448;          // dynamic shared memory a CTA may opt into
 constexpr int A_BYTES = BM * BK * 2;        // 16 KB
 constexpr int B_BYTES_MAX = 256 * BK * 2;   // 32 KB
 constexpr int STAGE_BYTES = A_BYTES + B_BYTES_MAX;
@@ -43,8 +45,8 @@ constexpr int EPI_BYTES = 4 * EPI_WARP_BYTES;
 constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*barriers*/ + EPI_BYTES + 1024 /*align slack*/;
 
 struct Bars {
-  uint64_t full[STAGES];
-  uint64_t empty[STAGES];
+  uint64_t full[MAX_STAGES];
+  uint64_t empty[MAX_STAGES];
   uint64_t tfull[2];
   uint64_t tempty[2];
   uint64_t drain;
@@ -436,7 +438,13 @@ __global__ void __launch_bounds__(NUM_THREADS, 1)
 gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  Bars* bars = reinterpret_cast<Bars*>(smem + STAGES * STAGE_BYTES);
+  // Stages of A (a_box rows; with fewer than 128 the tensor cores' reads of
+  // rows a_box..127 fall into the stage's B tile: rows no epilogue stores)
+  // and B (up to 256 rows); their number is set by the host to fill shared memory.
+  const int nst = p.nstages > 0 ? p.nstages : STAGES;
+  const uint32_t a_bytes = (uint32_t)(p.a_box ? p.a_box : BM) * BK * 2;
+  const uint32_t stage_bytes = a_bytes + B_BYTES_MAX;
+  Bars* bars = reinterpret_cast<Bars*>(smem + nst * stage_bytes);
   volatile int* abort_flag = &bars->abort;
 
   const int warp = threadIdx.x >> 5;
@@ -453,7 +461,7 @@ gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
   const uint32_t idesc = iris::umma_idesc_bf16_f32(BM, p.bn);
 
   if (threadIdx.x == 0) {
-    for (int s = 0; s < STAGES; s++) {
+    for (int s = 0; s < nst; s++) {
       iris::mbar_init(&bars->full[s], 1);
       iris::mbar_init(&bars->empty[s], 1);
     }
@@ -476,16 +484,16 @@ gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
   // The prologue above overlapped the previous kernel's tail; so do the
   // weight loads of the first stages when B is a resident weight.
   const int pre = (p.b_static && p.tp.size <= 1 && blockIdx.x < total && !kFold)
-                      ? min(STAGES, (blockIdx.x % nsplit + 1) * num_kb / nsplit - (blockIdx.x % nsplit) * num_kb / nsplit)
+                      ? min(nst, (blockIdx.x % nsplit + 1) * num_kb / nsplit - (blockIdx.x % nsplit) * num_kb / nsplit)
                       : 0;
   if (warp == 0 && lane == 0 && pre > 0) {
     int g, ml, n0;
     tile_coords(p, blockIdx.x / nsplit, mt0, mtot, g, ml, n0);
     const int kb0 = (blockIdx.x % nsplit) * num_kb / nsplit;
     for (int s = 0; s < pre; s++) {
-      iris::mbar_arrive_expect_tx(&bars->full[s], A_BYTES + b_bytes);
+      iris::mbar_arrive_expect_tx(&bars->full[s], a_bytes + b_bytes);
       for (int h = 0; h < p.bn / 128; h++)
-        iris::tma_load_2d(smem + s * STAGE_BYTES + A_BYTES + h * (128 * BK * 2), &p.tmap_b[g], &bars->full[s],
+        iris::tma_load_2d(smem + s * stage_bytes + a_bytes + h * (128 * BK * 2), &p.tmap_b[g], &bars->full[s],
                           (kb0 + s) * BK, n0 + 128 * h);
     }
   }
@@ -513,25 +521,25 @@ gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
           ok = false;
           break;
         }
-        uint8_t* sa = smem + stage * STAGE_BYTES;
-        uint8_t* sb = sa + A_BYTES;
+        uint8_t* sa = smem + stage * stage_bytes;
+        uint8_t* sb = sa + a_bytes;
         const bool b_done = issued < pre;  // the first unit's early weight stages
-        if (!b_done) iris::mbar_arrive_expect_tx(&bars->full[stage], A_BYTES + b_bytes);
+        if (!b_done) iris::mbar_arrive_expect_tx(&bars->full[stage], a_bytes + b_bytes);
         iris::tma_load_2d(sa, &p.tmap_a, &bars->full[stage], kb * BK, arow);
         for (int h = 0; h < p.bn / 128 && !b_done; h++)  // weight tensor maps have 128-row boxes
           iris::tma_load_2d(sb + h * (128 * BK * 2), &p.tmap_b[g], &bars->full[stage], kb * BK, n0 + 128 * h);
         issued++;
-        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        if (++stage == nst) { stage = 0; phase ^= 1; }
       }
     }
     if (!ok) {
       // Drain: wait (bounded) for the copies this thread issued last, so no
       // TMA write lands in shared memory after the CTA exits.
-      long n = issued < STAGES ? issued : STAGES;
+      long n = issued < nst ? issued : nst;
       int s = stage;
       uint32_t ph = phase;
       for (long i = 0; i < n; i++) {
-        if (--s < 0) { s = STAGES - 1; ph ^= 1; }
+        if (--s < 0) { s = nst - 1; ph ^= 1; }
         volatile int no_abort = 0;
         iris::mbar_wait(&bars->full[s], ph, &no_abort, p.status, IRIS_DEV_ERR_GEMM_DRAIN);
       }
@@ -558,8 +566,8 @@ gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
           break;
         }
         iris::tc_fence_after();
-        uint32_t sa = iris::smem_u32(smem + stage * STAGE_BYTES);
-        uint32_t sb = sa + A_BYTES;
+        uint32_t sa = iris::smem_u32(smem + stage * stage_bytes);
+        uint32_t sb = sa + a_bytes;
         uint64_t adesc = iris::umma_desc_k_sw128(sa);
         uint64_t bdesc = iris::umma_desc_k_sw128(sb);
 #pragma unroll
@@ -568,7 +576,7 @@ gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
           iris::umma_bf16(d_tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kb != kb0 || kk != 0));
         }
         iris::umma_commit(&bars->empty[stage]);
-        if (++stage == STAGES) { stage = 0; phase ^= 1; }
+        if (++stage == nst) { stage = 0; phase ^= 1; }
       }
       if (ok) iris::umma_commit(&bars->tfull[buf]);
     }
@@ -580,7 +588,8 @@ gemm_tc_kernel(const __grid_constant__ IrisGemmParams p) {
   } else if (warp >= 2) {
     // ------------------------------------------------ epilogue
     const int quarter = warp & 3;  // TMEM lane quarter this warp may access
-    float* stage = reinterpret_cast<float*>(smem + STAGES * STAGE_BYTES + 1024 + (warp - 2) * EPI_WARP_BYTES);
+    // f32 staging (only the epilogues that stage get it from the host)
+    float* stage = reinterpret_cast<float*>(smem + nst * stage_bytes + 1024 + (warp - 2) * EPI_WARP_BYTES);
     int it = 0;
     if (blockIdx.x < total && nsplit == 1) {
       int g, ml, n0;
@@ -1111,9 +1120,9 @@ static int g_max_pairs = 0;  // CTA pairs that can be resident at once
 extern "C" cudaError_t iris_gemm_init(void) {
   if (g_gemm_attr) return cudaSuccess;
   cudaError_t e = cudaFuncSetAttribute(gemm_tc_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       SMEM_BYTES);
+                                       SMEM_LIMIT);
   if (e == cudaSuccess)
-    e = cudaFuncSetAttribute(gemm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_BYTES);
+    e = cudaFuncSetAttribute(gemm_tc_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM_LIMIT);
   if (e == cudaSuccess)
     e = cudaFuncSetAttribute(gemm_tc2_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM2_BYTES);
   if (e == cudaSuccess)
@@ -1220,18 +1229,34 @@ extern "C" cudaError_t iris_launch_gemm_ex(const IrisGemmParams* p, int num_sms,
   q.splitk = plan.splitk;
   const int span = p->ngroups > 1 ? p->row0[1] + p->rows[1] : p->row0[0] + p->rows[0];
   const int grid = (int)plan.grid;
+  // A stages of a_box rows (every tile's rows must lie inside the box), and
+  // as many stages as shared memory holds next to the f32 staging of the
+  // epilogues that use it
+  if (p->a_box) {
+    if (p->a_box % 8 || p->a_box > BM || p->mode == IRIS_EPI_LORA_FOLD || p->rows[0] > p->a_box ||
+        (p->ngroups > 1 && p->rows[1] > p->a_box))
+      return cudaErrorInvalidValue;
+  }
+  const bool staging = p->mode == IRIS_EPI_RESID_GATE || p->mode == IRIS_EPI_F32 ||
+                       p->mode == IRIS_EPI_TP_SCATTER || q.splitk > 1;
+  const size_t stage_bytes = (size_t)(p->a_box ? p->a_box : BM) * BK * 2 + B_BYTES_MAX;
+  const size_t fixed = 1024 /*barriers*/ + (staging ? EPI_BYTES : 0) + 1024 /*align slack*/;
+  q.nstages = (int)((SMEM_LIMIT - fixed) / stage_bytes);
+  if (q.nstages > MAX_STAGES) q.nstages = MAX_STAGES;
+  const size_t smem = (size_t)q.nstages * stage_bytes + fixed;
   // the reduction applies the next adaLN when asked to (one CTA per row)
   const bool ln = q.splitk > 1 && p->ln_out && p->mode == IRIS_EPI_RESID_GATE && !p->resid_store &&
                   p->N % 128 == 0 && p->N <= 4 * 1024;
   if (p->ln_out && !ln) return cudaErrorInvalidValue;  // the caller relies on the adaLN being applied
   cudaError_t e;
   if (q.mode == IRIS_EPI_LORA_FOLD) {
+    q.nstages = STAGES;
     gemm_tc_kernel<true><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(q);
     e = cudaGetLastError();
   } else if (overlap) {
-    e = iris::launch_overlapped(gemm_tc_kernel<false>, dim3(grid), dim3(NUM_THREADS), SMEM_BYTES, stream, q);
+    e = iris::launch_overlapped(gemm_tc_kernel<false>, dim3(grid), dim3(NUM_THREADS), smem, stream, q);
   } else {
-    gemm_tc_kernel<false><<<grid, NUM_THREADS, SMEM_BYTES, stream>>>(q);
+    gemm_tc_kernel<false><<<grid, NUM_THREADS, smem, stream>>>(q);
     e = cudaGetLastError();
   }
   if (e != cudaSuccess || q.splitk == 1) return e;

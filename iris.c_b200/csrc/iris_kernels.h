@@ -106,6 +106,10 @@ typedef struct {
     float *ws;
     size_t ws_bytes;
     int splitk;               /* set by iris_launch_gemm                              */
+    int a_box;                /* rows of tmap_a's box when under 128 (a multiple of 8, at
+                                 least every group's row count): smaller A stages, so
+                                 more of them in flight; 0 = 128                       */
+    int nstages;              /* set by iris_launch_gemm                              */
     /* optional, RESID_GATE launches that split over K (iris_gemm_splits > 1):
        the reduction also applies the next adaLN to each finished row,
        ln_out[r] = bf16((1 + ln_scale[g]) * LayerNorm(out[r]) + ln_shift[g]),
