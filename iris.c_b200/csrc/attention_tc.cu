@@ -818,8 +818,9 @@ attn_pair_kernel(const __grid_constant__ AttnParams p) {
 // keys lane + 32i of the scores and head dimensions 4 lane .. 4 lane + 3 of
 // the output.  Masked keys take the logit -1e9 (natural-log units) as in the
 // tensor-core kernels.
-constexpr int SM_ROWS = 16;
 constexpr int SM_WARPS = 8;
+constexpr int SM_RPW = 2;                    // query rows per warp
+constexpr int SM_ROWS = SM_WARPS * SM_RPW;  // query rows per CTA
 constexpr int SM_KEYS = 128;
 constexpr int SM_SMEM = HD * SM_KEYS * 2 + SM_KEYS * HD * 2 + SM_ROWS * HD * 4 + SM_ROWS * SM_KEYS * 4;
 
@@ -832,6 +833,9 @@ struct SmallAttnArgs {
 };
 
 __global__ void __launch_bounds__(SM_WARPS * 32) attn_small_kernel(const __grid_constant__ SmallAttnArgs a) {
+  constexpr int NT = SM_WARPS * 32;
+  constexpr int VPT = SM_KEYS * (HD / 8) / NT;         // V chunks per thread
+  constexpr int QPT = (SM_ROWS * (HD / 8) + NT - 1) / NT;  // Q chunks per thread
   extern __shared__ __align__(16) uint8_t sm_raw[];
   __nv_bfloat16* kt = reinterpret_cast<__nv_bfloat16*>(sm_raw);  // [HD][SM_KEYS]
   __nv_bfloat16* vs = kt + HD * SM_KEYS;                          // [SM_KEYS][HD]
@@ -844,19 +848,23 @@ __global__ void __launch_bounds__(SM_WARPS * 32) attn_small_kernel(const __grid_
   // every global load of the CTA's K, V and Q in flight before the first
   // shared-memory store (one L2 round trip)
   const int key = tid & (SM_KEYS - 1), dh = (tid >> 7) * (HD / 2);  // K: one key, half its dimensions
-  uint4 kr[HD / 16], vr[SM_KEYS * (HD / 8) / (SM_WARPS * 32)], qr;
+  uint4 kr[HD / 16], vr[VPT], qr[QPT];
   if (key < a.sk) {
     const __nv_bfloat16* src = a.k + (size_t)key * a.ldk + kvh * HD + dh;
 #pragma unroll
     for (int c = 0; c < HD / 16; c++) kr[c] = *reinterpret_cast<const uint4*>(src + 8 * c);
   }
 #pragma unroll
-  for (int j = 0; j < SM_KEYS * (HD / 8) / (SM_WARPS * 32); j++) {  // V rows, 16-byte chunks
-    const int i = tid + j * SM_WARPS * 32, vk = i >> 4, c = (i & 15) * 8;
+  for (int j = 0; j < VPT; j++) {  // V rows, 16-byte chunks
+    const int i = tid + j * NT, vk = i >> 4, c = (i & 15) * 8;
     if (vk < a.sk) vr[j] = *reinterpret_cast<const uint4*>(a.v + (size_t)vk * a.ldk + kvh * HD + c);
   }
-  const int qrow = r0 + (tid >> 4), qc = (tid & 15) * 8;  // Q: 16 rows x 16 chunks = one per thread
-  if (qrow < a.sq) qr = *reinterpret_cast<const uint4*>(a.q + (size_t)qrow * a.ldq + head * HD + qc);
+#pragma unroll
+  for (int j = 0; j < QPT; j++) {  // Q rows, 16-byte chunks
+    const int i = tid + j * NT, row = r0 + (i >> 4), c = (i & 15) * 8;
+    if (i < SM_ROWS * (HD / 8) && row < a.sq)
+      qr[j] = *reinterpret_cast<const uint4*>(a.q + (size_t)row * a.ldq + head * HD + c);
+  }
   if (key < a.sk) {
 #pragma unroll
     for (int c = 0; c < HD / 16; c++) {
@@ -866,39 +874,48 @@ __global__ void __launch_bounds__(SM_WARPS * 32) attn_small_kernel(const __grid_
     }
   }
 #pragma unroll
-  for (int j = 0; j < SM_KEYS * (HD / 8) / (SM_WARPS * 32); j++) {
-    const int i = tid + j * SM_WARPS * 32, vk = i >> 4, c = (i & 15) * 8;
+  for (int j = 0; j < VPT; j++) {
+    const int i = tid + j * NT, vk = i >> 4, c = (i & 15) * 8;
     if (vk < a.sk) *reinterpret_cast<uint4*>(vs + vk * HD + c) = vr[j];
     else if (vk < ((a.sk + 3) & ~3)) *reinterpret_cast<uint4*>(vs + vk * HD + c) = make_uint4(0u, 0u, 0u, 0u);
   }
-  {
-    float* d = qs + (tid >> 4) * HD + qc;
-    if (qrow < a.sq) {
-      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&qr);
 #pragma unroll
-      for (int j = 0; j < 4; j++) {
-        const float2 f = __bfloat1622float2(h[j]);
-        d[2 * j] = f.x;
-        d[2 * j + 1] = f.y;
+  for (int j = 0; j < QPT; j++) {  // Q as f32, zeros past sq
+    const int i = tid + j * NT, r = i >> 4, c = (i & 15) * 8;
+    if (i >= SM_ROWS * (HD / 8)) continue;
+    float* d = qs + r * HD + c;
+    if (r0 + r < a.sq) {
+      const __nv_bfloat162* h = reinterpret_cast<const __nv_bfloat162*>(&qr[j]);
+#pragma unroll
+      for (int t = 0; t < 4; t++) {
+        const float2 f = __bfloat1622float2(h[t]);
+        d[2 * t] = f.x;
+        d[2 * t + 1] = f.y;
       }
     } else {
 #pragma unroll
-      for (int j = 0; j < 8; j++) d[j] = 0.f;
+      for (int t = 0; t < 8; t++) d[t] = 0.f;
     }
   }
   __syncthreads();
   iris::grid_dep_launch();
-  const int ra = 2 * warp;  // this warp's first row within the CTA
-  float sc[2][4];
+  const int ra = SM_RPW * warp;  // this warp's first row within the CTA
+  float sc[SM_RPW][4];
 #pragma unroll
-  for (int r = 0; r < 2; r++)
+  for (int r = 0; r < SM_RPW; r++)
 #pragma unroll
     for (int i = 0; i < 4; i++) sc[r][i] = 0.f;
 #pragma unroll 2
   for (int d0 = 0; d0 < HD; d0 += 4) {
-    const float4 q0 = *reinterpret_cast<const float4*>(qs + ra * HD + d0);
-    const float4 q1 = *reinterpret_cast<const float4*>(qs + (ra + 1) * HD + d0);
-    const float qa[4] = {q0.x, q0.y, q0.z, q0.w}, qb[4] = {q1.x, q1.y, q1.z, q1.w};
+    float qv[SM_RPW][4];
+#pragma unroll
+    for (int r = 0; r < SM_RPW; r++) {
+      const float4 q4 = *reinterpret_cast<const float4*>(qs + (ra + r) * HD + d0);
+      qv[r][0] = q4.x;
+      qv[r][1] = q4.y;
+      qv[r][2] = q4.z;
+      qv[r][3] = q4.w;
+    }
 #pragma unroll
     for (int dd = 0; dd < 4; dd++) {
       const uint2 u = *reinterpret_cast<const uint2*>(kt + (d0 + dd) * SM_KEYS + 4 * lane);  // keys 4 lane ..
@@ -906,15 +923,14 @@ __global__ void __launch_bounds__(SM_WARPS * 32) attn_small_kernel(const __grid_
       const float2 kb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
       const float kv[4] = {ka.x, ka.y, kb.x, kb.y};
 #pragma unroll
-      for (int i = 0; i < 4; i++) {
-        sc[0][i] = fmaf(qa[dd], kv[i], sc[0][i]);
-        sc[1][i] = fmaf(qb[dd], kv[i], sc[1][i]);
-      }
+      for (int r = 0; r < SM_RPW; r++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) sc[r][i] = fmaf(qv[r][dd], kv[i], sc[r][i]);
     }
   }
-  float inv[2];
+  float inv[SM_RPW];
 #pragma unroll
-  for (int r = 0; r < 2; r++) {
+  for (int r = 0; r < SM_RPW; r++) {
     const int row = r0 + ra + r;
     float x[4], m = -INFINITY;
 #pragma unroll
@@ -939,17 +955,23 @@ __global__ void __launch_bounds__(SM_WARPS * 32) attn_small_kernel(const __grid_
     inv[r] = 1.0f / l;
   }
   __syncwarp();  // the warp reads back its own rows of P
-  float acc[2][4];
+  float acc[SM_RPW][4];
 #pragma unroll
-  for (int r = 0; r < 2; r++)
+  for (int r = 0; r < SM_RPW; r++)
 #pragma unroll
     for (int i = 0; i < 4; i++) acc[r][i] = 0.f;
   const int sk4 = (a.sk + 3) & ~3;  // keys past sk: P = 0 and V rows of zeros
 #pragma unroll 2
   for (int k0 = 0; k0 < sk4; k0 += 4) {
-    const float4 pa = *reinterpret_cast<const float4*>(ps + ra * SM_KEYS + k0);
-    const float4 pb = *reinterpret_cast<const float4*>(ps + (ra + 1) * SM_KEYS + k0);
-    const float p0[4] = {pa.x, pa.y, pa.z, pa.w}, p1[4] = {pb.x, pb.y, pb.z, pb.w};
+    float pv[SM_RPW][4];
+#pragma unroll
+    for (int r = 0; r < SM_RPW; r++) {
+      const float4 p4 = *reinterpret_cast<const float4*>(ps + (ra + r) * SM_KEYS + k0);
+      pv[r][0] = p4.x;
+      pv[r][1] = p4.y;
+      pv[r][2] = p4.z;
+      pv[r][3] = p4.w;
+    }
 #pragma unroll
     for (int kk = 0; kk < 4; kk++) {
       const uint2 u = *reinterpret_cast<const uint2*>(vs + (k0 + kk) * HD + 4 * lane);
@@ -957,14 +979,13 @@ __global__ void __launch_bounds__(SM_WARPS * 32) attn_small_kernel(const __grid_
       const float2 vb = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162*>(&u.y));
       const float vv[4] = {va.x, va.y, vb.x, vb.y};
 #pragma unroll
-      for (int i = 0; i < 4; i++) {
-        acc[0][i] = fmaf(p0[kk], vv[i], acc[0][i]);
-        acc[1][i] = fmaf(p1[kk], vv[i], acc[1][i]);
-      }
+      for (int r = 0; r < SM_RPW; r++)
+#pragma unroll
+        for (int i = 0; i < 4; i++) acc[r][i] = fmaf(pv[r][kk], vv[i], acc[r][i]);
     }
   }
 #pragma unroll
-  for (int r = 0; r < 2; r++) {
+  for (int r = 0; r < SM_RPW; r++) {
     const int row = r0 + ra + r;
     if (row < a.sq)
       *reinterpret_cast<uint2*>(a.o + (size_t)row * a.ldo + head * HD + 4 * lane) =
@@ -1012,7 +1033,7 @@ extern "C" cudaError_t iris_launch_attention_gqa(const void* q, int ldq, const v
     cudaError_t e = iris_attention_tc_init();
     if (e != cudaSuccess) return e;
   }
-  if (sq <= SM_ROWS * 8 && sk <= SM_KEYS) {  // short sequences: the FMA-pipe kernel above
+  if (sq <= SM_KEYS && sk <= SM_KEYS) {  // short sequences: the FMA-pipe kernel above
     SmallAttnArgs a;
     a.q = static_cast<const __nv_bfloat16*>(q);
     a.k = static_cast<const __nv_bfloat16*>(k);
