@@ -16,7 +16,8 @@
  *   attn     bf16 [S, H]   double-block attention output
  *   mlp      bf16 [S, F]   SiLU(gate)*up (double blocks)
  *   cat      bf16 [S, H+F] single block [attention | SiLU(gate)*up]
- *   rope     f32  [S, 64]  cos / sin per (token, rotation pair)
+ *   rope_pos u16  [S, 4]   RoPE position ids (T, H, W, L) per row; the QKV
+ *                          epilogue evaluates cos / sin from them in registers
  * Weights (bf16, [out, in] row-major = K-major GEMM B operands)
  *   double   w_qkv[s] [3H, H] = to_q; to_k; to_v stacked, per stream s
  *            w_in[s]  [2F, H] = ff.linear_in with gate/up interleaved in
@@ -385,12 +386,11 @@ static void plan_free(flux_plan_t *P) {
     }
     if (P->recv) P->xmod = NULL;  /* tensor-parallel xmod lives in the symmetric arena */
     iris_dfree(P->hidden); iris_dfree(P->lat_in); iris_dfree(P->out); iris_dfree(P->txt_f32);
-    iris_dfree(P->rope_cos); iris_dfree(P->rope_sin); iris_dfree(P->xmod); iris_dfree(P->q);
+    iris_dfree(P->rope_pos); iris_dfree(P->rope_spec); iris_dfree(P->xmod); iris_dfree(P->q);
     iris_dfree(P->k); iris_dfree(P->v); iris_dfree(P->attn); iris_dfree(P->mlp);
     iris_dfree(P->cat); iris_dfree(P->tok_img); iris_dfree(P->tok_txt);
     iris_dfree(P->ws);
     iris_dfree(P->ip_q); iris_dfree(P->ip_o);
-    iris_dfree(P->rope_cos_k); iris_dfree(P->rope_sin_k);
     memset(P, 0, sizeof(*P));
 }
 
@@ -399,42 +399,43 @@ void iris_flux_invalidate_plan(iris_cuda_flux_t *tf) {
     plan_free(&tf->plan);
 }
 
-/* RoPE per token and rotation pair, computed exactly like the reference's
- * tables: base_freq[d] = 1/theta^(2d/32), angle = pos * base_freq[d] for the
- * T, H, W, L axes (compute_rope_2d :897, compute_rope_2d_with_t_offset :961,
- * compute_rope_text :1055).  Text rows: (0, 0, 0, i); image rows: (T, y, x, 0). */
-static void fill_rope(const iris_cuda_flux_t *tf, const flux_plan_t *P, float *cs, float *sn) {
-    float base[16];
-    for (int d = 0; d < 16; d++) base[d] = 1.0f / powf(tf->cfg.rope_theta, (float)(2 * d) / 32.0f);
-    int row = 0;
-    for (int i = 0; i < P->s_txt; i++, row++) {
-        float *c = cs + (size_t)row * 64, *s = sn + (size_t)row * 64;
-        for (int p = 0; p < 48; p++) { c[p] = 1.0f; s[p] = 0.0f; }
-        for (int d = 0; d < 16; d++) {
-            float a = (float)i * base[d];
-            c[48 + d] = cosf(a);
-            s[48 + d] = sinf(a);
+/* RoPE position ids per row and the per-pair spec, from which the QKV
+ * epilogue evaluates the rotation in registers.  The frequencies are the
+ * reference's own f32 values, base_freq[d] = 1/theta^(2d/32) for the T, H, W,
+ * L axes (pairs 16a + d of axis a); text rows are (0, 0, 0, i), image rows
+ * (T, y, x, 0) with T the reference latent's offset (compute_rope_2d :897,
+ * compute_rope_2d_with_t_offset :961, compute_rope_text :1055).  SREF band
+ * control scales cos and sin of the H and W pairs of the reference rows'
+ * K (band_scale_ref_krope :1272), set up here as kscale + rope_k_row0. */
+static int fill_rope(const iris_cuda_flux_t *tf, flux_plan_t *P, uint16_t *pos, IrisRopeSpec *spec) {
+    for (int d = 0; d < 16; d++) {
+        const float f = 1.0f / powf(tf->cfg.rope_theta, (float)(2 * d) / 32.0f);
+        for (int a = 0; a < 4; a++) {
+            spec->freq[16 * a + d] = f;
+            spec->axis[16 * a + d] = a;
+            spec->kscale[16 * a + d] = (a == 1 || a == 2) ? iris_flux_sref_band(tf, d) : 1.0f;
         }
     }
+    int row = 0;
+    for (int i = 0; i < P->s_txt; i++, row++) {
+        uint16_t *p = pos + (size_t)row * 4;
+        p[0] = p[1] = p[2] = 0;
+        p[3] = (uint16_t)i;
+    }
     for (int r = -1; r < P->num_refs; r++) {
-        int h = r < 0 ? P->img_h : P->ref_h[r], w = r < 0 ? P->img_w : P->ref_w[r];
-        int t = r < 0 ? 0 : P->ref_t[r];
+        const int h = r < 0 ? P->img_h : P->ref_h[r], w = r < 0 ? P->img_w : P->ref_w[r];
+        const int t = r < 0 ? 0 : P->ref_t[r];
+        if (t < 0 || t > 65535) return iris_fail(IRIS_CUDA_ERR_ARG, "reference T offset %d out of range", t);
         for (int y = 0; y < h; y++)
             for (int x = 0; x < w; x++, row++) {
-                float *c = cs + (size_t)row * 64, *s = sn + (size_t)row * 64;
-                for (int d = 0; d < 16; d++) {
-                    float at = (float)t * base[d], ay = (float)y * base[d], ax = (float)x * base[d];
-                    c[d] = t ? cosf(at) : 1.0f;
-                    s[d] = t ? sinf(at) : 0.0f;
-                    c[16 + d] = cosf(ay);
-                    s[16 + d] = sinf(ay);
-                    c[32 + d] = cosf(ax);
-                    s[32 + d] = sinf(ax);
-                    c[48 + d] = 1.0f;
-                    s[48 + d] = 0.0f;
-                }
+                uint16_t *p = pos + (size_t)row * 4;
+                p[0] = (uint16_t)t; p[1] = (uint16_t)y; p[2] = (uint16_t)x; p[3] = 0;
             }
     }
+    /* the band scale applies to the reference rows of the single blocks only */
+    const int ref0 = P->s_txt + P->n_img;
+    P->rope_k_row0 = (P->num_refs > 0 && (tf->sref_shf != 1.0f || tf->sref_slf != 1.0f)) ? ref0 : 0;
+    return 0;
 }
 
 static int plan_ensure(iris_cuda_flux_t *tf, int s_txt, int img_h, int img_w,
@@ -467,8 +468,12 @@ static int plan_ensure(iris_cuda_flux_t *tf, int s_txt, int img_h, int img_w,
     PA(P->lat_in, (size_t)C * P->n_img_total * 4);
     PA(P->out, (size_t)C * P->n_img * 4);
     PA(P->txt_f32, (size_t)s_txt * T * 4);
-    PA(P->rope_cos, (size_t)S * 64 * 4);
-    PA(P->rope_sin, (size_t)S * 64 * 4);
+    if (S > 65535 || img_h > 65535 || img_w > 65535) {
+        plan_free(P);
+        return iris_fail(IRIS_CUDA_ERR_ARG, "sequence of %d rows: RoPE position ids are 16-bit", S);
+    }
+    PA(P->rope_pos, (size_t)S * 4 * sizeof(uint16_t));
+    PA(P->rope_spec, sizeof(IrisRopeSpec));
     if (tp > 1) {
         /* collective: every rank plans the same shape at the same point */
         const size_t recv_b = (size_t)tp * P->chunk * H * 4, xmod_b = sH * 2;
@@ -522,28 +527,15 @@ static int plan_ensure(iris_cuda_flux_t *tf, int s_txt, int img_h, int img_w,
         return IRIS_CUDA_ERR_CUDA;
     }
     {
-        float *cs = (float *)malloc((size_t)S * 64 * 4), *sn = (float *)malloc((size_t)S * 64 * 4);
-        if (!cs || !sn) { free(cs); free(sn); goto oom; }
-        fill_rope(tf, P, cs, sn);
-        int rc = iris_h2d(P->rope_cos, cs, (size_t)S * 64 * 4) || iris_h2d(P->rope_sin, sn, (size_t)S * 64 * 4);
-        /* SREF band control (set_kside_krope, iris_transformer_flux.c:1297): single
-           blocks rotate K of the reference rows with H / W pairs scaled by s(d) */
-        const int ref0 = P->s_txt + P->n_img;
-        if (!rc && num_refs > 0 && (tf->sref_shf != 1.0f || tf->sref_slf != 1.0f)) {
-            for (int r = ref0; r < S; r++)
-                for (int d = 0; d < 16; d++) {
-                    const float f = iris_flux_sref_band(tf, d);
-                    cs[(size_t)r * 64 + 16 + d] *= f; sn[(size_t)r * 64 + 16 + d] *= f;
-                    cs[(size_t)r * 64 + 32 + d] *= f; sn[(size_t)r * 64 + 32 + d] *= f;
-                }
-            P->rope_cos_k = (float *)iris_dmalloc((size_t)S * 64 * 4);
-            P->rope_sin_k = (float *)iris_dmalloc((size_t)S * 64 * 4);
-            rc = !P->rope_cos_k || !P->rope_sin_k || iris_h2d(P->rope_cos_k, cs, (size_t)S * 64 * 4) ||
-                 iris_h2d(P->rope_sin_k, sn, (size_t)S * 64 * 4);
-        }
-        free(cs);
-        free(sn);
-        if (rc) { plan_free(P); return IRIS_CUDA_ERR_CUDA; }
+        uint16_t *pos = (uint16_t *)malloc((size_t)S * 4 * sizeof(uint16_t));
+        IrisRopeSpec spec;
+        if (!pos) goto oom;
+        int rc = fill_rope(tf, P, pos, &spec);
+        if (!rc)
+            rc = iris_h2d(P->rope_pos, pos, (size_t)S * 4 * sizeof(uint16_t)) ||
+                 iris_h2d(P->rope_spec, &spec, sizeof(spec));
+        free(pos);
+        if (rc) { plan_free(P); return rc < 0 ? rc : IRIS_CUDA_ERR_CUDA; }
     }
     P->valid = 1;
     return 0;
@@ -786,7 +778,7 @@ static void enq_double(iris_cuda_flux_t *tf, int i, enq_t *E) {
     gp_group(&gp, 1, &b->tm_qkv[1], St, Si);
     gp.qnorm[0] = b->qn[0]; gp.knorm[0] = b->kn[0];
     gp.qnorm[1] = b->qn[1]; gp.knorm[1] = b->kn[1];
-    gp.rope_cos = P->rope_cos; gp.rope_sin = P->rope_sin;
+    gp.rope_pos = P->rope_pos; gp.rope_spec = P->rope_spec;
     gp.q = P->q; gp.k = P->k; gp.v = P->v; gp.ldqkv = Hl; gp.H = Hl;
     enq_gemm(E, &gp, "dbl_qkv");
     enq_x(E, iris_launch_attention(P->q, Hl, P->k, P->v, Hl, P->attn, Hl, S, S, NHl,
@@ -838,8 +830,8 @@ static void enq_ip(iris_cuda_flux_t *tf, enq_t *E, int blk, int row0, int rows) 
     cudaStream_t st = g_rt.stream;
     const int H = tf->H, T = ip->T;
     const uint16_t *k = ip->kv + (size_t)blk * T * H, *v = ip->kv + (size_t)(ip->nb + blk) * T * H;
-    enq(E, iris_launch_ip_unrope(P->q + (size_t)row0 * H, H, P->rope_cos + (size_t)row0 * 64,
-                                 P->rope_sin + (size_t)row0 * 64, rows, H, P->ip_q, st), "ip_unrope");
+    enq(E, iris_launch_ip_unrope(P->q + (size_t)row0 * H, H, P->rope_pos + (size_t)row0 * 4, P->rope_spec, rows,
+                                 H, P->ip_q, st), "ip_unrope");
     enq_x(E, iris_launch_attention(P->ip_q, H, k, v, H, P->ip_o, H, rows, T, tf->NH, 1.0f / sqrtf(128.0f), NULL,
                                    st), "ip_attn", 4.0 * rows * T * (double)H, 2.0 * (rows + 2.0 * T) * H * 2.0);
     enq(E, iris_launch_ip_add(P->hidden + (size_t)row0 * H, H, P->ip_o, rows, H, ip->d_scale + blk, st), "ip_add");
@@ -859,8 +851,8 @@ static void enq_single(iris_cuda_flux_t *tf, int i, enq_t *E) {
     tp_reads_xmod(tf, &gp);
     gp_group(&gp, 0, &b->tm_fused, 0, S);
     gp.qnorm[0] = b->qn; gp.knorm[0] = b->kn;
-    gp.rope_cos = P->rope_cos; gp.rope_sin = P->rope_sin;
-    gp.rope_cos_k = P->rope_cos_k; gp.rope_sin_k = P->rope_sin_k;
+    gp.rope_pos = P->rope_pos; gp.rope_spec = P->rope_spec;
+    gp.rope_k_row0 = P->rope_k_row0;  /* SREF band control: reference rows' K (:3872) */
     gp.q = P->q; gp.k = P->k; gp.v = P->v; gp.ldqkv = Hl; gp.H = Hl;
     gp.mlp_out = P->cat; gp.ld_mlp = Hl + Fl; gp.mlp_col0 = Hl; gp.swiglu_base = 3 * Hl;
     enq_gemm(E, &gp, "sgl_fused");

@@ -25,7 +25,10 @@ typedef struct {
     int valid;
     int s_txt, img_h, img_w, n_img, n_img_total, S;
     int num_refs, ref_h[MAXREFS], ref_w[MAXREFS], ref_t[MAXREFS];
-    float *hidden, *lat_in, *out, *txt_f32, *rope_cos, *rope_sin;
+    float *hidden, *lat_in, *out, *txt_f32;
+    uint16_t *rope_pos;      /* [S][4] RoPE position ids (T, H, W, L) per row */
+    IrisRopeSpec *rope_spec; /* per rotation pair: frequency, axis, SREF K-side band scale */
+    int rope_k_row0;         /* first row whose K takes the band scale in the single blocks (0 = off) */
     uint16_t *xmod, *q, *k, *v, *attn, *mlp, *cat, *tok_img, *tok_txt;
     /* tensor parallelism (symmetric memory, see comm.c): rows owned in chunks,
        partial updates received in recv [tp][chunk][H] f32, xmod shared */
@@ -37,7 +40,6 @@ typedef struct {
     int ln_pending;         /* the last residual GEMM's reduction already applied the next adaLN */
     int a_box;              /* rows of the activation tensor maps' boxes (0 = 128): S rounded up to 8 when S <= 128 */
     uint16_t *ip_q, *ip_o;  /* IP-Adapter: pre-RoPE image Q and its attention output [S, H] */
-    float *rope_cos_k, *rope_sin_k;  /* SREF K-side tables (NULL = the Q tables) */
     float *ws;              /* split-K workspace of short sequences (NULL otherwise) */
     size_t ws_bytes;
     CUtensorMap tm_xmod, tm_attn, tm_mlp, tm_cat, tm_tok_img, tm_tok_txt;

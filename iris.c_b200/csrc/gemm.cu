@@ -18,6 +18,7 @@
 // run concurrently share one weight column band in L2.
 #include "iris_kernels.h"
 #include "ptx.cuh"
+#include "rope.cuh"
 
 #include <cuda_bf16.h>
 #include <stdlib.h>
@@ -89,10 +90,13 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float* v
 
 // Epilogue for one 128-column chunk that belongs to the Q/K/V region.
 // TMEM loads are warp-collective and always executed by all 32 lanes; only
-// the global-memory traffic is predicated on `valid`.  The RoPE factors of a
-// 32-column block (this row's own, an L2 access) are requested before the
-// block's TMEM load, so their latency overlaps it; the norm weights are the
-// same for every row and come from L1.
+// the global-memory traffic is predicated on `valid`.  The pair rotation is
+// evaluated in registers: the row's four position ids (one 8-byte load) and,
+// per 32-column block, the 16 pairs' frequencies and axes (the same for every
+// row: L1 broadcasts) give cos / sin of pos * freq (iris::rope_cos_sin); a
+// pair whose position is 0 is the identity (cos 1, sin 0, as the reference's
+// tables hold) and is skipped unless its K side is band-scaled.  The norm
+// weights come from L1 too.
 __device__ __forceinline__ void epi_qkv_chunk(const IrisGemmParams& p, uint32_t taddr, int g,
                                               int row, bool valid, int col0) {
   int which = col0 / p.H;
@@ -101,6 +105,11 @@ __device__ __forceinline__ void epi_qkv_chunk(const IrisGemmParams& p, uint32_t 
   dst += (size_t)row * p.ldqkv + cin;
   float r = 1.0f;
   const float* nw = nullptr;
+  const bool rope = which < 2 && p.rope_pos != nullptr && valid;
+  iris::RopePos pos = {{0u, 0u, 0u, 0u}};
+  if (rope) pos = iris::rope_load_pos(p.rope_pos, row);
+  // K of the rows a launch marks takes the band scale (SREF, single blocks)
+  const bool kscale = which == 1 && p.rope_k_row0 > 0 && row >= p.rope_k_row0;
   if (which < 2) {
     // pass 1: sum of squares over the 128-wide head (TMEM is re-read in pass 2
     // rather than keeping 128 values live in registers)
@@ -115,22 +124,8 @@ __device__ __forceinline__ void epi_qkv_chunk(const IrisGemmParams& p, uint32_t 
     }
     r = rsqrtf(ss * (1.0f / 128.0f) + p.eps);
   }
-  const bool kt = which == 1 && p.rope_cos_k;  // K-side tables (reference-row band scaling)
-  const float* rc = p.rope_cos ? (kt ? p.rope_cos_k : p.rope_cos) + (size_t)row * 64 : nullptr;
-  const float* rs = p.rope_cos ? (kt ? p.rope_sin_k : p.rope_sin) + (size_t)row * 64 : nullptr;
-  const bool rope = which < 2 && rc != nullptr && valid;
 #pragma unroll 1
   for (int j = 0; j < 4; j++) {
-    float4 c[4], sn[4];
-    if (rope) {
-      const float4* cp = reinterpret_cast<const float4*>(rc + 16 * j);
-      const float4* sp = reinterpret_cast<const float4*>(rs + 16 * j);
-#pragma unroll
-      for (int q4 = 0; q4 < 4; q4++) {
-        c[q4] = __ldg(cp + q4);
-        sn[q4] = __ldg(sp + q4);
-      }
-    }
     float v[32];
     iris::tmem_ld32(taddr + 32 * j, v);
     if (!valid) continue;
@@ -145,16 +140,22 @@ __device__ __forceinline__ void epi_qkv_chunk(const IrisGemmParams& p, uint32_t 
         v[4 * e + 3] = v[4 * e + 3] * r * w.w;
       }
       if (rope) {
+        const IrisRopeSpec* sp = p.rope_spec;
 #pragma unroll
-        for (int q4 = 0; q4 < 4; q4++) {
-          float cc[4] = {c[q4].x, c[q4].y, c[q4].z, c[q4].w}, ss4[4] = {sn[q4].x, sn[q4].y, sn[q4].z, sn[q4].w};
-#pragma unroll
-          for (int e = 0; e < 4; e++) {
-            int jj = 2 * (4 * q4 + e);
-            float x0 = v[jj], x1 = v[jj + 1];
-            v[jj] = x0 * cc[e] - x1 * ss4[e];
-            v[jj + 1] = x1 * cc[e] + x0 * ss4[e];
+        for (int e = 0; e < 16; e++) {
+          const int pr = 16 * j + e;
+          const uint32_t ps = iris::rope_axis_pos(pos, __ldg(sp->axis + pr));
+          if (ps == 0 && !kscale) continue;
+          float c = 1.0f, sn = 0.0f;
+          if (ps != 0) iris::rope_cos_sin(ps, __ldg(sp->freq + pr), c, sn);
+          if (kscale) {
+            const float f = __ldg(sp->kscale + pr);
+            c *= f;
+            sn *= f;
           }
+          const float x0 = v[2 * e], x1 = v[2 * e + 1];
+          v[2 * e] = x0 * c - x1 * sn;
+          v[2 * e + 1] = x1 * c + x0 * sn;
         }
       }
     }

@@ -23,6 +23,7 @@
 #include <stdint.h>
 
 #include "iris_kernels.h"
+#include "rope.cuh"
 
 namespace {
 
@@ -180,16 +181,19 @@ __global__ void ip_scale_rows_kernel(float* __restrict__ x, int rows, int H, int
   x[i] *= (i / H) < row_split ? s0 : s1;
 }
 
-// q_pre = R^-1 q: each rotated pair (x0 c - x1 s, x1 c + x0 s) back to (x0, x1);
+// q_pre = R^-1 q: each rotated pair (x0 c - x1 s, x1 c + x0 s) back to (x0, x1),
+// with c, s evaluated from the row's position ids as the QKV epilogue does;
 // grid (pairs / 256, rows): one thread per pair of one row
-__global__ void ip_unrope_kernel(const __nv_bfloat16* __restrict__ q, int ldq, const float* __restrict__ cosb,
-                                 const float* __restrict__ sinb, int H, __nv_bfloat16* __restrict__ out) {
+__global__ void ip_unrope_kernel(const __nv_bfloat16* __restrict__ q, int ldq, const uint16_t* __restrict__ pos,
+                                 const IrisRopeSpec* __restrict__ spec, int H, __nv_bfloat16* __restrict__ out) {
   const int p = blockIdx.x * blockDim.x + threadIdx.x, r = blockIdx.y;
   if (p >= H / 2) return;
   const int pr = p & 63;  // pair index inside its 128-wide head
   const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(q + (size_t)r * ldq + 2 * p);
   const float y0 = __bfloat162float(v.x), y1 = __bfloat162float(v.y);
-  const float c = __ldg(cosb + (size_t)r * 64 + pr), s = __ldg(sinb + (size_t)r * 64 + pr);
+  const uint32_t ps = iris::rope_axis_pos(iris::rope_load_pos(pos, r), __ldg(spec->axis + pr));
+  float c = 1.0f, s = 0.0f;
+  if (ps != 0) iris::rope_cos_sin(ps, __ldg(spec->freq + pr), c, s);
   *reinterpret_cast<__nv_bfloat162*>(out + (size_t)r * H + 2 * p) =
       __floats2bfloat162_rn(y0 * c + y1 * s, y1 * c - y0 * s);
 }
@@ -285,12 +289,12 @@ cudaError_t iris_launch_ip_scale_rows(float* x, int rows, int H, int row_split, 
   return cudaGetLastError();
 }
 
-cudaError_t iris_launch_ip_unrope(const void* q, int ldq, const float* cosb, const float* sinb, int rows, int H,
-                                  void* out, cudaStream_t stream) {
+cudaError_t iris_launch_ip_unrope(const void* q, int ldq, const uint16_t* pos, const IrisRopeSpec* spec, int rows,
+                                  int H, void* out, cudaStream_t stream) {
   if (rows <= 0) return cudaSuccess;
-  if ((H & 127) || (ldq & 1) || rows > 65535) return cudaErrorInvalidValue;
+  if ((H & 127) || (ldq & 1) || rows > 65535 || !pos || !spec) return cudaErrorInvalidValue;
   ip_unrope_kernel<<<dim3(blocks_for(H / 2, 256), rows), 256, 0, stream>>>(
-      static_cast<const __nv_bfloat16*>(q), ldq, cosb, sinb, H, static_cast<__nv_bfloat16*>(out));
+      static_cast<const __nv_bfloat16*>(q), ldq, pos, spec, H, static_cast<__nv_bfloat16*>(out));
   return cudaGetLastError();
 }
 

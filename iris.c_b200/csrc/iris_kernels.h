@@ -27,7 +27,8 @@ enum {
     IRIS_EPI_F32_NCHW = 2,    /* out f32 [col, nchw_rows] (channel-major, + bias)          */
     IRIS_EPI_RESID_GATE = 3,  /* f32 out[row, col] += gate[g][col] * acc                   */
     IRIS_EPI_QKV = 4,         /* cols [0,H) Q, [H,2H) K, [2H,3H) V; per-head RMSNorm on Q/K
-                                 then pair RoPE from rope_cos/sin[row][64]; bf16 stores     */
+                                 then pair RoPE evaluated in registers from the row's
+                                 position ids (rope_pos, rope_spec); bf16 stores            */
     IRIS_EPI_SWIGLU = 5,      /* 256-col tiles hold [gate 128 | up 128] of 128 features:
                                  mlp_out[row, mlp_col0 + f] = SiLU(gate) * up (bf16)       */
     IRIS_EPI_GATE_BF16 = 7,   /* out bf16 [row, ldo] = gate[g][col] * acc (tensor-parallel
@@ -62,6 +63,17 @@ enum {
 #define IRIS_TP_BASE_X 19
 #define IRIS_TP_BAR 20        /* [20, 28): call-start barrier arrivals, by sender */
 #define IRIS_TP_BASE_BAR 28
+/* Rotary embedding of one model, per rotation pair p (64 pairs of a 128-wide
+ * head; pair p rotates columns 2p, 2p + 1): angle = pos[axis[p]] * freq[p], with
+ * pos the row's position id on that axis, freq[p] = 1 / theta^(2i / axis_dim)
+ * computed on the host exactly as the reference does.  kscale[p] multiplies
+ * cos and sin of K on the rows a launch marks (SREF band control; 1 elsewhere). */
+typedef struct {
+    float freq[64];
+    float kscale[64];
+    int axis[64];
+} IrisRopeSpec;
+
 typedef struct {
     int size, rank;           /* size > 1 enables the peer-memory paths          */
     int chunk;                /* rows owned per rank                              */
@@ -87,10 +99,10 @@ typedef struct {
     int resid_store;          /* RESID: out = gate*acc instead of out += gate*acc      */
     const float *qnorm[2];    /* QKV: per group [128]                                  */
     const float *knorm[2];
-    const float *rope_cos;    /* QKV: [rows_total, 64] by absolute row (NULL = no RoPE) */
-    const float *rope_sin;
-    const float *rope_cos_k;  /* QKV: K-side tables (NULL = the Q tables)               */
-    const float *rope_sin_k;
+    const uint16_t *rope_pos; /* QKV: [rows_total][4] position ids by absolute row
+                                 (NULL = no RoPE)                                       */
+    const IrisRopeSpec *rope_spec;  /* QKV: frequency / axis / K scale per rotation pair */
+    int rope_k_row0;          /* QKV: K of rows >= this (when > 0) takes kscale         */
     void *q, *k, *v;          /* QKV destinations (bf16) with row stride ldqkv         */
     int ldqkv;
     int H;                    /* width of Q, K and V blocks (heads * 128)              */
@@ -295,9 +307,10 @@ cudaError_t iris_launch_ip_mha(const float *Q, const float *K, const float *V, i
                                float *out, cudaStream_t stream);
 cudaError_t iris_launch_ip_scale_rows(float *x, int rows, int H, int row_split, float s0, float s1,
                                       cudaStream_t stream);
-/* bf16 q [rows, ldq] after the pair RoPE of tables cos/sin [rows, 64] -> bf16 [rows, H] before it */
-cudaError_t iris_launch_ip_unrope(const void *q, int ldq, const float *cosb, const float *sinb, int rows, int H,
-                                  void *out, cudaStream_t stream);
+/* bf16 q [rows, ldq] after the pair RoPE of position ids pos [rows][4] and spec
+ * -> bf16 [rows, H] before it */
+cudaError_t iris_launch_ip_unrope(const void *q, int ldq, const uint16_t *pos, const IrisRopeSpec *spec,
+                                  int rows, int H, void *out, cudaStream_t stream);
 /* f32 hidden[rows, ldh] += *scale * bf16 o[rows, H] */
 cudaError_t iris_launch_ip_add(float *hidden, int ldh, const void *o, int rows, int H, const float *scale,
                                cudaStream_t stream);

@@ -40,7 +40,9 @@ typedef struct {
     int valid;
     int lat_h, lat_w, cap_seq;
     int n_img, n_cap, ni, nc, S;
-    float *hidden, *tmp, *lat_in, *out, *cap_f32, *rope_cos, *rope_sin, *tok_out;
+    float *hidden, *tmp, *lat_in, *out, *cap_f32, *tok_out;
+    uint16_t *rope_pos;        /* [S][4] RoPE position ids (T, H, W; the 4th unused) */
+    IrisRopeSpec *rope_spec;   /* per rotation pair: frequency and axis */
     uint16_t *xmod, *q, *k, *v, *attn, *mlp, *tok_img, *cap_bf16;
     uint8_t *mask;
     CUtensorMap tm_xmod, tm_attn, tm_mlp, tm_tok_img, tm_cap;
@@ -358,42 +360,45 @@ static void zi_plan_free(zi_plan_t *P) {
         cudaGraphExecDestroy(P->gexec);
         cudaGraphDestroy(P->graph);
     }
-    void *ps[] = {P->hidden, P->tmp, P->lat_in, P->out, P->cap_f32, P->rope_cos, P->rope_sin, P->tok_out,
+    void *ps[] = {P->hidden, P->tmp, P->lat_in, P->out, P->cap_f32, P->rope_pos, P->rope_spec, P->tok_out,
                   P->xmod, P->q, P->k, P->v, P->attn, P->mlp, P->tok_img, P->cap_bf16, P->mask};
     for (size_t i = 0; i < sizeof(ps) / sizeof(ps[0]); i++) iris_dfree(ps[i]);
     memset(P, 0, sizeof(*P));
 }
 
-/* RoPE per token: image rows (cap_padded + 1, y, x), image padding (0, 0, 0),
- * caption rows (1 + s, 0, 0); freq = 1/theta^(2i/d) per axis, positions
- * outside [0, 1024) unrotated (zi_precompute_rope :595, zi_apply_rope :620,
- * position ids :1832-1862). */
-static void zi_fill_rope(const iris_cuda_zimage_t *z, const zi_plan_t *P, float *cs, float *sn, uint8_t *mask) {
+/* RoPE position ids per token -- image rows (cap_padded + 1, y, x), image
+ * padding (0, 0, 0), caption rows (1 + s, 0, 0) -- and the per-pair spec,
+ * freq = 1/theta^(2i/d) per axis (pairs of axis 0 first, then 1, then 2),
+ * from which the QKV epilogue evaluates the rotation in registers.  A position
+ * outside [0, 1024) is left unrotated by the reference, so it is stored as 0,
+ * the identity (zi_precompute_rope :595, zi_apply_rope :620, position ids
+ * :1832-1862). */
+static void zi_fill_rope(const iris_cuda_zimage_t *z, const zi_plan_t *P, uint16_t *pos, IrisRopeSpec *spec,
+                         uint8_t *mask) {
     const int *ax = z->cfg.axes_dims;
     const int wt = P->lat_w / z->cfg.patch_size;
+    int pair = 0;
+    for (int a = 0; a < 3; a++)
+        for (int i = 0; i < ax[a] / 2; i++, pair++) {
+            spec->freq[pair] = 1.0f / powf(z->cfg.rope_theta, (float)(2 * i) / (float)ax[a]);
+            spec->axis[pair] = a;
+            spec->kscale[pair] = 1.0f;
+        }
     for (int row = 0; row < P->S; row++) {
-        int pos[3] = {0, 0, 0};
+        int p3[3] = {0, 0, 0};
         int valid;
         if (row < P->ni) {
             valid = row < P->n_img;
-            if (valid) { pos[0] = P->nc + 1; pos[1] = row / wt; pos[2] = row % wt; }
+            if (valid) { p3[0] = P->nc + 1; p3[1] = row / wt; p3[2] = row % wt; }
         } else {
             int s = row - P->ni;
             valid = s < P->n_cap;
-            pos[0] = 1 + s;
+            p3[0] = 1 + s;
         }
         mask[row] = (uint8_t)valid;
-        int pair = 0;
-        for (int a = 0; a < 3; a++) {
-            int half = ax[a] / 2;
-            for (int i = 0; i < half; i++, pair++) {
-                float freq = 1.0f / powf(z->cfg.rope_theta, (float)(2 * i) / (float)ax[a]);
-                int inb = pos[a] >= 0 && pos[a] < 1024;
-                float ang = (float)pos[a] * freq;
-                cs[(size_t)row * 64 + pair] = inb ? cosf(ang) : 1.0f;
-                sn[(size_t)row * 64 + pair] = inb ? sinf(ang) : 0.0f;
-            }
-        }
+        uint16_t *p = pos + (size_t)row * 4;
+        for (int a = 0; a < 3; a++) p[a] = (uint16_t)((p3[a] >= 0 && p3[a] < 1024) ? p3[a] : 0);
+        p[3] = 0;
     }
 }
 
@@ -420,8 +425,8 @@ static int zi_plan_ensure(iris_cuda_zimage_t *z, int lat_h, int lat_w, int cap_s
     PA(P->lat_in, (size_t)cin * lat_h * lat_w * 4);
     PA(P->out, (size_t)cin * lat_h * lat_w * 4);
     PA(P->cap_f32, (size_t)P->nc * cap * 4);
-    PA(P->rope_cos, (size_t)S * 64 * 4);
-    PA(P->rope_sin, (size_t)S * 64 * 4);
+    PA(P->rope_pos, (size_t)S * 4 * sizeof(uint16_t));
+    PA(P->rope_spec, sizeof(IrisRopeSpec));
     PA(P->tok_out, (size_t)P->n_img * 128 * 4);
     PA(P->xmod, sD * 2);
     PA(P->q, sD * 2);
@@ -444,13 +449,14 @@ static int zi_plan_ensure(iris_cuda_zimage_t *z, int lat_h, int lat_w, int cap_s
         return IRIS_CUDA_ERR_CUDA;
     }
     {
-        float *cs = (float *)malloc((size_t)S * 64 * 4), *sn = (float *)malloc((size_t)S * 64 * 4);
+        uint16_t *pos = (uint16_t *)malloc((size_t)S * 4 * sizeof(uint16_t));
         uint8_t *mk = (uint8_t *)malloc((size_t)S);
-        if (!cs || !sn || !mk) { free(cs); free(sn); free(mk); goto oom; }
-        zi_fill_rope(z, P, cs, sn, mk);
-        int rc = iris_h2d(P->rope_cos, cs, (size_t)S * 64 * 4) || iris_h2d(P->rope_sin, sn, (size_t)S * 64 * 4) ||
-                 iris_h2d(P->mask, mk, (size_t)S);
-        free(cs); free(sn); free(mk);
+        IrisRopeSpec spec;
+        if (!pos || !mk) { free(pos); free(mk); goto oom; }
+        zi_fill_rope(z, P, pos, &spec, mk);
+        int rc = iris_h2d(P->rope_pos, pos, (size_t)S * 4 * sizeof(uint16_t)) ||
+                 iris_h2d(P->rope_spec, &spec, sizeof(spec)) || iris_h2d(P->mask, mk, (size_t)S);
+        free(pos); free(mk);
         if (rc) { zi_plan_free(P); return IRIS_CUDA_ERR_CUDA; }
     }
     P->valid = 1;
@@ -499,7 +505,7 @@ static void zi_enq_block(iris_cuda_zimage_t *z, const zi_blk_t *b, int r0, int l
                               mod ? mod : NULL, st), "zi_norm1");
     memset(&gp, 0, sizeof(gp));
     gp.qnorm[0] = b->qn; gp.knorm[0] = b->kn;
-    gp.rope_cos = P->rope_cos; gp.rope_sin = P->rope_sin;
+    gp.rope_pos = P->rope_pos; gp.rope_spec = P->rope_spec;
     gp.q = P->q; gp.k = P->k; gp.v = P->v; gp.ldqkv = D; gp.H = D; gp.eps = ZI_EPS;
     zgemm(E, &P->tm_xmod, &b->tm_qkv, r0, len, 3 * D, D, IRIS_EPI_QKV, &gp, "zi_qkv");
     size_t o = (size_t)r0 * D;
