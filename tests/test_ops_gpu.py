@@ -33,6 +33,30 @@ def test_attention(iris, sq, sk, heads, scale_std):
     assert rel_l2(O.read((sq, heads * 128)), ref) < 1e-2
 
 
+# Shapes with many heads take the CTA-pair kernel (cta_group::2, four query
+# tiles per pair): the Klein-4B single-block shape, ragged query and key
+# counts, a key count under one tile (the IP-Adapter's 64 tokens) and a long
+# sequence.  `ramp` grows the keys' norm along the sequence so that later key
+# tiles raise the rows' maximum and the rescaling of O in TMEM is exercised.
+@pytest.mark.parametrize("sq,sk,heads,scale_std,ramp", [(1536, 1536, 24, 1.0, 0.0), (1100, 1100, 40, 4.0, 0.0),
+                                                        (1024, 64, 48, 1.0, 0.0), (300, 2000, 40, 2.0, 3.0),
+                                                        (4608, 4608, 6, 1.0, 3.0)])
+def test_attention_pair_kernel(iris, sq, sk, heads, scale_std, ramp):
+    rng = np.random.default_rng(sq * 7 + sk + heads)
+    q = bf16_round(rng.standard_normal((sq, heads * 128)) * scale_std)
+    k = bf16_round(rng.standard_normal((sk, heads * 128)) * (1.0 + ramp * np.arange(sk) / sk)[:, None])
+    v = bf16_round(rng.standard_normal((sk, heads * 128)))
+    Q, K, V, O = Dev(q), Dev(k), Dev(v), Dev(n=sq * heads * 128)
+    ok = iris.lib().iris_gpu_attention_fused_bf16(O.h, Q.h, K.h, V.h, sq, sk, heads, 128,
+                                                  1.0 / np.sqrt(128.0))
+    assert ok, iris.last_error()
+    assert iris.lib().iris_cuda_synchronize() == 0, iris.last_error()  # no device wait ran out
+    got = O.read((sq, heads * 128))
+    assert np.isfinite(got).all()
+    ref = fo.attention(q, k, v, heads)
+    assert rel_l2(got, ref) < 1e-2
+
+
 @pytest.mark.parametrize("seq,hidden", [(24, 256), (1536, 3072), (97, 512), (13, 4096), (9, 3072)])
 def test_adaln(iris, seq, hidden):
     rng = np.random.default_rng(seq)
