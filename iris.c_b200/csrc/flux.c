@@ -408,11 +408,12 @@ void iris_flux_invalidate_plan(iris_cuda_flux_t *tf) {
  * control scales cos and sin of the H and W pairs of the reference rows'
  * K (band_scale_ref_krope :1272), set up here as kscale + rope_k_row0. */
 static int fill_rope(const iris_cuda_flux_t *tf, flux_plan_t *P, uint16_t *pos, IrisRopeSpec *spec) {
+    memset(spec, 0, sizeof(*spec));
     for (int d = 0; d < 16; d++) {
         const float f = 1.0f / powf(tf->cfg.rope_theta, (float)(2 * d) / 32.0f);
         for (int a = 0; a < 4; a++) {
             spec->freq[16 * a + d] = f;
-            spec->axis[16 * a + d] = a;
+            iris_rope_set_axis(spec, 16 * a + d, a);
             spec->kscale[16 * a + d] = (a == 1 || a == 2) ? iris_flux_sref_band(tf, d) : 1.0f;
         }
     }

@@ -92,11 +92,14 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float* v
 // TMEM loads are warp-collective and always executed by all 32 lanes; only
 // the global-memory traffic is predicated on `valid`.  The pair rotation is
 // evaluated in registers: the row's four position ids (one 8-byte load) and,
-// per 32-column block, the 16 pairs' frequencies and axes (the same for every
-// row: L1 broadcasts) give cos / sin of pos * freq (iris::rope_cos_sin); a
-// pair whose position is 0 is the identity (cos 1, sin 0, as the reference's
-// tables hold) and is skipped unless its K side is band-scaled.  The norm
-// weights come from L1 too.
+// per 32-column block, the 16 pairs' frequencies, axes and K scales (the same
+// for every row: L1 broadcasts, requested before the block's TMEM load) give
+// cos / sin of pos * freq (iris::rope_cos_sin; position 0 gives exactly cos 1,
+// sin 0, the identity, as the reference's tables hold).  No branch per pair,
+// so the 16 evaluations of a block overlap; a block is skipped as a whole
+// when every row of the warp has position 0 on all of its axes (text rows have
+// only L, image rows T = 0 and L = 0) and no band scale.  The norm weights come
+// from L1 too.
 __device__ __forceinline__ void epi_qkv_chunk(const IrisGemmParams& p, uint32_t taddr, int g,
                                               int row, bool valid, int col0) {
   int which = col0 / p.H;
@@ -126,6 +129,25 @@ __device__ __forceinline__ void epi_qkv_chunk(const IrisGemmParams& p, uint32_t 
   }
 #pragma unroll 1
   for (int j = 0; j < 4; j++) {
+    float fq[16];
+    uint32_t axb = 0;
+    bool rot = false;  // some row of the warp has a non-zero position on an axis of this block
+    if (which < 2 && p.rope_pos) {
+      const uint32_t am = __ldg(p.rope_spec->axis_mask + j);
+      bool nz = kscale;
+#pragma unroll
+      for (int a = 0; a < 4; a++) nz |= ((am >> a) & 1u) && pos.v[a] != 0u;
+      rot = __any_sync(0xffffffffu, rope && nz);
+    }
+    if (rot) {
+      const float4* f4 = reinterpret_cast<const float4*>(p.rope_spec->freq + 16 * j);
+#pragma unroll
+      for (int q4 = 0; q4 < 4; q4++) {
+        const float4 f = __ldg(f4 + q4);
+        fq[4 * q4] = f.x; fq[4 * q4 + 1] = f.y; fq[4 * q4 + 2] = f.z; fq[4 * q4 + 3] = f.w;
+      }
+      axb = __ldg(p.rope_spec->axis_bits + j);
+    }
     float v[32];
     iris::tmem_ld32(taddr + 32 * j, v);
     if (!valid) continue;
@@ -139,17 +161,13 @@ __device__ __forceinline__ void epi_qkv_chunk(const IrisGemmParams& p, uint32_t 
         v[4 * e + 2] = v[4 * e + 2] * r * w.z;
         v[4 * e + 3] = v[4 * e + 3] * r * w.w;
       }
-      if (rope) {
-        const IrisRopeSpec* sp = p.rope_spec;
+      if (rot && rope) {
 #pragma unroll
         for (int e = 0; e < 16; e++) {
-          const int pr = 16 * j + e;
-          const uint32_t ps = iris::rope_axis_pos(pos, __ldg(sp->axis + pr));
-          if (ps == 0 && !kscale) continue;
-          float c = 1.0f, sn = 0.0f;
-          if (ps != 0) iris::rope_cos_sin(ps, __ldg(sp->freq + pr), c, sn);
+          float c, sn;
+          iris::rope_cos_sin(iris::rope_axis_pos(pos, (int)((axb >> (2 * e)) & 3u)), fq[e], c, sn);
           if (kscale) {
-            const float f = __ldg(sp->kscale + pr);
+            const float f = __ldg(p.rope_spec->kscale + 16 * j + e);
             c *= f;
             sn *= f;
           }
@@ -1202,6 +1220,7 @@ extern "C" int iris_gemm_splits(const IrisGemmParams* p, int num_sms) {
   return gemm_plan(p, num_sms).splitk;
 }
 
+
 extern "C" cudaError_t iris_launch_gemm_ex(const IrisGemmParams* p, int num_sms, cudaStream_t stream,
                                            int* launches) {
   if (launches) *launches = 1;
@@ -1216,6 +1235,7 @@ extern "C" cudaError_t iris_launch_gemm_ex(const IrisGemmParams* p, int num_sms,
   const bool overlap = p->tp.size <= 1;
   const GemmPlan plan = gemm_plan(p, num_sms);
   if (plan.pair) {
+    if (p->ln_out) return cudaErrorInvalidValue;  // the adaLN is applied by split-K reductions only
     if (p->mode == IRIS_EPI_LORA_FOLD)
       gemm_tc2_kernel<true><<<(int)plan.grid, NUM_THREADS2, FOLD_SMEM2_BYTES, stream>>>(*p);
     else if (overlap)

@@ -191,7 +191,8 @@ __global__ void ip_unrope_kernel(const __nv_bfloat16* __restrict__ q, int ldq, c
   const int pr = p & 63;  // pair index inside its 128-wide head
   const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(q + (size_t)r * ldq + 2 * p);
   const float y0 = __bfloat162float(v.x), y1 = __bfloat162float(v.y);
-  const uint32_t ps = iris::rope_axis_pos(iris::rope_load_pos(pos, r), __ldg(spec->axis + pr));
+  const int ax = (int)((__ldg(spec->axis_bits + pr / 16) >> (2 * (pr % 16))) & 3u);
+  const uint32_t ps = iris::rope_axis_pos(iris::rope_load_pos(pos, r), ax);
   float c = 1.0f, s = 0.0f;
   if (ps != 0) iris::rope_cos_sin(ps, __ldg(spec->freq + pr), c, s);
   *reinterpret_cast<__nv_bfloat162*>(out + (size_t)r * H + 2 * p) =

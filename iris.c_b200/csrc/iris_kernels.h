@@ -64,15 +64,23 @@ enum {
 #define IRIS_TP_BAR 20        /* [20, 28): call-start barrier arrivals, by sender */
 #define IRIS_TP_BASE_BAR 28
 /* Rotary embedding of one model, per rotation pair p (64 pairs of a 128-wide
- * head; pair p rotates columns 2p, 2p + 1): angle = pos[axis[p]] * freq[p], with
+ * head; pair p rotates columns 2p, 2p + 1): angle = pos[axis(p)] * freq[p], with
  * pos the row's position id on that axis, freq[p] = 1 / theta^(2i / axis_dim)
- * computed on the host exactly as the reference does.  kscale[p] multiplies
- * cos and sin of K on the rows a launch marks (SREF band control; 1 elsewhere). */
+ * computed on the host exactly as the reference does; axis(p) = bits 2(p % 16)
+ * and up of axis_bits[p / 16].  kscale[p] multiplies cos and sin of K on the
+ * rows a launch marks (SREF band control; 1 elsewhere). */
 typedef struct {
     float freq[64];
     float kscale[64];
-    int axis[64];
+    uint32_t axis_bits[4];
+    uint32_t axis_mask[4];    /* per 16-pair block: bit a set if a pair of it uses axis a */
 } IrisRopeSpec;
+
+static inline void iris_rope_set_axis(IrisRopeSpec *s, int pair, int axis) {
+    s->axis_bits[pair / 16] = (s->axis_bits[pair / 16] & ~(3u << (2 * (pair % 16)))) |
+                              ((uint32_t)axis << (2 * (pair % 16)));
+    s->axis_mask[pair / 16] |= 1u << axis;
+}
 
 typedef struct {
     int size, rank;           /* size > 1 enables the peer-memory paths          */

@@ -378,10 +378,11 @@ static void zi_fill_rope(const iris_cuda_zimage_t *z, const zi_plan_t *P, uint16
     const int *ax = z->cfg.axes_dims;
     const int wt = P->lat_w / z->cfg.patch_size;
     int pair = 0;
+    memset(spec, 0, sizeof(*spec));
     for (int a = 0; a < 3; a++)
         for (int i = 0; i < ax[a] / 2; i++, pair++) {
             spec->freq[pair] = 1.0f / powf(z->cfg.rope_theta, (float)(2 * i) / (float)ax[a]);
-            spec->axis[pair] = a;
+            iris_rope_set_axis(spec, pair, a);
             spec->kscale[pair] = 1.0f;
         }
     for (int row = 0; row < P->S; row++) {
