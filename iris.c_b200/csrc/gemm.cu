@@ -88,96 +88,112 @@ __device__ __forceinline__ void store_bf16x32(__nv_bfloat16* dst, const float* v
   }
 }
 
-// Epilogue for one 128-column chunk that belongs to the Q/K/V region.
-// TMEM loads are warp-collective and always executed by all 32 lanes; only
-// the global-memory traffic is predicated on `valid`.  The pair rotation is
+// Epilogue for NC consecutive 128-column chunks (heads) of one row that belong
+// to the Q/K/V region (NC = 2 only when both are Q or K heads).  TMEM loads
+// are warp-collective and always executed by all 32 lanes; only the
+// global-memory traffic is predicated on `valid`.  The pair rotation is
 // evaluated in registers: the row's four position ids (one 8-byte load) and,
 // per 32-column block, the 16 pairs' frequencies, axes and K scales (the same
-// for every row: L1 broadcasts, requested before the block's TMEM load) give
-// cos / sin of pos * freq (iris::rope_cos_sin; position 0 gives exactly cos 1,
-// sin 0, the identity, as the reference's tables hold).  No branch per pair,
-// so the 16 evaluations of a block overlap; a block is skipped as a whole
-// when every row of the warp has position 0 on all of its axes (text rows have
-// only L, image rows T = 0 and L = 0) and no band scale.  The norm weights come
-// from L1 too.
-__device__ __forceinline__ void epi_qkv_chunk(const IrisGemmParams& p, uint32_t taddr, int g,
-                                              int row, bool valid, int col0) {
-  int which = col0 / p.H;
-  int cin = col0 - which * p.H;
-  __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(which == 0 ? p.q : which == 1 ? p.k : p.v);
-  dst += (size_t)row * p.ldqkv + cin;
-  float r = 1.0f;
-  const float* nw = nullptr;
-  const bool rope = which < 2 && p.rope_pos != nullptr && valid;
+// for every row: L1 broadcasts) give cos / sin of pos * freq
+// (iris::rope_cos_sin; position 0 gives exactly cos 1, sin 0, the identity, as
+// the reference's tables hold).  A block's 16 evaluations have no branch
+// between them, so they overlap each other and the block's TMEM load, and
+// serve every head of the row; a block is skipped as a whole when every row of
+// the warp has position 0 on all of its axes (text rows have only L, image
+// rows T = 0 and L = 0) and no band scale.  The norm weights come from L1 too.
+template <int NC>
+__device__ __forceinline__ void epi_qkv_chunks(const IrisGemmParams& p, uint32_t taddr, int g, int row, bool valid,
+                                               int col0) {
+  int which[NC];
+  __nv_bfloat16* dst[NC];
+  const float* nw[NC];
+  float r[NC];
+  bool kscale[NC];
+  const bool qk = col0 / p.H < 2;  // (all NC chunks are Q / K heads, or NC = 1)
+  const bool rope = qk && p.rope_pos != nullptr && valid;
   iris::RopePos pos = {{0u, 0u, 0u, 0u}};
   if (rope) pos = iris::rope_load_pos(p.rope_pos, row);
-  // K of the rows a launch marks takes the band scale (SREF, single blocks)
-  const bool kscale = which == 1 && p.rope_k_row0 > 0 && row >= p.rope_k_row0;
-  if (which < 2) {
-    // pass 1: sum of squares over the 128-wide head (TMEM is re-read in pass 2
-    // rather than keeping 128 values live in registers)
-    nw = (which == 0) ? p.qnorm[g] : p.knorm[g];
-    float ss = 0.f;
-#pragma unroll 1
-    for (int j = 0; j < 4; j++) {
-      float v[32];
-      iris::tmem_ld32(taddr + 32 * j, v);
+  bool anyk = false;
 #pragma unroll
-      for (int e = 0; e < 32; e++) ss += v[e] * v[e];
+  for (int h = 0; h < NC; h++) {
+    const int c0 = col0 + 128 * h;
+    which[h] = c0 / p.H;
+    const int cin = c0 - which[h] * p.H;
+    dst[h] = reinterpret_cast<__nv_bfloat16*>(which[h] == 0 ? p.q : which[h] == 1 ? p.k : p.v) +
+             (size_t)row * p.ldqkv + cin;
+    // K of the rows a launch marks takes the band scale (SREF, single blocks)
+    kscale[h] = which[h] == 1 && p.rope_k_row0 > 0 && row >= p.rope_k_row0;
+    anyk |= kscale[h];
+    r[h] = 1.0f;
+    nw[h] = nullptr;
+    if (which[h] < 2) {
+      // pass 1: sum of squares over the 128-wide head (TMEM is re-read in pass 2
+      // rather than keeping 128 values live in registers)
+      nw[h] = (which[h] == 0) ? p.qnorm[g] : p.knorm[g];
+      float ss = 0.f;
+#pragma unroll 1
+      for (int j = 0; j < 4; j++) {
+        float v[32];
+        iris::tmem_ld32(taddr + 128 * h + 32 * j, v);
+#pragma unroll
+        for (int e = 0; e < 32; e++) ss += v[e] * v[e];
+      }
+      r[h] = rsqrtf(ss * (1.0f / 128.0f) + p.eps);
     }
-    r = rsqrtf(ss * (1.0f / 128.0f) + p.eps);
   }
 #pragma unroll 1
   for (int j = 0; j < 4; j++) {
-    float fq[16];
-    uint32_t axb = 0;
-    bool rot = false;  // some row of the warp has a non-zero position on an axis of this block
-    if (which < 2 && p.rope_pos) {
+    float rc[16], rs[16];  // this row's cos / sin of the block's 16 pairs
+    bool rot = false;      // some row of the warp has a non-zero position on an axis of this block
+    if (qk && p.rope_pos) {
       const uint32_t am = __ldg(p.rope_spec->axis_mask + j);
-      bool nz = kscale;
+      bool nz = anyk;
 #pragma unroll
       for (int a = 0; a < 4; a++) nz |= ((am >> a) & 1u) && pos.v[a] != 0u;
       rot = __any_sync(0xffffffffu, rope && nz);
     }
-    if (rot) {
+    if (rot && rope) {
       const float4* f4 = reinterpret_cast<const float4*>(p.rope_spec->freq + 16 * j);
+      const uint32_t axb = __ldg(p.rope_spec->axis_bits + j);
 #pragma unroll
       for (int q4 = 0; q4 < 4; q4++) {
         const float4 f = __ldg(f4 + q4);
-        fq[4 * q4] = f.x; fq[4 * q4 + 1] = f.y; fq[4 * q4 + 2] = f.z; fq[4 * q4 + 3] = f.w;
-      }
-      axb = __ldg(p.rope_spec->axis_bits + j);
-    }
-    float v[32];
-    iris::tmem_ld32(taddr + 32 * j, v);
-    if (!valid) continue;
-    if (which < 2) {
-      const float4* w4 = reinterpret_cast<const float4*>(nw + 32 * j);
+        const float fq[4] = {f.x, f.y, f.z, f.w};
 #pragma unroll
-      for (int e = 0; e < 8; e++) {
-        const float4 w = __ldg(w4 + e);
-        v[4 * e + 0] = v[4 * e + 0] * r * w.x;
-        v[4 * e + 1] = v[4 * e + 1] * r * w.y;
-        v[4 * e + 2] = v[4 * e + 2] * r * w.z;
-        v[4 * e + 3] = v[4 * e + 3] * r * w.w;
-      }
-      if (rot && rope) {
-#pragma unroll
-        for (int e = 0; e < 16; e++) {
-          float c, sn;
-          iris::rope_cos_sin(iris::rope_axis_pos(pos, (int)((axb >> (2 * e)) & 3u)), fq[e], c, sn);
-          if (kscale) {
-            const float f = __ldg(p.rope_spec->kscale + 16 * j + e);
-            c *= f;
-            sn *= f;
-          }
-          const float x0 = v[2 * e], x1 = v[2 * e + 1];
-          v[2 * e] = x0 * c - x1 * sn;
-          v[2 * e + 1] = x1 * c + x0 * sn;
+        for (int u = 0; u < 4; u++) {
+          const int e = 4 * q4 + u;
+          iris::rope_cos_sin(iris::rope_axis_pos(pos, (int)((axb >> (2 * e)) & 3u)), fq[u], rc[e], rs[e]);
         }
       }
     }
-    store_bf16x32(dst + 32 * j, v);
+#pragma unroll
+    for (int h = 0; h < NC; h++) {
+      float v[32];
+      iris::tmem_ld32(taddr + 128 * h + 32 * j, v);
+      if (!valid) continue;
+      if (which[h] < 2) {
+        const float4* w4 = reinterpret_cast<const float4*>(nw[h] + 32 * j);
+#pragma unroll
+        for (int e = 0; e < 8; e++) {
+          const float4 w = __ldg(w4 + e);
+          v[4 * e + 0] = v[4 * e + 0] * r[h] * w.x;
+          v[4 * e + 1] = v[4 * e + 1] * r[h] * w.y;
+          v[4 * e + 2] = v[4 * e + 2] * r[h] * w.z;
+          v[4 * e + 3] = v[4 * e + 3] * r[h] * w.w;
+        }
+        if (rot && rope) {
+#pragma unroll
+          for (int e = 0; e < 16; e++) {
+            const float f = kscale[h] ? __ldg(p.rope_spec->kscale + 16 * j + e) : 1.0f;
+            const float c = rc[e] * f, sn = rs[e] * f;
+            const float x0 = v[2 * e], x1 = v[2 * e + 1];
+            v[2 * e] = x0 * c - x1 * sn;
+            v[2 * e + 1] = x1 * c + x0 * sn;
+          }
+        }
+      }
+      store_bf16x32(dst[h] + 32 * j, v);
+    }
   }
 }
 
@@ -441,7 +457,12 @@ __device__ __forceinline__ void epi_tile(const IrisGemmParams& p, uint32_t taddr
       if (halves == 2 && nchunks == 2 && c != half) continue;
       if (qkv) {
         if (halves == 2 && nchunks == 1 && half) continue;
-        epi_qkv_chunk(p, taddr + c * 128, g, row, valid, col0);
+        // one warp holding both heads of a Q/K tile: their rotation is evaluated once
+        if (halves == 1 && nchunks == 2 && c == 0 && col0 + 256 <= 2 * p.H && col0 + 256 <= p.N) {
+          epi_qkv_chunks<2>(p, taddr, g, row, valid, col0);
+          break;
+        }
+        epi_qkv_chunks<1>(p, taddr + c * 128, g, row, valid, col0);
       } else if (halves == 2 && nchunks == 1) {
         epi_plain_chunk(p, taddr + c * 128, g, row, row_local, valid, col0, stage, lane, rows_valid, split,
                         2 * half, 2 * half + 2);
