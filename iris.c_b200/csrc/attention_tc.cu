@@ -60,6 +60,9 @@ constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units: a new reference max mo
 // P <= 2^16, which bf16 P and the f32 O / l accumulators take as they are;
 // only larger sums send the row's warp to the exact max / rescale path.
 constexpr float FAST_SUM_LIMIT = 65536.0f;
+// epilogue staging of one softmax warp's 32 output rows (128 bf16 + 16 bytes of padding each)
+constexpr int O_STAGE_LD = 128 * 2 + 16;
+constexpr int O_STAGE_BYTES = 32 * O_STAGE_LD;
 #define IRIS_DEV_ERR_ATTN_PRODUCER 0x201
 #define IRIS_DEV_ERR_ATTN_MMA 0x202
 #define IRIS_DEV_ERR_ATTN_SOFTMAX 0x203
@@ -141,7 +144,7 @@ template <bool kPair, bool kMasked>
 __device__ __forceinline__ void softmax_role(const AttnParams& p, uint32_t tmem, int t, int warp, int lane,
                                              uint64_t* s_full, uint64_t* p_full, uint32_t p_full_cluster,
                                              uint64_t* o_done, volatile int* abort_flag, int row0, int col0,
-                                             int n) {
+                                             int n, uint8_t* ostage) {
   const int quarter = warp & 3;
   const int r = quarter * 32 + lane;  // query row within the tile = TMEM lane
   const uint32_t lane_off = (uint32_t)(quarter * 32) << 16;
@@ -342,25 +345,35 @@ __device__ __forceinline__ void softmax_role(const AttnParams& p, uint32_t tmem,
   if (ok && n > 0 && iris::mbar_wait(o_done, 0, abort_flag, p.status, IRIS_DEV_ERR_ATTN_SOFTMAX)) {
     iris::tc_fence_after();
     const float inv = l > 0.f ? 1.0f / l : 0.f;
-    const int row = row0 + r;
-    __nv_bfloat16* dst = p.o + (size_t)row * p.ldo + col0;
+    // O / l of this warp's 32 rows goes through shared memory (the K / V rings,
+    // idle once every MMA is done; rows 272 bytes apart so that a 16-byte
+    // store of each lane spreads over the banks), then leaves as whole rows:
+    // each global store instruction writes two rows' 256 contiguous bytes.
 #pragma unroll 1
     for (int c = 0; c < 4; c++) {
       float o[32];
       iris::tmem_ld32(o_addr + 32 * c, o);
-      if (row < p.sq) {
-        uint4* d4 = reinterpret_cast<uint4*>(dst + 32 * c);
+      uint4* d4 = reinterpret_cast<uint4*>(ostage + lane * O_STAGE_LD + c * 64);
 #pragma unroll
-        for (int q = 0; q < 4; q++) {
-          uint4 w;
-          w.x = pack_bf16(o[8 * q + 0] * inv, o[8 * q + 1] * inv);
-          w.y = pack_bf16(o[8 * q + 2] * inv, o[8 * q + 3] * inv);
-          w.z = pack_bf16(o[8 * q + 4] * inv, o[8 * q + 5] * inv);
-          w.w = pack_bf16(o[8 * q + 6] * inv, o[8 * q + 7] * inv);
-          d4[q] = w;
-        }
+      for (int q = 0; q < 4; q++) {
+        uint4 w;
+        w.x = pack_bf16(o[8 * q + 0] * inv, o[8 * q + 1] * inv);
+        w.y = pack_bf16(o[8 * q + 2] * inv, o[8 * q + 3] * inv);
+        w.z = pack_bf16(o[8 * q + 4] * inv, o[8 * q + 5] * inv);
+        w.w = pack_bf16(o[8 * q + 6] * inv, o[8 * q + 7] * inv);
+        d4[q] = w;
       }
     }
+    __syncwarp();
+    const int wrow = row0 + (warp & 3) * 32;  // the warp's first row
+#pragma unroll 4
+    for (int k = 0; k < 16; k++) {
+      const int rr = 2 * k + (lane >> 4), cb = (lane & 15) * 16;
+      const uint4 val = *reinterpret_cast<const uint4*>(ostage + rr * O_STAGE_LD + cb);
+      if (wrow + rr < p.sq)
+        *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(p.o + (size_t)(wrow + rr) * p.ldo + col0) + cb) = val;
+    }
+    __syncwarp();
   }
 }
 
@@ -582,7 +595,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
     // ------------------------------------------------------------ softmax + epilogue
     const int t = warp >= 6 ? 1 : 0;  // query tile
     softmax_role<false, kMasked>(p, tmem, t, warp, lane, &bars->s_full[t], &bars->p_full[t], 0u, &bars->o_done, abort_flag,
-                        q0 + t * BQ, col0, n);
+                        q0 + t * BQ, col0, n, smem + OFF_K + (warp - 2) * O_STAGE_BYTES);
   }
 
   __syncthreads();
@@ -624,6 +637,8 @@ struct PairBars {
 };
 
 static_assert(sizeof(AttnBars) <= 256 && sizeof(PairBars) <= 512, "barrier blocks fit their reserved shared bytes");
+static_assert(8 * O_STAGE_BYTES <= (KST + VST) * TILE && 8 * O_STAGE_BYTES <= (PK_ST + PV_ST) * HALF,
+              "the epilogue staging of eight softmax warps fits the K / V rings");
 
 template <bool kMasked>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(NUM_THREADS, 1)
@@ -797,7 +812,7 @@ attn_pair_kernel(const __grid_constant__ AttnParams p) {
     // ------------------------------------------------------------ softmax + epilogue (both CTAs)
     const int t = warp >= 6 ? 1 : 0;
     softmax_role<true, kMasked>(p, tmem, t, warp, lane, &bars->s_full[t], nullptr, iris::mapa_shared(&bars->p_full[t], 0),
-                       &bars->o_done, abort_flag, q0 + t * BQ, col0, n);
+                       &bars->o_done, abort_flag, q0 + t * BQ, col0, n, smem + P_OFF_K + (warp - 2) * O_STAGE_BYTES);
   }
 
   __syncthreads();
