@@ -432,7 +432,10 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
   const int col0 = head * HD;
   const int kvcol0 = (head / p.kv_group) * HD;
 
-  iris::grid_dep_wait();  // the key mask below may come from the previous kernel
+  // Set-up before the wait for the previous kernel (a CTA that starts during
+  // its tail allocates and initialises meanwhile); the masked instantiation
+  // reads the key mask first, which the previous kernel may write.
+  if (kMasked) iris::grid_dep_wait();
   if (warp == 2) {
     const int nkv = live_key_tiles<kMasked>(p, q0, min(p.sq, q0 + (has1 ? 2 : 1) * BQ) - 1, lane);
     if (lane == 0) bars->nkv = nkv;
@@ -463,6 +466,7 @@ __global__ void __launch_bounds__(NUM_THREADS, 1) attn_tc_kernel(const __grid_co
   iris::tc_fence_before();
   __syncthreads();
   iris::tc_fence_after();
+  if (!kMasked) iris::grid_dep_wait();  // Q, K and V come from the previous kernel
   const uint32_t tmem = bars->tmem_base;
   iris::grid_dep_launch();  // after this CTA's TMEM allocation
   const int n = bars->nkv;
@@ -655,7 +659,10 @@ attn_pair_kernel(const __grid_constant__ AttnParams p) {
   const int col0 = head * HD;
   const int kvcol0 = (head / p.kv_group) * HD;
 
-  iris::grid_dep_wait();  // the key mask below may come from the previous kernel
+  // Set-up before the wait for the previous kernel (a CTA that starts during
+  // its tail allocates and initialises meanwhile); the masked instantiation
+  // reads the key mask first, which the previous kernel may write.
+  if (kMasked) iris::grid_dep_wait();
   if (warp == 2) {  // both CTAs of the pair: the same rows, the same count
     const int r0 = (blockIdx.x >> 1) * (4 * BQ);
     const int nkv = live_key_tiles<kMasked>(p, r0, min(p.sq, r0 + 4 * BQ) - 1, lane);
@@ -688,6 +695,7 @@ attn_pair_kernel(const __grid_constant__ AttnParams p) {
   __syncthreads();
   iris::cluster_sync();  // both CTAs' barriers exist before any remote arrive
   iris::tc_fence_after();
+  if (!kMasked) iris::grid_dep_wait();  // Q, K and V come from the previous kernel
   const uint32_t tmem = bars->tmem_base;
   iris::grid_dep_launch();  // after this CTA's TMEM allocation
   const int n = bars->nkv;
