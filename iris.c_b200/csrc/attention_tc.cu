@@ -27,7 +27,8 @@
 //               2^8; only then is O (already final for tiles < j, since the
 //               commit that signals S_j covers P_{j-1} V_{j-1}) scaled in TMEM.
 //               O and l always share the same m, so the result is exact.
-//               Epilogue: O / l -> bf16 -> global.
+//               Epilogue: O / l -> bf16 -> shared memory (the idle K / V
+//               rings) -> global, whole rows per store instruction.
 // Every wait is bounded (see ptx.cuh).
 #include "iris_kernels.h"
 #include "ptx.cuh"
